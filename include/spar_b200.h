@@ -1,0 +1,218 @@
+/* spar_b200 — B200 (sm_100a) training backend for Spar's Transformer hot path.
+ *
+ * New C ABI entry points. They keep the conventions of Spar's backend ABI
+ * (src/backend/cuda_kernels.hpp:41-44 status struct, int dtype tags, raw caller-owned device
+ * pointers, a device index per call) and add one thing: every call takes a CUDA stream
+ * (`stream`, a cudaStream_t passed as void*; NULL = the legacy default stream) and is
+ * asynchronous. A returned status reports argument and launch errors; errors that happen while
+ * the kernel runs surface at the caller's next synchronisation, and device-side data errors
+ * (bad class ids, non-finite gradient norms) are reported through caller-provided int32 flags.
+ *
+ * All tensors are row-major fp32 unless stated otherwise; index tensors are int32.
+ */
+#ifndef SPAR_B200_H
+#define SPAR_B200_H
+
+#include <stdint.h>
+
+#include "spar_cuda_kernels.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------------------------ */
+/* LayerNorm over the last axis of x[rows, cols] (cols % 4 == 0).                              */
+/* y = (x - mean) * rstd * gamma + beta with mean, rstd = 1/sqrt(var + epsilon), var biased.    */
+/* Spar has no LayerNorm op; this is the composition mean/subtract/square/mean/add_scalar/     */
+/* sqrt/divide/multiply/add of src/ops (pattern of src/nn/rmsnorm.cpp:50-52) fused into one.   */
+/* mean/rstd ([rows] each) are saved for the backward pass.                                     */
+struct SparCudaStatus spar_b200_layernorm_forward(float* y, float* mean, float* rstd,
+                                                  const float* x, const float* gamma,
+                                                  const float* beta, uint64_t rows, uint64_t cols,
+                                                  double epsilon, int device, void* stream);
+
+/* dX, dgamma, dbeta of the LayerNorm above in one pass over (x, dy). dgamma/dbeta are reduced */
+/* deterministically (fixed per-block partial order); accumulate != 0 adds them to the existing */
+/* contents (gradient accumulation across micro-steps, Spar autograd.cpp:240-246). dx may be   */
+/* accumulated into with accumulate_dx != 0 (residual-stream gradients).                       */
+struct SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma, float* dbeta,
+                                                   const float* dy, const float* x,
+                                                   const float* gamma, const float* mean,
+                                                   const float* rstd, uint64_t rows, uint64_t cols,
+                                                   int accumulate_params, int accumulate_dx,
+                                                   int device, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* GELU, tanh form: gelu(x) = x * sigmoid(2*sqrt(2/pi)*(x + 0.044715 x^3)), the identity that  */
+/* writes the tanh form with Spar's stable sigmoid (src/ops/unary.cpp:137-148).                 */
+struct SparCudaStatus spar_b200_gelu_forward(float* y, const float* x, uint64_t count, int device,
+                                             void* stream);
+/* dx = gelu'(x) * dy                                                                           */
+struct SparCudaStatus spar_b200_gelu_backward(float* dx, const float* dy, const float* x,
+                                              uint64_t count, int device, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Causal softmax over the last axis of `batch` square [T, T] score matrices (row stride ld).  */
+/* P[i, j] = softmax_j(scale * S[i, j] + mask) with mask = 0 for j <= i, -inf otherwise; this  */
+/* is Spar's scaled_dot_product_attention scale + causal_mask + softmax(axis 3) chain          */
+/* (src/nn/attention.cpp:128-134). Entries above the diagonal are never read; they are written */
+/* as 0 for j < zero_fill_to(i) = min(T, round_up(i + 1, zero_fill_block)), zero_fill_block == 0 */
+/* meaning the whole row.                                                                       */
+struct SparCudaStatus spar_b200_causal_softmax_forward(float* p, const float* s, uint64_t batch,
+                                                       uint64_t t, uint64_t ld, float scale,
+                                                       uint64_t zero_fill_block, int device,
+                                                       void* stream);
+/* dS[i, j] = scale * P[i, j] * (dP[i, j] - sum_k dP[i, k] P[i, k]) for j <= i (Spar softmax   */
+/* backward, src/ops/softmax.cpp:110-150, times the score scale of attention.cpp:128-129);      */
+/* zero fill above the diagonal as in the forward call. ds may alias dp.                        */
+struct SparCudaStatus spar_b200_causal_softmax_backward(float* ds, const float* dp, const float* p,
+                                                        uint64_t batch, uint64_t t, uint64_t ld,
+                                                        float scale, uint64_t zero_fill_block,
+                                                        int device, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Fused softmax cross-entropy forward + backward over logits[rows, classes] (row stride ld).   */
+/* For every row r with a target: loss[r] = logsumexp(z_r) - z_r[target] and                  */
+/* dlogits[r, :] = grad_scale * (softmax(z_r) - onehot(target)); rows without a target get     */
+/* loss 0 and dlogits 0. dlogits may alias logits (in-place).                                   */
+/* sequence_length == 0: target of row r is targets[r] (Spar loss::cross_entropy,              */
+/*   src/loss/cross_entropy.cpp:146-174).                                                       */
+/* sequence_length == T > 1: language-model shift (cross_entropy.cpp:176-214): row r = b*T + t */
+/*   has target targets[b*T + t + 1] for t < T-1 and no target for t = T-1.                     */
+/* grad_scale is the upstream gradient of the mean, 1/(number of targets) for Spar's mean      */
+/* reduction. Targets outside [0, classes) set *invalid_target = 1 (never cleared here) and the */
+/* row gets loss NaN and dlogits 0.                                                              */
+struct SparCudaStatus spar_b200_cross_entropy_forward_backward(
+    float* loss, float* dlogits, const float* logits, const int32_t* targets, uint64_t rows,
+    uint64_t classes, uint64_t ld, uint64_t sequence_length, float grad_scale,
+    int32_t* invalid_target, int device, void* stream);
+
+/* Deterministic sum of `count` floats into *out (double accumulation, fixed order).          */
+struct SparCudaStatus spar_b200_sum(float* out, const float* values, uint64_t count, int device,
+                                    void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Gradient clipping + AdamW over flat fp32 arrays.                                            */
+/* Step 1 (spar_b200_grad_norm_squared): norm_state[0] = sum of g^2 (double), norm_state[1] =   */
+/*   non-finite flag, over every (grad, count) pair in the list. Equivalent to Spar's          */
+/*   global_grad_norm (src/training/gradients.cpp:28-137) up to double rounding.               */
+/* Step 2 (spar_b200_adamw_clipped): clip factor = max_norm / norm when norm > max_norm        */
+/*   (clip_grad_norm, gradients.cpp:176-190), computed on the device from norm_state; then     */
+/*   Spar's AdamW update (src/optim/adamw.cpp:37-63) in double with moments rounded to fp32.   */
+/*   A non-finite norm sets *nonfinite_flag = 1 and leaves every tensor untouched (Spar throws */
+/*   "Cannot clip nonfinite gradients" before any update). max_norm < 0 disables clipping.     */
+struct SparB200TensorSlice {
+  float* parameter;
+  float* gradient;
+  float* first_moment;
+  float* second_moment;
+  uint64_t count;
+};
+struct SparCudaStatus spar_b200_grad_norm_squared(double* norm_state,
+                                                  const struct SparB200TensorSlice* slices,
+                                                  uint64_t slice_count, int device, void* stream);
+struct SparCudaStatus spar_b200_adamw_clipped(const struct SparB200TensorSlice* slices,
+                                              uint64_t slice_count, const double* norm_state,
+                                              double max_norm, double learning_rate, double beta1,
+                                              double beta2, double epsilon, double weight_decay,
+                                              uint64_t step, int32_t* nonfinite_flag,
+                                              int device, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Embedding gather out[i, :] = weight[ids[i], :] (src/ops/embedding.cpp:89-121, 55-67).             */
+/* Ids outside [0, vocab) set *invalid_index = 1 and produce a zero row.                        */
+struct SparCudaStatus spar_b200_embedding_forward(float* out, const float* weight,
+                                                  const int32_t* ids, uint64_t count,
+                                                  uint64_t vocab, uint64_t dim,
+                                                  int32_t* invalid_index, int device,
+                                                  void* stream);
+/* grad_weight[v, :] += sum_{i: ids[i] == v} grad_out[i, :], deterministic (no atomics): the   */
+/* ids are counting-sorted on the device and every vocabulary row is reduced in index order.   */
+/* Needs scratch of spar_b200_embedding_backward_scratch_bytes(count, vocab) bytes.            */
+uint64_t spar_b200_embedding_backward_scratch_bytes(uint64_t count, uint64_t vocab);
+struct SparCudaStatus spar_b200_embedding_backward(float* grad_weight, const float* grad_out,
+                                                   const int32_t* ids, uint64_t count,
+                                                   uint64_t vocab, uint64_t dim, void* scratch,
+                                                   int device, void* stream);
+
+/* Column sums: out[c] (+)= sum_r x[r, c] over x[rows, cols] (row stride ld): the bias gradient */
+/* db = reduce_gradient_to_shape(dY, [out]) (src/core/tensor.cpp:597-632), deterministic.      */
+struct SparCudaStatus spar_b200_column_sum(float* out, const float* x, uint64_t rows,
+                                           uint64_t cols, uint64_t ld, int accumulate, int device,
+                                           void* stream);
+
+/* Rotary embedding on interleaved pairs, in place on q/k heads laid out [B, T, H, D] with row */
+/* stride ld (elements between consecutive tokens). Angle table as Spar's apply_rope           */
+/* (src/nn/rope.cpp:35-66): angle = pos * theta^(-2i/D) in double, cos/sin rounded to fp32.    */
+/* `table` is [T, D/2] float2 (cos, sin) from spar_b200_rope_table; inverse != 0 rotates back  */
+/* (the backward pass).                                                                         */
+struct SparCudaStatus spar_b200_rope_table(float* table, uint64_t t, uint64_t d, double theta,
+                                           uint64_t start_position, int device, void* stream);
+struct SparCudaStatus spar_b200_rope_apply(float* x, const float* table, uint64_t batch,
+                                           uint64_t t, uint64_t heads, uint64_t d, uint64_t ld,
+                                           int inverse, int device, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Dense contraction on the tcgen05 tensor cores (TMA-fed, TMEM accumulators, fp32 accumulate). */
+/* Replaces Spar's cuBLAS seam spar::detail::cuda_blas::matmul (src/backend/cuda_blas.cppm:    */
+/* 122-194) and the transposed-operand copies of the matmul backward (src/ops/matmul.cpp:      */
+/* 140-153).                                                                                    */
+/*   C[b0,b1] = epilogue(alpha * opA(A[b0,b1]) * opB(B[b0,b1]))                                */
+/* A is logical [m, k]: stored row-major [m, k] (a_transposed = 0) or [k, m] (= 1).             */
+/* B is logical [k, n]: stored row-major [k, n] (b_transposed = 0) or [n, k] (= 1).             */
+/* Leading dimensions and batch strides are in elements and must be multiples of 4 (16 bytes); */
+/* base pointers 16-byte aligned.                                                               */
+enum SparB200Precision {
+  SPAR_B200_TF32 = 0,   /* operands rounded to TF32 (10-bit mantissa), fp32 accumulate */
+  SPAR_B200_TF32X3 = 1, /* split a = hi + lo, three TF32 products: fp32-faithful */
+};
+enum SparB200Epilogue {
+  SPAR_B200_EPI_NONE = 0,      /* C = alpha*acc                                            */
+  SPAR_B200_EPI_BIAS = 1,      /* C = alpha*acc + bias[n]                                  */
+  SPAR_B200_EPI_BIAS_GELU = 2, /* aux = alpha*acc + bias[n] (pre-activation); C = gelu(aux) */
+  SPAR_B200_EPI_GELU_BWD = 3,  /* C = alpha*acc * gelu'(aux)  (aux = saved pre-activation)  */
+};
+enum SparB200Causal {
+  SPAR_B200_CAUSAL_NONE = 0,
+  SPAR_B200_CAUSAL_LOWER = 1,  /* m == n: output tiles strictly above the diagonal skipped  */
+  SPAR_B200_CAUSAL_K_UPTO = 2, /* reduction limited to k <= row index (P*V, dS*K)          */
+  SPAR_B200_CAUSAL_K_FROM = 3, /* reduction limited to k >= row index (P^T*dO, dS^T*Q)     */
+};
+struct SparB200Gemm {
+  uint64_t m, n, k;
+  uint64_t batch[2];
+  const float* a;
+  uint64_t lda;
+  uint64_t a_batch_stride[2];
+  int a_transposed;
+  const float* b;
+  uint64_t ldb;
+  uint64_t b_batch_stride[2];
+  int b_transposed;
+  float* c;
+  uint64_t ldc;
+  uint64_t c_batch_stride[2];
+  float alpha;
+  int accumulate; /* 1: C += result (beta = 1) */
+  int epilogue;   /* SparB200Epilogue */
+  const float* bias;
+  float* aux; /* same shape/strides as C, leading dimension ldaux */
+  uint64_t ldaux;
+  int precision; /* SparB200Precision */
+  int causal;    /* SparB200Causal */
+};
+struct SparCudaStatus spar_b200_gemm(const struct SparB200Gemm* gemm, int device, void* stream);
+
+/* Returns 1 if a GEMM on `device` gave up on a bounded pipeline wait (the kernel records the    */
+/* event and exits instead of hanging), 0 otherwise, -1 on a CUDA error; clear != 0 resets it.  */
+int spar_b200_gemm_error(int device, int clear);
+
+/* Library version string. */
+const char* spar_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,107 @@
+// Shared host/device helpers for the spar_b200 kernel library.
+//
+// Status convention follows the reference C ABI (src/backend/cuda_kernels.cu:12-22):
+//   code 0 = success, 1 = invalid argument, 2 = CUDA runtime error (cuda_error filled in).
+// Unlike the reference, launches here are asynchronous on a caller-supplied stream; only
+// launch/configuration errors are reported by the call itself.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "spar_b200.h"
+
+namespace spar_b200 {
+
+inline SparCudaStatus ok() { return {0, static_cast<int>(cudaSuccess)}; }
+inline SparCudaStatus invalid() { return {1, static_cast<int>(cudaErrorInvalidValue)}; }
+inline SparCudaStatus runtime(cudaError_t e) { return {2, static_cast<int>(e)}; }
+
+// Selects `device` for the duration of a call and restores the caller's device afterwards,
+// mirroring the reference's select_device/finish_launch pair (cuda_kernels.cu:24-49).
+class DeviceScope {
+ public:
+  explicit DeviceScope(int device) {
+    error_ = cudaGetDevice(&previous_);
+    if (error_ == cudaSuccess && previous_ != device) {
+      error_ = cudaSetDevice(device);
+      changed_ = error_ == cudaSuccess;
+    }
+  }
+  ~DeviceScope() {
+    if (changed_) cudaSetDevice(previous_);
+  }
+  cudaError_t error() const { return error_; }
+
+ private:
+  int previous_ = 0;
+  bool changed_ = false;
+  cudaError_t error_ = cudaSuccess;
+};
+
+inline SparCudaStatus launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+constexpr int kNumSMs = 148;
+
+inline int sm_count(int device) {
+  static int cached[64] = {0};
+  if (device >= 0 && device < 64 && cached[device] != 0) return cached[device];
+  int n = kNumSMs;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  if (device >= 0 && device < 64) cached[device] = n;
+  return n;
+}
+
+inline unsigned grid_for(uint64_t work, unsigned per_block, unsigned cap) {
+  uint64_t b = (work + per_block - 1) / per_block;
+  if (b < 1) b = 1;
+  if (b > cap) b = cap;
+  return static_cast<unsigned>(b);
+}
+
+// ---------------------------------------------------------------- device reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum of one float per thread; every thread receives the total. `scratch` holds
+// at least 32 floats. Threads per block must be a multiple of 32.
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = lane < warps ? scratch[lane] : 0.f;
+  return warp_sum(t);
+}
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = lane < warps ? scratch[lane] : -INFINITY;
+  return warp_max(t);
+}
+
+// Streaming 128-bit global accesses (data touched once per kernel).
+__device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
+
+}  // namespace spar_b200

@@ -1,0 +1,574 @@
+// Dense fp32 contractions on the sm_100a tensor cores: tcgen05.mma kind::tf32, operands staged
+// in shared memory by TMA (128-byte swizzle), fp32 accumulators in TMEM.
+//
+// This replaces Spar's cuBLAS seam (src/backend/cuda_blas.cppm:122-194: a fresh handle and one
+// cublasSgemm per batch matrix, plus permute().contiguous() copies for every transposed operand,
+// src/ops/matmul.cpp:140-153). Both operand majors are read in place: a row-major [m, k] A is
+// "K-major" for the MMA, a row-major [k, m] (transposed) A is "MN-major"; the same for B. So
+// Y = X*W, dX = dY*W^T and dW = X^T*dY run without transposed copies, and the attention products
+// run on head-strided views of the fused QKV buffer through 4-D tensor maps.
+//
+// Kernel shape (persistent, one CTA per SM, 192 threads):
+//   warp 0     TMA producer: one elected thread fills a STAGES-deep ring of A/B k-slices
+//   warp 1     MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=8) into one of
+//              two TMEM accumulators; tcgen05.commit releases ring slots and publishes tiles
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31),
+//              alpha/bias/GELU/GELU'/accumulate applied in registers, 128-bit global stores
+// The double-buffered accumulator lets the epilogue of tile i overlap the mainloop of tile i+1.
+//
+// 3xTF32 ("fp32-faithful") mode: A = Ah + Al, B = Bh + Bl with Ah = A truncated to TF32 and
+// Al = A - Ah (exact in fp32); the kernel runs over three K sections reading (Ah,Bh), (Ah,Bl),
+// (Al,Bh) from split copies made by a streaming kernel, so A*B ~ Ah*Bh + Ah*Bl + Al*Bh
+// (error-compensated TF32, Ootomo & Yokota 2022) into one fp32 accumulator.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace spar_b200 {
+
+__device__ int g_gemm_error = 0;  // set when a bounded wait expires (read by the host)
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+
+struct GemmParams {
+  CUtensorMap a_map[3];
+  CUtensorMap b_map[3];
+  int sections;
+  int a_mn_major, b_mn_major;
+  uint32_t m, n, k;
+  uint32_t batch1;  // inner batch extent (b1); b0 derived
+  uint32_t tiles_m, tiles_n;
+  uint32_t total_tiles;
+  float* c;
+  uint64_t ldc, c_bs0, c_bs1;
+  float* aux;
+  uint64_t ldaux;
+  const float* bias;
+  float alpha;
+  int accumulate, epilogue, causal;
+};
+
+struct TileCoord {
+  uint32_t b0, b1, mt, nt;
+};
+
+template <int BN>
+__device__ __forceinline__ bool decode_tile(const GemmParams& p, uint32_t idx, TileCoord& t) {
+  const uint32_t per_batch = p.tiles_m * p.tiles_n;
+  const uint32_t bidx = idx / per_batch;
+  const uint32_t r = idx - bidx * per_batch;
+  t.b1 = bidx % p.batch1;
+  t.b0 = bidx / p.batch1;
+  // Grouped raster: 8 M-tiles share each sweep over N for L2 reuse of B.
+  constexpr uint32_t G = 8;
+  const uint32_t per_group = G * p.tiles_n;
+  const uint32_t group = r / per_group;
+  const uint32_t first_m = group * G;
+  const uint32_t gsize = min(p.tiles_m - first_m, G);
+  const uint32_t in_group = r - group * per_group;
+  t.mt = first_m + in_group % gsize;
+  t.nt = in_group / gsize;
+  if (p.causal == SPAR_B200_CAUSAL_LOWER && t.nt * BN >= (t.mt + 1) * BM) return false;
+  return true;
+}
+
+__device__ __forceinline__ void k_range(const GemmParams& p, uint32_t mt, uint32_t& kb0,
+                                        uint32_t& kb1) {
+  const uint32_t kb_total = (p.k + BK - 1) / BK;
+  kb0 = 0;
+  kb1 = kb_total;
+  if (p.causal == SPAR_B200_CAUSAL_K_UPTO) {
+    const uint32_t kend = min(p.k, (mt + 1) * BM);
+    kb1 = (kend + BK - 1) / BK;
+  } else if (p.causal == SPAR_B200_CAUSAL_K_FROM) {
+    kb0 = min((mt * BM) / BK, kb_total);
+  }
+}
+
+__device__ __forceinline__ void record_error() { atomicExch(&g_gemm_error, 1); }
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_constant__ GemmParams p) {
+  constexpr uint32_t A_BYTES = BM * BK * 4;
+  constexpr uint32_t B_BYTES = BN * BK * 4;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(full + s, 1);
+      tc::mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(tfull + b, 1);
+      tc::mbar_init(tempty + b, 4);
+    }
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < p.sections; ++s) {
+      tc::tma_prefetch(&p.a_map[s]);
+      tc::tma_prefetch(&p.b_map[s]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (tc::elect_one()) {
+      uint32_t stage = 0, phase = 0;
+      int last_phase[STAGES];  // parity of the last fill issued into each slot (-1: never)
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
+      for (uint32_t idx = blockIdx.x; idx < p.total_tiles && !*abort_flag; idx += gridDim.x) {
+        TileCoord t;
+        if (!decode_tile<BN>(p, idx, t)) continue;
+        uint32_t kb0, kb1;
+        k_range(p, t.mt, kb0, kb1);
+        const int m0 = static_cast<int>(t.mt * BM), n0 = static_cast<int>(t.nt * BN);
+        for (int sec = 0; sec < p.sections; ++sec) {
+          for (uint32_t kb = kb0; kb < kb1; ++kb) {
+            if (!tc::mbar_wait(empty + stage, phase ^ 1)) {
+              record_error();
+              *abort_flag = 1;
+              break;
+            }
+            uint8_t* a_s = smem + stage * STAGE_BYTES;
+            uint8_t* b_s = a_s + A_BYTES;
+            tc::mbar_arrive_expect_tx(full + stage, STAGE_BYTES);
+            last_phase[stage] = static_cast<int>(phase);
+            const int k0 = static_cast<int>(kb * BK);
+            if (p.a_mn_major) {
+#pragma unroll
+              for (int j = 0; j < BM / 32; ++j)
+                tc::tma_load_4d(a_s + j * 4096, &p.a_map[sec], full + stage, m0 + 32 * j, k0,
+                                t.b1, t.b0);
+            } else {
+              tc::tma_load_4d(a_s, &p.a_map[sec], full + stage, k0, m0, t.b1, t.b0);
+            }
+            if (p.b_mn_major) {
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                tc::tma_load_4d(b_s + j * 4096, &p.b_map[sec], full + stage, n0 + 32 * j, k0,
+                                t.b1, t.b0);
+            } else {
+              tc::tma_load_4d(b_s, &p.b_map[sec], full + stage, k0, n0, t.b1, t.b0);
+            }
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (*abort_flag) break;
+        }
+      }
+      // Every copy issued into a slot must have landed before the CTA exits (this matters only
+      // when a consumer gave up early; in the normal path these phases completed long ago).
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s)
+        if (last_phase[s] >= 0 && !tc::mbar_wait(full + s, static_cast<uint32_t>(last_phase[s])))
+          record_error();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = tc::idesc_tf32(BM, BN, p.a_mn_major, p.b_mn_major);
+    if (tc::elect_one()) {
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      for (uint32_t idx = blockIdx.x; idx < p.total_tiles && !*abort_flag; idx += gridDim.x) {
+        TileCoord t;
+        if (!decode_tile<BN>(p, idx, t)) continue;
+        uint32_t kb0, kb1;
+        k_range(p, t.mt, kb0, kb1);
+        if (!tc::mbar_wait(tempty + acc, acc_phase ^ 1)) {
+          record_error();
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        uint32_t issued = 0;
+        for (int sec = 0; sec < p.sections && !*abort_flag; ++sec) {
+          for (uint32_t kb = kb0; kb < kb1; ++kb) {
+            if (!tc::mbar_wait(full + stage, phase)) {
+              record_error();
+              *abort_flag = 1;
+              break;
+            }
+            tc::tc_fence_after();
+            const uint32_t a_addr = tc::smem_u32(smem + stage * STAGE_BYTES);
+            const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < BK / 8; ++ks) {
+              const uint64_t a_desc =
+                  p.a_mn_major ? tc::smem_desc_sw128(a_addr + ks * 1024, 4096, 1024)
+                               : tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024);
+              const uint64_t b_desc =
+                  p.b_mn_major ? tc::smem_desc_sw128(b_addr + ks * 1024, 4096, 1024)
+                               : tc::smem_desc_sw128(b_addr + ks * 32, 16, 1024);
+              tc::mma_tf32(d_tmem, a_desc, b_desc, idesc, (issued | ks) != 0 ? 1u : 0u);
+            }
+            issued = 1;
+            tc::mma_commit(empty + stage);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+        tc::mma_commit(tfull + acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // Make sure every MMA has retired before TMEM is released.
+      tc::mma_commit(drain);
+      if (!tc::mbar_wait(drain, 0)) record_error();
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const uint32_t quarter = static_cast<uint32_t>(warp & 3);
+    uint32_t acc = 0, acc_phase = 0;
+    for (uint32_t idx = blockIdx.x; idx < p.total_tiles; idx += gridDim.x) {
+      TileCoord t;
+      if (!decode_tile<BN>(p, idx, t)) continue;
+      if (*abort_flag) break;
+      if (!tc::mbar_wait(tfull + acc, acc_phase)) {
+        record_error();
+        *abort_flag = 1;
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t row = t.mt * BM + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
+      float* crow = p.c + t.b0 * p.c_bs0 + t.b1 * p.c_bs1 + static_cast<uint64_t>(row) * p.ldc;
+      float* arow = p.aux ? p.aux + t.b0 * p.c_bs0 + t.b1 * p.c_bs1 +
+                                static_cast<uint64_t>(row) * p.ldaux
+                          : nullptr;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tc::tmem_load_32x32(tmem_base + ((quarter * 32) << 16) + acc * BN + chunk * 32, r);
+        tc::tmem_load_wait();
+        const uint32_t col0 = t.nt * BN + chunk * 32;
+        if (!row_ok || col0 >= p.n) continue;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const uint32_t col = col0 + j;
+          if (col >= p.n) break;
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = p.alpha * __uint_as_float(r[j + e]);
+          const bool full4 = col + 3 < p.n;
+          if (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (col + e < p.n) v[e] += p.bias[col + e];
+          }
+          if (p.epilogue == SPAR_B200_EPI_BIAS_GELU) {
+            if (full4) {
+              *reinterpret_cast<float4*>(arow + col) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+              for (int e = 0; e < 4; ++e)
+                if (col + e < p.n) arow[col + e] = v[e];
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = gelu_value(v[e]);
+          } else if (p.epilogue == SPAR_B200_EPI_GELU_BWD) {
+            float pre[4] = {0.f, 0.f, 0.f, 0.f};
+            if (full4) {
+              const float4 q = *reinterpret_cast<const float4*>(arow + col);
+              pre[0] = q.x;
+              pre[1] = q.y;
+              pre[2] = q.z;
+              pre[3] = q.w;
+            } else {
+              for (int e = 0; e < 4; ++e)
+                if (col + e < p.n) pre[e] = arow[col + e];
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] *= gelu_derivative(pre[e]);
+          }
+          if (full4) {
+            float4* dst = reinterpret_cast<float4*>(crow + col);
+            if (p.accumulate) {
+              const float4 o = *dst;
+              v[0] += o.x;
+              v[1] += o.y;
+              v[2] += o.z;
+              v[3] += o.w;
+            }
+            *dst = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+            for (int e = 0; e < 4; ++e)
+              if (col + e < p.n) crow[col + e] = p.accumulate ? crow[col + e] + v[e] : v[e];
+          }
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tempty + acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ----------------------------------------------------------------- 3xTF32 operand split
+// hi = x with the low 13 mantissa bits cleared (exactly representable in TF32), lo = x - hi.
+__global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo,
+                                  const float* __restrict__ src, uint64_t inner, uint64_t rows,
+                                  uint64_t b1, uint64_t b0, uint64_t ld, uint64_t bs1,
+                                  uint64_t bs0, uint64_t out_ld) {
+  const uint64_t total = inner * rows * b1 * b0;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const uint64_t x = i % inner;
+    uint64_t rest = i / inner;
+    const uint64_t r = rest % rows;
+    rest /= rows;
+    const uint64_t q1 = rest % b1, q0 = rest / b1;
+    const float v = src[q0 * bs0 + q1 * bs1 + r * ld + x];
+    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    const uint64_t o = ((q0 * b1 + q1) * rows + r) * out_ld + x;
+    hi[o] = h;
+    lo[o] = v - h;
+  }
+}
+
+// ----------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// Stored operand view: element (x, r) of batch (q1, q0) at base + q0*bs0 + q1*bs1 + r*ld + x,
+// x the contiguous index. Box = 32 contiguous elements x box_rows rows.
+bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows, uint64_t b1,
+              uint64_t b0, uint64_t ld, uint64_t bs1, uint64_t bs0, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if (bs1 == 0) bs1 = ld * rows;
+  if (bs0 == 0) bs0 = bs1 * b1;
+  cuuint64_t dims[4] = {inner, rows, b1, b0};
+  cuuint64_t strides[3] = {ld * 4, bs1 * 4, bs0 * 4};
+  cuuint32_t box[4] = {32, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES>
+cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) {
+  constexpr size_t smem = STAGES * (BM * BK * 4 + BN * BK * 4) + 1024 + 256;
+  static bool configured[64] = {false};
+  auto k = gemm_tf32_kernel<BN, STAGES>;
+  if (device < 0 || device >= 64 || !configured[device]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    if (device >= 0 && device < 64) configured[device] = true;
+  }
+  const unsigned grid = std::min<uint32_t>(p.total_tiles, static_cast<uint32_t>(sm_count(device)));
+  k<<<grid, kThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
+  const uint64_t b = g.batch[0] * g.batch[1];
+  const uint64_t a_inner = g.a_transposed ? g.m : g.k, a_rows = g.a_transposed ? g.k : g.m;
+  const uint64_t b_inner = g.b_transposed ? g.k : g.n, b_rows = g.b_transposed ? g.n : g.k;
+  auto pad = [](uint64_t x) { return (x + 3) & ~3ull; };
+  return 2 * b * (pad(a_inner) * a_rows + pad(b_inner) * b_rows);
+}
+
+cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
+                        cudaStream_t stream) {
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
+  const bool split = g.precision == SPAR_B200_TF32X3;
+  int bn = g.n > 128 ? 256 : (g.n > 64 ? 128 : 64);
+  p.sections = split ? 3 : 1;
+  p.a_mn_major = g.a_transposed ? 1 : 0;
+  p.b_mn_major = g.b_transposed ? 0 : 1;
+
+  const uint64_t a_inner = g.a_transposed ? g.m : g.k, a_rows = g.a_transposed ? g.k : g.m;
+  const uint64_t b_inner = g.b_transposed ? g.k : g.n, b_rows = g.b_transposed ? g.n : g.k;
+  const uint32_t a_box_rows = p.a_mn_major ? BK : BM;
+  const uint32_t b_box_rows = p.b_mn_major ? BK : static_cast<uint32_t>(bn);
+
+  if (!split) {
+    if (!make_map(&p.a_map[0], g.a, a_inner, a_rows, b1, b0, g.lda, g.a_batch_stride[1],
+                  g.a_batch_stride[0], a_box_rows) ||
+        !make_map(&p.b_map[0], g.b, b_inner, b_rows, b1, b0, g.ldb, g.b_batch_stride[1],
+                  g.b_batch_stride[0], b_box_rows))
+      return cudaErrorInvalidValue;
+  } else {
+    auto pad = [](uint64_t x) { return (x + 3) & ~3ull; };
+    const uint64_t a_ld = pad(a_inner), b_ld = pad(b_inner);
+    float* ah = split_workspace;
+    float* al = ah + b0 * b1 * a_ld * a_rows;
+    float* bh = al + b0 * b1 * a_ld * a_rows;
+    float* bl = bh + b0 * b1 * b_ld * b_rows;
+    const int sms = sm_count(device);
+    split_tf32_kernel<<<sms * 8, 256, 0, stream>>>(ah, al, g.a, a_inner, a_rows, b1, b0, g.lda,
+                                                   g.a_batch_stride[1], g.a_batch_stride[0], a_ld);
+    split_tf32_kernel<<<sms * 8, 256, 0, stream>>>(bh, bl, g.b, b_inner, b_rows, b1, b0, g.ldb,
+                                                   g.b_batch_stride[1], g.b_batch_stride[0], b_ld);
+    const uint64_t abs1 = a_ld * a_rows, abs0 = abs1 * b1;
+    const uint64_t bbs1 = b_ld * b_rows, bbs0 = bbs1 * b1;
+    const float* am[3] = {ah, ah, al};
+    const float* bm[3] = {bh, bl, bh};
+    for (int s = 0; s < 3; ++s) {
+      if (!make_map(&p.a_map[s], am[s], a_inner, a_rows, b1, b0, a_ld, abs1, abs0, a_box_rows) ||
+          !make_map(&p.b_map[s], bm[s], b_inner, b_rows, b1, b0, b_ld, bbs1, bbs0, b_box_rows))
+        return cudaErrorInvalidValue;
+    }
+  }
+  p.m = static_cast<uint32_t>(g.m);
+  p.n = static_cast<uint32_t>(g.n);
+  p.k = static_cast<uint32_t>(g.k);
+  p.batch1 = static_cast<uint32_t>(b1);
+  p.tiles_m = static_cast<uint32_t>((g.m + BM - 1) / BM);
+  p.tiles_n = static_cast<uint32_t>((g.n + bn - 1) / bn);
+  p.total_tiles = static_cast<uint32_t>(p.tiles_m * p.tiles_n * b0 * b1);
+  p.c = g.c;
+  p.ldc = g.ldc;
+  p.c_bs0 = g.c_batch_stride[0];
+  p.c_bs1 = g.c_batch_stride[1];
+  p.aux = g.aux;
+  p.ldaux = g.ldaux;
+  p.bias = g.bias;
+  p.alpha = g.alpha;
+  p.accumulate = g.accumulate;
+  p.epilogue = g.epilogue;
+  p.causal = g.causal;
+  switch (bn) {
+    case 256:
+      return launch_kernel<256, 4>(p, device, stream);
+    case 128:
+      return launch_kernel<128, 6>(p, device, stream);
+    default:
+      return launch_kernel<64, 8>(p, device, stream);
+  }
+}
+
+SparCudaStatus gemm_validate(const SparB200Gemm* g) {
+  if (!g) return invalid();
+  const SparB200Gemm& x = *g;
+  const uint64_t b1 = x.batch[1] ? x.batch[1] : 1, b0 = x.batch[0] ? x.batch[0] : 1;
+  if (x.m == 0 || x.n == 0 || x.k == 0) return invalid();
+  if (x.m > 0x7fffffffull || x.n > 0x7fffffffull || x.k > 0x7fffffffull) return invalid();
+  if ((x.m + BM - 1) / BM * ((x.n + 63) / 64) * b0 * b1 > 0xffffffffull) return invalid();
+  if (!x.a || !x.b || !x.c) return invalid();
+  if (!aligned16(x.a) || !aligned16(x.b) || !aligned16(x.c)) return invalid();
+  if (x.lda % 4 || x.ldb % 4 || x.ldc % 4 || x.a_batch_stride[0] % 4 || x.a_batch_stride[1] % 4 ||
+      x.b_batch_stride[0] % 4 || x.b_batch_stride[1] % 4)
+    return invalid();
+  const uint64_t a_inner = x.a_transposed ? x.m : x.k;
+  const uint64_t b_inner = x.b_transposed ? x.k : x.n;
+  if (x.lda < a_inner || x.ldb < b_inner || x.ldc < x.n) return invalid();
+  if (x.epilogue < 0 || x.epilogue > SPAR_B200_EPI_GELU_BWD) return invalid();
+  if ((x.epilogue == SPAR_B200_EPI_BIAS || x.epilogue == SPAR_B200_EPI_BIAS_GELU) && !x.bias)
+    return invalid();
+  if ((x.epilogue == SPAR_B200_EPI_BIAS_GELU || x.epilogue == SPAR_B200_EPI_GELU_BWD) &&
+      (!x.aux || !aligned16(x.aux) || x.ldaux % 4 || x.ldaux < x.n))
+    return invalid();
+  if (x.precision != SPAR_B200_TF32 && x.precision != SPAR_B200_TF32X3) return invalid();
+  if (x.causal < 0 || x.causal > SPAR_B200_CAUSAL_K_FROM) return invalid();
+  if (x.causal == SPAR_B200_CAUSAL_LOWER && x.m != x.n) return invalid();
+  if ((x.causal == SPAR_B200_CAUSAL_K_UPTO || x.causal == SPAR_B200_CAUSAL_K_FROM) && x.m != x.k)
+    return invalid();
+  return ok();
+}
+
+}  // namespace spar_b200
+
+using namespace spar_b200;
+
+extern "C" SparCudaStatus spar_b200_gemm(const SparB200Gemm* gemm, int device, void* stream) {
+  const SparCudaStatus v = gemm_validate(gemm);
+  if (v.code != 0) return v;
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* ws = nullptr;
+  if (gemm->precision == SPAR_B200_TF32X3) {
+    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws),
+                                          gemm_split_workspace_floats(*gemm) * sizeof(float), s);
+    if (e != cudaSuccess) return runtime(e);
+  }
+  const cudaError_t e = gemm_launch(*gemm, ws, device, s);
+  if (ws) cudaFreeAsync(ws, s);
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" int spar_b200_gemm_error(int device, int clear) {
+  DeviceScope scope(device);
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int));
+  }
+  return v;
+}

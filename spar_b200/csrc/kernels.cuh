@@ -1,0 +1,95 @@
+// Internal launchers shared by the C ABI wrappers and the training-step runtime, plus the
+// element functions that several kernels (and GEMM epilogues) evaluate.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace spar_b200 {
+
+// Spar's stable sigmoid (src/ops/unary.cpp:55-61 / cuda_kernels.cu:105-111), in fp32.
+__device__ __forceinline__ float stable_sigmoid(float v) {
+  if (v >= 0.f) return 1.f / (1.f + expf(-v));
+  const float e = expf(v);
+  return e / (1.f + e);
+}
+
+// GELU (tanh form) written through the sigmoid: x * sigmoid(2*sqrt(2/pi)*(x + 0.044715 x^3)).
+// Constants are fp32, as Spar's scalar ops round their scalar to the tensor dtype
+// (src/ops/scalar.cpp:40).
+constexpr float kGeluA = 1.5957691216057308f;  // 2*sqrt(2/pi)
+constexpr float kGeluB = 0.044715f;
+
+__device__ __forceinline__ float gelu_value(float x) {
+  const float x3 = (x * x) * x;
+  const float u = (x + x3 * kGeluB) * kGeluA;
+  return x * stable_sigmoid(u);
+}
+
+__device__ __forceinline__ float gelu_derivative(float x) {
+  const float x2 = x * x;
+  const float u = (x + (x2 * x) * kGeluB) * kGeluA;
+  const float s = stable_sigmoid(u);
+  const float du = kGeluA * (1.f + 3.f * kGeluB * x2);
+  return s + x * (s * (1.f - s)) * du;
+}
+
+// ---------------------------------------------------------------- launchers (async, on stream)
+cudaError_t layernorm_forward_launch(float* y, float* mean, float* rstd, const float* x,
+                                     const float* gamma, const float* beta, uint64_t rows,
+                                     uint64_t cols, float eps, int device, cudaStream_t stream);
+int layernorm_backward_parts(uint64_t rows, int device);
+cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, const float* dy,
+                                      const float* x, const float* gamma, const float* mean,
+                                      const float* rstd, uint64_t rows, uint64_t cols,
+                                      int accumulate_params, int accumulate_dx, float* workspace,
+                                      int device, cudaStream_t stream);
+
+cudaError_t gelu_launch(float* y, const float* dy, const float* x, uint64_t n, int backward,
+                        int device, cudaStream_t stream);
+cudaError_t rope_table_launch(float* table, uint64_t t, uint64_t d, double theta, uint64_t start,
+                              cudaStream_t stream);
+cudaError_t rope_apply_launch(float* x, const float* table, uint64_t tokens, uint64_t t,
+                              uint64_t heads, uint64_t d, uint64_t ld, int inverse, int device,
+                              cudaStream_t stream);
+int column_sum_parts(uint64_t rows, uint64_t cols, int device);
+cudaError_t column_sum_launch(float* out, const float* x, uint64_t rows, uint64_t cols,
+                              uint64_t ld, int accumulate, float* workspace, int device,
+                              cudaStream_t stream);
+cudaError_t sum_launch(float* out, const float* v, uint64_t n, cudaStream_t stream);
+
+cudaError_t causal_softmax_launch(float* out, const float* in, const float* p, uint64_t batch,
+                                  uint64_t t, uint64_t ld, float scale, uint64_t zero_fill_block,
+                                  int backward, cudaStream_t stream);
+
+cudaError_t cross_entropy_launch(float* loss, float* dlogits, const float* logits,
+                                 const int32_t* targets, uint64_t rows, uint64_t classes,
+                                 uint64_t ld, uint64_t sequence_length, float grad_scale,
+                                 int32_t* invalid_target, int device, cudaStream_t stream);
+
+// Multi-slice gradient norm + clipped AdamW. `norm_state` holds kNormStateDoubles doubles.
+constexpr int kNormStateDoubles = 1024;
+struct Slice {
+  float* parameter;
+  float* gradient;
+  float* first_moment;
+  float* second_moment;
+  uint64_t count;
+};
+cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t slice_count,
+                             int device, cudaStream_t stream);
+cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double* norm_state,
+                         double max_norm, double lr, double beta1, double beta2, double eps,
+                         double weight_decay, uint64_t step, int32_t* nonfinite_flag, int device,
+                         cudaStream_t stream);
+
+cudaError_t embedding_forward_launch(float* out, const float* weight, const int32_t* ids,
+                                     uint64_t count, uint64_t vocab, uint64_t dim,
+                                     int32_t* invalid_index, int device, cudaStream_t stream);
+uint64_t embedding_backward_scratch(uint64_t count, uint64_t vocab);
+cudaError_t embedding_backward_launch(float* grad_weight, const float* grad_out,
+                                      const int32_t* ids, uint64_t count, uint64_t vocab,
+                                      uint64_t dim, void* scratch, int device,
+                                      cudaStream_t stream);
+
+}  // namespace spar_b200

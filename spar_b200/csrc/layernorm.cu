@@ -1,0 +1,330 @@
+// LayerNorm forward/backward over the last axis, fp32.
+//
+// Spar has no LayerNorm op. The harness composes it from Spar ops in the order
+//   mean(x) -> subtract -> square -> mean -> add_scalar(eps) -> sqrt -> divide -> multiply(gamma)
+//   -> add(beta)
+// which is the RMSNorm pattern of src/nn/rmsnorm.cpp:50-52 with a centring step; the forward here
+// evaluates that chain with the same operation order per element (divide by sqrt(var + eps), not
+// multiply by a reciprocal). The backward is the closed form of that chain's autograd:
+//   xhat = (x - mean) * rstd, g = dy * gamma
+//   dx = rstd * (g - mean(g) - xhat * mean(g * xhat)), dgamma = sum_rows dy * xhat, dbeta = sum dy
+//
+// Layout: one warp per row, the row held in registers as float4 (lane l owns float4 columns
+// l, l + 32, ...), so x and dy are read from HBM exactly once per pass. dgamma/dbeta are
+// accumulated per lane in registers, reduced over the block's warps in shared memory and written
+// as one partial row per block; a second kernel sums the partials in block order
+// (deterministic, no atomics).
+#include "common.cuh"
+
+namespace spar_b200 {
+namespace {
+
+constexpr int kWarps = 8;  // rows in flight per block
+
+template <int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
+                         float* __restrict__ rstd_out, const float* __restrict__ x,
+                         const float* __restrict__ gamma, const float* __restrict__ beta,
+                         uint64_t rows, int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int vec_cols = cols >> 2;
+  const float inv_cols = 1.0f / static_cast<float>(cols);
+  float4 g[VPL], b[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int f = lane + 32 * j;
+    if (f < vec_cols) {
+      g[j] = reinterpret_cast<const float4*>(gamma)[f];
+      b[j] = reinterpret_cast<const float4*>(beta)[f];
+    }
+  }
+  const uint64_t warp_global = (static_cast<uint64_t>(blockIdx.x) * kWarps) + (threadIdx.x >> 5);
+  const uint64_t warp_stride = static_cast<uint64_t>(gridDim.x) * kWarps;
+  for (uint64_t row = warp_global; row < rows; row += warp_stride) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+    float4 v[VPL];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int f = lane + 32 * j;
+      if (f < vec_cols) {
+        v[j] = ld_stream(xr + f);
+        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+      }
+    }
+    const float mean = warp_sum(s) * inv_cols;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int f = lane + 32 * j;
+      if (f < vec_cols) {
+        const float a = v[j].x - mean, c = v[j].y - mean, d = v[j].z - mean, e = v[j].w - mean;
+        q += (a * a + c * c) + (d * d + e * e);
+      }
+    }
+    const float var = warp_sum(q) * inv_cols;
+    const float denom = sqrtf(var + eps);
+    float4* yr = reinterpret_cast<float4*>(y + row * cols);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int f = lane + 32 * j;
+      if (f < vec_cols) {
+        float4 o;
+        o.x = (v[j].x - mean) / denom * g[j].x + b[j].x;
+        o.y = (v[j].y - mean) / denom * g[j].y + b[j].y;
+        o.z = (v[j].z - mean) / denom * g[j].z + b[j].z;
+        o.w = (v[j].w - mean) / denom * g[j].w + b[j].w;
+        yr[f] = o;
+      }
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = 1.0f / denom;
+    }
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(kWarps * 32)
+layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dgamma,
+                          float* __restrict__ partial_dbeta, const float* __restrict__ dy,
+                          const float* __restrict__ x, const float* __restrict__ gamma,
+                          const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                          uint64_t rows, int cols, uint64_t rows_per_block, int accumulate_dx) {
+  extern __shared__ float smem[];  // [kWarps][cols] twice
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int vec_cols = cols >> 2;
+  const float inv_cols = 1.0f / static_cast<float>(cols);
+  float4 g[VPL], pg[VPL], pb[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int f = lane + 32 * j;
+    pg[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    pb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (f < vec_cols) g[j] = reinterpret_cast<const float4*>(gamma)[f];
+  }
+  const uint64_t row_begin = static_cast<uint64_t>(blockIdx.x) * rows_per_block;
+  uint64_t row_end = row_begin + rows_per_block;
+  if (row_end > rows) row_end = rows;
+  for (uint64_t row = row_begin + warp; row < row_end; row += kWarps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+    const float4* dyr = reinterpret_cast<const float4*>(dy + row * cols);
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float4 xh[VPL], d[VPL];
+    float sg = 0.f, sgx = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int f = lane + 32 * j;
+      if (f < vec_cols) {
+        const float4 xv = ld_stream(xr + f);
+        d[j] = ld_stream(dyr + f);
+        xh[j] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
+                            (xv.w - mean) * rstd);
+        const float g0 = d[j].x * g[j].x, g1 = d[j].y * g[j].y, g2 = d[j].z * g[j].z,
+                    g3 = d[j].w * g[j].w;
+        sg += (g0 + g1) + (g2 + g3);
+        sgx += (g0 * xh[j].x + g1 * xh[j].y) + (g2 * xh[j].z + g3 * xh[j].w);
+        pg[j].x += d[j].x * xh[j].x;
+        pg[j].y += d[j].y * xh[j].y;
+        pg[j].z += d[j].z * xh[j].z;
+        pg[j].w += d[j].w * xh[j].w;
+        pb[j].x += d[j].x;
+        pb[j].y += d[j].y;
+        pb[j].z += d[j].z;
+        pb[j].w += d[j].w;
+      }
+    }
+    const float mg = warp_sum(sg) * inv_cols;
+    const float mgx = warp_sum(sgx) * inv_cols;
+    float4* dxr = reinterpret_cast<float4*>(dx + row * cols);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int f = lane + 32 * j;
+      if (f < vec_cols) {
+        float4 o;
+        o.x = rstd * (d[j].x * g[j].x - mg - xh[j].x * mgx);
+        o.y = rstd * (d[j].y * g[j].y - mg - xh[j].y * mgx);
+        o.z = rstd * (d[j].z * g[j].z - mg - xh[j].z * mgx);
+        o.w = rstd * (d[j].w * g[j].w - mg - xh[j].w * mgx);
+        if (accumulate_dx) {
+          const float4 prev = dxr[f];
+          o.x += prev.x;
+          o.y += prev.y;
+          o.z += prev.z;
+          o.w += prev.w;
+        }
+        dxr[f] = o;
+      }
+    }
+  }
+  // Reduce the per-warp partials over the block (fixed warp order).
+  float* sg_ = smem;
+  float* sb_ = smem + kWarps * cols;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int f = lane + 32 * j;
+    if (f < vec_cols) {
+      reinterpret_cast<float4*>(sg_ + warp * cols)[f] = pg[j];
+      reinterpret_cast<float4*>(sb_ + warp * cols)[f] = pb[j];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float a = 0.f, bsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      a += sg_[w * cols + c];
+      bsum += sb_[w * cols + c];
+    }
+    partial_dgamma[static_cast<uint64_t>(blockIdx.x) * cols + c] = a;
+    partial_dbeta[static_cast<uint64_t>(blockIdx.x) * cols + c] = bsum;
+  }
+}
+
+// Sums `parts` partial rows of length cols in order; out (+)= result.
+__global__ void reduce_partials_kernel(float* __restrict__ out_a, float* __restrict__ out_b,
+                                       const float* __restrict__ pa, const float* __restrict__ pb,
+                                       int parts, int cols, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float a = 0.f, b = 0.f;
+  for (int p = 0; p < parts; ++p) {
+    a += pa[static_cast<uint64_t>(p) * cols + c];
+    b += pb[static_cast<uint64_t>(p) * cols + c];
+  }
+  if (accumulate) {
+    a += out_a[c];
+    b += out_b[c];
+  }
+  out_a[c] = a;
+  out_b[c] = b;
+}
+
+int vectors_per_lane(uint64_t cols) {
+  const uint64_t v = (cols / 4 + 31) / 32;
+  if (v <= 1) return 1;
+  if (v <= 2) return 2;
+  if (v <= 4) return 4;
+  if (v <= 6) return 6;
+  if (v <= 8) return 8;
+  if (v <= 12) return 12;
+  if (v <= 16) return 16;
+  return 0;
+}
+
+}  // namespace
+
+// Number of partial rows the backward writes for `rows` (workspace = 2 * parts * cols floats).
+int layernorm_backward_parts(uint64_t rows, int device) {
+  uint64_t parts = static_cast<uint64_t>(sm_count(device)) * 2;
+  const uint64_t by_rows = (rows + kWarps - 1) / kWarps;
+  if (parts > by_rows) parts = by_rows;
+  if (parts < 1) parts = 1;
+  return static_cast<int>(parts);
+}
+
+cudaError_t layernorm_forward_launch(float* y, float* mean, float* rstd, const float* x,
+                                     const float* gamma, const float* beta, uint64_t rows,
+                                     uint64_t cols, float eps, int device, cudaStream_t stream) {
+  const unsigned grid = grid_for(rows, kWarps, sm_count(device) * 8);
+  const int c = static_cast<int>(cols);
+  switch (vectors_per_lane(cols)) {
+#define SPAR_LN_FWD(V) \
+  case V:              \
+    layernorm_forward_kernel<V><<<grid, kWarps * 32, 0, stream>>>(y, mean, rstd, x, gamma, beta, rows, c, eps); \
+    break;
+    SPAR_LN_FWD(1) SPAR_LN_FWD(2) SPAR_LN_FWD(4) SPAR_LN_FWD(6) SPAR_LN_FWD(8) SPAR_LN_FWD(12)
+    SPAR_LN_FWD(16)
+#undef SPAR_LN_FWD
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, const float* dy,
+                                      const float* x, const float* gamma, const float* mean,
+                                      const float* rstd, uint64_t rows, uint64_t cols,
+                                      int accumulate_params, int accumulate_dx, float* workspace,
+                                      int device, cudaStream_t stream) {
+  const int parts = layernorm_backward_parts(rows, device);
+  const uint64_t rows_per_block = (rows + parts - 1) / parts;
+  const int c = static_cast<int>(cols);
+  const size_t smem = 2 * kWarps * cols * sizeof(float);
+  float* pa = workspace;
+  float* pb = workspace + static_cast<uint64_t>(parts) * cols;
+  switch (vectors_per_lane(cols)) {
+#define SPAR_LN_BWD(V)                                                                          \
+  case V: {                                                                                    \
+    auto k = layernorm_backward_kernel<V>;                                                     \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                               static_cast<int>(smem));                         \
+    k<<<parts, kWarps * 32, smem, stream>>>(dx, pa, pb, dy, x, gamma, mean, rstd, rows, c,     \
+                                            rows_per_block, accumulate_dx);                     \
+    break;                                                                                     \
+  }
+    SPAR_LN_BWD(1) SPAR_LN_BWD(2) SPAR_LN_BWD(4) SPAR_LN_BWD(6) SPAR_LN_BWD(8) SPAR_LN_BWD(12)
+    SPAR_LN_BWD(16)
+#undef SPAR_LN_BWD
+    default:
+      return cudaErrorInvalidValue;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  reduce_partials_kernel<<<(c + 255) / 256, 256, 0, stream>>>(dgamma, dbeta, pa, pb, parts, c,
+                                                              accumulate_params);
+  return cudaGetLastError();
+}
+
+}  // namespace spar_b200
+
+using namespace spar_b200;
+
+extern "C" SparCudaStatus spar_b200_layernorm_forward(float* y, float* mean, float* rstd,
+                                                      const float* x, const float* gamma,
+                                                      const float* beta, uint64_t rows,
+                                                      uint64_t cols, double epsilon, int device,
+                                                      void* stream) {
+  if (rows == 0) return ok();
+  if (cols == 0 || cols % 4 != 0 || vectors_per_lane(cols) == 0 || !y || !mean || !rstd || !x ||
+      !gamma || !beta || !(epsilon > 0.0))
+    return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const cudaError_t e = layernorm_forward_launch(y, mean, rstd, x, gamma, beta, rows, cols,
+                                                 static_cast<float>(epsilon), device,
+                                                 static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma, float* dbeta,
+                                                       const float* dy, const float* x,
+                                                       const float* gamma, const float* mean,
+                                                       const float* rstd, uint64_t rows,
+                                                       uint64_t cols, int accumulate_params,
+                                                       int accumulate_dx, int device,
+                                                       void* stream) {
+  if (cols == 0 || cols % 4 != 0 || vectors_per_lane(cols) == 0 || !dgamma || !dbeta || !gamma)
+    return invalid();
+  if (rows != 0 && (!dx || !dy || !x || !mean || !rstd)) return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (accumulate_params) return ok();
+    cudaError_t e = cudaMemsetAsync(dgamma, 0, cols * sizeof(float), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dbeta, 0, cols * sizeof(float), s);
+    return e == cudaSuccess ? ok() : runtime(e);
+  }
+  const int parts = layernorm_backward_parts(rows, device);
+  float* workspace = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&workspace),
+                                  2ull * parts * cols * sizeof(float), s);
+  if (e != cudaSuccess) return runtime(e);
+  e = layernorm_backward_launch(dx, dgamma, dbeta, dy, x, gamma, mean, rstd, rows, cols,
+                                accumulate_params, accumulate_dx, workspace, device, s);
+  const cudaError_t f = cudaFreeAsync(workspace, s);
+  if (e != cudaSuccess) return runtime(e);
+  return f == cudaSuccess ? ok() : runtime(f);
+}

@@ -1,0 +1,193 @@
+"""Parity of the tcgen05 GEMM (through the C ABI) against a float64 matmul.
+
+Tolerances: TF32 mode rel-L2 <= 2e-3 (TF32 keeps 10 mantissa bits), 3xTF32 mode rel-L2 <= 1e-5
+and max relative error <= 1e-5 (fp32-faithful), the bars stated for the GEMMs.
+"""
+import numpy as np
+import pytest
+
+from _util import rel_err, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _mats(m, n, k, a_t, b_t, seed=0):
+    r = np.random.default_rng(seed)
+    a = r.standard_normal((k, m) if a_t else (m, k)).astype(np.float32)
+    b = (0.02 * r.standard_normal((n, k) if b_t else (k, n))).astype(np.float32)
+    a64 = a.astype(np.float64).T if a_t else a.astype(np.float64)
+    b64 = b.astype(np.float64).T if b_t else b.astype(np.float64)
+    return a, b, a64 @ b64
+
+
+SHAPES = [
+    (128, 256, 64),
+    (256, 512, 1024),
+    (200, 300, 96),     # ragged M/N, K multiple of 32
+    (1000, 768, 3072),
+    (64, 64, 64),
+    (384, 100, 40),     # ragged K
+    (2048, 1024, 4096),
+]
+
+
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_gemm_tf32_layouts(cuda, shape, a_t, b_t):
+    import torch
+    from spar_b200 import ops
+
+    m, n, k = shape
+    if (a_t and m % 4) or (not b_t and n % 4) or (not a_t and k % 4) or (b_t and k % 4):
+        pytest.skip("leading dimension must be a multiple of 4")
+    a, b, ref = _mats(m, n, k, a_t, b_t, seed=m + n + k)
+    c = ops.matmul(torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda), a_t=a_t, b_t=b_t)
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+    assert rel_l2(c.cpu().numpy(), ref) <= 2e-3
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False)])
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (200, 300, 96), (1024, 1024, 2048)])
+def test_gemm_3xtf32(cuda, shape, a_t, b_t):
+    import torch
+    from spar_b200 import ops
+
+    m, n, k = shape
+    a, b, ref = _mats(m, n, k, a_t, b_t, seed=7)
+    c = ops.matmul(torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda), a_t=a_t, b_t=b_t,
+                   precision=ops.TF32X3)
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+    got = c.cpu().numpy()
+    assert rel_l2(got, ref) <= 1e-5
+    assert rel_err(got, ref) <= 1e-5
+
+
+def test_gemm_epilogues(cuda):
+    import torch
+    from spar_b200 import ops
+    from oracle import spar_oracle as O
+
+    m, n, k = 256, 512, 256
+    a, b, ref = _mats(m, n, k, False, False, seed=3)
+    bias = np.random.default_rng(4).standard_normal(n).astype(np.float32)
+    at, bt = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    biast = torch.from_numpy(bias).to(cuda)
+    prec = ops.TF32X3
+    c = ops.matmul(at, bt, epilogue=ops.EPI_BIAS, bias=biast, precision=prec, alpha=0.5)
+    pre = torch.empty(m, n, device=cuda)
+    g = ops.matmul(at, bt, epilogue=ops.EPI_BIAS_GELU, bias=biast, aux=pre, precision=prec)
+    dpre = ops.matmul(at, bt, epilogue=ops.EPI_GELU_BWD, aux=pre, precision=prec)
+    acc = torch.ones(m, n, device=cuda)
+    ops.matmul(at, bt, out=acc, accumulate=True, precision=prec)
+    torch.cuda.synchronize()
+    pre_ref = ref + bias
+    assert rel_err(c.cpu().numpy(), 0.5 * ref + bias) <= 1e-5
+    assert rel_err(pre.cpu().numpy(), pre_ref) <= 1e-5
+    assert rel_err(g.cpu().numpy(), O.gelu_forward(pre_ref, np.float64)) <= 1e-5
+    pre32 = pre.cpu().numpy()
+    assert rel_err(dpre.cpu().numpy(), ref * O.gelu_derivative(pre32)) <= 1e-5
+    assert rel_err(acc.cpu().numpy(), ref + 1.0) <= 1e-5
+
+
+def _attention_views(cuda, b, h, t, dh, seed=0):
+    import torch
+
+    d = h * dh
+    r = np.random.default_rng(seed)
+    qkv = r.standard_normal((b * t, 3 * d)).astype(np.float32)
+    return qkv, torch.from_numpy(qkv).to(cuda)
+
+
+@pytest.mark.parametrize("b,h,t,dh", [(2, 4, 256, 64), (1, 2, 512, 64), (2, 3, 64, 32)])
+def test_gemm_attention_batched_causal(cuda, b, h, t, dh):
+    """The six attention products on head-strided views of a fused [B*T, 3d] QKV buffer."""
+    import torch
+    from spar_b200 import ops
+
+    d = h * dh
+    qkv, qkvt = _attention_views(cuda, b, h, t, dh, seed=t)
+    ld = 3 * d
+    base = qkvt.data_ptr()
+    q_ptr, k_ptr, v_ptr = base, base + 4 * d, base + 8 * d
+    bs = (t * ld, dh)  # (batch, head) strides in elements
+    dev, stream = 0, torch.cuda.current_stream().cuda_stream
+    prec = ops.TF32X3
+    S = torch.empty(b, h, t, t, device=cuda)
+    s_bs = (h * t * t, t * t)
+    # S = Q K^T (lower tiles only)
+    ops.gemm_run(ops.gemm_desc(t, t, dh, q_ptr, ld, k_ptr, ld, S.data_ptr(), t, b_t=True,
+                               batch=(b, h), a_bs=bs, b_bs=bs, c_bs=s_bs, precision=prec,
+                               causal=ops.CAUSAL_LOWER), dev, stream)
+    P = ops.causal_softmax_forward(S, 1.0 / np.sqrt(dh), zero_fill_block=128)
+    # O = P V  (k <= row)
+    ctx = torch.empty(b * t, d, device=cuda)
+    ops.gemm_run(ops.gemm_desc(t, dh, t, P.data_ptr(), t, v_ptr, ld, ctx.data_ptr(), d,
+                               batch=(b, h), a_bs=s_bs, b_bs=bs, c_bs=(t * d, dh),
+                               precision=prec, causal=ops.CAUSAL_K_UPTO), dev, stream)
+    dO = torch.randn(b * t, d, device=cuda)
+    # dV = P^T dO (k >= row)
+    dV = torch.empty(b * t, d, device=cuda)
+    ops.gemm_run(ops.gemm_desc(t, dh, t, P.data_ptr(), t, dO.data_ptr(), d, dV.data_ptr(), d,
+                               a_t=True, batch=(b, h), a_bs=s_bs, b_bs=(t * d, dh),
+                               c_bs=(t * d, dh), precision=prec, causal=ops.CAUSAL_K_FROM),
+                 dev, stream)
+    # dP = dO V^T (lower tiles)
+    dP = torch.empty_like(S)
+    ops.gemm_run(ops.gemm_desc(t, t, dh, dO.data_ptr(), d, v_ptr, ld, dP.data_ptr(), t,
+                               b_t=True, batch=(b, h), a_bs=(t * d, dh), b_bs=bs, c_bs=s_bs,
+                               precision=prec, causal=ops.CAUSAL_LOWER), dev, stream)
+    dS = ops.causal_softmax_backward(dP, P, 1.0 / np.sqrt(dh), zero_fill_block=128)
+    # dQ = dS K (k <= row), dK = dS^T Q (k >= row)
+    dQ = torch.empty(b * t, d, device=cuda)
+    dK = torch.empty(b * t, d, device=cuda)
+    ops.gemm_run(ops.gemm_desc(t, dh, t, dS.data_ptr(), t, k_ptr, ld, dQ.data_ptr(), d,
+                               batch=(b, h), a_bs=s_bs, b_bs=bs, c_bs=(t * d, dh),
+                               precision=prec, causal=ops.CAUSAL_K_UPTO), dev, stream)
+    ops.gemm_run(ops.gemm_desc(t, dh, t, dS.data_ptr(), t, q_ptr, ld, dK.data_ptr(), d,
+                               a_t=True, batch=(b, h), a_bs=s_bs, b_bs=bs, c_bs=(t * d, dh),
+                               precision=prec, causal=ops.CAUSAL_K_FROM), dev, stream)
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+
+    def heads(x):
+        return x.reshape(b, t, h, dh).transpose(0, 2, 1, 3).astype(np.float64)
+
+    q = heads(qkv[:, :d])
+    k = heads(qkv[:, d:2 * d])
+    v = heads(qkv[:, 2 * d:])
+    mask = np.triu(np.ones((t, t), bool), 1)
+    s = np.where(mask, -np.inf, q @ k.transpose(0, 1, 3, 2) / np.sqrt(dh))
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    o = p @ v
+    do = heads(dO.cpu().numpy())
+    dv = p.transpose(0, 1, 3, 2) @ do
+    dp = do @ v.transpose(0, 1, 3, 2)
+    ds = p * (dp - (dp * p).sum(-1, keepdims=True)) / np.sqrt(dh)
+    dq = ds @ k
+    dk = ds.transpose(0, 1, 3, 2) @ q
+    merge = lambda x: x.transpose(0, 2, 1, 3).reshape(b * t, d)
+    lower = ~mask
+    assert rel_err(np.where(lower, S.cpu().numpy(), 0), np.where(lower, q @ k.transpose(0, 1, 3, 2), 0)) <= 1e-5
+    assert rel_err(ctx.cpu().numpy(), merge(o)) <= 1e-5
+    assert rel_err(dV.cpu().numpy(), merge(dv)) <= 1e-5
+    assert rel_err(dQ.cpu().numpy(), merge(dq)) <= 1e-5
+    assert rel_err(dK.cpu().numpy(), merge(dk)) <= 1e-5
+
+
+def test_gemm_invalid_arguments(cuda):
+    import torch
+    from spar_b200 import ops
+    from spar_b200._lib import SparError
+
+    a = torch.randn(64, 64, device=cuda)
+    with pytest.raises(SparError) as e:
+        ops.gemm_run(ops.gemm_desc(64, 64, 0, a.data_ptr(), 64, a.data_ptr(), 64, a.data_ptr(), 64),
+                     0, 0)
+    assert e.value.code == 1
+    with pytest.raises(SparError):  # unaligned leading dimension
+        ops.gemm_run(ops.gemm_desc(64, 64, 62, a.data_ptr(), 62, a.data_ptr(), 64, a.data_ptr(), 64),
+                     0, 0)
