@@ -16,8 +16,8 @@
 //              alpha/bias/GELU/GELU'/accumulate applied in registers, 128-bit global stores
 // The double-buffered accumulator lets the epilogue of tile i overlap the mainloop of tile i+1.
 //
-// 3xTF32 ("fp32-faithful") mode: A = Ah + Al, B = Bh + Bl with Ah = A truncated to TF32 and
-// Al = A - Ah (exact in fp32); the kernel runs over three K sections reading (Ah,Bh), (Ah,Bl),
+// 3xTF32 ("fp32-faithful") mode: A = Ah + Al, B = Bh + Bl with Ah = A rounded to TF32 and
+// Al = A - Ah rounded to TF32; the kernel runs over three K sections reading (Ah,Bh), (Ah,Bl),
 // (Al,Bh) from split copies made by a streaming kernel, so A*B ~ Ah*Bh + Ah*Bl + Al*Bh
 // (error-compensated TF32, Ootomo & Yokota 2022) into one fp32 accumulator.
 #include <cudaTypedefs.h>
@@ -232,12 +232,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
             const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
             for (int ks = 0; ks < BK / 8; ++ks) {
+              // K-major: 8 rows of 128 B per 1024 B atom, K step = 32 B inside the row.
+              // MN-major: 32-element MN chunks (one TMA box of 32 K-rows = 4 KB) at LBO, 4-row
+              // K groups at SBO = 512 B, K step = 8 rows = 1024 B.
               const uint64_t a_desc =
-                  p.a_mn_major ? tc::smem_desc_sw128(a_addr + ks * 1024, 4096, 1024)
-                               : tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024);
+                  p.a_mn_major
+                      ? tc::smem_desc(a_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                      : tc::smem_desc(a_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
               const uint64_t b_desc =
-                  p.b_mn_major ? tc::smem_desc_sw128(b_addr + ks * 1024, 4096, 1024)
-                               : tc::smem_desc_sw128(b_addr + ks * 32, 16, 1024);
+                  p.b_mn_major
+                      ? tc::smem_desc(b_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                      : tc::smem_desc(b_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
               tc::mma_tf32(d_tmem, a_desc, b_desc, idesc, (issued | ks) != 0 ? 1u : 0u);
             }
             issued = 1;
@@ -283,7 +288,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
         tc::tmem_load_32x32(tmem_base + ((quarter * 32) << 16) + acc * BN + chunk * 32, r);
-        tc::tmem_load_wait();
         const uint32_t col0 = t.nt * BN + chunk * 32;
         if (!row_ok || col0 >= p.n) continue;
 #pragma unroll
@@ -356,7 +360,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
 }
 
 // ----------------------------------------------------------------- 3xTF32 operand split
-// hi = x with the low 13 mantissa bits cleared (exactly representable in TF32), lo = x - hi.
+// Round-to-nearest to a TF32-representable fp32 (10 explicit mantissa bits): add half an ulp
+// of the 13 dropped bits, then clear them. Both halves are rounded, so the tensor cores see
+// exact TF32 values and the split error is unbiased: hi = rn(x), lo = rn(x - hi).
+__device__ __forceinline__ float round_tf32(float v) {
+  const uint32_t b = __float_as_uint(v);
+  if ((b & 0x7f800000u) == 0x7f800000u) return v;  // inf / nan unchanged
+  return __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
+}
+
 __global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo,
                                   const float* __restrict__ src, uint64_t inner, uint64_t rows,
                                   uint64_t b1, uint64_t b0, uint64_t ld, uint64_t bs1,
@@ -371,10 +383,10 @@ __global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo
     rest /= rows;
     const uint64_t q1 = rest % b1, q0 = rest / b1;
     const float v = src[q0 * bs0 + q1 * bs1 + r * ld + x];
-    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    const float h = round_tf32(v);
     const uint64_t o = ((q0 * b1 + q1) * rows + r) * out_ld + x;
     hi[o] = h;
-    lo[o] = v - h;
+    lo[o] = round_tf32(v - h);
   }
 }
 
@@ -395,8 +407,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // Stored operand view: element (x, r) of batch (q1, q0) at base + q0*bs0 + q1*bs1 + r*ld + x,
 // x the contiguous index. Box = 32 contiguous elements x box_rows rows.
+// MN-major boxes use the 32-byte-atom 128-byte swizzle that the MMA descriptor above expects.
 bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows, uint64_t b1,
-              uint64_t b0, uint64_t ld, uint64_t bs1, uint64_t bs0, uint32_t box_rows) {
+              uint64_t b0, uint64_t ld, uint64_t bs1, uint64_t bs0, uint32_t box_rows,
+              bool mn_major) {
   auto fn = encode_fn();
   if (!fn) return false;
   if (bs1 == 0) bs1 = ld * rows;
@@ -407,7 +421,8 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -458,9 +473,9 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
 
   if (!split) {
     if (!make_map(&p.a_map[0], g.a, a_inner, a_rows, b1, b0, g.lda, g.a_batch_stride[1],
-                  g.a_batch_stride[0], a_box_rows) ||
+                  g.a_batch_stride[0], a_box_rows, p.a_mn_major) ||
         !make_map(&p.b_map[0], g.b, b_inner, b_rows, b1, b0, g.ldb, g.b_batch_stride[1],
-                  g.b_batch_stride[0], b_box_rows))
+                  g.b_batch_stride[0], b_box_rows, p.b_mn_major))
       return cudaErrorInvalidValue;
   } else {
     auto pad = [](uint64_t x) { return (x + 3) & ~3ull; };
@@ -479,8 +494,10 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     const float* am[3] = {ah, ah, al};
     const float* bm[3] = {bh, bl, bh};
     for (int s = 0; s < 3; ++s) {
-      if (!make_map(&p.a_map[s], am[s], a_inner, a_rows, b1, b0, a_ld, abs1, abs0, a_box_rows) ||
-          !make_map(&p.b_map[s], bm[s], b_inner, b_rows, b1, b0, b_ld, bbs1, bbs0, b_box_rows))
+      if (!make_map(&p.a_map[s], am[s], a_inner, a_rows, b1, b0, a_ld, abs1, abs0, a_box_rows,
+                    p.a_mn_major) ||
+          !make_map(&p.b_map[s], bm[s], b_inner, b_rows, b1, b0, b_ld, bbs1, bbs0, b_box_rows,
+                    p.b_mn_major))
         return cudaErrorInvalidValue;
     }
   }

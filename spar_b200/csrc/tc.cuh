@@ -136,32 +136,42 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives row (lane base + i).
+// The tcgen05.wait::ld sits in the same asm statement, so no instruction that consumes the
+// destination registers can be scheduled between the asynchronous load and its completion.
 __device__ __forceinline__ void tmem_load_32x32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_load_wait() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 }
 
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading/stride byte offsets,
-// descriptor version 1 (bits 46-47) and the 128-byte swizzle layout (value 2 in bits 61-63).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// descriptor version 1 (bits 46-47) and the swizzle layout in bits 61-63.
+//   kLayoutSw128      (2): 128-byte swizzle of 16-byte chunks; K-major operands
+//                          (canonical ((8,m),(T,2)) : ((8T,SBO),(1,T)), SBO = 8 rows = 1024 B)
+//   kLayoutSw128Base32 (1): 128-byte swizzle of 32-byte chunks; the only layout the tensor cores
+//                          accept for MN-major 32-bit (tf32) operands
+//                          (canonical ((T,8,m),(4,k)) : ((1,T,LBO),(8T,SBO)): 128 contiguous MN
+//                          bytes, 4-row K groups at SBO, MN chunks of 32 elements at LBO)
+constexpr uint32_t kLayoutSw128Base32 = 1;
+constexpr uint32_t kLayoutSw128 = 2;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }
 
