@@ -172,6 +172,7 @@ enum SparB200Epilogue {
   SPAR_B200_EPI_BIAS = 1,      /* C = alpha*acc + bias[n]                                  */
   SPAR_B200_EPI_BIAS_GELU = 2, /* aux = alpha*acc + bias[n] (pre-activation); C = gelu(aux) */
   SPAR_B200_EPI_GELU_BWD = 3,  /* C = alpha*acc * gelu'(aux)  (aux = saved pre-activation)  */
+  SPAR_B200_EPI_BIAS_ADD = 4,  /* C = alpha*acc (+ bias[n] if bias) + aux  (residual add)    */
 };
 enum SparB200Causal {
   SPAR_B200_CAUSAL_NONE = 0,
@@ -207,6 +208,73 @@ struct SparCudaStatus spar_b200_gemm(const struct SparB200Gemm* gemm, int device
 /* Returns 1 if a GEMM on `device` gave up on a bounded pipeline wait (the kernel records the    */
 /* event and exits instead of hanging), 0 otherwise, -1 on a CUDA error; clear != 0 resets it.  */
 int spar_b200_gemm_error(int device, int clear);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Training-step runtime for the pre-LN / GELU decoder LM (BASELINE's model family): tied token */
+/* embedding, `num_layers` blocks of LayerNorm -> causal self-attention with RoPE (fused QKV     */
+/* projection, biases) -> residual -> LayerNorm -> Linear/GELU/Linear MLP -> residual, final     */
+/* LayerNorm, logits = h E^T, language-model cross-entropy, global-norm clip and AdamW. This is  */
+/* the work one Spar training step does through DecoderLM::forward (src/nn/decoder.cpp:73-90),  */
+/* loss::language_model_cross_entropy (src/loss/cross_entropy.cpp:176-214), Tensor::backward     */
+/* (src/autograd/autograd.cpp:201-265), training::clip_grad_norm (gradients.cpp:176-190) and    */
+/* optim::AdamW::step (src/optim/adamw.cpp:83-170), scheduled on one CUDA stream.               */
+/* Parameters are exposed under Spar's named_parameters names (src/nn/parameters.cpp:51-132).   */
+struct SparB200LMConfig {
+  uint64_t vocab_size, model_dim, hidden_dim, num_layers, num_heads, sequence_length;
+  uint64_t micro_batch; /* sequences per micro-step */
+  double norm_epsilon;  /* LayerNorm epsilon (Spar's norm default 1e-5) */
+  double rope_theta;    /* 10000 in Spar */
+  int use_rope;
+  int precision; /* SparB200Precision of every GEMM */
+  double beta1, beta2, adam_epsilon, weight_decay;
+  double max_grad_norm; /* < 0: no clipping */
+};
+struct SparCudaStatus spar_b200_lm_create(const struct SparB200LMConfig* config, int device,
+                                          void** handle);
+void spar_b200_lm_destroy(void* handle);
+uint64_t spar_b200_lm_parameter_count(void* handle);
+uint64_t spar_b200_lm_flat_size(void* handle);
+/* which: 0 parameters, 1 gradients, 2 first moments, 3 second moments (flat device arrays). */
+float* spar_b200_lm_flat_buffer(void* handle, int which);
+struct SparCudaStatus spar_b200_lm_parameter_info(void* handle, uint64_t index, char* name,
+                                                  uint64_t name_capacity, uint64_t* rows,
+                                                  uint64_t* cols);
+struct SparCudaStatus spar_b200_lm_parameter_copy(void* handle, uint64_t index, int which,
+                                                  int to_device, float* host);
+struct SparCudaStatus spar_b200_lm_init_normal(void* handle, uint64_t seed, double std,
+                                               void* stream);
+struct SparCudaStatus spar_b200_lm_zero_grad(void* handle, void* stream);
+struct SparCudaStatus spar_b200_lm_forward_backward(void* handle, const int32_t* ids,
+                                                    uint64_t micro_index, float grad_scale,
+                                                    int last_micro, void* stream);
+struct SparCudaStatus spar_b200_lm_optimizer_step(void* handle, double learning_rate,
+                                                  uint64_t step, void* stream);
+struct SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* ids, int ids_on_host,
+                                              uint64_t micro_steps, double learning_rate,
+                                              uint64_t step, float* loss_out,
+                                              double* grad_norm_out, int32_t* flags_out,
+                                              void* stream);
+struct SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int world_size);
+struct SparCudaStatus spar_b200_lm_read_losses(void* handle, float* host, uint64_t count);
+/* Event timing of every tensor-core GEMM launch (for roofline accounting) and a kernel-launch */
+/* counter; profile_read synchronises the device.                                              */
+struct SparCudaStatus spar_b200_lm_profile(void* handle, int enable);
+struct SparCudaStatus spar_b200_lm_profile_read(void* handle, double* gemm_ms, double* gemm_flops,
+                                                uint64_t* gemm_launches,
+                                                uint64_t* kernel_launches);
+double spar_b200_warmup_cosine(double peak, double minimum, uint64_t warmup_steps,
+                               uint64_t decay_steps, uint64_t completed_steps);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Data-parallel communicator (NCCL). Status code 3 = communication error (ncclResult_t in      */
+/* cuda_error). Spar has no distributed backend; this is the new gradient exchange.             */
+struct SparCudaStatus spar_b200_comm_unique_id(char* out, uint64_t capacity);
+struct SparCudaStatus spar_b200_comm_init(const char* unique_id, int rank, int world_size,
+                                          int device, void** comm);
+struct SparCudaStatus spar_b200_comm_allreduce_sum(void* comm, float* data, uint64_t count,
+                                                   void* stream);
+struct SparCudaStatus spar_b200_comm_check(void* comm);
+struct SparCudaStatus spar_b200_comm_destroy(void* comm, int abort);
 
 /* Library version string. */
 const char* spar_b200_version(void);

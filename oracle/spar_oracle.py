@@ -377,13 +377,13 @@ def lm_forward_backward(params, ids, cfg, dtype=np.float64):
     grads = {name: np.zeros_like(val) for name, val in P.items()}
     grads["token_embedding.weight"] += dlogits.T @ hf
     dhf = dlogits @ E
-    dh, dgf, dbf = layer_norm_backward(dhf, h, P["final_norm.weight"], eps, dtype)
+    dres, dgf, dbf = layer_norm_backward(dhf, h, P["final_norm.weight"], eps, dtype)
     grads["final_norm.weight"] += dgf
     grads["final_norm.bias"] += dbf
     for i in reversed(range(layers)):
         pre = f"blocks.{i}."
         x, a, qh, kh, vh, pr, ctx, h1, a2, u, g = cache[i]
-        dm = dh
+        dm = dres
         grads[pre + "mlp.down_proj.weight"] += g.T @ dm
         grads[pre + "mlp.down_proj.bias"] += dm.sum(0)
         dg = dm @ P[pre + "mlp.down_proj.weight"].T
@@ -394,7 +394,7 @@ def lm_forward_backward(params, ids, cfg, dtype=np.float64):
         dx2, dg2, db2 = layer_norm_backward(da2, h1, P[pre + "mlp_norm.weight"], eps, dtype)
         grads[pre + "mlp_norm.weight"] += dg2
         grads[pre + "mlp_norm.bias"] += db2
-        dh1 = dh + dx2
+        dh1 = dres + dx2
         grads[pre + "attention.out_proj.weight"] += ctx.T @ dh1
         grads[pre + "attention.out_proj.bias"] += dh1.sum(0)
         dctx = heads_of(dh1 @ P[pre + "attention.out_proj.weight"].T)
@@ -412,8 +412,8 @@ def lm_forward_backward(params, ids, cfg, dtype=np.float64):
         dx1, dg1, db1 = layer_norm_backward(da, x, P[pre + "attention_norm.weight"], eps, dtype)
         grads[pre + "attention_norm.weight"] += dg1
         grads[pre + "attention_norm.bias"] += db1
-        dh = dh1 + dx1
-    np.add.at(grads["token_embedding.weight"], ids.reshape(-1), dh)
+        dres = dh1 + dx1
+    np.add.at(grads["token_embedding.weight"], ids.reshape(-1), dres)
     return float(loss), grads
 
 

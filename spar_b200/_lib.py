@@ -72,6 +72,30 @@ SIGNATURES = {
     "spar_b200_rope_apply": (S, [p, p, u64, u64, u64, u64, u64, i, i, p]),
     "spar_b200_gemm": (S, [POINTER(SparB200Gemm), i, p]),
     "spar_b200_gemm_error": (c_int, [i, i]),
+    "spar_b200_lm_create": (S, [POINTER(SparB200LMConfig), i, POINTER(c_void_p)]),
+    "spar_b200_lm_destroy": (None, [p]),
+    "spar_b200_lm_parameter_count": (u64, [p]),
+    "spar_b200_lm_flat_size": (u64, [p]),
+    "spar_b200_lm_flat_buffer": (c_void_p, [p, i]),
+    "spar_b200_lm_parameter_info": (S, [p, u64, c_char_p, u64, POINTER(c_uint64), POINTER(c_uint64)]),
+    "spar_b200_lm_parameter_copy": (S, [p, u64, i, i, p]),
+    "spar_b200_lm_init_normal": (S, [p, u64, d, p]),
+    "spar_b200_lm_zero_grad": (S, [p, p]),
+    "spar_b200_lm_forward_backward": (S, [p, p, u64, f, i, p]),
+    "spar_b200_lm_optimizer_step": (S, [p, d, u64, p]),
+    "spar_b200_lm_train_step": (S, [p, p, i, u64, d, u64, POINTER(c_float), POINTER(c_double),
+                                    POINTER(c_int32), p]),
+    "spar_b200_lm_set_comm": (S, [p, p, i]),
+    "spar_b200_lm_read_losses": (S, [p, p, u64]),
+    "spar_b200_warmup_cosine": (d, [d, d, u64, u64, u64]),
+    "spar_b200_lm_profile": (S, [p, i]),
+    "spar_b200_lm_profile_read": (S, [p, POINTER(c_double), POINTER(c_double), POINTER(c_uint64),
+                                      POINTER(c_uint64)]),
+    "spar_b200_comm_unique_id": (S, [c_char_p, u64]),
+    "spar_b200_comm_init": (S, [c_char_p, i, i, i, POINTER(c_void_p)]),
+    "spar_b200_comm_allreduce_sum": (S, [p, p, u64, p]),
+    "spar_b200_comm_check": (S, [p]),
+    "spar_b200_comm_destroy": (S, [p, i]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -1,0 +1,134 @@
+// Data-parallel gradient reduction over NCCL (NVLink / NVSwitch inside one box).
+//
+// Spar itself has no collectives (cross-device copies bounce through the host,
+// src/backend/cuda_runtime.cppm:212-237); this is the new data-parallel exchange: one sum
+// all-reduce per gradient bucket, issued on a communication stream. NCCL is resolved at run time
+// with dlopen("libnccl.so.2"), so the library binds to whichever NCCL the process already loaded
+// (torch's) and needs no link-time dependency.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "spar_b200.h"
+
+namespace spar_b200 {
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& api() {
+  static NcclApi a;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
+    a.async_error = reinterpret_cast<decltype(a.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    a.ok = a.get_unique_id && a.init_rank && a.all_reduce && a.destroy && a.abort;
+  });
+  return a;
+}
+
+struct Comm {
+  ncclComm_t nccl = nullptr;
+  int rank = 0, world = 1, device = 0;
+};
+
+// Status for a failed NCCL call: code 3, the ncclResult_t in cuda_error.
+SparCudaStatus nccl_status(ncclResult_t r) { return {r == ncclSuccess ? 0 : 3, static_cast<int>(r)}; }
+
+}  // namespace
+
+cudaError_t comm_allreduce_sum(void* comm, float* data, uint64_t count, cudaStream_t stream) {
+  const Comm* c = static_cast<const Comm*>(comm);
+  if (!c || !api().ok) return cudaErrorInvalidValue;
+  const ncclResult_t r = api().all_reduce(data, data, count, ncclFloat32, ncclSum, c->nccl, stream);
+  return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+}  // namespace spar_b200
+
+using namespace spar_b200;
+
+extern "C" SparCudaStatus spar_b200_comm_unique_id(char* out, uint64_t capacity) {
+  if (!out || capacity < sizeof(ncclUniqueId)) return {1, static_cast<int>(cudaErrorInvalidValue)};
+  if (!api().ok) return {3, static_cast<int>(ncclSystemError)};
+  ncclUniqueId id;
+  const ncclResult_t r = api().get_unique_id(&id);
+  if (r == ncclSuccess) std::memcpy(out, &id, sizeof(id));
+  return nccl_status(r);
+}
+
+extern "C" SparCudaStatus spar_b200_comm_init(const char* unique_id, int rank, int world_size,
+                                              int device, void** comm) {
+  if (!unique_id || !comm || world_size < 1 || rank < 0 || rank >= world_size)
+    return {1, static_cast<int>(cudaErrorInvalidValue)};
+  *comm = nullptr;
+  if (!api().ok) return {3, static_cast<int>(ncclSystemError)};
+  int previous = 0;
+  cudaGetDevice(&previous);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return {2, static_cast<int>(e)};
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  Comm* c = new Comm();
+  c->rank = rank;
+  c->world = world_size;
+  c->device = device;
+  const ncclResult_t r = api().init_rank(&c->nccl, world_size, id, rank);
+  cudaSetDevice(previous);
+  if (r != ncclSuccess) {
+    delete c;
+    return nccl_status(r);
+  }
+  *comm = c;
+  return {0, 0};
+}
+
+extern "C" SparCudaStatus spar_b200_comm_allreduce_sum(void* comm, float* data, uint64_t count,
+                                                       void* stream) {
+  if (!comm || (count && !data)) return {1, static_cast<int>(cudaErrorInvalidValue)};
+  if (count == 0) return {0, 0};
+  const Comm* c = static_cast<const Comm*>(comm);
+  const ncclResult_t r = api().all_reduce(data, data, count, ncclFloat32, ncclSum, c->nccl,
+                                          static_cast<cudaStream_t>(stream));
+  return nccl_status(r);
+}
+
+// Polls the communicator's asynchronous error state (a peer that died, a network failure).
+extern "C" SparCudaStatus spar_b200_comm_check(void* comm) {
+  if (!comm) return {1, static_cast<int>(cudaErrorInvalidValue)};
+  const Comm* c = static_cast<const Comm*>(comm);
+  if (!api().async_error) return {0, 0};
+  ncclResult_t async = ncclSuccess;
+  const ncclResult_t r = api().async_error(c->nccl, &async);
+  return nccl_status(r != ncclSuccess ? r : async);
+}
+
+// Tears the communicator down; abort != 0 cancels outstanding operations (failure path).
+extern "C" SparCudaStatus spar_b200_comm_destroy(void* comm, int abort) {
+  if (!comm) return {0, 0};
+  Comm* c = static_cast<Comm*>(comm);
+  const ncclResult_t r = abort ? api().abort(c->nccl) : api().destroy(c->nccl);
+  delete c;
+  return nccl_status(r);
+}

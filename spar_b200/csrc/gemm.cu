@@ -298,10 +298,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
 #pragma unroll
           for (int e = 0; e < 4; ++e) v[e] = p.alpha * __uint_as_float(r[j + e]);
           const bool full4 = col + 3 < p.n;
-          if (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU) {
+          if (p.bias && (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU ||
+                         p.epilogue == SPAR_B200_EPI_BIAS_ADD)) {
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               if (col + e < p.n) v[e] += p.bias[col + e];
+          }
+          if (p.epilogue == SPAR_B200_EPI_BIAS_ADD) {
+            if (full4) {
+              const float4 q = *reinterpret_cast<const float4*>(arow + col);
+              v[0] += q.x;
+              v[1] += q.y;
+              v[2] += q.z;
+              v[3] += q.w;
+            } else {
+              for (int e = 0; e < 4; ++e)
+                if (col + e < p.n) v[e] += arow[col + e];
+            }
           }
           if (p.epilogue == SPAR_B200_EPI_BIAS_GELU) {
             if (full4) {
@@ -544,10 +557,11 @@ SparCudaStatus gemm_validate(const SparB200Gemm* g) {
   const uint64_t a_inner = x.a_transposed ? x.m : x.k;
   const uint64_t b_inner = x.b_transposed ? x.k : x.n;
   if (x.lda < a_inner || x.ldb < b_inner || x.ldc < x.n) return invalid();
-  if (x.epilogue < 0 || x.epilogue > SPAR_B200_EPI_GELU_BWD) return invalid();
+  if (x.epilogue < 0 || x.epilogue > SPAR_B200_EPI_BIAS_ADD) return invalid();
   if ((x.epilogue == SPAR_B200_EPI_BIAS || x.epilogue == SPAR_B200_EPI_BIAS_GELU) && !x.bias)
     return invalid();
-  if ((x.epilogue == SPAR_B200_EPI_BIAS_GELU || x.epilogue == SPAR_B200_EPI_GELU_BWD) &&
+  if ((x.epilogue == SPAR_B200_EPI_BIAS_GELU || x.epilogue == SPAR_B200_EPI_GELU_BWD ||
+       x.epilogue == SPAR_B200_EPI_BIAS_ADD) &&
       (!x.aux || !aligned16(x.aux) || x.ldaux % 4 || x.ldaux < x.n))
     return invalid();
   if (x.precision != SPAR_B200_TF32 && x.precision != SPAR_B200_TF32X3) return invalid();

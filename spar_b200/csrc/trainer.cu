@@ -1,0 +1,809 @@
+// Training-step runtime for the pre-LN decoder: parameter/gradient/moment arena, saved
+// activations, forward, hand-scheduled backward, gradient accumulation, data-parallel
+// all-reduce hooks and the fused clip + AdamW update, all enqueued on one CUDA stream.
+//
+// Model (Spar modules composed as in src/nn/decoder.cpp:73-90 and
+// src/nn/transformer.cpp:53-69, with Spar's RMSNorm/SwiGLU swapped for LayerNorm/GELU):
+//   h0 = E[ids]                                        Embedding (src/nn/embedding.cpp:40-42)
+//   per block:  a = LN1(x); q,k,v = a W{q,k,v} + b     Linear, weight [in, out] (linear.cpp:48-63)
+//               q,k = rope(q,k)                        apply_rope (src/nn/rope.cpp:70-92)
+//               P = causal_softmax(q k^T / sqrt(dh))   scaled_dot_product_attention
+//               h1 = x + (P v) Wo + bo                   (src/nn/attention.cpp:122-135, 188-225)
+//               x' = h1 + gelu(LN2(h1) W1 + b1) W2 + b2
+//   logits = LN_f(h_L) E^T (tied, decoder.cpp:88-89); loss = LM cross-entropy
+//   (src/loss/cross_entropy.cpp:176-214)
+// Backward is the reverse-mode sweep Spar's tape performs (src/autograd/autograd.cpp:201-265),
+// written out per layer so every GEMM reads its operands in place (no transposed copies), the
+// GELU derivative and residual adds ride in GEMM epilogues, and leaf gradients accumulate on the
+// device across micro-steps. Q/K/V weights live fused as one [d, 3d] matrix (columns q | k | v);
+// the named-parameter view below splits them back into Spar's q_proj/k_proj/v_proj tensors.
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace spar_b200 {
+
+cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
+                        cudaStream_t stream);
+uint64_t gemm_split_workspace_floats(const SparB200Gemm& g);
+cudaError_t comm_allreduce_sum(void* comm, float* data, uint64_t count, cudaStream_t stream);
+
+namespace {
+
+constexpr uint64_t kAlign = 64;  // floats (256 bytes)
+uint64_t align_up(uint64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// SplitMix64 draw `counter` (0-based) of a Spar Random seeded with `seed`
+// (src/core/random.cpp:22-28: state += golden; mix).
+__device__ __forceinline__ uint64_t splitmix_draw(uint64_t seed, uint64_t counter) {
+  uint64_t z = seed + (counter + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// N(0, std) by Box-Muller on two uniform_double draws (random.cpp:35-38), element i of a
+// [rows, cols] tensor taking draws first + 2i and first + 2i + 1; written at dst[r*ld + c].
+__global__ void init_normal_kernel(float* dst, uint64_t rows, uint64_t cols, uint64_t ld,
+                                   uint64_t seed, uint64_t first, double std) {
+  const uint64_t n = rows * cols;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += stride) {
+    const double u1 = static_cast<double>(splitmix_draw(seed, first + 2 * i) >> 11) / 9007199254740992.0;
+    const double u2 = static_cast<double>(splitmix_draw(seed, first + 2 * i + 1) >> 11) / 9007199254740992.0;
+    const double z = sqrt(-2.0 * log1p(-u1)) * cos(2.0 * 3.141592653589793 * u2);
+    dst[(i / cols) * ld + i % cols] = static_cast<float>(z * std);
+  }
+}
+
+__global__ void fill_kernel(float* dst, uint64_t n, float v) {
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    dst[i] = v;
+}
+
+struct NamedTensor {
+  std::string name;
+  uint64_t offset;  // into the flat arena (floats)
+  uint64_t rows, cols;  // cols == 0: 1-D of length rows
+  uint64_t ld;          // row stride in the arena (fused qkv: 3d)
+  bool draws;           // consumes normal draws at init (weight matrices)
+};
+
+struct LayerOffsets {
+  uint64_t ln1_g, ln1_b, wqkv, bqkv, wo, bo, ln2_g, ln2_b, w1, b1, w2, b2, begin, end;
+};
+
+struct LayerActs {
+  float *x, *mean1, *rstd1, *a1, *qkv, *p, *ctx, *h1, *mean2, *rstd2, *a2, *u, *g;
+};
+
+}  // namespace
+
+#define SPAR_TRY_RAW(expr)              \
+  do {                                  \
+    const cudaError_t e_ = (expr);      \
+    if (e_ != cudaSuccess) return e_;   \
+  } while (0)
+
+class LMTrainer {
+ public:
+  SparB200LMConfig cfg;
+  int device = 0;
+  uint64_t V, d, F, L, H, T, B, N, dh, Vp;
+  uint64_t flat = 0;  // parameter floats (with alignment padding)
+  std::vector<NamedTensor> named;
+  std::vector<LayerOffsets> lay;
+  uint64_t off_E = 0, off_lnf_g = 0, off_lnf_b = 0;
+  float *params = nullptr, *grads = nullptr, *m1 = nullptr, *m2 = nullptr;
+  // activations
+  char* act_base = nullptr;
+  std::vector<LayerActs> acts;
+  float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
+  float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
+  float *ln_ws = nullptr, *col_ws = nullptr, *split_ws = nullptr, *rope_tab = nullptr;
+  void* emb_scratch = nullptr;
+  float* row_loss = nullptr;     // [N]
+  float* loss_sums = nullptr;    // [kMaxMicro]
+  double* norm_state = nullptr;  // [kNormStateDoubles]
+  int32_t* flags = nullptr;      // [0] invalid target/id, [1] non-finite grad norm
+  int32_t* ids_dev = nullptr;    // [kMaxMicro * N]
+  static constexpr uint64_t kMaxMicro = 64;
+  void* comm = nullptr;
+  int world = 1;
+  bool last_micro = false;
+  cudaStream_t comm_stream = nullptr;
+  std::vector<cudaEvent_t> layer_ev;
+  cudaEvent_t tail_ev = nullptr, comm_done = nullptr;
+  uint64_t split_floats = 0;
+  // Live profiling of the tensor-core GEMMs (CUDA events around every launch on its stream).
+  bool profiling = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev_pool;
+  size_t ev_used = 0;
+  std::vector<double> ev_flops;
+  uint64_t launches = 0;  // kernels this runtime launched since the counter was reset
+
+  SparCudaStatus init(const SparB200LMConfig& c, int dev);
+  ~LMTrainer();
+  SparCudaStatus forward_backward(const int32_t* ids, float grad_scale, uint64_t micro,
+                                  cudaStream_t s);
+  cudaError_t gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, uint64_t lda, bool at,
+                   const float* b, uint64_t ldb, bool bt, float* c, uint64_t ldc,
+                   bool accumulate, int epi, const float* bias, float* aux, uint64_t ldaux,
+                   cudaStream_t s, int causal = SPAR_B200_CAUSAL_NONE, uint64_t b0 = 1,
+                   uint64_t b1 = 1, const uint64_t* a_bs = nullptr, const uint64_t* b_bs = nullptr,
+                   const uint64_t* c_bs = nullptr);
+  cudaError_t attention_forward(LayerActs& A, cudaStream_t s);
+  cudaError_t layer_backward(uint64_t l, cudaStream_t s);
+};
+
+LMTrainer::~LMTrainer() {
+  DeviceScope scope(device);
+  cudaDeviceSynchronize();
+  for (auto ev : layer_ev) cudaEventDestroy(ev);
+  if (tail_ev) cudaEventDestroy(tail_ev);
+  if (comm_done) cudaEventDestroy(comm_done);
+  if (comm_stream) cudaStreamDestroy(comm_stream);
+  cudaFree(params);
+  cudaFree(act_base);
+}
+
+SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
+  cfg = c;
+  device = dev;
+  V = c.vocab_size;
+  d = c.model_dim;
+  F = c.hidden_dim;
+  L = c.num_layers;
+  H = c.num_heads;
+  T = c.sequence_length;
+  B = c.micro_batch;
+  if (V == 0 || d == 0 || F == 0 || L == 0 || H == 0 || T < 2 || B == 0 || d % H != 0)
+    return invalid();
+  dh = d / H;
+  N = B * T;
+  Vp = (V + 3) / 4 * 4;
+  if (d % 32 != 0 || F % 4 != 0 || dh % 32 != 0 || T % 4 != 0) return invalid();
+  if (c.precision != SPAR_B200_TF32 && c.precision != SPAR_B200_TF32X3) return invalid();
+
+  // ---- parameter arena in Spar's named_parameters order (src/nn/parameters.cpp:51-132)
+  uint64_t o = 0;
+  auto take = [&](uint64_t n) {
+    const uint64_t at = o;
+    o = align_up(o + n);
+    return at;
+  };
+  off_E = take(V * d);
+  named.push_back({"token_embedding.weight", off_E, V, d, d, true});
+  for (uint64_t l = 0; l < L; ++l) {
+    LayerOffsets lo{};
+    lo.begin = o;
+    lo.ln1_g = take(d);
+    lo.ln1_b = take(d);
+    lo.wqkv = take(d * 3 * d);
+    lo.bqkv = take(3 * d);
+    lo.wo = take(d * d);
+    lo.bo = take(d);
+    lo.ln2_g = take(d);
+    lo.ln2_b = take(d);
+    lo.w1 = take(d * F);
+    lo.b1 = take(F);
+    lo.w2 = take(F * d);
+    lo.b2 = take(d);
+    lo.end = o;
+    lay.push_back(lo);
+    const std::string p = "blocks." + std::to_string(l) + ".";
+    named.push_back({p + "attention_norm.weight", lo.ln1_g, d, 0, 0, false});
+    named.push_back({p + "attention_norm.bias", lo.ln1_b, d, 0, 0, false});
+    const char* proj[3] = {"q_proj", "k_proj", "v_proj"};
+    for (int j = 0; j < 3; ++j) {
+      named.push_back({p + "attention." + proj[j] + ".weight", lo.wqkv + j * d, d, d, 3 * d, true});
+      named.push_back({p + "attention." + proj[j] + ".bias", lo.bqkv + j * d, d, 0, 0, false});
+    }
+    named.push_back({p + "attention.out_proj.weight", lo.wo, d, d, d, true});
+    named.push_back({p + "attention.out_proj.bias", lo.bo, d, 0, 0, false});
+    named.push_back({p + "mlp_norm.weight", lo.ln2_g, d, 0, 0, false});
+    named.push_back({p + "mlp_norm.bias", lo.ln2_b, d, 0, 0, false});
+    named.push_back({p + "mlp.up_proj.weight", lo.w1, d, F, F, true});
+    named.push_back({p + "mlp.up_proj.bias", lo.b1, F, 0, 0, false});
+    named.push_back({p + "mlp.down_proj.weight", lo.w2, F, d, d, true});
+    named.push_back({p + "mlp.down_proj.bias", lo.b2, d, 0, 0, false});
+  }
+  off_lnf_g = take(d);
+  off_lnf_b = take(d);
+  named.push_back({"final_norm.weight", off_lnf_g, d, 0, 0, false});
+  named.push_back({"final_norm.bias", off_lnf_b, d, 0, 0, false});
+  flat = o;
+
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&params), 4 * flat * sizeof(float));
+  if (e != cudaSuccess) return runtime(e);
+  grads = params + flat;
+  m1 = grads + flat;
+  m2 = m1 + flat;
+  e = cudaMemset(params, 0, 4 * flat * sizeof(float));
+  if (e != cudaSuccess) return runtime(e);
+
+  // ---- activation arena
+  const uint64_t PS = B * H * T * T;  // one layer's attention probabilities
+  const int ln_parts = layernorm_backward_parts(N, device);
+  const uint64_t max_cols = std::max<uint64_t>(3 * d, F);
+  const int col_parts = column_sum_parts(N, max_cols, device);
+  std::vector<std::pair<void**, uint64_t>> plan;  // (pointer slot, bytes)
+  acts.resize(L);
+  auto f = [&](float** p, uint64_t n) { plan.push_back({reinterpret_cast<void**>(p), n * 4}); };
+  for (uint64_t l = 0; l < L; ++l) {
+    LayerActs& A = acts[l];
+    f(&A.x, N * d);
+    f(&A.mean1, N);
+    f(&A.rstd1, N);
+    f(&A.a1, N * d);
+    f(&A.qkv, N * 3 * d);
+    f(&A.p, PS);
+    f(&A.ctx, N * d);
+    f(&A.h1, N * d);
+    f(&A.mean2, N);
+    f(&A.rstd2, N);
+    f(&A.a2, N * d);
+    f(&A.u, N * F);
+    f(&A.g, N * F);
+  }
+  f(&xL, N * d);
+  f(&meanf, N);
+  f(&rstdf, N);
+  f(&hf, N * d);
+  f(&logits, N * Vp);
+  f(&dres, N * d);
+  f(&dtmp, N * d);
+  f(&dqkv, N * 3 * d);
+  f(&dS, PS);
+  f(&du, N * F);
+  f(&ln_ws, 2ull * ln_parts * d);
+  f(&col_ws, static_cast<uint64_t>(col_parts) * max_cols);
+  f(&rope_tab, T * dh);
+  f(&row_loss, N);
+  f(&loss_sums, kMaxMicro);
+  plan.push_back({reinterpret_cast<void**>(&emb_scratch), embedding_backward_scratch(N, V)});
+  plan.push_back({reinterpret_cast<void**>(&norm_state), kNormStateDoubles * sizeof(double)});
+  plan.push_back({reinterpret_cast<void**>(&flags), 64});
+  plan.push_back({reinterpret_cast<void**>(&ids_dev), kMaxMicro * N * sizeof(int32_t)});
+  if (c.precision == SPAR_B200_TF32X3) {
+    // 3xTF32 splits both operands of every GEMM into hi/lo copies; size the workspace for the
+    // largest of the step's GEMMs (m, n, k, A transposed, B transposed, batch), all listed here.
+    struct Shape { uint64_t m, n, k; int at, bt; uint64_t b0, b1; };
+    const Shape shapes[] = {
+        {N, 3 * d, d, 0, 0, 1, 1},  {T, T, dh, 0, 1, B, H},  {T, dh, T, 0, 0, B, H},
+        {N, d, d, 0, 0, 1, 1},      {N, F, d, 0, 0, 1, 1},   {N, d, F, 0, 0, 1, 1},
+        {N, V, d, 0, 1, 1, 1},      {V, d, N, 1, 0, 1, 1},   {N, d, V, 0, 0, 1, 1},
+        {F, d, N, 1, 0, 1, 1},      {N, F, d, 0, 1, 1, 1},   {d, F, N, 1, 0, 1, 1},
+        {N, d, F, 0, 1, 1, 1},      {d, d, N, 1, 0, 1, 1},   {N, d, d, 0, 1, 1, 1},
+        {T, dh, T, 1, 0, B, H},     {T, T, dh, 0, 1, B, H},  {T, dh, T, 0, 0, B, H},
+        {T, dh, T, 1, 0, B, H},     {d, 3 * d, N, 1, 0, 1, 1}, {N, d, 3 * d, 0, 1, 1, 1},
+    };
+    for (const Shape& sh : shapes) {
+      SparB200Gemm g{};
+      g.m = sh.m; g.n = sh.n; g.k = sh.k; g.a_transposed = sh.at; g.b_transposed = sh.bt;
+      g.batch[0] = sh.b0; g.batch[1] = sh.b1;
+      split_floats = std::max(split_floats, gemm_split_workspace_floats(g));
+    }
+    f(&split_ws, split_floats);
+  }
+  uint64_t total = 0;
+  for (auto& pb : plan) total += (pb.second + 255) / 256 * 256;
+  e = cudaMalloc(reinterpret_cast<void**>(&act_base), total);
+  if (e != cudaSuccess) return runtime(e);
+  uint64_t pos = 0;
+  for (auto& pb : plan) {
+    *pb.first = act_base + pos;
+    pos += (pb.second + 255) / 256 * 256;
+  }
+  e = cudaMemset(flags, 0, 64);
+  if (e == cudaSuccess) e = rope_table_launch(rope_tab, T, dh, c.rope_theta, 0, 0);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return runtime(e);
+  // LayerNorm gamma = 1, beta = 0; biases 0 (BASELINE init, Linear bias init linear.cpp:40-42).
+  for (const auto& t : named)
+    if (t.name.find("norm.weight") != std::string::npos)
+      fill_kernel<<<grid_for(t.rows, 256, 1024), 256>>>(params + t.offset, t.rows, 1.f);
+  e = cudaDeviceSynchronize();
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, uint64_t lda,
+                            bool at, const float* b, uint64_t ldb, bool bt, float* c, uint64_t ldc,
+                            bool accumulate, int epi, const float* bias, float* aux,
+                            uint64_t ldaux, cudaStream_t s, int causal, uint64_t b0, uint64_t b1,
+                            const uint64_t* a_bs, const uint64_t* b_bs, const uint64_t* c_bs) {
+  SparB200Gemm g{};
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.batch[0] = b0;
+  g.batch[1] = b1;
+  g.a = a;
+  g.lda = lda;
+  g.a_transposed = at;
+  g.b = b;
+  g.ldb = ldb;
+  g.b_transposed = bt;
+  g.c = c;
+  g.ldc = ldc;
+  if (a_bs) g.a_batch_stride[0] = a_bs[0], g.a_batch_stride[1] = a_bs[1];
+  if (b_bs) g.b_batch_stride[0] = b_bs[0], g.b_batch_stride[1] = b_bs[1];
+  if (c_bs) g.c_batch_stride[0] = c_bs[0], g.c_batch_stride[1] = c_bs[1];
+  g.alpha = 1.f;
+  g.accumulate = accumulate;
+  g.epilogue = epi;
+  g.bias = bias;
+  g.aux = aux;
+  g.ldaux = ldaux;
+  g.precision = cfg.precision;
+  g.causal = causal;
+  launches += cfg.precision == SPAR_B200_TF32X3 ? 3 : 1;
+  // Never let a split copy run past the workspace sized in init().
+  if (cfg.precision == SPAR_B200_TF32X3 && gemm_split_workspace_floats(g) > split_floats)
+    return cudaErrorInvalidValue;
+  if (!profiling) return gemm_launch(g, split_ws, device, s);
+  if (ev_used == ev_pool.size()) {
+    std::pair<cudaEvent_t, cudaEvent_t> pr;
+    SPAR_TRY_RAW(cudaEventCreate(&pr.first));
+    SPAR_TRY_RAW(cudaEventCreate(&pr.second));
+    ev_pool.push_back(pr);
+  }
+  // Algorithmic FLOPs: 2mnk per batch entry; the causal products do half of that useful work.
+  double fl = 2.0 * m * n * k * b0 * b1;
+  if (causal != SPAR_B200_CAUSAL_NONE) fl *= 0.5;
+  auto& pr = ev_pool[ev_used++];
+  ev_flops.push_back(fl);
+  SPAR_TRY_RAW(cudaEventRecord(pr.first, s));
+  SPAR_TRY_RAW(gemm_launch(g, split_ws, device, s));
+  return cudaEventRecord(pr.second, s);
+}
+
+#define SPAR_TRY(expr)                  \
+  do {                                  \
+    const cudaError_t e_ = (expr);      \
+    if (e_ != cudaSuccess) return e_;   \
+  } while (0)
+
+// S = QK^T (lower tiles), P = causal softmax in place, ctx = P V (k <= row).
+cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
+  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
+  const uint64_t ld = 3 * d;
+  const uint64_t qkv_bs[2] = {T * ld, dh};
+  const uint64_t p_bs[2] = {H * T * T, T * T};
+  const uint64_t ctx_bs[2] = {T * d, dh};
+  const float* q = A.qkv;
+  const float* k = A.qkv + d;
+  const float* v = A.qkv + 2 * d;
+  SPAR_TRY(gemm(T, T, dh, q, ld, false, k, ld, true, A.p, T, false, SPAR_B200_EPI_NONE, nullptr,
+                nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, qkv_bs, qkv_bs, p_bs));
+  SPAR_TRY(causal_softmax_launch(A.p, A.p, nullptr, B * H, T, T, scale, 128, 0, s));
+  SPAR_TRY(gemm(T, dh, T, A.p, T, false, v, ld, false, A.ctx, d, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, qkv_bs, ctx_bs));
+  return cudaSuccess;
+}
+
+SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale, uint64_t micro,
+                                           cudaStream_t s) {
+#define SPAR_CHECK(expr)                              \
+  do {                                                \
+    const cudaError_t e_ = (expr);                    \
+    if (e_ != cudaSuccess) return runtime(e_);        \
+  } while (0)
+  const float eps = static_cast<float>(cfg.norm_epsilon);
+  float* P = params;
+  float* G = grads;
+  // ---------------------------------------------------------------- forward
+  launches += 1;
+  SPAR_CHECK(embedding_forward_launch(acts[0].x, P + off_E, ids, N, V, d, flags, device, s));
+  for (uint64_t l = 0; l < L; ++l) {
+    LayerActs& A = acts[l];
+    const LayerOffsets& lo = lay[l];
+    float* out = l + 1 < L ? acts[l + 1].x : xL;
+    launches += 2 + (cfg.use_rope ? 1 : 0) + 1;  // 2 LayerNorms, rope, softmax
+    SPAR_CHECK(layernorm_forward_launch(A.a1, A.mean1, A.rstd1, A.x, P + lo.ln1_g, P + lo.ln1_b,
+                                        N, d, eps, device, s));
+    SPAR_CHECK(gemm(N, 3 * d, d, A.a1, d, false, P + lo.wqkv, 3 * d, false, A.qkv, 3 * d, false,
+                    SPAR_B200_EPI_BIAS, P + lo.bqkv, nullptr, 0, s));
+    if (cfg.use_rope)  // q and k heads are adjacent: rotate 2H heads of dh at row stride 3d
+      SPAR_CHECK(rope_apply_launch(A.qkv, rope_tab, N, T, 2 * H, dh, 3 * d, 0, device, s));
+    SPAR_CHECK(attention_forward(A, s));
+    SPAR_CHECK(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
+                    SPAR_B200_EPI_BIAS_ADD, P + lo.bo, A.x, d, s));
+    SPAR_CHECK(layernorm_forward_launch(A.a2, A.mean2, A.rstd2, A.h1, P + lo.ln2_g, P + lo.ln2_b,
+                                        N, d, eps, device, s));
+    SPAR_CHECK(gemm(N, F, d, A.a2, d, false, P + lo.w1, F, false, A.g, F, false,
+                    SPAR_B200_EPI_BIAS_GELU, P + lo.b1, A.u, F, s));
+    SPAR_CHECK(gemm(N, d, F, A.g, F, false, P + lo.w2, d, false, out, d, false,
+                    SPAR_B200_EPI_BIAS_ADD, P + lo.b2, A.h1, d, s));
+  }
+  launches += 1 + 2 + 2;  // final LayerNorm, cross-entropy + loss sum, final LayerNorm backward
+  SPAR_CHECK(layernorm_forward_launch(hf, meanf, rstdf, xL, P + off_lnf_g, P + off_lnf_b, N, d,
+                                      eps, device, s));
+  SPAR_CHECK(gemm(N, V, d, hf, d, false, P + off_E, d, true, logits, Vp, false,
+                  SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+  // Fused log-softmax + NLL + mean backward; dlogits overwrite the logits in place.
+  SPAR_CHECK(cross_entropy_launch(row_loss, logits, logits, ids, N, V, Vp, T, grad_scale,
+                                  flags, device, s));
+  SPAR_CHECK(sum_launch(loss_sums + micro, row_loss, N, s));
+  // ---------------------------------------------------------------- backward
+  // dE += dlogits^T hf ; dhf = dlogits E
+  SPAR_CHECK(gemm(V, d, N, logits, Vp, true, hf, d, false, G + off_E, d, true, SPAR_B200_EPI_NONE,
+                  nullptr, nullptr, 0, s));
+  SPAR_CHECK(gemm(N, d, V, logits, Vp, false, P + off_E, d, false, dtmp, d, false,
+                  SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+  SPAR_CHECK(layernorm_backward_launch(dres, G + off_lnf_g, G + off_lnf_b, dtmp, xL,
+                                       P + off_lnf_g, meanf, rstdf, N, d, 1, 0, ln_ws, device, s));
+  for (uint64_t l = L; l-- > 0;) {
+    SPAR_CHECK(layer_backward(l, s));
+  }
+  launches += 5;
+  SPAR_CHECK(embedding_backward_launch(G + off_E, dres, ids, N, V, d, emb_scratch, device, s));
+  if (comm && last_micro) {
+    // Tied embedding and final norm (first and last gradients of the sweep), then join.
+    SPAR_CHECK(cudaEventRecord(tail_ev, s));
+    SPAR_CHECK(cudaStreamWaitEvent(comm_stream, tail_ev, 0));
+    SPAR_CHECK(comm_allreduce_sum(comm, G + off_E, lay[0].begin - off_E, comm_stream));
+    SPAR_CHECK(comm_allreduce_sum(comm, G + off_lnf_g, flat - off_lnf_g, comm_stream));
+    SPAR_CHECK(cudaEventRecord(comm_done, comm_stream));
+    SPAR_CHECK(cudaStreamWaitEvent(s, comm_done, 0));
+  }
+  return ok();
+#undef SPAR_CHECK
+}
+
+cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
+  LayerActs& A = acts[l];
+  const LayerOffsets& lo = lay[l];
+  float* P = params;
+  float* G = grads;
+  launches += 4 * 2 + 2 * 2 + 1 + (cfg.use_rope ? 1 : 0);  // col sums, LN bwd, softmax bwd, rope
+  // dres = dL/d(layer output) = dL/d(h1 + mlp)
+  // MLP: mlp = g W2 + b2, g = gelu(u), u = a2 W1 + b1
+  SPAR_TRY(gemm(F, d, N, A.g, F, true, dres, d, false, G + lo.w2, d, true, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s));
+  SPAR_TRY(column_sum_launch(G + lo.b2, dres, N, d, d, 1, col_ws, device, s));
+  SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, du, F, false, SPAR_B200_EPI_GELU_BWD,
+                nullptr, A.u, F, s));
+  SPAR_TRY(gemm(d, F, N, A.a2, d, true, du, F, false, G + lo.w1, F, true, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s));
+  SPAR_TRY(column_sum_launch(G + lo.b1, du, N, F, F, 1, col_ws, device, s));
+  SPAR_TRY(gemm(N, d, F, du, F, false, P + lo.w1, F, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s));
+  // dres += LN2 backward  ->  dL/dh1
+  SPAR_TRY(layernorm_backward_launch(dres, G + lo.ln2_g, G + lo.ln2_b, dtmp, A.h1, P + lo.ln2_g,
+                                     A.mean2, A.rstd2, N, d, 1, 1, ln_ws, device, s));
+  // out projection: h1 = x + ctx Wo + bo
+  SPAR_TRY(gemm(d, d, N, A.ctx, d, true, dres, d, false, G + lo.wo, d, true, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s));
+  SPAR_TRY(column_sum_launch(G + lo.bo, dres, N, d, d, 1, col_ws, device, s));
+  SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s));
+  // attention core: dtmp = dctx [N, d]
+  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
+  const uint64_t ld = 3 * d;
+  const uint64_t qkv_bs[2] = {T * ld, dh};
+  const uint64_t p_bs[2] = {H * T * T, T * T};
+  const uint64_t ctx_bs[2] = {T * d, dh};
+  const float* q = A.qkv;
+  const float* k = A.qkv + d;
+  const float* v = A.qkv + 2 * d;
+  // dV = P^T dctx (k >= row)
+  SPAR_TRY(gemm(T, dh, T, A.p, T, true, dtmp, d, false, dqkv + 2 * d, ld, false,
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs,
+                ctx_bs, qkv_bs));
+  // dP = dctx V^T (lower tiles), dS = softmax backward (scaled) in place
+  SPAR_TRY(gemm(T, T, dh, dtmp, d, false, v, ld, true, dS, T, false, SPAR_B200_EPI_NONE, nullptr,
+                nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, ctx_bs, qkv_bs, p_bs));
+  SPAR_TRY(causal_softmax_launch(dS, dS, A.p, B * H, T, T, scale, 128, 1, s));
+  // dQ = dS K (k <= row), dK = dS^T Q (k >= row)
+  SPAR_TRY(gemm(T, dh, T, dS, T, false, k, ld, false, dqkv, ld, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, qkv_bs, qkv_bs));
+  SPAR_TRY(gemm(T, dh, T, dS, T, true, q, ld, false, dqkv + d, ld, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs, qkv_bs, qkv_bs));
+  if (cfg.use_rope) SPAR_TRY(rope_apply_launch(dqkv, rope_tab, N, T, 2 * H, dh, ld, 1, device, s));
+  // QKV projection
+  SPAR_TRY(gemm(d, 3 * d, N, A.a1, d, true, dqkv, ld, false, G + lo.wqkv, ld, true,
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+  SPAR_TRY(column_sum_launch(G + lo.bqkv, dqkv, N, 3 * d, ld, 1, col_ws, device, s));
+  SPAR_TRY(gemm(N, d, 3 * d, dqkv, ld, false, P + lo.wqkv, ld, true, dtmp, d, false,
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+  // dres += LN1 backward -> dL/dx
+  SPAR_TRY(layernorm_backward_launch(dres, G + lo.ln1_g, G + lo.ln1_b, dtmp, A.x, P + lo.ln1_g,
+                                     A.mean1, A.rstd1, N, d, 1, 1, ln_ws, device, s));
+  if (comm && last_micro) {
+    // This layer's gradients are final: reduce them on the communication stream while the
+    // remaining layers run backward (bucket = one block's contiguous parameter range).
+    SPAR_TRY(cudaEventRecord(layer_ev[l], s));
+    SPAR_TRY(cudaStreamWaitEvent(comm_stream, layer_ev[l], 0));
+    SPAR_TRY(comm_allreduce_sum(comm, G + lo.begin, lo.end - lo.begin, comm_stream));
+  }
+  return cudaSuccess;
+}
+
+}  // namespace spar_b200
+
+// ===================================================================================== C ABI
+using namespace spar_b200;
+
+namespace {
+LMTrainer* as_trainer(void* h) { return static_cast<LMTrainer*>(h); }
+}  // namespace
+
+extern "C" SparCudaStatus spar_b200_lm_create(const SparB200LMConfig* config, int device,
+                                              void** handle) {
+  if (!config || !handle) return invalid();
+  *handle = nullptr;
+  LMTrainer* t = new LMTrainer();
+  const SparCudaStatus st = t->init(*config, device);
+  if (st.code != 0) {
+    delete t;
+    return st;
+  }
+  *handle = t;
+  return ok();
+}
+
+extern "C" void spar_b200_lm_destroy(void* handle) { delete as_trainer(handle); }
+
+extern "C" uint64_t spar_b200_lm_parameter_count(void* handle) {
+  return handle ? as_trainer(handle)->named.size() : 0;
+}
+
+extern "C" uint64_t spar_b200_lm_flat_size(void* handle) {
+  return handle ? as_trainer(handle)->flat : 0;
+}
+
+extern "C" float* spar_b200_lm_flat_buffer(void* handle, int which) {
+  if (!handle || which < 0 || which > 3) return nullptr;
+  LMTrainer* t = as_trainer(handle);
+  return t->params + static_cast<uint64_t>(which) * t->flat;
+}
+
+extern "C" SparCudaStatus spar_b200_lm_parameter_info(void* handle, uint64_t index, char* name,
+                                                      uint64_t name_capacity, uint64_t* rows,
+                                                      uint64_t* cols) {
+  if (!handle) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  if (index >= t->named.size()) return invalid();
+  const NamedTensor& n = t->named[index];
+  if (name && name_capacity) {
+    std::strncpy(name, n.name.c_str(), name_capacity - 1);
+    name[name_capacity - 1] = 0;
+  }
+  if (rows) *rows = n.rows;
+  if (cols) *cols = n.cols;
+  return ok();
+}
+
+// which: 0 parameter, 1 gradient, 2 first moment, 3 second moment. Synchronous copy of one
+// named tensor between host memory and its (possibly column-strided) place in the arena.
+extern "C" SparCudaStatus spar_b200_lm_parameter_copy(void* handle, uint64_t index, int which,
+                                                      int to_device, float* host) {
+  if (!handle || !host || which < 0 || which > 3) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  if (index >= t->named.size()) return invalid();
+  const NamedTensor& n = t->named[index];
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  float* dev = t->params + static_cast<uint64_t>(which) * t->flat + n.offset;
+  const uint64_t cols = n.cols ? n.cols : n.rows, rows = n.cols ? n.rows : 1;
+  const uint64_t ld = n.cols ? n.ld : n.rows;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) {
+    if (to_device)
+      e = cudaMemcpy2D(dev, ld * 4, host, cols * 4, cols * 4, rows, cudaMemcpyHostToDevice);
+    else
+      e = cudaMemcpy2D(host, cols * 4, dev, ld * 4, cols * 4, rows, cudaMemcpyDeviceToHost);
+  }
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+// Device-side N(0, std) initialisation of every weight matrix and the embedding, drawing from one
+// SplitMix64 stream in named-parameter order (the same stream the CPU oracle uses).
+extern "C" SparCudaStatus spar_b200_lm_init_normal(void* handle, uint64_t seed, double std,
+                                                   void* stream) {
+  if (!handle) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint64_t draws = 0;
+  for (const auto& n : t->named) {
+    if (!n.draws) continue;
+    init_normal_kernel<<<grid_for(n.rows * n.cols, 256, sm_count(t->device) * 16), 256, 0, s>>>(
+        t->params + n.offset, n.rows, n.cols, n.ld, seed, draws, std);
+    draws += 2 * n.rows * n.cols;
+  }
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" SparCudaStatus spar_b200_lm_zero_grad(void* handle, void* stream) {
+  if (!handle) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  const cudaError_t e = cudaMemsetAsync(t->grads, 0, t->flat * sizeof(float),
+                                        static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+// One micro-step: forward, loss, backward; gradients accumulate into the gradient arena.
+// ids: device int32 [micro_batch, sequence_length]. grad_scale = upstream gradient of each row
+// loss (1 / rows of the whole optimiser batch for Spar's mean reduction).
+extern "C" SparCudaStatus spar_b200_lm_forward_backward(void* handle, const int32_t* ids,
+                                                        uint64_t micro_index, float grad_scale,
+                                                        int last_micro, void* stream) {
+  if (!handle || !ids) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  if (micro_index >= LMTrainer::kMaxMicro) return invalid();
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  t->last_micro = last_micro != 0;
+  return t->forward_backward(ids, grad_scale, micro_index, static_cast<cudaStream_t>(stream));
+}
+
+// Global-norm clip + AdamW over every parameter (decoupled decay on all, src/optim/adamw.cpp:
+// 83-170); `step` is the 1-based AdamW step used for bias correction.
+extern "C" SparCudaStatus spar_b200_lm_optimizer_step(void* handle, double learning_rate,
+                                                      uint64_t step, void* stream) {
+  if (!handle || step == 0) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Slice slice{t->params, t->grads, t->m1, t->m2, t->flat};
+  t->launches += 3;
+  cudaError_t e = grad_norm_launch(t->norm_state, &slice, 1, t->device, s);
+  if (e == cudaSuccess)
+    e = adamw_launch(&slice, 1, t->norm_state, t->cfg.max_grad_norm, learning_rate, t->cfg.beta1,
+                     t->cfg.beta2, t->cfg.adam_epsilon, t->cfg.weight_decay, step, t->flags + 1,
+                     t->device, s);
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+// A whole optimiser step: zero gradients, `micro_steps` forward/backward passes over
+// ids[micro_steps, micro_batch, T] (host memory when ids_on_host, copied in this call), the
+// data-parallel gradient reduction when a communicator is attached, clip + AdamW, then a
+// device->host read of the mean loss, the pre-clip gradient norm and the error flags
+// ([0] invalid token/target id, [1] non-finite gradient norm). Synchronises `stream`.
+extern "C" SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* ids,
+                                                  int ids_on_host, uint64_t micro_steps,
+                                                  double learning_rate, uint64_t step,
+                                                  float* loss_out, double* grad_norm_out,
+                                                  int32_t* flags_out, void* stream) {
+  if (!handle || !ids || micro_steps == 0 || micro_steps > LMTrainer::kMaxMicro || step == 0)
+    return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint64_t n_ids = micro_steps * t->N;
+  const int32_t* dev_ids = ids;
+  cudaError_t e = cudaSuccess;
+  if (ids_on_host) {
+    e = cudaMemcpyAsync(t->ids_dev, ids, n_ids * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    dev_ids = t->ids_dev;
+  }
+  if (e == cudaSuccess) e = cudaMemsetAsync(t->grads, 0, t->flat * sizeof(float), s);
+  if (e != cudaSuccess) return runtime(e);
+  const double rows = static_cast<double>(t->B) * static_cast<double>(t->T - 1) *
+                      static_cast<double>(micro_steps) * static_cast<double>(t->world);
+  const float grad_scale = static_cast<float>(1.0 / rows);
+  for (uint64_t m = 0; m < micro_steps; ++m) {
+    t->last_micro = m + 1 == micro_steps;
+    const SparCudaStatus st = t->forward_backward(dev_ids + m * t->N, grad_scale, m, s);
+    if (st.code != 0) return st;
+  }
+  SparCudaStatus st = spar_b200_lm_optimizer_step(handle, learning_rate, step, stream);
+  if (st.code != 0) return st;
+  float sums[LMTrainer::kMaxMicro];
+  double norm_state[2];
+  int32_t flags[2];
+  e = cudaMemcpyAsync(sums, t->loss_sums, micro_steps * sizeof(float), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(norm_state, t->norm_state, 2 * sizeof(double), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(flags, t->flags, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return runtime(e);
+  double total = 0.0;
+  for (uint64_t m = 0; m < micro_steps; ++m) total += sums[m];
+  if (loss_out) *loss_out = static_cast<float>(total / (rows / t->world));
+  if (grad_norm_out) *grad_norm_out = std::sqrt(norm_state[0]);
+  if (flags_out) {
+    flags_out[0] = flags[0];
+    flags_out[1] = flags[1];
+  }
+  return ok();
+}
+
+// Attaches a communicator from spar_b200_comm_init: gradients of each block are then summed
+// across ranks during the last micro-step's backward pass.
+extern "C" SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int world_size) {
+  if (!handle || world_size < 1 || (world_size > 1 && !comm)) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  t->comm = world_size > 1 ? comm : nullptr;
+  t->world = world_size;
+  if (t->comm && !t->comm_stream) {
+    cudaError_t e = cudaStreamCreateWithFlags(&t->comm_stream, cudaStreamNonBlocking);
+    t->layer_ev.resize(t->L);
+    for (auto& ev : t->layer_ev)
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&t->tail_ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&t->comm_done, cudaEventDisableTiming);
+    if (e != cudaSuccess) return runtime(e);
+  }
+  return ok();
+}
+
+// Mean loss of the micro-steps run since the last train step (host read, synchronous).
+extern "C" SparCudaStatus spar_b200_lm_read_losses(void* handle, float* host, uint64_t count) {
+  if (!handle || !host || count > LMTrainer::kMaxMicro) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(host, t->loss_sums, count * 4, cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+// Warmup-cosine learning rate (training::warmup_cosine_learning_rate,
+// src/training/schedule.cpp:9-38). Returns NaN for an invalid configuration.
+extern "C" double spar_b200_warmup_cosine(double peak, double minimum, uint64_t warmup_steps,
+                                          uint64_t decay_steps, uint64_t completed_steps) {
+  if (!std::isfinite(peak) || peak < 0.0 || !std::isfinite(minimum) || minimum < 0.0 ||
+      minimum > peak || decay_steps == 0)
+    return NAN;
+  if (completed_steps < warmup_steps)
+    return peak * static_cast<double>(completed_steps + 1) / static_cast<double>(warmup_steps);
+  const uint64_t idx = completed_steps - warmup_steps;
+  if (idx >= decay_steps || decay_steps == 1) return minimum;
+  const double progress = static_cast<double>(idx) / static_cast<double>(decay_steps - 1);
+  return minimum + 0.5 * (peak - minimum) * (1.0 + std::cos(M_PI * progress));
+}
+
+// Enables (1) or disables (0) event timing of every tensor-core GEMM launch; enabling resets the
+// accumulators and the launch counter.
+extern "C" SparCudaStatus spar_b200_lm_profile(void* handle, int enable) {
+  if (!handle) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  t->profiling = enable != 0;
+  if (enable) {
+    t->ev_used = 0;
+    t->ev_flops.clear();
+    t->launches = 0;
+  }
+  return ok();
+}
+
+// Synchronises, then reports the summed device time (ms) and algorithmic FLOPs of the GEMM
+// launches timed since profiling was enabled, and the number of kernels launched.
+extern "C" SparCudaStatus spar_b200_lm_profile_read(void* handle, double* gemm_ms,
+                                                    double* gemm_flops, uint64_t* gemm_launches,
+                                                    uint64_t* kernel_launches) {
+  if (!handle) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return runtime(e);
+  double ms = 0.0, fl = 0.0;
+  for (size_t i = 0; i < t->ev_used; ++i) {
+    float x = 0.f;
+    e = cudaEventElapsedTime(&x, t->ev_pool[i].first, t->ev_pool[i].second);
+    if (e != cudaSuccess) return runtime(e);
+    ms += x;
+    fl += t->ev_flops[i];
+  }
+  if (gemm_ms) *gemm_ms = ms;
+  if (gemm_flops) *gemm_flops = fl;
+  if (gemm_launches) *gemm_launches = t->ev_used;
+  if (kernel_launches) *kernel_launches = t->launches;
+  return ok();
+}

@@ -1,0 +1,199 @@
+"""Host-side handle for the decoder training runtime in libspar_b200.so.
+
+Mirrors the reference's model/optimiser surface for this path: parameters are addressed by Spar's
+named_parameters names (src/nn/parameters.cpp:51-132), weights are [in, out] as in nn::Linear
+(src/nn/linear.cpp:33-35), and a training step is forward -> LM cross-entropy -> backward ->
+clip_grad_norm -> AdamW (src/training/gradients.cpp:176-190, src/optim/adamw.cpp:83-170) with the
+learning rate from warmup_cosine_learning_rate (src/training/schedule.cpp:9-38). Errors raise
+SparError with the reference's status codes.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import SparB200LMConfig, SparError, check
+
+WHICH = {"param": 0, "grad": 1, "m": 2, "v": 3}
+
+
+@dataclass
+class LMConfig:
+    vocab: int
+    dim: int
+    hidden: int
+    layers: int
+    heads: int
+    seq: int
+    micro_batch: int
+    eps: float = 1e-5
+    rope_theta: float = 10000.0
+    use_rope: bool = True
+    precision: int = 0  # 0 TF32, 1 3xTF32
+    beta1: float = 0.9
+    beta2: float = 0.95
+    adam_eps: float = 1e-8
+    weight_decay: float = 0.1
+    max_grad_norm: float = 1.0
+
+    def oracle_dict(self):
+        return {"vocab": self.vocab, "dim": self.dim, "hidden": self.hidden, "layers": self.layers,
+                "heads": self.heads, "eps": self.eps, "rope_theta": self.rope_theta}
+
+    def opt_dict(self):
+        return {"beta1": self.beta1, "beta2": self.beta2, "eps": self.adam_eps,
+                "weight_decay": self.weight_decay, "max_grad_norm": self.max_grad_norm}
+
+    def flops_per_token(self) -> float:
+        """6 * matmul params + attention (12 * L * d * T, half of it under the causal mask is
+        skipped by the kernels but counted here as the standard estimate)."""
+        n_mm = self.layers * (4 * self.dim * self.dim + 2 * self.dim * self.hidden) + self.vocab * self.dim
+        return 6.0 * n_mm + 12.0 * self.layers * self.dim * self.seq
+
+
+class DecoderLM:
+    """One decoder + optimiser state resident on one GPU."""
+
+    def __init__(self, cfg: LMConfig, device: int = 0):
+        self.cfg = cfg
+        self.device = device
+        self.lib = _lib.load()
+        c = SparB200LMConfig(cfg.vocab, cfg.dim, cfg.hidden, cfg.layers, cfg.heads, cfg.seq,
+                             cfg.micro_batch, cfg.eps, cfg.rope_theta, int(cfg.use_rope),
+                             cfg.precision, cfg.beta1, cfg.beta2, cfg.adam_eps, cfg.weight_decay,
+                             cfg.max_grad_norm)
+        h = ctypes.c_void_p()
+        check("spar_b200_lm_create", self.lib.spar_b200_lm_create(ctypes.byref(c), device,
+                                                                  ctypes.byref(h)))
+        self.handle = h
+        self.names = []
+        self.shapes = {}
+        buf = ctypes.create_string_buffer(256)
+        for i in range(self.lib.spar_b200_lm_parameter_count(h)):
+            r, col = ctypes.c_uint64(), ctypes.c_uint64()
+            check("spar_b200_lm_parameter_info",
+                  self.lib.spar_b200_lm_parameter_info(h, i, buf, 256, ctypes.byref(r), ctypes.byref(col)))
+            name = buf.value.decode()
+            self.names.append(name)
+            self.shapes[name] = (r.value, col.value) if col.value else (r.value,)
+        self.index = {n: i for i, n in enumerate(self.names)}
+        self.step_count = 0
+
+    def close(self):
+        if self.handle:
+            self.lib.spar_b200_lm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------------ parameters
+    def set(self, name: str, value, which: str = "param"):
+        a = np.ascontiguousarray(value, dtype=np.float32)
+        if a.shape != self.shapes[name]:
+            raise ValueError(f"{name}: shape {a.shape} != {self.shapes[name]}")
+        check("spar_b200_lm_parameter_copy",
+              self.lib.spar_b200_lm_parameter_copy(self.handle, self.index[name], WHICH[which], 1,
+                                                   a.ctypes.data))
+
+    def get(self, name: str, which: str = "param") -> np.ndarray:
+        a = np.empty(self.shapes[name], dtype=np.float32)
+        check("spar_b200_lm_parameter_copy",
+              self.lib.spar_b200_lm_parameter_copy(self.handle, self.index[name], WHICH[which], 0,
+                                                   a.ctypes.data))
+        return a
+
+    def load_state_dict(self, params: dict):
+        """nn::load_state_dict equivalent (src/nn/state.cpp:22-54): every name must be present."""
+        missing = set(self.names) - set(params)
+        if missing:
+            raise KeyError(f"missing parameters: {sorted(missing)[:5]}")
+        for n in self.names:
+            self.set(n, params[n])
+
+    def state_dict(self, which: str = "param") -> dict:
+        return {n: self.get(n, which) for n in self.names}
+
+    def init_normal(self, seed: int, std: float = 0.02, stream: int = 0):
+        check("spar_b200_lm_init_normal", self.lib.spar_b200_lm_init_normal(self.handle, seed, std, stream))
+
+    def flat_size(self) -> int:
+        return self.lib.spar_b200_lm_flat_size(self.handle)
+
+    def flat_buffer(self, which: str = "grad") -> int:
+        return self.lib.spar_b200_lm_flat_buffer(self.handle, WHICH[which])
+
+    def profile(self, enable: bool):
+        check("spar_b200_lm_profile", self.lib.spar_b200_lm_profile(self.handle, int(enable)))
+
+    def profile_read(self):
+        """(gemm_ms, gemm_flops, gemm_launches, kernel_launches) since profiling was enabled."""
+        ms, fl = ctypes.c_double(), ctypes.c_double()
+        gl, kl = ctypes.c_uint64(), ctypes.c_uint64()
+        check("spar_b200_lm_profile_read",
+              self.lib.spar_b200_lm_profile_read(self.handle, ctypes.byref(ms), ctypes.byref(fl),
+                                                 ctypes.byref(gl), ctypes.byref(kl)))
+        return ms.value, fl.value, gl.value, kl.value
+
+    # ------------------------------------------------------------------ training
+    def attach_comm(self, comm, world_size: int):
+        check("spar_b200_lm_set_comm", self.lib.spar_b200_lm_set_comm(self.handle, comm, world_size))
+
+    def train_step(self, ids, lr: float, step: int | None = None, stream: int = 0):
+        """ids: int32 array [micro_steps, micro_batch, seq] in host memory (numpy or pinned
+        torch tensor), or a CUDA int32 tensor of that shape. Returns (loss, grad_norm, flags)."""
+        if step is None:
+            step = self.step_count + 1
+        on_host = 1
+        if hasattr(ids, "is_cuda"):
+            on_host = 0 if ids.is_cuda else 1
+            ptr = ids.data_ptr()
+            micro = ids.shape[0]
+            if ids.dtype.__repr__() != "torch.int32":
+                raise ValueError("ids must be int32")
+        else:
+            ids = np.ascontiguousarray(ids, dtype=np.int32)
+            ptr = ids.ctypes.data
+            micro = ids.shape[0]
+        loss = ctypes.c_float()
+        norm = ctypes.c_double()
+        flags = (ctypes.c_int32 * 2)()
+        check("spar_b200_lm_train_step",
+              self.lib.spar_b200_lm_train_step(self.handle, ptr, on_host, micro, lr, step,
+                                               ctypes.byref(loss), ctypes.byref(norm), flags, stream))
+        self.step_count = step
+        return loss.value, norm.value, (flags[0], flags[1])
+
+
+def warmup_cosine(peak: float, minimum: float, warmup: int, decay: int, step: int) -> float:
+    v = _lib.load().spar_b200_warmup_cosine(peak, minimum, warmup, decay, step)
+    if v != v:
+        raise ValueError("invalid warmup-cosine configuration")
+    return v
+
+
+C1 = LMConfig(vocab=256, dim=128, hidden=512, layers=2, heads=4, seq=64, micro_batch=8)
+C4 = LMConfig(vocab=50257, dim=768, hidden=3072, layers=12, heads=12, seq=1024, micro_batch=8)
+C5 = LMConfig(vocab=32768, dim=1024, hidden=4096, layers=24, heads=16, seq=1024, micro_batch=16)
+
+
+def smoke_step(device) -> None:
+    """One tiny training step on `device` (the flagship path end to end); raises on failure."""
+    import torch
+
+    cfg = LMConfig(vocab=256, dim=128, hidden=256, layers=1, heads=4, seq=32, micro_batch=2)
+    lm = DecoderLM(cfg, device.index or 0)
+    lm.init_normal(1234)
+    rng = np.random.default_rng(0)
+    ids = rng.integers(0, cfg.vocab, (1, cfg.micro_batch, cfg.seq)).astype(np.int32)
+    loss, norm, flags = lm.train_step(ids, 3e-4)
+    torch.cuda.synchronize()
+    if not (np.isfinite(loss) and np.isfinite(norm)) or flags != (0, 0):
+        raise SparError("smoke", _lib.SparCudaStatus(2, 0))
+    lm.close()

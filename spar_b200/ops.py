@@ -15,7 +15,7 @@ from . import _lib
 from ._lib import SparB200Gemm, SparB200TensorSlice, call
 
 TF32, TF32X3 = 0, 1
-EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_GELU_BWD = 0, 1, 2, 3
+EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_GELU_BWD, EPI_BIAS_ADD = 0, 1, 2, 3, 4
 CAUSAL_NONE, CAUSAL_LOWER, CAUSAL_K_UPTO, CAUSAL_K_FROM = 0, 1, 2, 3
 NORM_STATE_DOUBLES = 1024
 

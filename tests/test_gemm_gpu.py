@@ -82,6 +82,9 @@ def test_gemm_epilogues(cuda):
     dpre = ops.matmul(at, bt, epilogue=ops.EPI_GELU_BWD, aux=pre, precision=prec)
     acc = torch.ones(m, n, device=cuda)
     ops.matmul(at, bt, out=acc, accumulate=True, precision=prec)
+    resid = torch.randn(m, n, device=cuda)
+    radd = ops.matmul(at, bt, epilogue=ops.EPI_BIAS_ADD, bias=biast, aux=resid, precision=prec)
+    radd_nb = ops.matmul(at, bt, epilogue=ops.EPI_BIAS_ADD, aux=resid, precision=prec)
     torch.cuda.synchronize()
     pre_ref = ref + bias
     assert rel_err(c.cpu().numpy(), 0.5 * ref + bias) <= 1e-5
@@ -90,6 +93,9 @@ def test_gemm_epilogues(cuda):
     pre32 = pre.cpu().numpy()
     assert rel_err(dpre.cpu().numpy(), ref * O.gelu_derivative(pre32)) <= 1e-5
     assert rel_err(acc.cpu().numpy(), ref + 1.0) <= 1e-5
+    r = resid.cpu().numpy().astype(np.float64)
+    assert rel_err(radd.cpu().numpy(), ref + bias + r) <= 1e-5
+    assert rel_err(radd_nb.cpu().numpy(), ref + r) <= 1e-5
 
 
 def _attention_views(cuda, b, h, t, dh, seed=0):

@@ -1,0 +1,138 @@
+"""One full training step of the decoder (forward, LM cross-entropy, backward, clip, AdamW)
+through the C ABI, against the CPU oracle on identical seeded weights and ids.
+
+Tolerances (gradient and parameter relative L2 error after one step): <= 1e-5 in 3xTF32 mode,
+<= 2e-3 in TF32 mode; loss relative error at the same bars.
+"""
+import numpy as np
+import pytest
+
+from _util import rel_l2
+from oracle import spar_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SEED_W, SEED_IDS = 0x5EED0001, 0x5EED1001
+
+
+def _setup(cfg, micro_steps, seed_w=SEED_W):
+    params = O.init_parameters(cfg.oracle_dict(), seed_w)
+    rng = O.Random(SEED_IDS)
+    ids = rng.bounded(micro_steps * cfg.micro_batch * cfg.seq, cfg.vocab)
+    return params, ids.reshape(micro_steps, cfg.micro_batch, cfg.seq).astype(np.int32)
+
+
+def _run(cfg, micro_steps, lr=3e-4):
+    from spar_b200.lm import DecoderLM
+
+    params, ids = _setup(cfg, micro_steps)
+    lm = DecoderLM(cfg, 0)
+    lm.load_state_dict(params)
+    loss, norm, flags = lm.train_step(ids, lr, step=1)
+    grads = lm.state_dict("grad")
+    new = lm.state_dict("param")
+    lm.close()
+    o_loss, o_grads, o_new, _ = O.lm_train_step(params, {}, list(ids), cfg.oracle_dict(), 1, lr,
+                                                cfg.opt_dict())
+    return (loss, norm, flags, grads, new), (o_loss, o_grads, o_new)
+
+
+def _flat(d, names):
+    return np.concatenate([np.asarray(d[n], np.float64).ravel() for n in names])
+
+
+@pytest.mark.parametrize("precision,tol", [(1, 1e-5), (0, 2e-3)])
+def test_c1_one_step_parity(cuda, precision, tol):
+    from spar_b200.lm import C1
+    from dataclasses import replace
+
+    cfg = replace(C1, precision=precision)
+    (loss, norm, flags, grads, new), (o_loss, o_grads, o_new) = _run(cfg, 1)
+    names = list(o_grads)
+    assert flags == (0, 0)
+    assert abs(loss - o_loss) <= tol * abs(o_loss)
+    assert abs(norm - O.global_grad_norm([o_grads[n] for n in names])) <= tol * norm
+    assert rel_l2(_flat(grads, names), _flat(o_grads, names)) <= tol
+    for n in names:  # every tensor, including biases and LayerNorm parameters
+        assert rel_l2(grads[n], o_grads[n]) <= 10 * tol, n
+    assert rel_l2(_flat(new, names), _flat(o_new, names)) <= tol
+
+
+def test_gradient_accumulation_over_micro_steps(cuda):
+    """Two micro-steps accumulate on the device to the gradient of the mean loss."""
+    from spar_b200.lm import C1
+    from dataclasses import replace
+
+    cfg = replace(C1, precision=1, micro_batch=4)
+    (loss, norm, flags, grads, new), (o_loss, o_grads, o_new) = _run(cfg, 2)
+    names = list(o_grads)
+    assert flags == (0, 0)
+    assert abs(loss - o_loss) <= 1e-5 * abs(o_loss)
+    assert rel_l2(_flat(grads, names), _flat(o_grads, names)) <= 1e-5
+
+
+def test_device_init_matches_oracle_stream(cuda):
+    from spar_b200.lm import C1, DecoderLM
+
+    lm = DecoderLM(C1, 0)
+    lm.init_normal(SEED_W, 0.02)
+    got = lm.state_dict()
+    lm.close()
+    ref = O.init_parameters(C1.oracle_dict(), SEED_W)
+    for n in ref:
+        np.testing.assert_allclose(got[n], ref[n], rtol=1e-6, atol=1e-9, err_msg=n)
+
+
+def test_steps_are_deterministic(cuda):
+    from spar_b200.lm import C1, DecoderLM
+
+    params, ids = _setup(C1, 1)
+    outs = []
+    for _ in range(2):
+        lm = DecoderLM(C1, 0)
+        lm.load_state_dict(params)
+        for step in range(1, 3):
+            lm.train_step(ids, 3e-4, step=step)
+        outs.append(_flat(lm.state_dict(), lm.names))
+        lm.close()
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_invalid_token_sets_flag(cuda):
+    from spar_b200.lm import C1, DecoderLM
+
+    params, ids = _setup(C1, 1)
+    ids[0, 0, 5] = C1.vocab + 3
+    lm = DecoderLM(C1, 0)
+    lm.load_state_dict(params)
+    _, _, flags = lm.train_step(ids, 3e-4, step=1)
+    lm.close()
+    assert flags[0] == 1
+
+
+def test_nonfinite_gradient_skips_update(cuda):
+    """clip_grad_norm throws on a non-finite norm before any parameter changes
+    (src/training/gradients.cpp:181-183); the fused kernel reports it and updates nothing."""
+    from spar_b200.lm import C1, DecoderLM
+
+    params, ids = _setup(C1, 1)
+    bad = dict(params)
+    w = bad["blocks.0.mlp.up_proj.weight"].copy()
+    w[3, 7] = np.nan
+    bad["blocks.0.mlp.up_proj.weight"] = w
+    lm = DecoderLM(C1, 0)
+    lm.load_state_dict(bad)
+    _, norm, flags = lm.train_step(ids, 3e-4, step=1)
+    after = lm.state_dict()
+    lm.close()
+    assert flags[1] == 1 and not np.isfinite(norm)
+    for n in params:
+        np.testing.assert_array_equal(after[n], bad[n])
+
+
+def test_warmup_cosine_matches_reference_schedule():
+    from spar_b200.lm import warmup_cosine
+
+    for s in [0, 1, 50, 99, 100, 101, 500, 998, 999, 1000, 5000]:
+        assert warmup_cosine(3e-4, 3e-5, 100, 900, s) == pytest.approx(
+            O.warmup_cosine(3e-4, 3e-5, 100, 900, s), rel=1e-15, abs=0)
