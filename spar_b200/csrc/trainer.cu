@@ -233,8 +233,11 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   // ---- activation arena
   const uint64_t PS = B * H * T * T;  // one layer's attention probabilities
   const int ln_parts = layernorm_backward_parts(N, device);
-  const uint64_t max_cols = std::max<uint64_t>(3 * d, F);
-  const int col_parts = column_sum_parts(N, max_cols, device);
+  // Column-sum partials: the partition count depends on the width, so take the largest
+  // parts x cols over the widths reduced in the backward pass (d, 3d, F).
+  uint64_t col_floats = 0;
+  for (uint64_t w : {d, 3 * d, F})
+    col_floats = std::max<uint64_t>(col_floats, static_cast<uint64_t>(column_sum_parts(N, w, device)) * w);
   std::vector<std::pair<void**, uint64_t>> plan;  // (pointer slot, bytes)
   acts.resize(L);
   auto f = [&](float** p, uint64_t n) { plan.push_back({reinterpret_cast<void**>(p), n * 4}); };
@@ -265,7 +268,7 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   f(&dS, PS);
   f(&du, N * F);
   f(&ln_ws, 2ull * ln_parts * d);
-  f(&col_ws, static_cast<uint64_t>(col_parts) * max_cols);
+  f(&col_ws, col_floats);
   f(&rope_tab, T * dh);
   f(&row_loss, N);
   f(&loss_sums, kMaxMicro);
