@@ -43,6 +43,18 @@ struct SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma, flo
                                                    int accumulate_params, int accumulate_dx,
                                                    int device, void* stream);
 
+/* Allocation-free LayerNorm backward: same arguments and results as                            */
+/* spar_b200_layernorm_backward, for callers that cannot allocate device memory at call time.   */
+/* No counterpart in the reference (Spar's ops allocate their outputs and scratch per call).    */
+/* Scratch is a static device array shared by all calls: cols <= 2048, at most 296 partial rows */
+/* (4.85 MB per GPU, held until exit); rejects larger sizes with code 1. The first call on a    */
+/* device looks up the array's address (make it before any stream capture); calls that overlap */
+/* on the GPU race and must be serialised by the caller.                                        */
+struct SparCudaStatus spar_b200_layernorm_backward_noalloc(
+    float* dx, float* dgamma, float* dbeta, const float* dy, const float* x, const float* gamma,
+    const float* mean, const float* rstd, uint64_t rows, uint64_t cols, int accumulate_params,
+    int accumulate_dx, int device, void* stream);
+
 /* ------------------------------------------------------------------------------------------ */
 /* GELU, tanh form: gelu(x) = x * sigmoid(2*sqrt(2/pi)*(x + 0.044715 x^3)), the identity that  */
 /* writes the tanh form with Spar's stable sigmoid (src/ops/unary.cpp:137-148).                 */

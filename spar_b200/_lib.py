@@ -55,6 +55,7 @@ SIGNATURES = {
     # ---- new asynchronous entry points (include/spar_b200.h)
     "spar_b200_layernorm_forward": (S, [p, p, p, p, p, p, u64, u64, d, i, p]),
     "spar_b200_layernorm_backward": (S, [p, p, p, p, p, p, p, p, u64, u64, i, i, i, p]),
+    "spar_b200_layernorm_backward_noalloc": (S, [p, p, p, p, p, p, p, p, u64, u64, i, i, i, p]),
     "spar_b200_gelu_forward": (S, [p, p, u64, i, p]),
     "spar_b200_gelu_backward": (S, [p, p, p, u64, i, p]),
     "spar_b200_causal_softmax_forward": (S, [p, p, u64, u64, u64, f, u64, i, p]),

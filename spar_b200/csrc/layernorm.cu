@@ -14,6 +14,8 @@
 // accumulated per lane in registers, reduced over the block's warps in shared memory and written
 // as one partial row per block; a second kernel sums the partials in block order
 // (deterministic, no atomics).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace spar_b200 {
@@ -327,4 +329,71 @@ extern "C" SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma,
   const cudaError_t f = cudaFreeAsync(workspace, s);
   if (e != cudaSuccess) return runtime(e);
   return f == cudaSuccess ? ok() : runtime(f);
+}
+
+// ============================================================== allocation-free backward
+// Variant of spar_b200_layernorm_backward for callers that cannot allocate device memory at call
+// time (for example a host whose device memory is reserved up front by its own allocator, or a
+// step loop that must not allocate because an allocation can fail or stall in the middle of a
+// step). The per-block dgamma/dbeta partial rows live in the file-scope array below instead of a
+// stream-ordered allocation. Limits: cols <= 2048 (the kernel's own limit) and at most 296
+// partial rows (two per SM on a 148-SM B200), i.e. 2 * 296 * 2048 floats = 4.85 MB that every GPU
+// which loads this library holds until the process exits.
+namespace spar_b200 {
+namespace {
+
+constexpr uint64_t kNoAllocMaxCols = 2048;
+constexpr int kNoAllocMaxParts = 296;
+static __device__ __align__(256) float g_ln_backward_scratch[2ull * kNoAllocMaxParts * kNoAllocMaxCols];
+
+std::mutex g_scratch_mutex;
+float* g_scratch_address[64] = {};  // device address of g_ln_backward_scratch, per device
+
+// Host code cannot pass &g_ln_backward_scratch to a kernel (on the host that name is only a
+// stand-in); the device address is looked up once per device, with that device current.
+cudaError_t scratch_address(int device, float** out) {
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_ln_backward_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_address[device] = static_cast<float*>(p);
+  }
+  *out = g_scratch_address[device];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace spar_b200
+
+// Same arguments and results as spar_b200_layernorm_backward; allocates nothing.
+// The first call on a device looks up the scratch address (make that first call before any
+// stream capture). All calls share one scratch array, so calls that overlap on the GPU (two
+// streams, or two host threads on one device) race; serialise them. The array keeps the previous
+// call's partials, which is harmless: every partial row a call reads is written earlier in the
+// same call, so nothing has to start at zero.
+extern "C" SparCudaStatus spar_b200_layernorm_backward_noalloc(
+    float* dx, float* dgamma, float* dbeta, const float* dy, const float* x, const float* gamma,
+    const float* mean, const float* rstd, uint64_t rows, uint64_t cols, int accumulate_params,
+    int accumulate_dx, int device, void* stream) {
+  if (cols == 0 || cols % 4 != 0 || !dgamma || !dbeta || !gamma) return invalid();
+  if (cols > kNoAllocMaxCols) return invalid();  // beyond the static scratch size
+  if (rows != 0 && (!dx || !dy || !x || !mean || !rstd)) return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (accumulate_params) return ok();
+    cudaError_t e = cudaMemsetAsync(dgamma, 0, cols * sizeof(float), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dbeta, 0, cols * sizeof(float), s);
+    return e == cudaSuccess ? ok() : runtime(e);
+  }
+  if (layernorm_backward_parts(rows, device) > kNoAllocMaxParts) return invalid();
+  float* scratch = nullptr;
+  cudaError_t e = scratch_address(device, &scratch);
+  if (e != cudaSuccess) return runtime(e);
+  e = layernorm_backward_launch(dx, dgamma, dbeta, dy, x, gamma, mean, rstd, rows, cols,
+                                accumulate_params, accumulate_dx, scratch, device, s);
+  return e == cudaSuccess ? ok() : runtime(e);
 }
