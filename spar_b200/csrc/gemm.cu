@@ -19,7 +19,9 @@
 // 3xTF32 ("fp32-faithful") mode: A = Ah + Al, B = Bh + Bl with Ah = A rounded to TF32 and
 // Al = A - Ah rounded to TF32; the kernel runs over three K sections reading (Ah,Bh), (Ah,Bl),
 // (Al,Bh) from split copies made by a streaming kernel, so A*B ~ Ah*Bh + Ah*Bl + Al*Bh
-// (error-compensated TF32, Ootomo & Yokota 2022) into one fp32 accumulator.
+// (error-compensated TF32, Ootomo & Yokota 2022). The tensor cores' fp32 accumulation rounds
+// toward zero, so this mode accumulates in chunks of 128 K elements per TMEM accumulator and
+// sums the chunks in registers with round-to-nearest adds.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -56,6 +58,7 @@ struct GemmParams {
   const float* bias;
   float alpha;
   int accumulate, epilogue, causal;
+  uint32_t kchunk;  // k-blocks per accumulation chunk (chunked kernels only)
 };
 
 struct TileCoord {
@@ -97,7 +100,83 @@ __device__ __forceinline__ void k_range(const GemmParams& p, uint32_t mt, uint32
 
 __device__ __forceinline__ void record_error() { atomicExch(&g_gemm_error, 1); }
 
-template <int BN, int STAGES>
+// Applies alpha, the epilogue and the accumulate flag to 32 consecutive accumulator columns of
+// one row and stores them (128-bit accesses where the row end allows).
+__device__ __forceinline__ void store_row32(const GemmParams& p, const float* acc32, uint32_t col0,
+                                            float* crow, float* arow) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const uint32_t col = col0 + j;
+    if (col >= p.n) break;
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = p.alpha * acc32[j + e];
+    const bool full4 = col + 3 < p.n;
+    if (p.bias && (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU ||
+                   p.epilogue == SPAR_B200_EPI_BIAS_ADD)) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (col + e < p.n) v[e] += p.bias[col + e];
+    }
+    if (p.epilogue == SPAR_B200_EPI_BIAS_ADD) {
+      if (full4) {
+        const float4 q = *reinterpret_cast<const float4*>(arow + col);
+        v[0] += q.x;
+        v[1] += q.y;
+        v[2] += q.z;
+        v[3] += q.w;
+      } else {
+        for (int e = 0; e < 4; ++e)
+          if (col + e < p.n) v[e] += arow[col + e];
+      }
+    }
+    if (p.epilogue == SPAR_B200_EPI_BIAS_GELU) {
+      if (full4) {
+        *reinterpret_cast<float4*>(arow + col) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+        for (int e = 0; e < 4; ++e)
+          if (col + e < p.n) arow[col + e] = v[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = gelu_value(v[e]);
+    } else if (p.epilogue == SPAR_B200_EPI_GELU_BWD) {
+      float pre[4] = {0.f, 0.f, 0.f, 0.f};
+      if (full4) {
+        const float4 q = *reinterpret_cast<const float4*>(arow + col);
+        pre[0] = q.x;
+        pre[1] = q.y;
+        pre[2] = q.z;
+        pre[3] = q.w;
+      } else {
+        for (int e = 0; e < 4; ++e)
+          if (col + e < p.n) pre[e] = arow[col + e];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] *= gelu_derivative(pre[e]);
+    }
+    if (full4) {
+      float4* dst = reinterpret_cast<float4*>(crow + col);
+      if (p.accumulate) {
+        const float4 o = *dst;
+        v[0] += o.x;
+        v[1] += o.y;
+        v[2] += o.z;
+        v[3] += o.w;
+      }
+      *dst = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      for (int e = 0; e < 4; ++e)
+        if (col + e < p.n) crow[col + e] = p.accumulate ? crow[col + e] + v[e] : v[e];
+    }
+  }
+}
+
+// CHUNKED (3xTF32): the tile's K range is accumulated in chunks of p.kchunk k-blocks, each chunk
+// into a fresh TMEM accumulator that the epilogue adds into fp32 registers with round-to-nearest
+// adds. The tensor cores' own accumulation rounds toward zero, so long hardware-accumulated
+// sums drift; chunking bounds that drift to one chunk, which keeps the split mode fp32-faithful
+// at any K.
+template <int BN, int STAGES, bool CHUNKED>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_constant__ GemmParams p) {
   constexpr uint32_t A_BYTES = BM * BK * 4;
   constexpr uint32_t B_BYTES = BN * BK * 4;
@@ -158,8 +237,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         uint32_t kb0, kb1;
         k_range(p, t.mt, kb0, kb1);
         const int m0 = static_cast<int>(t.mt * BM), n0 = static_cast<int>(t.nt * BN);
-        for (int sec = 0; sec < p.sections; ++sec) {
-          for (uint32_t kb = kb0; kb < kb1; ++kb) {
+        for (uint32_t kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
+          const int k0 = static_cast<int>(kb * BK);
+          for (int sec = 0; sec < p.sections; ++sec) {
             if (!tc::mbar_wait(empty + stage, phase ^ 1)) {
               record_error();
               *abort_flag = 1;
@@ -169,7 +249,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
             uint8_t* b_s = a_s + A_BYTES;
             tc::mbar_arrive_expect_tx(full + stage, STAGE_BYTES);
             last_phase[stage] = static_cast<int>(phase);
-            const int k0 = static_cast<int>(kb * BK);
             if (p.a_mn_major) {
 #pragma unroll
               for (int j = 0; j < BM / 32; ++j)
@@ -191,7 +270,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
               phase ^= 1;
             }
           }
-          if (*abort_flag) break;
         }
       }
       // Every copy issued into a slot must have landed before the CTA exits (this matters only
@@ -212,51 +290,55 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         if (!decode_tile<BN>(p, idx, t)) continue;
         uint32_t kb0, kb1;
         k_range(p, t.mt, kb0, kb1);
-        if (!tc::mbar_wait(tempty + acc, acc_phase ^ 1)) {
-          record_error();
-          *abort_flag = 1;
-          break;
-        }
-        tc::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        uint32_t issued = 0;
-        for (int sec = 0; sec < p.sections && !*abort_flag; ++sec) {
-          for (uint32_t kb = kb0; kb < kb1; ++kb) {
-            if (!tc::mbar_wait(full + stage, phase)) {
-              record_error();
-              *abort_flag = 1;
-              break;
-            }
-            tc::tc_fence_after();
-            const uint32_t a_addr = tc::smem_u32(smem + stage * STAGE_BYTES);
-            const uint32_t b_addr = a_addr + A_BYTES;
+        const uint32_t chunk = CHUNKED ? p.kchunk : (kb1 - kb0);
+        for (uint32_t c0 = kb0; c0 < kb1 && !*abort_flag; c0 += chunk) {
+          const uint32_t c1 = min(c0 + chunk, kb1);
+          if (!tc::mbar_wait(tempty + acc, acc_phase ^ 1)) {
+            record_error();
+            *abort_flag = 1;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * BN;
+          uint32_t issued = 0;
+          for (uint32_t kb = c0; kb < c1 && !*abort_flag; ++kb) {
+            for (int sec = 0; sec < p.sections; ++sec) {
+              if (!tc::mbar_wait(full + stage, phase)) {
+                record_error();
+                *abort_flag = 1;
+                break;
+              }
+              tc::tc_fence_after();
+              const uint32_t a_addr = tc::smem_u32(smem + stage * STAGE_BYTES);
+              const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-            for (int ks = 0; ks < BK / 8; ++ks) {
-              // K-major: 8 rows of 128 B per 1024 B atom, K step = 32 B inside the row.
-              // MN-major: 32-element MN chunks (one TMA box of 32 K-rows = 4 KB) at LBO, 4-row
-              // K groups at SBO = 512 B, K step = 8 rows = 1024 B.
-              const uint64_t a_desc =
-                  p.a_mn_major
-                      ? tc::smem_desc(a_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
-                      : tc::smem_desc(a_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
-              const uint64_t b_desc =
-                  p.b_mn_major
-                      ? tc::smem_desc(b_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
-                      : tc::smem_desc(b_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
-              tc::mma_tf32(d_tmem, a_desc, b_desc, idesc, (issued | ks) != 0 ? 1u : 0u);
-            }
-            issued = 1;
-            tc::mma_commit(empty + stage);
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1;
+              for (int ks = 0; ks < BK / 8; ++ks) {
+                // K-major: 8 rows of 128 B per 1024 B atom, K step = 32 B inside the row.
+                // MN-major: 32-element MN chunks (one TMA box of 32 K-rows = 4 KB) at LBO, 4-row
+                // K groups at SBO = 512 B, K step = 8 rows = 1024 B.
+                const uint64_t a_desc =
+                    p.a_mn_major
+                        ? tc::smem_desc(a_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                        : tc::smem_desc(a_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
+                const uint64_t b_desc =
+                    p.b_mn_major
+                        ? tc::smem_desc(b_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                        : tc::smem_desc(b_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
+                tc::mma_tf32(d_tmem, a_desc, b_desc, idesc, (issued | ks) != 0 ? 1u : 0u);
+              }
+              issued = 1;
+              tc::mma_commit(empty + stage);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
             }
           }
-        }
-        tc::mma_commit(tfull + acc);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1;
+          tc::mma_commit(tfull + acc);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
         }
       }
       // Make sure every MMA has retired before TMEM is released.
@@ -272,96 +354,76 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
       TileCoord t;
       if (!decode_tile<BN>(p, idx, t)) continue;
       if (*abort_flag) break;
-      if (!tc::mbar_wait(tfull + acc, acc_phase)) {
-        record_error();
-        *abort_flag = 1;
-        break;
-      }
-      tc::tc_fence_after();
       const uint32_t row = t.mt * BM + quarter * 32 + lane;
       const bool row_ok = row < p.m;
       float* crow = p.c + t.b0 * p.c_bs0 + t.b1 * p.c_bs1 + static_cast<uint64_t>(row) * p.ldc;
       float* arow = p.aux ? p.aux + t.b0 * p.c_bs0 + t.b1 * p.c_bs1 +
                                 static_cast<uint64_t>(row) * p.ldaux
                           : nullptr;
+      const uint32_t lane_base = tmem_base + ((quarter * 32) << 16);
+      if constexpr (!CHUNKED) {
+        if (!tc::mbar_wait(tfull + acc, acc_phase)) {
+          record_error();
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
 #pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
-        uint32_t r[32];
-        tc::tmem_load_32x32(tmem_base + ((quarter * 32) << 16) + acc * BN + chunk * 32, r);
-        const uint32_t col0 = t.nt * BN + chunk * 32;
-        if (!row_ok || col0 >= p.n) continue;
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          uint32_t r[32];
+          tc::tmem_load_32x32(lane_base + acc * BN + chunk * 32, r);
+          const uint32_t col0 = t.nt * BN + chunk * 32;
+          if (!row_ok || col0 >= p.n) continue;
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const uint32_t col = col0 + j;
-          if (col >= p.n) break;
-          float v[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) v[e] = p.alpha * __uint_as_float(r[j + e]);
-          const bool full4 = col + 3 < p.n;
-          if (p.bias && (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU ||
-                         p.epilogue == SPAR_B200_EPI_BIAS_ADD)) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (col + e < p.n) v[e] += p.bias[col + e];
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+          store_row32(p, v, col0, crow, arow);
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(tempty + acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      } else {
+        uint32_t kb0, kb1;
+        k_range(p, t.mt, kb0, kb1);
+        float sum[BN];
+        bool ok = true;
+        for (uint32_t c0 = kb0; c0 < kb1; c0 += p.kchunk) {
+          if (!tc::mbar_wait(tfull + acc, acc_phase)) {
+            record_error();
+            *abort_flag = 1;
+            ok = false;
+            break;
           }
-          if (p.epilogue == SPAR_B200_EPI_BIAS_ADD) {
-            if (full4) {
-              const float4 q = *reinterpret_cast<const float4*>(arow + col);
-              v[0] += q.x;
-              v[1] += q.y;
-              v[2] += q.z;
-              v[3] += q.w;
-            } else {
-              for (int e = 0; e < 4; ++e)
-                if (col + e < p.n) v[e] += arow[col + e];
-            }
-          }
-          if (p.epilogue == SPAR_B200_EPI_BIAS_GELU) {
-            if (full4) {
-              *reinterpret_cast<float4*>(arow + col) = make_float4(v[0], v[1], v[2], v[3]);
-            } else {
-              for (int e = 0; e < 4; ++e)
-                if (col + e < p.n) arow[col + e] = v[e];
-            }
+          tc::tc_fence_after();
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[e] = gelu_value(v[e]);
-          } else if (p.epilogue == SPAR_B200_EPI_GELU_BWD) {
-            float pre[4] = {0.f, 0.f, 0.f, 0.f};
-            if (full4) {
-              const float4 q = *reinterpret_cast<const float4*>(arow + col);
-              pre[0] = q.x;
-              pre[1] = q.y;
-              pre[2] = q.z;
-              pre[3] = q.w;
-            } else {
-              for (int e = 0; e < 4; ++e)
-                if (col + e < p.n) pre[e] = arow[col + e];
-            }
+          for (int chunk = 0; chunk < BN / 32; ++chunk) {
+            uint32_t r[32];
+            tc::tmem_load_32x32(lane_base + acc * BN + chunk * 32, r);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[e] *= gelu_derivative(pre[e]);
+            for (int e = 0; e < 32; ++e)
+              sum[chunk * 32 + e] = c0 == kb0 ? __uint_as_float(r[e])
+                                              : sum[chunk * 32 + e] + __uint_as_float(r[e]);
           }
-          if (full4) {
-            float4* dst = reinterpret_cast<float4*>(crow + col);
-            if (p.accumulate) {
-              const float4 o = *dst;
-              v[0] += o.x;
-              v[1] += o.y;
-              v[2] += o.z;
-              v[3] += o.w;
-            }
-            *dst = make_float4(v[0], v[1], v[2], v[3]);
-          } else {
-            for (int e = 0; e < 4; ++e)
-              if (col + e < p.n) crow[col + e] = p.accumulate ? crow[col + e] + v[e] : v[e];
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(tempty + acc);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
           }
         }
-      }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(tempty + acc);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1;
+        if (!ok) break;
+        if (row_ok) {
+#pragma unroll
+          for (int chunk = 0; chunk < BN / 32; ++chunk) {
+            const uint32_t col0 = t.nt * BN + chunk * 32;
+            if (col0 < p.n) store_row32(p, sum + chunk * 32, col0, crow, arow);
+          }
+        }
       }
     }
   }
@@ -440,11 +502,11 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool CHUNKED>
 cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) {
   constexpr size_t smem = STAGES * (BM * BK * 4 + BN * BK * 4) + 1024 + 256;
   static bool configured[64] = {false};
-  auto k = gemm_tf32_kernel<BN, STAGES>;
+  auto k = gemm_tf32_kernel<BN, STAGES, CHUNKED>;
   if (device < 0 || device >= 64 || !configured[device]) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -474,7 +536,8 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   memset(&p, 0, sizeof(p));
   const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
   const bool split = g.precision == SPAR_B200_TF32X3;
-  int bn = g.n > 128 ? 256 : (g.n > 64 ? 128 : 64);
+  // 3xTF32 keeps its running sums in registers (one 64-column row segment per thread).
+  int bn = split ? 64 : (g.n > 128 ? 256 : (g.n > 64 ? 128 : 64));
   p.sections = split ? 3 : 1;
   p.a_mn_major = g.a_transposed ? 1 : 0;
   p.b_mn_major = g.b_transposed ? 0 : 1;
@@ -532,13 +595,15 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   p.accumulate = g.accumulate;
   p.epilogue = g.epilogue;
   p.causal = g.causal;
+  p.kchunk = 4;  // 4 k-blocks = 128 K elements x 3 sections per hardware-accumulated chunk
+  if (split) return launch_kernel<64, 8, true>(p, device, stream);
   switch (bn) {
     case 256:
-      return launch_kernel<256, 4>(p, device, stream);
+      return launch_kernel<256, 4, false>(p, device, stream);
     case 128:
-      return launch_kernel<128, 6>(p, device, stream);
+      return launch_kernel<128, 6, false>(p, device, stream);
     default:
-      return launch_kernel<64, 8>(p, device, stream);
+      return launch_kernel<64, 8, false>(p, device, stream);
   }
 }
 
