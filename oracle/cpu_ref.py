@@ -1,0 +1,187 @@
+"""ctypes access to the reference implementation compiled from its own sources
+(oracle/_ref/libspar_ref.so, built by oracle/make_ref.py). TEST INFRASTRUCTURE ONLY: used by the
+golden-fixture generator, the oracle tests and bench.py's CPU baseline / reference arm.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int64, c_uint64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+LIB = Path(__file__).resolve().parent / "_ref" / "libspar_ref.so"
+_lib = None
+
+F = POINTER(c_float)
+I32 = POINTER(ctypes.c_int32)
+
+
+def available() -> bool:
+    return LIB.exists()
+
+
+def load():
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            raise FileNotFoundError(f"{LIB} not built (python oracle/make_ref.py)")
+        lib = ctypes.CDLL(str(LIB))
+        lib.ref_last_error.restype = c_char_p
+        sig = {
+            "ref_layernorm": [F, F, F, F, c_int64, c_int64, c_double, F, F, F, F],
+            "ref_gelu": [F, F, c_int64, F, F],
+            "ref_causal_softmax": [F, F, c_int64, c_int64, c_double, F, F],
+            "ref_cross_entropy": [F, I32, c_int64, c_int64, c_int64, F, F],
+            "ref_matmul": [F, F, F, c_int64, c_int64, c_int64, F, F, F],
+            "ref_adamw": [F, F, F, F, c_int64, c_int64, c_double, c_double, c_double, c_double,
+                          c_double, c_double, POINTER(c_double)],
+            "ref_rope": [F, F, c_int64, c_int64, c_int64, c_double, F, F],
+            "ref_lm_step": [c_int64] * 8 + [c_double, c_double, POINTER(F), I32, c_double,
+                                            c_double, c_double, c_double, c_double, c_double, F,
+                                            POINTER(c_double), POINTER(F), POINTER(F)],
+        }
+        for name, args in sig.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = c_int
+        lib.ref_warmup_cosine.argtypes = [c_double, c_double, c_uint64, c_uint64, c_uint64]
+        lib.ref_warmup_cosine.restype = c_double
+        lib.ref_train_sample_seconds.argtypes = [c_int64] * 6
+        lib.ref_train_sample_seconds.restype = c_double
+        _lib = lib
+    return _lib
+
+
+def _f(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _p(a):
+    return a.ctypes.data_as(F)
+
+
+def _check(rc):
+    if rc != 0:
+        raise RuntimeError("reference: " + load().ref_last_error().decode())
+
+
+def layernorm(x, gamma, beta, dy, eps=1e-5):
+    x, gamma, beta, dy = map(_f, (x, gamma, beta, dy))
+    rows, cols = x.shape
+    y, dx = np.empty_like(x), np.empty_like(x)
+    dg, db = np.empty(cols, np.float32), np.empty(cols, np.float32)
+    _check(load().ref_layernorm(_p(x), _p(gamma), _p(beta), _p(dy), rows, cols, eps, _p(y), _p(dx),
+                                _p(dg), _p(db)))
+    return y, dx, dg, db
+
+
+def gelu(x, dy):
+    x, dy = _f(x).ravel(), _f(dy).ravel()
+    y, dx = np.empty_like(x), np.empty_like(x)
+    _check(load().ref_gelu(_p(x), _p(dy), x.size, _p(y), _p(dx)))
+    return y, dx
+
+
+def causal_softmax(s, dp, scale):
+    s, dp = _f(s), _f(dp)
+    b, t, _ = s.shape
+    p, ds = np.empty_like(s), np.empty_like(s)
+    _check(load().ref_causal_softmax(_p(s), _p(dp), b, t, scale, _p(p), _p(ds)))
+    return p, ds
+
+
+def cross_entropy(logits, targets, seq=0):
+    z = _f(logits)
+    rows, classes = z.shape
+    tg = np.ascontiguousarray(targets, dtype=np.int32)
+    loss = np.zeros(1, np.float32)
+    dz = np.empty_like(z)
+    _check(load().ref_cross_entropy(_p(z), tg.ctypes.data_as(I32), rows, classes, seq, _p(loss), _p(dz)))
+    return float(loss[0]), dz
+
+
+def matmul(a, b, dc):
+    a, b, dc = map(_f, (a, b, dc))
+    m, k = a.shape
+    n = b.shape[1]
+    c, da, db = np.empty((m, n), np.float32), np.empty_like(a), np.empty_like(b)
+    _check(load().ref_matmul(_p(a), _p(b), _p(dc), m, k, n, _p(c), _p(da), _p(db)))
+    return c, da, db
+
+
+def adamw(p, g, steps, lr, beta1, beta2, eps, wd, max_norm):
+    p, g = _f(p).copy(), _f(g)
+    m, v = np.empty_like(p), np.empty_like(p)
+    norm = c_double(0.0)
+    _check(load().ref_adamw(_p(p), _p(g), _p(m), _p(v), p.size, steps, lr, beta1, beta2, eps, wd,
+                            max_norm, ctypes.byref(norm)))
+    return p, m, v, norm.value
+
+
+def warmup_cosine(peak, minimum, warmup, decay, step):
+    return load().ref_warmup_cosine(peak, minimum, warmup, decay, step)
+
+
+def rope(x, dy, theta=10000.0):
+    x, dy = _f(x), _f(dy)
+    outer, t, d = x.shape
+    out, dx = np.empty_like(x), np.empty_like(x)
+    _check(load().ref_rope(_p(x), _p(dy), outer, t, d, theta, _p(out), _p(dx)))
+    return out, dx
+
+
+def lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
+    """One reference training step; ids [micro, batch, t]. Returns (loss, norm, grads, new)."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    micro, batch, t = ids.shape
+    ps = [_f(params[n]) for n in names]
+    gs = [np.empty_like(p) for p in ps]
+    outs = [np.empty_like(p) for p in ps]
+    arr = lambda lst: (F * len(lst))(*[_p(a) for a in lst])
+    loss = np.zeros(1, np.float32)
+    norm = c_double(0.0)
+    _check(load().ref_lm_step(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"],
+                              batch, t, micro, cfg.get("eps", 1e-5), cfg.get("rope_theta", 1e4),
+                              arr(ps), ids.ctypes.data_as(I32), lr, opt["beta1"], opt["beta2"],
+                              opt["eps"], opt["weight_decay"], opt["max_grad_norm"], _p(loss),
+                              ctypes.byref(norm), arr(gs), arr(outs)))
+    return float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs))
+
+
+def _sample_worker(args):
+    vocab, d, f, heads, t, iters = args
+    return load().ref_train_sample_seconds(vocab, d, f, heads, t, iters)
+
+
+def run_reference_sample(cfg, seconds_budget: float = 20.0, processes: int = 1):
+    """Times the reference CPU training step on a bounded sample of `cfg`'s workload: one block
+    with cfg's d_model / heads / d_ff / vocab on a short sequence (forward, LM loss, backward,
+    clip, AdamW), in `processes` concurrent single-threaded processes (the reference has no
+    threading). Its FLOP rate is converted to tokens/s of the full configuration with the per-token
+    FLOPs (6 x matmul params + 12 L d T attention)."""
+    t = 8
+    per_token_sample = 6.0 * (4 * cfg.dim ** 2 + 2 * cfg.dim * cfg.hidden + cfg.vocab * cfg.dim) \
+        + 12.0 * cfg.dim * t
+    args = (cfg.vocab, cfg.dim, cfg.hidden, cfg.heads, t, 1)
+    if processes <= 1:
+        secs = [_sample_worker(args)]
+    else:
+        import multiprocessing as mp
+
+        with mp.get_context("spawn").Pool(processes) as pool:
+            secs = pool.map(_sample_worker, [args] * processes)
+    if min(secs) <= 0:
+        raise RuntimeError("reference sample failed")
+    rate = sum(per_token_sample * t / s for s in secs)  # FLOP/s over all processes
+    tokens_per_s = rate / cfg.flops_per_token()
+    return {"tokens_per_s": tokens_per_s, "cores": processes, "kind": "reference",
+            "sample": (f"{processes}x one training step (fwd+loss+bwd+clip+AdamW) of a 1-block "
+                       f"decoder d={cfg.dim} H={cfg.heads} F={cfg.hidden} V={cfg.vocab} on 1x{t} "
+                       f"tokens, {max(secs):.1f} s; FLOP rate extrapolated to the full step by "
+                       f"{cfg.flops_per_token() / 1e9:.3f} GFLOP/token"),
+            "seconds": secs}
+
+
+_ = (c_void_p, os)

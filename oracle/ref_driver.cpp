@@ -1,0 +1,319 @@
+// C API over the reference's public C++ API (bzzling/spar), compiled together with the reference
+// sources by oracle/make_ref.py. TEST INFRASTRUCTURE: used to pin the numpy oracle (golden
+// fixtures) and as the CPU baseline; never part of the product.
+//
+// LayerNorm and GELU do not exist in Spar; they are composed from Spar ops exactly as the
+// oracle documents (mean/subtract/square/mean/add_scalar/sqrt/divide/multiply/add, and
+// x * sigmoid(2*sqrt(2/pi)*(x + 0.044715 x^3))). The decoder uses Spar's own Embedding,
+// SelfAttention (bias, RoPE) and Linear modules, Spar's autograd, LM cross-entropy,
+// clip_grad_norm, AdamW and warmup-cosine schedule.
+#include "spar.hpp"
+
+#include <chrono>
+#include <cstring>
+#include <string>
+#include <utility>
+#include <vector>
+
+using namespace spar;
+
+namespace {
+
+thread_local std::string g_error;
+
+using dim = Shape::dimension_type;
+
+Tensor from_host(const float* data, std::vector<dim> shape, bool grad) {
+  Tensor t{Shape{std::move(shape)}, DType::Float32};
+  auto s = t.span<float>();
+  std::memcpy(s.data(), data, s.size() * sizeof(float));
+  if (grad) t.set_requires_grad(true);
+  return t;
+}
+
+Tensor ids_from_host(const int32_t* data, std::vector<dim> shape) {
+  Tensor t{Shape{std::move(shape)}, DType::Int32};
+  auto s = t.span<int32_t>();
+  std::memcpy(s.data(), data, s.size() * sizeof(int32_t));
+  return t;
+}
+
+void to_host(const Tensor& t, float* out) {
+  const Tensor c = t.detach().contiguous();
+  auto s = std::as_const(c).span<float>();
+  std::memcpy(out, s.data(), s.size() * sizeof(float));
+}
+
+Tensor layer_norm(const Tensor& x, const Tensor& gamma, const Tensor& beta, double eps) {
+  const std::size_t axis = x.rank() - 1;
+  const Tensor mu = mean(x, axis, true);
+  const Tensor xc = subtract(x, mu);
+  const Tensor var = mean(square(xc), axis, true);
+  const Tensor den = sqrt(add_scalar(var, eps));
+  return add(multiply(divide(xc, den), gamma), beta);
+}
+
+Tensor gelu(const Tensor& x) {
+  const Tensor x3 = multiply(multiply(x, x), x);
+  const Tensor u = multiply_scalar(add(x, multiply_scalar(x3, 0.044715)), 1.5957691216057308);
+  return multiply(x, sigmoid(u));
+}
+
+Tensor weighted_sum(const Tensor& y, const float* w) {
+  std::vector<dim> shape(y.shape().dimensions().begin(), y.shape().dimensions().end());
+  return sum(multiply(y, from_host(w, shape, false)));
+}
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
+struct Block {
+  nn::Parameter ln1_g, ln1_b;
+  nn::SelfAttention attn;
+  nn::Parameter ln2_g, ln2_b;
+  nn::Linear up, down;
+  Block(std::size_t d, std::size_t f, std::size_t h, double theta, Random& rng)
+      : ln1_g{ones(Shape{dim(d)}, DType::Float32)}, ln1_b{zeros(Shape{dim(d)}, DType::Float32)},
+        attn{d, h, h, DType::Float32, rng, true, theta},
+        ln2_g{ones(Shape{dim(d)}, DType::Float32)}, ln2_b{zeros(Shape{dim(d)}, DType::Float32)},
+        up{d, f, DType::Float32, rng, true}, down{f, d, DType::Float32, rng, true} {}
+};
+
+struct Model {
+  nn::Embedding embedding;
+  std::vector<Block> blocks;
+  nn::Parameter lnf_g, lnf_b;
+  double eps;
+  Model(std::size_t v, std::size_t d, std::size_t f, std::size_t layers, std::size_t h,
+        double theta, double eps_, Random& rng)
+      : embedding{v, d, DType::Float32, rng}, lnf_g{ones(Shape{dim(d)}, DType::Float32)},
+        lnf_b{zeros(Shape{dim(d)}, DType::Float32)}, eps{eps_} {
+    blocks.reserve(layers);
+    for (std::size_t i = 0; i < layers; ++i) blocks.emplace_back(d, f, h, theta, rng);
+  }
+  // Named-parameter order (src/nn/parameters.cpp:51-132 with LayerNorm weight+bias).
+  std::vector<nn::Parameter> parameters() {
+    std::vector<nn::Parameter> p{embedding.weight()};
+    for (Block& b : blocks) {
+      p.push_back(b.ln1_g);
+      p.push_back(b.ln1_b);
+      for (nn::Linear* l : {&b.attn.q_proj(), &b.attn.k_proj(), &b.attn.v_proj(), &b.attn.out_proj()}) {
+        p.push_back(l->weight());
+        p.push_back(*l->bias());
+      }
+      p.push_back(b.ln2_g);
+      p.push_back(b.ln2_b);
+      for (nn::Linear* l : {&b.up, &b.down}) {
+        p.push_back(l->weight());
+        p.push_back(*l->bias());
+      }
+    }
+    p.push_back(lnf_g);
+    p.push_back(lnf_b);
+    return p;
+  }
+  Tensor logits(const Tensor& ids) {
+    Tensor h = embedding.forward(ids);
+    for (Block& b : blocks) {
+      const Tensor h1 = add(h, b.attn.forward(layer_norm(h, b.ln1_g.tensor(), b.ln1_b.tensor(), eps)));
+      const Tensor a2 = layer_norm(h1, b.ln2_g.tensor(), b.ln2_b.tensor(), eps);
+      h = add(h1, b.down.forward(gelu(b.up.forward(a2))));
+    }
+    const Tensor hf = layer_norm(h, lnf_g.tensor(), lnf_b.tensor(), eps);
+    return matmul(hf, embedding.weight().tensor().transpose(0, 1));
+  }
+};
+
+void load(nn::Parameter& p, const float* src) {
+  Tensor values = p.tensor().detach();
+  auto s = values.span<float>();
+  std::memcpy(s.data(), src, s.size() * sizeof(float));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ref_last_error() { return g_error.c_str(); }
+
+// Composed LayerNorm forward + backward of sum(y * dy).
+int ref_layernorm(const float* x, const float* gamma, const float* beta, const float* dy,
+                  int64_t rows, int64_t cols, double eps, float* y, float* dx, float* dgamma,
+                  float* dbeta) {
+  return guarded([&] {
+    Tensor tx = from_host(x, {rows, cols}, true);
+    Tensor tg = from_host(gamma, {cols}, true);
+    Tensor tb = from_host(beta, {cols}, true);
+    Tensor out = layer_norm(tx, tg, tb, eps);
+    to_host(out, y);
+    Tensor loss = weighted_sum(out, dy);
+    loss.backward();
+    to_host(tx.grad(), dx);
+    to_host(tg.grad(), dgamma);
+    to_host(tb.grad(), dbeta);
+  });
+}
+
+int ref_gelu(const float* x, const float* dy, int64_t n, float* y, float* dx) {
+  return guarded([&] {
+    Tensor tx = from_host(x, {n}, true);
+    Tensor out = gelu(tx);
+    to_host(out, y);
+    Tensor loss = weighted_sum(out, dy);
+    loss.backward();
+    to_host(tx.grad(), dx);
+  });
+}
+
+// scores [batch, t, t] -> P = softmax(scale * s + causal mask, axis 2); dS for upstream dp.
+int ref_causal_softmax(const float* s, const float* dp, int64_t batch, int64_t t, double scale,
+                       float* p, float* ds) {
+  return guarded([&] {
+    Tensor ts = from_host(s, {batch, t, t}, true);
+    Tensor mask = zeros(Shape{t, t}, DType::Float32);
+    auto mv = mask.span<float>();
+    for (int64_t i = 0; i < t; ++i)
+      for (int64_t j = i + 1; j < t; ++j) mv[i * t + j] = -std::numeric_limits<float>::infinity();
+    Tensor probs = softmax(add(multiply_scalar(ts, scale), mask), 2);
+    to_host(probs, p);
+    Tensor loss = weighted_sum(probs, dp);
+    loss.backward();
+    to_host(ts.grad(), ds);
+  });
+}
+
+// seq == 0: loss::cross_entropy over [rows, classes]; seq > 1: language_model_cross_entropy
+// over [rows/seq, seq, classes] with targets = the id tensor. Mean reduction.
+int ref_cross_entropy(const float* logits, const int32_t* targets, int64_t rows, int64_t classes,
+                      int64_t seq, float* loss_out, float* dlogits) {
+  return guarded([&] {
+    Tensor z = seq ? from_host(logits, {rows / seq, seq, classes}, true)
+                   : from_host(logits, {rows, classes}, true);
+    Tensor loss = seq ? loss::language_model_cross_entropy(z, ids_from_host(targets, {rows / seq, seq}))
+                      : loss::cross_entropy(z, ids_from_host(targets, {rows}));
+    *loss_out = std::as_const(loss).span<float>()[0];
+    loss.backward();
+    to_host(z.grad(), dlogits);
+  });
+}
+
+int ref_matmul(const float* a, const float* b, const float* dc, int64_t m, int64_t k, int64_t n,
+               float* c, float* da, float* db) {
+  return guarded([&] {
+    Tensor ta = from_host(a, {m, k}, true);
+    Tensor tb = from_host(b, {k, n}, true);
+    Tensor out = matmul(ta, tb);
+    to_host(out, c);
+    Tensor loss = weighted_sum(out, dc);
+    loss.backward();
+    to_host(ta.grad(), da);
+    to_host(tb.grad(), db);
+  });
+}
+
+// `steps` consecutive clip_grad_norm + AdamW steps on one parameter with a fixed gradient.
+int ref_adamw(float* p, const float* g, float* m_out, float* v_out, int64_t n, int64_t steps,
+              double lr, double beta1, double beta2, double eps, double wd, double max_norm,
+              double* norm_out) {
+  return guarded([&] {
+    nn::Parameter param{from_host(p, {n}, false)};
+    optim::AdamW opt{{param}, lr, beta1, beta2, eps, wd};
+    std::vector<nn::Parameter> list{param};
+    for (int64_t s = 0; s < steps; ++s) {
+      param.zero_grad();
+      Tensor loss = weighted_sum(param.tensor(), g);  // d loss / d p = g
+      loss.backward();
+      if (max_norm >= 0) *norm_out = training::clip_grad_norm(list, max_norm).total_norm;
+      opt.step();
+    }
+    to_host(param.tensor(), p);
+    const auto state = opt.parameter_state(param);
+    to_host(state->first_moment, m_out);
+    to_host(state->second_moment, v_out);
+  });
+}
+
+double ref_warmup_cosine(double peak, double minimum, uint64_t warmup, uint64_t decay,
+                         uint64_t step) {
+  return training::warmup_cosine_learning_rate({peak, minimum, warmup, decay}, step);
+}
+
+// apply_rope on x [outer, t, d] (forward), then its backward of sum(out * dy).
+int ref_rope(const float* x, const float* dy, int64_t outer, int64_t t, int64_t d, double theta,
+             float* out, float* dx) {
+  return guarded([&] {
+    Tensor tx = from_host(x, {outer, t, d}, true);
+    Tensor r = nn::apply_rope(tx, 0, theta);
+    to_host(r, out);
+    Tensor loss = weighted_sum(r, dy);
+    loss.backward();
+    to_host(tx.grad(), dx);
+  });
+}
+
+// One optimiser step of the LN/GELU decoder: `micro` micro-batches of ids [batch, t] each,
+// mean-of-micro-batch-means loss, Spar backward, clip_grad_norm, AdamW. params/grads/out_params
+// are arrays of pointers in named-parameter order (embedding, per block: ln1 w/b, q/k/v/out
+// w/b, ln2 w/b, up w/b, down w/b; final ln w/b). grads are the pre-clip gradients.
+int ref_lm_step(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t heads, int64_t batch,
+                int64_t t, int64_t micro, double eps, double theta, const float* const* params,
+                const int32_t* ids, double lr, double beta1, double beta2, double adam_eps,
+                double wd, double max_norm, float* loss_out, double* norm_out, float** grads,
+                float** out_params) {
+  return guarded([&] {
+    Random rng{1};
+    Model model(vocab, d, f, layers, heads, theta, eps, rng);
+    std::vector<nn::Parameter> ps = model.parameters();
+    for (std::size_t i = 0; i < ps.size(); ++i) load(ps[i], params[i]);
+    double total = 0.0;
+    for (int64_t mi = 0; mi < micro; ++mi) {
+      Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t});
+      Tensor loss = loss::language_model_cross_entropy(model.logits(tid), tid);
+      total += std::as_const(loss).span<float>()[0];
+      Tensor scaled = multiply_scalar(loss, 1.0 / static_cast<double>(micro));
+      scaled.backward();
+    }
+    *loss_out = static_cast<float>(total / static_cast<double>(micro));
+    for (std::size_t i = 0; i < ps.size(); ++i) to_host(ps[i].grad(), grads[i]);
+    *norm_out = training::clip_grad_norm(ps, max_norm).total_norm;
+    optim::AdamW opt{ps, lr, beta1, beta2, adam_eps, wd};
+    opt.step();
+    for (std::size_t i = 0; i < ps.size(); ++i) to_host(ps[i].tensor(), out_params[i]);
+  });
+}
+
+// Seconds for `iters` training steps (forward, loss, backward, clip, AdamW) of a one-block
+// decoder with the given dimensions on [1, t] token ids: the bounded CPU-baseline sample.
+double ref_train_sample_seconds(int64_t vocab, int64_t d, int64_t f, int64_t heads, int64_t t,
+                                int64_t iters) {
+  double seconds = -1.0;
+  guarded([&] {
+    Random rng{7};
+    Model model(vocab, d, f, 1, heads, 10000.0, 1e-5, rng);
+    std::vector<nn::Parameter> ps = model.parameters();
+    optim::AdamW opt{ps, 3e-4, 0.9, 0.95, 1e-8, 0.1};
+    Tensor tid{Shape{1, t}, DType::Int32};
+    auto s = tid.span<int32_t>();
+    for (int64_t i = 0; i < t; ++i) s[i] = static_cast<int32_t>((i * 7919) % vocab);
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int64_t it = 0; it < iters; ++it) {
+      for (auto& p : ps) p.zero_grad();
+      Tensor loss = loss::language_model_cross_entropy(model.logits(tid), tid);
+      loss.backward();
+      (void)training::clip_grad_norm(ps, 1.0);
+      opt.step();
+    }
+    seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  });
+  return seconds;
+}
+
+}  // extern "C"

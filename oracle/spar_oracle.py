@@ -237,7 +237,7 @@ def adamw_update(p, g, m, v, step, lr, beta1, beta2, eps, weight_decay, clip=1.0
 def warmup_cosine(peak, minimum, warmup, decay, step):
     """training::warmup_cosine_learning_rate (src/training/schedule.cpp:9-38)."""
     if step < warmup:
-        return peak * (step + 1) / warmup
+        return peak * ((step + 1) / warmup)  # progress first, as schedule.cpp:25-27
     idx = step - warmup
     if idx >= decay or decay == 1:
         return minimum

@@ -764,8 +764,8 @@ extern "C" double spar_b200_warmup_cosine(double peak, double minimum, uint64_t 
   if (!std::isfinite(peak) || peak < 0.0 || !std::isfinite(minimum) || minimum < 0.0 ||
       minimum > peak || decay_steps == 0)
     return NAN;
-  if (completed_steps < warmup_steps)
-    return peak * static_cast<double>(completed_steps + 1) / static_cast<double>(warmup_steps);
+  if (completed_steps < warmup_steps)  // progress first, then scale (schedule.cpp:25-27)
+    return peak * (static_cast<double>(completed_steps + 1) / static_cast<double>(warmup_steps));
   const uint64_t idx = completed_steps - warmup_steps;
   if (idx >= decay_steps || decay_steps == 1) return minimum;
   const double progress = static_cast<double>(idx) / static_cast<double>(decay_steps - 1);

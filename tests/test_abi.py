@@ -87,3 +87,14 @@ def test_product_does_not_import_oracle():
 
 if __name__ == "__main__":
     pytest.main([__file__])
+
+
+def test_warmup_cosine_entry_point_matches_reference_fixture():
+    """spar_b200_warmup_cosine reproduces the reference schedule bit for bit."""
+    import numpy as np
+
+    from spar_b200.lm import warmup_cosine
+
+    f = np.load(ROOT / "tests" / "golden" / "schedule.npz")
+    for s, lr in zip(f["steps"], f["lr"]):
+        assert warmup_cosine(3e-4, 3e-5, 100, 900, int(s)) == lr

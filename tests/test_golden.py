@@ -1,0 +1,230 @@
+"""Golden fixtures produced by the reference itself (tests/golden/make_golden.py runs bzzling/spar
+compiled from its own sources). CPU tests pin the numpy oracle to them; GPU tests check the CUDA
+path against the same fixtures.
+
+Tolerance: max relative error <= 1e-5 (fp32 reference vs float64 restatement / our fp32 kernels);
+gradients of the training step: relative L2 <= 1e-5.
+"""
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from _util import rel_err, rel_l2
+from oracle import spar_oracle as O
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = 1e-5
+
+
+def load(name):
+    return dict(np.load(GOLDEN / f"{name}.npz"))
+
+
+# ------------------------------------------------------------------------------ oracle (CPU)
+def test_oracle_layernorm_matches_reference():
+    f = load("layernorm")
+    y, _, _ = O.layer_norm_forward(f["x"], f["gamma"], f["beta"], 1e-5, np.float64)
+    dx, dg, db = O.layer_norm_backward(f["dy"], f["x"], f["gamma"], 1e-5)
+    assert rel_err(f["y"], y) <= TOL
+    assert rel_err(f["dx"], dx) <= TOL
+    assert rel_err(f["dgamma"], dg) <= TOL and rel_err(f["dbeta"], db) <= TOL
+
+
+def test_oracle_gelu_matches_reference():
+    f = load("gelu")
+    assert rel_err(f["y"], O.gelu_forward(f["x"], np.float64)) <= TOL
+    assert rel_err(f["dx"], f["dy"] * O.gelu_derivative(f["x"])) <= TOL
+
+
+def test_oracle_causal_softmax_matches_reference():
+    f = load("causal_softmax")
+    scale = float(f["scale"])
+    p = O.causal_softmax_forward(f["s"], scale, np.float64)
+    assert rel_err(f["p"], p) <= TOL
+    assert rel_err(f["ds"], O.causal_softmax_backward(f["dp"], p, scale)) <= TOL
+
+
+def test_oracle_cross_entropy_matches_reference():
+    f = load("cross_entropy")
+    loss, _, d = O.cross_entropy_forward_backward(f["logits"], f["targets"])
+    assert abs(loss - f["loss"]) <= TOL * abs(f["loss"])
+    assert rel_err(f["dlogits"], d) <= TOL
+    seq = int(f["lm_seq"])
+    rows, targets = O.lm_targets(f["lm_ids"].reshape(-1, seq))
+    loss, _, d = O.cross_entropy_forward_backward(f["lm_logits"], targets, rows)
+    assert abs(loss - f["lm_loss"]) <= TOL * abs(f["lm_loss"])
+    assert rel_err(f["lm_dlogits"], d) <= TOL
+    assert np.all(f["lm_dlogits"].reshape(-1, seq, f["lm_logits"].shape[1])[:, -1] == 0)
+
+
+def test_oracle_matmul_matches_reference():
+    f = load("matmul")
+    a, b, dc = (f[k].astype(np.float64) for k in ("a", "b", "dc"))
+    assert rel_err(f["c"], a @ b) <= TOL
+    assert rel_err(f["da"], dc @ b.T) <= TOL and rel_err(f["db"], a.T @ dc) <= TOL
+
+
+def test_oracle_adamw_matches_reference():
+    f = load("adamw")
+    p, m, v = f["p0"], np.zeros_like(f["p0"]), np.zeros_like(f["p0"])
+    for step in range(1, int(f["steps"]) + 1):
+        norm = O.global_grad_norm([f["g"]])
+        p, m, v = O.adamw_update(p, f["g"], m, v, step, 3e-4, 0.9, 0.95, 1e-8, 0.1,
+                                 O.clip_factor(norm, 1.0))
+    assert abs(norm - float(f["norm"])) <= 1e-12 * norm
+    # the same double-precision update rounded to fp32: bit-identical
+    np.testing.assert_array_equal(p, f["p"])
+    np.testing.assert_array_equal(m, f["m"])
+    np.testing.assert_array_equal(v, f["v"])
+
+
+def test_oracle_schedule_matches_reference():
+    f = load("schedule")
+    for s, lr in zip(f["steps"], f["lr"]):
+        assert O.warmup_cosine(3e-4, 3e-5, 100, 900, int(s)) == lr
+
+
+def test_oracle_rope_matches_reference():
+    f = load("rope")
+    cos, sin = O.rope_table(f["x"].shape[1], f["x"].shape[2])
+    assert rel_err(f["out"], O.rope_apply(f["x"].astype(np.float64), cos, sin)) <= TOL
+    assert rel_err(f["dx"], O.rope_apply(f["dy"].astype(np.float64), cos, sin, inverse=True)) <= TOL
+
+
+def test_oracle_tiny_lm_step_matches_reference():
+    f = load("lm_tiny")
+    cfg = {"vocab": 32, "dim": 32, "hidden": 64, "layers": 2, "heads": 2}
+    opt = {"beta1": 0.9, "beta2": 0.95, "eps": 1e-8, "weight_decay": 0.1, "max_grad_norm": 1.0}
+    params = O.init_parameters(cfg, 0x5EED0101)
+    loss, grads, new, _ = O.lm_train_step(params, {}, list(f["ids"]), cfg, 1, 3e-4, opt)
+    names = O.parameter_names(2)
+    assert abs(loss - f["loss"]) <= TOL * abs(loss)
+    assert abs(O.global_grad_norm([grads[n] for n in names]) - f["norm"]) <= TOL * f["norm"]
+    flat = lambda d, pre: np.concatenate([np.ravel(d[pre + n]) for n in names])
+    assert rel_l2(flat(f, "grad/"), np.concatenate([grads[n].ravel() for n in names])) <= TOL
+    assert rel_l2(flat(f, "new/"), np.concatenate([new[n].ravel() for n in names])) <= TOL
+
+
+def test_oracle_c1_lm_step_matches_reference():
+    f = load("lm_c1")
+    from spar_b200.lm import C1
+
+    params = O.init_parameters(C1.oracle_dict(), 0x5EED0001)
+    loss, grads, new, _ = O.lm_train_step(params, {}, list(f["ids"]), C1.oracle_dict(), 1, 3e-4,
+                                          C1.opt_dict())
+    names = O.parameter_names(2)
+    assert abs(loss - f["loss"]) <= TOL * abs(loss)
+    assert abs(O.global_grad_norm([grads[n] for n in names]) - f["norm"]) <= TOL * f["norm"]
+    for n in names:
+        gn = float(f["gnorm/" + n])
+        assert abs(np.linalg.norm(grads[n]) - gn) <= TOL * gn + 1e-12, n
+        idx = f["idx/" + n]
+        assert np.abs(grads[n].ravel()[idx] - f["grad/" + n]).max() <= TOL * gn + 1e-12, n
+
+
+def test_reference_library_agrees_with_oracle_when_built():
+    """When oracle/_ref is built on this machine, the live reference and the restatement agree
+    on fresh inputs too (not only on the committed fixtures)."""
+    import sys
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "oracle"))
+    import cpu_ref
+
+    if not cpu_ref.available():
+        pytest.skip("oracle/_ref not built on this machine")
+    r = np.random.default_rng(99)
+    x = r.standard_normal((7, 40)).astype(np.float32)
+    g = np.ones(40, np.float32)
+    b = np.zeros(40, np.float32)
+    dy = r.standard_normal((7, 40)).astype(np.float32)
+    y, dx, _, _ = cpu_ref.layernorm(x, g, b, dy)
+    assert rel_err(y, O.layer_norm_forward(x, g, b, 1e-5, np.float64)[0]) <= TOL
+    assert rel_err(dx, O.layer_norm_backward(dy, x, g)[0]) <= TOL
+
+
+# ------------------------------------------------------------------------------ CUDA (GPU)
+@pytest.mark.gpu
+def test_cuda_ops_match_reference_fixtures(cuda):
+    import torch
+    from spar_b200 import ops
+
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    f = load("layernorm")
+    y, mean, rstd = ops.layer_norm_forward(T(f["x"]), T(f["gamma"]), T(f["beta"]))
+    dx, dg, db = ops.layer_norm_backward(T(f["dy"]), T(f["x"]), T(f["gamma"]), mean, rstd)
+    f2 = load("gelu")
+    gy = ops.gelu_forward(T(f2["x"]))
+    gdx = ops.gelu_backward(T(f2["dy"]), T(f2["x"]))
+    f3 = load("causal_softmax")
+    p = ops.causal_softmax_forward(T(f3["s"]), float(f3["scale"]))
+    ds = ops.causal_softmax_backward(T(f3["dp"]), p, float(f3["scale"]))
+    f4 = load("cross_entropy")
+    loss, dz, inv = ops.cross_entropy_forward_backward(T(f4["logits"]), T(f4["targets"]))
+    seq = int(f4["lm_seq"])
+    lml, lmd, inv2 = ops.cross_entropy_forward_backward(T(f4["lm_logits"]), T(f4["lm_ids"]),
+                                                        sequence_length=seq)
+    f5 = load("rope")
+    outer, t, d = f5["x"].shape
+    xr = T(f5["x"]).clone()
+    tab = ops.rope_table(t, d, 10000.0, device=cuda)
+    ops.rope_apply_(xr, tab, outer, t, 1, d, d)
+    dr = T(f5["dy"]).clone()
+    ops.rope_apply_(dr, tab, outer, t, 1, d, d, inverse=True)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), f["y"]) <= TOL and rel_err(dx.cpu().numpy(), f["dx"]) <= TOL
+    assert rel_err(dg.cpu().numpy(), f["dgamma"]) <= TOL and rel_err(db.cpu().numpy(), f["dbeta"]) <= TOL
+    assert rel_err(gy.cpu().numpy(), f2["y"]) <= TOL and rel_err(gdx.cpu().numpy(), f2["dx"]) <= TOL
+    assert rel_err(p.cpu().numpy(), f3["p"]) <= TOL and rel_err(ds.cpu().numpy(), f3["ds"]) <= TOL
+    assert inv.item() == 0 and inv2.item() == 0
+    assert abs(loss.cpu().numpy().astype(np.float64).mean() - f4["loss"]) <= TOL * f4["loss"]
+    assert rel_err(dz.cpu().numpy(), f4["dlogits"]) <= TOL
+    assert rel_err(lmd.cpu().numpy(), f4["lm_dlogits"]) <= TOL
+    n_lm = len(f4["lm_ids"]) // seq * (seq - 1)
+    assert abs(lml.cpu().numpy().astype(np.float64).sum() / n_lm - f4["lm_loss"]) <= TOL * f4["lm_loss"]
+    assert rel_err(xr.cpu().numpy(), f5["out"]) <= TOL and rel_err(dr.cpu().numpy(), f5["dx"]) <= TOL
+
+
+@pytest.mark.gpu
+def test_cuda_adamw_matches_reference_fixture(cuda):
+    import torch
+    from spar_b200 import ops
+
+    f = load("adamw")
+    p = torch.from_numpy(f["p0"].copy()).to(cuda)
+    g = torch.from_numpy(f["g"]).to(cuda)
+    m = torch.zeros_like(p)
+    v = torch.zeros_like(p)
+    for step in range(1, int(f["steps"]) + 1):
+        st = ops.grad_norm_squared([g])
+        flag = ops.adamw_clipped([p], [g], [m], [v], st, lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8,
+                                 weight_decay=0.1, step=step, max_norm=1.0)
+    torch.cuda.synchronize()
+    assert flag.item() == 0
+    assert abs(math.sqrt(st[0].item()) - float(f["norm"])) <= 1e-12 * float(f["norm"])
+    # double-precision update as the reference: expect bit equality (allow 1 ulp)
+    for got, want in ((p, f["p"]), (m, f["m"]), (v, f["v"])):
+        np.testing.assert_array_max_ulp(got.cpu().numpy(), want, maxulp=1)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision,tol", [(1, 1e-5), (0, 2e-3)])
+def test_cuda_c1_step_matches_reference_fixture(cuda, precision, tol):
+    from dataclasses import replace
+
+    from spar_b200.lm import C1, DecoderLM
+
+    f = load("lm_c1")
+    cfg = replace(C1, precision=precision)
+    lm = DecoderLM(cfg, 0)
+    lm.load_state_dict(O.init_parameters(C1.oracle_dict(), 0x5EED0001))
+    loss, norm, flags = lm.train_step(f["ids"], 3e-4, step=1)
+    grads = lm.state_dict("grad")
+    lm.close()
+    assert flags == (0, 0)
+    assert abs(loss - f["loss"]) <= tol * abs(f["loss"])
+    assert abs(norm - f["norm"]) <= tol * f["norm"]
+    for n in O.parameter_names(2):
+        gn = float(f["gnorm/" + n])
+        assert abs(np.linalg.norm(grads[n].astype(np.float64)) - gn) <= 10 * tol * gn + 1e-12, n
