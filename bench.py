@@ -123,13 +123,13 @@ def make_ids(step: int, rank: int, world: int, seq: int, vocab: int):
     return np.ascontiguousarray(mine.reshape(ACCUM, per // ACCUM, seq).astype(np.int32))
 
 
-def cpu_baseline_sample(cfg, seconds_budget=20.0):
+def cpu_baseline_sample(cfg, seconds_budget=20.0, processes=1):
     """The reference CPU path timed on a bounded sample of the same workload: one block with the
     config's dimensions (d, heads, d_ff, vocab) on a short sequence, forward + backward; the
     measured FLOP rate is converted to tokens/s of the full step by the per-token FLOPs."""
     from cpu_ref import run_reference_sample  # oracle/cpu_ref.py
 
-    return run_reference_sample(cfg, seconds_budget)
+    return run_reference_sample(cfg, seconds_budget, processes=processes)
 
 
 def run_reference_arm(args):
@@ -139,13 +139,16 @@ def run_reference_arm(args):
     sys.path.insert(0, str(ROOT / "oracle"))
     from spar_b200.lm import C5
 
+    from cpu_ref import default_processes
+
     cfg = C5
     steps = []
     info = None
-    for _ in range(args.warmup):
-        pass  # the CPU reference has no warm-up state; each step below is one bounded sample
+    procs = default_processes()
+    # The CPU reference keeps no state between steps, so warm-up steps are not run; each timed
+    # step is one bounded sample per host core (the reference is single-threaded).
     for _ in range(args.steps):
-        info = cpu_baseline_sample(cfg, seconds_budget=max(5.0, 60.0 / max(args.steps, 1)))
+        info = cpu_baseline_sample(cfg, processes=procs)
         steps.append(info["tokens_per_s"])
     value = statistics.median(steps)
     line = {

@@ -155,13 +155,25 @@ def _sample_worker(args):
     return load().ref_train_sample_seconds(vocab, d, f, heads, t, iters)
 
 
-def run_reference_sample(cfg, seconds_budget: float = 20.0, processes: int = 1):
+def default_processes() -> int:
+    """All host cores, capped so the concurrent samples (~1.5 GB each at config 5) fit in RAM."""
+    n = os.cpu_count() or 1
+    try:
+        import psutil
+
+        n = min(n, max(1, int(psutil.virtual_memory().available / 1.5e9)))
+    except ImportError:
+        pass
+    return max(1, n)
+
+
+def run_reference_sample(cfg, seconds_budget: float = 20.0, processes: int = 1, t: int = 2):
     """Times the reference CPU training step on a bounded sample of `cfg`'s workload: one block
     with cfg's d_model / heads / d_ff / vocab on a short sequence (forward, LM loss, backward,
     clip, AdamW), in `processes` concurrent single-threaded processes (the reference has no
     threading). Its FLOP rate is converted to tokens/s of the full configuration with the per-token
-    FLOPs (6 x matmul params + 12 L d T attention)."""
-    t = 8
+    FLOPs (6 x matmul params + 12 L d T attention). t=2 tokens keeps one sample near 15 s at
+    config 5's dimensions."""
     per_token_sample = 6.0 * (4 * cfg.dim ** 2 + 2 * cfg.dim * cfg.hidden + cfg.vocab * cfg.dim) \
         + 12.0 * cfg.dim * t
     args = (cfg.vocab, cfg.dim, cfg.hidden, cfg.heads, t, 1)

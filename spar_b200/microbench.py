@@ -1,0 +1,134 @@
+"""Per-kernel timing of the spar_b200 hot-path kernels at a given size (CUDA events, inputs larger
+than L2, warm-up first) with the achieved rate against the B200 peaks.
+
+  python -m spar_b200.microbench all
+  python -m spar_b200.microbench gemm --m 8192 --n 4096 --k 4096 [--at] [--bt] [--x3]
+  python -m spar_b200.microbench layernorm_bwd|gelu_bwd|softmax_bwd|cross_entropy|adamw|attention
+
+Bandwidth kernels report algorithmic bytes / time (GB/s); GEMMs report 2mnk / time (TFLOP/s).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+from . import ops
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    d = json.loads(p.read_text()) if p.exists() else {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+    return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0) / 2.0
+
+
+def timed(fn, iters=10, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def report(name, ms, work, unit, peak):
+    rate = work / (ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+    line = {"kernel": name, "ms": round(ms, 4), "achieved": round(rate, 1), "unit": unit,
+            "peak": round(peak, 1), "frac": round(rate / peak, 3)}
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def run_gemm(m, n, k, at=False, bt=False, x3=False, iters=10):
+    dev = torch.device("cuda")
+    a = torch.randn((k, m) if at else (m, k), device=dev)
+    b = torch.randn((n, k) if bt else (k, n), device=dev) * 0.02
+    c = torch.empty(m, n, device=dev)
+    prec = ops.TF32X3 if x3 else ops.TF32
+    ms = timed(lambda: ops.matmul(a, b, a_t=at, b_t=bt, out=c, precision=prec), iters=iters)
+    _, tf = peaks()
+    return report(f"gemm {m}x{n}x{k} a_t={int(at)} b_t={int(bt)} {'3xtf32' if x3 else 'tf32'}",
+                  ms, 2.0 * m * n * k, "TFLOP/s", tf)
+
+
+def run_bandwidth(name, iters=10):
+    dev = torch.device("cuda")
+    hbm, _ = peaks()
+    if name == "layernorm_bwd":
+        x = torch.randn(16384, 1024, device=dev)
+        dy = torch.randn_like(x)
+        g = torch.ones(1024, device=dev)
+        _, mean, rstd = ops.layer_norm_forward(x, g, torch.zeros_like(g))
+        return report("layernorm_bwd 16384x1024", timed(lambda: ops.layer_norm_backward(dy, x, g, mean, rstd), iters),
+                      12 * x.numel(), "GB/s", hbm)
+    if name == "gelu_bwd":
+        x = torch.randn(16384, 4096, device=dev)
+        dy = torch.randn_like(x)
+        return report("gelu_bwd 16384x4096", timed(lambda: ops.gelu_backward(dy, x), iters),
+                      12 * x.numel(), "GB/s", hbm)
+    if name == "softmax_bwd":
+        t = 1024
+        s = torch.randn(96, t, t, device=dev)
+        p = ops.causal_softmax_forward(s, 0.125)
+        dp = torch.randn_like(s)
+        ds = torch.empty_like(s)
+        causal = 96 * (2 * t * (t + 1) // 2 + t * t) * 4
+        return report("causal_softmax_bwd 96x1024x1024", timed(lambda: ops.causal_softmax_backward(dp, p, 0.125, out=ds), iters),
+                      causal, "GB/s", hbm)
+    if name == "cross_entropy":
+        z = 2 * torch.randn(8192, 32768, device=dev)
+        tg = torch.randint(0, 32768, (8192,), dtype=torch.int32, device=dev)
+        return report("cross_entropy 8192x32768", timed(lambda: ops.cross_entropy_forward_backward(z, tg, in_place=True), iters),
+                      8 * z.numel(), "GB/s", hbm)
+    if name == "adamw":
+        n = 350_000_000
+        p = torch.randn(n, device=dev) * 0.02
+        g = torch.randn(n, device=dev) * 1e-3
+        m = torch.zeros_like(p)
+        v = torch.zeros_like(p)
+        st = ops.grad_norm_squared([g])
+        ms = timed(lambda: ops.adamw_clipped([p], [g], [m], [v], st, lr=3e-4, beta1=0.9, beta2=0.95,
+                                             weight_decay=0.1, step=1, max_norm=1.0), min(iters, 5))
+        report("adamw 350M", ms, 28 * n, "GB/s", hbm)
+        return report("grad_norm 350M", timed(lambda: ops.grad_norm_squared([g], st), min(iters, 5)),
+                      4 * n, "GB/s", hbm)
+    raise SystemExit(f"unknown kernel {name}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel")
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--at", action="store_true")
+    ap.add_argument("--bt", action="store_true")
+    ap.add_argument("--x3", action="store_true")
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    if a.kernel == "gemm":
+        run_gemm(a.m, a.n, a.k, a.at, a.bt, a.x3, a.iters)
+    elif a.kernel == "all":
+        for (m, n, k, at, bt) in [(8192, 4096, 4096, 0, 0), (8192, 4096, 4096, 0, 1),
+                                  (4096, 4096, 8192, 1, 0), (16384, 3072, 1024, 0, 0),
+                                  (16384, 1024, 4096, 0, 0), (1024, 4096, 16384, 1, 0),
+                                  (16384, 32768, 1024, 0, 1)]:
+            run_gemm(m, n, k, bool(at), bool(bt), False, a.iters)
+        for name in ("layernorm_bwd", "gelu_bwd", "softmax_bwd", "cross_entropy", "adamw"):
+            run_bandwidth(name, a.iters)
+    else:
+        run_bandwidth(a.kernel, a.iters)
+
+
+if __name__ == "__main__":
+    _ = math
+    main()
