@@ -41,10 +41,13 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
+constexpr uint32_t kEpiBytes = 4 * 2 * 4096;  // epilogue staging: 4 warps x 2 boxes x 4 KB
 
 struct GemmParams {
   CUtensorMap a_map[3];
   CUtensorMap b_map[3];
+  CUtensorMap c_map;    // output, {32 cols, 32 rows} boxes, 128-byte swizzle
+  CUtensorMap aux_map;  // epilogue side input/output (residual, pre-activation), same boxes
   int sections;
   int a_mn_major, b_mn_major;
   uint32_t m, n, k;
@@ -100,75 +103,89 @@ __device__ __forceinline__ void k_range(const GemmParams& p, uint32_t mt, uint32
 
 __device__ __forceinline__ void record_error() { atomicExch(&g_gemm_error, 1); }
 
-// Applies alpha, the epilogue and the accumulate flag to 32 consecutive accumulator columns of
-// one row and stores them (128-bit accesses where the row end allows).
-__device__ __forceinline__ void store_row32(const GemmParams& p, const float* acc32, uint32_t col0,
-                                            float* crow, float* arow) {
-#pragma unroll
-  for (int j = 0; j < 32; j += 4) {
-    const uint32_t col = col0 + j;
-    if (col >= p.n) break;
-    float v[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = p.alpha * acc32[j + e];
-    const bool full4 = col + 3 < p.n;
-    if (p.bias && (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU ||
-                   p.epilogue == SPAR_B200_EPI_BIAS_ADD)) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (col + e < p.n) v[e] += p.bias[col + e];
-    }
-    if (p.epilogue == SPAR_B200_EPI_BIAS_ADD) {
-      if (full4) {
-        const float4 q = *reinterpret_cast<const float4*>(arow + col);
-        v[0] += q.x;
-        v[1] += q.y;
-        v[2] += q.z;
-        v[3] += q.w;
-      } else {
-        for (int e = 0; e < 4; ++e)
-          if (col + e < p.n) v[e] += arow[col + e];
-      }
-    }
-    if (p.epilogue == SPAR_B200_EPI_BIAS_GELU) {
-      if (full4) {
-        *reinterpret_cast<float4*>(arow + col) = make_float4(v[0], v[1], v[2], v[3]);
-      } else {
-        for (int e = 0; e < 4; ++e)
-          if (col + e < p.n) arow[col + e] = v[e];
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = gelu_value(v[e]);
-    } else if (p.epilogue == SPAR_B200_EPI_GELU_BWD) {
-      float pre[4] = {0.f, 0.f, 0.f, 0.f};
-      if (full4) {
-        const float4 q = *reinterpret_cast<const float4*>(arow + col);
-        pre[0] = q.x;
-        pre[1] = q.y;
-        pre[2] = q.z;
-        pre[3] = q.w;
-      } else {
-        for (int e = 0; e < 4; ++e)
-          if (col + e < p.n) pre[e] = arow[col + e];
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] *= gelu_derivative(pre[e]);
-    }
-    if (full4) {
-      float4* dst = reinterpret_cast<float4*>(crow + col);
-      if (p.accumulate) {
-        const float4 o = *dst;
-        v[0] += o.x;
-        v[1] += o.y;
-        v[2] += o.z;
-        v[3] += o.w;
-      }
-      *dst = make_float4(v[0], v[1], v[2], v[3]);
-    } else {
-      for (int e = 0; e < 4; ++e)
-        if (col + e < p.n) crow[col + e] = p.accumulate ? crow[col + e] + v[e] : v[e];
+// Byte offset of 16-byte chunk `c` of row `r` in a 32x32 fp32 box stored with the 128-byte
+// swizzle (the layout TMA reads and writes for a {32, 32} box): rows of 128 B, chunk index
+// XOR-ed with the row's low three bits, so the 8 threads of a shared-memory phase hit 8
+// different bank groups.
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+struct EpiState {
+  uint8_t* bufs;      // this warp's two 4 KB staging boxes
+  uint64_t* aux_bar;  // this warp's two mbarriers for aux-tile loads
+  uint32_t aux_phase[2];
+  uint32_t sel;
+};
+
+// Epilogue of one 32 x 32 box (this warp's 32 accumulator rows x 32 columns): optional aux tile
+// brought in by TMA, alpha/bias/GELU/GELU'/residual applied in registers (thread = row), the
+// result staged in shared memory and written by a TMA store (TMA reduce-add when accumulating).
+// Rows/columns outside the matrix are clipped by the tensor maps.
+__device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, float (&v)[32],
+                                             uint32_t col0, uint32_t row0, uint32_t b1,
+                                             uint32_t b0, bool& ok) {
+  const int lane = threadIdx.x & 31;
+  const bool needs_aux = p.epilogue == SPAR_B200_EPI_BIAS_ADD || p.epilogue == SPAR_B200_EPI_GELU_BWD;
+  const bool two_outputs = p.epilogue == SPAR_B200_EPI_BIAS_GELU;
+  uint8_t* buf = st.bufs + st.sel * 4096;
+  uint8_t* buf2 = st.bufs + (st.sel ^ 1) * 4096;
+  // The staging box (both boxes for two outputs) must be free of earlier stores.
+  if (lane == 0) {
+    if (two_outputs) tc::bulk_wait_read<0>();
+    else tc::bulk_wait_read<1>();
+  }
+  __syncwarp();
+  if (needs_aux) {
+    if (lane == 0) {
+      tc::mbar_arrive_expect_tx(st.aux_bar + st.sel, 4096);
+      tc::tma_load_4d(buf, &p.aux_map, st.aux_bar + st.sel, col0, row0, b1, b0);
     }
   }
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] *= p.alpha;
+  if (p.bias && (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU ||
+                 p.epilogue == SPAR_B200_EPI_BIAS_ADD)) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (col0 + e < p.n) v[e] += __ldg(p.bias + col0 + e);
+  }
+  if (needs_aux) {
+    if (!tc::mbar_wait(st.aux_bar + st.sel, st.aux_phase[st.sel])) {
+      record_error();
+      ok = false;
+    }
+    st.aux_phase[st.sel] ^= 1;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float4 q = *reinterpret_cast<const float4*>(buf + swz(lane, c));
+      const float a4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (p.epilogue == SPAR_B200_EPI_BIAS_ADD) v[4 * c + e] += a4[e];
+        else v[4 * c + e] *= gelu_derivative(a4[e]);
+      }
+    }
+  }
+  if (two_outputs) {  // pre-activation to aux, gelu(pre) to C
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(buf2 + swz(lane, c)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = gelu_value(v[e]);
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(buf + swz(lane, c)) =
+        make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  tc::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (two_outputs) tc::tma_store_4d(&p.aux_map, buf2, col0, row0, b1, b0);
+    if (p.accumulate) tc::tma_reduce_add_4d(&p.c_map, buf, col0, row0, b1, b0);
+    else tc::tma_store_4d(&p.c_map, buf, col0, row0, b1, b0);
+    tc::bulk_commit();
+  }
+  st.sel ^= 1;
 }
 
 // CHUNKED (3xTF32): the tile's K range is accumulated in chunks of p.kchunk k-blocks, each chunk
@@ -185,12 +202,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;  // 4 warps x 2 staging boxes x 4 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + kEpiBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* aux_bars = drain + 1;  // 4 warps x 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -206,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
       tc::mbar_init(tempty + b, 4);
     }
     tc::mbar_init(drain, 1);
+    for (int b = 0; b < 8; ++b) tc::mbar_init(aux_bars + b, 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -349,17 +369,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const uint32_t quarter = static_cast<uint32_t>(warp & 3);
+    EpiState st;
+    st.bufs = epi_smem + quarter * 8192;
+    st.aux_bar = aux_bars + quarter * 2;
+    st.aux_phase[0] = st.aux_phase[1] = 0;
+    st.sel = 0;
+    bool ok = true;
     uint32_t acc = 0, acc_phase = 0;
-    for (uint32_t idx = blockIdx.x; idx < p.total_tiles; idx += gridDim.x) {
+    for (uint32_t idx = blockIdx.x; idx < p.total_tiles && ok; idx += gridDim.x) {
       TileCoord t;
       if (!decode_tile<BN>(p, idx, t)) continue;
       if (*abort_flag) break;
-      const uint32_t row = t.mt * BM + quarter * 32 + lane;
-      const bool row_ok = row < p.m;
-      float* crow = p.c + t.b0 * p.c_bs0 + t.b1 * p.c_bs1 + static_cast<uint64_t>(row) * p.ldc;
-      float* arow = p.aux ? p.aux + t.b0 * p.c_bs0 + t.b1 * p.c_bs1 +
-                                static_cast<uint64_t>(row) * p.ldaux
-                          : nullptr;
+      const uint32_t row0 = t.mt * BM + quarter * 32;
       const uint32_t lane_base = tmem_base + ((quarter * 32) << 16);
       if constexpr (!CHUNKED) {
         if (!tc::mbar_wait(tfull + acc, acc_phase)) {
@@ -370,14 +391,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         tc::tc_fence_after();
 #pragma unroll 1
         for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          const uint32_t col0 = t.nt * BN + chunk * 32;
           uint32_t r[32];
           tc::tmem_load_32x32(lane_base + acc * BN + chunk * 32, r);
-          const uint32_t col0 = t.nt * BN + chunk * 32;
-          if (!row_ok || col0 >= p.n) continue;
+          if (col0 >= p.n) continue;
           float v[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
-          store_row32(p, v, col0, crow, arow);
+          epilogue_box(p, st, v, col0, row0, t.b1, t.b0, ok);
         }
         tc::tc_fence_before();
         __syncwarp();
@@ -390,7 +411,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         uint32_t kb0, kb1;
         k_range(p, t.mt, kb0, kb1);
         float sum[BN];
-        bool ok = true;
         for (uint32_t c0 = kb0; c0 < kb1; c0 += p.kchunk) {
           if (!tc::mbar_wait(tfull + acc, acc_phase)) {
             record_error();
@@ -417,15 +437,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
           }
         }
         if (!ok) break;
-        if (row_ok) {
 #pragma unroll
-          for (int chunk = 0; chunk < BN / 32; ++chunk) {
-            const uint32_t col0 = t.nt * BN + chunk * 32;
-            if (col0 < p.n) store_row32(p, sum + chunk * 32, col0, crow, arow);
-          }
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          const uint32_t col0 = t.nt * BN + chunk * 32;
+          if (col0 >= p.n) continue;
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = sum[chunk * 32 + e];
+          epilogue_box(p, st, v, col0, row0, t.b1, t.b0, ok);
         }
       }
     }
+    if (!ok) *abort_flag = 1;
+    // All staged stores must have finished before the CTA (and its shared memory) goes away.
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
   }
 
   tc::tc_fence_before();
@@ -504,7 +530,7 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows
 
 template <int BN, int STAGES, bool CHUNKED>
 cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) {
-  constexpr size_t smem = STAGES * (BM * BK * 4 + BN * BK * 4) + 1024 + 256;
+  constexpr size_t smem = STAGES * (BM * BK * 4 + BN * BK * 4) + kEpiBytes + 1024 + 256;
   static bool configured[64] = {false};
   auto k = gemm_tf32_kernel<BN, STAGES, CHUNKED>;
   if (device < 0 || device >= 64 || !configured[device]) {
@@ -577,6 +603,12 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
         return cudaErrorInvalidValue;
     }
   }
+  if (!make_map(&p.c_map, g.c, g.n, g.m, b1, b0, g.ldc, g.c_batch_stride[1], g.c_batch_stride[0],
+                32, false))
+    return cudaErrorInvalidValue;
+  if (g.aux && !make_map(&p.aux_map, g.aux, g.n, g.m, b1, b0, g.ldaux, g.c_batch_stride[1],
+                         g.c_batch_stride[0], 32, false))
+    return cudaErrorInvalidValue;
   p.m = static_cast<uint32_t>(g.m);
   p.n = static_cast<uint32_t>(g.n);
   p.k = static_cast<uint32_t>(g.k);
@@ -617,7 +649,8 @@ SparCudaStatus gemm_validate(const SparB200Gemm* g) {
   if (!x.a || !x.b || !x.c) return invalid();
   if (!aligned16(x.a) || !aligned16(x.b) || !aligned16(x.c)) return invalid();
   if (x.lda % 4 || x.ldb % 4 || x.ldc % 4 || x.a_batch_stride[0] % 4 || x.a_batch_stride[1] % 4 ||
-      x.b_batch_stride[0] % 4 || x.b_batch_stride[1] % 4)
+      x.b_batch_stride[0] % 4 || x.b_batch_stride[1] % 4 || x.c_batch_stride[0] % 4 ||
+      x.c_batch_stride[1] % 4)
     return invalid();
   const uint64_t a_inner = x.a_transposed ? x.m : x.k;
   const uint64_t b_inner = x.b_transposed ? x.k : x.n;
