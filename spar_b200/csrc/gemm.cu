@@ -48,6 +48,7 @@ struct GemmParams {
   CUtensorMap b_map[3];
   CUtensorMap c_map;    // output, {32 cols, 32 rows} boxes, 128-byte swizzle
   CUtensorMap aux_map;  // epilogue side input/output (residual, pre-activation), same boxes
+  CUtensorMap part_map;  // split-K partial tiles [kparts][m][n] (raw sums, no epilogue)
   int sections;
   int a_mn_major, b_mn_major;
   uint32_t m, n, k;
@@ -62,14 +63,18 @@ struct GemmParams {
   float alpha;
   int accumulate, epilogue, causal;
   uint32_t kchunk;  // k-blocks per accumulation chunk (chunked kernels only)
+  uint32_t kparts;  // split-K factor (1: no split); partial sums go to part_map
 };
 
 struct TileCoord {
-  uint32_t b0, b1, mt, nt;
+  uint32_t b0, b1, mt, nt, ks;
 };
 
 template <int BN>
 __device__ __forceinline__ bool decode_tile(const GemmParams& p, uint32_t idx, TileCoord& t) {
+  const uint32_t per_split = p.total_tiles / p.kparts;
+  t.ks = idx / per_split;
+  idx -= t.ks * per_split;
   const uint32_t per_batch = p.tiles_m * p.tiles_n;
   const uint32_t bidx = idx / per_batch;
   const uint32_t r = idx - bidx * per_batch;
@@ -88,8 +93,9 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& p, uint32_t idx, T
   return true;
 }
 
-__device__ __forceinline__ void k_range(const GemmParams& p, uint32_t mt, uint32_t& kb0,
+__device__ __forceinline__ void k_range(const GemmParams& p, const TileCoord& t, uint32_t& kb0,
                                         uint32_t& kb1) {
+  const uint32_t mt = t.mt;
   const uint32_t kb_total = (p.k + BK - 1) / BK;
   kb0 = 0;
   kb1 = kb_total;
@@ -98,6 +104,11 @@ __device__ __forceinline__ void k_range(const GemmParams& p, uint32_t mt, uint32
     kb1 = (kend + BK - 1) / BK;
   } else if (p.causal == SPAR_B200_CAUSAL_K_FROM) {
     kb0 = min((mt * BM) / BK, kb_total);
+  }
+  if (p.kparts > 1) {  // split t.ks of kparts (the host guarantees every split is non-empty)
+    const uint32_t per = (kb1 - kb0 + p.kparts - 1) / p.kparts;
+    kb0 = kb0 + t.ks * per;
+    kb1 = min(kb1, kb0 + per);
   }
 }
 
@@ -122,8 +133,25 @@ struct EpiState {
 // Rows/columns outside the matrix are clipped by the tensor maps.
 __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, float (&v)[32],
                                              uint32_t col0, uint32_t row0, uint32_t b1,
-                                             uint32_t b0, bool& ok) {
+                                             uint32_t b0, uint32_t ks, bool& ok) {
   const int lane = threadIdx.x & 31;
+  if (p.kparts > 1) {  // raw partial sum of this K split; the reduction applies the epilogue
+    uint8_t* buf = st.bufs + st.sel * 4096;
+    if (lane == 0) tc::bulk_wait_read<1>();
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(buf + swz(lane, c)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    tc::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tc::tma_store_4d(&p.part_map, buf, col0, row0, ks, 0);
+      tc::bulk_commit();
+    }
+    st.sel ^= 1;
+    return;
+  }
   const bool needs_aux = p.epilogue == SPAR_B200_EPI_BIAS_ADD || p.epilogue == SPAR_B200_EPI_GELU_BWD;
   const bool two_outputs = p.epilogue == SPAR_B200_EPI_BIAS_GELU;
   uint8_t* buf = st.bufs + st.sel * 4096;
@@ -255,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         TileCoord t;
         if (!decode_tile<BN>(p, idx, t)) continue;
         uint32_t kb0, kb1;
-        k_range(p, t.mt, kb0, kb1);
+        k_range(p, t, kb0, kb1);
         const int m0 = static_cast<int>(t.mt * BM), n0 = static_cast<int>(t.nt * BN);
         for (uint32_t kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
           const int k0 = static_cast<int>(kb * BK);
@@ -309,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         TileCoord t;
         if (!decode_tile<BN>(p, idx, t)) continue;
         uint32_t kb0, kb1;
-        k_range(p, t.mt, kb0, kb1);
+        k_range(p, t, kb0, kb1);
         const uint32_t chunk = CHUNKED ? p.kchunk : (kb1 - kb0);
         for (uint32_t c0 = kb0; c0 < kb1 && !*abort_flag; c0 += chunk) {
           const uint32_t c1 = min(c0 + chunk, kb1);
@@ -398,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
           float v[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
-          epilogue_box(p, st, v, col0, row0, t.b1, t.b0, ok);
+          epilogue_box(p, st, v, col0, row0, t.b1, t.b0, t.ks, ok);
         }
         tc::tc_fence_before();
         __syncwarp();
@@ -409,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         }
       } else {
         uint32_t kb0, kb1;
-        k_range(p, t.mt, kb0, kb1);
+        k_range(p, t, kb0, kb1);
         float sum[BN];
         for (uint32_t c0 = kb0; c0 < kb1; c0 += p.kchunk) {
           if (!tc::mbar_wait(tfull + acc, acc_phase)) {
@@ -444,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
           float v[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = sum[chunk * 32 + e];
-          epilogue_box(p, st, v, col0, row0, t.b1, t.b0, ok);
+          epilogue_box(p, st, v, col0, row0, t.b1, t.b0, t.ks, ok);
         }
       }
     }
@@ -488,6 +516,40 @@ __global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo
     const uint64_t o = ((q0 * b1 + q1) * rows + r) * out_ld + x;
     hi[o] = h;
     lo[o] = round_tf32(v - h);
+  }
+}
+
+// Split-K reduction: C (+)= alpha * sum over splits of the partial tiles, summed in split order
+// (deterministic). part: [kparts][m][ldp].
+__global__ void splitk_reduce_kernel(float* __restrict__ c, uint64_t ldc,
+                                     const float* __restrict__ part, uint64_t ldp, uint32_t kparts,
+                                     uint32_t m, uint32_t n, float alpha, int accumulate) {
+  const uint32_t n4 = n / 4;
+  const uint64_t total = static_cast<uint64_t>(m) * n4;
+  const uint64_t plane = static_cast<uint64_t>(m) * ldp;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const uint64_t r = i / n4, c4 = i % n4;
+    const float* src = part + r * ldp + 4 * c4;
+    float4 acc = *reinterpret_cast<const float4*>(src);
+    for (uint32_t s = 1; s < kparts; ++s) {
+      const float4 q = *reinterpret_cast<const float4*>(src + s * plane);
+      acc.x += q.x;
+      acc.y += q.y;
+      acc.z += q.z;
+      acc.w += q.w;
+    }
+    float4* dst = reinterpret_cast<float4*>(c + r * ldc + 4 * c4);
+    float4 o = make_float4(alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w);
+    if (accumulate) {
+      const float4 prev = *dst;
+      o.x += prev.x;
+      o.y += prev.y;
+      o.z += prev.z;
+      o.w += prev.w;
+    }
+    *dst = o;
   }
 }
 
@@ -556,8 +618,38 @@ uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
   return 2 * b * (pad(a_inner) * a_rows + pad(b_inner) * b_rows);
 }
 
+// K splits worth using for this GEMM on `sms` SMs (1 = none): only plain products (no epilogue,
+// no causal limits, no batch, no 3xTF32) with at least 8 k-blocks per split. The persistent grid
+// runs ceil(tiles * parts / sms) rounds of 1/parts-sized work units; the split count with the
+// fewest full-tile-equivalent rounds wins when it saves at least 15% over no split.
+uint32_t splitk_parts(const SparB200Gemm& g, int bn, int sms) {
+  if (g.precision != SPAR_B200_TF32 || g.epilogue != SPAR_B200_EPI_NONE ||
+      g.causal != SPAR_B200_CAUSAL_NONE || (g.batch[0] > 1) || (g.batch[1] > 1) || g.n % 4)
+    return 1;
+  const uint64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + bn - 1) / bn);
+  const uint64_t kblocks = (g.k + BK - 1) / BK;
+  const uint64_t s = static_cast<uint64_t>(sms);
+  double best = static_cast<double>((tiles + s - 1) / s);
+  uint32_t best_parts = 1;
+  for (uint64_t parts = 2; parts <= 8 && parts * 8 <= kblocks; ++parts) {
+    const double rounds = static_cast<double>((tiles * parts + s - 1) / s) / parts;
+    if (rounds < 0.85 * best) {
+      best = rounds;
+      best_parts = static_cast<uint32_t>(parts);
+    }
+  }
+  return best_parts;
+}
+
+uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device) {
+  const int bn = g.n > 128 ? 256 : (g.n > 64 ? 128 : 64);
+  const uint32_t parts = splitk_parts(g, bn, sm_count(device));
+  return parts > 1 ? static_cast<uint64_t>(parts) * g.m * ((g.n + 3) / 4 * 4) : 0;
+}
+
 cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, float* splitk_workspace = nullptr,
+                        uint64_t splitk_floats = 0) {
   GemmParams p;
   memset(&p, 0, sizeof(p));
   const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
@@ -628,6 +720,25 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   p.epilogue = g.epilogue;
   p.causal = g.causal;
   p.kchunk = 4;  // 4 k-blocks = 128 K elements x 3 sections per hardware-accumulated chunk
+  p.kparts = 1;
+  const uint32_t kparts = split ? 1 : splitk_parts(g, bn, sm_count(device));
+  const uint64_t ldp = (g.n + 3) / 4 * 4;
+  if (kparts > 1 && splitk_workspace && splitk_floats >= kparts * g.m * ldp) {
+    if (!make_map(&p.part_map, splitk_workspace, g.n, g.m, kparts, 1, ldp, g.m * ldp,
+                  kparts * g.m * ldp, 32, false))
+      return cudaErrorInvalidValue;
+    p.kparts = kparts;
+    p.total_tiles *= kparts;
+    const cudaError_t e = bn == 256 ? launch_kernel<256, 4, false>(p, device, stream)
+                        : bn == 128 ? launch_kernel<128, 6, false>(p, device, stream)
+                                    : launch_kernel<64, 8, false>(p, device, stream);
+    if (e != cudaSuccess) return e;
+    const uint64_t work = g.m * (g.n / 4);
+    splitk_reduce_kernel<<<grid_for(work, 256, sm_count(device) * 8), 256, 0, stream>>>(
+        g.c, g.ldc, splitk_workspace, ldp, kparts, static_cast<uint32_t>(g.m),
+        static_cast<uint32_t>(g.n), g.alpha, g.accumulate);
+    return cudaGetLastError();
+  }
   if (split) return launch_kernel<64, 8, true>(p, device, stream);
   switch (bn) {
     case 256:
@@ -681,13 +792,20 @@ extern "C" SparCudaStatus spar_b200_gemm(const SparB200Gemm* gemm, int device, v
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* ws = nullptr;
+  float* kws = nullptr;
   if (gemm->precision == SPAR_B200_TF32X3) {
     const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws),
                                           gemm_split_workspace_floats(*gemm) * sizeof(float), s);
     if (e != cudaSuccess) return runtime(e);
   }
-  const cudaError_t e = gemm_launch(*gemm, ws, device, s);
+  const uint64_t kfloats = gemm_splitk_workspace_floats(*gemm, device);
+  if (kfloats) {
+    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&kws), kfloats * sizeof(float), s);
+    if (e != cudaSuccess) return runtime(e);
+  }
+  const cudaError_t e = gemm_launch(*gemm, ws, device, s, kws, kfloats);
   if (ws) cudaFreeAsync(ws, s);
+  if (kws) cudaFreeAsync(kws, s);
   return e == cudaSuccess ? ok() : runtime(e);
 }
 

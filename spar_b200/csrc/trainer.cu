@@ -28,8 +28,9 @@
 namespace spar_b200 {
 
 cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
-                        cudaStream_t stream);
+                        cudaStream_t stream, float* splitk_workspace, uint64_t splitk_floats);
 uint64_t gemm_split_workspace_floats(const SparB200Gemm& g);
+uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device);
 cudaError_t comm_allreduce_sum(void* comm, float* data, uint64_t count, cudaStream_t stream);
 
 namespace {
@@ -107,6 +108,8 @@ class LMTrainer {
   float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
   float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
   float *ln_ws = nullptr, *col_ws = nullptr, *split_ws = nullptr, *rope_tab = nullptr;
+  float* splitk_ws = nullptr;  // split-K partial tiles of the small weight-gradient GEMMs
+  uint64_t splitk_floats = 0;
   void* emb_scratch = nullptr;
   float* row_loss = nullptr;     // [N]
   float* loss_sums = nullptr;    // [kMaxMicro]
@@ -297,6 +300,18 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     }
     f(&split_ws, split_floats);
   }
+  {
+    // Weight-gradient GEMMs whose outputs are small enough to be split along K (tokens).
+    struct Shape { uint64_t m, n; };
+    const Shape dw[] = {{d, 3 * d}, {d, d}, {d, F}, {F, d}, {V, d}};
+    for (const Shape& sh : dw) {
+      SparB200Gemm g{};
+      g.m = sh.m; g.n = sh.n; g.k = N; g.a_transposed = 1; g.batch[0] = g.batch[1] = 1;
+      g.precision = c.precision;
+      splitk_floats = std::max(splitk_floats, gemm_splitk_workspace_floats(g, device));
+    }
+    if (splitk_floats) f(&splitk_ws, splitk_floats);
+  }
   uint64_t total = 0;
   for (auto& pb : plan) total += (pb.second + 255) / 256 * 256;
   e = cudaMalloc(reinterpret_cast<void**>(&act_base), total);
@@ -352,7 +367,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
   // Never let a split copy run past the workspace sized in init().
   if (cfg.precision == SPAR_B200_TF32X3 && gemm_split_workspace_floats(g) > split_floats)
     return cudaErrorInvalidValue;
-  if (!profiling) return gemm_launch(g, split_ws, device, s);
+  if (!profiling) return gemm_launch(g, split_ws, device, s, splitk_ws, splitk_floats);
   if (ev_used == ev_pool.size()) {
     std::pair<cudaEvent_t, cudaEvent_t> pr;
     SPAR_TRY_RAW(cudaEventCreate(&pr.first));
@@ -365,7 +380,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
   auto& pr = ev_pool[ev_used++];
   ev_flops.push_back(fl);
   SPAR_TRY_RAW(cudaEventRecord(pr.first, s));
-  SPAR_TRY_RAW(gemm_launch(g, split_ws, device, s));
+  SPAR_TRY_RAW(gemm_launch(g, split_ws, device, s, splitk_ws, splitk_floats));
   return cudaEventRecord(pr.second, s);
 }
 

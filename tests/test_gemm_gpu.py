@@ -98,6 +98,28 @@ def test_gemm_epilogues(cuda):
     assert rel_err(radd_nb.cpu().numpy(), ref + r) <= 1e-5
 
 
+@pytest.mark.parametrize("m,n,k", [(1024, 1024, 16384), (1024, 3072, 8192), (768, 768, 4096)])
+def test_gemm_split_k_weight_gradient(cuda, m, n, k):
+    """Weight-gradient shapes (A transposed, K = tokens) take the split-K path: partial tiles
+    summed in split order, so accumulate + alpha hold and repeated runs are bitwise equal."""
+    import torch
+    from spar_b200 import ops
+
+    a, b, ref = _mats(m, n, k, True, False, seed=11)
+    at, bt = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    base = torch.from_numpy(np.random.default_rng(12).standard_normal((m, n)).astype(np.float32))
+    outs = []
+    for _ in range(2):
+        c = base.to(cuda)
+        ops.matmul(at, bt, a_t=True, out=c, accumulate=True, alpha=0.5)
+        outs.append(c.cpu().numpy())
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+    assert np.array_equal(outs[0], outs[1])
+    expect = 0.5 * ref + base.numpy().astype(np.float64)
+    assert rel_l2(outs[0], expect) <= 2e-3
+
+
 def _attention_views(cuda, b, h, t, dh, seed=0):
     import torch
 
