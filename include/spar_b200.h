@@ -214,12 +214,38 @@ struct SparB200Gemm {
   uint64_t ldaux;
   int precision; /* SparB200Precision */
   int causal;    /* SparB200Causal */
+  int round_output; /* 1: store C rounded to nearest TF32 (for results that only feed TF32
+                       products, which otherwise drop the low mantissa bits by truncation) */
 };
 struct SparCudaStatus spar_b200_gemm(const struct SparB200Gemm* gemm, int device, void* stream);
 
 /* Returns 1 if a GEMM on `device` gave up on a bounded pipeline wait (the kernel records the    */
 /* event and exits instead of hanging), 0 otherwise, -1 on a CUDA error; clear != 0 resets it.  */
 int spar_b200_gemm_error(int device, int clear);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Fused causal self-attention (tensor cores, TF32 products, fp32 softmax and accumulation).    */
+/* Replaces scaled_dot_product_attention (reference src/nn/attention.cpp:121-135: scores =     */
+/* Q K^T / sqrt(head_dim), causal -inf mask, softmax over keys, P V) and the backward of that   */
+/* chain, without materialising the [seq, seq] scores or probabilities.                         */
+/* qkv: [batch, seq, 3 * heads * head_dim] row-major, Q | K | V thirds, head h at columns       */
+/* h * head_dim of each third (the fused projection output). ctx: [batch, seq, heads*head_dim]. */
+/* row_max / row_inv: [batch, heads, seq] softmax statistics written by the forward (row max of */
+/* scores * scale * log2(e), 1 / sum of exponentials) and read by the backward.                 */
+/* Backward: dctx in, dqkv [batch, seq, 3 * heads * head_dim] out (every column of every row     */
+/* overwritten); delta [batch, heads, seq] is scratch. head_dim must be 32 or 64; pointers      */
+/* 16-byte aligned. Asynchronous on `stream`; deterministic (no atomics).                       */
+struct SparCudaStatus spar_b200_attention_forward(const float* qkv, float* ctx, float* row_max,
+                                                  float* row_inv, uint64_t batch, uint64_t seq,
+                                                  uint64_t heads, uint64_t head_dim, int device,
+                                                  void* stream);
+struct SparCudaStatus spar_b200_attention_backward(const float* qkv, const float* ctx,
+                                                   const float* dctx, const float* row_max,
+                                                   const float* row_inv, float* delta, float* dqkv,
+                                                   uint64_t batch, uint64_t seq, uint64_t heads,
+                                                   uint64_t head_dim, int device, void* stream);
+/* As spar_b200_gemm_error, for the attention kernels' bounded waits. */
+int spar_b200_attention_error(int device, int clear);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Training-step runtime for the pre-LN / GELU decoder LM (BASELINE's model family): tied token */

@@ -167,6 +167,41 @@ def causal_softmax_backward(dp, p, scale, dtype=np.float64):
     return np.where(mask, p * (dp - dot) * scale, 0.0)
 
 
+def attention_forward_backward(qkv, heads, dctx=None, dtype=np.float64):
+    """Causal self-attention over a packed projection buffer qkv [B, T, 3d] (Q | K | V thirds,
+    head h at columns h*dh of each): scaled_dot_product_attention (src/nn/attention.cpp:121-135:
+    matmul(Q, K^T) * 1/sqrt(dh), + causal_mask, softmax over keys, matmul(P, V)) and, given
+    dctx [B, T, d], the autograd backward of that chain (matmul backward, softmax backward
+    src/ops/softmax.cpp:110-150, scalar-multiply backward). Returns (ctx, dqkv or None)."""
+    qkv = np.asarray(qkv, dtype)
+    b, t, d3 = qkv.shape
+    d = d3 // 3
+    dh = d // heads
+    scale = 1.0 / math.sqrt(dh)
+
+    def split(x):  # [B, T, d] -> [B, H, T, dh]
+        return x.reshape(b, t, heads, dh).transpose(0, 2, 1, 3)
+
+    def merge(x):
+        return x.transpose(0, 2, 1, 3).reshape(b, t, d)
+
+    q, k, v = split(qkv[..., :d]), split(qkv[..., d:2 * d]), split(qkv[..., 2 * d:])
+    mask = np.triu(np.ones((t, t), dtype=bool), 1)
+    s = np.where(mask, -np.inf, (q @ k.transpose(0, 1, 3, 2)) * scale)
+    e = np.exp(s - s.max(-1, keepdims=True))
+    pr = e / e.sum(-1, keepdims=True)
+    ctx = merge(pr @ v)
+    if dctx is None:
+        return ctx, None
+    do = split(np.asarray(dctx, dtype))
+    dp = do @ v.transpose(0, 1, 3, 2)
+    dv = pr.transpose(0, 1, 3, 2) @ do
+    ds = pr * (dp - (dp * pr).sum(-1, keepdims=True)) * scale
+    dq = ds @ k
+    dk = ds.transpose(0, 1, 3, 2) @ q
+    return ctx, np.concatenate([merge(dq), merge(dk), merge(dv)], axis=-1)
+
+
 # ------------------------------------------------------------------------------ cross-entropy
 def lm_targets(ids):
     """language_model_cross_entropy target/row selection (src/loss/cross_entropy.cpp:198-209):

@@ -26,6 +26,7 @@ SOURCES = [
     "adamw.cu",
     "embedding.cu",
     "gemm.cu",
+    "attention.cu",
     "compat.cu",
     "trainer.cu",
     "comm.cpp",

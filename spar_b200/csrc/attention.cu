@@ -1,0 +1,1139 @@
+// Fused causal self-attention on the sm_100a tensor cores: tcgen05.mma kind::tf32 with TMEM
+// accumulators, operands staged in shared memory by TMA, the softmax done by the warps that read
+// the score tile out of TMEM. The [T, T] score and probability matrices never reach HBM.
+//
+// This computes what Spar's scaled_dot_product_attention does (src/nn/attention.cpp:121-135:
+// scores = (Q K^T) * 1/sqrt(head_dim), causal -inf mask, softmax over the last axis, P V) and its
+// autograd backward (matmul / softmax backward), for the packed projection buffer
+// qkv [batch, seq, 3*model_dim] (Q | K | V, head h at columns h*head_dim of each third).
+//
+// Forward (one CTA per SM, persistent; work item = (batch, head, 128-query tile), heaviest first):
+//   pass 1  S_j = Q K_j^T for the causal key tiles j, row maxima only (no exponentials);
+//   pass 2  S_j again, P_j = exp(S_j * scale - max) written to shared memory in the MMA's K-major
+//           layout, O += P_j V_j in TMEM, row sums in registers; O / sum stored by TMA.
+//   With the final maximum known before any exponential, O needs no rescaling, and the
+//   probabilities are those of the reference's max-subtracted softmax. The row maximum and
+//   1 / row sum are saved for the backward.
+// Backward (deterministic: every gradient element is written by exactly one CTA, no atomics):
+//   query kernel  per (batch, head, 128-query tile): D = rowsum(dO o O); for each 64-key tile
+//                 S, dP = dO V^T, P recomputed from the saved statistics,
+//                 dS = P o (dP - D) * scale, dQ += dS K; D is saved for the key kernel.
+//   key kernel    per (batch, head, 128-key tile): for each 64-query tile S^T = K Q^T,
+//                 dP^T = V dO^T, P^T and dS^T as above, dV += P^T dO, dK += dS^T Q.
+// Warp roles in every kernel: warp 0 TMA producer, warp 1 MMA issuer (one elected thread),
+// warps 2-9 softmax / epilogue: TMEM lane = tile row (warp w reads lanes 32*(w%4)..+31), and the
+// two warps of each lane quarter split the tile's columns. They exchange row partials through
+// shared memory, synchronised by an mbarrier with a bounded wait (never bar.sync, which cannot
+// time out if a partner warp gave up).
+// Every wait is bounded (2 s) and records an error flag instead of hanging.
+//
+// Precision: products are TF32 with fp32 accumulation. The operands the kernels write themselves
+// (P, dS) are rounded to nearest TF32; Q, K, V and dO are read as stored, so the tensor cores drop
+// their low 13 mantissa bits (truncation) unless the producer stored them rounded to nearest
+// (the training runtime does: QKV projection + RoPE outputs and d ctx are stored TF32-rounded).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace spar_b200 {
+
+__device__ int g_attn_error = 0;
+
+namespace {
+
+constexpr int kSoftWarps = 8;  // two column groups x four TMEM lane quarters
+constexpr int kThreads = 64 + 32 * kSoftWarps;
+constexpr uint32_t kMaxSmem = 232448;  // per-CTA dynamic shared memory limit
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnParams {
+  CUtensorMap qk128;   // qkv, K-major boxes {32 cols, 128 rows}
+  CUtensorMap qk64;    // qkv, K-major boxes {32, 64}
+  CUtensorMap qkv_mn;  // qkv, MN-major boxes {32, 32}
+  CUtensorMap do128;   // dO (= d ctx), K-major {32, 128}
+  CUtensorMap do64;    // dO, K-major {32, 64}
+  CUtensorMap do_mn;   // dO, MN-major {32, 32}
+  CUtensorMap out;     // output store boxes {32, 32}: ctx (forward) or dqkv (backward)
+  const float* o;      // forward output (backward: D = rowsum(dO o O))
+  const float* d_o;    // dO
+  float* row_max;      // [batch*heads, seq]: max of scores * scale * log2(e)
+  float* row_inv;      // [batch*heads, seq]: 1 / sum of exponentials
+  float* delta;        // [batch*heads, seq]: D
+  uint32_t heads, seq, model_dim, bh;
+  uint64_t ld_o;  // row stride of O and dO
+  float scale, scale_log2;
+  uint32_t tiles;  // stationary tiles per (batch, head)
+  uint32_t total;  // work items
+};
+
+__device__ __forceinline__ void record_error() { atomicExch(&g_attn_error, 1); }
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Byte offset of 16-byte chunk c of row r in a K-major operand block stored with the 128-byte
+// swizzle (rows of 128 B = 32 fp32; chunk index XOR the row's low three bits).
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
+  return r * 128 + ((c ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// K-major operand (rows of 32 fp32 per 128-byte swizzle row, 32-column blocks `block_bytes`
+// apart), K step ks of 8 elements.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, uint32_t block_bytes, int ks) {
+  return tc::smem_desc(base + (ks >> 2) * block_bytes + (ks & 3) * 32, 16, 1024, tc::kLayoutSw128);
+}
+
+// MN-major operand stored as 32-row K blocks of DH/32 boxes {32 MN, 32 K} (4 KB each).
+template <int DH>
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int ks) {
+  return tc::smem_desc(base + (ks >> 2) * (DH / 32) * 4096 + (ks & 3) * 1024, 4096, 512,
+                       tc::kLayoutSw128Base32);
+}
+
+// Writes 32 fp32 values (columns c*32..c*32+31 of row r) into a K-major swizzled block.
+__device__ __forceinline__ void store_row32(uint8_t* block, uint32_t r, const float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    *reinterpret_cast<float4*>(block + swz(r, i)) =
+        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+struct Item {
+  uint32_t b, h, t;
+};
+
+__device__ __forceinline__ Item decode(const AttnParams& p, uint32_t idx, bool descending) {
+  const uint32_t tile = idx / p.bh;
+  const uint32_t bh = idx - tile * p.bh;
+  Item it;
+  it.b = bh / p.heads;
+  it.h = bh - it.b * p.heads;
+  it.t = descending ? p.tiles - 1 - tile : tile;
+  return it;
+}
+
+// Stages one 32-row x 32-column fp32 box (this warp's rows) and stores it through `map`.
+__device__ __forceinline__ void store_box(const CUtensorMap* map, uint8_t* buf, const float (&v)[32],
+                                          int col, int row, int b) {
+  const uint32_t lane = threadIdx.x & 31;
+  store_row32(buf, lane, v);
+  tc::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) tc::tma_store_4d(map, buf, col, row, b, 0);
+}
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (tc::mbar_wait(bar, parity)) return true;
+  record_error();
+  *abort = 1;
+  return false;
+}
+
+// Rendezvous of the softmax warps (mbarrier with kSoftWarps arrivals, bounded wait). Shared
+// memory written before it is visible to every softmax thread after it.
+__device__ __forceinline__ bool soft_sync(uint64_t* bar, uint32_t& phase, volatile int* abort) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) tc::mbar_arrive(bar);
+  const bool ok = wait_or_abort(bar, phase, abort);
+  phase ^= 1;
+  return ok;
+}
+
+// Identity of a softmax thread: tile row r (= TMEM lane), column group, lane quarter.
+struct SoftThread {
+  uint32_t quarter, grp, r, lanes;
+  __device__ SoftThread(int warp, int lane, uint32_t tmem) {
+    quarter = warp & 3;
+    grp = (warp - 2) >> 2;
+    r = quarter * 32 + lane;
+    lanes = tmem + ((quarter * 32) << 16);
+  }
+};
+
+// ============================================================================ forward
+template <int DH>
+struct Fwd {
+  static constexpr uint32_t kTile = DH * 512;  // 128 rows x DH fp32
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kK = kQ + kTile;      // 2 stages
+  static constexpr uint32_t kV = kK + 2 * kTile;  // 2 stages
+  static constexpr uint32_t kP = kV + 2 * kTile;  // 128 x 128 probabilities, 4 K blocks of 16 KB
+  static constexpr uint32_t kBar = kP + 65536;
+  static constexpr uint32_t kSmem = kBar + 256 + 1024;
+  static_assert(kSmem <= kMaxSmem, "forward shared memory");
+};
+
+template <int DH>
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
+  using L = Fwd<DH>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;   // [2]
+  uint64_t* kv_empty = bars + 4;  // [2]
+  uint64_t* s_full = bars + 6;    // [2]
+  uint64_t* s_empty = bars + 8;   // [2]
+  uint64_t* p_full = bars + 10;
+  uint64_t* p_empty = bars + 11;
+  uint64_t* o_full = bars + 12;
+  uint64_t* o_empty = bars + 13;
+  uint64_t* xbar = bars + 14;  // softmax-warp rendezvous
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    tc::mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(kv_full + i, 1);
+      tc::mbar_init(kv_empty + i, 1);
+      tc::mbar_init(s_full + i, 1);
+      tc::mbar_init(s_empty + i, kSoftWarps);
+    }
+    tc::mbar_init(p_full, kSoftWarps);
+    tc::mbar_init(p_empty, 1);
+    tc::mbar_init(o_full, 1);
+    tc::mbar_init(o_empty, kSoftWarps);
+    tc::mbar_init(xbar, kSoftWarps);
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int dcol = static_cast<int>(p.model_dim);
+
+  if (warp == 0) {
+    // -------------------------------------------------------------- TMA producer
+    if (tc::elect_one()) {
+      tc::tma_prefetch(&p.qk128);
+      tc::tma_prefetch(&p.qkv_mn);
+      uint32_t n = 0, item = 0;
+      int last_q = -1, last_kv[2] = {-1, -1};
+      for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
+        const Item it = decode(p, idx, true);
+        const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
+        if (!wait_or_abort(q_empty, (item & 1) ^ 1, abort_flag)) break;
+        tc::mbar_arrive_expect_tx(q_full, L::kTile);
+        last_q = item & 1;
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c)
+          tc::tma_load_4d(smem + L::kQ + c * 16384, &p.qk128, q_full, hc + 32 * c,
+                          static_cast<int>(it.t * 128), b, 0);
+        const uint32_t nkv = it.t + 1;
+        for (uint32_t pass = 0; pass < 2 && !*abort_flag; ++pass) {
+          for (uint32_t j = 0; j < nkv; ++j, ++n) {
+            const uint32_t st = n & 1;
+            if (!wait_or_abort(kv_empty + st, ((n >> 1) & 1) ^ 1, abort_flag)) break;
+            tc::mbar_arrive_expect_tx(kv_full + st, pass ? 2 * L::kTile : L::kTile);
+            last_kv[st] = (n >> 1) & 1;
+            const int row = static_cast<int>(j * 128);
+#pragma unroll
+            for (int c = 0; c < DH / 32; ++c)
+              tc::tma_load_4d(smem + L::kK + st * L::kTile + c * 16384, &p.qk128, kv_full + st,
+                              dcol + hc + 32 * c, row, b, 0);
+            if (pass) {
+#pragma unroll
+              for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+                for (int c = 0; c < DH / 32; ++c)
+                  tc::tma_load_4d(smem + L::kV + st * L::kTile + (kb * (DH / 32) + c) * 4096,
+                                  &p.qkv_mn, kv_full + st, 2 * dcol + hc + 32 * c, row + 32 * kb,
+                                  b, 0);
+            }
+          }
+        }
+      }
+      if (last_q >= 0 && !tc::mbar_wait(q_full, last_q)) record_error();
+      for (int s = 0; s < 2; ++s)
+        if (last_kv[s] >= 0 && !tc::mbar_wait(kv_full + s, last_kv[s])) record_error();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- MMA issuer
+    if (tc::elect_one()) {
+      const uint32_t idesc_s = tc::idesc_tf32(128, 128, 0, 0);
+      const uint32_t idesc_o = tc::idesc_tf32(128, DH, 0, 1);
+      const uint32_t q_addr = tc::smem_u32(smem + L::kQ);
+      const uint32_t k_addr = tc::smem_u32(smem + L::kK);
+      const uint32_t v_addr = tc::smem_u32(smem + L::kV);
+      const uint32_t p_addr = tc::smem_u32(smem + L::kP);
+      uint32_t n = 0, sn = 0, pn = 0, item = 0;
+      bool ok = true;
+      // S[sn & 1] = Q K^T for the kv stage of load number kn.
+      auto issue_s = [&](uint32_t kn) -> bool {
+        const uint32_t st = kn & 1, sb = sn & 1;
+        if (!wait_or_abort(kv_full + st, (kn >> 1) & 1, abort_flag)) return false;
+        if (!wait_or_abort(s_empty + sb, ((sn >> 1) & 1) ^ 1, abort_flag)) return false;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < DH / 8; ++ks)
+          tc::mma_tf32(tmem + sb * 128, kmajor_desc(q_addr, 16384, ks),
+                       kmajor_desc(k_addr + st * L::kTile, 16384, ks), idesc_s, ks > 0);
+        tc::mma_commit(s_full + sb);
+        ++sn;
+        return true;
+      };
+      for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x, ++item) {
+        const Item it = decode(p, idx, true);
+        const uint32_t nkv = it.t + 1;
+        if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        for (uint32_t j = 0; j < nkv && ok; ++j, ++n) {  // pass 1
+          if (!(ok = issue_s(n))) break;
+          tc::mma_commit(kv_empty + (n & 1));
+        }
+        if (!ok) break;
+        // pass 2: S_{j+1} is issued before O += P_j V_j so the softmax of tile j+1 overlaps it.
+        const uint32_t n0 = n;
+        if (!(ok = issue_s(n0))) break;
+        for (uint32_t j = 0; j < nkv && ok; ++j) {
+          if (j + 1 < nkv) {
+            if (!(ok = issue_s(n0 + j + 1))) break;
+          }
+          if (j + 1 == nkv) tc::mma_commit(q_empty);  // Q is no longer read in this item
+          if (!(ok = wait_or_abort(p_full, pn & 1, abort_flag))) break;
+          ++pn;
+          if (j == 0 && !(ok = wait_or_abort(o_empty, (item & 1) ^ 1, abort_flag))) break;
+          tc::tc_fence_after();
+          const uint32_t st = (n0 + j) & 1;
+#pragma unroll
+          for (int ks = 0; ks < 16; ++ks)
+            tc::mma_tf32(tmem + 256, kmajor_desc(p_addr, 16384, ks),
+                         mnmajor_desc<DH>(v_addr + st * L::kTile, ks), idesc_o, (j | ks) != 0);
+          tc::mma_commit(p_empty);
+          tc::mma_commit(kv_empty + st);
+        }
+        n = n0 + nkv;
+        if (ok) tc::mma_commit(o_full);
+      }
+      tc::mma_commit(drain);
+      if (!tc::mbar_wait(drain, 0)) record_error();
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------------- softmax + epilogue
+    // Thread (r, grp) owns columns [64*grp, 64*grp + 64) of row r of every 128 x 128 score tile.
+    const SoftThread th(warp, lane, tmem);
+    const uint32_t r = th.r, grp = th.grp;
+    uint8_t* pbuf = smem + L::kP;
+    // Row partials are exchanged through K block 3 of the P buffer, which no MMA reads and no
+    // output staging uses at the points where the exchanges happen.
+    float* xmax = reinterpret_cast<float*>(pbuf + 3 * 16384);  // [2][128]
+    float* xsum = xmax + 256;                                   // [2][128]
+    uint32_t sn = 0, pn = 0, item = 0, xphase = 0;
+    bool ok = true;
+    for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
+      const Item it = decode(p, idx, true);
+      const uint32_t nkv = it.t + 1;
+      const uint32_t qrow = it.t * 128 + r;
+      float vmax = -INFINITY;  // max of the raw scores (scale > 0 commutes with max)
+      for (uint32_t j = 0; j < nkv && ok; ++j, ++sn) {  // pass 1: row maxima
+        if (!(ok = wait_or_abort(s_full + (sn & 1), (sn >> 1) & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        uint32_t v0[32], v1[32];
+        const uint32_t base = th.lanes + (sn & 1) * 128 + grp * 64;
+        tc::tmem_load_2x32(base, base + 32, v0, v1);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(s_empty + (sn & 1));
+        if (j != it.t) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            vmax = fmaxf(vmax, fmaxf(__uint_as_float(v0[e]), __uint_as_float(v1[e])));
+        } else {  // diagonal tile: keys up to the row only
+          const uint32_t c0 = grp * 64;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (c0 + e <= r) vmax = fmaxf(vmax, __uint_as_float(v0[e]));
+            if (c0 + 32 + e <= r) vmax = fmaxf(vmax, __uint_as_float(v1[e]));
+          }
+        }
+      }
+      if (!ok) break;
+      xmax[grp * 128 + r] = vmax;
+      if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
+      const float mx = fmaxf(xmax[r], xmax[128 + r]) * p.scale_log2;
+      if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;  // K block 3 free for P again
+      float sum = 0.f;
+      if (lane == 0) tc::bulk_wait_read<0>();  // earlier output staging in the P block is read
+      __syncwarp();
+      for (uint32_t j = 0; j < nkv && ok; ++j, ++sn) {  // pass 2: probabilities
+        if (!(ok = wait_or_abort(s_full + (sn & 1), (sn >> 1) & 1, abort_flag))) break;
+        if (pn > 0 && !(ok = wait_or_abort(p_empty, (pn - 1) & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        uint32_t v0[32], v1[32];
+        const uint32_t base = th.lanes + (sn & 1) * 128 + grp * 64;
+        tc::tmem_load_2x32(base, base + 32, v0, v1);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(s_empty + (sn & 1));
+        float pr[32];
+        const bool diag = j == it.t;
+        const uint32_t c0 = grp * 64;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float pe = ex2(fmaf(__uint_as_float(v0[e]), p.scale_log2, -mx));
+          if (diag && c0 + e > r) pe = 0.f;
+          sum += pe;
+          pr[e] = round_tf32(pe);  // the P V operand, rounded to nearest instead of truncated
+        }
+        store_row32(pbuf + (2 * grp) * 16384, r, pr);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float pe = ex2(fmaf(__uint_as_float(v1[e]), p.scale_log2, -mx));
+          if (diag && c0 + 32 + e > r) pe = 0.f;
+          sum += pe;
+          pr[e] = round_tf32(pe);
+        }
+        store_row32(pbuf + (2 * grp + 1) * 16384, r, pr);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(p_full);
+        ++pn;
+      }
+      if (!ok) break;
+      if (!(ok = wait_or_abort(o_full, item & 1, abort_flag))) break;
+      tc::tc_fence_after();
+      xsum[grp * 128 + r] = sum;
+      if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
+      const float inv = 1.f / (xsum[r] + xsum[128 + r]);
+      if (grp < DH / 32) {
+        uint32_t v[32];
+        tc::tmem_load_32x32(th.lanes + 256 + grp * 32, v);
+        float o[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]) * inv;
+        // This warp's rows of K block grp of the (now idle) P buffer serve as its staging box.
+        store_box(&p.out, pbuf + grp * 16384 + th.quarter * 4096, o,
+                  static_cast<int>(it.h * DH + 32 * grp),
+                  static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
+        if (lane == 0) tc::bulk_commit();
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(o_empty);
+      if (grp == 0 && qrow < p.seq) {
+        const uint64_t s = static_cast<uint64_t>(it.b * p.heads + it.h) * p.seq + qrow;
+        p.row_max[s] = mx;
+        p.row_inv[s] = inv;
+      }
+    }
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ============================================================================ backward: queries
+template <int DH>
+struct BwdQ {
+  static constexpr uint32_t kTile128 = DH * 512;  // 128 rows x DH
+  static constexpr uint32_t kTile64 = DH * 256;   // 64 rows x DH
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kDO = kQ + kTile128;
+  static constexpr uint32_t kStage = 3 * kTile64;  // K (K-major), V (K-major), K (MN-major)
+  static constexpr uint32_t kKV = kDO + kTile128;   // 2 stages
+  static constexpr uint32_t kDS = kKV + 2 * kStage;  // 128 x 64 dS, 2 K blocks of 16 KB
+  static constexpr uint32_t kBar = kDS + 32768;
+  static constexpr uint32_t kSmem = kBar + 256 + 1024;
+  static_assert(kSmem <= kMaxSmem, "query-kernel shared memory");
+};
+
+template <int DH>
+__global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_constant__ AttnParams p) {
+  using L = BwdQ<DH>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;   // [2]
+  uint64_t* kv_empty = bars + 4;  // [2]
+  uint64_t* s_full = bars + 6;    // [2]
+  uint64_t* s_empty = bars + 8;   // [2]
+  uint64_t* ds_full = bars + 10;
+  uint64_t* ds_empty = bars + 11;
+  uint64_t* acc_full = bars + 12;
+  uint64_t* acc_empty = bars + 13;
+  uint64_t* drain = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    tc::mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(kv_full + i, 1);
+      tc::mbar_init(kv_empty + i, 1);
+      tc::mbar_init(s_full + i, 1);
+      tc::mbar_init(s_empty + i, kSoftWarps);
+    }
+    tc::mbar_init(ds_full, kSoftWarps);
+    tc::mbar_init(ds_empty, 1);
+    tc::mbar_init(acc_full, 1);
+    tc::mbar_init(acc_empty, kSoftWarps);
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int dcol = static_cast<int>(p.model_dim);
+  const uint32_t seq = p.seq;
+
+  if (warp == 0) {
+    if (tc::elect_one()) {
+      uint32_t n = 0, item = 0;
+      int last_q = -1, last_kv[2] = {-1, -1};
+      for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
+        const Item it = decode(p, idx, true);
+        const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
+        if (!wait_or_abort(q_empty, (item & 1) ^ 1, abort_flag)) break;
+        tc::mbar_arrive_expect_tx(q_full, 2 * L::kTile128);
+        last_q = item & 1;
+        const int q0 = static_cast<int>(it.t * 128);
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) {
+          tc::tma_load_4d(smem + L::kQ + c * 16384, &p.qk128, q_full, hc + 32 * c, q0, b, 0);
+          tc::tma_load_4d(smem + L::kDO + c * 16384, &p.do128, q_full, hc + 32 * c, q0, b, 0);
+        }
+        const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
+        for (uint32_t j = 0; j < nkv; ++j, ++n) {
+          const uint32_t st = n & 1;
+          if (!wait_or_abort(kv_empty + st, ((n >> 1) & 1) ^ 1, abort_flag)) break;
+          tc::mbar_arrive_expect_tx(kv_full + st, L::kStage);
+          last_kv[st] = (n >> 1) & 1;
+          uint8_t* s = smem + L::kKV + st * L::kStage;
+          const int row = static_cast<int>(j * 64);
+#pragma unroll
+          for (int c = 0; c < DH / 32; ++c) {
+            tc::tma_load_4d(s + c * 8192, &p.qk64, kv_full + st, dcol + hc + 32 * c, row, b, 0);
+            tc::tma_load_4d(s + L::kTile64 + c * 8192, &p.qk64, kv_full + st,
+                            2 * dcol + hc + 32 * c, row, b, 0);
+          }
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int c = 0; c < DH / 32; ++c)
+              tc::tma_load_4d(s + 2 * L::kTile64 + (kb * (DH / 32) + c) * 4096, &p.qkv_mn,
+                              kv_full + st, dcol + hc + 32 * c, row + 32 * kb, b, 0);
+        }
+      }
+      if (last_q >= 0 && !tc::mbar_wait(q_full, last_q)) record_error();
+      for (int s = 0; s < 2; ++s)
+        if (last_kv[s] >= 0 && !tc::mbar_wait(kv_full + s, last_kv[s])) record_error();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (tc::elect_one()) {
+      const uint32_t idesc_s = tc::idesc_tf32(128, 64, 0, 0);
+      const uint32_t idesc_q = tc::idesc_tf32(128, DH, 0, 1);
+      const uint32_t q_addr = tc::smem_u32(smem + L::kQ);
+      const uint32_t do_addr = tc::smem_u32(smem + L::kDO);
+      const uint32_t kv_addr = tc::smem_u32(smem + L::kKV);
+      const uint32_t ds_addr = tc::smem_u32(smem + L::kDS);
+      uint32_t n = 0, sn = 0, dn = 0, item = 0;
+      bool ok = true;
+      auto issue_s = [&](uint32_t kn) -> bool {  // S and dP for kv load number kn
+        const uint32_t st = kn & 1, sb = sn & 1;
+        if (!wait_or_abort(kv_full + st, (kn >> 1) & 1, abort_flag)) return false;
+        if (!wait_or_abort(s_empty + sb, ((sn >> 1) & 1) ^ 1, abort_flag)) return false;
+        tc::tc_fence_after();
+        const uint32_t s = kv_addr + st * L::kStage;
+#pragma unroll
+        for (int ks = 0; ks < DH / 8; ++ks) {
+          tc::mma_tf32(tmem + sb * 64, kmajor_desc(q_addr, 16384, ks), kmajor_desc(s, 8192, ks),
+                       idesc_s, ks > 0);
+          tc::mma_tf32(tmem + 128 + sb * 64, kmajor_desc(do_addr, 16384, ks),
+                       kmajor_desc(s + L::kTile64, 8192, ks), idesc_s, ks > 0);
+        }
+        tc::mma_commit(s_full + sb);
+        ++sn;
+        return true;
+      };
+      for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x, ++item) {
+        const Item it = decode(p, idx, true);
+        const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
+        if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        const uint32_t n0 = n;
+        if (!(ok = issue_s(n0))) break;
+        for (uint32_t j = 0; j < nkv && ok; ++j) {
+          if (j + 1 < nkv) {
+            if (!(ok = issue_s(n0 + j + 1))) break;
+          }
+          if (j + 1 == nkv) tc::mma_commit(q_empty);
+          if (!(ok = wait_or_abort(ds_full, dn & 1, abort_flag))) break;
+          ++dn;
+          if (j == 0 && !(ok = wait_or_abort(acc_empty, (item & 1) ^ 1, abort_flag))) break;
+          tc::tc_fence_after();
+          const uint32_t st = (n0 + j) & 1;
+          const uint32_t kmn = kv_addr + st * L::kStage + 2 * L::kTile64;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            tc::mma_tf32(tmem + 256, kmajor_desc(ds_addr, 16384, ks), mnmajor_desc<DH>(kmn, ks),
+                         idesc_q, (j | ks) != 0);
+          tc::mma_commit(ds_empty);
+          tc::mma_commit(kv_empty + st);
+        }
+        n = n0 + nkv;
+        if (ok) tc::mma_commit(acc_full);
+      }
+      tc::mma_commit(drain);
+      if (!tc::mbar_wait(drain, 0)) record_error();
+    }
+    __syncwarp();
+  } else {
+    // Thread (r, grp) owns key columns [32*grp, 32*grp + 32) of every 128 x 64 tile.
+    const SoftThread th(warp, lane, tmem);
+    const uint32_t r = th.r, grp = th.grp;
+    uint8_t* dsbuf = smem + L::kDS;
+    uint32_t sn = 0, dn = 0, item = 0;
+    bool ok = true;
+    for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
+      const Item it = decode(p, idx, true);
+      const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
+      const uint32_t q = it.t * 128 + r;
+      const bool valid = q < seq;
+      const uint64_t srow = static_cast<uint64_t>(it.b * p.heads + it.h) * seq + q;
+      // Rows past the sequence: mx = 0, inv = 0 make every probability 0 (their scores are 0).
+      float mx = 0.f, inv = 0.f, dd = 0.f;
+      if (valid) {
+        mx = p.row_max[srow];
+        inv = p.row_inv[srow];
+        const uint64_t off = (static_cast<uint64_t>(it.b) * seq + q) * p.ld_o + it.h * DH;
+        const float4* a = reinterpret_cast<const float4*>(p.d_o + off);
+        const float4* o = reinterpret_cast<const float4*>(p.o + off);
+#pragma unroll
+        for (int i = 0; i < DH / 4; ++i) {
+          const float4 x = __ldg(a + i), y = __ldg(o + i);
+          dd += x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
+        }
+        if (grp == 0) p.delta[srow] = dd;
+      }
+      const float ninv_scale = inv * p.scale;
+      if (lane == 0) tc::bulk_wait_read<0>();
+      __syncwarp();
+      for (uint32_t j = 0; j < nkv && ok; ++j, ++sn) {
+        if (!(ok = wait_or_abort(s_full + (sn & 1), (sn >> 1) & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        uint32_t sv[32], pv[32];
+        tc::tmem_load_2x32(th.lanes + (sn & 1) * 64 + grp * 32,
+                           th.lanes + 128 + (sn & 1) * 64 + grp * 32, sv, pv);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(s_empty + (sn & 1));
+        const uint32_t kv0 = j * 64 + grp * 32;
+        float ds[32];
+        if (kv0 + 31 <= it.t * 128) {  // every key of this chunk precedes every row of the tile
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float pr = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -mx));
+            ds[e] = round_tf32(pr * ninv_scale * (__uint_as_float(pv[e]) - dd));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float pr = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -mx));
+            if (kv0 + e > q) pr = 0.f;
+            ds[e] = round_tf32(pr * ninv_scale * (__uint_as_float(pv[e]) - dd));
+          }
+        }
+        if (dn > 0 && !(ok = wait_or_abort(ds_empty, (dn - 1) & 1, abort_flag))) break;
+        store_row32(dsbuf + grp * 16384, r, ds);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(ds_full);
+        ++dn;
+      }
+      if (!ok) break;
+      if (!(ok = wait_or_abort(acc_full, item & 1, abort_flag))) break;
+      tc::tc_fence_after();
+      if (grp < DH / 32) {
+        uint32_t v[32];
+        tc::tmem_load_32x32(th.lanes + 256 + grp * 32, v);
+        float o[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);
+        store_box(&p.out, dsbuf + grp * 16384 + th.quarter * 4096, o,
+                  static_cast<int>(it.h * DH + 32 * grp),
+                  static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
+        if (lane == 0) tc::bulk_commit();
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(acc_empty);
+    }
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ============================================================================ backward: keys
+template <int DH>
+struct BwdKV {
+  static constexpr uint32_t kTile128 = DH * 512;
+  static constexpr uint32_t kTile64 = DH * 256;
+  static constexpr uint32_t kK = 0;
+  static constexpr uint32_t kV = kK + kTile128;
+  static constexpr uint32_t kKQ = kV + kTile128;      // 2 stages: Q and dO K-major (64 rows)
+  static constexpr uint32_t kMN = kKQ + 4 * kTile64;  // 1 stage: Q and dO MN-major
+  static constexpr uint32_t kPT = kMN + 2 * kTile64;  // 128 x 64 P^T
+  static constexpr uint32_t kDST = kPT + 32768;       // 128 x 64 dS^T
+  static constexpr uint32_t kStats = kDST + 32768;    // [2 steps][row max, 1/sum, D][64 queries]
+  static constexpr uint32_t kBar = kStats + 2 * 3 * 64 * 4;
+  static constexpr uint32_t kSmem = kBar + 192 + 1024;
+  static_assert(kSmem <= kMaxSmem, "key-kernel shared memory");
+};
+
+template <int DH>
+__global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_constant__ AttnParams p) {
+  using L = BwdKV<DH>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* kq_full = bars + 2;   // [2]
+  uint64_t* kq_empty = bars + 4;  // [2]
+  uint64_t* s_full = bars + 6;    // [2]
+  uint64_t* s_empty = bars + 8;   // [2]
+  uint64_t* mn_full = bars + 10;
+  uint64_t* mn_empty = bars + 11;
+  uint64_t* pd_full = bars + 12;
+  uint64_t* pd_empty = bars + 13;
+  uint64_t* acc_full = bars + 14;
+  uint64_t* acc_empty = bars + 15;
+  uint64_t* drain = bars + 16;
+  uint64_t* xbar = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(kv_full, 1);
+    tc::mbar_init(kv_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(kq_full + i, 1);
+      tc::mbar_init(kq_empty + i, 1);
+      tc::mbar_init(s_full + i, 1);
+      tc::mbar_init(s_empty + i, kSoftWarps);
+    }
+    tc::mbar_init(mn_full, 1);
+    tc::mbar_init(mn_empty, 1);
+    tc::mbar_init(pd_full, kSoftWarps);
+    tc::mbar_init(pd_empty, 1);
+    tc::mbar_init(acc_full, 1);
+    tc::mbar_init(acc_empty, kSoftWarps);
+    tc::mbar_init(drain, 1);
+    tc::mbar_init(xbar, kSoftWarps);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int dcol = static_cast<int>(p.model_dim);
+  const uint32_t seq = p.seq;
+  const uint32_t nq_all = (seq + 63) / 64;
+
+  if (warp == 0) {
+    if (tc::elect_one()) {
+      uint32_t n = 0, item = 0;
+      int last_kv = -1, last_kq[2] = {-1, -1}, last_mn = -1;
+      for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
+        const Item it = decode(p, idx, false);
+        const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
+        if (!wait_or_abort(kv_empty, (item & 1) ^ 1, abort_flag)) break;
+        tc::mbar_arrive_expect_tx(kv_full, 2 * L::kTile128);
+        last_kv = item & 1;
+        const int k0 = static_cast<int>(it.t * 128);
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) {
+          tc::tma_load_4d(smem + L::kK + c * 16384, &p.qk128, kv_full, dcol + hc + 32 * c, k0, b, 0);
+          tc::tma_load_4d(smem + L::kV + c * 16384, &p.qk128, kv_full, 2 * dcol + hc + 32 * c, k0,
+                          b, 0);
+        }
+        for (uint32_t i = 2 * it.t; i < nq_all; ++i, ++n) {
+          const uint32_t st = n & 1;
+          const int row = static_cast<int>(i * 64);
+          if (!wait_or_abort(kq_empty + st, ((n >> 1) & 1) ^ 1, abort_flag)) break;
+          tc::mbar_arrive_expect_tx(kq_full + st, 2 * L::kTile64);
+          last_kq[st] = (n >> 1) & 1;
+          uint8_t* s = smem + L::kKQ + st * 2 * L::kTile64;
+#pragma unroll
+          for (int c = 0; c < DH / 32; ++c) {
+            tc::tma_load_4d(s + c * 8192, &p.qk64, kq_full + st, hc + 32 * c, row, b, 0);
+            tc::tma_load_4d(s + L::kTile64 + c * 8192, &p.do64, kq_full + st, hc + 32 * c, row, b, 0);
+          }
+          if (!wait_or_abort(mn_empty, (n & 1) ^ 1, abort_flag)) break;
+          tc::mbar_arrive_expect_tx(mn_full, 2 * L::kTile64);
+          last_mn = n & 1;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int c = 0; c < DH / 32; ++c) {
+              const uint32_t o = (kb * (DH / 32) + c) * 4096;
+              tc::tma_load_4d(smem + L::kMN + o, &p.qkv_mn, mn_full, hc + 32 * c, row + 32 * kb, b, 0);
+              tc::tma_load_4d(smem + L::kMN + L::kTile64 + o, &p.do_mn, mn_full, hc + 32 * c,
+                              row + 32 * kb, b, 0);
+            }
+        }
+      }
+      if (last_kv >= 0 && !tc::mbar_wait(kv_full, last_kv)) record_error();
+      if (last_mn >= 0 && !tc::mbar_wait(mn_full, last_mn)) record_error();
+      for (int s = 0; s < 2; ++s)
+        if (last_kq[s] >= 0 && !tc::mbar_wait(kq_full + s, last_kq[s])) record_error();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (tc::elect_one()) {
+      const uint32_t idesc_s = tc::idesc_tf32(128, 64, 0, 0);
+      const uint32_t idesc_g = tc::idesc_tf32(128, DH, 0, 1);
+      const uint32_t k_addr = tc::smem_u32(smem + L::kK);
+      const uint32_t v_addr = tc::smem_u32(smem + L::kV);
+      const uint32_t kq_addr = tc::smem_u32(smem + L::kKQ);
+      const uint32_t mn_addr = tc::smem_u32(smem + L::kMN);
+      const uint32_t pt_addr = tc::smem_u32(smem + L::kPT);
+      const uint32_t dst_addr = tc::smem_u32(smem + L::kDST);
+      uint32_t n = 0, sn = 0, item = 0;
+      bool ok = true;
+      auto issue_s = [&](uint32_t qn) -> bool {  // S^T and dP^T for query load number qn
+        const uint32_t st = qn & 1, sb = sn & 1;
+        if (!wait_or_abort(kq_full + st, (qn >> 1) & 1, abort_flag)) return false;
+        if (!wait_or_abort(s_empty + sb, ((sn >> 1) & 1) ^ 1, abort_flag)) return false;
+        tc::tc_fence_after();
+        const uint32_t s = kq_addr + st * 2 * L::kTile64;
+#pragma unroll
+        for (int ks = 0; ks < DH / 8; ++ks) {
+          tc::mma_tf32(tmem + sb * 64, kmajor_desc(k_addr, 16384, ks), kmajor_desc(s, 8192, ks),
+                       idesc_s, ks > 0);
+          tc::mma_tf32(tmem + 128 + sb * 64, kmajor_desc(v_addr, 16384, ks),
+                       kmajor_desc(s + L::kTile64, 8192, ks), idesc_s, ks > 0);
+        }
+        tc::mma_commit(kq_empty + st);
+        tc::mma_commit(s_full + sb);
+        ++sn;
+        return true;
+      };
+      for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x, ++item) {
+        const Item it = decode(p, idx, false);
+        const uint32_t steps = nq_all - 2 * it.t;  // >= 1: every 128-key tile starts below seq
+        if (!(ok = wait_or_abort(kv_full, item & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        const uint32_t n0 = n;
+        if (!(ok = issue_s(n0))) break;
+        for (uint32_t i = 0; i < steps && ok; ++i) {
+          if (i + 1 < steps) {
+            if (!(ok = issue_s(n0 + i + 1))) break;
+          }
+          if (i + 1 == steps) tc::mma_commit(kv_empty);
+          if (!(ok = wait_or_abort(pd_full, (n0 + i) & 1, abort_flag))) break;
+          if (!(ok = wait_or_abort(mn_full, (n0 + i) & 1, abort_flag))) break;
+          if (i == 0 && !(ok = wait_or_abort(acc_empty, (item & 1) ^ 1, abort_flag))) break;
+          tc::tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            tc::mma_tf32(tmem + 256, kmajor_desc(pt_addr, 16384, ks),
+                         mnmajor_desc<DH>(mn_addr + L::kTile64, ks), idesc_g, (i | ks) != 0);
+            tc::mma_tf32(tmem + 256 + DH, kmajor_desc(dst_addr, 16384, ks),
+                         mnmajor_desc<DH>(mn_addr, ks), idesc_g, (i | ks) != 0);
+          }
+          tc::mma_commit(pd_empty);
+          tc::mma_commit(mn_empty);
+        }
+        n = n0 + steps;
+        if (ok) tc::mma_commit(acc_full);
+      }
+      tc::mma_commit(drain);
+      if (!tc::mbar_wait(drain, 0)) record_error();
+    }
+    __syncwarp();
+  } else {
+    // Thread (r, grp) owns query columns [32*grp, 32*grp + 32) of every 128 x 64 tile (rows are
+    // keys). The 64 queries' statistics are staged in shared memory once per step: softmax thread
+    // u < 192 fetches value u % 64 of array u / 64 (row max, 1 / sum, D) one step ahead.
+    const SoftThread th(warp, lane, tmem);
+    const uint32_t r = th.r, grp = th.grp;
+    const uint32_t u = (warp - 2) * 32 + lane;
+    const float* src = u < 64 ? p.row_max : (u < 128 ? p.row_inv : p.delta);
+    float* stats = reinterpret_cast<float*>(smem + L::kStats);  // [2][3][64]
+    uint8_t* ptbuf = smem + L::kPT;
+    uint8_t* dstbuf = smem + L::kDST;
+    uint32_t n = 0, item = 0, xphase = 0;
+    bool ok = true;
+    // Queries past the sequence get zero statistics: their probabilities come out 0.
+    auto fetch = [&](uint64_t sbase, uint32_t q0) -> float {
+      const uint32_t q = q0 + (u & 63);
+      return (u < 192 && q < seq) ? __ldg(src + sbase + q) : 0.f;
+    };
+    for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
+      const Item it = decode(p, idx, false);
+      const uint32_t i0 = 2 * it.t;
+      const uint32_t steps = nq_all - i0;
+      const uint32_t kv = it.t * 128 + r;
+      const uint64_t sbase = static_cast<uint64_t>(it.b * p.heads + it.h) * seq;
+      float next = fetch(sbase, i0 * 64);
+      if (lane == 0) tc::bulk_wait_read<0>();
+      __syncwarp();
+      for (uint32_t i = 0; i < steps && ok; ++i, ++n) {
+        float* st = stats + (n & 1) * 192;
+        if (u < 192) st[u] = next;
+        if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
+        if (i + 1 < steps) next = fetch(sbase, (i0 + i + 1) * 64);
+        if (!(ok = wait_or_abort(s_full + (n & 1), (n >> 1) & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        uint32_t sv[32], pv[32];
+        tc::tmem_load_2x32(th.lanes + (n & 1) * 64 + grp * 32,
+                           th.lanes + 128 + (n & 1) * 64 + grp * 32, sv, pv);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(s_empty + (n & 1));
+        const uint32_t q0 = (i0 + i) * 64 + grp * 32;
+        const float4* mx4 = reinterpret_cast<const float4*>(st + grp * 32);
+        const float4* inv4 = reinterpret_cast<const float4*>(st + 64 + grp * 32);
+        const float4* dd4 = reinterpret_cast<const float4*>(st + 128 + grp * 32);
+        float pt[32], dst[32];
+        const bool full = q0 >= it.t * 128 + 127;  // every query of the chunk follows every key
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          const float4 m4 = mx4[g], i4 = inv4[g], d4 = dd4[g];
+          const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+          const float iv[4] = {i4.x, i4.y, i4.z, i4.w};
+          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const int e = 4 * g + e4;
+            float pr = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -mv[e4])) * iv[e4];
+            if (!full && q0 + e < kv) pr = 0.f;
+            pt[e] = round_tf32(pr);
+            dst[e] = round_tf32(pr * (__uint_as_float(pv[e]) - dv[e4]) * p.scale);
+          }
+        }
+        if (n > 0 && !(ok = wait_or_abort(pd_empty, (n - 1) & 1, abort_flag))) break;
+        store_row32(ptbuf + grp * 16384, r, pt);
+        store_row32(dstbuf + grp * 16384, r, dst);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(pd_full);
+      }
+      if (!ok) break;
+      if (!(ok = wait_or_abort(acc_full, item & 1, abort_flag))) break;
+      tc::tc_fence_after();
+      if (grp < DH / 32) {
+        const int row = static_cast<int>(it.t * 128 + th.quarter * 32);
+        uint32_t v[32], w[32];
+        tc::tmem_load_2x32(th.lanes + 256 + grp * 32, th.lanes + 256 + DH + grp * 32, v, w);
+        float o[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);  // dV
+        store_box(&p.out, ptbuf + grp * 16384 + th.quarter * 4096, o,
+                  static_cast<int>(2 * p.model_dim + it.h * DH + 32 * grp), row,
+                  static_cast<int>(it.b));
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(w[e]);  // dK
+        store_box(&p.out, dstbuf + grp * 16384 + th.quarter * 4096, o,
+                  static_cast<int>(p.model_dim + it.h * DH + 32 * grp), row,
+                  static_cast<int>(it.b));
+        if (lane == 0) tc::bulk_commit();
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(acc_empty);
+    }
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ============================================================================ host side
+template <typename K>
+cudaError_t launch(K kernel, uint32_t smem, const AttnParams& p, int device, cudaStream_t stream,
+                   bool* configured) {
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  if (!configured[device]) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[device] = true;
+  }
+  const unsigned grid = std::min<uint32_t>(p.total, static_cast<uint32_t>(sm_count(device)));
+  if (grid == 0) return cudaSuccess;
+  kernel<<<grid, kThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+void base_params(AttnParams& p, uint64_t batch, uint64_t seq, uint64_t heads, uint64_t head_dim) {
+  memset(&p, 0, sizeof(p));
+  p.heads = static_cast<uint32_t>(heads);
+  p.seq = static_cast<uint32_t>(seq);
+  p.model_dim = static_cast<uint32_t>(heads * head_dim);
+  p.bh = static_cast<uint32_t>(batch * heads);
+  p.ld_o = heads * head_dim;
+  p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)));
+  p.scale_log2 = p.scale * kLog2e;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+bool attention_supported(uint64_t head_dim) { return head_dim == 32 || head_dim == 64; }
+
+cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_max, float* row_inv,
+                                     uint64_t batch, uint64_t seq, uint64_t heads,
+                                     uint64_t head_dim, int device, cudaStream_t stream) {
+  AttnParams p;
+  base_params(p, batch, seq, heads, head_dim);
+  const uint64_t d = heads * head_dim;
+  if (!make_map(&p.qk128, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 128, false) ||
+      !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true) ||
+      !make_map(&p.out, ctx, d, seq, batch, 1, d, seq * d, 0, 32, false))
+    return cudaErrorInvalidValue;
+  p.row_max = row_max;
+  p.row_inv = row_inv;
+  p.tiles = static_cast<uint32_t>((seq + 127) / 128);
+  p.total = p.tiles * p.bh;
+  static bool cfg32[64] = {}, cfg64[64] = {};
+  return head_dim == 64 ? launch(attn_fwd_kernel<64>, Fwd<64>::kSmem, p, device, stream, cfg64)
+                        : launch(attn_fwd_kernel<32>, Fwd<32>::kSmem, p, device, stream, cfg32);
+}
+
+cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const float* dctx,
+                                      const float* row_max, const float* row_inv, float* delta,
+                                      float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
+                                      uint64_t head_dim, int device, cudaStream_t stream) {
+  AttnParams p;
+  base_params(p, batch, seq, heads, head_dim);
+  const uint64_t d = heads * head_dim;
+  if (!make_map(&p.qk128, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 128, false) ||
+      !make_map(&p.qk64, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 64, false) ||
+      !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true) ||
+      !make_map(&p.do128, dctx, d, seq, batch, 1, d, seq * d, 0, 128, false) ||
+      !make_map(&p.do64, dctx, d, seq, batch, 1, d, seq * d, 0, 64, false) ||
+      !make_map(&p.do_mn, dctx, d, seq, batch, 1, d, seq * d, 0, 32, true) ||
+      !make_map(&p.out, dqkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, false))
+    return cudaErrorInvalidValue;
+  p.o = ctx;
+  p.d_o = dctx;
+  p.row_max = const_cast<float*>(row_max);
+  p.row_inv = const_cast<float*>(row_inv);
+  p.delta = delta;
+  static bool q32[64] = {}, q64[64] = {}, k32[64] = {}, k64[64] = {};
+  // Query kernel first: it produces D, which the key kernel reads.
+  p.tiles = static_cast<uint32_t>((seq + 127) / 128);
+  p.total = p.tiles * p.bh;
+  cudaError_t e = head_dim == 64
+                      ? launch(attn_bwd_q_kernel<64>, BwdQ<64>::kSmem, p, device, stream, q64)
+                      : launch(attn_bwd_q_kernel<32>, BwdQ<32>::kSmem, p, device, stream, q32);
+  if (e != cudaSuccess) return e;
+  return head_dim == 64 ? launch(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, p, device, stream, k64)
+                        : launch(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, p, device, stream, k32);
+}
+
+namespace {
+SparCudaStatus attention_validate(const float* const* ptrs, int count, uint64_t batch,
+                                  uint64_t seq, uint64_t heads, uint64_t head_dim) {
+  for (int i = 0; i < count; ++i)
+    if (!ptrs[i] || !aligned16(ptrs[i])) return invalid();
+  if (batch == 0 || seq == 0 || heads == 0 || !attention_supported(head_dim)) return invalid();
+  if (batch * heads > (1ull << 31) || seq > (1ull << 31) || batch * seq * 3 * heads * head_dim >= (1ull << 40))
+    return invalid();
+  return ok();
+}
+}  // namespace
+
+}  // namespace spar_b200
+
+using namespace spar_b200;
+
+extern "C" SparCudaStatus spar_b200_attention_forward(const float* qkv, float* ctx, float* row_max,
+                                                      float* row_inv, uint64_t batch, uint64_t seq,
+                                                      uint64_t heads, uint64_t head_dim, int device,
+                                                      void* stream) {
+  const float* ptrs[4] = {qkv, ctx, row_max, row_inv};
+  const SparCudaStatus v = attention_validate(ptrs, 4, batch, seq, heads, head_dim);
+  if (v.code) return v;
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const cudaError_t e = attention_forward_launch(qkv, ctx, row_max, row_inv, batch, seq, heads,
+                                                 head_dim, device, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" SparCudaStatus spar_b200_attention_backward(const float* qkv, const float* ctx,
+                                                       const float* dctx, const float* row_max,
+                                                       const float* row_inv, float* delta,
+                                                       float* dqkv, uint64_t batch, uint64_t seq,
+                                                       uint64_t heads, uint64_t head_dim,
+                                                       int device, void* stream) {
+  const float* ptrs[7] = {qkv, ctx, dctx, row_max, row_inv, delta, dqkv};
+  const SparCudaStatus v = attention_validate(ptrs, 7, batch, seq, heads, head_dim);
+  if (v.code) return v;
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const cudaError_t e = attention_backward_launch(qkv, ctx, dctx, row_max, row_inv, delta, dqkv,
+                                                  batch, seq, heads, head_dim, device,
+                                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" int spar_b200_attention_error(int device, int clear) {
+  DeviceScope scope(device);
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_attn_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_attn_error, &zero, sizeof(int));
+  }
+  return v;
+}

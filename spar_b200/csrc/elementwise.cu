@@ -57,7 +57,7 @@ __global__ void rope_table_kernel(float2* table, uint64_t t, uint64_t half, uint
 // x: rows of `heads * d` features per token (row stride ld); rotates each head's pairs.
 __global__ void rope_apply_kernel(float* __restrict__ x, const float2* __restrict__ table,
                                   uint64_t tokens, uint64_t t, uint64_t heads, uint64_t half,
-                                  uint64_t ld, int inverse) {
+                                  uint64_t ld, int inverse, int round) {
   const uint64_t pairs_per_token = heads * half;
   const uint64_t total = tokens * pairs_per_token;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
@@ -70,7 +70,9 @@ __global__ void rope_apply_kernel(float* __restrict__ x, const float2* __restric
     const float sine = inverse ? -cs.y : cs.y;
     float2* p = reinterpret_cast<float2*>(x + token * ld) + within;
     const float2 v = *p;
-    *p = make_float2(v.x * cs.x - v.y * sine, v.x * sine + v.y * cs.x);
+    float2 o = make_float2(v.x * cs.x - v.y * sine, v.x * sine + v.y * cs.x);
+    if (round) o = make_float2(round_tf32(o.x), round_tf32(o.y));
+    *p = o;
   }
 }
 
@@ -161,11 +163,11 @@ cudaError_t rope_table_launch(float* table, uint64_t t, uint64_t d, double theta
 
 cudaError_t rope_apply_launch(float* x, const float* table, uint64_t tokens, uint64_t t,
                               uint64_t heads, uint64_t d, uint64_t ld, int inverse, int device,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, int round) {
   const uint64_t half = d / 2;
   const unsigned grid = grid_for(tokens * heads * half, 256, sm_count(device) * 16);
   rope_apply_kernel<<<grid, 256, 0, stream>>>(x, reinterpret_cast<const float2*>(table), tokens,
-                                              t, heads, half, ld, inverse);
+                                              t, heads, half, ld, inverse, round);
   return cudaGetLastError();
 }
 

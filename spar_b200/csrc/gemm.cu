@@ -64,6 +64,7 @@ struct GemmParams {
   int accumulate, epilogue, causal;
   uint32_t kchunk;  // k-blocks per accumulation chunk (chunked kernels only)
   uint32_t kparts;  // split-K factor (1: no split); partial sums go to part_map
+  int round_out;    // round the stored C to nearest TF32
 };
 
 struct TileCoord {
@@ -200,6 +201,10 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
           make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] = gelu_value(v[e]);
+  }
+  if (p.round_out) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = round_tf32(v[e]);
   }
 #pragma unroll
   for (int c = 0; c < 8; ++c)
@@ -489,14 +494,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
 }
 
 // ----------------------------------------------------------------- 3xTF32 operand split
-// Round-to-nearest to a TF32-representable fp32 (10 explicit mantissa bits): add half an ulp
-// of the 13 dropped bits, then clear them. Both halves are rounded, so the tensor cores see
-// exact TF32 values and the split error is unbiased: hi = rn(x), lo = rn(x - hi).
-__device__ __forceinline__ float round_tf32(float v) {
-  const uint32_t b = __float_as_uint(v);
-  if ((b & 0x7f800000u) == 0x7f800000u) return v;  // inf / nan unchanged
-  return __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
-}
+// Both halves are rounded to nearest TF32 (round_tf32), so the tensor cores see exact TF32
+// values and the split error is unbiased: hi = rn(x), lo = rn(x - hi).
 
 __global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo,
                                   const float* __restrict__ src, uint64_t inner, uint64_t rows,
@@ -553,6 +552,8 @@ __global__ void splitk_reduce_kernel(float* __restrict__ c, uint64_t ldc,
   }
 }
 
+}  // namespace
+
 // ----------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -590,6 +591,8 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows
   return r == CUDA_SUCCESS;
 }
 
+namespace {
+
 template <int BN, int STAGES, bool CHUNKED>
 cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) {
   constexpr size_t smem = STAGES * (BM * BK * 4 + BN * BK * 4) + kEpiBytes + 1024 + 256;
@@ -623,7 +626,7 @@ uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
 // runs ceil(tiles * parts / sms) rounds of 1/parts-sized work units; the split count with the
 // fewest full-tile-equivalent rounds wins when it saves at least 15% over no split.
 uint32_t splitk_parts(const SparB200Gemm& g, int bn, int sms) {
-  if (g.precision != SPAR_B200_TF32 || g.epilogue != SPAR_B200_EPI_NONE ||
+  if (g.precision != SPAR_B200_TF32 || g.epilogue != SPAR_B200_EPI_NONE || g.round_output ||
       g.causal != SPAR_B200_CAUSAL_NONE || (g.batch[0] > 1) || (g.batch[1] > 1) || g.n % 4)
     return 1;
   const uint64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + bn - 1) / bn);
@@ -721,6 +724,7 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   p.causal = g.causal;
   p.kchunk = 4;  // 4 k-blocks = 128 K elements x 3 sections per hardware-accumulated chunk
   p.kparts = 1;
+  p.round_out = g.round_output != 0;
   const uint32_t kparts = split ? 1 : splitk_parts(g, bn, sm_count(device));
   const uint64_t ldp = (g.n + 3) / 4 * 4;
   if (kparts > 1 && splitk_workspace && splitk_floats >= kparts * g.m * ldp) {

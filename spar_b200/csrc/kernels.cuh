@@ -2,10 +2,32 @@
 // element functions that several kernels (and GEMM epilogues) evaluate.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace spar_b200 {
+
+// 4-D fp32 TMA tensor map: element (x, r) of batch (q1, q0) at base + q0*bs0 + q1*bs1 + r*ld + x
+// (x contiguous, extents inner x rows x b1 x b0), boxes of 32 x box_rows elements; 128-byte
+// swizzle of 16-byte chunks (K-major operands, staging boxes) or of 32-byte chunks (mn_major:
+// MN-major tf32 operands). Bytes outside the extents read as zero and are not written.
+bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows, uint64_t b1,
+              uint64_t b0, uint64_t ld, uint64_t bs1, uint64_t bs0, uint32_t box_rows,
+              bool mn_major);
+
+// Fused causal attention over the packed qkv buffer [batch, seq, 3 * heads * head_dim]
+// (head_dim 32 or 64): ctx [batch, seq, heads * head_dim]; per (batch, head, row) statistics
+// row_max (max of scores * scale * log2 e) and row_inv (1 / sum of exponentials).
+bool attention_supported(uint64_t head_dim);
+cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_max, float* row_inv,
+                                     uint64_t batch, uint64_t seq, uint64_t heads,
+                                     uint64_t head_dim, int device, cudaStream_t stream);
+// dqkv (every column of the rows < seq written) from dctx; delta [batch * heads * seq] scratch.
+cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const float* dctx,
+                                      const float* row_max, const float* row_inv, float* delta,
+                                      float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
+                                      uint64_t head_dim, int device, cudaStream_t stream);
 
 // Spar's stable sigmoid (src/ops/unary.cpp:55-61 / cuda_kernels.cu:105-111), in fp32.
 __device__ __forceinline__ float stable_sigmoid(float v) {
@@ -19,6 +41,16 @@ __device__ __forceinline__ float stable_sigmoid(float v) {
 // (src/ops/scalar.cpp:40).
 constexpr float kGeluA = 1.5957691216057308f;  // 2*sqrt(2/pi)
 constexpr float kGeluB = 0.044715f;
+
+// Round-to-nearest to a TF32-representable fp32 (10 explicit mantissa bits): add half an ulp
+// of the 13 dropped bits, then clear them. The tensor cores read an fp32 operand as TF32 by
+// dropping those bits (truncation, biased toward zero); values stored pre-rounded by this enter
+// the products unbiased.
+__device__ __forceinline__ float round_tf32(float v) {
+  const uint32_t b = __float_as_uint(v);
+  if ((b & 0x7f800000u) == 0x7f800000u) return v;  // inf / nan unchanged
+  return __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
+}
 
 __device__ __forceinline__ float gelu_value(float x) {
   const float x3 = (x * x) * x;
@@ -49,9 +81,10 @@ cudaError_t gelu_launch(float* y, const float* dy, const float* x, uint64_t n, i
                         int device, cudaStream_t stream);
 cudaError_t rope_table_launch(float* table, uint64_t t, uint64_t d, double theta, uint64_t start,
                               cudaStream_t stream);
+// round != 0: results stored rounded to nearest TF32 (rotated q / k that only feed TF32 products).
 cudaError_t rope_apply_launch(float* x, const float* table, uint64_t tokens, uint64_t t,
                               uint64_t heads, uint64_t d, uint64_t ld, int inverse, int device,
-                              cudaStream_t stream);
+                              cudaStream_t stream, int round = 0);
 int column_sum_parts(uint64_t rows, uint64_t cols, int device);
 cudaError_t column_sum_launch(float* out, const float* x, uint64_t rows, uint64_t cols,
                               uint64_t ld, int accumulate, float* workspace, int device,

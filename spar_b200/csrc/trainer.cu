@@ -81,7 +81,9 @@ struct LayerOffsets {
 };
 
 struct LayerActs {
-  float *x, *mean1, *rstd1, *a1, *qkv, *p, *ctx, *h1, *mean2, *rstd2, *a2, *u, *g;
+  float *x, *mean1, *rstd1, *a1, *qkv, *ctx, *h1, *mean2, *rstd2, *a2, *u, *g;
+  float* p;      // attention probabilities [B, H, T, T] (unfused path only)
+  float* stats;  // fused attention softmax statistics: row max [B*H*T], 1 / row sum [B*H*T]
 };
 
 }  // namespace
@@ -107,6 +109,9 @@ class LMTrainer {
   std::vector<LayerActs> acts;
   float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
   float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
+  // Fused attention (TF32 mode, head_dim 32 / 64): no [T, T] buffers; dS holds the backward's
+  // D = rowsum(dO o O) [B*H*T] instead of dS.
+  bool fused_attention = false;
   float *ln_ws = nullptr, *col_ws = nullptr, *split_ws = nullptr, *rope_tab = nullptr;
   float* splitk_ws = nullptr;  // split-K partial tiles of the small weight-gradient GEMMs
   uint64_t splitk_floats = 0;
@@ -140,8 +145,9 @@ class LMTrainer {
                    bool accumulate, int epi, const float* bias, float* aux, uint64_t ldaux,
                    cudaStream_t s, int causal = SPAR_B200_CAUSAL_NONE, uint64_t b0 = 1,
                    uint64_t b1 = 1, const uint64_t* a_bs = nullptr, const uint64_t* b_bs = nullptr,
-                   const uint64_t* c_bs = nullptr);
+                   const uint64_t* c_bs = nullptr, bool round_out = false);
   cudaError_t attention_forward(LayerActs& A, cudaStream_t s);
+  cudaError_t attention_backward(LayerActs& A, cudaStream_t s);
   cudaError_t layer_backward(uint64_t l, cudaStream_t s);
 };
 
@@ -234,7 +240,9 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   if (e != cudaSuccess) return runtime(e);
 
   // ---- activation arena
-  const uint64_t PS = B * H * T * T;  // one layer's attention probabilities
+  fused_attention = c.precision == SPAR_B200_TF32 && attention_supported(dh);
+  // One layer's attention probabilities (unfused) or softmax statistics (fused).
+  const uint64_t PS = fused_attention ? 2 * B * H * T : B * H * T * T;
   const int ln_parts = layernorm_backward_parts(N, device);
   // Column-sum partials: the partition count depends on the width, so take the largest
   // parts x cols over the widths reduced in the backward pass (d, 3d, F).
@@ -251,7 +259,7 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     f(&A.rstd1, N);
     f(&A.a1, N * d);
     f(&A.qkv, N * 3 * d);
-    f(&A.p, PS);
+    f(fused_attention ? &A.stats : &A.p, PS);
     f(&A.ctx, N * d);
     f(&A.h1, N * d);
     f(&A.mean2, N);
@@ -268,7 +276,7 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   f(&dres, N * d);
   f(&dtmp, N * d);
   f(&dqkv, N * 3 * d);
-  f(&dS, PS);
+  f(&dS, fused_attention ? B * H * T : PS);
   f(&du, N * F);
   f(&ln_ws, 2ull * ln_parts * d);
   f(&col_ws, col_floats);
@@ -337,7 +345,8 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
                             bool at, const float* b, uint64_t ldb, bool bt, float* c, uint64_t ldc,
                             bool accumulate, int epi, const float* bias, float* aux,
                             uint64_t ldaux, cudaStream_t s, int causal, uint64_t b0, uint64_t b1,
-                            const uint64_t* a_bs, const uint64_t* b_bs, const uint64_t* c_bs) {
+                            const uint64_t* a_bs, const uint64_t* b_bs, const uint64_t* c_bs,
+                            bool round_out) {
   SparB200Gemm g{};
   g.m = m;
   g.n = n;
@@ -363,6 +372,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
   g.ldaux = ldaux;
   g.precision = cfg.precision;
   g.causal = causal;
+  g.round_output = round_out;
   launches += cfg.precision == SPAR_B200_TF32X3 ? 3 : 1;
   // Never let a split copy run past the workspace sized in init().
   if (cfg.precision == SPAR_B200_TF32X3 && gemm_split_workspace_floats(g) > split_floats)
@@ -392,6 +402,9 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
 
 // S = QK^T (lower tiles), P = causal softmax in place, ctx = P V (k <= row).
 cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
+  if (fused_attention)
+    return attention_forward_launch(A.qkv, A.ctx, A.stats, A.stats + B * H * T, B, T, H, dh,
+                                    device, s);
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
   const uint64_t ld = 3 * d;
   const uint64_t qkv_bs[2] = {T * ld, dh};
@@ -428,10 +441,14 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
     launches += 2 + (cfg.use_rope ? 1 : 0) + 1;  // 2 LayerNorms, rope, softmax
     SPAR_CHECK(layernorm_forward_launch(A.a1, A.mean1, A.rstd1, A.x, P + lo.ln1_g, P + lo.ln1_b,
                                         N, d, eps, device, s));
+    // q, k, v only feed attention products: with fused attention they are stored rounded to
+    // nearest TF32 (GEMM epilogue, then RoPE re-rounds the rotated q and k).
     SPAR_CHECK(gemm(N, 3 * d, d, A.a1, d, false, P + lo.wqkv, 3 * d, false, A.qkv, 3 * d, false,
-                    SPAR_B200_EPI_BIAS, P + lo.bqkv, nullptr, 0, s));
+                    SPAR_B200_EPI_BIAS, P + lo.bqkv, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1,
+                    nullptr, nullptr, nullptr, fused_attention));
     if (cfg.use_rope)  // q and k heads are adjacent: rotate 2H heads of dh at row stride 3d
-      SPAR_CHECK(rope_apply_launch(A.qkv, rope_tab, N, T, 2 * H, dh, 3 * d, 0, device, s));
+      SPAR_CHECK(rope_apply_launch(A.qkv, rope_tab, N, T, 2 * H, dh, 3 * d, 0, device, s,
+                                   fused_attention));
     SPAR_CHECK(attention_forward(A, s));
     SPAR_CHECK(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
                     SPAR_B200_EPI_BIAS_ADD, P + lo.bo, A.x, d, s));
@@ -477,6 +494,38 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
 #undef SPAR_CHECK
 }
 
+// dqkv from dctx (in dtmp): fused kernels, or the six batched GEMMs around the materialised
+// probabilities and the softmax backward.
+cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
+  if (fused_attention) {
+    launches += 1;  // query and key kernels (one counted with the softmax in layer_backward)
+    return attention_backward_launch(A.qkv, A.ctx, dtmp, A.stats, A.stats + B * H * T, dS, dqkv,
+                                     B, T, H, dh, device, s);
+  }
+  const uint64_t ld = 3 * d;
+  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
+  const uint64_t qkv_bs[2] = {T * ld, dh};
+  const uint64_t p_bs[2] = {H * T * T, T * T};
+  const uint64_t ctx_bs[2] = {T * d, dh};
+  const float* q = A.qkv;
+  const float* k = A.qkv + d;
+  const float* v = A.qkv + 2 * d;
+  // dV = P^T dctx (k >= row)
+  SPAR_TRY(gemm(T, dh, T, A.p, T, true, dtmp, d, false, dqkv + 2 * d, ld, false,
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs,
+                ctx_bs, qkv_bs));
+  // dP = dctx V^T (lower tiles), dS = softmax backward (scaled) in place
+  SPAR_TRY(gemm(T, T, dh, dtmp, d, false, v, ld, true, dS, T, false, SPAR_B200_EPI_NONE, nullptr,
+                nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, ctx_bs, qkv_bs, p_bs));
+  SPAR_TRY(causal_softmax_launch(dS, dS, A.p, B * H, T, T, scale, 128, 1, s));
+  // dQ = dS K (k <= row), dK = dS^T Q (k >= row)
+  SPAR_TRY(gemm(T, dh, T, dS, T, false, k, ld, false, dqkv, ld, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, qkv_bs, qkv_bs));
+  SPAR_TRY(gemm(T, dh, T, dS, T, true, q, ld, false, dqkv + d, ld, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs, qkv_bs, qkv_bs));
+  return cudaSuccess;
+}
+
 cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   LayerActs& A = acts[l];
   const LayerOffsets& lo = lay[l];
@@ -503,29 +552,11 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
                 nullptr, nullptr, 0, s));
   SPAR_TRY(column_sum_launch(G + lo.bo, dres, N, d, d, 1, col_ws, device, s));
   SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s));
-  // attention core: dtmp = dctx [N, d]
-  const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
+                fused_attention));
+  // attention core: dtmp = dctx [N, d] -> dqkv
+  SPAR_TRY(attention_backward(A, s));
   const uint64_t ld = 3 * d;
-  const uint64_t qkv_bs[2] = {T * ld, dh};
-  const uint64_t p_bs[2] = {H * T * T, T * T};
-  const uint64_t ctx_bs[2] = {T * d, dh};
-  const float* q = A.qkv;
-  const float* k = A.qkv + d;
-  const float* v = A.qkv + 2 * d;
-  // dV = P^T dctx (k >= row)
-  SPAR_TRY(gemm(T, dh, T, A.p, T, true, dtmp, d, false, dqkv + 2 * d, ld, false,
-                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs,
-                ctx_bs, qkv_bs));
-  // dP = dctx V^T (lower tiles), dS = softmax backward (scaled) in place
-  SPAR_TRY(gemm(T, T, dh, dtmp, d, false, v, ld, true, dS, T, false, SPAR_B200_EPI_NONE, nullptr,
-                nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, ctx_bs, qkv_bs, p_bs));
-  SPAR_TRY(causal_softmax_launch(dS, dS, A.p, B * H, T, T, scale, 128, 1, s));
-  // dQ = dS K (k <= row), dK = dS^T Q (k >= row)
-  SPAR_TRY(gemm(T, dh, T, dS, T, false, k, ld, false, dqkv, ld, false, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, qkv_bs, qkv_bs));
-  SPAR_TRY(gemm(T, dh, T, dS, T, true, q, ld, false, dqkv + d, ld, false, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs, qkv_bs, qkv_bs));
   if (cfg.use_rope) SPAR_TRY(rope_apply_launch(dqkv, rope_tab, N, T, 2 * H, dh, ld, 1, device, s));
   // QKV projection
   SPAR_TRY(gemm(d, 3 * d, N, A.a1, d, true, dqkv, ld, false, G + lo.wqkv, ld, true,

@@ -60,6 +60,23 @@ def run_gemm(m, n, k, at=False, bt=False, x3=False, iters=10):
                   ms, 2.0 * m * n * k, "TFLOP/s", tf)
 
 
+def run_attention(b=16, t=1024, h=16, dh=64, iters=10):
+    """Fused causal attention at the C5 shape; rate = causal useful FLOPs (QK^T and PV forward,
+    five products backward) over time."""
+    dev = torch.device("cuda")
+    d = h * dh
+    qkv = torch.randn(b, t, 3 * d, device=dev)
+    do = torch.randn(b, t, d, device=dev)
+    ctx, mx, inv = ops.attention_forward(qkv, h)
+    _, tf = peaks()
+    half = b * h * t * (t + 1) / 2 * dh * 2.0  # one causal [t, t] x dh product
+    report(f"attention_fwd {b}x{h}x{t}x{dh}", timed(lambda: ops.attention_forward(qkv, h), iters),
+           2 * half, "TFLOP/s", tf)
+    return report(f"attention_bwd {b}x{h}x{t}x{dh}",
+                  timed(lambda: ops.attention_backward(do, qkv, ctx, mx, inv, h), iters),
+                  5 * half, "TFLOP/s", tf)
+
+
 def run_bandwidth(name, iters=10):
     dev = torch.device("cuda")
     hbm, _ = peaks()
@@ -123,8 +140,11 @@ def main():
                                   (16384, 1024, 4096, 0, 0), (1024, 4096, 16384, 1, 0),
                                   (16384, 32768, 1024, 0, 1)]:
             run_gemm(m, n, k, bool(at), bool(bt), False, a.iters)
+        run_attention(iters=a.iters)
         for name in ("layernorm_bwd", "gelu_bwd", "softmax_bwd", "cross_entropy", "adamw"):
             run_bandwidth(name, a.iters)
+    elif a.kernel == "attention":
+        run_attention(iters=a.iters)
     else:
         run_bandwidth(a.kernel, a.iters)
 

@@ -102,6 +102,39 @@ def causal_softmax_backward(dp, p, scale: float, zero_fill_block: int = 0, out=N
     return ds
 
 
+# ------------------------------------------------------------------------------- attention
+def attention_forward(qkv, heads: int):
+    """Fused causal attention over the packed projection buffer qkv [batch, seq, 3*d].
+
+    Returns (ctx [batch, seq, d], row_max [batch, heads, seq], row_inv [batch, heads, seq])."""
+    _f32(qkv, "qkv")
+    batch, seq, d3 = qkv.shape
+    d = d3 // 3
+    ctx = torch.empty(batch, seq, d, device=qkv.device, dtype=torch.float32)
+    row_max = torch.empty(batch, heads, seq, device=qkv.device, dtype=torch.float32)
+    row_inv = torch.empty_like(row_max)
+    call("spar_b200_attention_forward", qkv.data_ptr(), ctx.data_ptr(), row_max.data_ptr(),
+         row_inv.data_ptr(), batch, seq, heads, d // heads, _dev(qkv), _stream(qkv))
+    return ctx, row_max, row_inv
+
+
+def attention_backward(dctx, qkv, ctx, row_max, row_inv, heads: int):
+    """dqkv [batch, seq, 3*d] of the fused causal attention."""
+    batch, seq, d3 = qkv.shape
+    d = d3 // 3
+    dqkv = torch.empty_like(qkv)
+    delta = torch.empty(batch, heads, seq, device=qkv.device, dtype=torch.float32)
+    call("spar_b200_attention_backward", _f32(qkv, "qkv").data_ptr(), _f32(ctx, "ctx").data_ptr(),
+         _f32(dctx, "dctx").data_ptr(), _f32(row_max, "row_max").data_ptr(),
+         _f32(row_inv, "row_inv").data_ptr(), delta.data_ptr(), dqkv.data_ptr(), batch, seq, heads,
+         d // heads, _dev(qkv), _stream(qkv))
+    return dqkv
+
+
+def attention_error(device: int = 0, clear: bool = True) -> int:
+    return _lib.load().spar_b200_attention_error(device, int(clear))
+
+
 # ------------------------------------------------------------------------------- cross-entropy
 def cross_entropy_forward_backward(logits, targets, sequence_length: int = 0,
                                    grad_scale: float | None = None, in_place: bool = False):

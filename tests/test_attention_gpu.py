@@ -1,0 +1,98 @@
+"""Fused causal attention (forward, and the query / key backward kernels) through the C ABI
+against the float64 oracle restatement of the reference's attention chain.
+
+Tolerance: relative L2 error <= 2e-3 for ctx and every third of dqkv (TF32 products: 10 explicit
+mantissa bits in Q K^T, P V, dS K, ...), the bar stated for TF32 mode. The tensor cores read fp32
+operands by dropping their low 13 mantissa bits, so inputs are handed over rounded to nearest
+TF32 (as the training runtime stores them); the oracle sees the unrounded values.
+"""
+import numpy as np
+import pytest
+
+from _util import rel_l2
+from oracle import spar_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def rn_tf32(x):
+    """Round fp32 to the nearest TF32-representable value (10 explicit mantissa bits)."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return (((b + 0x1000) & 0xFFFFE000).astype(np.uint32)).view(np.float32)
+
+
+def _run(cuda, b, t, h, dh, seed):
+    import torch
+    from spar_b200 import ops
+
+    r = np.random.default_rng(seed)
+    d = h * dh
+    qkv = r.standard_normal((b, t, 3 * d)).astype(np.float32)
+    dctx = r.standard_normal((b, t, d)).astype(np.float32)
+    q = torch.from_numpy(rn_tf32(qkv)).to(cuda)
+    ctx, row_max, row_inv = ops.attention_forward(q, h)
+    dqkv = ops.attention_backward(torch.from_numpy(rn_tf32(dctx)).to(cuda), q, ctx, row_max,
+                                  row_inv, h)
+    torch.cuda.synchronize()
+    assert ops.attention_error(0) == 0
+    ref_ctx, ref_dqkv = O.attention_forward_backward(qkv, h, dctx)
+    return ctx.cpu().numpy(), dqkv.cpu().numpy(), ref_ctx, ref_dqkv, d
+
+
+@pytest.mark.parametrize("b,t,h,dh", [
+    (2, 256, 4, 64),    # whole 128-row tiles
+    (1, 1024, 2, 64),   # the C4/C5 sequence length
+    (2, 64, 4, 32),     # C1 shape: one partial tile, head_dim 32
+    (1, 200, 3, 64),    # ragged sequence (partial query and key tiles)
+    (3, 130, 2, 32),    # one row past a tile boundary
+])
+def test_attention_matches_oracle(cuda, b, t, h, dh):
+    ctx, dqkv, ref_ctx, ref_dqkv, d = _run(cuda, b, t, h, dh, seed=b * 1000 + t + h + dh)
+    assert rel_l2(ctx, ref_ctx) <= 2e-3
+    for part, name in enumerate(("dq", "dk", "dv")):
+        got = dqkv[..., part * d:(part + 1) * d]
+        ref = ref_dqkv[..., part * d:(part + 1) * d]
+        assert rel_l2(got, ref) <= 2e-3, name
+
+
+def test_attention_is_deterministic(cuda):
+    import torch
+    from spar_b200 import ops
+
+    r = np.random.default_rng(5)
+    q = torch.from_numpy(r.standard_normal((2, 512, 3 * 256)).astype(np.float32)).to(cuda)
+    do = torch.from_numpy(r.standard_normal((2, 512, 256)).astype(np.float32)).to(cuda)
+    outs = []
+    for _ in range(2):
+        ctx, mx, inv = ops.attention_forward(q, 4)
+        outs.append((ctx.cpu().numpy(), ops.attention_backward(do, q, ctx, mx, inv, 4).cpu().numpy()))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
+
+
+def test_attention_statistics(cuda):
+    """row_max * ln 2 is the row maximum of the scaled scores; 1 / row_inv the sum of
+    exp(scaled score - max) over the causal keys."""
+    import torch
+    from spar_b200 import ops
+
+    b, t, h, dh = 1, 96, 2, 32
+    r = np.random.default_rng(9)
+    qkv = r.standard_normal((b, t, 3 * h * dh)).astype(np.float32)
+    ctx, row_max, row_inv = ops.attention_forward(torch.from_numpy(qkv).to(cuda), h)
+    d = h * dh
+    q = qkv[..., :d].reshape(b, t, h, dh).transpose(0, 2, 1, 3).astype(np.float64)
+    k = qkv[..., d:2 * d].reshape(b, t, h, dh).transpose(0, 2, 1, 3).astype(np.float64)
+    s = np.where(np.triu(np.ones((t, t), bool), 1), -np.inf, q @ k.transpose(0, 1, 3, 2) / np.sqrt(dh))
+    m = s.max(-1)
+    assert rel_l2(row_max.cpu().numpy() * np.log(2.0), m) <= 2e-3
+    assert rel_l2(1.0 / row_inv.cpu().numpy(), np.exp(s - m[..., None]).sum(-1)) <= 2e-3
+
+
+def test_attention_invalid_arguments(cuda):
+    import torch
+    from spar_b200 import _lib, ops
+
+    q = torch.zeros(1, 64, 3 * 4 * 48, device=cuda)
+    with pytest.raises(_lib.SparError):
+        ops.attention_forward(q, 4)  # head_dim 48 is not supported

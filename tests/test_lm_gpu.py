@@ -29,6 +29,9 @@ def _run(cfg, micro_steps, lr=3e-4):
     lm = DecoderLM(cfg, 0)
     lm.load_state_dict(params)
     loss, norm, flags = lm.train_step(ids, lr, step=1)
+    from spar_b200 import ops
+
+    assert ops.gemm_error(0) == 0 and ops.attention_error(0) == 0
     grads = lm.state_dict("grad")
     new = lm.state_dict("param")
     lm.close()
