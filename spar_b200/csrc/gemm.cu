@@ -190,7 +190,7 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         if (p.epilogue == SPAR_B200_EPI_BIAS_ADD) v[4 * c + e] += a4[e];
-        else v[4 * c + e] *= gelu_derivative(a4[e]);
+        else v[4 * c + e] *= gelu_derivative_fast(a4[e]);
       }
     }
   }
@@ -200,7 +200,7 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
       *reinterpret_cast<float4*>(buf2 + swz(lane, c)) =
           make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) v[e] = gelu_value(v[e]);
+    for (int e = 0; e < 32; ++e) v[e] = gelu_value_fast(v[e]);
   }
   if (p.round_out) {
 #pragma unroll

@@ -66,6 +66,29 @@ __device__ __forceinline__ float gelu_derivative(float x) {
   return s + x * (s * (1.f - s)) * du;
 }
 
+// The same sigmoid / GELU / GELU' through the hardware exponential and an approximate divide
+// (__expf, __fdividef: a few ulp from the correctly rounded forms), for GEMM epilogues, where
+// the accurate library calls made the epilogue, not the tensor cores, the bound.
+__device__ __forceinline__ float fast_sigmoid(float v) {
+  const float e = __expf(-fabsf(v));
+  const float r = __fdividef(1.f, 1.f + e);
+  return v >= 0.f ? r : e * r;
+}
+
+__device__ __forceinline__ float gelu_value_fast(float x) {
+  const float x3 = (x * x) * x;
+  const float u = (x + x3 * kGeluB) * kGeluA;
+  return x * fast_sigmoid(u);
+}
+
+__device__ __forceinline__ float gelu_derivative_fast(float x) {
+  const float x2 = x * x;
+  const float u = (x + (x2 * x) * kGeluB) * kGeluA;
+  const float s = fast_sigmoid(u);
+  const float du = kGeluA * (1.f + 3.f * kGeluB * x2);
+  return s + x * (s * (1.f - s)) * du;
+}
+
 // ---------------------------------------------------------------- launchers (async, on stream)
 cudaError_t layernorm_forward_launch(float* y, float* mean, float* rstd, const float* x,
                                      const float* gamma, const float* beta, uint64_t rows,

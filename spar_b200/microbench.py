@@ -48,16 +48,23 @@ def report(name, ms, work, unit, peak):
     return line
 
 
-def run_gemm(m, n, k, at=False, bt=False, x3=False, iters=10):
+EPILOGUES = {"none": ops.EPI_NONE, "bias": ops.EPI_BIAS, "bias_gelu": ops.EPI_BIAS_GELU,
+             "gelu_bwd": ops.EPI_GELU_BWD, "bias_add": ops.EPI_BIAS_ADD}
+
+
+def run_gemm(m, n, k, at=False, bt=False, x3=False, iters=10, epi="none"):
     dev = torch.device("cuda")
     a = torch.randn((k, m) if at else (m, k), device=dev)
     b = torch.randn((n, k) if bt else (k, n), device=dev) * 0.02
     c = torch.empty(m, n, device=dev)
+    bias = torch.randn(n, device=dev) if epi in ("bias", "bias_gelu", "bias_add") else None
+    aux = torch.randn(m, n, device=dev) if epi in ("bias_gelu", "gelu_bwd", "bias_add") else None
     prec = ops.TF32X3 if x3 else ops.TF32
-    ms = timed(lambda: ops.matmul(a, b, a_t=at, b_t=bt, out=c, precision=prec), iters=iters)
+    ms = timed(lambda: ops.matmul(a, b, a_t=at, b_t=bt, out=c, precision=prec,
+                                  epilogue=EPILOGUES[epi], bias=bias, aux=aux), iters=iters)
     _, tf = peaks()
-    return report(f"gemm {m}x{n}x{k} a_t={int(at)} b_t={int(bt)} {'3xtf32' if x3 else 'tf32'}",
-                  ms, 2.0 * m * n * k, "TFLOP/s", tf)
+    return report(f"gemm {m}x{n}x{k} a_t={int(at)} b_t={int(bt)} {'3xtf32' if x3 else 'tf32'} "
+                  f"epi={epi}", ms, 2.0 * m * n * k, "TFLOP/s", tf)
 
 
 def run_attention(b=16, t=1024, h=16, dh=64, iters=10):
@@ -131,9 +138,10 @@ def main():
     ap.add_argument("--bt", action="store_true")
     ap.add_argument("--x3", action="store_true")
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--epi", default="none", choices=sorted(EPILOGUES))
     a = ap.parse_args()
     if a.kernel == "gemm":
-        run_gemm(a.m, a.n, a.k, a.at, a.bt, a.x3, a.iters)
+        run_gemm(a.m, a.n, a.k, a.at, a.bt, a.x3, a.iters, a.epi)
     elif a.kernel == "all":
         for (m, n, k, at, bt) in [(8192, 4096, 4096, 0, 0), (8192, 4096, 4096, 0, 1),
                                   (4096, 4096, 8192, 1, 0), (16384, 3072, 1024, 0, 0),
