@@ -216,6 +216,14 @@ struct SparB200Gemm {
   int causal;    /* SparB200Causal */
   int round_output; /* 1: store C rounded to nearest TF32 (for results that only feed TF32
                        products, which otherwise drop the low mantissa bits by truncation) */
+  /* Optional RoPE rotation in the epilogue (after bias, before rounding / storing), as           */
+  /* spar_b200_rope_apply on the result: for columns c < rope_cols, pairs (c, c+1) with c even    */
+  /* rotate by table[(row % rope_seq) * rope_dim/2 + (c % rope_dim)/2] (cos, sin). The fused      */
+  /* QKV projection uses it for its q and k thirds. Unbatched, non-accumulating GEMMs only.      */
+  const float* rope_table; /* [rope_seq, rope_dim/2] float2 from spar_b200_rope_table, or NULL */
+  uint64_t rope_seq;
+  uint64_t rope_dim;  /* even */
+  uint64_t rope_cols; /* multiple of rope_dim */
 };
 struct SparCudaStatus spar_b200_gemm(const struct SparB200Gemm* gemm, int device, void* stream);
 
@@ -234,7 +242,9 @@ int spar_b200_gemm_error(int device, int clear);
 /* scores * scale * log2(e), 1 / sum of exponentials) and read by the backward.                 */
 /* Backward: dctx in, dqkv [batch, seq, 3 * heads * head_dim] out (every column of every row     */
 /* overwritten); delta [batch, heads, seq] is scratch. head_dim must be 32 or 64; pointers      */
-/* 16-byte aligned. Asynchronous on `stream`; deterministic (no atomics).                       */
+/* 16-byte aligned. Asynchronous on `stream`; deterministic (no atomics). With a RoPE table     */
+/* ([seq, head_dim/2] float2 from spar_b200_rope_table, else NULL) the q and k thirds of dqkv    */
+/* are returned rotated back (the gradient of the projection before RoPE).                      */
 struct SparCudaStatus spar_b200_attention_forward(const float* qkv, float* ctx, float* row_max,
                                                   float* row_inv, uint64_t batch, uint64_t seq,
                                                   uint64_t heads, uint64_t head_dim, int device,
@@ -243,7 +253,8 @@ struct SparCudaStatus spar_b200_attention_backward(const float* qkv, const float
                                                    const float* dctx, const float* row_max,
                                                    const float* row_inv, float* delta, float* dqkv,
                                                    uint64_t batch, uint64_t seq, uint64_t heads,
-                                                   uint64_t head_dim, int device, void* stream);
+                                                   uint64_t head_dim, const float* rope_table,
+                                                   int device, void* stream);
 /* As spar_b200_gemm_error, for the attention kernels' bounded waits. */
 int spar_b200_attention_error(int device, int clear);
 

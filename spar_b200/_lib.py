@@ -34,7 +34,8 @@ class SparB200Gemm(ctypes.Structure):
         ("c", c_void_p), ("ldc", c_uint64), ("c_batch_stride", c_uint64 * 2),
         ("alpha", c_float), ("accumulate", c_int), ("epilogue", c_int), ("bias", c_void_p),
         ("aux", c_void_p), ("ldaux", c_uint64), ("precision", c_int), ("causal", c_int),
-        ("round_output", c_int),
+        ("round_output", c_int), ("rope_table", c_void_p), ("rope_seq", c_uint64),
+        ("rope_dim", c_uint64), ("rope_cols", c_uint64),
     ]
 
 
@@ -75,7 +76,7 @@ SIGNATURES = {
     "spar_b200_gemm": (S, [POINTER(SparB200Gemm), i, p]),
     "spar_b200_gemm_error": (c_int, [i, i]),
     "spar_b200_attention_forward": (S, [p, p, p, p, u64, u64, u64, u64, i, p]),
-    "spar_b200_attention_backward": (S, [p, p, p, p, p, p, p, u64, u64, u64, u64, i, p]),
+    "spar_b200_attention_backward": (S, [p, p, p, p, p, p, p, u64, u64, u64, u64, p, i, p]),
     "spar_b200_attention_error": (c_int, [i, i]),
     "spar_b200_lm_create": (S, [POINTER(SparB200LMConfig), i, POINTER(c_void_p)]),
     "spar_b200_lm_destroy": (None, [p]),

@@ -67,6 +67,7 @@ struct AttnParams {
   float* row_max;      // [batch*heads, seq]: max of scores * scale * log2(e)
   float* row_inv;      // [batch*heads, seq]: 1 / sum of exponentials
   float* delta;        // [batch*heads, seq]: D
+  const float2* rope;  // optional RoPE table [seq, head_dim / 2]: dQ, dK leave inverse-rotated
   uint32_t heads, seq, model_dim, bh;
   uint64_t ld_o;  // row stride of O and dO
   float scale, scale_log2;
@@ -111,6 +112,19 @@ __device__ __forceinline__ void store_row32(uint8_t* block, uint32_t r, const fl
   for (int i = 0; i < 8; ++i)
     *reinterpret_cast<float4*>(block + swz(r, i)) =
         make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+// Rotates 16 (x0, x1) column pairs back by their RoPE angles: (x0 c + x1 s, x1 c - x0 s), the
+// transpose of the forward rotation (src/nn/rope.cpp:35-66), so a gradient with respect to
+// rotated q / k becomes the gradient with respect to the unrotated projection.
+__device__ __forceinline__ void inverse_rope(float (&o)[32], const float2* tab) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 cs = __ldg(tab + i);
+    const float x0 = o[2 * i], x1 = o[2 * i + 1];
+    o[2 * i] = x0 * cs.x + x1 * cs.y;
+    o[2 * i + 1] = x1 * cs.x - x0 * cs.y;
+  }
 }
 
 struct Item {
@@ -691,6 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
         float o[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);
+        if (p.rope && valid) inverse_rope(o, p.rope + static_cast<uint64_t>(q) * (DH / 2) + grp * 16);
         store_box(&p.out, dsbuf + grp * 16384 + th.quarter * 4096, o,
                   static_cast<int>(it.h * DH + 32 * grp),
                   static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
@@ -977,6 +992,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
                   static_cast<int>(it.b));
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(w[e]);  // dK
+        if (p.rope && kv < seq) inverse_rope(o, p.rope + static_cast<uint64_t>(kv) * (DH / 2) + grp * 16);
         store_box(&p.out, dstbuf + grp * 16384 + th.quarter * 4096, o,
                   static_cast<int>(p.model_dim + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
@@ -1051,7 +1067,8 @@ cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_ma
 cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const float* dctx,
                                       const float* row_max, const float* row_inv, float* delta,
                                       float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
-                                      uint64_t head_dim, int device, cudaStream_t stream) {
+                                      uint64_t head_dim, int device, cudaStream_t stream,
+                                      const float* rope_table) {
   AttnParams p;
   base_params(p, batch, seq, heads, head_dim);
   const uint64_t d = heads * head_dim;
@@ -1068,6 +1085,7 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
   p.row_max = const_cast<float*>(row_max);
   p.row_inv = const_cast<float*>(row_inv);
   p.delta = delta;
+  p.rope = reinterpret_cast<const float2*>(rope_table);
   static bool q32[64] = {}, q64[64] = {}, k32[64] = {}, k64[64] = {};
   // Query kernel first: it produces D, which the key kernel reads.
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
@@ -1115,15 +1133,17 @@ extern "C" SparCudaStatus spar_b200_attention_backward(const float* qkv, const f
                                                        const float* row_inv, float* delta,
                                                        float* dqkv, uint64_t batch, uint64_t seq,
                                                        uint64_t heads, uint64_t head_dim,
-                                                       int device, void* stream) {
+                                                       const float* rope_table, int device,
+                                                       void* stream) {
   const float* ptrs[7] = {qkv, ctx, dctx, row_max, row_inv, delta, dqkv};
   const SparCudaStatus v = attention_validate(ptrs, 7, batch, seq, heads, head_dim);
   if (v.code) return v;
+  if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7)) return invalid();
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   const cudaError_t e = attention_backward_launch(qkv, ctx, dctx, row_max, row_inv, delta, dqkv,
                                                   batch, seq, heads, head_dim, device,
-                                                  static_cast<cudaStream_t>(stream));
+                                                  static_cast<cudaStream_t>(stream), rope_table);
   return e == cudaSuccess ? ok() : runtime(e);
 }
 

@@ -65,6 +65,8 @@ struct GemmParams {
   uint32_t kchunk;  // k-blocks per accumulation chunk (chunked kernels only)
   uint32_t kparts;  // split-K factor (1: no split); partial sums go to part_map
   int round_out;    // round the stored C to nearest TF32
+  const float2* rope;  // optional RoPE table [rope_seq, rope_half]
+  uint32_t rope_seq, rope_half, rope_dim, rope_cols;
 };
 
 struct TileCoord {
@@ -201,6 +203,17 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
           make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] = gelu_value_fast(v[e]);
+  }
+  if (p.rope && col0 < p.rope_cols) {  // RoPE on this row's 16 column pairs
+    const uint32_t pos = (row0 + lane) % p.rope_seq;
+    const float2* tab = p.rope + static_cast<uint64_t>(pos) * p.rope_half;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 cs = __ldg(tab + ((col0 + 2 * i) % p.rope_dim) / 2);
+      const float x0 = v[2 * i], x1 = v[2 * i + 1];
+      v[2 * i] = x0 * cs.x - x1 * cs.y;
+      v[2 * i + 1] = x0 * cs.y + x1 * cs.x;
+    }
   }
   if (p.round_out) {
 #pragma unroll
@@ -627,6 +640,7 @@ uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
 // fewest full-tile-equivalent rounds wins when it saves at least 15% over no split.
 uint32_t splitk_parts(const SparB200Gemm& g, int bn, int sms) {
   if (g.precision != SPAR_B200_TF32 || g.epilogue != SPAR_B200_EPI_NONE || g.round_output ||
+      g.rope_table ||
       g.causal != SPAR_B200_CAUSAL_NONE || (g.batch[0] > 1) || (g.batch[1] > 1) || g.n % 4)
     return 1;
   const uint64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + bn - 1) / bn);
@@ -725,6 +739,13 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   p.kchunk = 4;  // 4 k-blocks = 128 K elements x 3 sections per hardware-accumulated chunk
   p.kparts = 1;
   p.round_out = g.round_output != 0;
+  if (g.rope_table) {
+    p.rope = reinterpret_cast<const float2*>(g.rope_table);
+    p.rope_seq = static_cast<uint32_t>(g.rope_seq);
+    p.rope_half = static_cast<uint32_t>(g.rope_dim / 2);
+    p.rope_dim = static_cast<uint32_t>(g.rope_dim);
+    p.rope_cols = static_cast<uint32_t>(g.rope_cols);
+  }
   const uint32_t kparts = split ? 1 : splitk_parts(g, bn, sm_count(device));
   const uint64_t ldp = (g.n + 3) / 4 * 4;
   if (kparts > 1 && splitk_workspace && splitk_floats >= kparts * g.m * ldp) {
@@ -780,6 +801,11 @@ SparCudaStatus gemm_validate(const SparB200Gemm* g) {
   if (x.precision != SPAR_B200_TF32 && x.precision != SPAR_B200_TF32X3) return invalid();
   if (x.causal < 0 || x.causal > SPAR_B200_CAUSAL_K_FROM) return invalid();
   if (x.causal == SPAR_B200_CAUSAL_LOWER && x.m != x.n) return invalid();
+  if (x.rope_table &&
+      (x.rope_seq == 0 || x.rope_dim == 0 || x.rope_dim % 2 || x.rope_cols % x.rope_dim ||
+       x.rope_cols > x.n || b0 * b1 != 1 || x.accumulate || x.rope_seq > 0x7fffffffull ||
+       x.rope_cols > 0x7fffffffull || (x.epilogue != SPAR_B200_EPI_NONE && x.epilogue != SPAR_B200_EPI_BIAS)))
+    return invalid();
   if ((x.causal == SPAR_B200_CAUSAL_K_UPTO || x.causal == SPAR_B200_CAUSAL_K_FROM) && x.m != x.k)
     return invalid();
   return ok();

@@ -27,7 +27,8 @@ cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_ma
 cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const float* dctx,
                                       const float* row_max, const float* row_inv, float* delta,
                                       float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
-                                      uint64_t head_dim, int device, cudaStream_t stream);
+                                      uint64_t head_dim, int device, cudaStream_t stream,
+                                      const float* rope_table = nullptr);
 
 // Spar's stable sigmoid (src/ops/unary.cpp:55-61 / cuda_kernels.cu:105-111), in fp32.
 __device__ __forceinline__ float stable_sigmoid(float v) {

@@ -145,7 +145,7 @@ class LMTrainer {
                    bool accumulate, int epi, const float* bias, float* aux, uint64_t ldaux,
                    cudaStream_t s, int causal = SPAR_B200_CAUSAL_NONE, uint64_t b0 = 1,
                    uint64_t b1 = 1, const uint64_t* a_bs = nullptr, const uint64_t* b_bs = nullptr,
-                   const uint64_t* c_bs = nullptr, bool round_out = false);
+                   const uint64_t* c_bs = nullptr, bool round_out = false, bool rope = false);
   cudaError_t attention_forward(LayerActs& A, cudaStream_t s);
   cudaError_t attention_backward(LayerActs& A, cudaStream_t s);
   cudaError_t layer_backward(uint64_t l, cudaStream_t s);
@@ -346,7 +346,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
                             bool accumulate, int epi, const float* bias, float* aux,
                             uint64_t ldaux, cudaStream_t s, int causal, uint64_t b0, uint64_t b1,
                             const uint64_t* a_bs, const uint64_t* b_bs, const uint64_t* c_bs,
-                            bool round_out) {
+                            bool round_out, bool rope) {
   SparB200Gemm g{};
   g.m = m;
   g.n = n;
@@ -373,6 +373,12 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
   g.precision = cfg.precision;
   g.causal = causal;
   g.round_output = round_out;
+  if (rope) {  // RoPE on the q and k thirds of the fused projection output
+    g.rope_table = rope_tab;
+    g.rope_seq = T;
+    g.rope_dim = dh;
+    g.rope_cols = 2 * d;
+  }
   launches += cfg.precision == SPAR_B200_TF32X3 ? 3 : 1;
   // Never let a split copy run past the workspace sized in init().
   if (cfg.precision == SPAR_B200_TF32X3 && gemm_split_workspace_floats(g) > split_floats)
@@ -438,17 +444,14 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
     LayerActs& A = acts[l];
     const LayerOffsets& lo = lay[l];
     float* out = l + 1 < L ? acts[l + 1].x : xL;
-    launches += 2 + (cfg.use_rope ? 1 : 0) + 1;  // 2 LayerNorms, rope, softmax
+    launches += 2 + 1;  // 2 LayerNorms, softmax (or fused attention)
     SPAR_CHECK(layernorm_forward_launch(A.a1, A.mean1, A.rstd1, A.x, P + lo.ln1_g, P + lo.ln1_b,
                                         N, d, eps, device, s));
-    // q, k, v only feed attention products: with fused attention they are stored rounded to
-    // nearest TF32 (GEMM epilogue, then RoPE re-rounds the rotated q and k).
+    // qkv = a1 Wqkv + b, RoPE on the q and k thirds in the epilogue. q, k, v only feed
+    // attention products: with fused attention they are stored rounded to nearest TF32.
     SPAR_CHECK(gemm(N, 3 * d, d, A.a1, d, false, P + lo.wqkv, 3 * d, false, A.qkv, 3 * d, false,
                     SPAR_B200_EPI_BIAS, P + lo.bqkv, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1,
-                    nullptr, nullptr, nullptr, fused_attention));
-    if (cfg.use_rope)  // q and k heads are adjacent: rotate 2H heads of dh at row stride 3d
-      SPAR_CHECK(rope_apply_launch(A.qkv, rope_tab, N, T, 2 * H, dh, 3 * d, 0, device, s,
-                                   fused_attention));
+                    nullptr, nullptr, nullptr, fused_attention, cfg.use_rope != 0));
     SPAR_CHECK(attention_forward(A, s));
     SPAR_CHECK(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
                     SPAR_B200_EPI_BIAS_ADD, P + lo.bo, A.x, d, s));
@@ -500,7 +503,7 @@ cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
   if (fused_attention) {
     launches += 1;  // query and key kernels (one counted with the softmax in layer_backward)
     return attention_backward_launch(A.qkv, A.ctx, dtmp, A.stats, A.stats + B * H * T, dS, dqkv,
-                                     B, T, H, dh, device, s);
+                                     B, T, H, dh, device, s, cfg.use_rope ? rope_tab : nullptr);
   }
   const uint64_t ld = 3 * d;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
@@ -531,7 +534,7 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   const LayerOffsets& lo = lay[l];
   float* P = params;
   float* G = grads;
-  launches += 4 * 2 + 2 * 2 + 1 + (cfg.use_rope ? 1 : 0);  // col sums, LN bwd, softmax bwd, rope
+  launches += 4 * 2 + 2 * 2 + 1 + (cfg.use_rope && !fused_attention ? 1 : 0);  // col sums, LN bwd, softmax bwd, rope
   // dres = dL/d(layer output) = dL/d(h1 + mlp)
   // MLP: mlp = g W2 + b2, g = gelu(u), u = a2 W1 + b1
   SPAR_TRY(gemm(F, d, N, A.g, F, true, dres, d, false, G + lo.w2, d, true, SPAR_B200_EPI_NONE,
@@ -557,7 +560,9 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   // attention core: dtmp = dctx [N, d] -> dqkv
   SPAR_TRY(attention_backward(A, s));
   const uint64_t ld = 3 * d;
-  if (cfg.use_rope) SPAR_TRY(rope_apply_launch(dqkv, rope_tab, N, T, 2 * H, dh, ld, 1, device, s));
+  // Inverse RoPE on dq, dk (the fused attention kernels apply it in their epilogues).
+  if (cfg.use_rope && !fused_attention)
+    SPAR_TRY(rope_apply_launch(dqkv, rope_tab, N, T, 2 * H, dh, ld, 1, device, s));
   // QKV projection
   SPAR_TRY(gemm(d, 3 * d, N, A.a1, d, true, dqkv, ld, false, G + lo.wqkv, ld, true,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));

@@ -118,8 +118,9 @@ def attention_forward(qkv, heads: int):
     return ctx, row_max, row_inv
 
 
-def attention_backward(dctx, qkv, ctx, row_max, row_inv, heads: int):
-    """dqkv [batch, seq, 3*d] of the fused causal attention."""
+def attention_backward(dctx, qkv, ctx, row_max, row_inv, heads: int, rope_table=None):
+    """dqkv [batch, seq, 3*d] of the fused causal attention (q, k thirds rotated back by the
+    RoPE table when one is given)."""
     batch, seq, d3 = qkv.shape
     d = d3 // 3
     dqkv = torch.empty_like(qkv)
@@ -127,7 +128,7 @@ def attention_backward(dctx, qkv, ctx, row_max, row_inv, heads: int):
     call("spar_b200_attention_backward", _f32(qkv, "qkv").data_ptr(), _f32(ctx, "ctx").data_ptr(),
          _f32(dctx, "dctx").data_ptr(), _f32(row_max, "row_max").data_ptr(),
          _f32(row_inv, "row_inv").data_ptr(), delta.data_ptr(), dqkv.data_ptr(), batch, seq, heads,
-         d // heads, _dev(qkv), _stream(qkv))
+         d // heads, _ptr(rope_table), _dev(qkv), _stream(qkv))
     return dqkv
 
 
@@ -238,8 +239,12 @@ def rope_apply_(x, table, batch: int, t: int, heads: int, d: int, ld: int, inver
 def gemm_desc(m, n, k, a, lda, b, ldb, c, ldc, *, a_t=False, b_t=False, alpha=1.0,
               accumulate=False, epilogue=EPI_NONE, bias=None, aux=None, ldaux=0,
               precision=TF32, causal=CAUSAL_NONE, batch=(1, 1), a_bs=(0, 0), b_bs=(0, 0),
-              c_bs=(0, 0)) -> SparB200Gemm:
+              c_bs=(0, 0), round_output=False, rope=None) -> SparB200Gemm:
+    """rope = (table, seq, dim, cols) applies RoPE to columns < cols in the epilogue."""
     g = SparB200Gemm()
+    g.round_output = int(round_output)
+    if rope is not None:
+        g.rope_table, g.rope_seq, g.rope_dim, g.rope_cols = rope[0].data_ptr(), *rope[1:]
     g.m, g.n, g.k = m, n, k
     g.batch[0], g.batch[1] = batch
     g.a, g.lda, g.a_transposed = a, lda, int(a_t)
@@ -259,7 +264,7 @@ def gemm_run(desc: SparB200Gemm, device: int, stream: int) -> None:
 
 
 def matmul(a, b, *, a_t=False, b_t=False, out=None, alpha=1.0, accumulate=False,
-           epilogue=EPI_NONE, bias=None, aux=None, precision=TF32):
+           epilogue=EPI_NONE, bias=None, aux=None, precision=TF32, round_output=False, rope=None):
     """C = alpha * op(a) @ op(b) (+ epilogue) for 2-D row-major float32 tensors.
 
     op(a) = a.T when a_t (a stored [k, m]); op(b) = b.T when b_t (b stored [n, k]).
@@ -274,7 +279,8 @@ def matmul(a, b, *, a_t=False, b_t=False, out=None, alpha=1.0, accumulate=False,
     desc = gemm_desc(m, n, k, a.data_ptr(), a.shape[1], b.data_ptr(), b.shape[1], c.data_ptr(),
                      c.shape[1], a_t=a_t, b_t=b_t, alpha=alpha, accumulate=accumulate,
                      epilogue=epilogue, bias=_ptr(bias), aux=_ptr(aux),
-                     ldaux=(aux.shape[1] if aux is not None else 0), precision=precision)
+                     ldaux=(aux.shape[1] if aux is not None else 0), precision=precision,
+                     round_output=round_output, rope=rope)
     gemm_run(desc, _dev(a), _stream(a))
     return c
 

@@ -96,3 +96,23 @@ def test_attention_invalid_arguments(cuda):
     q = torch.zeros(1, 64, 3 * 4 * 48, device=cuda)
     with pytest.raises(_lib.SparError):
         ops.attention_forward(q, 4)  # head_dim 48 is not supported
+
+
+def test_attention_backward_inverse_rope(cuda):
+    """With a RoPE table the backward returns dq, dk rotated back: the same as rotating the
+    plain result with the standalone inverse rotation."""
+    import torch
+    from spar_b200 import ops
+
+    b, t, h, dh = 2, 160, 2, 64
+    d = h * dh
+    r = np.random.default_rng(31)
+    q = torch.from_numpy(rn_tf32(r.standard_normal((b, t, 3 * d)).astype(np.float32))).to(cuda)
+    do = torch.from_numpy(rn_tf32(r.standard_normal((b, t, d)).astype(np.float32))).to(cuda)
+    tab = ops.rope_table(t, dh, 10000.0, device=cuda)
+    ctx, mx, inv = ops.attention_forward(q, h)
+    rot = ops.attention_backward(do, q, ctx, mx, inv, h, rope_table=tab)
+    plain = ops.attention_backward(do, q, ctx, mx, inv, h)
+    ops.rope_apply_(plain, tab, b, t, 2 * h, dh, 3 * d, inverse=True)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(rot.cpu().numpy(), plain.cpu().numpy(), rtol=1e-5, atol=1e-6)

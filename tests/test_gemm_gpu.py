@@ -219,3 +219,26 @@ def test_gemm_invalid_arguments(cuda):
     with pytest.raises(SparError):  # unaligned leading dimension
         ops.gemm_run(ops.gemm_desc(64, 64, 62, a.data_ptr(), 62, a.data_ptr(), 64, a.data_ptr(), 64),
                      0, 0)
+
+
+def test_gemm_rope_epilogue(cuda):
+    """RoPE in the epilogue (fused QKV projection: q and k thirds rotated, v not) equals the
+    GEMM followed by the standalone rotation kernel."""
+    import torch
+    from spar_b200 import ops
+
+    b, t, h, dh = 2, 96, 4, 32
+    d = h * dh
+    r = np.random.default_rng(21)
+    x = torch.from_numpy(r.standard_normal((b * t, d)).astype(np.float32)).to(cuda)
+    w = torch.from_numpy((0.05 * r.standard_normal((d, 3 * d))).astype(np.float32)).to(cuda)
+    bias = torch.from_numpy(r.standard_normal(3 * d).astype(np.float32)).to(cuda)
+    tab = ops.rope_table(t, dh, 10000.0, device=cuda)
+    for prec in (ops.TF32, ops.TF32X3):
+        fused = ops.matmul(x, w, epilogue=ops.EPI_BIAS, bias=bias, precision=prec,
+                           rope=(tab, t, dh, 2 * d))
+        plain = ops.matmul(x, w, epilogue=ops.EPI_BIAS, bias=bias, precision=prec)
+        ops.rope_apply_(plain, tab, b, t, 2 * h, dh, 3 * d)
+        torch.cuda.synchronize()
+        assert ops.gemm_error(0) == 0
+        np.testing.assert_allclose(fused.cpu().numpy(), plain.cpu().numpy(), rtol=1e-5, atol=1e-5)
