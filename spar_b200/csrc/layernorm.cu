@@ -11,8 +11,8 @@
 //
 // Layout: one warp per row, the row held in registers as float4 (lane l owns float4 columns
 // l, l + 32, ...), so x and dy are read from HBM exactly once per pass. dgamma/dbeta are
-// accumulated per lane in registers, reduced over the block's warps in shared memory and written
-// as one partial row per block; a second kernel sums the partials in block order
+// accumulated per warp in shared memory, reduced over the block's warps in a fixed order and
+// written as one partial row per block; a second kernel sums the partials in a fixed order
 // (deterministic, no atomics).
 #include <mutex>
 
@@ -88,90 +88,99 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
 }
 
 template <int VPL>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, VPL <= 8 ? 2 : 1)
 layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dgamma,
                           float* __restrict__ partial_dbeta, const float* __restrict__ dy,
                           const float* __restrict__ x, const float* __restrict__ gamma,
                           const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                           uint64_t rows, int cols, uint64_t rows_per_block, int accumulate_dx) {
-  extern __shared__ float smem[];  // [kWarps][cols] twice
+  // Per-warp dgamma / dbeta accumulators live in shared memory ([kWarps][cols] twice; lane l
+  // owns float4 columns l, l + 32, ... of its warp's slice), which keeps the registers for the
+  // row in flight and lets two blocks share an SM.
+  extern __shared__ float smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int vec_cols = cols >> 2;
   const float inv_cols = 1.0f / static_cast<float>(cols);
-  float4 g[VPL], pg[VPL], pb[VPL];
+  float4* acc_g = reinterpret_cast<float4*>(smem + warp * cols);
+  float4* acc_b = reinterpret_cast<float4*>(smem + (kWarps + warp) * cols);
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int f = lane + 32 * j;
-    pg[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    pb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (f < vec_cols) g[j] = reinterpret_cast<const float4*>(gamma)[f];
+    if (f < vec_cols) {
+      acc_g[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+      acc_b[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
   const uint64_t row_begin = static_cast<uint64_t>(blockIdx.x) * rows_per_block;
   uint64_t row_end = row_begin + rows_per_block;
   if (row_end > rows) row_end = rows;
   for (uint64_t row = row_begin + warp; row < row_end; row += kWarps) {
     const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
     const float4* dyr = reinterpret_cast<const float4*>(dy + row * cols);
+    float4* dxr = reinterpret_cast<float4*>(dx + row * cols);
     const float mean = mean_in[row], rstd = rstd_in[row];
-    float4 xh[VPL], d[VPL];
+    float4 xh[VPL], d[VPL], prev[VPL];
+    // Issue every load of the row (x, dy and the dx being accumulated into) before any use.
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int f = lane + 32 * j;
+      if (f < vec_cols) {
+        xh[j] = ld_stream(xr + f);
+        d[j] = ld_stream(dyr + f);
+        if (accumulate_dx) prev[j] = dxr[f];
+      }
+    }
     float sg = 0.f, sgx = 0.f;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int f = lane + 32 * j;
       if (f < vec_cols) {
-        const float4 xv = ld_stream(xr + f);
-        d[j] = ld_stream(dyr + f);
-        xh[j] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
-                            (xv.w - mean) * rstd);
-        const float g0 = d[j].x * g[j].x, g1 = d[j].y * g[j].y, g2 = d[j].z * g[j].z,
-                    g3 = d[j].w * g[j].w;
+        xh[j] = make_float4((xh[j].x - mean) * rstd, (xh[j].y - mean) * rstd,
+                            (xh[j].z - mean) * rstd, (xh[j].w - mean) * rstd);
+        const float4 g = __ldg(g4 + f);
+        const float g0 = d[j].x * g.x, g1 = d[j].y * g.y, g2 = d[j].z * g.z, g3 = d[j].w * g.w;
         sg += (g0 + g1) + (g2 + g3);
         sgx += (g0 * xh[j].x + g1 * xh[j].y) + (g2 * xh[j].z + g3 * xh[j].w);
-        pg[j].x += d[j].x * xh[j].x;
-        pg[j].y += d[j].y * xh[j].y;
-        pg[j].z += d[j].z * xh[j].z;
-        pg[j].w += d[j].w * xh[j].w;
-        pb[j].x += d[j].x;
-        pb[j].y += d[j].y;
-        pb[j].z += d[j].z;
-        pb[j].w += d[j].w;
+        float4 ag = acc_g[f], ab = acc_b[f];
+        ag.x += d[j].x * xh[j].x;
+        ag.y += d[j].y * xh[j].y;
+        ag.z += d[j].z * xh[j].z;
+        ag.w += d[j].w * xh[j].w;
+        ab.x += d[j].x;
+        ab.y += d[j].y;
+        ab.z += d[j].z;
+        ab.w += d[j].w;
+        acc_g[f] = ag;
+        acc_b[f] = ab;
       }
     }
     const float mg = warp_sum(sg) * inv_cols;
     const float mgx = warp_sum(sgx) * inv_cols;
-    float4* dxr = reinterpret_cast<float4*>(dx + row * cols);
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int f = lane + 32 * j;
       if (f < vec_cols) {
+        const float4 g = __ldg(g4 + f);
         float4 o;
-        o.x = rstd * (d[j].x * g[j].x - mg - xh[j].x * mgx);
-        o.y = rstd * (d[j].y * g[j].y - mg - xh[j].y * mgx);
-        o.z = rstd * (d[j].z * g[j].z - mg - xh[j].z * mgx);
-        o.w = rstd * (d[j].w * g[j].w - mg - xh[j].w * mgx);
+        o.x = rstd * (d[j].x * g.x - mg - xh[j].x * mgx);
+        o.y = rstd * (d[j].y * g.y - mg - xh[j].y * mgx);
+        o.z = rstd * (d[j].z * g.z - mg - xh[j].z * mgx);
+        o.w = rstd * (d[j].w * g.w - mg - xh[j].w * mgx);
         if (accumulate_dx) {
-          const float4 prev = dxr[f];
-          o.x += prev.x;
-          o.y += prev.y;
-          o.z += prev.z;
-          o.w += prev.w;
+          o.x += prev[j].x;
+          o.y += prev[j].y;
+          o.z += prev[j].z;
+          o.w += prev[j].w;
         }
         dxr[f] = o;
       }
     }
   }
   // Reduce the per-warp partials over the block (fixed warp order).
-  float* sg_ = smem;
-  float* sb_ = smem + kWarps * cols;
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) {
-    const int f = lane + 32 * j;
-    if (f < vec_cols) {
-      reinterpret_cast<float4*>(sg_ + warp * cols)[f] = pg[j];
-      reinterpret_cast<float4*>(sb_ + warp * cols)[f] = pb[j];
-    }
-  }
   __syncthreads();
+  const float* sg_ = smem;
+  const float* sb_ = smem + kWarps * cols;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
     float a = 0.f, bsum = 0.f;
 #pragma unroll
@@ -184,23 +193,39 @@ layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dg
   }
 }
 
-// Sums `parts` partial rows of length cols in order; out (+)= result.
-__global__ void reduce_partials_kernel(float* __restrict__ out_a, float* __restrict__ out_b,
-                                       const float* __restrict__ pa, const float* __restrict__ pb,
-                                       int parts, int cols, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+// Sums `parts` partial rows of length cols in a fixed order; out (+)= result. Block = 32 columns
+// x 8 warps: warp w sums parts w, w + 8, ... in increasing order, then warp 0 adds the eight
+// warp sums in warp order (deterministic).
+__global__ void __launch_bounds__(256)
+reduce_partials_kernel(float* __restrict__ out_a, float* __restrict__ out_b,
+                       const float* __restrict__ pa, const float* __restrict__ pb, int parts,
+                       int cols, int accumulate) {
+  __shared__ float sa[8][32], sb[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
   float a = 0.f, b = 0.f;
-  for (int p = 0; p < parts; ++p) {
-    a += pa[static_cast<uint64_t>(p) * cols + c];
-    b += pb[static_cast<uint64_t>(p) * cols + c];
+  if (c < cols)
+    for (int p = warp; p < parts; p += 8) {
+      a += pa[static_cast<uint64_t>(p) * cols + c];
+      b += pb[static_cast<uint64_t>(p) * cols + c];
+    }
+  sa[warp][lane] = a;
+  sb[warp][lane] = b;
+  __syncthreads();
+  if (warp == 0 && c < cols) {
+    float ta = 0.f, tb = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      ta += sa[w][lane];
+      tb += sb[w][lane];
+    }
+    if (accumulate) {
+      ta += out_a[c];
+      tb += out_b[c];
+    }
+    out_a[c] = ta;
+    out_b[c] = tb;
   }
-  if (accumulate) {
-    a += out_a[c];
-    b += out_b[c];
-  }
-  out_a[c] = a;
-  out_b[c] = b;
 }
 
 int vectors_per_lane(uint64_t cols) {
@@ -274,8 +299,8 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  reduce_partials_kernel<<<(c + 255) / 256, 256, 0, stream>>>(dgamma, dbeta, pa, pb, parts, c,
-                                                              accumulate_params);
+  reduce_partials_kernel<<<(c + 31) / 32, 256, 0, stream>>>(dgamma, dbeta, pa, pb, parts, c,
+                                                            accumulate_params);
   return cudaGetLastError();
 }
 
