@@ -59,6 +59,7 @@ struct AttnParams {
   CUtensorMap qk64;    // qkv, K-major boxes {32, 64}
   CUtensorMap qkv_mn;  // qkv, MN-major boxes {32, 32}
   CUtensorMap do128;   // dO (= d ctx), K-major {32, 128}
+  CUtensorMap o128;    // O (= ctx), K-major {32, 128} (D = rowsum(dO o O) from shared memory)
   CUtensorMap do64;    // dO, K-major {32, 64}
   CUtensorMap do_mn;   // dO, MN-major {32, 32}
   CUtensorMap out;     // output store boxes {32, 32}: ctx (forward) or dqkv (backward)
@@ -475,8 +476,9 @@ struct BwdQ {
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kDO = kQ + kTile128;
   static constexpr uint32_t kStage = 3 * kTile64;  // K (K-major), V (K-major), K (MN-major)
-  static constexpr uint32_t kKV = kDO + kTile128;   // 2 stages
-  static constexpr uint32_t kDS = kKV + 2 * kStage;  // 128 x 64 dS, 2 K blocks of 16 KB
+  static constexpr uint32_t kO = kDO + kTile128;
+  static constexpr uint32_t kKV = kO + kTile128;     // 2 stages
+  static constexpr uint32_t kDS = kKV + 2 * kStage;  // dQ output staging (4 KB per warp)
   static constexpr uint32_t kBar = kDS + 32768;
   static constexpr uint32_t kSmem = kBar + 256 + 1024;
   static_assert(kSmem <= kMaxSmem, "query-kernel shared memory");
@@ -495,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
   uint64_t* s_full = bars + 6;    // [2]
   uint64_t* s_empty = bars + 8;   // [2]
   uint64_t* ds_full = bars + 10;
-  uint64_t* ds_empty = bars + 11;
+  uint64_t* d_done = bars + 11;  // softmax warps finished reading O / dO for D
   uint64_t* acc_full = bars + 12;
   uint64_t* acc_empty = bars + 13;
   uint64_t* drain = bars + 14;
@@ -510,10 +512,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       tc::mbar_init(kv_full + i, 1);
       tc::mbar_init(kv_empty + i, 1);
       tc::mbar_init(s_full + i, 1);
-      tc::mbar_init(s_empty + i, kSoftWarps);
+      tc::mbar_init(s_empty + i, 1);  // freed by the MMA once dQ has read dS (aliasing S)
     }
     tc::mbar_init(ds_full, kSoftWarps);
-    tc::mbar_init(ds_empty, 1);
+    tc::mbar_init(d_done, kSoftWarps);
     tc::mbar_init(acc_full, 1);
     tc::mbar_init(acc_empty, kSoftWarps);
     tc::mbar_init(drain, 1);
@@ -539,13 +541,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
         const Item it = decode(p, idx, true);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
         if (!wait_or_abort(q_empty, (item & 1) ^ 1, abort_flag)) break;
-        tc::mbar_arrive_expect_tx(q_full, 2 * L::kTile128);
+        tc::mbar_arrive_expect_tx(q_full, 3 * L::kTile128);
         last_q = item & 1;
         const int q0 = static_cast<int>(it.t * 128);
 #pragma unroll
         for (int c = 0; c < DH / 32; ++c) {
           tc::tma_load_4d(smem + L::kQ + c * 16384, &p.qk128, q_full, hc + 32 * c, q0, b, 0);
           tc::tma_load_4d(smem + L::kDO + c * 16384, &p.do128, q_full, hc + 32 * c, q0, b, 0);
+          tc::tma_load_4d(smem + L::kO + c * 16384, &p.o128, q_full, hc + 32 * c, q0, b, 0);
         }
         const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
         for (uint32_t j = 0; j < nkv; ++j, ++n) {
@@ -581,7 +584,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       const uint32_t q_addr = tc::smem_u32(smem + L::kQ);
       const uint32_t do_addr = tc::smem_u32(smem + L::kDO);
       const uint32_t kv_addr = tc::smem_u32(smem + L::kKV);
-      const uint32_t ds_addr = tc::smem_u32(smem + L::kDS);
       uint32_t n = 0, sn = 0, dn = 0, item = 0;
       bool ok = true;
       auto issue_s = [&](uint32_t kn) -> bool {  // S and dP for kv load number kn
@@ -606,24 +608,28 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
         const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
         if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
         tc::tc_fence_after();
-        const uint32_t n0 = n;
+        const uint32_t n0 = n, sn0 = sn;
         if (!(ok = issue_s(n0))) break;
         for (uint32_t j = 0; j < nkv && ok; ++j) {
           if (j + 1 < nkv) {
             if (!(ok = issue_s(n0 + j + 1))) break;
           }
-          if (j + 1 == nkv) tc::mma_commit(q_empty);
+          if (j + 1 == nkv) {  // Q, dO, O free once the MMAs and the D readers are done
+            if (!(ok = wait_or_abort(d_done, item & 1, abort_flag))) break;
+            tc::mma_commit(q_empty);
+          }
           if (!(ok = wait_or_abort(ds_full, dn & 1, abort_flag))) break;
           ++dn;
           if (j == 0 && !(ok = wait_or_abort(acc_empty, (item & 1) ^ 1, abort_flag))) break;
           tc::tc_fence_after();
-          const uint32_t st = (n0 + j) & 1;
+          const uint32_t st = (n0 + j) & 1, sb = (sn0 + j) & 1;
           const uint32_t kmn = kv_addr + st * L::kStage + 2 * L::kTile64;
+          // dQ += dS K with dS read from TMEM, where the softmax warps wrote it over S.
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            tc::mma_tf32(tmem + 256, kmajor_desc(ds_addr, 16384, ks), mnmajor_desc<DH>(kmn, ks),
-                         idesc_q, (j | ks) != 0);
-          tc::mma_commit(ds_empty);
+            tc::mma_tf32_ts(tmem + 256, tmem + sb * 64 + ks * 8, mnmajor_desc<DH>(kmn, ks),
+                            idesc_q, (j | ks) != 0);
+          tc::mma_commit(s_empty + sb);
           tc::mma_commit(kv_empty + st);
         }
         n = n0 + nkv;
@@ -638,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
     const SoftThread th(warp, lane, tmem);
     const uint32_t r = th.r, grp = th.grp;
     uint8_t* dsbuf = smem + L::kDS;
-    uint32_t sn = 0, dn = 0, item = 0;
+    uint32_t sn = 0, item = 0;
     bool ok = true;
     for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
       const Item it = decode(p, idx, true);
@@ -651,16 +657,23 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       if (valid) {
         mx = p.row_max[srow];
         inv = p.row_inv[srow];
-        const uint64_t off = (static_cast<uint64_t>(it.b) * seq + q) * p.ld_o + it.h * DH;
-        const float4* a = reinterpret_cast<const float4*>(p.d_o + off);
-        const float4* o = reinterpret_cast<const float4*>(p.o + off);
+      }
+      // D = rowsum(dO o O) of this row, from the tiles the producer staged (zeros past seq).
+      if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
 #pragma unroll
-        for (int i = 0; i < DH / 4; ++i) {
-          const float4 x = __ldg(a + i), y = __ldg(o + i);
+      for (int c = 0; c < DH / 32; ++c) {
+        const uint8_t* a = smem + L::kDO + c * 16384;
+        const uint8_t* o = smem + L::kO + c * 16384;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 x = *reinterpret_cast<const float4*>(a + swz(r, i));
+          const float4 y = *reinterpret_cast<const float4*>(o + swz(r, i));
           dd += x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
         }
-        if (grp == 0) p.delta[srow] = dd;
       }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(d_done);
+      if (valid && grp == 0) p.delta[srow] = dd;
       const float ninv_scale = inv * p.scale;
       if (lane == 0) tc::bulk_wait_read<0>();
       __syncwarp();
@@ -670,9 +683,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
         uint32_t sv[32], pv[32];
         tc::tmem_load_2x32(th.lanes + (sn & 1) * 64 + grp * 32,
                            th.lanes + 128 + (sn & 1) * 64 + grp * 32, sv, pv);
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(s_empty + (sn & 1));
         const uint32_t kv0 = j * 64 + grp * 32;
         float ds[32];
         if (kv0 + 31 <= it.t * 128) {  // every key of this chunk precedes every row of the tile
@@ -689,12 +699,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
             ds[e] = round_tf32(pr * ninv_scale * (__uint_as_float(pv[e]) - dd));
           }
         }
-        if (dn > 0 && !(ok = wait_or_abort(ds_empty, (dn - 1) & 1, abort_flag))) break;
-        store_row32(dsbuf + grp * 16384, r, ds);
-        tc::fence_proxy_async_smem();
+        // dS overwrites this thread's S columns in TMEM: the A operand of dQ += dS K.
+        uint32_t dsu[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) dsu[e] = __float_as_uint(ds[e]);
+        tc::tmem_store_32x32(th.lanes + (sn & 1) * 64 + grp * 32, dsu);
+        tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(ds_full);
-        ++dn;
       }
       if (!ok) break;
       if (!(ok = wait_or_abort(acc_full, item & 1, abort_flag))) break;
@@ -1076,6 +1088,7 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
       !make_map(&p.qk64, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 64, false) ||
       !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true) ||
       !make_map(&p.do128, dctx, d, seq, batch, 1, d, seq * d, 0, 128, false) ||
+      !make_map(&p.o128, ctx, d, seq, batch, 1, d, seq * d, 0, 128, false) ||
       !make_map(&p.do64, dctx, d, seq, batch, 1, d, seq * d, 0, 64, false) ||
       !make_map(&p.do_mn, dctx, d, seq, batch, 1, d, seq * d, 0, 32, true) ||
       !make_map(&p.out, dqkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, false))
