@@ -744,15 +744,17 @@ struct BwdKV {
   static constexpr uint32_t kK = 0;
   static constexpr uint32_t kV = kK + kTile128;
   static constexpr uint32_t kKQ = kV + kTile128;      // 2 stages: Q and dO K-major (64 rows)
-  static constexpr uint32_t kMN = kKQ + 4 * kTile64;  // 1 stage: Q and dO MN-major
-  static constexpr uint32_t kPT = kMN + 2 * kTile64;  // 128 x 64 P^T
-  static constexpr uint32_t kDST = kPT + 32768;       // 128 x 64 dS^T
-  static constexpr uint32_t kStats = kDST + 32768;    // [2 steps][row max, 1/sum, D][64 queries]
+  static constexpr uint32_t kMN = kKQ + 4 * kTile64;  // 2 stages: Q and dO MN-major
+  static constexpr uint32_t kStg = kMN + 4 * kTile64;  // output staging, 4 KB per softmax warp
+  static constexpr uint32_t kStats = kStg + kSoftWarps * 4096;  // [2 steps][max, 1/sum, D][64]
   static constexpr uint32_t kBar = kStats + 2 * 3 * 64 * 4;
   static constexpr uint32_t kSmem = kBar + 192 + 1024;
   static_assert(kSmem <= kMaxSmem, "key-kernel shared memory");
 };
 
+// TMEM columns: S^T / P^T [2][64] at 0, dP^T / dS^T [2][64] at 128, dV at 256, dK at 256 + DH.
+// P^T and dS^T overwrite S^T and dP^T in place and are the A operands of dV += P^T dO and
+// dK += dS^T Q, read straight from TMEM.
 template <int DH>
 __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_constant__ AttnParams p) {
   using L = BwdKV<DH>;
@@ -765,15 +767,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
   uint64_t* kq_empty = bars + 4;  // [2]
   uint64_t* s_full = bars + 6;    // [2]
   uint64_t* s_empty = bars + 8;   // [2]
-  uint64_t* mn_full = bars + 10;
-  uint64_t* mn_empty = bars + 11;
-  uint64_t* pd_full = bars + 12;
-  uint64_t* pd_empty = bars + 13;
-  uint64_t* acc_full = bars + 14;
-  uint64_t* acc_empty = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint64_t* xbar = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* mn_full = bars + 10;  // [2]
+  uint64_t* mn_empty = bars + 12;  // [2]
+  uint64_t* pd_full = bars + 14;
+  uint64_t* acc_full = bars + 15;
+  uint64_t* acc_empty = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint64_t* xbar = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -784,12 +785,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       tc::mbar_init(kq_full + i, 1);
       tc::mbar_init(kq_empty + i, 1);
       tc::mbar_init(s_full + i, 1);
-      tc::mbar_init(s_empty + i, kSoftWarps);
+      tc::mbar_init(s_empty + i, 1);  // freed by the MMA once dV / dK have read P^T / dS^T
+      tc::mbar_init(mn_full + i, 1);
+      tc::mbar_init(mn_empty + i, 1);
     }
-    tc::mbar_init(mn_full, 1);
-    tc::mbar_init(mn_empty, 1);
     tc::mbar_init(pd_full, kSoftWarps);
-    tc::mbar_init(pd_empty, 1);
     tc::mbar_init(acc_full, 1);
     tc::mbar_init(acc_empty, kSoftWarps);
     tc::mbar_init(drain, 1);
@@ -812,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
   if (warp == 0) {
     if (tc::elect_one()) {
       uint32_t n = 0, item = 0;
-      int last_kv = -1, last_kq[2] = {-1, -1}, last_mn = -1;
+      int last_kv = -1, last_kq[2] = {-1, -1}, last_mn[2] = {-1, -1};
       for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
         const Item it = decode(p, idx, false);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
@@ -827,35 +827,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
                           b, 0);
         }
         for (uint32_t i = 2 * it.t; i < nq_all; ++i, ++n) {
-          const uint32_t st = n & 1;
+          const uint32_t st = n & 1, ph = (n >> 1) & 1;
           const int row = static_cast<int>(i * 64);
-          if (!wait_or_abort(kq_empty + st, ((n >> 1) & 1) ^ 1, abort_flag)) break;
+          if (!wait_or_abort(kq_empty + st, ph ^ 1, abort_flag)) break;
           tc::mbar_arrive_expect_tx(kq_full + st, 2 * L::kTile64);
-          last_kq[st] = (n >> 1) & 1;
+          last_kq[st] = ph;
           uint8_t* s = smem + L::kKQ + st * 2 * L::kTile64;
 #pragma unroll
           for (int c = 0; c < DH / 32; ++c) {
             tc::tma_load_4d(s + c * 8192, &p.qk64, kq_full + st, hc + 32 * c, row, b, 0);
             tc::tma_load_4d(s + L::kTile64 + c * 8192, &p.do64, kq_full + st, hc + 32 * c, row, b, 0);
           }
-          if (!wait_or_abort(mn_empty, (n & 1) ^ 1, abort_flag)) break;
-          tc::mbar_arrive_expect_tx(mn_full, 2 * L::kTile64);
-          last_mn = n & 1;
+          if (!wait_or_abort(mn_empty + st, ph ^ 1, abort_flag)) break;
+          tc::mbar_arrive_expect_tx(mn_full + st, 2 * L::kTile64);
+          last_mn[st] = ph;
+          uint8_t* m = smem + L::kMN + st * 2 * L::kTile64;
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
             for (int c = 0; c < DH / 32; ++c) {
               const uint32_t o = (kb * (DH / 32) + c) * 4096;
-              tc::tma_load_4d(smem + L::kMN + o, &p.qkv_mn, mn_full, hc + 32 * c, row + 32 * kb, b, 0);
-              tc::tma_load_4d(smem + L::kMN + L::kTile64 + o, &p.do_mn, mn_full, hc + 32 * c,
+              tc::tma_load_4d(m + o, &p.qkv_mn, mn_full + st, hc + 32 * c, row + 32 * kb, b, 0);
+              tc::tma_load_4d(m + L::kTile64 + o, &p.do_mn, mn_full + st, hc + 32 * c,
                               row + 32 * kb, b, 0);
             }
         }
       }
       if (last_kv >= 0 && !tc::mbar_wait(kv_full, last_kv)) record_error();
-      if (last_mn >= 0 && !tc::mbar_wait(mn_full, last_mn)) record_error();
-      for (int s = 0; s < 2; ++s)
+      for (int s = 0; s < 2; ++s) {
         if (last_kq[s] >= 0 && !tc::mbar_wait(kq_full + s, last_kq[s])) record_error();
+        if (last_mn[s] >= 0 && !tc::mbar_wait(mn_full + s, last_mn[s])) record_error();
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -866,8 +868,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       const uint32_t v_addr = tc::smem_u32(smem + L::kV);
       const uint32_t kq_addr = tc::smem_u32(smem + L::kKQ);
       const uint32_t mn_addr = tc::smem_u32(smem + L::kMN);
-      const uint32_t pt_addr = tc::smem_u32(smem + L::kPT);
-      const uint32_t dst_addr = tc::smem_u32(smem + L::kDST);
       uint32_t n = 0, sn = 0, item = 0;
       bool ok = true;
       auto issue_s = [&](uint32_t qn) -> bool {  // S^T and dP^T for query load number qn
@@ -893,26 +893,28 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         const uint32_t steps = nq_all - 2 * it.t;  // >= 1: every 128-key tile starts below seq
         if (!(ok = wait_or_abort(kv_full, item & 1, abort_flag))) break;
         tc::tc_fence_after();
-        const uint32_t n0 = n;
+        const uint32_t n0 = n, sn0 = sn;
         if (!(ok = issue_s(n0))) break;
         for (uint32_t i = 0; i < steps && ok; ++i) {
           if (i + 1 < steps) {
             if (!(ok = issue_s(n0 + i + 1))) break;
           }
           if (i + 1 == steps) tc::mma_commit(kv_empty);
-          if (!(ok = wait_or_abort(pd_full, (n0 + i) & 1, abort_flag))) break;
-          if (!(ok = wait_or_abort(mn_full, (n0 + i) & 1, abort_flag))) break;
+          const uint32_t qn = n0 + i, st = qn & 1, sb = (sn0 + i) & 1;
+          if (!(ok = wait_or_abort(pd_full, qn & 1, abort_flag))) break;
+          if (!(ok = wait_or_abort(mn_full + st, (qn >> 1) & 1, abort_flag))) break;
           if (i == 0 && !(ok = wait_or_abort(acc_empty, (item & 1) ^ 1, abort_flag))) break;
           tc::tc_fence_after();
+          const uint32_t m = mn_addr + st * 2 * L::kTile64;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
-            tc::mma_tf32(tmem + 256, kmajor_desc(pt_addr, 16384, ks),
-                         mnmajor_desc<DH>(mn_addr + L::kTile64, ks), idesc_g, (i | ks) != 0);
-            tc::mma_tf32(tmem + 256 + DH, kmajor_desc(dst_addr, 16384, ks),
-                         mnmajor_desc<DH>(mn_addr, ks), idesc_g, (i | ks) != 0);
+            tc::mma_tf32_ts(tmem + 256, tmem + sb * 64 + ks * 8,
+                            mnmajor_desc<DH>(m + L::kTile64, ks), idesc_g, (i | ks) != 0);
+            tc::mma_tf32_ts(tmem + 256 + DH, tmem + 128 + sb * 64 + ks * 8,
+                            mnmajor_desc<DH>(m, ks), idesc_g, (i | ks) != 0);
           }
-          tc::mma_commit(pd_empty);
-          tc::mma_commit(mn_empty);
+          tc::mma_commit(s_empty + sb);
+          tc::mma_commit(mn_empty + st);
         }
         n = n0 + steps;
         if (ok) tc::mma_commit(acc_full);
@@ -930,8 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
     const uint32_t u = (warp - 2) * 32 + lane;
     const float* src = u < 64 ? p.row_max : (u < 128 ? p.row_inv : p.delta);
     float* stats = reinterpret_cast<float*>(smem + L::kStats);  // [2][3][64]
-    uint8_t* ptbuf = smem + L::kPT;
-    uint8_t* dstbuf = smem + L::kDST;
+    uint8_t* stg = smem + L::kStg + (warp - 2) * 4096;
     uint32_t n = 0, item = 0, xphase = 0;
     bool ok = true;
     // Queries past the sequence get zero statistics: their probabilities come out 0.
@@ -946,8 +947,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       const uint32_t kv = it.t * 128 + r;
       const uint64_t sbase = static_cast<uint64_t>(it.b * p.heads + it.h) * seq;
       float next = fetch(sbase, i0 * 64);
-      if (lane == 0) tc::bulk_wait_read<0>();
-      __syncwarp();
       for (uint32_t i = 0; i < steps && ok; ++i, ++n) {
         float* st = stats + (n & 1) * 192;
         if (u < 192) st[u] = next;
@@ -956,16 +955,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         if (!(ok = wait_or_abort(s_full + (n & 1), (n >> 1) & 1, abort_flag))) break;
         tc::tc_fence_after();
         uint32_t sv[32], pv[32];
-        tc::tmem_load_2x32(th.lanes + (n & 1) * 64 + grp * 32,
-                           th.lanes + 128 + (n & 1) * 64 + grp * 32, sv, pv);
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(s_empty + (n & 1));
+        const uint32_t s_col = th.lanes + (n & 1) * 64 + grp * 32;
+        tc::tmem_load_2x32(s_col, s_col + 128, sv, pv);
         const uint32_t q0 = (i0 + i) * 64 + grp * 32;
         const float4* mx4 = reinterpret_cast<const float4*>(st + grp * 32);
         const float4* inv4 = reinterpret_cast<const float4*>(st + 64 + grp * 32);
         const float4* dd4 = reinterpret_cast<const float4*>(st + 128 + grp * 32);
-        float pt[32], dst[32];
         const bool full = q0 >= it.t * 128 + 127;  // every query of the chunk follows every key
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
@@ -978,14 +973,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
             const int e = 4 * g + e4;
             float pr = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -mv[e4])) * iv[e4];
             if (!full && q0 + e < kv) pr = 0.f;
-            pt[e] = round_tf32(pr);
-            dst[e] = round_tf32(pr * (__uint_as_float(pv[e]) - dv[e4]) * p.scale);
+            const float ds = pr * (__uint_as_float(pv[e]) - dv[e4]) * p.scale;
+            sv[e] = __float_as_uint(round_tf32(pr));
+            pv[e] = __float_as_uint(round_tf32(ds));
           }
         }
-        if (n > 0 && !(ok = wait_or_abort(pd_empty, (n - 1) & 1, abort_flag))) break;
-        store_row32(ptbuf + grp * 16384, r, pt);
-        store_row32(dstbuf + grp * 16384, r, dst);
-        tc::fence_proxy_async_smem();
+        // P^T and dS^T overwrite S^T and dP^T: the TMEM A operands of dV and dK.
+        tc::tmem_store_2x32(s_col, s_col + 128, sv, pv);
+        tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(pd_full);
       }
@@ -997,16 +992,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         uint32_t v[32], w[32];
         tc::tmem_load_2x32(th.lanes + 256 + grp * 32, th.lanes + 256 + DH + grp * 32, v, w);
         float o[32];
+        if (lane == 0) tc::bulk_wait_read<0>();  // this warp's staging box is free again
+        __syncwarp();
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);  // dV
-        store_box(&p.out, ptbuf + grp * 16384 + th.quarter * 4096, o,
-                  static_cast<int>(2 * p.model_dim + it.h * DH + 32 * grp), row,
+        store_box(&p.out, stg, o, static_cast<int>(2 * p.model_dim + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
+        if (lane == 0) {
+          tc::bulk_commit();
+          tc::bulk_wait_read<0>();
+        }
+        __syncwarp();
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(w[e]);  // dK
         if (p.rope && kv < seq) inverse_rope(o, p.rope + static_cast<uint64_t>(kv) * (DH / 2) + grp * 16);
-        store_box(&p.out, dstbuf + grp * 16384 + th.quarter * 4096, o,
-                  static_cast<int>(p.model_dim + it.h * DH + 32 * grp), row,
+        store_box(&p.out, stg, o, static_cast<int>(p.model_dim + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
         if (lane == 0) tc::bulk_commit();
       }
