@@ -187,12 +187,15 @@ struct Fwd {
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kK = kQ + kTile;      // 2 stages
   static constexpr uint32_t kV = kK + 2 * kTile;  // 2 stages
-  static constexpr uint32_t kP = kV + 2 * kTile;  // 128 x 128 probabilities, 4 K blocks of 16 KB
-  static constexpr uint32_t kBar = kP + 65536;
+  static constexpr uint32_t kStg = kV + 2 * kTile;  // output staging, 4 KB per softmax warp
+  static constexpr uint32_t kX = kStg + kSoftWarps * 4096;  // row partials [max 2x128][sum 2x128]
+  static constexpr uint32_t kBar = kX + 2048;
   static constexpr uint32_t kSmem = kBar + 256 + 1024;
   static_assert(kSmem <= kMaxSmem, "forward shared memory");
 };
 
+// TMEM columns: S / P [2][128] at 0 and 128 (P overwrites S and is the A operand of O += P V),
+// O at 256.
 template <int DH>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   using L = Fwd<DH>;
@@ -201,17 +204,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;   // [2]
-  uint64_t* kv_empty = bars + 4;  // [2]
-  uint64_t* s_full = bars + 6;    // [2]
-  uint64_t* s_empty = bars + 8;   // [2]
-  uint64_t* p_full = bars + 10;
-  uint64_t* p_empty = bars + 11;
-  uint64_t* o_full = bars + 12;
-  uint64_t* o_empty = bars + 13;
-  uint64_t* xbar = bars + 14;  // softmax-warp rendezvous
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* kv_full = bars + 2;    // [2]
+  uint64_t* kv_empty = bars + 4;   // [2]
+  uint64_t* s_full = bars + 6;     // [2]
+  uint64_t* s_read = bars + 8;     // [2] pass 1: the softmax warps have read S
+  uint64_t* s_used = bars + 10;    // [2] pass 2: the P V product has read P
+  uint64_t* p_full = bars + 12;
+  uint64_t* o_full = bars + 13;
+  uint64_t* o_empty = bars + 14;
+  uint64_t* xbar = bars + 15;  // softmax-warp rendezvous
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -222,10 +225,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       tc::mbar_init(kv_full + i, 1);
       tc::mbar_init(kv_empty + i, 1);
       tc::mbar_init(s_full + i, 1);
-      tc::mbar_init(s_empty + i, kSoftWarps);
+      tc::mbar_init(s_read + i, kSoftWarps);
+      tc::mbar_init(s_used + i, 1);
     }
     tc::mbar_init(p_full, kSoftWarps);
-    tc::mbar_init(p_empty, 1);
     tc::mbar_init(o_full, 1);
     tc::mbar_init(o_empty, kSoftWarps);
     tc::mbar_init(xbar, kSoftWarps);
@@ -297,20 +300,33 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       const uint32_t q_addr = tc::smem_u32(smem + L::kQ);
       const uint32_t k_addr = tc::smem_u32(smem + L::kK);
       const uint32_t v_addr = tc::smem_u32(smem + L::kV);
-      const uint32_t p_addr = tc::smem_u32(smem + L::kP);
       uint32_t n = 0, sn = 0, pn = 0, item = 0;
+      // An S buffer is freed by the softmax warps after a pass-1 use (s_read) and by the P V
+      // product after a pass-2 use (s_used); per buffer: which freed it last, and how many
+      // completions each barrier has had.
+      uint32_t reads[2] = {0, 0}, useds[2] = {0, 0}, last[2] = {0, 0};
       bool ok = true;
       // S[sn & 1] = Q K^T for the kv stage of load number kn.
-      auto issue_s = [&](uint32_t kn) -> bool {
+      auto issue_s = [&](uint32_t kn, uint32_t pass) -> bool {
         const uint32_t st = kn & 1, sb = sn & 1;
         if (!wait_or_abort(kv_full + st, (kn >> 1) & 1, abort_flag)) return false;
-        if (!wait_or_abort(s_empty + sb, ((sn >> 1) & 1) ^ 1, abort_flag)) return false;
+        if (last[sb] == 1 && !wait_or_abort(s_read + sb, (reads[sb] - 1) & 1, abort_flag))
+          return false;
+        if (last[sb] == 2 && !wait_or_abort(s_used + sb, (useds[sb] - 1) & 1, abort_flag))
+          return false;
         tc::tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < DH / 8; ++ks)
           tc::mma_tf32(tmem + sb * 128, kmajor_desc(q_addr, 16384, ks),
                        kmajor_desc(k_addr + st * L::kTile, 16384, ks), idesc_s, ks > 0);
         tc::mma_commit(s_full + sb);
+        if (pass == 0) {
+          last[sb] = 1;
+          ++reads[sb];
+        } else {
+          last[sb] = 2;
+          ++useds[sb];
+        }
         ++sn;
         return true;
       };
@@ -320,28 +336,28 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
         tc::tc_fence_after();
         for (uint32_t j = 0; j < nkv && ok; ++j, ++n) {  // pass 1
-          if (!(ok = issue_s(n))) break;
+          if (!(ok = issue_s(n, 0))) break;
           tc::mma_commit(kv_empty + (n & 1));
         }
         if (!ok) break;
         // pass 2: S_{j+1} is issued before O += P_j V_j so the softmax of tile j+1 overlaps it.
-        const uint32_t n0 = n;
-        if (!(ok = issue_s(n0))) break;
+        const uint32_t n0 = n, sn0 = sn;
+        if (!(ok = issue_s(n0, 1))) break;
         for (uint32_t j = 0; j < nkv && ok; ++j) {
           if (j + 1 < nkv) {
-            if (!(ok = issue_s(n0 + j + 1))) break;
+            if (!(ok = issue_s(n0 + j + 1, 1))) break;
           }
           if (j + 1 == nkv) tc::mma_commit(q_empty);  // Q is no longer read in this item
           if (!(ok = wait_or_abort(p_full, pn & 1, abort_flag))) break;
           ++pn;
           if (j == 0 && !(ok = wait_or_abort(o_empty, (item & 1) ^ 1, abort_flag))) break;
           tc::tc_fence_after();
-          const uint32_t st = (n0 + j) & 1;
+          const uint32_t st = (n0 + j) & 1, sb = (sn0 + j) & 1;
 #pragma unroll
           for (int ks = 0; ks < 16; ++ks)
-            tc::mma_tf32(tmem + 256, kmajor_desc(p_addr, 16384, ks),
-                         mnmajor_desc<DH>(v_addr + st * L::kTile, ks), idesc_o, (j | ks) != 0);
-          tc::mma_commit(p_empty);
+            tc::mma_tf32_ts(tmem + 256, tmem + sb * 128 + ks * 8,
+                            mnmajor_desc<DH>(v_addr + st * L::kTile, ks), idesc_o, (j | ks) != 0);
+          tc::mma_commit(s_used + sb);
           tc::mma_commit(kv_empty + st);
         }
         n = n0 + nkv;
@@ -356,12 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     // Thread (r, grp) owns columns [64*grp, 64*grp + 64) of row r of every 128 x 128 score tile.
     const SoftThread th(warp, lane, tmem);
     const uint32_t r = th.r, grp = th.grp;
-    uint8_t* pbuf = smem + L::kP;
-    // Row partials are exchanged through K block 3 of the P buffer, which no MMA reads and no
-    // output staging uses at the points where the exchanges happen.
-    float* xmax = reinterpret_cast<float*>(pbuf + 3 * 16384);  // [2][128]
-    float* xsum = xmax + 256;                                   // [2][128]
-    uint32_t sn = 0, pn = 0, item = 0, xphase = 0;
+    uint8_t* stg = smem + L::kStg + (warp - 2) * 4096;
+    float* xmax = reinterpret_cast<float*>(smem + L::kX);  // [2][128]
+    float* xsum = xmax + 256;                              // [2][128]
+    uint32_t sn = 0, item = 0, xphase = 0;
     bool ok = true;
     for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
       const Item it = decode(p, idx, true);
@@ -376,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         tc::tmem_load_2x32(base, base + 32, v0, v1);
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(s_empty + (sn & 1));
+        if (lane == 0) tc::mbar_arrive(s_read + (sn & 1));
         if (j != it.t) {
 #pragma unroll
           for (int e = 0; e < 32; ++e)
@@ -394,43 +408,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       xmax[grp * 128 + r] = vmax;
       if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
       const float mx = fmaxf(xmax[r], xmax[128 + r]) * p.scale_log2;
-      if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;  // K block 3 free for P again
       float sum = 0.f;
-      if (lane == 0) tc::bulk_wait_read<0>();  // earlier output staging in the P block is read
-      __syncwarp();
       for (uint32_t j = 0; j < nkv && ok; ++j, ++sn) {  // pass 2: probabilities
         if (!(ok = wait_or_abort(s_full + (sn & 1), (sn >> 1) & 1, abort_flag))) break;
-        if (pn > 0 && !(ok = wait_or_abort(p_empty, (pn - 1) & 1, abort_flag))) break;
         tc::tc_fence_after();
         uint32_t v0[32], v1[32];
         const uint32_t base = th.lanes + (sn & 1) * 128 + grp * 64;
         tc::tmem_load_2x32(base, base + 32, v0, v1);
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(s_empty + (sn & 1));
-        float pr[32];
         const bool diag = j == it.t;
         const uint32_t c0 = grp * 64;
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          float pe = ex2(fmaf(__uint_as_float(v0[e]), p.scale_log2, -mx));
-          if (diag && c0 + e > r) pe = 0.f;
-          sum += pe;
-          pr[e] = round_tf32(pe);  // the P V operand, rounded to nearest instead of truncated
+          float p0 = ex2(fmaf(__uint_as_float(v0[e]), p.scale_log2, -mx));
+          float p1 = ex2(fmaf(__uint_as_float(v1[e]), p.scale_log2, -mx));
+          if (diag && c0 + e > r) p0 = 0.f;
+          if (diag && c0 + 32 + e > r) p1 = 0.f;
+          sum += p0 + p1;
+          // The P V operand, rounded to nearest instead of truncated.
+          v0[e] = __float_as_uint(round_tf32(p0));
+          v1[e] = __float_as_uint(round_tf32(p1));
         }
-        store_row32(pbuf + (2 * grp) * 16384, r, pr);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float pe = ex2(fmaf(__uint_as_float(v1[e]), p.scale_log2, -mx));
-          if (diag && c0 + 32 + e > r) pe = 0.f;
-          sum += pe;
-          pr[e] = round_tf32(pe);
-        }
-        store_row32(pbuf + (2 * grp + 1) * 16384, r, pr);
-        tc::fence_proxy_async_smem();
+        tc::tmem_store_2x32(base, base + 32, v0, v1);  // P over S: the A operand of O += P V
+        tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(p_full);
-        ++pn;
       }
       if (!ok) break;
       if (!(ok = wait_or_abort(o_full, item & 1, abort_flag))) break;
@@ -444,9 +445,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         float o[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]) * inv;
-        // This warp's rows of K block grp of the (now idle) P buffer serve as its staging box.
-        store_box(&p.out, pbuf + grp * 16384 + th.quarter * 4096, o,
-                  static_cast<int>(it.h * DH + 32 * grp),
+        if (lane == 0) tc::bulk_wait_read<0>();  // this warp's staging box is free again
+        __syncwarp();
+        store_box(&p.out, stg, o, static_cast<int>(it.h * DH + 32 * grp),
                   static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
         if (lane == 0) tc::bulk_commit();
       }
