@@ -40,8 +40,10 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
-constexpr uint32_t kEpiBytes = 4 * 2 * 4096;  // epilogue staging: 4 warps x 2 boxes x 4 KB
+// Threads: producer warp, MMA warp, EW epilogue warps (4: one per TMEM lane quarter; 8: two per
+// quarter, splitting each tile's columns, for epilogues with real per-element work).
+__host__ __device__ constexpr int threads_for(int ew) { return 64 + 32 * ew; }
+__host__ __device__ constexpr uint32_t epi_bytes(int ew) { return ew * 2 * 4096; }  // 2 staging boxes of 4 KB per warp
 
 struct GemmParams {
   CUtensorMap a_map[3];
@@ -175,9 +177,22 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
   for (int e = 0; e < 32; ++e) v[e] *= p.alpha;
   if (p.bias && (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU ||
                  p.epilogue == SPAR_B200_EPI_BIAS_ADD)) {
+    if (col0 + 32 <= p.n && (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0) {
+      // Same 32 values for every lane: eight broadcast 16-byte loads.
+      const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
 #pragma unroll
-    for (int e = 0; e < 32; ++e)
-      if (col0 + e < p.n) v[e] += __ldg(p.bias + col0 + e);
+      for (int i = 0; i < 8; ++i) {
+        const float4 b = __ldg(b4 + i);
+        v[4 * i] += b.x;
+        v[4 * i + 1] += b.y;
+        v[4 * i + 2] += b.z;
+        v[4 * i + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (col0 + e < p.n) v[e] += __ldg(p.bias + col0 + e);
+    }
   }
   if (needs_aux) {
     if (!tc::mbar_wait(st.aux_bar + st.sel, st.aux_phase[st.sel])) {
@@ -207,9 +222,12 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
   if (p.rope && col0 < p.rope_cols) {  // RoPE on this row's 16 column pairs
     const uint32_t pos = (row0 + lane) % p.rope_seq;
     const float2* tab = p.rope + static_cast<uint64_t>(pos) * p.rope_half;
+    const uint32_t pair0 = (col0 % p.rope_dim) / 2;
+    const bool one_head = pair0 + 16 <= p.rope_half;  // the box does not cross a head boundary
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float2 cs = __ldg(tab + ((col0 + 2 * i) % p.rope_dim) / 2);
+      const uint32_t pair = one_head ? pair0 + i : ((col0 + 2 * i) % p.rope_dim) / 2;
+      const float2 cs = __ldg(tab + pair);
       const float x0 = v[2 * i], x1 = v[2 * i + 1];
       v[2 * i] = x0 * cs.x - x1 * cs.y;
       v[2 * i + 1] = x0 * cs.y + x1 * cs.x;
@@ -239,8 +257,10 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
 // adds. The tensor cores' own accumulation rounds toward zero, so long hardware-accumulated
 // sums drift; chunking bounds that drift to one chunk, which keeps the split mode fp32-faithful
 // at any K.
-template <int BN, int STAGES, bool CHUNKED>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_constant__ GemmParams p) {
+template <int BN, int STAGES, bool CHUNKED, int EW>
+__global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __grid_constant__ GemmParams p) {
+  static_assert(EW == 4 || (EW == 8 && !CHUNKED), "epilogue warps");
+  constexpr uint32_t kEpiBytes = epi_bytes(EW);
   constexpr uint32_t A_BYTES = BM * BK * 4;
   constexpr uint32_t B_BYTES = BN * BK * 4;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -248,14 +268,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;  // 4 warps x 2 staging boxes x 4 KB
+  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;  // EW warps x 2 staging boxes x 4 KB
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + kEpiBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_bars = drain + 1;  // 4 warps x 2
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 8);
+  uint64_t* aux_bars = drain + 1;  // EW warps x 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 2 * EW);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -268,10 +288,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(tfull + b, 1);
-      tc::mbar_init(tempty + b, 4);
+      tc::mbar_init(tempty + b, EW);
     }
     tc::mbar_init(drain, 1);
-    for (int b = 0; b < 8; ++b) tc::mbar_init(aux_bars + b, 1);
+    for (int b = 0; b < 2 * EW; ++b) tc::mbar_init(aux_bars + b, 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -413,11 +433,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------------ epilogue (warps 2..)
     const uint32_t quarter = static_cast<uint32_t>(warp & 3);
+    const uint32_t ew = static_cast<uint32_t>(warp - 2);
+    constexpr int kChunks = BN / 32 / (EW / 4);  // 32-column boxes per warp and tile
+    const int chunk0 = static_cast<int>(ew / 4) * kChunks;
     EpiState st;
-    st.bufs = epi_smem + quarter * 8192;
-    st.aux_bar = aux_bars + quarter * 2;
+    st.bufs = epi_smem + ew * 8192;
+    st.aux_bar = aux_bars + ew * 2;
     st.aux_phase[0] = st.aux_phase[1] = 0;
     st.sel = 0;
     bool ok = true;
@@ -436,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tf32_kernel(const __grid_con
         }
         tc::tc_fence_after();
 #pragma unroll 1
-        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        for (int chunk = chunk0; chunk < chunk0 + kChunks; ++chunk) {
           const uint32_t col0 = t.nt * BN + chunk * 32;
           uint32_t r[32];
           tc::tmem_load_32x32(lane_base + acc * BN + chunk * 32, r);
@@ -606,11 +629,12 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows
 
 namespace {
 
-template <int BN, int STAGES, bool CHUNKED>
+template <int BN, int STAGES, bool CHUNKED, int EW = 4>
 cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) {
-  constexpr size_t smem = STAGES * (BM * BK * 4 + BN * BK * 4) + kEpiBytes + 1024 + 256;
+  constexpr size_t smem = STAGES * (BM * BK * 4 + BN * BK * 4) + epi_bytes(EW) + 1024 + 256;
+  static_assert(smem <= 232448, "GEMM shared memory");
   static bool configured[64] = {false};
-  auto k = gemm_tf32_kernel<BN, STAGES, CHUNKED>;
+  auto k = gemm_tf32_kernel<BN, STAGES, CHUNKED, EW>;
   if (device < 0 || device >= 64 || !configured[device]) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -618,7 +642,7 @@ cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) 
     if (device >= 0 && device < 64) configured[device] = true;
   }
   const unsigned grid = std::min<uint32_t>(p.total_tiles, static_cast<uint32_t>(sm_count(device)));
-  k<<<grid, kThreads, smem, stream>>>(p);
+  k<<<grid, threads_for(EW), smem, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -765,6 +789,20 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     return cudaGetLastError();
   }
   if (split) return launch_kernel<64, 8, true>(p, device, stream);
+  // Epilogues with per-element work beyond a bias add (GELU, GELU', residual / aux tiles, RoPE)
+  // get eight epilogue warps (one fewer operand stage makes room for their staging boxes).
+  const bool heavy = g.epilogue == SPAR_B200_EPI_BIAS_GELU || g.epilogue == SPAR_B200_EPI_GELU_BWD ||
+                     g.epilogue == SPAR_B200_EPI_BIAS_ADD || g.rope_table;
+  if (heavy) {
+    switch (bn) {
+      case 256:
+        return launch_kernel<256, 3, false, 8>(p, device, stream);
+      case 128:
+        return launch_kernel<128, 5, false, 8>(p, device, stream);
+      default:
+        return launch_kernel<64, 6, false, 8>(p, device, stream);
+    }
+  }
   switch (bn) {
     case 256:
       return launch_kernel<256, 4, false>(p, device, stream);

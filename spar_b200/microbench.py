@@ -139,6 +139,7 @@ def main():
     ap.add_argument("--x3", action="store_true")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--epi", default="none", choices=sorted(EPILOGUES))
+    ap.add_argument("--batch", type=int, default=16, help="attention: sequences (C5: 16)")
     a = ap.parse_args()
     if a.kernel == "gemm":
         run_gemm(a.m, a.n, a.k, a.at, a.bt, a.x3, a.iters, a.epi)
@@ -152,7 +153,7 @@ def main():
         for name in ("layernorm_bwd", "gelu_bwd", "softmax_bwd", "cross_entropy", "adamw"):
             run_bandwidth(name, a.iters)
     elif a.kernel == "attention":
-        run_attention(iters=a.iters)
+        run_attention(b=a.batch, iters=a.iters)
     else:
         run_bandwidth(a.kernel, a.iters)
 
