@@ -113,14 +113,9 @@ class ClockSampler:
 def make_ids(step: int, rank: int, world: int, seq: int, vocab: int):
     """Global batch of GLOBAL_SEQS sequences for optimiser step `step` (Spar Random stream,
     bounded_index sampling); this rank's contiguous share as [ACCUM, micro_batch, seq]."""
-    import numpy as np
+    from spar_b200.data import rank_share
 
-    from spar_b200.data import token_ids
-
-    ids = token_ids(SEED_IDS + step, GLOBAL_SEQS * seq, vocab).reshape(GLOBAL_SEQS, seq)
-    per = GLOBAL_SEQS // world
-    mine = ids[rank * per:(rank + 1) * per]
-    return np.ascontiguousarray(mine.reshape(ACCUM, per // ACCUM, seq).astype(np.int32))
+    return rank_share(SEED_IDS + step, GLOBAL_SEQS, ACCUM, seq, vocab, rank, world)
 
 
 def cpu_baseline_sample(cfg, seconds_budget=20.0, processes=1):

@@ -304,6 +304,19 @@ struct SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* ids, 
                                               double* grad_norm_out, int32_t* flags_out,
                                               void* stream);
 struct SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int world_size);
+/* Host-only queries of the parameter-arena layout a config produces (no device work, usable   */
+/* without a GPU): flat size in floats, the named tensors (Spar's names, offset into the arena, */
+/* rows x cols with row stride ld; cols == 0 for vectors) and the gradient all-reduce buckets    */
+/* (offset, count) in the order a data-parallel step issues them (last block first, then the    */
+/* tied embedding and the final norm). The buckets tile [0, flat).                              */
+struct SparCudaStatus spar_b200_lm_layout(const struct SparB200LMConfig* config, uint64_t* flat_size,
+                                          uint64_t* num_tensors, uint64_t* num_buckets);
+struct SparCudaStatus spar_b200_lm_layout_tensor(const struct SparB200LMConfig* config,
+                                                 uint64_t index, char* name, uint64_t name_capacity,
+                                                 uint64_t* offset, uint64_t* rows, uint64_t* cols,
+                                                 uint64_t* ld);
+struct SparCudaStatus spar_b200_lm_layout_bucket(const struct SparB200LMConfig* config,
+                                                 uint64_t index, uint64_t* offset, uint64_t* count);
 struct SparCudaStatus spar_b200_lm_read_losses(void* handle, float* host, uint64_t count);
 /* Event timing of every tensor-core GEMM launch (for roofline accounting) and a kernel-launch */
 /* counter; profile_read synchronises the device.                                              */

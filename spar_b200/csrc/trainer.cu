@@ -88,6 +88,83 @@ struct LayerActs {
 
 }  // namespace
 
+// Host-only layout of the parameter arena (no device work): Spar's named_parameters order, every
+// tensor 256-byte aligned, fused [d, 3d] QKV. Shared by the runtime and the layout queries.
+struct ParamLayout {
+  uint64_t flat = 0, off_E = 0, off_lnf_g = 0, off_lnf_b = 0;
+  std::vector<NamedTensor> named;
+  std::vector<LayerOffsets> lay;
+  // Gradient all-reduce buckets in the order the data-parallel step issues them: blocks from last
+  // to first (each block's range as soon as its backward finishes), then the tied embedding and
+  // the final norm. Together they tile [0, flat).
+  std::vector<std::pair<uint64_t, uint64_t>> buckets() const {
+    std::vector<std::pair<uint64_t, uint64_t>> b;
+    for (size_t l = lay.size(); l-- > 0;) b.push_back({lay[l].begin, lay[l].end - lay[l].begin});
+    b.push_back({off_E, lay[0].begin - off_E});
+    b.push_back({off_lnf_g, flat - off_lnf_g});
+    return b;
+  }
+};
+
+SparCudaStatus plan_params(const SparB200LMConfig& c, ParamLayout& pl) {
+  const uint64_t V = c.vocab_size, d = c.model_dim, F = c.hidden_dim, L = c.num_layers,
+                 H = c.num_heads, T = c.sequence_length, B = c.micro_batch;
+  if (V == 0 || d == 0 || F == 0 || L == 0 || H == 0 || T < 2 || B == 0 || d % H != 0)
+    return invalid();
+  const uint64_t dh = d / H;
+  if (d % 32 != 0 || F % 4 != 0 || dh % 32 != 0 || T % 4 != 0) return invalid();
+  if (c.precision != SPAR_B200_TF32 && c.precision != SPAR_B200_TF32X3) return invalid();
+  // ---- parameter arena in Spar's named_parameters order (src/nn/parameters.cpp:51-132)
+  uint64_t o = 0;
+  auto take = [&](uint64_t n) {
+    const uint64_t at = o;
+    o = align_up(o + n);
+    return at;
+  };
+  pl.off_E = take(V * d);
+  pl.named.push_back({"token_embedding.weight", pl.off_E, V, d, d, true});
+  for (uint64_t l = 0; l < L; ++l) {
+    LayerOffsets lo{};
+    lo.begin = o;
+    lo.ln1_g = take(d);
+    lo.ln1_b = take(d);
+    lo.wqkv = take(d * 3 * d);
+    lo.bqkv = take(3 * d);
+    lo.wo = take(d * d);
+    lo.bo = take(d);
+    lo.ln2_g = take(d);
+    lo.ln2_b = take(d);
+    lo.w1 = take(d * F);
+    lo.b1 = take(F);
+    lo.w2 = take(F * d);
+    lo.b2 = take(d);
+    lo.end = o;
+    pl.lay.push_back(lo);
+    const std::string p = "blocks." + std::to_string(l) + ".";
+    pl.named.push_back({p + "attention_norm.weight", lo.ln1_g, d, 0, 0, false});
+    pl.named.push_back({p + "attention_norm.bias", lo.ln1_b, d, 0, 0, false});
+    const char* proj[3] = {"q_proj", "k_proj", "v_proj"};
+    for (int j = 0; j < 3; ++j) {
+      pl.named.push_back({p + "attention." + proj[j] + ".weight", lo.wqkv + j * d, d, d, 3 * d, true});
+      pl.named.push_back({p + "attention." + proj[j] + ".bias", lo.bqkv + j * d, d, 0, 0, false});
+    }
+    pl.named.push_back({p + "attention.out_proj.weight", lo.wo, d, d, d, true});
+    pl.named.push_back({p + "attention.out_proj.bias", lo.bo, d, 0, 0, false});
+    pl.named.push_back({p + "mlp_norm.weight", lo.ln2_g, d, 0, 0, false});
+    pl.named.push_back({p + "mlp_norm.bias", lo.ln2_b, d, 0, 0, false});
+    pl.named.push_back({p + "mlp.up_proj.weight", lo.w1, d, F, F, true});
+    pl.named.push_back({p + "mlp.up_proj.bias", lo.b1, F, 0, 0, false});
+    pl.named.push_back({p + "mlp.down_proj.weight", lo.w2, F, d, d, true});
+    pl.named.push_back({p + "mlp.down_proj.bias", lo.b2, d, 0, 0, false});
+  }
+  pl.off_lnf_g = take(d);
+  pl.off_lnf_b = take(d);
+  pl.named.push_back({"final_norm.weight", pl.off_lnf_g, d, 0, 0, false});
+  pl.named.push_back({"final_norm.bias", pl.off_lnf_b, d, 0, 0, false});
+  pl.flat = o;
+  return ok();
+}
+
 #define SPAR_TRY_RAW(expr)              \
   do {                                  \
     const cudaError_t e_ = (expr);      \
@@ -103,6 +180,7 @@ class LMTrainer {
   std::vector<NamedTensor> named;
   std::vector<LayerOffsets> lay;
   uint64_t off_E = 0, off_lnf_g = 0, off_lnf_b = 0;
+  std::vector<std::pair<uint64_t, uint64_t>> buckets;  // all-reduce buckets in issue order
   float *params = nullptr, *grads = nullptr, *m1 = nullptr, *m2 = nullptr;
   // activations
   char* act_base = nullptr;
@@ -180,54 +258,16 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   if (d % 32 != 0 || F % 4 != 0 || dh % 32 != 0 || T % 4 != 0) return invalid();
   if (c.precision != SPAR_B200_TF32 && c.precision != SPAR_B200_TF32X3) return invalid();
 
-  // ---- parameter arena in Spar's named_parameters order (src/nn/parameters.cpp:51-132)
-  uint64_t o = 0;
-  auto take = [&](uint64_t n) {
-    const uint64_t at = o;
-    o = align_up(o + n);
-    return at;
-  };
-  off_E = take(V * d);
-  named.push_back({"token_embedding.weight", off_E, V, d, d, true});
-  for (uint64_t l = 0; l < L; ++l) {
-    LayerOffsets lo{};
-    lo.begin = o;
-    lo.ln1_g = take(d);
-    lo.ln1_b = take(d);
-    lo.wqkv = take(d * 3 * d);
-    lo.bqkv = take(3 * d);
-    lo.wo = take(d * d);
-    lo.bo = take(d);
-    lo.ln2_g = take(d);
-    lo.ln2_b = take(d);
-    lo.w1 = take(d * F);
-    lo.b1 = take(F);
-    lo.w2 = take(F * d);
-    lo.b2 = take(d);
-    lo.end = o;
-    lay.push_back(lo);
-    const std::string p = "blocks." + std::to_string(l) + ".";
-    named.push_back({p + "attention_norm.weight", lo.ln1_g, d, 0, 0, false});
-    named.push_back({p + "attention_norm.bias", lo.ln1_b, d, 0, 0, false});
-    const char* proj[3] = {"q_proj", "k_proj", "v_proj"};
-    for (int j = 0; j < 3; ++j) {
-      named.push_back({p + "attention." + proj[j] + ".weight", lo.wqkv + j * d, d, d, 3 * d, true});
-      named.push_back({p + "attention." + proj[j] + ".bias", lo.bqkv + j * d, d, 0, 0, false});
-    }
-    named.push_back({p + "attention.out_proj.weight", lo.wo, d, d, d, true});
-    named.push_back({p + "attention.out_proj.bias", lo.bo, d, 0, 0, false});
-    named.push_back({p + "mlp_norm.weight", lo.ln2_g, d, 0, 0, false});
-    named.push_back({p + "mlp_norm.bias", lo.ln2_b, d, 0, 0, false});
-    named.push_back({p + "mlp.up_proj.weight", lo.w1, d, F, F, true});
-    named.push_back({p + "mlp.up_proj.bias", lo.b1, F, 0, 0, false});
-    named.push_back({p + "mlp.down_proj.weight", lo.w2, F, d, d, true});
-    named.push_back({p + "mlp.down_proj.bias", lo.b2, d, 0, 0, false});
-  }
-  off_lnf_g = take(d);
-  off_lnf_b = take(d);
-  named.push_back({"final_norm.weight", off_lnf_g, d, 0, 0, false});
-  named.push_back({"final_norm.bias", off_lnf_b, d, 0, 0, false});
-  flat = o;
+  ParamLayout pl;
+  const SparCudaStatus ls = plan_params(c, pl);
+  if (ls.code) return ls;
+  flat = pl.flat;
+  off_E = pl.off_E;
+  off_lnf_g = pl.off_lnf_g;
+  off_lnf_b = pl.off_lnf_b;
+  buckets = pl.buckets();
+  named = std::move(pl.named);
+  lay = std::move(pl.lay);
 
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
@@ -488,8 +528,8 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
     // Tied embedding and final norm (first and last gradients of the sweep), then join.
     SPAR_CHECK(cudaEventRecord(tail_ev, s));
     SPAR_CHECK(cudaStreamWaitEvent(comm_stream, tail_ev, 0));
-    SPAR_CHECK(comm_allreduce_sum(comm, G + off_E, lay[0].begin - off_E, comm_stream));
-    SPAR_CHECK(comm_allreduce_sum(comm, G + off_lnf_g, flat - off_lnf_g, comm_stream));
+    for (size_t i = L; i < buckets.size(); ++i)
+      SPAR_CHECK(comm_allreduce_sum(comm, G + buckets[i].first, buckets[i].second, comm_stream));
     SPAR_CHECK(cudaEventRecord(comm_done, comm_stream));
     SPAR_CHECK(cudaStreamWaitEvent(s, comm_done, 0));
   }
@@ -577,7 +617,8 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
     // remaining layers run backward (bucket = one block's contiguous parameter range).
     SPAR_TRY(cudaEventRecord(layer_ev[l], s));
     SPAR_TRY(cudaStreamWaitEvent(comm_stream, layer_ev[l], 0));
-    SPAR_TRY(comm_allreduce_sum(comm, G + lo.begin, lo.end - lo.begin, comm_stream));
+    const auto& bk = buckets[L - 1 - l];  // == [lo.begin, lo.end)
+    SPAR_TRY(comm_allreduce_sum(comm, G + bk.first, bk.second, comm_stream));
   }
   return cudaSuccess;
 }
@@ -859,5 +900,50 @@ extern "C" SparCudaStatus spar_b200_lm_profile_read(void* handle, double* gemm_m
   if (gemm_flops) *gemm_flops = fl;
   if (gemm_launches) *gemm_launches = t->ev_used;
   if (kernel_launches) *kernel_launches = t->launches;
+  return ok();
+}
+
+// ------------------------------------------------------------ host-only layout queries (no GPU)
+extern "C" SparCudaStatus spar_b200_lm_layout(const SparB200LMConfig* config, uint64_t* flat_size,
+                                              uint64_t* num_tensors, uint64_t* num_buckets) {
+  if (!config) return invalid();
+  ParamLayout pl;
+  const SparCudaStatus st = plan_params(*config, pl);
+  if (st.code) return st;
+  if (flat_size) *flat_size = pl.flat;
+  if (num_tensors) *num_tensors = pl.named.size();
+  if (num_buckets) *num_buckets = pl.buckets().size();
+  return ok();
+}
+
+extern "C" SparCudaStatus spar_b200_lm_layout_tensor(const SparB200LMConfig* config, uint64_t index,
+                                                     char* name, uint64_t name_capacity,
+                                                     uint64_t* offset, uint64_t* rows,
+                                                     uint64_t* cols, uint64_t* ld) {
+  if (!config || !name || name_capacity == 0) return invalid();
+  ParamLayout pl;
+  const SparCudaStatus st = plan_params(*config, pl);
+  if (st.code) return st;
+  if (index >= pl.named.size()) return invalid();
+  const NamedTensor& t = pl.named[index];
+  if (t.name.size() + 1 > name_capacity) return invalid();
+  memcpy(name, t.name.c_str(), t.name.size() + 1);
+  if (offset) *offset = t.offset;
+  if (rows) *rows = t.rows;
+  if (cols) *cols = t.cols;
+  if (ld) *ld = t.ld;
+  return ok();
+}
+
+extern "C" SparCudaStatus spar_b200_lm_layout_bucket(const SparB200LMConfig* config, uint64_t index,
+                                                     uint64_t* offset, uint64_t* count) {
+  if (!config || !offset || !count) return invalid();
+  ParamLayout pl;
+  const SparCudaStatus st = plan_params(*config, pl);
+  if (st.code) return st;
+  const auto b = pl.buckets();
+  if (index >= b.size()) return invalid();
+  *offset = b[index].first;
+  *count = b[index].second;
   return ok();
 }

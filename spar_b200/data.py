@@ -43,3 +43,17 @@ def token_ids(seed: int, count: int, vocab: int) -> np.ndarray:
             accepted = np.nonzero(v >= threshold)[0] if threshold else np.arange(len(v))
             pos = pos - len(v) + int(accepted[take - 1]) + 1
     return out
+
+
+def rank_share(seed: int, global_seqs: int, accum: int, seq: int, vocab: int, rank: int,
+               world: int) -> np.ndarray:
+    """Data-parallel share of one optimiser step's global batch: `global_seqs` sequences of `seq`
+    ids drawn from one stream, rank r taking the contiguous sequences [r*per, (r+1)*per) with
+    per = global_seqs / world, as int32 [accum, per / accum, seq] micro-steps. Every rank draws
+    the same global batch, so the shares partition it without any communication."""
+    if global_seqs % world or (global_seqs // world) % accum:
+        raise ValueError("global batch must split evenly over ranks and micro-steps")
+    ids = token_ids(seed, global_seqs * seq, vocab).reshape(global_seqs, seq)
+    per = global_seqs // world
+    mine = ids[rank * per:(rank + 1) * per]
+    return np.ascontiguousarray(mine.reshape(accum, per // accum, seq).astype(np.int32))

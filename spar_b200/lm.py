@@ -54,6 +54,14 @@ class LMConfig:
         return 6.0 * n_mm + 12.0 * self.layers * self.dim * self.seq
 
 
+def native_config(cfg: LMConfig) -> SparB200LMConfig:
+    """The C-ABI config struct of a model config."""
+    return SparB200LMConfig(cfg.vocab, cfg.dim, cfg.hidden, cfg.layers, cfg.heads, cfg.seq,
+                            cfg.micro_batch, cfg.eps, cfg.rope_theta, int(cfg.use_rope),
+                            cfg.precision, cfg.beta1, cfg.beta2, cfg.adam_eps, cfg.weight_decay,
+                            cfg.max_grad_norm)
+
+
 class DecoderLM:
     """One decoder + optimiser state resident on one GPU."""
 
@@ -61,10 +69,7 @@ class DecoderLM:
         self.cfg = cfg
         self.device = device
         self.lib = _lib.load()
-        c = SparB200LMConfig(cfg.vocab, cfg.dim, cfg.hidden, cfg.layers, cfg.heads, cfg.seq,
-                             cfg.micro_batch, cfg.eps, cfg.rope_theta, int(cfg.use_rope),
-                             cfg.precision, cfg.beta1, cfg.beta2, cfg.adam_eps, cfg.weight_decay,
-                             cfg.max_grad_norm)
+        c = native_config(cfg)
         h = ctypes.c_void_p()
         check("spar_b200_lm_create", self.lib.spar_b200_lm_create(ctypes.byref(c), device,
                                                                   ctypes.byref(h)))
