@@ -529,6 +529,245 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
   if (warp == 1) tc::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// ----------------------------------------------------------------- paired-SM GEMM
+// A cluster of two CTAs on two SMs computes one 256 x 256 tile with tcgen05.mma.cta_group::2:
+// CTA r loads rows [128r, 128r + 128) of the A tile and rows [128r, 128r + 128) of the B tile's
+// N extent into its own shared memory, and its TMEM receives its 128 rows of the 256 x 256
+// accumulator. Per FLOP this moves a third fewer operand bytes from L2 than two independent
+// 128 x 256 tiles, and each stage is 32 KB instead of 48 KB, so more stages fit.
+// Roles (both CTAs): warp 0 TMA producer into its own shared memory, completing on the even CTA's
+// "full" barrier (armed by the even CTA for both CTAs' bytes); warp 1 of the even CTA issues every
+// MMA; warps 2.. epilogue of the CTA's own rows.
+// Completions: the MMA commits each stage's "empty" and each accumulator's "full" to the barrier
+// of the same name in both CTAs (two plain commits); both CTAs' epilogue warps arrive on the even
+// CTA's accumulator-empty barrier. Every wait is bounded; the closing cluster barrier keeps each
+// CTA (and its shared memory) alive until the even CTA has drained or given up.
+template <int STAGES, int EW>
+__global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+  constexpr int BN = 256;    // tile N, both CTAs
+  constexpr int BNH = 128;   // B rows (N) staged by each CTA
+  constexpr uint32_t A_BYTES = BM * BK * 4;
+  constexpr uint32_t B_BYTES = BNH * BK * 4;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t kEpiBytes = epi_bytes(EW);
+  constexpr uint32_t TMEM_COLS = 512;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + kEpiBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* aux_bars = drain + 1;  // EW warps x 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bars + 2 * EW);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(full + s, 1);  // even CTA: armed by its producer with both CTAs' bytes
+      tc::mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(tfull + b, 1);
+      tc::mbar_init(tempty + b, 2 * EW);  // epilogue warps of both CTAs (even CTA's barrier)
+    }
+    tc::mbar_init(drain, 1);
+    for (int b = 0; b < 2 * EW; ++b) tc::mbar_init(aux_bars + b, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tc::tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::tma_prefetch(&p.a_map[0]);
+    tc::tma_prefetch(&p.b_map[0]);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrival
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (tc::elect_one()) {
+      uint32_t stage = 0, phase = 0;
+      int last_phase[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
+      for (uint32_t idx = cluster; idx < p.total_tiles && !*abort_flag; idx += nclusters) {
+        TileCoord t;
+        if (!decode_tile<BN>(p, idx, t)) continue;
+        uint32_t kb0, kb1;
+        k_range(p, t, kb0, kb1);
+        const int m0 = static_cast<int>(t.mt * 256 + rank * BM);
+        const int n0 = static_cast<int>(t.nt * BN + rank * BNH);
+        for (uint32_t kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
+          const int k0 = static_cast<int>(kb * BK);
+          if (!tc::mbar_wait_cluster(empty + stage, phase ^ 1)) {
+            record_error();
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* a_s = smem + stage * STAGE_BYTES;
+          uint8_t* b_s = a_s + A_BYTES;
+          const uint32_t fb = tc::map_to_rank(tc::smem_u32(full + stage), 0);
+          if (leader) {
+            tc::mbar_arrive_expect_tx(full + stage, 2 * STAGE_BYTES);
+            last_phase[stage] = static_cast<int>(phase);
+          }
+          if (p.a_mn_major) {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j)
+              tc::tma_load_4d_pair(a_s + j * 4096, &p.a_map[0], fb, m0 + 32 * j, k0, 0, 0);
+          } else {
+            tc::tma_load_4d_pair(a_s, &p.a_map[0], fb, k0, m0, 0, 0);
+          }
+          if (p.b_mn_major) {
+#pragma unroll
+            for (int j = 0; j < BNH / 32; ++j)
+              tc::tma_load_4d_pair(b_s + j * 4096, &p.b_map[0], fb, n0 + 32 * j, k0, 0, 0);
+          } else {
+            tc::tma_load_4d_pair(b_s, &p.b_map[0], fb, k0, n0, 0, 0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Every armed stage (both CTAs' bytes) must have landed before the pair exits.
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s)
+        if (last_phase[s] >= 0 && !tc::mbar_wait_cluster(full + s, static_cast<uint32_t>(last_phase[s])))
+          record_error();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA;
+    // warp 1 of the odd CTA has no role after the TMEM allocation)
+    const uint32_t idesc = tc::idesc_tf32(256, BN, p.a_mn_major, p.b_mn_major);
+    if (leader && tc::elect_one()) {
+      const uint32_t peer = 1;
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      for (uint32_t idx = cluster; idx < p.total_tiles && !*abort_flag; idx += nclusters) {
+        TileCoord t;
+        if (!decode_tile<BN>(p, idx, t)) continue;
+        uint32_t kb0, kb1;
+        k_range(p, t, kb0, kb1);
+        if (!tc::mbar_wait_cluster(tempty + acc, acc_phase ^ 1)) {
+          record_error();
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (uint32_t kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
+          if (!tc::mbar_wait_cluster(full + stage, phase)) {
+            record_error();
+            *abort_flag = 1;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t a_addr = tc::smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < BK / 8; ++ks) {
+            const uint64_t a_desc =
+                p.a_mn_major ? tc::smem_desc(a_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                             : tc::smem_desc(a_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
+            const uint64_t b_desc =
+                p.b_mn_major ? tc::smem_desc(b_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                             : tc::smem_desc(b_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
+            tc::mma_tf32_pair(d_tmem, a_desc, b_desc, idesc, (kb != kb0 || ks != 0) ? 1u : 0u);
+          }
+          const uint32_t e = tc::smem_u32(empty + stage);
+          tc::mma_commit_pair(e);
+          tc::mma_commit_pair(tc::map_to_rank(e, peer));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        const uint32_t f = tc::smem_u32(tfull + acc);
+        tc::mma_commit_pair(f);
+        tc::mma_commit_pair(tc::map_to_rank(f, peer));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      tc::mma_commit_pair(tc::smem_u32(drain));
+      if (!tc::mbar_wait(drain, 0)) record_error();
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..)
+    const uint32_t quarter = static_cast<uint32_t>(warp & 3);
+    const uint32_t ew = static_cast<uint32_t>(warp - 2);
+    constexpr int kChunks = BN / 32 / (EW / 4);
+    const int chunk0 = static_cast<int>(ew / 4) * kChunks;
+    EpiState st;
+    st.bufs = epi_smem + ew * 8192;
+    st.aux_bar = aux_bars + ew * 2;
+    st.aux_phase[0] = st.aux_phase[1] = 0;
+    st.sel = 0;
+    bool ok = true;
+    uint32_t acc = 0, acc_phase = 0;
+    const uint32_t tempty_leader = tc::map_to_rank(tc::smem_u32(tempty), 0);
+    for (uint32_t idx = cluster; idx < p.total_tiles && ok; idx += nclusters) {
+      TileCoord t;
+      if (!decode_tile<BN>(p, idx, t)) continue;
+      if (*abort_flag) break;
+      const uint32_t row0 = t.mt * 256 + rank * BM + quarter * 32;
+      const uint32_t lane_base = tmem_base + ((quarter * 32) << 16);
+      if (!tc::mbar_wait_cluster(tfull + acc, acc_phase)) {
+        record_error();
+        *abort_flag = 1;
+        break;
+      }
+      tc::tc_fence_after();
+#pragma unroll 1
+      for (int chunk = chunk0; chunk < chunk0 + kChunks; ++chunk) {
+        const uint32_t col0 = t.nt * BN + chunk * 32;
+        uint32_t r[32];
+        tc::tmem_load_32x32(lane_base + acc * BN + chunk * 32, r);
+        if (col0 >= p.n) continue;
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+        epilogue_box(p, st, v, col0, row0, t.b1, t.b0, t.ks, ok);
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(tempty_leader + acc * 8);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (!ok) *abort_flag = 1;
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // the pair's MMAs and both epilogues are done with TMEM
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
 // ----------------------------------------------------------------- 3xTF32 operand split
 // Both halves are rounded to nearest TF32 (round_tf32), so the tensor cores see exact TF32
 // values and the split error is unbiased: hi = rn(x), lo = rn(x - hi).
@@ -646,6 +885,40 @@ cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) 
   return cudaGetLastError();
 }
 
+// Paired-SM launch: clusters of two CTAs, at most as many clusters as fit at once.
+template <int STAGES, int EW>
+cudaError_t launch_pair(const GemmParams& p, int device, cudaStream_t stream) {
+  constexpr size_t smem = STAGES * (BM * BK * 4 + 128 * BK * 4) + epi_bytes(EW) + 1024 + 256;
+  static_assert(smem <= 232448, "paired GEMM shared memory");
+  static int max_clusters[64] = {0};
+  auto k = gemm_pair_kernel<STAGES, EW>;
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(threads_for(EW));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!max_clusters[device]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(2 * (sm_count(device) / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, k, &cfg);
+    if (e != cudaSuccess) return e;
+    max_clusters[device] = n > 0 ? n : 1;
+  }
+  const uint32_t clusters = std::min<uint32_t>(p.total_tiles, static_cast<uint32_t>(max_clusters[device]));
+  cfg.gridDim = dim3(2 * clusters);
+  return cudaLaunchKernelEx(&cfg, k, p);
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -703,8 +976,12 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
 
   const uint64_t a_inner = g.a_transposed ? g.m : g.k, a_rows = g.a_transposed ? g.k : g.m;
   const uint64_t b_inner = g.b_transposed ? g.k : g.n, b_rows = g.b_transposed ? g.n : g.k;
+  // Wide unbatched TF32 products run on SM pairs (256 x 256 tiles); split-K, batched, causal
+  // and 3xTF32 products keep the single-SM kernel.
+  const bool pair = !split && b0 * b1 == 1 && g.causal == SPAR_B200_CAUSAL_NONE && bn == 256 &&
+                    g.m >= 256 && splitk_parts(g, bn, sm_count(device)) == 1;
   const uint32_t a_box_rows = p.a_mn_major ? BK : BM;
-  const uint32_t b_box_rows = p.b_mn_major ? BK : static_cast<uint32_t>(bn);
+  const uint32_t b_box_rows = p.b_mn_major ? BK : (pair ? 128u : static_cast<uint32_t>(bn));
 
   if (!split) {
     if (!make_map(&p.a_map[0], g.a, a_inner, a_rows, b1, b0, g.lda, g.a_batch_stride[1],
@@ -746,7 +1023,7 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   p.n = static_cast<uint32_t>(g.n);
   p.k = static_cast<uint32_t>(g.k);
   p.batch1 = static_cast<uint32_t>(b1);
-  p.tiles_m = static_cast<uint32_t>((g.m + BM - 1) / BM);
+  p.tiles_m = static_cast<uint32_t>(pair ? (g.m + 255) / 256 : (g.m + BM - 1) / BM);
   p.tiles_n = static_cast<uint32_t>((g.n + bn - 1) / bn);
   p.total_tiles = static_cast<uint32_t>(p.tiles_m * p.tiles_n * b0 * b1);
   p.c = g.c;
@@ -793,6 +1070,8 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   // get eight epilogue warps (one fewer operand stage makes room for their staging boxes).
   const bool heavy = g.epilogue == SPAR_B200_EPI_BIAS_GELU || g.epilogue == SPAR_B200_EPI_GELU_BWD ||
                      g.epilogue == SPAR_B200_EPI_BIAS_ADD || g.rope_table;
+  if (pair)
+    return heavy ? launch_pair<5, 8>(p, device, stream) : launch_pair<6, 4>(p, device, stream);
   if (heavy) {
     switch (bn) {
       case 256:

@@ -242,3 +242,32 @@ def test_gemm_rope_epilogue(cuda):
         torch.cuda.synchronize()
         assert ops.gemm_error(0) == 0
         np.testing.assert_allclose(fused.cpu().numpy(), plain.cpu().numpy(), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("epi", ["none", "bias_gelu", "bias_add"])
+def test_gemm_many_tiles_per_sm_pair(cuda, epi):
+    """More 256 x 256 tiles than SM pairs, so every persistent CTA pair runs several tiles and
+    cycles both TMEM accumulators and the operand-stage ring (plain and eight-warp epilogues)."""
+    import torch
+    from spar_b200 import ops
+    from oracle import spar_oracle as O
+
+    m, n, k = 4096, 3072, 288
+    a, b, ref = _mats(m, n, k, False, False, seed=23)
+    at, bt = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    r = np.random.default_rng(24)
+    bias = r.standard_normal(n).astype(np.float32)
+    aux = r.standard_normal((m, n)).astype(np.float32)
+    biast, auxt = torch.from_numpy(bias).to(cuda), torch.from_numpy(aux).to(cuda)
+    if epi == "none":
+        c = ops.matmul(at, bt)
+        expect = ref
+    elif epi == "bias_gelu":
+        c = ops.matmul(at, bt, epilogue=ops.EPI_BIAS_GELU, bias=biast, aux=auxt)
+        expect = O.gelu_forward(ref + bias, np.float64)
+    else:
+        c = ops.matmul(at, bt, epilogue=ops.EPI_BIAS_ADD, bias=biast, aux=auxt)
+        expect = ref + bias + aux
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+    assert rel_l2(c.cpu().numpy(), expect) <= 2e-3
