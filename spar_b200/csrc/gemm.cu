@@ -935,14 +935,14 @@ uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
 // no causal limits, no batch, no 3xTF32) with at least 8 k-blocks per split. The persistent grid
 // runs ceil(tiles * parts / sms) rounds of 1/parts-sized work units; the split count with the
 // fewest full-tile-equivalent rounds wins when it saves at least 15% over no split.
-uint32_t splitk_parts(const SparB200Gemm& g, int bn, int sms) {
+uint32_t splitk_parts(const SparB200Gemm& g, uint64_t tile_m, uint64_t tile_n, int units) {
   if (g.precision != SPAR_B200_TF32 || g.epilogue != SPAR_B200_EPI_NONE || g.round_output ||
       g.rope_table ||
       g.causal != SPAR_B200_CAUSAL_NONE || (g.batch[0] > 1) || (g.batch[1] > 1) || g.n % 4)
     return 1;
-  const uint64_t tiles = ((g.m + BM - 1) / BM) * ((g.n + bn - 1) / bn);
+  const uint64_t tiles = ((g.m + tile_m - 1) / tile_m) * ((g.n + tile_n - 1) / tile_n);
   const uint64_t kblocks = (g.k + BK - 1) / BK;
-  const uint64_t s = static_cast<uint64_t>(sms);
+  const uint64_t s = static_cast<uint64_t>(units);
   double best = static_cast<double>((tiles + s - 1) / s);
   uint32_t best_parts = 1;
   for (uint64_t parts = 2; parts <= 8 && parts * 8 <= kblocks; ++parts) {
@@ -955,10 +955,29 @@ uint32_t splitk_parts(const SparB200Gemm& g, int bn, int sms) {
   return best_parts;
 }
 
+// How a GEMM runs: wide unbatched TF32 products on SM pairs (256 x 256 tiles over 2-CTA
+// clusters), everything else (batched, causal, 3xTF32, narrow) on single SMs; either may split K.
+struct GemmPlan {
+  bool pair;
+  int bn;
+  uint32_t kparts;
+};
+
+GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
+  const bool split = g.precision == SPAR_B200_TF32X3;
+  const uint64_t b = (g.batch[0] ? g.batch[0] : 1) * (g.batch[1] ? g.batch[1] : 1);
+  GemmPlan pl;
+  pl.bn = split ? 64 : (g.n > 128 ? 256 : (g.n > 64 ? 128 : 64));
+  pl.pair = !split && b == 1 && g.causal == SPAR_B200_CAUSAL_NONE && pl.bn == 256 && g.m >= 256;
+  const int sms = sm_count(device);
+  pl.kparts = split ? 1 : (pl.pair ? splitk_parts(g, 256, 256, sms / 2)
+                                   : splitk_parts(g, BM, static_cast<uint64_t>(pl.bn), sms));
+  return pl;
+}
+
 uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device) {
-  const int bn = g.n > 128 ? 256 : (g.n > 64 ? 128 : 64);
-  const uint32_t parts = splitk_parts(g, bn, sm_count(device));
-  return parts > 1 ? static_cast<uint64_t>(parts) * g.m * ((g.n + 3) / 4 * 4) : 0;
+  const GemmPlan pl = gemm_plan(g, device);
+  return pl.kparts > 1 ? static_cast<uint64_t>(pl.kparts) * g.m * ((g.n + 3) / 4 * 4) : 0;
 }
 
 cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
@@ -969,17 +988,15 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
   const bool split = g.precision == SPAR_B200_TF32X3;
   // 3xTF32 keeps its running sums in registers (one 64-column row segment per thread).
-  int bn = split ? 64 : (g.n > 128 ? 256 : (g.n > 64 ? 128 : 64));
+  const GemmPlan plan = gemm_plan(g, device);
+  const int bn = plan.bn;
   p.sections = split ? 3 : 1;
   p.a_mn_major = g.a_transposed ? 1 : 0;
   p.b_mn_major = g.b_transposed ? 0 : 1;
 
   const uint64_t a_inner = g.a_transposed ? g.m : g.k, a_rows = g.a_transposed ? g.k : g.m;
   const uint64_t b_inner = g.b_transposed ? g.k : g.n, b_rows = g.b_transposed ? g.n : g.k;
-  // Wide unbatched TF32 products run on SM pairs (256 x 256 tiles); split-K, batched, causal
-  // and 3xTF32 products keep the single-SM kernel.
-  const bool pair = !split && b0 * b1 == 1 && g.causal == SPAR_B200_CAUSAL_NONE && bn == 256 &&
-                    g.m >= 256 && splitk_parts(g, bn, sm_count(device)) == 1;
+  const bool pair = plan.pair;
   const uint32_t a_box_rows = p.a_mn_major ? BK : BM;
   const uint32_t b_box_rows = p.b_mn_major ? BK : (pair ? 128u : static_cast<uint32_t>(bn));
 
@@ -1047,7 +1064,7 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     p.rope_dim = static_cast<uint32_t>(g.rope_dim);
     p.rope_cols = static_cast<uint32_t>(g.rope_cols);
   }
-  const uint32_t kparts = split ? 1 : splitk_parts(g, bn, sm_count(device));
+  const uint32_t kparts = plan.kparts;
   const uint64_t ldp = (g.n + 3) / 4 * 4;
   if (kparts > 1 && splitk_workspace && splitk_floats >= kparts * g.m * ldp) {
     if (!make_map(&p.part_map, splitk_workspace, g.n, g.m, kparts, 1, ldp, g.m * ldp,
@@ -1055,7 +1072,8 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
       return cudaErrorInvalidValue;
     p.kparts = kparts;
     p.total_tiles *= kparts;
-    const cudaError_t e = bn == 256 ? launch_kernel<256, 4, false>(p, device, stream)
+    const cudaError_t e = pair     ? launch_pair<6, 4>(p, device, stream)
+                        : bn == 256 ? launch_kernel<256, 4, false>(p, device, stream)
                         : bn == 128 ? launch_kernel<128, 6, false>(p, device, stream)
                                     : launch_kernel<64, 8, false>(p, device, stream);
     if (e != cudaSuccess) return e;
