@@ -15,9 +15,9 @@
 //   probabilities are those of the reference's max-subtracted softmax. The row maximum and
 //   1 / row sum are saved for the backward.
 // Backward (deterministic: every gradient element is written by exactly one CTA, no atomics):
-//   query kernel  per (batch, head, 128-query tile): D = rowsum(dO o O); for each 64-key tile
-//                 S, dP = dO V^T, P recomputed from the saved statistics,
-//                 dS = P o (dP - D) * scale, dQ += dS K; D is saved for the key kernel.
+//   D = rowsum(dO o O) per (row, head) first, by a small streaming kernel.
+//   query kernel  per (batch, head, 128-query tile): for each 64-key tile S, dP = dO V^T,
+//                 P recomputed from the saved statistics, dS = P o (dP - D) * scale, dQ += dS K.
 //   key kernel    per (batch, head, 128-key tile): for each 64-query tile S^T = K Q^T,
 //                 dP^T = V dO^T, P^T and dS^T as above, dV += P^T dO, dK += dS^T Q.
 // Warp roles in every kernel: warp 0 TMA producer, warp 1 MMA issuer (one elected thread),
@@ -59,7 +59,6 @@ struct AttnParams {
   CUtensorMap qk64;    // qkv, K-major boxes {32, 64}
   CUtensorMap qkv_mn;  // qkv, MN-major boxes {32, 32}
   CUtensorMap do128;   // dO (= d ctx), K-major {32, 128}
-  CUtensorMap o128;    // O (= ctx), K-major {32, 128} (D = rowsum(dO o O) from shared memory)
   CUtensorMap do64;    // dO, K-major {32, 64}
   CUtensorMap do_mn;   // dO, MN-major {32, 32}
   CUtensorMap out;     // output store boxes {32, 32}: ctx (forward) or dqkv (backward)
@@ -477,10 +476,10 @@ struct BwdQ {
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kDO = kQ + kTile128;
   static constexpr uint32_t kStage = 3 * kTile64;  // K (K-major), V (K-major), K (MN-major)
-  static constexpr uint32_t kO = kDO + kTile128;
-  static constexpr uint32_t kKV = kO + kTile128;     // 2 stages
-  static constexpr uint32_t kDS = kKV + 2 * kStage;  // dQ output staging (4 KB per warp)
-  static constexpr uint32_t kBar = kDS + 32768;
+  static constexpr uint32_t kStages = 3;
+  static constexpr uint32_t kKV = kDO + kTile128;
+  static constexpr uint32_t kDS = kKV + kStages * kStage;  // dQ staging: 4 warps x 4 KB
+  static constexpr uint32_t kBar = kDS + 16384;
   static constexpr uint32_t kSmem = kBar + 256 + 1024;
   static_assert(kSmem <= kMaxSmem, "query-kernel shared memory");
 };
@@ -493,30 +492,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;   // [2]
-  uint64_t* kv_empty = bars + 4;  // [2]
-  uint64_t* s_full = bars + 6;    // [2]
-  uint64_t* s_empty = bars + 8;   // [2]
-  uint64_t* ds_full = bars + 10;
-  uint64_t* d_done = bars + 11;  // softmax warps finished reading O / dO for D
-  uint64_t* acc_full = bars + 12;
-  uint64_t* acc_empty = bars + 13;
-  uint64_t* drain = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* kv_full = bars + 2;   // [kStages]
+  uint64_t* kv_empty = bars + 5;  // [kStages]
+  uint64_t* s_full = bars + 8;    // [2]
+  uint64_t* s_empty = bars + 10;  // [2]
+  uint64_t* ds_full = bars + 12;
+  uint64_t* acc_full = bars + 13;
+  uint64_t* acc_empty = bars + 14;
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
     tc::mbar_init(q_empty, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (uint32_t i = 0; i < L::kStages; ++i) {
       tc::mbar_init(kv_full + i, 1);
       tc::mbar_init(kv_empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(s_full + i, 1);
       tc::mbar_init(s_empty + i, 1);  // freed by the MMA once dQ has read dS (aliasing S)
     }
     tc::mbar_init(ds_full, kSoftWarps);
-    tc::mbar_init(d_done, kSoftWarps);
     tc::mbar_init(acc_full, 1);
     tc::mbar_init(acc_empty, kSoftWarps);
     tc::mbar_init(drain, 1);
@@ -536,27 +535,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
 
   if (warp == 0) {
     if (tc::elect_one()) {
-      uint32_t n = 0, item = 0;
-      int last_q = -1, last_kv[2] = {-1, -1};
+      uint32_t n = 0, item = 0, st = 0, ph = 0;
+      int last_q = -1, last_kv[L::kStages];
+      for (uint32_t i = 0; i < L::kStages; ++i) last_kv[i] = -1;
       for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
         const Item it = decode(p, idx, true);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
         if (!wait_or_abort(q_empty, (item & 1) ^ 1, abort_flag)) break;
-        tc::mbar_arrive_expect_tx(q_full, 3 * L::kTile128);
+        tc::mbar_arrive_expect_tx(q_full, 2 * L::kTile128);
         last_q = item & 1;
         const int q0 = static_cast<int>(it.t * 128);
 #pragma unroll
         for (int c = 0; c < DH / 32; ++c) {
           tc::tma_load_4d(smem + L::kQ + c * 16384, &p.qk128, q_full, hc + 32 * c, q0, b, 0);
           tc::tma_load_4d(smem + L::kDO + c * 16384, &p.do128, q_full, hc + 32 * c, q0, b, 0);
-          tc::tma_load_4d(smem + L::kO + c * 16384, &p.o128, q_full, hc + 32 * c, q0, b, 0);
         }
         const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
         for (uint32_t j = 0; j < nkv; ++j, ++n) {
-          const uint32_t st = n & 1;
-          if (!wait_or_abort(kv_empty + st, ((n >> 1) & 1) ^ 1, abort_flag)) break;
+          if (!wait_or_abort(kv_empty + st, ph ^ 1, abort_flag)) break;
           tc::mbar_arrive_expect_tx(kv_full + st, L::kStage);
-          last_kv[st] = (n >> 1) & 1;
+          last_kv[st] = static_cast<int>(ph);
           uint8_t* s = smem + L::kKV + st * L::kStage;
           const int row = static_cast<int>(j * 64);
 #pragma unroll
@@ -571,10 +569,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
             for (int c = 0; c < DH / 32; ++c)
               tc::tma_load_4d(s + 2 * L::kTile64 + (kb * (DH / 32) + c) * 4096, &p.qkv_mn,
                               kv_full + st, dcol + hc + 32 * c, row + 32 * kb, b, 0);
+          if (++st == L::kStages) {
+            st = 0;
+            ph ^= 1;
+          }
         }
       }
       if (last_q >= 0 && !tc::mbar_wait(q_full, last_q)) record_error();
-      for (int s = 0; s < 2; ++s)
+      for (uint32_t s = 0; s < L::kStages; ++s)
         if (last_kv[s] >= 0 && !tc::mbar_wait(kv_full + s, last_kv[s])) record_error();
     }
     __syncwarp();
@@ -587,9 +589,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       const uint32_t kv_addr = tc::smem_u32(smem + L::kKV);
       uint32_t n = 0, sn = 0, dn = 0, item = 0;
       bool ok = true;
+      // kv load number kn sits in stage kn % kStages, phase (kn / kStages) & 1.
       auto issue_s = [&](uint32_t kn) -> bool {  // S and dP for kv load number kn
-        const uint32_t st = kn & 1, sb = sn & 1;
-        if (!wait_or_abort(kv_full + st, (kn >> 1) & 1, abort_flag)) return false;
+        const uint32_t st = kn % L::kStages, sb = sn & 1;
+        if (!wait_or_abort(kv_full + st, (kn / L::kStages) & 1, abort_flag)) return false;
         if (!wait_or_abort(s_empty + sb, ((sn >> 1) & 1) ^ 1, abort_flag)) return false;
         tc::tc_fence_after();
         const uint32_t s = kv_addr + st * L::kStage;
@@ -615,15 +618,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
           if (j + 1 < nkv) {
             if (!(ok = issue_s(n0 + j + 1))) break;
           }
-          if (j + 1 == nkv) {  // Q, dO, O free once the MMAs and the D readers are done
-            if (!(ok = wait_or_abort(d_done, item & 1, abort_flag))) break;
-            tc::mma_commit(q_empty);
-          }
+          if (j + 1 == nkv) tc::mma_commit(q_empty);  // Q, dO no longer read in this item
           if (!(ok = wait_or_abort(ds_full, dn & 1, abort_flag))) break;
           ++dn;
           if (j == 0 && !(ok = wait_or_abort(acc_empty, (item & 1) ^ 1, abort_flag))) break;
           tc::tc_fence_after();
-          const uint32_t st = (n0 + j) & 1, sb = (sn0 + j) & 1;
+          const uint32_t st = (n0 + j) % L::kStages, sb = (sn0 + j) & 1;
           const uint32_t kmn = kv_addr + st * L::kStage + 2 * L::kTile64;
           // dQ += dS K with dS read from TMEM, where the softmax warps wrote it over S.
 #pragma unroll
@@ -654,27 +654,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       const bool valid = q < seq;
       const uint64_t srow = static_cast<uint64_t>(it.b * p.heads + it.h) * seq + q;
       // Rows past the sequence: mx = 0, inv = 0 make every probability 0 (their scores are 0).
+      // D = rowsum(dO o O) comes precomputed (attn_delta_kernel).
       float mx = 0.f, inv = 0.f, dd = 0.f;
       if (valid) {
         mx = p.row_max[srow];
         inv = p.row_inv[srow];
+        dd = p.delta[srow];
       }
-      // D = rowsum(dO o O) of this row, from the tiles the producer staged (zeros past seq).
-      if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
-#pragma unroll
-      for (int c = 0; c < DH / 32; ++c) {
-        const uint8_t* a = smem + L::kDO + c * 16384;
-        const uint8_t* o = smem + L::kO + c * 16384;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 x = *reinterpret_cast<const float4*>(a + swz(r, i));
-          const float4 y = *reinterpret_cast<const float4*>(o + swz(r, i));
-          dd += x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
-        }
-      }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(d_done);
-      if (valid && grp == 0) p.delta[srow] = dd;
       const float ninv_scale = inv * p.scale;
       if (lane == 0) tc::bulk_wait_read<0>();
       __syncwarp();
@@ -712,17 +698,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       if (!ok) break;
       if (!(ok = wait_or_abort(acc_full, item & 1, abort_flag))) break;
       tc::tc_fence_after();
-      if (grp < DH / 32) {
-        uint32_t v[32];
-        tc::tmem_load_32x32(th.lanes + 256 + grp * 32, v);
-        float o[32];
+      if (grp == 0) {  // the four warps of column group 0 store dQ, one 32-column box at a time
+        uint8_t* stg = dsbuf + th.quarter * 4096;
+#pragma unroll 1
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t v[32];
+          tc::tmem_load_32x32(th.lanes + 256 + c * 32, v);
+          float o[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);
-        if (p.rope && valid) inverse_rope(o, p.rope + static_cast<uint64_t>(q) * (DH / 2) + grp * 16);
-        store_box(&p.out, dsbuf + grp * 16384 + th.quarter * 4096, o,
-                  static_cast<int>(it.h * DH + 32 * grp),
-                  static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
-        if (lane == 0) tc::bulk_commit();
+          for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);
+          if (p.rope && valid) inverse_rope(o, p.rope + static_cast<uint64_t>(q) * (DH / 2) + c * 16);
+          if (c > 0) {
+            if (lane == 0) tc::bulk_wait_read<0>();
+            __syncwarp();
+          }
+          store_box(&p.out, stg, o, static_cast<int>(it.h * DH + 32 * c),
+                    static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
+          if (lane == 0) tc::bulk_commit();
+        }
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -1024,6 +1017,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
   if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
+// ============================================================================ D = rowsum(dO o O)
+// One warp per (token row, head): the dot product of the head's dO and O slices (coalesced 128-
+// and 256-byte reads), written as D[(b * heads + h) * seq + t] for the backward kernels.
+__global__ void __launch_bounds__(256) attn_delta_kernel(float* __restrict__ delta,
+                                                         const float* __restrict__ d_o,
+                                                         const float* __restrict__ o, uint64_t rows,
+                                                         uint32_t seq, uint32_t heads, uint32_t dh,
+                                                         uint64_t ld) {
+  const uint64_t w = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  if (w >= rows * heads) return;
+  const uint64_t row = w / heads;
+  const uint32_t h = static_cast<uint32_t>(w - row * heads);
+  const float* a = d_o + row * ld + static_cast<uint64_t>(h) * dh;
+  const float* b = o + row * ld + static_cast<uint64_t>(h) * dh;
+  float acc = 0.f;
+  for (uint32_t c = lane; c < dh; c += 32) acc += __ldg(a + c) * __ldg(b + c);
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const uint64_t bb = row / seq, t = row - bb * seq;
+    delta[(bb * heads + h) * seq + t] = acc;
+  }
+}
+
 // ============================================================================ host side
 template <typename K>
 cudaError_t launch(K kernel, uint32_t smem, const AttnParams& p, int device, cudaStream_t stream,
@@ -1089,7 +1106,6 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
       !make_map(&p.qk64, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 64, false) ||
       !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true) ||
       !make_map(&p.do128, dctx, d, seq, batch, 1, d, seq * d, 0, 128, false) ||
-      !make_map(&p.o128, ctx, d, seq, batch, 1, d, seq * d, 0, 128, false) ||
       !make_map(&p.do64, dctx, d, seq, batch, 1, d, seq * d, 0, 64, false) ||
       !make_map(&p.do_mn, dctx, d, seq, batch, 1, d, seq * d, 0, 32, true) ||
       !make_map(&p.out, dqkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, false))
@@ -1101,7 +1117,11 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
   p.delta = delta;
   p.rope = reinterpret_cast<const float2*>(rope_table);
   static bool q32[64] = {}, q64[64] = {}, k32[64] = {}, k64[64] = {};
-  // Query kernel first: it produces D, which the key kernel reads.
+  const uint64_t warps = batch * seq * heads;
+  attn_delta_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
+      delta, dctx, ctx, batch * seq, static_cast<uint32_t>(seq), static_cast<uint32_t>(heads),
+      static_cast<uint32_t>(head_dim), d);
+  if (cudaGetLastError() != cudaSuccess) return cudaGetLastError();
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
   p.total = p.tiles * p.bh;
   cudaError_t e = head_dim == 64
