@@ -184,10 +184,12 @@ template <int DH>
 struct Fwd {
   static constexpr uint32_t kTile = DH * 512;  // 128 rows x DH fp32
   static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kK = kQ + kTile;      // 2 stages
-  static constexpr uint32_t kV = kK + 2 * kTile;  // 2 stages
-  static constexpr uint32_t kStg = kV + 2 * kTile;  // output staging, 4 KB per softmax warp
-  static constexpr uint32_t kX = kStg + kSoftWarps * 4096;  // row partials [max 2x128][sum 2x128]
+  static constexpr uint32_t kKStages = 3;  // K is read in both passes: the deeper ring
+  static constexpr uint32_t kVStages = 2;
+  static constexpr uint32_t kK = kQ + kTile;
+  static constexpr uint32_t kV = kK + kKStages * kTile;
+  static constexpr uint32_t kStg = kV + kVStages * kTile;  // output staging, 4 warps x 4 KB
+  static constexpr uint32_t kX = kStg + 16384;  // row partials [max 2x128][sum 2x128]
   static constexpr uint32_t kBar = kX + 2048;
   static constexpr uint32_t kSmem = kBar + 256 + 1024;
   static_assert(kSmem <= kMaxSmem, "forward shared memory");
@@ -203,26 +205,34 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;    // [2]
-  uint64_t* kv_empty = bars + 4;   // [2]
-  uint64_t* s_full = bars + 6;     // [2]
-  uint64_t* s_read = bars + 8;     // [2] pass 1: the softmax warps have read S
-  uint64_t* s_used = bars + 10;    // [2] pass 2: the P V product has read P
-  uint64_t* p_full = bars + 12;
-  uint64_t* o_full = bars + 13;
-  uint64_t* o_empty = bars + 14;
-  uint64_t* xbar = bars + 15;  // softmax-warp rendezvous
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* k_full = bars + 2;     // [kKStages]
+  uint64_t* k_empty = bars + 5;    // [kKStages]
+  uint64_t* v_full = bars + 8;     // [kVStages]
+  uint64_t* v_empty = bars + 10;   // [kVStages]
+  uint64_t* s_full = bars + 12;    // [2]
+  uint64_t* s_read = bars + 14;    // [2] pass 1: the softmax warps have read S
+  uint64_t* s_used = bars + 16;    // [2] pass 2: the P V product has read P
+  uint64_t* p_full = bars + 18;
+  uint64_t* o_full = bars + 19;
+  uint64_t* o_empty = bars + 20;
+  uint64_t* xbar = bars + 21;  // softmax-warp rendezvous
+  uint64_t* drain = bars + 22;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
     tc::mbar_init(q_empty, 1);
+    for (uint32_t i = 0; i < L::kKStages; ++i) {
+      tc::mbar_init(k_full + i, 1);
+      tc::mbar_init(k_empty + i, 1);
+    }
+    for (uint32_t i = 0; i < L::kVStages; ++i) {
+      tc::mbar_init(v_full + i, 1);
+      tc::mbar_init(v_empty + i, 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(kv_full + i, 1);
-      tc::mbar_init(kv_empty + i, 1);
       tc::mbar_init(s_full + i, 1);
       tc::mbar_init(s_read + i, kSoftWarps);
       tc::mbar_init(s_used + i, 1);
@@ -250,8 +260,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     if (tc::elect_one()) {
       tc::tma_prefetch(&p.qk128);
       tc::tma_prefetch(&p.qkv_mn);
-      uint32_t n = 0, item = 0;
-      int last_q = -1, last_kv[2] = {-1, -1};
+      uint32_t item = 0, kn = 0, vn = 0;  // loads issued into the K and V rings
+      int last_q = -1, last_k[L::kKStages], last_v[L::kVStages];
+      for (uint32_t i = 0; i < L::kKStages; ++i) last_k[i] = -1;
+      for (uint32_t i = 0; i < L::kVStages; ++i) last_v[i] = -1;
       for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
         const Item it = decode(p, idx, true);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
@@ -264,31 +276,41 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                           static_cast<int>(it.t * 128), b, 0);
         const uint32_t nkv = it.t + 1;
         for (uint32_t pass = 0; pass < 2 && !*abort_flag; ++pass) {
-          for (uint32_t j = 0; j < nkv; ++j, ++n) {
-            const uint32_t st = n & 1;
-            if (!wait_or_abort(kv_empty + st, ((n >> 1) & 1) ^ 1, abort_flag)) break;
-            tc::mbar_arrive_expect_tx(kv_full + st, pass ? 2 * L::kTile : L::kTile);
-            last_kv[st] = (n >> 1) & 1;
+          for (uint32_t j = 0; j < nkv && !*abort_flag; ++j) {
             const int row = static_cast<int>(j * 128);
+            {  // K tile j (both passes)
+              const uint32_t st = kn % L::kKStages, ph = (kn / L::kKStages) & 1;
+              if (!wait_or_abort(k_empty + st, ph ^ 1, abort_flag)) break;
+              tc::mbar_arrive_expect_tx(k_full + st, L::kTile);
+              last_k[st] = static_cast<int>(ph);
 #pragma unroll
-            for (int c = 0; c < DH / 32; ++c)
-              tc::tma_load_4d(smem + L::kK + st * L::kTile + c * 16384, &p.qk128, kv_full + st,
-                              dcol + hc + 32 * c, row, b, 0);
-            if (pass) {
+              for (int c = 0; c < DH / 32; ++c)
+                tc::tma_load_4d(smem + L::kK + st * L::kTile + c * 16384, &p.qk128, k_full + st,
+                                dcol + hc + 32 * c, row, b, 0);
+              ++kn;
+            }
+            if (pass) {  // V tile j (pass 2)
+              const uint32_t st = vn % L::kVStages, ph = (vn / L::kVStages) & 1;
+              if (!wait_or_abort(v_empty + st, ph ^ 1, abort_flag)) break;
+              tc::mbar_arrive_expect_tx(v_full + st, L::kTile);
+              last_v[st] = static_cast<int>(ph);
 #pragma unroll
               for (int kb = 0; kb < 4; ++kb)
 #pragma unroll
                 for (int c = 0; c < DH / 32; ++c)
                   tc::tma_load_4d(smem + L::kV + st * L::kTile + (kb * (DH / 32) + c) * 4096,
-                                  &p.qkv_mn, kv_full + st, 2 * dcol + hc + 32 * c, row + 32 * kb,
+                                  &p.qkv_mn, v_full + st, 2 * dcol + hc + 32 * c, row + 32 * kb,
                                   b, 0);
+              ++vn;
             }
           }
         }
       }
       if (last_q >= 0 && !tc::mbar_wait(q_full, last_q)) record_error();
-      for (int s = 0; s < 2; ++s)
-        if (last_kv[s] >= 0 && !tc::mbar_wait(kv_full + s, last_kv[s])) record_error();
+      for (uint32_t s = 0; s < L::kKStages; ++s)
+        if (last_k[s] >= 0 && !tc::mbar_wait(k_full + s, last_k[s])) record_error();
+      for (uint32_t s = 0; s < L::kVStages; ++s)
+        if (last_v[s] >= 0 && !tc::mbar_wait(v_full + s, last_v[s])) record_error();
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -299,16 +321,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       const uint32_t q_addr = tc::smem_u32(smem + L::kQ);
       const uint32_t k_addr = tc::smem_u32(smem + L::kK);
       const uint32_t v_addr = tc::smem_u32(smem + L::kV);
-      uint32_t n = 0, sn = 0, pn = 0, item = 0;
+      uint32_t kn = 0, vn = 0, sn = 0, pn = 0, item = 0;
       // An S buffer is freed by the softmax warps after a pass-1 use (s_read) and by the P V
       // product after a pass-2 use (s_used); per buffer: which freed it last, and how many
       // completions each barrier has had.
       uint32_t reads[2] = {0, 0}, useds[2] = {0, 0}, last[2] = {0, 0};
       bool ok = true;
-      // S[sn & 1] = Q K^T for the kv stage of load number kn.
-      auto issue_s = [&](uint32_t kn, uint32_t pass) -> bool {
-        const uint32_t st = kn & 1, sb = sn & 1;
-        if (!wait_or_abort(kv_full + st, (kn >> 1) & 1, abort_flag)) return false;
+      // S[sn & 1] = Q K^T for the next K tile of the ring; the K stage is free once it is read.
+      auto issue_s = [&](uint32_t pass) -> bool {
+        const uint32_t st = kn % L::kKStages, sb = sn & 1;
+        if (!wait_or_abort(k_full + st, (kn / L::kKStages) & 1, abort_flag)) return false;
         if (last[sb] == 1 && !wait_or_abort(s_read + sb, (reads[sb] - 1) & 1, abort_flag))
           return false;
         if (last[sb] == 2 && !wait_or_abort(s_used + sb, (useds[sb] - 1) & 1, abort_flag))
@@ -319,6 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           tc::mma_tf32(tmem + sb * 128, kmajor_desc(q_addr, 16384, ks),
                        kmajor_desc(k_addr + st * L::kTile, 16384, ks), idesc_s, ks > 0);
         tc::mma_commit(s_full + sb);
+        tc::mma_commit(k_empty + st);
+        ++kn;
         if (pass == 0) {
           last[sb] = 1;
           ++reads[sb];
@@ -334,32 +358,31 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const uint32_t nkv = it.t + 1;
         if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
         tc::tc_fence_after();
-        for (uint32_t j = 0; j < nkv && ok; ++j, ++n) {  // pass 1
-          if (!(ok = issue_s(n, 0))) break;
-          tc::mma_commit(kv_empty + (n & 1));
-        }
+        for (uint32_t j = 0; j < nkv && ok; ++j)  // pass 1
+          ok = issue_s(0);
         if (!ok) break;
         // pass 2: S_{j+1} is issued before O += P_j V_j so the softmax of tile j+1 overlaps it.
-        const uint32_t n0 = n, sn0 = sn;
-        if (!(ok = issue_s(n0, 1))) break;
+        const uint32_t sn0 = sn;
+        if (!(ok = issue_s(1))) break;
         for (uint32_t j = 0; j < nkv && ok; ++j) {
           if (j + 1 < nkv) {
-            if (!(ok = issue_s(n0 + j + 1, 1))) break;
+            if (!(ok = issue_s(1))) break;
           }
           if (j + 1 == nkv) tc::mma_commit(q_empty);  // Q is no longer read in this item
           if (!(ok = wait_or_abort(p_full, pn & 1, abort_flag))) break;
           ++pn;
           if (j == 0 && !(ok = wait_or_abort(o_empty, (item & 1) ^ 1, abort_flag))) break;
+          const uint32_t vst = vn % L::kVStages, sb = (sn0 + j) & 1;
+          if (!(ok = wait_or_abort(v_full + vst, (vn / L::kVStages) & 1, abort_flag))) break;
           tc::tc_fence_after();
-          const uint32_t st = (n0 + j) & 1, sb = (sn0 + j) & 1;
 #pragma unroll
           for (int ks = 0; ks < 16; ++ks)
             tc::mma_tf32_ts(tmem + 256, tmem + sb * 128 + ks * 8,
-                            mnmajor_desc<DH>(v_addr + st * L::kTile, ks), idesc_o, (j | ks) != 0);
+                            mnmajor_desc<DH>(v_addr + vst * L::kTile, ks), idesc_o, (j | ks) != 0);
           tc::mma_commit(s_used + sb);
-          tc::mma_commit(kv_empty + st);
+          tc::mma_commit(v_empty + vst);
+          ++vn;
         }
-        n = n0 + nkv;
         if (ok) tc::mma_commit(o_full);
       }
       tc::mma_commit(drain);
@@ -371,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     // Thread (r, grp) owns columns [64*grp, 64*grp + 64) of row r of every 128 x 128 score tile.
     const SoftThread th(warp, lane, tmem);
     const uint32_t r = th.r, grp = th.grp;
-    uint8_t* stg = smem + L::kStg + (warp - 2) * 4096;
+    uint8_t* stg = smem + L::kStg + th.quarter * 4096;
     float* xmax = reinterpret_cast<float*>(smem + L::kX);  // [2][128]
     float* xsum = xmax + 256;                              // [2][128]
     uint32_t sn = 0, item = 0, xphase = 0;
@@ -438,17 +461,20 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       xsum[grp * 128 + r] = sum;
       if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
       const float inv = 1.f / (xsum[r] + xsum[128 + r]);
-      if (grp < DH / 32) {
-        uint32_t v[32];
-        tc::tmem_load_32x32(th.lanes + 256 + grp * 32, v);
-        float o[32];
+      if (grp == 0) {  // the four warps of column group 0 store O, one 32-column box at a time
+#pragma unroll 1
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t v[32];
+          tc::tmem_load_32x32(th.lanes + 256 + c * 32, v);
+          float o[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]) * inv;
-        if (lane == 0) tc::bulk_wait_read<0>();  // this warp's staging box is free again
-        __syncwarp();
-        store_box(&p.out, stg, o, static_cast<int>(it.h * DH + 32 * grp),
-                  static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
-        if (lane == 0) tc::bulk_commit();
+          for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]) * inv;
+          if (lane == 0) tc::bulk_wait_read<0>();  // this warp's staging box is free again
+          __syncwarp();
+          store_box(&p.out, stg, o, static_cast<int>(it.h * DH + 32 * c),
+                    static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
+          if (lane == 0) tc::bulk_commit();
+        }
       }
       tc::tc_fence_before();
       __syncwarp();
