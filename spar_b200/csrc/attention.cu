@@ -212,12 +212,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* s_full = bars + 12;    // [2]
   uint64_t* s_read = bars + 14;    // [2] pass 1: the softmax warps have read S
   uint64_t* s_used = bars + 16;    // [2] pass 2: the P V product has read P
+  // [2] P ready, alternating by P count: the softmax can be one P ahead of the MMA's wait (the
+  // MMA issues S_{j+1} before waiting for P_j), so one barrier could complete two phases unseen.
   uint64_t* p_full = bars + 18;
-  uint64_t* o_full = bars + 19;
-  uint64_t* o_empty = bars + 20;
-  uint64_t* xbar = bars + 21;  // softmax-warp rendezvous
-  uint64_t* drain = bars + 22;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
+  uint64_t* o_full = bars + 20;
+  uint64_t* o_empty = bars + 21;
+  uint64_t* xbar = bars + 22;  // softmax-warp rendezvous
+  uint64_t* drain = bars + 23;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -238,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       tc::mbar_init(s_used + i, 1);
     }
     tc::mbar_init(p_full, kSoftWarps);
+    tc::mbar_init(p_full + 1, kSoftWarps);
     tc::mbar_init(o_full, 1);
     tc::mbar_init(o_empty, kSoftWarps);
     tc::mbar_init(xbar, kSoftWarps);
@@ -369,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             if (!(ok = issue_s(1))) break;
           }
           if (j + 1 == nkv) tc::mma_commit(q_empty);  // Q is no longer read in this item
-          if (!(ok = wait_or_abort(p_full, pn & 1, abort_flag))) break;
+          if (!(ok = wait_or_abort(p_full + (pn & 1), (pn >> 1) & 1, abort_flag))) break;
           ++pn;
           if (j == 0 && !(ok = wait_or_abort(o_empty, (item & 1) ^ 1, abort_flag))) break;
           const uint32_t vst = vn % L::kVStages, sb = (sn0 + j) & 1;
@@ -397,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     uint8_t* stg = smem + L::kStg + th.quarter * 4096;
     float* xmax = reinterpret_cast<float*>(smem + L::kX);  // [2][128]
     float* xsum = xmax + 256;                              // [2][128]
-    uint32_t sn = 0, item = 0, xphase = 0;
+    uint32_t sn = 0, pn = 0, item = 0, xphase = 0;
     bool ok = true;
     for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
       const Item it = decode(p, idx, true);
@@ -453,7 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         tc::tmem_store_2x32(base, base + 32, v0, v1);  // P over S: the A operand of O += P V
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(p_full);
+        if (lane == 0) tc::mbar_arrive(p_full + (pn & 1));
+        ++pn;
       }
       if (!ok) break;
       if (!(ok = wait_or_abort(o_full, item & 1, abort_flag))) break;
@@ -522,11 +526,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
   uint64_t* kv_empty = bars + 5;  // [kStages]
   uint64_t* s_full = bars + 8;    // [2]
   uint64_t* s_empty = bars + 10;  // [2]
-  uint64_t* ds_full = bars + 12;
-  uint64_t* acc_full = bars + 13;
-  uint64_t* acc_empty = bars + 14;
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* ds_full = bars + 12;  // [2] dS ready, alternating by step (see p_full above)
+  uint64_t* acc_full = bars + 14;
+  uint64_t* acc_empty = bars + 15;
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -542,6 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       tc::mbar_init(s_empty + i, 1);  // freed by the MMA once dQ has read dS (aliasing S)
     }
     tc::mbar_init(ds_full, kSoftWarps);
+    tc::mbar_init(ds_full + 1, kSoftWarps);
     tc::mbar_init(acc_full, 1);
     tc::mbar_init(acc_empty, kSoftWarps);
     tc::mbar_init(drain, 1);
@@ -645,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
             if (!(ok = issue_s(n0 + j + 1))) break;
           }
           if (j + 1 == nkv) tc::mma_commit(q_empty);  // Q, dO no longer read in this item
-          if (!(ok = wait_or_abort(ds_full, dn & 1, abort_flag))) break;
+          if (!(ok = wait_or_abort(ds_full + (dn & 1), (dn >> 1) & 1, abort_flag))) break;
           ++dn;
           if (j == 0 && !(ok = wait_or_abort(acc_empty, (item & 1) ^ 1, abort_flag))) break;
           tc::tc_fence_after();
@@ -719,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
         tc::tmem_store_32x32(th.lanes + (sn & 1) * 64 + grp * 32, dsu);
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(ds_full);
+        if (lane == 0) tc::mbar_arrive(ds_full + (sn & 1));
       }
       if (!ok) break;
       if (!(ok = wait_or_abort(acc_full, item & 1, abort_flag))) break;
@@ -789,12 +794,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
   uint64_t* s_empty = bars + 8;   // [2]
   uint64_t* mn_full = bars + 10;  // [2]
   uint64_t* mn_empty = bars + 12;  // [2]
-  uint64_t* pd_full = bars + 14;
-  uint64_t* acc_full = bars + 15;
-  uint64_t* acc_empty = bars + 16;
-  uint64_t* drain = bars + 17;
-  uint64_t* xbar = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* pd_full = bars + 14;  // [2] P^T / dS^T ready, alternating by step (see p_full above)
+  uint64_t* acc_full = bars + 16;
+  uint64_t* acc_empty = bars + 17;
+  uint64_t* drain = bars + 18;
+  uint64_t* xbar = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -810,6 +815,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       tc::mbar_init(mn_empty + i, 1);
     }
     tc::mbar_init(pd_full, kSoftWarps);
+    tc::mbar_init(pd_full + 1, kSoftWarps);
     tc::mbar_init(acc_full, 1);
     tc::mbar_init(acc_empty, kSoftWarps);
     tc::mbar_init(drain, 1);
@@ -921,7 +927,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
           }
           if (i + 1 == steps) tc::mma_commit(kv_empty);
           const uint32_t qn = n0 + i, st = qn & 1, sb = (sn0 + i) & 1;
-          if (!(ok = wait_or_abort(pd_full, qn & 1, abort_flag))) break;
+          if (!(ok = wait_or_abort(pd_full + (qn & 1), (qn >> 1) & 1, abort_flag))) break;
           if (!(ok = wait_or_abort(mn_full + st, (qn >> 1) & 1, abort_flag))) break;
           if (i == 0 && !(ok = wait_or_abort(acc_empty, (item & 1) ^ 1, abort_flag))) break;
           tc::tc_fence_after();
@@ -1002,7 +1008,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         tc::tmem_store_2x32(s_col, s_col + 128, sv, pv);
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(pd_full);
+        if (lane == 0) tc::mbar_arrive(pd_full + (n & 1));
       }
       if (!ok) break;
       if (!(ok = wait_or_abort(acc_full, item & 1, abort_flag))) break;

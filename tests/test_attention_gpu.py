@@ -116,3 +116,23 @@ def test_attention_backward_inverse_rope(cuda):
     ops.rope_apply_(plain, tab, b, t, 2 * h, dh, 3 * d, inverse=True)
     torch.cuda.synchronize()
     np.testing.assert_allclose(rot.cpu().numpy(), plain.cpu().numpy(), rtol=1e-5, atol=1e-6)
+
+
+def test_attention_c5_shape_repeated_without_timeouts(cuda):
+    """The training shape (16 x 1024 tokens, 16 heads of 64, RoPE in the backward) run back to
+    back: every CTA walks many work items, so the producer / MMA / softmax pipelines wrap many
+    times; no bounded wait may expire and every output stays finite."""
+    import torch
+    from spar_b200 import ops
+
+    b, t, h, dh = 16, 1024, 16, 64
+    g = torch.Generator(device=cuda).manual_seed(3)
+    qkv = torch.randn(b, t, 3 * h * dh, device=cuda, generator=g)
+    do = torch.randn(b, t, h * dh, device=cuda, generator=g)
+    tab = ops.rope_table(t, dh, 10000.0, device=cuda)
+    for _ in range(6):
+        ctx, mx, inv = ops.attention_forward(qkv, h)
+        dqkv = ops.attention_backward(do, qkv, ctx, mx, inv, h, rope_table=tab)
+    torch.cuda.synchronize()
+    assert ops.attention_error(0) == 0
+    assert torch.isfinite(ctx).all() and torch.isfinite(dqkv).all()
