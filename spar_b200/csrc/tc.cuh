@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a asynchronous machinery used by the GEMM:
-// mbarriers, TMA tensor loads (no multicast anywhere in this library), tcgen05 tensor-core MMAs
+// mbarriers, TMA tensor loads (each into the issuing CTA's own shared memory only), tcgen05 MMAs
 // with TMEM accumulators, TMEM allocation and TMEM -> register loads.
 //
 // Every wait is bounded: it polls with a wall-clock limit (the %globaltimer register) and
@@ -144,7 +144,7 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
 }
 
 // Paired-SM form of the load: lands in this CTA's shared memory and completes its bytes on an
-// mbarrier of either CTA of the pair (`bar_cluster`, a shared::cluster address). No multicast.
+// mbarrier of either CTA of the pair (`bar_cluster`, a shared::cluster address); one destination.
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map,
                                                  uint32_t bar_cluster, int c0, int c1, int c2, int c3) {
   asm volatile(
