@@ -86,9 +86,6 @@ __global__ void norm_final_kernel(double* state, int parts) {
   state[1] = bad;
 }
 
-struct AdamWArgs {
-  double lr, beta1, beta2, eps, decay_factor, c1, c2, max_norm;
-};
 
 __device__ __forceinline__ void adamw_element(float& p, float g, float& m, float& v,
                                               const AdamWArgs& a, double clip) {
@@ -104,8 +101,11 @@ __device__ __forceinline__ void adamw_element(float& p, float g, float& m, float
 
 __global__ void __launch_bounds__(256)
 adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
-             float* __restrict__ v, uint64_t count, const double* __restrict__ state, AdamWArgs a,
-             int32_t* nonfinite_flag) {
+             float* __restrict__ v, uint64_t count, const double* __restrict__ state,
+             AdamWArgs args, const AdamWArgs* __restrict__ args_dev, int32_t* nonfinite_flag) {
+  // Scalars by value, or (args_dev != nullptr) from device memory, which a replayed CUDA graph
+  // reads afresh every step.
+  const AdamWArgs a = args_dev ? *args_dev : args;
   const double ssq = state[0];
   const bool bad = state[1] != 0.0 || !isfinite(ssq);
   if (bad) {
@@ -162,10 +162,8 @@ cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t s
   return cudaGetLastError();
 }
 
-cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double* norm_state,
-                         double max_norm, double lr, double beta1, double beta2, double eps,
-                         double weight_decay, uint64_t step, int32_t* nonfinite_flag, int device,
-                         cudaStream_t stream) {
+AdamWArgs adamw_args(double max_norm, double lr, double beta1, double beta2, double eps,
+                     double weight_decay, uint64_t step) {
   AdamWArgs a;
   a.lr = lr;
   a.beta1 = beta1;
@@ -175,13 +173,21 @@ cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double
   a.c1 = 1.0 - pow(beta1, static_cast<double>(step));
   a.c2 = 1.0 - pow(beta2, static_cast<double>(step));
   a.max_norm = max_norm;
+  return a;
+}
+
+cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double* norm_state,
+                         double max_norm, double lr, double beta1, double beta2, double eps,
+                         double weight_decay, uint64_t step, int32_t* nonfinite_flag, int device,
+                         cudaStream_t stream, const AdamWArgs* args_dev) {
+  const AdamWArgs a = adamw_args(max_norm, lr, beta1, beta2, eps, weight_decay, step);
   const int sms = sm_count(device);
   for (uint64_t i = 0; i < slice_count; ++i) {
     const Slice& s = slices[i];
     if (s.count == 0) continue;
     const unsigned grid = grid_for((s.count + 3) / 4, 256, sms * 8);
     adamw_kernel<<<grid, 256, 0, stream>>>(s.parameter, s.gradient, s.first_moment,
-                                           s.second_moment, s.count, norm_state, a,
+                                           s.second_moment, s.count, norm_state, a, args_dev,
                                            nonfinite_flag);
   }
   return cudaGetLastError();

@@ -135,10 +135,18 @@ struct Slice {
 };
 cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t slice_count,
                              int device, cudaStream_t stream);
+// AdamW scalars for one step (bias corrections c1 = 1 - beta1^step, c2 = 1 - beta2^step).
+struct AdamWArgs {
+  double lr, beta1, beta2, eps, decay_factor, c1, c2, max_norm;
+};
+AdamWArgs adamw_args(double max_norm, double lr, double beta1, double beta2, double eps,
+                     double weight_decay, uint64_t step);
+// args_dev != nullptr: the kernels read the scalars from that device struct instead of the
+// values given (so a captured launch can be replayed for later steps).
 cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double* norm_state,
                          double max_norm, double lr, double beta1, double beta2, double eps,
                          double weight_decay, uint64_t step, int32_t* nonfinite_flag, int device,
-                         cudaStream_t stream);
+                         cudaStream_t stream, const AdamWArgs* args_dev = nullptr);
 
 cudaError_t embedding_forward_launch(float* out, const float* weight, const int32_t* ids,
                                      uint64_t count, uint64_t vocab, uint64_t dim,

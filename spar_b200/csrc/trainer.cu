@@ -19,6 +19,7 @@
 // the named-parameter view below splits them back into Spar's q_proj/k_proj/v_proj tensors.
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -213,6 +214,23 @@ class LMTrainer {
   size_t ev_used = 0;
   std::vector<double> ev_flops;
   uint64_t launches = 0;  // kernels this runtime launched since the counter was reset
+  // CUDA-graph replay of whole training steps (zero gradients, micro-steps, clip + AdamW): one
+  // graph per micro-step count, captured on the second train_step call (the first runs eagerly
+  // and configures every kernel), replayed on an internal stream ordered after the caller's by
+  // events. AdamW's step-dependent scalars come from opt_args, refreshed before each replay.
+  struct StepGraph {
+    cudaGraphExec_t exec;
+    uint64_t launches;
+  };
+  std::map<uint64_t, StepGraph> graphs;
+  bool graphs_enabled = true;
+  uint64_t eager_steps = 0;
+  cudaStream_t exec_stream = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  AdamWArgs* opt_args = nullptr;       // device
+  AdamWArgs* opt_args_host = nullptr;  // pinned host
+  SparCudaStatus step_body(uint64_t micro_steps, float grad_scale, double lr, uint64_t step,
+                           cudaStream_t s, bool device_args);
 
   SparCudaStatus init(const SparB200LMConfig& c, int dev);
   ~LMTrainer();
@@ -236,6 +254,11 @@ LMTrainer::~LMTrainer() {
   if (tail_ev) cudaEventDestroy(tail_ev);
   if (comm_done) cudaEventDestroy(comm_done);
   if (comm_stream) cudaStreamDestroy(comm_stream);
+  for (auto& g : graphs) cudaGraphExecDestroy(g.second.exec);
+  if (exec_stream) cudaStreamDestroy(exec_stream);
+  if (ev_in) cudaEventDestroy(ev_in);
+  if (ev_out) cudaEventDestroy(ev_out);
+  if (opt_args_host) cudaFreeHost(opt_args_host);
   cudaFree(params);
   cudaFree(act_base);
 }
@@ -326,6 +349,7 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   plan.push_back({reinterpret_cast<void**>(&emb_scratch), embedding_backward_scratch(N, V)});
   plan.push_back({reinterpret_cast<void**>(&norm_state), kNormStateDoubles * sizeof(double)});
   plan.push_back({reinterpret_cast<void**>(&flags), 64});
+  plan.push_back({reinterpret_cast<void**>(&opt_args), sizeof(AdamWArgs)});
   plan.push_back({reinterpret_cast<void**>(&ids_dev), kMaxMicro * N * sizeof(int32_t)});
   if (c.precision == SPAR_B200_TF32X3) {
     // 3xTF32 splits both operands of every GEMM into hi/lo copies; size the workspace for the
@@ -370,6 +394,11 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     pos += (pb.second + 255) / 256 * 256;
   }
   e = cudaMemset(flags, 0, 64);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&exec_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+  if (e == cudaSuccess)
+    e = cudaMallocHost(reinterpret_cast<void**>(&opt_args_host), sizeof(AdamWArgs));
   if (e == cudaSuccess) e = rope_table_launch(rope_tab, T, dh, c.rope_theta, 0, 0);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return runtime(e);
@@ -465,6 +494,28 @@ cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
   SPAR_TRY(gemm(T, dh, T, A.p, T, false, v, ld, false, A.ctx, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, qkv_bs, ctx_bs));
   return cudaSuccess;
+}
+
+// One whole optimiser step on stream s with the token ids already in ids_dev: zero the gradient
+// arena, the micro-step sweeps, the global-norm pass and clip + AdamW (scalars by value, or from
+// opt_args when the launches are being captured for replay).
+SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, double lr,
+                                    uint64_t step, cudaStream_t s, bool device_args) {
+  cudaError_t e = cudaMemsetAsync(grads, 0, flat * sizeof(float), s);
+  if (e != cudaSuccess) return runtime(e);
+  for (uint64_t m = 0; m < micro_steps; ++m) {
+    last_micro = m + 1 == micro_steps;
+    const SparCudaStatus st = forward_backward(ids_dev + m * N, grad_scale, m, s);
+    if (st.code != 0) return st;
+  }
+  Slice slice{params, grads, m1, m2, flat};
+  launches += 3;
+  e = grad_norm_launch(norm_state, &slice, 1, device, s);
+  if (e == cudaSuccess)
+    e = adamw_launch(&slice, 1, norm_state, cfg.max_grad_norm, lr, cfg.beta1, cfg.beta2,
+                     cfg.adam_epsilon, cfg.weight_decay, step, flags + 1, device, s,
+                     device_args ? opt_args : nullptr);
+  return e == cudaSuccess ? ok() : runtime(e);
 }
 
 SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale, uint64_t micro,
@@ -781,24 +832,60 @@ extern "C" SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* i
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint64_t n_ids = micro_steps * t->N;
-  const int32_t* dev_ids = ids;
   cudaError_t e = cudaSuccess;
-  if (ids_on_host) {
+  // The step always reads its ids from ids_dev (fixed address, so a captured step replays).
+  if (ids_on_host)
     e = cudaMemcpyAsync(t->ids_dev, ids, n_ids * sizeof(int32_t), cudaMemcpyHostToDevice, s);
-    dev_ids = t->ids_dev;
-  }
-  if (e == cudaSuccess) e = cudaMemsetAsync(t->grads, 0, t->flat * sizeof(float), s);
+  else if (ids != t->ids_dev)
+    e = cudaMemcpyAsync(t->ids_dev, ids, n_ids * sizeof(int32_t), cudaMemcpyDeviceToDevice, s);
   if (e != cudaSuccess) return runtime(e);
   const double rows = static_cast<double>(t->B) * static_cast<double>(t->T - 1) *
                       static_cast<double>(micro_steps) * static_cast<double>(t->world);
   const float grad_scale = static_cast<float>(1.0 / rows);
-  for (uint64_t m = 0; m < micro_steps; ++m) {
-    t->last_micro = m + 1 == micro_steps;
-    const SparCudaStatus st = t->forward_backward(dev_ids + m * t->N, grad_scale, m, s);
+  if (!t->graphs_enabled || t->profiling || t->eager_steps == 0) {
+    const SparCudaStatus st = t->step_body(micro_steps, grad_scale, learning_rate, step, s, false);
     if (st.code != 0) return st;
+    ++t->eager_steps;
+  } else {
+    *t->opt_args_host = adamw_args(t->cfg.max_grad_norm, learning_rate, t->cfg.beta1,
+                                   t->cfg.beta2, t->cfg.adam_epsilon, t->cfg.weight_decay, step);
+    e = cudaMemcpyAsync(t->opt_args, t->opt_args_host, sizeof(AdamWArgs), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaEventRecord(t->ev_in, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(t->exec_stream, t->ev_in, 0);
+    if (e != cudaSuccess) return runtime(e);
+    auto it = t->graphs.find(micro_steps);
+    if (it == t->graphs.end()) {
+      const uint64_t before = t->launches;
+      cudaGraph_t graph = nullptr;
+      cudaGraphExec_t exec = nullptr;
+      e = cudaStreamBeginCapture(t->exec_stream, cudaStreamCaptureModeThreadLocal);
+      SparCudaStatus st = ok();
+      if (e == cudaSuccess) st = t->step_body(micro_steps, grad_scale, learning_rate, step, t->exec_stream, true);
+      const cudaError_t ce = cudaStreamEndCapture(t->exec_stream, &graph);
+      if (e == cudaSuccess && st.code == 0 && ce == cudaSuccess && graph)
+        e = cudaGraphInstantiate(&exec, graph, 0);
+      else if (e == cudaSuccess)
+        e = ce != cudaSuccess ? ce : cudaErrorStreamCaptureInvalidated;
+      if (graph) cudaGraphDestroy(graph);
+      const uint64_t captured = t->launches - before;
+      t->launches = before;
+      if (e != cudaSuccess || !exec) {
+        // Capture did not work here (e.g. a library refused it): run this and later steps eagerly.
+        cudaGetLastError();
+        t->graphs_enabled = false;
+        const SparCudaStatus es = t->step_body(micro_steps, grad_scale, learning_rate, step, s, false);
+        if (es.code != 0) return es;
+        goto done;
+      }
+      it = t->graphs.emplace(micro_steps, LMTrainer::StepGraph{exec, captured}).first;
+    }
+    e = cudaGraphLaunch(it->second.exec, t->exec_stream);
+    if (e == cudaSuccess) e = cudaEventRecord(t->ev_out, t->exec_stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, t->ev_out, 0);
+    if (e != cudaSuccess) return runtime(e);
+    t->launches += it->second.launches;
   }
-  SparCudaStatus st = spar_b200_lm_optimizer_step(handle, learning_rate, step, stream);
-  if (st.code != 0) return st;
+done:
   float sums[LMTrainer::kMaxMicro];
   double norm_state[2];
   int32_t flags[2];

@@ -131,3 +131,28 @@ def test_nonfinite_gradient_skips_update(cuda):
     assert flags[1] == 1 and not np.isfinite(norm)
     for n in params:
         np.testing.assert_array_equal(after[n], bad[n])
+
+
+def test_graph_replay_matches_eager_steps(cuda):
+    """train_step runs its first step eagerly, captures the second into a CUDA graph and replays
+    it afterwards (AdamW scalars refreshed from device memory): three steps must give the same
+    parameters, bit for bit, as three eager steps (profiling keeps a runtime eager)."""
+    from spar_b200.lm import C1, DecoderLM
+
+    params, ids = _setup(C1, 2)
+    outs, losses = [], []
+    for eager in (False, True):
+        lm = DecoderLM(C1, 0)
+        lm.load_state_dict(params)
+        if eager:
+            lm.profile(True)
+        ls = []
+        for step in range(1, 4):
+            loss, _, flags = lm.train_step(ids, 3e-4 * step, step=step)
+            assert flags == (0, 0)
+            ls.append(loss)
+        outs.append(_flat(lm.state_dict(), lm.names))
+        losses.append(ls)
+        lm.close()
+    assert losses[0] == losses[1]
+    assert np.array_equal(outs[0], outs[1])
