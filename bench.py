@@ -339,9 +339,9 @@ def main():
             result["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
     if rank == 0:
         print(json.dumps(result), flush=True)
+    lm.close()  # releases the captured step graphs (which hold NCCL calls) first
     if comm is not None:
         lib.spar_b200_comm_destroy(comm, 0)
-    lm.close()
     if pg:
         pg.destroy_process_group()
     return 0
