@@ -793,30 +793,82 @@ __global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo
   }
 }
 
-// Split-K reduction: C (+)= alpha * sum over splits of the partial tiles, summed in split order
-// (deterministic). part: [kparts][m][ldp].
-__global__ void splitk_reduce_kernel(float* __restrict__ c, uint64_t ldc,
-                                     const float* __restrict__ part, uint64_t ldp, uint32_t kparts,
-                                     uint32_t m, uint32_t n, float alpha, int accumulate) {
-  const uint32_t n4 = n / 4;
-  const uint64_t total = static_cast<uint64_t>(m) * n4;
-  const uint64_t plane = static_cast<uint64_t>(m) * ldp;
+// Split-K reduction and epilogue: the partial tiles [kparts][m][ldp] are summed in split order
+// (deterministic), then the GEMM's epilogue is applied exactly as the tile epilogue does it
+// (alpha, bias, residual / GELU' aux, bias + GELU with the pre-activation to aux, RoPE,
+// rounding to TF32, accumulate into C).
+struct SplitEpilogue {
+  float* c;
+  uint64_t ldc;
+  const float* part;
+  uint64_t ldp;
+  uint32_t kparts, m, n;
+  float alpha;
+  int accumulate, epilogue, round_out;
+  const float* bias;
+  float* aux;
+  uint64_t ldaux;
+  const float2* rope;
+  uint32_t rope_seq, rope_dim, rope_cols, rope_half;
+};
+
+__global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
+  const uint32_t n4 = q.n / 4;
+  const uint64_t total = static_cast<uint64_t>(q.m) * n4;
+  const uint64_t plane = static_cast<uint64_t>(q.m) * q.ldp;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  const bool bias = q.bias && (q.epilogue == SPAR_B200_EPI_BIAS ||
+                               q.epilogue == SPAR_B200_EPI_BIAS_GELU ||
+                               q.epilogue == SPAR_B200_EPI_BIAS_ADD);
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += stride) {
-    const uint64_t r = i / n4, c4 = i % n4;
-    const float* src = part + r * ldp + 4 * c4;
+    const uint64_t r = i / n4;
+    const uint32_t col = static_cast<uint32_t>(i % n4) * 4;
+    const float* src = q.part + r * q.ldp + col;
     float4 acc = *reinterpret_cast<const float4*>(src);
-    for (uint32_t s = 1; s < kparts; ++s) {
-      const float4 q = *reinterpret_cast<const float4*>(src + s * plane);
-      acc.x += q.x;
-      acc.y += q.y;
-      acc.z += q.z;
-      acc.w += q.w;
+    for (uint32_t s = 1; s < q.kparts; ++s) {
+      const float4 x = *reinterpret_cast<const float4*>(src + s * plane);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
     }
-    float4* dst = reinterpret_cast<float4*>(c + r * ldc + 4 * c4);
-    float4 o = make_float4(alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w);
-    if (accumulate) {
+    float v[4] = {q.alpha * acc.x, q.alpha * acc.y, q.alpha * acc.z, q.alpha * acc.w};
+    if (bias) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] += __ldg(q.bias + col + e);
+    }
+    float* auxp = q.aux ? q.aux + r * q.ldaux + col : nullptr;
+    if (q.epilogue == SPAR_B200_EPI_BIAS_ADD || q.epilogue == SPAR_B200_EPI_GELU_BWD) {
+      const float4 x = *reinterpret_cast<const float4*>(auxp);
+      const float a4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (q.epilogue == SPAR_B200_EPI_BIAS_ADD) v[e] += a4[e];
+        else v[e] *= gelu_derivative_fast(a4[e]);
+      }
+    } else if (q.epilogue == SPAR_B200_EPI_BIAS_GELU) {
+      *reinterpret_cast<float4*>(auxp) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = gelu_value_fast(v[e]);
+    }
+    if (q.rope && col < q.rope_cols) {
+      const float2* tab = q.rope + (r % q.rope_seq) * q.rope_half;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float2 cs = __ldg(tab + ((col + 2 * k) % q.rope_dim) / 2);
+        const float x0 = v[2 * k], x1 = v[2 * k + 1];
+        v[2 * k] = x0 * cs.x - x1 * cs.y;
+        v[2 * k + 1] = x0 * cs.y + x1 * cs.x;
+      }
+    }
+    if (q.round_out) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = round_tf32(v[e]);
+    }
+    float4* dst = reinterpret_cast<float4*>(q.c + r * q.ldc + col);
+    float4 o = make_float4(v[0], v[1], v[2], v[3]);
+    if (q.accumulate) {
       const float4 prev = *dst;
       o.x += prev.x;
       o.y += prev.y;
@@ -931,14 +983,15 @@ uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
   return 2 * b * (pad(a_inner) * a_rows + pad(b_inner) * b_rows);
 }
 
-// K splits worth using for this GEMM on `sms` SMs (1 = none): only plain products (no epilogue,
-// no causal limits, no batch, no 3xTF32) with at least 8 k-blocks per split. The persistent grid
+// K splits worth using for this GEMM on `units` parallel units (SMs, or SM pairs; 1 = none):
+// TF32 products without causal limits or batching, with at least 8 k-blocks per split (the
+// reduction kernel applies any epilogue). The persistent grid
 // runs ceil(tiles * parts / sms) rounds of 1/parts-sized work units; the split count with the
 // fewest full-tile-equivalent rounds wins when it saves at least 15% over no split.
 uint32_t splitk_parts(const SparB200Gemm& g, uint64_t tile_m, uint64_t tile_n, int units) {
-  if (g.precision != SPAR_B200_TF32 || g.epilogue != SPAR_B200_EPI_NONE || g.round_output ||
-      g.rope_table ||
-      g.causal != SPAR_B200_CAUSAL_NONE || (g.batch[0] > 1) || (g.batch[1] > 1) || g.n % 4)
+  // Any epilogue: the reduction applies it. Not for 3xTF32, causal or batched products.
+  if (g.precision != SPAR_B200_TF32 || g.causal != SPAR_B200_CAUSAL_NONE || (g.batch[0] > 1) ||
+      (g.batch[1] > 1) || g.n % 4)
     return 1;
   const uint64_t tiles = ((g.m + tile_m - 1) / tile_m) * ((g.n + tile_n - 1) / tile_n);
   const uint64_t kblocks = (g.k + BK - 1) / BK;
@@ -1077,10 +1130,28 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
                         : bn == 128 ? launch_kernel<128, 6, false>(p, device, stream)
                                     : launch_kernel<64, 8, false>(p, device, stream);
     if (e != cudaSuccess) return e;
+    SplitEpilogue q;
+    q.c = g.c;
+    q.ldc = g.ldc;
+    q.part = splitk_workspace;
+    q.ldp = ldp;
+    q.kparts = kparts;
+    q.m = static_cast<uint32_t>(g.m);
+    q.n = static_cast<uint32_t>(g.n);
+    q.alpha = g.alpha;
+    q.accumulate = g.accumulate;
+    q.epilogue = g.epilogue;
+    q.round_out = g.round_output != 0;
+    q.bias = g.bias;
+    q.aux = g.aux;
+    q.ldaux = g.ldaux;
+    q.rope = p.rope;
+    q.rope_seq = p.rope_seq;
+    q.rope_dim = p.rope_dim;
+    q.rope_cols = p.rope_cols;
+    q.rope_half = p.rope_half;
     const uint64_t work = g.m * (g.n / 4);
-    splitk_reduce_kernel<<<grid_for(work, 256, sm_count(device) * 8), 256, 0, stream>>>(
-        g.c, g.ldc, splitk_workspace, ldp, kparts, static_cast<uint32_t>(g.m),
-        static_cast<uint32_t>(g.n), g.alpha, g.accumulate);
+    splitk_reduce_kernel<<<grid_for(work, 256, sm_count(device) * 8), 256, 0, stream>>>(q);
     return cudaGetLastError();
   }
   if (split) return launch_kernel<64, 8, true>(p, device, stream);

@@ -373,12 +373,15 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     f(&split_ws, split_floats);
   }
   {
-    // Weight-gradient GEMMs whose outputs are small enough to be split along K (tokens).
-    struct Shape { uint64_t m, n; };
-    const Shape dw[] = {{d, 3 * d}, {d, d}, {d, F}, {F, d}, {V, d}};
-    for (const Shape& sh : dw) {
+    // Partial tiles of every product of the step that may be split along K (few output tiles
+    // for the SMs: the weight gradients, and the token-dimension products at small batches).
+    struct Shape { uint64_t m, n, k; };
+    const Shape shapes[] = {{N, 3 * d, d}, {N, d, d},     {N, F, d},  {N, d, F}, {N, V, d},
+                            {V, d, N},     {N, d, V},     {F, d, N},  {d, F, N}, {d, d, N},
+                            {d, 3 * d, N}, {N, d, 3 * d}};
+    for (const Shape& sh : shapes) {
       SparB200Gemm g{};
-      g.m = sh.m; g.n = sh.n; g.k = N; g.a_transposed = 1; g.batch[0] = g.batch[1] = 1;
+      g.m = sh.m; g.n = sh.n; g.k = sh.k; g.batch[0] = g.batch[1] = 1;
       g.precision = c.precision;
       splitk_floats = std::max(splitk_floats, gemm_splitk_workspace_floats(g, device));
     }

@@ -271,3 +271,54 @@ def test_gemm_many_tiles_per_sm_pair(cuda, epi):
     torch.cuda.synchronize()
     assert ops.gemm_error(0) == 0
     assert rel_l2(c.cpu().numpy(), expect) <= 2e-3
+
+
+@pytest.mark.parametrize("epi", ["bias", "bias_gelu", "gelu_bwd", "bias_add", "rope_round", "accumulate"])
+def test_gemm_split_k_with_epilogues(cuda, epi):
+    """Few output tiles and a long K: the product is split along K and the reduction kernel
+    applies the epilogue. Same results as the unsplit definition (fp64 reference)."""
+    import torch
+    from spar_b200 import ops
+    from oracle import spar_oracle as O
+
+    m, n, k = 512, 512, 8192
+    a, b, ref = _mats(m, n, k, False, False, seed=31)
+    at, bt = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    r = np.random.default_rng(32)
+    bias = r.standard_normal(n).astype(np.float32)
+    aux = r.standard_normal((m, n)).astype(np.float32)
+    biast, auxt = torch.from_numpy(bias).to(cuda), torch.from_numpy(aux).to(cuda)
+    tol = 2e-3
+    if epi == "bias":
+        got = ops.matmul(at, bt, epilogue=ops.EPI_BIAS, bias=biast)
+        expect = ref + bias
+    elif epi == "bias_gelu":
+        pre = torch.empty(m, n, device=cuda)
+        got = ops.matmul(at, bt, epilogue=ops.EPI_BIAS_GELU, bias=biast, aux=pre)
+        torch.cuda.synchronize()
+        assert rel_l2(pre.cpu().numpy(), ref + bias) <= tol
+        expect = O.gelu_forward(ref + bias, np.float64)
+    elif epi == "gelu_bwd":
+        got = ops.matmul(at, bt, epilogue=ops.EPI_GELU_BWD, aux=auxt)
+        expect = ref * O.gelu_derivative(aux)
+    elif epi == "bias_add":
+        got = ops.matmul(at, bt, epilogue=ops.EPI_BIAS_ADD, bias=biast, aux=auxt)
+        expect = ref + bias + aux
+    elif epi == "rope_round":
+        t, dh = 128, 64
+        tab = ops.rope_table(t, dh, 10000.0, device=cuda)
+        got = ops.matmul(at, bt, epilogue=ops.EPI_BIAS, bias=biast, round_output=True,
+                         rope=(tab, t, dh, 256))
+        plain = ops.matmul(at, bt, epilogue=ops.EPI_BIAS, bias=biast)
+        ops.rope_apply_(plain, tab, m // t, t, 4, dh, n)
+        torch.cuda.synchronize()
+        g = got.cpu().numpy()
+        assert np.array_equal(g.view(np.uint32) & 0x1FFF, np.zeros_like(g.view(np.uint32)))
+        expect = plain.cpu().numpy().astype(np.float64)
+    else:
+        got = auxt.clone()
+        ops.matmul(at, bt, out=got, accumulate=True, alpha=0.25)
+        expect = 0.25 * ref + aux
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+    assert rel_l2(got.cpu().numpy(), expect) <= tol
