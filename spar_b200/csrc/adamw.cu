@@ -30,6 +30,7 @@ int norm_blocks(int device) {
 __global__ void __launch_bounds__(512)
 norm_partial_kernel(double* __restrict__ state, const float* __restrict__ g, uint64_t count,
                     int first) {
+  pdl_begin();
   __shared__ double red[16];
   __shared__ int bad_any;
   if (threadIdx.x == 0) bad_any = 0;
@@ -75,6 +76,7 @@ norm_partial_kernel(double* __restrict__ state, const float* __restrict__ g, uin
 }
 
 __global__ void norm_final_kernel(double* state, int parts) {
+  pdl_begin();
   if (threadIdx.x != 0) return;
   double s = 0.0, bad = 0.0;
   const double* partial = state + kPartialBase;
@@ -103,6 +105,7 @@ __global__ void __launch_bounds__(256)
 adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
              float* __restrict__ v, uint64_t count, const double* __restrict__ state,
              AdamWArgs args, const AdamWArgs* __restrict__ args_dev, int32_t* nonfinite_flag) {
+  pdl_begin();
   // Scalars by value, or (args_dev != nullptr) from device memory, which a replayed CUDA graph
   // reads afresh every step.
   const AdamWArgs a = args_dev ? *args_dev : args;
@@ -149,7 +152,7 @@ cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t s
   bool first = true;
   for (uint64_t i = 0; i < slice_count; ++i) {
     if (slices[i].count == 0) continue;
-    norm_partial_kernel<<<parts, 512, 0, stream>>>(norm_state, slices[i].gradient,
+    launch(norm_partial_kernel, dim3(parts), dim3(512), 0, stream, norm_state, slices[i].gradient,
                                                    slices[i].count, first ? 1 : 0);
     first = false;
   }
@@ -158,7 +161,7 @@ cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t s
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
-  norm_final_kernel<<<1, 32, 0, stream>>>(norm_state, parts);
+  launch(norm_final_kernel, dim3(1), dim3(32), 0, stream, norm_state, parts);
   return cudaGetLastError();
 }
 
@@ -186,7 +189,7 @@ cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double
     const Slice& s = slices[i];
     if (s.count == 0) continue;
     const unsigned grid = grid_for((s.count + 3) / 4, 256, sms * 8);
-    adamw_kernel<<<grid, 256, 0, stream>>>(s.parameter, s.gradient, s.first_moment,
+    launch(adamw_kernel, dim3(grid), dim3(256), 0, stream, s.parameter, s.gradient, s.first_moment,
                                            s.second_moment, s.count, norm_state, a, args_dev,
                                            nonfinite_flag);
   }

@@ -256,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_begin();  // set-up done; global memory from here on
   const int dcol = static_cast<int>(p.model_dim);
 
   if (warp == 0) {
@@ -561,6 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_begin();  // set-up done; global memory from here on
   const int dcol = static_cast<int>(p.model_dim);
   const uint32_t seq = p.seq;
 
@@ -831,6 +833,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_begin();  // set-up done; global memory from here on
   const int dcol = static_cast<int>(p.model_dim);
   const uint32_t seq = p.seq;
   const uint32_t nq_all = (seq + 63) / 64;
@@ -1057,6 +1060,7 @@ __global__ void __launch_bounds__(256) attn_delta_kernel(float* __restrict__ del
                                                          const float* __restrict__ o, uint64_t rows,
                                                          uint32_t seq, uint32_t heads, uint32_t dh,
                                                          uint64_t ld) {
+  pdl_begin();
   const uint64_t w = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const uint32_t lane = threadIdx.x & 31;
   if (w >= rows * heads) return;
@@ -1075,8 +1079,8 @@ __global__ void __launch_bounds__(256) attn_delta_kernel(float* __restrict__ del
 
 // ============================================================================ host side
 template <typename K>
-cudaError_t launch(K kernel, uint32_t smem, const AttnParams& p, int device, cudaStream_t stream,
-                   bool* configured) {
+cudaError_t launch_attn(K kernel, uint32_t smem, const AttnParams& p, int device,
+                        cudaStream_t stream, bool* configured) {
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
   if (!configured[device]) {
     const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1086,8 +1090,7 @@ cudaError_t launch(K kernel, uint32_t smem, const AttnParams& p, int device, cud
   }
   const unsigned grid = std::min<uint32_t>(p.total, static_cast<uint32_t>(sm_count(device)));
   if (grid == 0) return cudaSuccess;
-  kernel<<<grid, kThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  return launch(kernel, dim3(grid), dim3(kThreads), smem, stream, p);
 }
 
 void base_params(AttnParams& p, uint64_t batch, uint64_t seq, uint64_t heads, uint64_t head_dim) {
@@ -1122,8 +1125,8 @@ cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_ma
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
   p.total = p.tiles * p.bh;
   static bool cfg32[64] = {}, cfg64[64] = {};
-  return head_dim == 64 ? launch(attn_fwd_kernel<64>, Fwd<64>::kSmem, p, device, stream, cfg64)
-                        : launch(attn_fwd_kernel<32>, Fwd<32>::kSmem, p, device, stream, cfg32);
+  return head_dim == 64 ? launch_attn(attn_fwd_kernel<64>, Fwd<64>::kSmem, p, device, stream, cfg64)
+                        : launch_attn(attn_fwd_kernel<32>, Fwd<32>::kSmem, p, device, stream, cfg32);
 }
 
 cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const float* dctx,
@@ -1150,18 +1153,20 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
   p.rope = reinterpret_cast<const float2*>(rope_table);
   static bool q32[64] = {}, q64[64] = {}, k32[64] = {}, k64[64] = {};
   const uint64_t warps = batch * seq * heads;
-  attn_delta_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
-      delta, dctx, ctx, batch * seq, static_cast<uint32_t>(seq), static_cast<uint32_t>(heads),
-      static_cast<uint32_t>(head_dim), d);
-  if (cudaGetLastError() != cudaSuccess) return cudaGetLastError();
+  cudaError_t e = launch(attn_delta_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)),
+                         dim3(256), 0, stream, delta, static_cast<const float*>(dctx),
+                         static_cast<const float*>(ctx), batch * seq,
+                         static_cast<uint32_t>(seq), static_cast<uint32_t>(heads),
+                         static_cast<uint32_t>(head_dim), static_cast<uint64_t>(d));
+  if (e != cudaSuccess) return e;
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
   p.total = p.tiles * p.bh;
-  cudaError_t e = head_dim == 64
-                      ? launch(attn_bwd_q_kernel<64>, BwdQ<64>::kSmem, p, device, stream, q64)
-                      : launch(attn_bwd_q_kernel<32>, BwdQ<32>::kSmem, p, device, stream, q32);
+  e = head_dim == 64
+          ? launch_attn(attn_bwd_q_kernel<64>, BwdQ<64>::kSmem, p, device, stream, q64)
+                      : launch_attn(attn_bwd_q_kernel<32>, BwdQ<32>::kSmem, p, device, stream, q32);
   if (e != cudaSuccess) return e;
-  return head_dim == 64 ? launch(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, p, device, stream, k64)
-                        : launch(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, p, device, stream, k32);
+  return head_dim == 64 ? launch_attn(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, p, device, stream, k64)
+                        : launch_attn(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, p, device, stream, k32);
 }
 
 namespace {

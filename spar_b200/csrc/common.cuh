@@ -8,6 +8,9 @@
 
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "spar_b200.h"
 
@@ -60,6 +63,46 @@ inline unsigned grid_for(uint64_t work, unsigned per_block, unsigned cap) {
   if (b < 1) b = 1;
   if (b > cap) b = cap;
   return static_cast<unsigned>(b);
+}
+
+// ------------------------------------------------------ programmatic dependent launches
+// Every kernel of the library is launched with programmatic stream serialization: its CTAs may
+// be scheduled while the previous kernel on the stream is still finishing, run their set-up
+// (barrier init, TMEM allocation), then block in pdl_wait() until that kernel has completed and
+// its memory is visible. pdl_wait() therefore comes before a kernel's first global-memory
+// access (read or write). pdl_trigger() lets the next kernel's launch begin once every CTA of
+// this one has passed its wait. Outside such a launch both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Both, in that order: the usual first statement of a kernel.
+__device__ __forceinline__ void pdl_begin() {
+  pdl_wait();
+  pdl_trigger();
+}
+
+// SPAR_B200_PDL=0 in the environment launches without the attribute (plain stream order).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SPAR_B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- device reductions

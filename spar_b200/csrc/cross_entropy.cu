@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(1024)
 ce_block_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                 const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes, uint64_t ld,
                 uint64_t seq, float grad_scale, int32_t* invalid) {
+  pdl_begin();
   __shared__ float scratch[32];
   const uint64_t vec = classes / 4;
   for (uint64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(256)
 ce_warp_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes, uint64_t ld,
                uint64_t seq, float grad_scale, int32_t* invalid) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const uint64_t vec = classes / 4;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * 8;
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(256)
 ce_generic_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                   const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes,
                   uint64_t ld, uint64_t seq, float grad_scale, int32_t* invalid) {
+  pdl_begin();
   __shared__ float scratch[32];
   for (uint64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     bool has_target;
@@ -202,7 +205,7 @@ cudaError_t cross_entropy_launch(float* loss, float* dlogits, const float* logit
     const uint64_t v = (vec + 31) / 32;
     const unsigned grid = grid_for(rows, 8, sms * 16);
     switch (v <= 1 ? 1 : v <= 2 ? 2 : v <= 4 ? 4 : v <= 8 ? 8 : 16) {
-#define SPAR_CE_W(V) case V: ce_warp_kernel<V><<<grid, 256, 0, stream>>>(loss, dlogits, logits, targets, rows, classes, ld, seq, grad_scale, invalid); break;
+#define SPAR_CE_W(V) case V: launch(ce_warp_kernel<V>, dim3(grid), dim3(256), 0, stream, loss, dlogits, logits, targets, rows, classes, ld, seq, grad_scale, invalid); break;
       SPAR_CE_W(1) SPAR_CE_W(2) SPAR_CE_W(4) SPAR_CE_W(8) SPAR_CE_W(16)
 #undef SPAR_CE_W
     }
@@ -210,13 +213,13 @@ cudaError_t cross_entropy_launch(float* loss, float* dlogits, const float* logit
     const uint64_t e = (vec + 1023) / 1024;
     const unsigned grid = grid_for(rows, 1, sms * 2);
     switch (e <= 4 ? 4 : e <= 8 ? 8 : e <= 12 ? 12 : 16) {
-#define SPAR_CE_B(E) case E: ce_block_kernel<E><<<grid, 1024, 0, stream>>>(loss, dlogits, logits, targets, rows, classes, ld, seq, grad_scale, invalid); break;
+#define SPAR_CE_B(E) case E: launch(ce_block_kernel<E>, dim3(grid), dim3(1024), 0, stream, loss, dlogits, logits, targets, rows, classes, ld, seq, grad_scale, invalid); break;
       SPAR_CE_B(4) SPAR_CE_B(8) SPAR_CE_B(12) SPAR_CE_B(16)
 #undef SPAR_CE_B
     }
   } else {
     const unsigned grid = grid_for(rows, 1, sms * 8);
-    ce_generic_kernel<<<grid, 256, 0, stream>>>(loss, dlogits, logits, targets, rows, classes, ld,
+    launch(ce_generic_kernel, dim3(grid), dim3(256), 0, stream, loss, dlogits, logits, targets, rows, classes, ld,
                                                 seq, grad_scale, invalid);
   }
   return cudaGetLastError();

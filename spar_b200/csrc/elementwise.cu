@@ -14,6 +14,7 @@ namespace {
 
 __global__ void gelu_forward_kernel(float4* __restrict__ y, const float4* __restrict__ x,
                                     uint64_t n4) {
+  pdl_begin();
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
        i += stride) {
@@ -25,6 +26,7 @@ __global__ void gelu_forward_kernel(float4* __restrict__ y, const float4* __rest
 
 __global__ void gelu_backward_kernel(float4* __restrict__ dx, const float4* __restrict__ dy,
                                      const float4* __restrict__ x, uint64_t n4) {
+  pdl_begin();
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
        i += stride) {
@@ -37,6 +39,7 @@ __global__ void gelu_backward_kernel(float4* __restrict__ dx, const float4* __re
 
 __global__ void gelu_tail_kernel(float* y, const float* dy, const float* x, uint64_t begin,
                                  uint64_t n, int backward) {
+  pdl_begin();
   const uint64_t i = begin + threadIdx.x;
   if (i >= n) return;
   y[i] = backward ? dy[i] * gelu_derivative(x[i]) : gelu_value(x[i]);
@@ -45,6 +48,7 @@ __global__ void gelu_tail_kernel(float* y, const float* dy, const float* x, uint
 // One thread per (position, pair): cos/sin of pos * theta^(-2i/D), computed in double.
 __global__ void rope_table_kernel(float2* table, uint64_t t, uint64_t half, uint64_t d,
                                   double theta, uint64_t start) {
+  pdl_begin();
   const uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= t * half) return;
   const uint64_t pos = idx / half, pair = idx % half;
@@ -58,6 +62,7 @@ __global__ void rope_table_kernel(float2* table, uint64_t t, uint64_t half, uint
 __global__ void rope_apply_kernel(float* __restrict__ x, const float2* __restrict__ table,
                                   uint64_t tokens, uint64_t t, uint64_t heads, uint64_t half,
                                   uint64_t ld, int inverse, int round) {
+  pdl_begin();
   const uint64_t pairs_per_token = heads * half;
   const uint64_t total = tokens * pairs_per_token;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
@@ -81,6 +86,7 @@ constexpr int kColWarps = 8;
 __global__ void __launch_bounds__(kColWarps * 32)
 column_sum_partial_kernel(float* __restrict__ partial, const float* __restrict__ x, uint64_t rows,
                           uint64_t cols, uint64_t ld, uint64_t rows_per_part) {
+  pdl_begin();
   __shared__ float4 red[kColWarps][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t col4 = static_cast<uint64_t>(blockIdx.x) * 32 + lane;  // float4 column index
@@ -113,6 +119,7 @@ column_sum_partial_kernel(float* __restrict__ partial, const float* __restrict__
 
 __global__ void column_sum_final_kernel(float* __restrict__ out, const float* __restrict__ partial,
                                         int parts, uint64_t cols, int accumulate) {
+  pdl_begin();
   const uint64_t c = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   float s = 0.f;
@@ -121,6 +128,7 @@ __global__ void column_sum_final_kernel(float* __restrict__ out, const float* __
 }
 
 __global__ void sum_kernel(float* out, const float* __restrict__ v, uint64_t n) {
+  pdl_begin();
   __shared__ double red[32];
   double s = 0.0;
   for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) s += static_cast<double>(v[i]);
@@ -142,21 +150,21 @@ cudaError_t gelu_launch(float* y, const float* dy, const float* x, uint64_t n, i
   if (n4 > 0) {
     const unsigned grid = grid_for(n4, 256, sm_count(device) * 16);
     if (backward)
-      gelu_backward_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<float4*>(y),
+      launch(gelu_backward_kernel, dim3(grid), dim3(256), 0, stream, reinterpret_cast<float4*>(y),
                                                      reinterpret_cast<const float4*>(dy),
                                                      reinterpret_cast<const float4*>(x), n4);
     else
-      gelu_forward_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<float4*>(y),
+      launch(gelu_forward_kernel, dim3(grid), dim3(256), 0, stream, reinterpret_cast<float4*>(y),
                                                     reinterpret_cast<const float4*>(x), n4);
   }
-  if (n % 4) gelu_tail_kernel<<<1, 32, 0, stream>>>(y, dy, x, n4 * 4, n, backward);
+  if (n % 4) launch(gelu_tail_kernel, dim3(1), dim3(32), 0, stream, y, dy, x, n4 * 4, n, backward);
   return cudaGetLastError();
 }
 
 cudaError_t rope_table_launch(float* table, uint64_t t, uint64_t d, double theta, uint64_t start,
                               cudaStream_t stream) {
   const uint64_t half = d / 2, n = t * half;
-  rope_table_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+  launch(rope_table_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream, 
       reinterpret_cast<float2*>(table), t, half, d, theta, start);
   return cudaGetLastError();
 }
@@ -166,7 +174,7 @@ cudaError_t rope_apply_launch(float* x, const float* table, uint64_t tokens, uin
                               cudaStream_t stream, int round) {
   const uint64_t half = d / 2;
   const unsigned grid = grid_for(tokens * heads * half, 256, sm_count(device) * 16);
-  rope_apply_kernel<<<grid, 256, 0, stream>>>(x, reinterpret_cast<const float2*>(table), tokens,
+  launch(rope_apply_kernel, dim3(grid), dim3(256), 0, stream, x, reinterpret_cast<const float2*>(table), tokens,
                                               t, heads, half, ld, inverse, round);
   return cudaGetLastError();
 }
@@ -186,15 +194,15 @@ cudaError_t column_sum_launch(float* out, const float* x, uint64_t rows, uint64_
   const int parts = column_sum_parts(rows, cols, device);
   const uint64_t rows_per_part = (rows + parts - 1) / parts;
   dim3 grid(static_cast<unsigned>((cols + 127) / 128), static_cast<unsigned>(parts));
-  column_sum_partial_kernel<<<grid, kColWarps * 32, 0, stream>>>(workspace, x, rows, cols, ld,
+  launch(column_sum_partial_kernel, dim3(grid), dim3(kColWarps * 32), 0, stream, workspace, x, rows, cols, ld,
                                                                  rows_per_part);
-  column_sum_final_kernel<<<static_cast<unsigned>((cols + 255) / 256), 256, 0, stream>>>(
+  launch(column_sum_final_kernel, dim3(static_cast<unsigned>((cols + 255) / 256)), dim3(256), 0, stream, 
       out, workspace, parts, cols, accumulate);
   return cudaGetLastError();
 }
 
 cudaError_t sum_launch(float* out, const float* v, uint64_t n, cudaStream_t stream) {
-  sum_kernel<<<1, 1024, 0, stream>>>(out, v, n);
+  launch(sum_kernel, dim3(1), dim3(1024), 0, stream, out, v, n);
   return cudaGetLastError();
 }
 

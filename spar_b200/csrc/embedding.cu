@@ -16,6 +16,7 @@ namespace {
 __global__ void embedding_forward_kernel(float4* __restrict__ out, const float4* __restrict__ w,
                                          const int32_t* __restrict__ ids, uint64_t count,
                                          uint64_t vocab, uint64_t dim4, int32_t* invalid) {
+  pdl_begin();
   const uint64_t total = count * dim4;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t idx = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
@@ -33,6 +34,7 @@ __global__ void embedding_forward_kernel(float4* __restrict__ out, const float4*
 
 __global__ void count_kernel(int32_t* counts, const int32_t* __restrict__ ids, uint64_t n,
                              uint64_t vocab) {
+  pdl_begin();
   const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int32_t id = ids[i];
@@ -42,6 +44,7 @@ __global__ void count_kernel(int32_t* counts, const int32_t* __restrict__ ids, u
 // Exclusive scan of counts[0, vocab) into offsets[0, vocab], single block.
 __global__ void __launch_bounds__(1024) scan_kernel(int32_t* offsets, const int32_t* counts,
                                                     uint64_t vocab) {
+  pdl_begin();
   __shared__ int32_t sums[1024];
   const uint64_t per = (vocab + blockDim.x - 1) / blockDim.x;
   const uint64_t b = per * threadIdx.x;
@@ -67,6 +70,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(int32_t* offsets, const int3
 
 __global__ void fill_kernel(int32_t* slots, int32_t* cursor, const int32_t* __restrict__ offsets,
                             const int32_t* __restrict__ ids, uint64_t n, uint64_t vocab) {
+  pdl_begin();
   const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int32_t id = ids[i];
@@ -78,6 +82,7 @@ __global__ void fill_kernel(int32_t* slots, int32_t* cursor, const int32_t* __re
 __global__ void rank_kernel(int32_t* sorted, const int32_t* __restrict__ slots,
                             const int32_t* __restrict__ offsets, const int32_t* __restrict__ ids,
                             uint64_t vocab) {
+  pdl_begin();
   const uint64_t s = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   // offsets[vocab] = number of valid ids = number of filled slots.
   if (s >= static_cast<uint64_t>(offsets[vocab])) return;
@@ -94,6 +99,7 @@ __global__ void __launch_bounds__(256)
 segment_reduce_kernel(float* __restrict__ gw, const float* __restrict__ go,
                       const int32_t* __restrict__ sorted, const int32_t* __restrict__ offsets,
                       uint64_t vocab, uint64_t dim) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * 8;
   const uint64_t dim4 = dim / 4;
@@ -126,7 +132,7 @@ cudaError_t embedding_forward_launch(float* out, const float* weight, const int3
                                      int32_t* invalid, int device, cudaStream_t stream) {
   const uint64_t dim4 = dim / 4;
   const unsigned grid = grid_for(count * dim4, 256, sm_count(device) * 16);
-  embedding_forward_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<float4*>(out),
+  launch(embedding_forward_kernel, dim3(grid), dim3(256), 0, stream, reinterpret_cast<float4*>(out),
                                                      reinterpret_cast<const float4*>(weight), ids,
                                                      count, vocab, dim4, invalid);
   return cudaGetLastError();
@@ -155,14 +161,14 @@ cudaError_t embedding_backward_launch(float* grad_weight, const float* grad_out,
   if (e == cudaSuccess) e = cudaMemsetAsync(cursor, 0, 4 * vocab, stream);
   if (e != cudaSuccess) return e;
   const unsigned gn = static_cast<unsigned>((count + 255) / 256);
-  count_kernel<<<gn, 256, 0, stream>>>(counts, ids, count, vocab);
-  scan_kernel<<<1, 1024, 0, stream>>>(offsets, counts, vocab);
-  fill_kernel<<<gn, 256, 0, stream>>>(slots, cursor, offsets, ids, count, vocab);
+  launch(count_kernel, dim3(gn), dim3(256), 0, stream, counts, ids, count, vocab);
+  launch(scan_kernel, dim3(1), dim3(1024), 0, stream, offsets, counts, vocab);
+  launch(fill_kernel, dim3(gn), dim3(256), 0, stream, slots, cursor, offsets, ids, count, vocab);
   // Invalid ids are skipped, so only offsets[vocab] <= count slots are filled; the rank kernel
   // reads that bound on the device.
-  rank_kernel<<<gn, 256, 0, stream>>>(sorted, slots, offsets, ids, vocab);
+  launch(rank_kernel, dim3(gn), dim3(256), 0, stream, sorted, slots, offsets, ids, vocab);
   const unsigned gv = grid_for(vocab, 8, sm_count(device) * 16);
-  segment_reduce_kernel<<<gv, 256, 0, stream>>>(grad_weight, grad_out, sorted, offsets, vocab,
+  launch(segment_reduce_kernel, dim3(gv), dim3(256), 0, stream, grad_weight, grad_out, sorted, offsets, vocab,
                                                 dim);
   return cudaGetLastError();
 }

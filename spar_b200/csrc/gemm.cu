@@ -309,6 +309,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_begin();  // set-up done; global memory from here on
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -542,15 +543,15 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
 // of the same name in both CTAs (two plain commits); both CTAs' epilogue warps arrive on the even
 // CTA's accumulator-empty barrier. Every wait is bounded; the closing cluster barrier keeps each
 // CTA (and its shared memory) alive until the even CTA has drained or given up.
-template <int STAGES, int EW>
+template <int BN, int STAGES, int EW>
 __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
-  constexpr int BN = 256;    // tile N, both CTAs
-  constexpr int BNH = 128;   // B rows (N) staged by each CTA
+  static_assert(BN == 256 || BN == 128, "paired tile N");
+  constexpr int BNH = BN / 2;  // B rows (N) staged by each CTA
   constexpr uint32_t A_BYTES = BM * BK * 4;
   constexpr uint32_t B_BYTES = BNH * BK * 4;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t kEpiBytes = epi_bytes(EW);
-  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulator buffers of BN columns
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -597,6 +598,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __g
   tc::cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrival
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_begin();  // set-up done; global memory from here on
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -776,6 +778,7 @@ __global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo
                                   const float* __restrict__ src, uint64_t inner, uint64_t rows,
                                   uint64_t b1, uint64_t b0, uint64_t ld, uint64_t bs1,
                                   uint64_t bs0, uint64_t out_ld) {
+  pdl_begin();
   const uint64_t total = inner * rows * b1 * b0;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -813,6 +816,7 @@ struct SplitEpilogue {
 };
 
 __global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
+  pdl_begin();
   const uint32_t n4 = q.n / 4;
   const uint64_t total = static_cast<uint64_t>(q.m) * n4;
   const uint64_t plane = static_cast<uint64_t>(q.m) * q.ldp;
@@ -933,24 +937,25 @@ cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) 
     if (device >= 0 && device < 64) configured[device] = true;
   }
   const unsigned grid = std::min<uint32_t>(p.total_tiles, static_cast<uint32_t>(sm_count(device)));
-  k<<<grid, threads_for(EW), smem, stream>>>(p);
-  return cudaGetLastError();
+  return launch(k, dim3(grid), dim3(threads_for(EW)), smem, stream, p);
 }
 
 // Paired-SM launch: clusters of two CTAs, at most as many clusters as fit at once.
-template <int STAGES, int EW>
+template <int BN, int STAGES, int EW>
 cudaError_t launch_pair(const GemmParams& p, int device, cudaStream_t stream) {
-  constexpr size_t smem = STAGES * (BM * BK * 4 + 128 * BK * 4) + epi_bytes(EW) + 1024 + 256;
+  constexpr size_t smem = STAGES * (BM * BK * 4 + (BN / 2) * BK * 4) + epi_bytes(EW) + 1024 + 256;
   static_assert(smem <= 232448, "paired GEMM shared memory");
   static int max_clusters[64] = {0};
-  auto k = gemm_pair_kernel<STAGES, EW>;
+  auto k = gemm_pair_kernel<BN, STAGES, EW>;
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(threads_for(EW));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -968,6 +973,7 @@ cudaError_t launch_pair(const GemmParams& p, int device, cudaStream_t stream) {
   }
   const uint32_t clusters = std::min<uint32_t>(p.total_tiles, static_cast<uint32_t>(max_clusters[device]));
   cfg.gridDim = dim3(2 * clusters);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, k, p);
 }
 
@@ -983,33 +989,58 @@ uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
   return 2 * b * (pad(a_inner) * a_rows + pad(b_inner) * b_rows);
 }
 
-// K splits worth using for this GEMM on `units` parallel units (SMs, or SM pairs; 1 = none):
-// TF32 products without causal limits or batching, with at least 8 k-blocks per split (the
-// reduction kernel applies any epilogue). The persistent grid
-// runs ceil(tiles * parts / sms) rounds of 1/parts-sized work units; the split count with the
-// fewest full-tile-equivalent rounds wins when it saves at least 15% over no split.
-uint32_t splitk_parts(const SparB200Gemm& g, uint64_t tile_m, uint64_t tile_n, int units) {
-  // Any epilogue: the reduction applies it. Not for 3xTF32, causal or batched products.
-  if (g.precision != SPAR_B200_TF32 || g.causal != SPAR_B200_CAUSAL_NONE || (g.batch[0] > 1) ||
-      (g.batch[1] > 1) || g.n % 4)
-    return 1;
-  const uint64_t tiles = ((g.m + tile_m - 1) / tile_m) * ((g.n + tile_n - 1) / tile_n);
-  const uint64_t kblocks = (g.k + BK - 1) / BK;
-  const uint64_t s = static_cast<uint64_t>(units);
-  double best = static_cast<double>((tiles + s - 1) / s);
-  uint32_t best_parts = 1;
-  for (uint64_t parts = 2; parts <= 8 && parts * 8 <= kblocks; ++parts) {
-    const double rounds = static_cast<double>((tiles * parts + s - 1) / s) / parts;
-    if (rounds < 0.85 * best) {
-      best = rounds;
-      best_parts = static_cast<uint32_t>(parts);
-    }
+// How a TF32 product runs, from a small timing model of the persistent kernels: tiles of
+// tile_m x tile_n on `units` parallel units (SM pairs or SMs) that each finish a tile of depth k in
+// 2 * tile_m * tile_n * k / rate + overhead, optionally split `parts` ways along K into partial
+// tiles that a reduction pass then streams (parts + 1 planes of m x n floats, plus the aux plane).
+// Rates and overheads are per unit, measured on B200 at C5 shapes.
+struct TileModel {
+  uint64_t tm, tn;
+  double rate;         // FLOP/s per unit
+  double overhead_us;  // per tile: accumulator hand-off, epilogue tail
+  int units;
+};
+
+double model_us(const SparB200Gemm& g, const TileModel& t, uint32_t parts) {
+  const uint64_t tiles = ((g.m + t.tm - 1) / t.tm) * ((g.n + t.tn - 1) / t.tn);
+  const uint64_t kb = (g.k + BK - 1) / BK;
+  const double kper = static_cast<double>((kb + parts - 1) / parts) * BK;
+  const double rounds = static_cast<double>((tiles * parts + t.units - 1) / t.units);
+  double us = rounds * (2.0 * t.tm * t.tn * kper / t.rate * 1e6 + t.overhead_us);
+  if (parts > 1) {
+    const bool aux_in = g.epilogue == SPAR_B200_EPI_BIAS_ADD || g.epilogue == SPAR_B200_EPI_GELU_BWD;
+    us += 3.0 + (parts + 1 + (aux_in ? 1 : 0)) * static_cast<double>(g.m) * g.n * 4.0 / 5.0e12 * 1e6;
   }
-  return best_parts;
+  return us;
 }
 
-// How a GEMM runs: wide unbatched TF32 products on SM pairs (256 x 256 tiles over 2-CTA
-// clusters), everything else (batched, causal, 3xTF32, narrow) on single SMs; either may split K.
+// Whether K may be split: TF32 products without causal limits or batching (the reduction pass
+// applies any epilogue).
+bool splittable(const SparB200Gemm& g) {
+  return g.precision == SPAR_B200_TF32 && g.causal == SPAR_B200_CAUSAL_NONE && g.batch[0] <= 1 &&
+         g.batch[1] <= 1 && g.n % 4 == 0;
+}
+
+// Fewest modelled microseconds over K splits 1..8 (at least 8 k-blocks per split) for tile model t.
+uint32_t best_parts(const SparB200Gemm& g, const TileModel& t, double* best_us) {
+  const uint64_t kblocks = (g.k + BK - 1) / BK;
+  uint32_t best = 1;
+  double us = model_us(g, t, 1);
+  if (splittable(g))
+    for (uint32_t parts = 2; parts <= 8 && parts * 8 <= kblocks; ++parts) {
+      const double u = model_us(g, t, parts);
+      if (u < 0.97 * us) {
+        us = u;
+        best = parts;
+      }
+    }
+  if (best_us) *best_us = us;
+  return best;
+}
+
+// How a GEMM runs: unbatched non-causal TF32 products with m >= 256 on SM pairs (256 x 256 or
+// 256 x 128 tiles over 2-CTA clusters, whichever the model finishes first), everything else
+// (batched, causal, 3xTF32, short) on single SMs; either may split K.
 struct GemmPlan {
   bool pair;
   int bn;
@@ -1017,14 +1048,33 @@ struct GemmPlan {
 };
 
 GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
-  const bool split = g.precision == SPAR_B200_TF32X3;
+  const bool x3 = g.precision == SPAR_B200_TF32X3;
   const uint64_t b = (g.batch[0] ? g.batch[0] : 1) * (g.batch[1] ? g.batch[1] : 1);
-  GemmPlan pl;
-  pl.bn = split ? 64 : (g.n > 128 ? 256 : (g.n > 64 ? 128 : 64));
-  pl.pair = !split && b == 1 && g.causal == SPAR_B200_CAUSAL_NONE && pl.bn == 256 && g.m >= 256;
   const int sms = sm_count(device);
-  pl.kparts = split ? 1 : (pl.pair ? splitk_parts(g, 256, 256, sms / 2)
-                                   : splitk_parts(g, BM, static_cast<uint64_t>(pl.bn), sms));
+  GemmPlan pl;
+  pl.pair = false;
+  pl.bn = x3 ? 64 : (g.n > 128 ? 256 : (g.n > 64 ? 128 : 64));
+  pl.kparts = 1;
+  if (x3) return pl;
+  if (b == 1 && g.causal == SPAR_B200_CAUSAL_NONE && g.m >= 256 && g.n > 64) {
+    const TileModel wide{256, 256, 10.0e12, 1.0, sms / 2};
+    const TileModel narrow{256, 128, 7.0e12, 1.0, sms / 2};  // half the reuse of each A stage
+    double us_wide = 1e30, us_narrow = 0.0;
+    uint32_t parts_wide = 1;
+    if (g.n > 128) parts_wide = best_parts(g, wide, &us_wide);
+    const uint32_t parts_narrow = best_parts(g, narrow, &us_narrow);
+    pl.pair = true;
+    if (us_wide <= us_narrow) {
+      pl.bn = 256;
+      pl.kparts = parts_wide;
+    } else {
+      pl.bn = 128;
+      pl.kparts = parts_narrow;
+    }
+    return pl;
+  }
+  const TileModel single{BM, static_cast<uint64_t>(pl.bn), pl.bn == 256 ? 5.0e12 : 3.5e12, 1.0, sms};
+  pl.kparts = best_parts(g, single, nullptr);
   return pl;
 }
 
@@ -1051,7 +1101,7 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   const uint64_t b_inner = g.b_transposed ? g.k : g.n, b_rows = g.b_transposed ? g.n : g.k;
   const bool pair = plan.pair;
   const uint32_t a_box_rows = p.a_mn_major ? BK : BM;
-  const uint32_t b_box_rows = p.b_mn_major ? BK : (pair ? 128u : static_cast<uint32_t>(bn));
+  const uint32_t b_box_rows = p.b_mn_major ? BK : static_cast<uint32_t>(pair ? bn / 2 : bn);
 
   if (!split) {
     if (!make_map(&p.a_map[0], g.a, a_inner, a_rows, b1, b0, g.lda, g.a_batch_stride[1],
@@ -1067,10 +1117,13 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     float* bh = al + b0 * b1 * a_ld * a_rows;
     float* bl = bh + b0 * b1 * b_ld * b_rows;
     const int sms = sm_count(device);
-    split_tf32_kernel<<<sms * 8, 256, 0, stream>>>(ah, al, g.a, a_inner, a_rows, b1, b0, g.lda,
-                                                   g.a_batch_stride[1], g.a_batch_stride[0], a_ld);
-    split_tf32_kernel<<<sms * 8, 256, 0, stream>>>(bh, bl, g.b, b_inner, b_rows, b1, b0, g.ldb,
-                                                   g.b_batch_stride[1], g.b_batch_stride[0], b_ld);
+    cudaError_t e = launch(split_tf32_kernel, dim3(sms * 8), dim3(256), 0, stream, ah, al, g.a,
+                           a_inner, a_rows, b1, b0, g.lda, g.a_batch_stride[1],
+                           g.a_batch_stride[0], a_ld);
+    if (e == cudaSuccess)
+      e = launch(split_tf32_kernel, dim3(sms * 8), dim3(256), 0, stream, bh, bl, g.b, b_inner,
+                 b_rows, b1, b0, g.ldb, g.b_batch_stride[1], g.b_batch_stride[0], b_ld);
+    if (e != cudaSuccess) return e;
     const uint64_t abs1 = a_ld * a_rows, abs0 = abs1 * b1;
     const uint64_t bbs1 = b_ld * b_rows, bbs0 = bbs1 * b1;
     const float* am[3] = {ah, ah, al};
@@ -1125,7 +1178,8 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
       return cudaErrorInvalidValue;
     p.kparts = kparts;
     p.total_tiles *= kparts;
-    const cudaError_t e = pair     ? launch_pair<6, 4>(p, device, stream)
+    const cudaError_t e = pair      ? (bn == 256 ? launch_pair<256, 6, 4>(p, device, stream)
+                                                 : launch_pair<128, 8, 4>(p, device, stream))
                         : bn == 256 ? launch_kernel<256, 4, false>(p, device, stream)
                         : bn == 128 ? launch_kernel<128, 6, false>(p, device, stream)
                                     : launch_kernel<64, 8, false>(p, device, stream);
@@ -1151,8 +1205,8 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     q.rope_cols = p.rope_cols;
     q.rope_half = p.rope_half;
     const uint64_t work = g.m * (g.n / 4);
-    splitk_reduce_kernel<<<grid_for(work, 256, sm_count(device) * 8), 256, 0, stream>>>(q);
-    return cudaGetLastError();
+    return launch(splitk_reduce_kernel, dim3(grid_for(work, 256, sm_count(device) * 8)), dim3(256),
+                  0, stream, q);
   }
   if (split) return launch_kernel<64, 8, true>(p, device, stream);
   // Epilogues with per-element work beyond a bias add (GELU, GELU', residual / aux tiles, RoPE)
@@ -1160,7 +1214,10 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   const bool heavy = g.epilogue == SPAR_B200_EPI_BIAS_GELU || g.epilogue == SPAR_B200_EPI_GELU_BWD ||
                      g.epilogue == SPAR_B200_EPI_BIAS_ADD || g.rope_table;
   if (pair)
-    return heavy ? launch_pair<5, 8>(p, device, stream) : launch_pair<6, 4>(p, device, stream);
+    return bn == 256 ? (heavy ? launch_pair<256, 5, 8>(p, device, stream)
+                              : launch_pair<256, 6, 4>(p, device, stream))
+                     : (heavy ? launch_pair<128, 6, 8>(p, device, stream)
+                              : launch_pair<128, 8, 4>(p, device, stream));
   if (heavy) {
     switch (bn) {
       case 256:

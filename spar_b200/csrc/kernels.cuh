@@ -99,7 +99,7 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
                                       const float* x, const float* gamma, const float* mean,
                                       const float* rstd, uint64_t rows, uint64_t cols,
                                       int accumulate_params, int accumulate_dx, float* workspace,
-                                      int device, cudaStream_t stream);
+                                      int device, cudaStream_t stream, float* dsum = nullptr);
 
 cudaError_t gelu_launch(float* y, const float* dy, const float* x, uint64_t n, int backward,
                         int device, cudaStream_t stream);

@@ -29,6 +29,7 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
                          float* __restrict__ rstd_out, const float* __restrict__ x,
                          const float* __restrict__ gamma, const float* __restrict__ beta,
                          uint64_t rows, int cols, float eps) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int vec_cols = cols >> 2;
   const float inv_cols = 1.0f / static_cast<float>(cols);
@@ -90,25 +91,31 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
 template <int VPL>
 __global__ void __launch_bounds__(kWarps * 32, VPL <= 8 ? 2 : 1)
 layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dgamma,
-                          float* __restrict__ partial_dbeta, const float* __restrict__ dy,
-                          const float* __restrict__ x, const float* __restrict__ gamma,
-                          const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
-                          uint64_t rows, int cols, uint64_t rows_per_block, int accumulate_dx) {
+                          float* __restrict__ partial_dbeta, float* __restrict__ partial_dsum,
+                          const float* __restrict__ dy, const float* __restrict__ x,
+                          const float* __restrict__ gamma, const float* __restrict__ mean_in,
+                          const float* __restrict__ rstd_in, uint64_t rows, int cols,
+                          uint64_t rows_per_block, int accumulate_dx) {
+  pdl_begin();
   // Per-warp dgamma / dbeta accumulators live in shared memory ([kWarps][cols] twice; lane l
   // owns float4 columns l, l + 32, ... of its warp's slice), which keeps the registers for the
-  // row in flight and lets two blocks share an SM.
+  // row in flight and lets two blocks share an SM. With partial_dsum, a third slice sums the
+  // stored dx rows: the column sums of dx (the bias gradient of the layer whose output dx is).
   extern __shared__ float smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int vec_cols = cols >> 2;
   const float inv_cols = 1.0f / static_cast<float>(cols);
+  const bool with_sum = partial_dsum != nullptr;
   float4* acc_g = reinterpret_cast<float4*>(smem + warp * cols);
   float4* acc_b = reinterpret_cast<float4*>(smem + (kWarps + warp) * cols);
+  float4* acc_s = reinterpret_cast<float4*>(smem + (2 * kWarps + warp) * cols);
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int f = lane + 32 * j;
     if (f < vec_cols) {
       acc_g[f] = make_float4(0.f, 0.f, 0.f, 0.f);
       acc_b[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (with_sum) acc_s[f] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
@@ -174,6 +181,14 @@ layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dg
           o.w += prev[j].w;
         }
         dxr[f] = o;
+        if (with_sum) {
+          float4 as = acc_s[f];
+          as.x += o.x;
+          as.y += o.y;
+          as.z += o.z;
+          as.w += o.w;
+          acc_s[f] = as;
+        }
       }
     }
   }
@@ -181,50 +196,58 @@ layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dg
   __syncthreads();
   const float* sg_ = smem;
   const float* sb_ = smem + kWarps * cols;
+  const float* ss_ = smem + 2 * kWarps * cols;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    float a = 0.f, bsum = 0.f;
+    float a = 0.f, bsum = 0.f, ssum = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       a += sg_[w * cols + c];
       bsum += sb_[w * cols + c];
+      if (with_sum) ssum += ss_[w * cols + c];
     }
     partial_dgamma[static_cast<uint64_t>(blockIdx.x) * cols + c] = a;
     partial_dbeta[static_cast<uint64_t>(blockIdx.x) * cols + c] = bsum;
+    if (with_sum) partial_dsum[static_cast<uint64_t>(blockIdx.x) * cols + c] = ssum;
   }
 }
 
-// Sums `parts` partial rows of length cols in a fixed order; out (+)= result. Block = 32 columns
-// x 8 warps: warp w sums parts w, w + 8, ... in increasing order, then warp 0 adds the eight
-// warp sums in warp order (deterministic).
-__global__ void __launch_bounds__(256)
-reduce_partials_kernel(float* __restrict__ out_a, float* __restrict__ out_b,
-                       const float* __restrict__ pa, const float* __restrict__ pb, int parts,
-                       int cols, int accumulate) {
-  __shared__ float sa[8][32], sb[8][32];
+// Sums `parts` partial rows of length cols in a fixed order; out (+)= result. blockIdx.y picks
+// the array (0: dgamma, 1: dbeta, 2: dx column sums). Block = 32 columns x 16 warps: warp w
+// sums parts w, w + 16, ... into four interleaved accumulators (independent loads in flight),
+// combined in a fixed order; warp 0 then adds the 16 warp sums in warp order (deterministic).
+struct PartialJobs {
+  float* out[3];
+  const float* part[3];
+  int accumulate[3];
+};
+
+constexpr int kReduceWarps = 16;
+
+__global__ void __launch_bounds__(kReduceWarps * 32)
+reduce_partials_kernel(const __grid_constant__ PartialJobs jobs, int parts, int cols) {
+  pdl_begin();
+  __shared__ float sums[kReduceWarps][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
-  float a = 0.f, b = 0.f;
-  if (c < cols)
-    for (int p = warp; p < parts; p += 8) {
-      a += pa[static_cast<uint64_t>(p) * cols + c];
-      b += pb[static_cast<uint64_t>(p) * cols + c];
+  const float* part = jobs.part[blockIdx.y];
+  float* out = jobs.out[blockIdx.y];
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (c < cols) {
+    int p = warp;
+    for (; p + 3 * kReduceWarps < parts; p += 4 * kReduceWarps) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += part[static_cast<uint64_t>(p + u * kReduceWarps) * cols + c];
     }
-  sa[warp][lane] = a;
-  sb[warp][lane] = b;
+    for (int u = 0; p < parts; p += kReduceWarps, ++u) acc[u] += part[static_cast<uint64_t>(p) * cols + c];
+  }
+  sums[warp][lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   __syncthreads();
   if (warp == 0 && c < cols) {
-    float ta = 0.f, tb = 0.f;
+    float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      ta += sa[w][lane];
-      tb += sb[w][lane];
-    }
-    if (accumulate) {
-      ta += out_a[c];
-      tb += out_b[c];
-    }
-    out_a[c] = ta;
-    out_b[c] = tb;
+    for (int w = 0; w < kReduceWarps; ++w) t += sums[w][lane];
+    if (jobs.accumulate[blockIdx.y]) t += out[c];
+    out[c] = t;
   }
 }
 
@@ -242,7 +265,8 @@ int vectors_per_lane(uint64_t cols) {
 
 }  // namespace
 
-// Number of partial rows the backward writes for `rows` (workspace = 2 * parts * cols floats).
+// Number of partial rows the backward writes for `rows` (workspace = 3 * parts * cols floats
+// with the dx column sums, 2 * parts * cols without).
 int layernorm_backward_parts(uint64_t rows, int device) {
   uint64_t parts = static_cast<uint64_t>(sm_count(device)) * 2;
   const uint64_t by_rows = (rows + kWarps - 1) / kWarps;
@@ -259,7 +283,7 @@ cudaError_t layernorm_forward_launch(float* y, float* mean, float* rstd, const f
   switch (vectors_per_lane(cols)) {
 #define SPAR_LN_FWD(V) \
   case V:              \
-    layernorm_forward_kernel<V><<<grid, kWarps * 32, 0, stream>>>(y, mean, rstd, x, gamma, beta, rows, c, eps); \
+    launch(layernorm_forward_kernel<V>, dim3(grid), dim3(kWarps * 32), 0, stream, y, mean, rstd, x, gamma, beta, rows, c, eps); \
     break;
     SPAR_LN_FWD(1) SPAR_LN_FWD(2) SPAR_LN_FWD(4) SPAR_LN_FWD(6) SPAR_LN_FWD(8) SPAR_LN_FWD(12)
     SPAR_LN_FWD(16)
@@ -274,21 +298,23 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
                                       const float* x, const float* gamma, const float* mean,
                                       const float* rstd, uint64_t rows, uint64_t cols,
                                       int accumulate_params, int accumulate_dx, float* workspace,
-                                      int device, cudaStream_t stream) {
+                                      int device, cudaStream_t stream, float* dsum) {
   const int parts = layernorm_backward_parts(rows, device);
   const uint64_t rows_per_block = (rows + parts - 1) / parts;
   const int c = static_cast<int>(cols);
-  const size_t smem = 2 * kWarps * cols * sizeof(float);
+  const int arrays = dsum ? 3 : 2;
+  const size_t smem = arrays * kWarps * cols * sizeof(float);
   float* pa = workspace;
   float* pb = workspace + static_cast<uint64_t>(parts) * cols;
+  float* ps = dsum ? workspace + 2 * static_cast<uint64_t>(parts) * cols : nullptr;
   switch (vectors_per_lane(cols)) {
 #define SPAR_LN_BWD(V)                                                                          \
   case V: {                                                                                    \
     auto k = layernorm_backward_kernel<V>;                                                     \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                                static_cast<int>(smem));                         \
-    k<<<parts, kWarps * 32, smem, stream>>>(dx, pa, pb, dy, x, gamma, mean, rstd, rows, c,     \
-                                            rows_per_block, accumulate_dx);                     \
+    launch(k, dim3(parts), dim3(kWarps * 32), smem, stream, dx, pa, pb, ps, dy, x, gamma, mean, \
+           rstd, rows, c, rows_per_block, accumulate_dx);                                       \
     break;                                                                                     \
   }
     SPAR_LN_BWD(1) SPAR_LN_BWD(2) SPAR_LN_BWD(4) SPAR_LN_BWD(6) SPAR_LN_BWD(8) SPAR_LN_BWD(12)
@@ -299,9 +325,9 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  reduce_partials_kernel<<<(c + 31) / 32, 256, 0, stream>>>(dgamma, dbeta, pa, pb, parts, c,
-                                                            accumulate_params);
-  return cudaGetLastError();
+  PartialJobs jobs = {{dgamma, dbeta, dsum}, {pa, pb, ps}, {accumulate_params, accumulate_params, 1}};
+  return launch(reduce_partials_kernel, dim3((c + 31) / 32, arrays), dim3(kReduceWarps * 32), 0,
+                stream, jobs, parts, c);
 }
 
 }  // namespace spar_b200
@@ -350,7 +376,7 @@ extern "C" SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma,
                                   2ull * parts * cols * sizeof(float), s);
   if (e != cudaSuccess) return runtime(e);
   e = layernorm_backward_launch(dx, dgamma, dbeta, dy, x, gamma, mean, rstd, rows, cols,
-                                accumulate_params, accumulate_dx, workspace, device, s);
+                                accumulate_params, accumulate_dx, workspace, device, s, nullptr);
   const cudaError_t f = cudaFreeAsync(workspace, s);
   if (e != cudaSuccess) return runtime(e);
   return f == cudaSuccess ? ok() : runtime(f);
@@ -419,6 +445,6 @@ extern "C" SparCudaStatus spar_b200_layernorm_backward_noalloc(
   cudaError_t e = scratch_address(device, &scratch);
   if (e != cudaSuccess) return runtime(e);
   e = layernorm_backward_launch(dx, dgamma, dbeta, dy, x, gamma, mean, rstd, rows, cols,
-                                accumulate_params, accumulate_dx, scratch, device, s);
+                                accumulate_params, accumulate_dx, scratch, device, s, nullptr);
   return e == cudaSuccess ? ok() : runtime(e);
 }

@@ -29,6 +29,7 @@ template <int VPL>
 __global__ void __launch_bounds__(kWarps * 32)
 causal_softmax_forward_kernel(float* __restrict__ p, const float* __restrict__ s, uint64_t rows,
                               uint64_t t, uint64_t ld, float scale, uint64_t zblock) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kWarps;
   for (uint64_t r = static_cast<uint64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); r < rows;
@@ -96,6 +97,7 @@ __global__ void __launch_bounds__(kWarps * 32)
 causal_softmax_backward_kernel(float* ds, const float* dp, const float* __restrict__ p,
                                uint64_t rows, uint64_t t, uint64_t ld, float scale,
                                uint64_t zblock) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kWarps;
   for (uint64_t r = static_cast<uint64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); r < rows;
@@ -160,11 +162,11 @@ cudaError_t causal_softmax_launch(float* out, const float* in, const float* p, u
 #define SPAR_SMX(V)                                                                              \
   case V:                                                                                       \
     if (backward)                                                                               \
-      causal_softmax_backward_kernel<V><<<grid, kWarps * 32, 0, stream>>>(out, in, p, rows, t,  \
+      launch(causal_softmax_backward_kernel<V>, dim3(grid), dim3(kWarps * 32), 0, stream, out, in, p, rows, t,  \
                                                                           ld, scale,            \
                                                                           zero_fill_block);     \
     else                                                                                        \
-      causal_softmax_forward_kernel<V><<<grid, kWarps * 32, 0, stream>>>(out, in, rows, t, ld, \
+      launch(causal_softmax_forward_kernel<V>, dim3(grid), dim3(kWarps * 32), 0, stream, out, in, rows, t, ld, \
                                                                          scale,                 \
                                                                          zero_fill_block);      \
     break;

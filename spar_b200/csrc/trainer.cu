@@ -341,7 +341,7 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   f(&dqkv, N * 3 * d);
   f(&dS, fused_attention ? B * H * T : PS);
   f(&du, N * F);
-  f(&ln_ws, 2ull * ln_parts * d);
+  f(&ln_ws, 3ull * ln_parts * d);  // dgamma, dbeta and dx column-sum partials
   f(&col_ws, col_floats);
   f(&rope_tab, T * dh);
   f(&row_loss, N);
@@ -571,8 +571,10 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
                   nullptr, nullptr, 0, s));
   SPAR_CHECK(gemm(N, d, V, logits, Vp, false, P + off_E, d, false, dtmp, d, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+  // The final norm's dx is dL/d(last block output): its column sums are that block's b2 gradient.
   SPAR_CHECK(layernorm_backward_launch(dres, G + off_lnf_g, G + off_lnf_b, dtmp, xL,
-                                       P + off_lnf_g, meanf, rstdf, N, d, 1, 0, ln_ws, device, s));
+                                       P + off_lnf_g, meanf, rstdf, N, d, 1, 0, ln_ws, device, s,
+                                       G + lay[L - 1].b2));
   for (uint64_t l = L; l-- > 0;) {
     SPAR_CHECK(layer_backward(l, s));
   }
@@ -628,12 +630,13 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   const LayerOffsets& lo = lay[l];
   float* P = params;
   float* G = grads;
-  launches += 4 * 2 + 2 * 2 + 1 + (cfg.use_rope && !fused_attention ? 1 : 0);  // col sums, LN bwd, softmax bwd, rope
+  launches += 2 * 2 + 2 * 2 + 1 + (cfg.use_rope && !fused_attention ? 1 : 0);  // col sums, LN bwd, softmax bwd, rope
   // dres = dL/d(layer output) = dL/d(h1 + mlp)
-  // MLP: mlp = g W2 + b2, g = gelu(u), u = a2 W1 + b1
+  // MLP: mlp = g W2 + b2, g = gelu(u), u = a2 W1 + b1. The b2 gradient (column sums of dres)
+  // came out of the LayerNorm backward that produced dres (the next block's LN1, or the final
+  // norm).
   SPAR_TRY(gemm(F, d, N, A.g, F, true, dres, d, false, G + lo.w2, d, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
-  SPAR_TRY(column_sum_launch(G + lo.b2, dres, N, d, d, 1, col_ws, device, s));
   SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, du, F, false, SPAR_B200_EPI_GELU_BWD,
                 nullptr, A.u, F, s));
   SPAR_TRY(gemm(d, F, N, A.a2, d, true, du, F, false, G + lo.w1, F, true, SPAR_B200_EPI_NONE,
@@ -641,13 +644,12 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   SPAR_TRY(column_sum_launch(G + lo.b1, du, N, F, F, 1, col_ws, device, s));
   SPAR_TRY(gemm(N, d, F, du, F, false, P + lo.w1, F, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
-  // dres += LN2 backward  ->  dL/dh1
+  // dres += LN2 backward  ->  dL/dh1, whose column sums are the bo gradient
   SPAR_TRY(layernorm_backward_launch(dres, G + lo.ln2_g, G + lo.ln2_b, dtmp, A.h1, P + lo.ln2_g,
-                                     A.mean2, A.rstd2, N, d, 1, 1, ln_ws, device, s));
+                                     A.mean2, A.rstd2, N, d, 1, 1, ln_ws, device, s, G + lo.bo));
   // out projection: h1 = x + ctx Wo + bo
   SPAR_TRY(gemm(d, d, N, A.ctx, d, true, dres, d, false, G + lo.wo, d, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
-  SPAR_TRY(column_sum_launch(G + lo.bo, dres, N, d, d, 1, col_ws, device, s));
   SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
                 fused_attention));
@@ -663,9 +665,11 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   SPAR_TRY(column_sum_launch(G + lo.bqkv, dqkv, N, 3 * d, ld, 1, col_ws, device, s));
   SPAR_TRY(gemm(N, d, 3 * d, dqkv, ld, false, P + lo.wqkv, ld, true, dtmp, d, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
-  // dres += LN1 backward -> dL/dx
+  // dres += LN1 backward -> dL/dx = dL/d(previous block output): its column sums are the
+  // previous block's b2 gradient
   SPAR_TRY(layernorm_backward_launch(dres, G + lo.ln1_g, G + lo.ln1_b, dtmp, A.x, P + lo.ln1_g,
-                                     A.mean1, A.rstd1, N, d, 1, 1, ln_ws, device, s));
+                                     A.mean1, A.rstd1, N, d, 1, 1, ln_ws, device, s,
+                                     l > 0 ? G + lay[l - 1].b2 : nullptr));
   if (comm && last_micro) {
     // This layer's gradients are final: reduce them on the communication stream while the
     // remaining layers run backward (bucket = one block's contiguous parameter range).

@@ -28,14 +28,31 @@ def peaks():
 
 
 def timed(fn, iters=10, warmup=3):
+    """Milliseconds per call: `iters` calls captured in one CUDA graph and replayed, so host-side
+    launch and allocation overhead is not timed (eager timing if the call cannot be captured)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(iters):
-        fn()
-    b.record()
+    try:
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            fn()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(iters):
+                    fn()
+        g.replay()
+        torch.cuda.synchronize()
+        a.record()
+        g.replay()
+        b.record()
+    except RuntimeError:
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b) / iters
 
@@ -92,8 +109,15 @@ def run_bandwidth(name, iters=10):
         dy = torch.randn_like(x)
         g = torch.ones(1024, device=dev)
         _, mean, rstd = ops.layer_norm_forward(x, g, torch.zeros_like(g))
-        return report("layernorm_bwd 16384x1024", timed(lambda: ops.layer_norm_backward(dy, x, g, mean, rstd), iters),
-                      12 * x.numel(), "GB/s", hbm)
+        report("layernorm_fwd 16384x1024", timed(lambda: ops.layer_norm_forward(x, g, g), iters),
+               8 * x.numel(), "GB/s", hbm)
+        # As in the training step: dx accumulates into the residual-stream gradient (read + write).
+        dx = torch.zeros_like(x)
+        dg, db = torch.empty_like(g), torch.empty_like(g)
+        return report("layernorm_bwd 16384x1024",
+                      timed(lambda: ops.layer_norm_backward(dy, x, g, mean, rstd, dg, db, dx,
+                                                            accumulate_dx=True), iters),
+                      16 * x.numel(), "GB/s", hbm)
     if name == "gelu_bwd":
         x = torch.randn(16384, 4096, device=dev)
         dy = torch.randn_like(x)

@@ -98,10 +98,12 @@ def test_gemm_epilogues(cuda):
     assert rel_err(radd_nb.cpu().numpy(), ref + r) <= 1e-5
 
 
-@pytest.mark.parametrize("m,n,k", [(1024, 1024, 16384), (1024, 3072, 8192), (768, 768, 4096)])
+@pytest.mark.parametrize("m,n,k", [(1024, 1024, 16384), (1024, 3072, 8192), (768, 768, 4096),
+                                   (300, 196, 8192), (200, 100, 6144)])
 def test_gemm_split_k_weight_gradient(cuda, m, n, k):
     """Weight-gradient shapes (A transposed, K = tokens) take the split-K path: partial tiles
-    summed in split order, so accumulate + alpha hold and repeated runs are bitwise equal."""
+    summed in split order, so accumulate + alpha hold and repeated runs are bitwise equal.
+    Ragged shapes cover clipped rows/columns on the paired and the single-SM kernels."""
     import torch
     from spar_b200 import ops
 
@@ -244,15 +246,17 @@ def test_gemm_rope_epilogue(cuda):
         np.testing.assert_allclose(fused.cpu().numpy(), plain.cpu().numpy(), rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("shape", [(4096, 3072, 288), (16384, 1024, 288), (6144, 1000, 160)])
 @pytest.mark.parametrize("epi", ["none", "bias_gelu", "bias_add"])
-def test_gemm_many_tiles_per_sm_pair(cuda, epi):
-    """More 256 x 256 tiles than SM pairs, so every persistent CTA pair runs several tiles and
-    cycles both TMEM accumulators and the operand-stage ring (plain and eight-warp epilogues)."""
+def test_gemm_many_tiles_per_sm_pair(cuda, epi, shape):
+    """More paired tiles (256 x 256, or 256 x 128 for the narrower outputs) than SM pairs, so every
+    persistent CTA pair runs several tiles and cycles both TMEM accumulators and the operand-stage
+    ring (plain and eight-warp epilogues; a ragged N on the last shape)."""
     import torch
     from spar_b200 import ops
     from oracle import spar_oracle as O
 
-    m, n, k = 4096, 3072, 288
+    m, n, k = shape
     a, b, ref = _mats(m, n, k, False, False, seed=23)
     at, bt = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
     r = np.random.default_rng(24)
