@@ -1055,25 +1055,33 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
 // ============================================================================ D = rowsum(dO o O)
 // One warp per (token row, head): the dot product of the head's dO and O slices (coalesced 128-
 // and 256-byte reads), written as D[(b * heads + h) * seq + t] for the backward kernels.
+// D[b, h, t] = sum over the head's columns of dO * O: one warp per token row covering every head
+// with coalesced float4 loads (lane l takes float4 chunks l, l + 32, ...); the dh / 4 lanes that
+// hold one head's chunks combine their products with butterfly shuffles.
 __global__ void __launch_bounds__(256) attn_delta_kernel(float* __restrict__ delta,
                                                          const float* __restrict__ d_o,
                                                          const float* __restrict__ o, uint64_t rows,
                                                          uint32_t seq, uint32_t heads, uint32_t dh,
                                                          uint64_t ld) {
   pdl_begin();
-  const uint64_t w = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t row = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const uint32_t lane = threadIdx.x & 31;
-  if (w >= rows * heads) return;
-  const uint64_t row = w / heads;
-  const uint32_t h = static_cast<uint32_t>(w - row * heads);
-  const float* a = d_o + row * ld + static_cast<uint64_t>(h) * dh;
-  const float* b = o + row * ld + static_cast<uint64_t>(h) * dh;
-  float acc = 0.f;
-  for (uint32_t c = lane; c < dh; c += 32) acc += __ldg(a + c) * __ldg(b + c);
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    const uint64_t bb = row / seq, t = row - bb * seq;
-    delta[(bb * heads + h) * seq + t] = acc;
+  if (row >= rows) return;
+  const uint32_t group = dh / 4;  // lanes per head: 8, 16 or 32
+  const uint32_t n4 = heads * group;
+  const float4* a = reinterpret_cast<const float4*>(d_o + row * ld);
+  const float4* b = reinterpret_cast<const float4*>(o + row * ld);
+  const uint64_t bb = row / seq, t = row - bb * seq;
+#pragma unroll 4
+  for (uint32_t f0 = 0; f0 < n4; f0 += 32) {
+    const uint32_t f = f0 + lane;
+    float acc = 0.f;
+    if (f < n4) {
+      const float4 x = __ldg(a + f), y = __ldg(b + f);
+      acc = (x.x * y.x + x.y * y.y) + (x.z * y.z + x.w * y.w);
+    }
+    for (uint32_t off = group / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (f < n4 && lane % group == 0) delta[(bb * heads + f / group) * seq + t] = acc;
   }
 }
 
@@ -1152,7 +1160,7 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
   p.delta = delta;
   p.rope = reinterpret_cast<const float2*>(rope_table);
   static bool q32[64] = {}, q64[64] = {}, k32[64] = {}, k64[64] = {};
-  const uint64_t warps = batch * seq * heads;
+  const uint64_t warps = batch * seq;  // one per token row
   cudaError_t e = launch(attn_delta_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)),
                          dim3(256), 0, stream, delta, static_cast<const float*>(dctx),
                          static_cast<const float*>(ctx), batch * seq,

@@ -7,8 +7,8 @@
 // nll_gradient), g = 1/N. This kernel evaluates exactly that per row, without materialising
 // logp or a zeroed [rows, V] gradient: one read of the logits row, one write of dlogits.
 //
-// Large vocabularies: one 1024-thread block per row with the row held in registers
-// (EPT float4 per thread). Small vocabularies: one warp per row.
+// Large vocabularies: one block per row streaming the row twice (the second read from L2).
+// Small vocabularies: one warp per row with the row in registers.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -26,13 +26,30 @@ __device__ __forceinline__ int row_target(const int32_t* targets, uint64_t r, ui
   return *has_target ? targets[r + 1] : 0;
 }
 
-template <int EPT>
-__global__ void __launch_bounds__(1024)
-ce_block_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
-                const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes, uint64_t ld,
-                uint64_t seq, float grad_scale, int32_t* invalid) {
+// Large vocabularies: one 256-thread block per row, two passes over the row. Pass 1 keeps a
+// running (max, sum of exponentials) per thread over batches of eight float4 (one rescale per
+// batch); the block combines the pairs in a fixed order. Pass 2 reads the row again (an L2 hit:
+// only a few rows per SM are in flight) and writes dlogits. With several rows per SM, one row's
+// loads overlap another's arithmetic; a row held in registers (128 KB at 32K classes, half the
+// register file) would allow one row per SM and leave its memory idle during the reductions.
+constexpr int kCeThreads = 256;
+constexpr int kCeBatch = 8;
+
+// (m, s) <- the pair for the union of two sets, s relative to the larger maximum.
+__device__ __forceinline__ void ms_combine(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  s = (m == -INFINITY ? 0.f : s * expf(m - mn)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - mn));
+  m = mn;
+}
+
+__global__ void __launch_bounds__(kCeThreads, 3)
+ce_stream_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
+                 const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes, uint64_t ld,
+                 uint64_t seq, float grad_scale, int32_t* invalid) {
   pdl_begin();
-  __shared__ float scratch[32];
+  __shared__ float part_m[kCeThreads / 32], part_s[kCeThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t vec = classes / 4;
   for (uint64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     bool has_target;
@@ -41,52 +58,76 @@ ce_block_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
     const float4* zr = reinterpret_cast<const float4*>(logits + r * ld);
     float4* dr = reinterpret_cast<float4*>(dlogits + r * ld);
     if (!has_target || bad) {
-      for (uint64_t f = threadIdx.x; f < vec; f += blockDim.x) dr[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (uint64_t f = threadIdx.x; f < vec; f += kCeThreads) dr[f] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (threadIdx.x == 0) {
         loss[r] = bad ? NAN : 0.f;
         if (bad) atomicExch(invalid, 1);
       }
       continue;
     }
-    float4 v[EPT];
-    float m = -INFINITY;
+    // Pass 1: running maximum and sum of exponentials relative to it.
+    float m = -INFINITY, s = 0.f;
+    for (uint64_t f0 = threadIdx.x; f0 < vec; f0 += kCeThreads * kCeBatch) {
+      float4 x[kCeBatch];
+      float bm = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < EPT; ++j) {
-      const uint64_t f = threadIdx.x + 1024ull * j;
-      if (f < vec) {
-        v[j] = ld_stream(zr + f);
-        m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+      for (int u = 0; u < kCeBatch; ++u) {
+        const uint64_t f = f0 + static_cast<uint64_t>(u) * kCeThreads;
+        x[u] = f < vec ? __ldcg(zr + f) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        bm = fmaxf(bm, fmaxf(fmaxf(x[u].x, x[u].y), fmaxf(x[u].z, x[u].w)));
       }
-    }
-    m = block_max(m, scratch);
-    float s = 0.f;
+      const float mn = fmaxf(m, bm);
+      if (mn == -INFINITY) continue;
+      float bs = 0.f;
 #pragma unroll
-    for (int j = 0; j < EPT; ++j) {
-      const uint64_t f = threadIdx.x + 1024ull * j;
-      if (f < vec)
-        s += (expf(v[j].x - m) + expf(v[j].y - m)) + (expf(v[j].z - m) + expf(v[j].w - m));
+      for (int u = 0; u < kCeBatch; ++u)
+        bs += (expf(x[u].x - mn) + expf(x[u].y - mn)) + (expf(x[u].z - mn) + expf(x[u].w - mn));
+      s = (m == -INFINITY ? 0.f : s * expf(m - mn)) + bs;
+      m = mn;
     }
-    s = block_sum(s, scratch);
-    const float log_sum = logf(s);
 #pragma unroll
-    for (int j = 0; j < EPT; ++j) {
-      const uint64_t f = threadIdx.x + 1024ull * j;
-      if (f < vec) {
-        const uint64_t c = 4 * f;
-        float4 o;
-        o.x = grad_scale * (expf((v[j].x - m) - log_sum) - (c == (uint64_t)target ? 1.f : 0.f));
-        o.y = grad_scale * (expf((v[j].y - m) - log_sum) - (c + 1 == (uint64_t)target ? 1.f : 0.f));
-        o.z = grad_scale * (expf((v[j].z - m) - log_sum) - (c + 2 == (uint64_t)target ? 1.f : 0.f));
-        o.w = grad_scale * (expf((v[j].w - m) - log_sum) - (c + 3 == (uint64_t)target ? 1.f : 0.f));
-        if (c <= (uint64_t)target && (uint64_t)target < c + 4) {
-          const float zt = target == c ? v[j].x : target == c + 1 ? v[j].y
-                         : target == c + 2 ? v[j].z : v[j].w;
-          loss[r] = -((zt - m) - log_sum);
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      ms_combine(m, s, m2, s2);
+    }
+    if (lane == 0) {
+      part_m[warp] = m;
+      part_s[warp] = s;
+    }
+    __syncthreads();
+    float M = part_m[0], S = part_s[0];
+#pragma unroll
+    for (int w = 1; w < kCeThreads / 32; ++w) ms_combine(M, S, part_m[w], part_s[w]);
+    const float log_sum = logf(S);
+    // Pass 2: dlogits = g * (softmax - onehot), the row's last read.
+    for (uint64_t f0 = threadIdx.x; f0 < vec; f0 += kCeThreads * kCeBatch) {
+      float4 x[kCeBatch];
+#pragma unroll
+      for (int u = 0; u < kCeBatch; ++u) {
+        const uint64_t f = f0 + static_cast<uint64_t>(u) * kCeThreads;
+        if (f < vec) x[u] = ld_stream(zr + f);
+      }
+#pragma unroll
+      for (int u = 0; u < kCeBatch; ++u) {
+        const uint64_t f = f0 + static_cast<uint64_t>(u) * kCeThreads;
+        if (f < vec) {
+          const uint64_t c = 4 * f;
+          float4 o;
+          o.x = grad_scale * (expf((x[u].x - M) - log_sum) - (c == (uint64_t)target ? 1.f : 0.f));
+          o.y = grad_scale * (expf((x[u].y - M) - log_sum) - (c + 1 == (uint64_t)target ? 1.f : 0.f));
+          o.z = grad_scale * (expf((x[u].z - M) - log_sum) - (c + 2 == (uint64_t)target ? 1.f : 0.f));
+          o.w = grad_scale * (expf((x[u].w - M) - log_sum) - (c + 3 == (uint64_t)target ? 1.f : 0.f));
+          if (c <= (uint64_t)target && (uint64_t)target < c + 4) {
+            const float zt = target == c ? x[u].x : target == c + 1 ? x[u].y
+                           : target == c + 2 ? x[u].z : x[u].w;
+            loss[r] = -((zt - M) - log_sum);
+          }
+          st_stream(dr + f, o);
         }
-        st_stream(dr + f, o);
       }
     }
-    __syncthreads();  // scratch reuse in the next row
+    __syncthreads();  // part_m / part_s reuse in the next row
   }
 }
 
@@ -209,14 +250,10 @@ cudaError_t cross_entropy_launch(float* loss, float* dlogits, const float* logit
       SPAR_CE_W(1) SPAR_CE_W(2) SPAR_CE_W(4) SPAR_CE_W(8) SPAR_CE_W(16)
 #undef SPAR_CE_W
     }
-  } else if (vec_ok && vec <= 1024ull * 16) {
-    const uint64_t e = (vec + 1023) / 1024;
-    const unsigned grid = grid_for(rows, 1, sms * 2);
-    switch (e <= 4 ? 4 : e <= 8 ? 8 : e <= 12 ? 12 : 16) {
-#define SPAR_CE_B(E) case E: launch(ce_block_kernel<E>, dim3(grid), dim3(1024), 0, stream, loss, dlogits, logits, targets, rows, classes, ld, seq, grad_scale, invalid); break;
-      SPAR_CE_B(4) SPAR_CE_B(8) SPAR_CE_B(12) SPAR_CE_B(16)
-#undef SPAR_CE_B
-    }
+  } else if (vec_ok) {
+    const unsigned grid = grid_for(rows, 1, sms * 3);
+    launch(ce_stream_kernel, dim3(grid), dim3(kCeThreads), 0, stream, loss, dlogits, logits,
+           targets, rows, classes, ld, seq, grad_scale, invalid);
   } else {
     const unsigned grid = grid_for(rows, 1, sms * 8);
     launch(ce_generic_kernel, dim3(grid), dim3(256), 0, stream, loss, dlogits, logits, targets, rows, classes, ld,

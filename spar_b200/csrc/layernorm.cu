@@ -23,8 +23,11 @@ namespace {
 
 constexpr int kWarps = 8;  // rows in flight per block
 
+// One warp per row, the row in registers (VPL float4 per lane); gamma and beta are read per use
+// (L1-resident, the same for every row) rather than held, which keeps the registers low enough
+// for three blocks (24 rows in flight) per SM.
 template <int VPL>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, 3)
 layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
                          float* __restrict__ rstd_out, const float* __restrict__ x,
                          const float* __restrict__ gamma, const float* __restrict__ beta,
@@ -33,15 +36,8 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
   const int lane = threadIdx.x & 31;
   const int vec_cols = cols >> 2;
   const float inv_cols = 1.0f / static_cast<float>(cols);
-  float4 g[VPL], b[VPL];
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) {
-    const int f = lane + 32 * j;
-    if (f < vec_cols) {
-      g[j] = reinterpret_cast<const float4*>(gamma)[f];
-      b[j] = reinterpret_cast<const float4*>(beta)[f];
-    }
-  }
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
   const uint64_t warp_global = (static_cast<uint64_t>(blockIdx.x) * kWarps) + (threadIdx.x >> 5);
   const uint64_t warp_stride = static_cast<uint64_t>(gridDim.x) * kWarps;
   for (uint64_t row = warp_global; row < rows; row += warp_stride) {
@@ -67,23 +63,24 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
       }
     }
     const float var = warp_sum(q) * inv_cols;
-    const float denom = sqrtf(var + eps);
+    const float rstd = 1.0f / sqrtf(var + eps);
     float4* yr = reinterpret_cast<float4*>(y + row * cols);
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int f = lane + 32 * j;
       if (f < vec_cols) {
+        const float4 g = __ldg(g4 + f), b = __ldg(b4 + f);
         float4 o;
-        o.x = (v[j].x - mean) / denom * g[j].x + b[j].x;
-        o.y = (v[j].y - mean) / denom * g[j].y + b[j].y;
-        o.z = (v[j].z - mean) / denom * g[j].z + b[j].z;
-        o.w = (v[j].w - mean) / denom * g[j].w + b[j].w;
-        yr[f] = o;
+        o.x = (v[j].x - mean) * rstd * g.x + b.x;
+        o.y = (v[j].y - mean) * rstd * g.y + b.y;
+        o.z = (v[j].z - mean) * rstd * g.z + b.z;
+        o.w = (v[j].w - mean) * rstd * g.w + b.w;
+        yr[f] = o;  // read next by the projection GEMM: left in L2
       }
     }
     if (lane == 0) {
       mean_out[row] = mean;
-      rstd_out[row] = 1.0f / denom;
+      rstd_out[row] = rstd;
     }
   }
 }
