@@ -7,13 +7,12 @@
 // autograd backward (matmul / softmax backward), for the packed projection buffer
 // qkv [batch, seq, 3*model_dim] (Q | K | V, head h at columns h*head_dim of each third).
 //
-// Forward (one CTA per SM, persistent; work item = (batch, head, 128-query tile), heaviest first):
-//   pass 1  S_j = Q K_j^T for the causal key tiles j, row maxima only (no exponentials);
-//   pass 2  S_j again, P_j = exp(S_j * scale - max) written to shared memory in the MMA's K-major
-//           layout, O += P_j V_j in TMEM, row sums in registers; O / sum stored by TMA.
-//   With the final maximum known before any exponential, O needs no rescaling, and the
-//   probabilities are those of the reference's max-subtracted softmax. The row maximum and
-//   1 / row sum are saved for the backward.
+// Forward (one CTA per SM, persistent; work item = (batch, head, query tiles t and T-1-t), so
+// every item costs the same T+1 key-tile products): the two query tiles alternate on the tensor
+// cores, S_X = Q_X K_j^T and O_X += P_X V_j, while four softmax warps per tile turn S into
+// P = exp2(S * scale * log2(e) - m) in TMEM (the A operand of the P V product). m is a running
+// row maximum that only moves, with O and the row sum rescaled, when a tile exceeds it by more
+// than 8 (log2 units). m and 1 / row sum are saved for the backward.
 // Backward (deterministic: every gradient element is written by exactly one CTA, no atomics):
 //   D = rowsum(dO o O) per (row, head) first, by a small streaming kernel.
 //   query kernel  per (batch, head, 128-query tile): for each 64-key tile S, dP = dO V^T,
@@ -63,6 +62,7 @@ struct AttnParams {
   CUtensorMap do_mn;   // dO, MN-major {32, 32}
   CUtensorMap out;     // output store boxes {32, 32}: ctx (forward) or dqkv (backward)
   const float* o;      // forward output (backward: D = rowsum(dO o O))
+  float* o_out;        // forward: where the output is stored
   const float* d_o;    // dO
   float* row_max;      // [batch*heads, seq]: max of scores * scale * log2(e)
   float* row_inv;      // [batch*heads, seq]: 1 / sum of exponentials
@@ -179,53 +179,149 @@ struct SoftThread {
   }
 };
 
+// Round to nearest TF32 (ties away from zero) a value that only feeds the tensor cores: one
+// conversion instruction (the MMA reads the upper 19 bits).
+__device__ __forceinline__ uint32_t tf32_operand(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return r;
+}
+
+// Running maxima of 64 score columns (c0 .. c0+63 of the row) into eight accumulators; on the
+// diagonal key tile only columns <= r (the query row) count.
+template <bool kDiag>
+__device__ __forceinline__ void row_max64(const uint32_t (&v0)[32], const uint32_t (&v1)[32],
+                                          uint32_t c0, uint32_t r, float (&mxs)[8]) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    if (!kDiag || c0 + e <= r) mxs[e & 7] = fmaxf(mxs[e & 7], __uint_as_float(v0[e]));
+    if (!kDiag || c0 + 32 + e <= r) mxs[e & 7] = fmaxf(mxs[e & 7], __uint_as_float(v1[e]));
+  }
+}
+
+// P = exp2(S * scale_log2 - m) over 64 columns in place (as TF32 operands), adding the unrounded
+// values into four partial sums; masked columns of the diagonal tile become 0.
+template <bool kDiag>
+__device__ __forceinline__ void probs64(uint32_t (&v0)[32], uint32_t (&v1)[32], float scale_log2,
+                                        float m, uint32_t c0, uint32_t r, float (&sums)[4]) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    float p0 = ex2(fmaf(__uint_as_float(v0[e]), scale_log2, -m));
+    float p1 = ex2(fmaf(__uint_as_float(v1[e]), scale_log2, -m));
+    if (kDiag && c0 + e > r) p0 = 0.f;
+    if (kDiag && c0 + 32 + e > r) p1 = 0.f;
+    sums[e & 3] += p0 + p1;
+    v0[e] = tf32_operand(p0);
+    v1[e] = tf32_operand(p1);
+  }
+}
+
 // ============================================================================ forward
+// Work item = (batch, head, pair of query tiles t and T-1-t): the two tiles need T+1 key-tile
+// products together, the same for every item, so the causal triangle balances across SMs.
+// Four softmax warps per query tile (thread = query row, all 128 scores of its row).
+// The item is a list of jobs: for each key tile j, (A, j) while j <= t, then (B, j). Job g
+// (counted over the CTA's items) computes S = Q_X K_j^T into TMEM score buffer g % 3, its
+// softmax warps overwrite S with P there, and O_X += P V_j reads it. With three buffers the
+// MMA warp runs up to three S products ahead of the P V products, so a tile's next scores are
+// ready when its softmax warps finish, including the stretch where only tile B has keys left.
+// One pass over the keys with a running maximum per row: P = exp2(S * scale * log2(e) - m), m the
+// maximum in use. m moves (O and the row sum are rescaled by exp2(m_old - m_new)) only when a
+// tile's maximum exceeds it by more than 8, so P <= 2^8 and rescaling is rare. The saved
+// statistics are that m and 1 / sum, which give the normalised probabilities exactly as the
+// backward recomputes them.
 template <int DH>
 struct Fwd {
   static constexpr uint32_t kTile = DH * 512;  // 128 rows x DH fp32
-  static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kKStages = 3;  // K is read in both passes: the deeper ring
+  static constexpr uint32_t kKStages = DH == 64 ? 3 : 4;
   static constexpr uint32_t kVStages = 2;
-  static constexpr uint32_t kK = kQ + kTile;
+  static constexpr uint32_t kQ = 0;  // [2] query tiles A, B
+  static constexpr uint32_t kK = kQ + 2 * kTile;
   static constexpr uint32_t kV = kK + kKStages * kTile;
-  static constexpr uint32_t kStg = kV + kVStages * kTile;  // output staging, 4 warps x 4 KB
-  static constexpr uint32_t kX = kStg + 16384;  // row partials [max 2x128][sum 2x128]
-  static constexpr uint32_t kBar = kX + 2048;
-  static constexpr uint32_t kSmem = kBar + 256 + 1024;
+  static constexpr uint32_t kBar = kV + kVStages * kTile;
+  static constexpr uint32_t kSmem = kBar + 320 + 1024;
   static_assert(kSmem <= kMaxSmem, "forward shared memory");
 };
 
-// TMEM columns: S / P [2][128] at 0 and 128 (P overwrites S and is the A operand of O += P V),
-// O at 256.
+constexpr float kRescaleLog2 = 8.f;  // move the running maximum only past this margin
+constexpr uint32_t kSBufs = 3;       // TMEM score / probability buffers (128 columns each)
+
+// The item's two query tiles: A = t (absent when it equals B, the middle tile of an odd count)
+// and B = T-1-t; nA, nB key tiles each.
+struct PairItem {
+  uint32_t b, h, ta, tb, na, nb;
+};
+
+__device__ __forceinline__ PairItem decode_pair(const AttnParams& p, uint32_t idx) {
+  const uint32_t pair = idx / p.bh;
+  const uint32_t bh = idx - pair * p.bh;
+  PairItem it;
+  it.b = bh / p.heads;
+  it.h = bh - it.b * p.heads;
+  it.ta = pair;
+  it.tb = p.tiles - 1 - pair;
+  it.na = it.ta != it.tb ? it.ta + 1 : 0;
+  it.nb = it.tb + 1;
+  return it;
+}
+
+// Job i of an item: (A, i / 2) and (B, i / 2) alternate while A has keys, then (B, i - nA).
+__device__ __forceinline__ void job_of(const PairItem& it, uint32_t i, uint32_t& x, uint32_t& j) {
+  if (i < 2 * it.na) {
+    x = i & 1;
+    j = i >> 1;
+  } else {
+    x = 1;
+    j = i - it.na;
+  }
+}
+
+__device__ __forceinline__ uint32_t job_index(const PairItem& it, uint32_t x, uint32_t j) {
+  return x == 0 ? 2 * j : (j < it.na ? 2 * j + 1 : it.na + j);
+}
+
+// TMEM columns: score / probability buffers at 0, 128, 256; O of tile X at 384 + X * 64.
 template <int DH>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   using L = Fwd<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;     // [kKStages]
-  uint64_t* k_empty = bars + 5;    // [kKStages]
-  uint64_t* v_full = bars + 8;     // [kVStages]
-  uint64_t* v_empty = bars + 10;   // [kVStages]
-  uint64_t* s_full = bars + 12;    // [2]
-  uint64_t* s_read = bars + 14;    // [2] pass 1: the softmax warps have read S
-  uint64_t* s_used = bars + 16;    // [2] pass 2: the P V product has read P
-  // [2] P ready, alternating by P count: the softmax can be one P ahead of the MMA's wait (the
-  // MMA issues S_{j+1} before waiting for P_j), so one barrier could complete two phases unseen.
-  uint64_t* p_full = bars + 18;
-  uint64_t* o_full = bars + 20;
-  uint64_t* o_empty = bars + 21;
-  uint64_t* xbar = bars + 22;  // softmax-warp rendezvous
-  uint64_t* drain = bars + 23;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  uint64_t* q_full = bars + 0;     // [2]
+  uint64_t* q_empty = bars + 2;    // [2]
+  uint64_t* o_pv = bars + 4;       // [2] an O_X += P V product finished
+  uint64_t* o_full = bars + 6;     // [2]
+  uint64_t* o_empty = bars + 8;    // [2]
+  // [2 tiles][3 buffers] scores of tile X in the buffer. Per tile: a tile's softmax warps can be
+  // many jobs (several uses of a buffer by the other tile) past their previous job, so a
+  // barrier shared by both tiles could complete two phases between their waits.
+  uint64_t* s_full = bars + 10;
+  uint64_t* s_used = bars + 16;    // [3] the P V product has read the buffer
+  uint64_t* p_full = bars + 19;    // [3] probabilities in buffer
+  uint64_t* drain = bars + 22;
+  uint64_t* k_full = bars + 23;                      // [kKStages]
+  uint64_t* k_empty = k_full + L::kKStages;          // [kKStages]
+  uint64_t* v_full = k_empty + L::kKStages;          // [kVStages]
+  uint64_t* v_empty = v_full + L::kVStages;          // [kVStages]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_empty + L::kVStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    tc::mbar_init(q_full, 1);
-    tc::mbar_init(q_empty, 1);
+    for (int x = 0; x < 2; ++x) {
+      tc::mbar_init(q_full + x, 1);
+      tc::mbar_init(q_empty + x, 1);
+      tc::mbar_init(o_pv + x, 1);
+      tc::mbar_init(o_full + x, 1);
+      tc::mbar_init(o_empty + x, 4);
+    }
+    for (uint32_t b = 0; b < kSBufs; ++b) {
+      tc::mbar_init(s_full + b, 1);
+      tc::mbar_init(s_full + kSBufs + b, 1);
+      tc::mbar_init(s_used + b, 1);
+      tc::mbar_init(p_full + b, 4);
+    }
+    tc::mbar_init(drain, 1);
     for (uint32_t i = 0; i < L::kKStages; ++i) {
       tc::mbar_init(k_full + i, 1);
       tc::mbar_init(k_empty + i, 1);
@@ -234,17 +330,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       tc::mbar_init(v_full + i, 1);
       tc::mbar_init(v_empty + i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(s_full + i, 1);
-      tc::mbar_init(s_read + i, kSoftWarps);
-      tc::mbar_init(s_used + i, 1);
-    }
-    tc::mbar_init(p_full, kSoftWarps);
-    tc::mbar_init(p_full + 1, kSoftWarps);
-    tc::mbar_init(o_full, 1);
-    tc::mbar_init(o_empty, kSoftWarps);
-    tc::mbar_init(xbar, kSoftWarps);
-    tc::mbar_init(drain, 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -264,53 +349,58 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     if (tc::elect_one()) {
       tc::tma_prefetch(&p.qk128);
       tc::tma_prefetch(&p.qkv_mn);
-      uint32_t item = 0, kn = 0, vn = 0;  // loads issued into the K and V rings
-      int last_q = -1, last_k[L::kKStages], last_v[L::kVStages];
+      uint32_t kn = 0, vn = 0, qn[2] = {0, 0};
+      int last_q[2] = {-1, -1}, last_k[L::kKStages], last_v[L::kVStages];
       for (uint32_t i = 0; i < L::kKStages; ++i) last_k[i] = -1;
       for (uint32_t i = 0; i < L::kVStages; ++i) last_v[i] = -1;
-      for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
-        const Item it = decode(p, idx, true);
+      for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x) {
+        const PairItem it = decode_pair(p, idx);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
-        if (!wait_or_abort(q_empty, (item & 1) ^ 1, abort_flag)) break;
-        tc::mbar_arrive_expect_tx(q_full, L::kTile);
-        last_q = item & 1;
+        bool ok = true;
+        for (int x = it.na ? 0 : 1; x < 2 && ok; ++x) {
+          const uint32_t t = x ? it.tb : it.ta;
+          if (!(ok = wait_or_abort(q_empty + x, (qn[x] & 1) ^ 1, abort_flag))) break;
+          tc::mbar_arrive_expect_tx(q_full + x, L::kTile);
+          last_q[x] = qn[x] & 1;
+          ++qn[x];
 #pragma unroll
-        for (int c = 0; c < DH / 32; ++c)
-          tc::tma_load_4d(smem + L::kQ + c * 16384, &p.qk128, q_full, hc + 32 * c,
-                          static_cast<int>(it.t * 128), b, 0);
-        const uint32_t nkv = it.t + 1;
-        for (uint32_t pass = 0; pass < 2 && !*abort_flag; ++pass) {
-          for (uint32_t j = 0; j < nkv && !*abort_flag; ++j) {
-            const int row = static_cast<int>(j * 128);
-            {  // K tile j (both passes)
-              const uint32_t st = kn % L::kKStages, ph = (kn / L::kKStages) & 1;
-              if (!wait_or_abort(k_empty + st, ph ^ 1, abort_flag)) break;
-              tc::mbar_arrive_expect_tx(k_full + st, L::kTile);
-              last_k[st] = static_cast<int>(ph);
+          for (int c = 0; c < DH / 32; ++c)
+            tc::tma_load_4d(smem + L::kQ + x * L::kTile + c * 16384, &p.qk128, q_full + x,
+                            hc + 32 * c, static_cast<int>(t * 128), b, 0);
+        }
+        if (!ok) break;
+        for (uint32_t j = 0; j < it.nb && !*abort_flag; ++j) {
+          const int row = static_cast<int>(j * 128);
+          {
+            const uint32_t st = kn % L::kKStages, ph = (kn / L::kKStages) & 1;
+            if (!wait_or_abort(k_empty + st, ph ^ 1, abort_flag)) break;
+            tc::mbar_arrive_expect_tx(k_full + st, L::kTile);
+            last_k[st] = static_cast<int>(ph);
+#pragma unroll
+            for (int c = 0; c < DH / 32; ++c)
+              tc::tma_load_4d(smem + L::kK + st * L::kTile + c * 16384, &p.qk128, k_full + st,
+                              dcol + hc + 32 * c, row, b, 0);
+            ++kn;
+          }
+          {
+            const uint32_t st = vn % L::kVStages, ph = (vn / L::kVStages) & 1;
+            if (!wait_or_abort(v_empty + st, ph ^ 1, abort_flag)) break;
+            tc::mbar_arrive_expect_tx(v_full + st, L::kTile);
+            last_v[st] = static_cast<int>(ph);
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb)
 #pragma unroll
               for (int c = 0; c < DH / 32; ++c)
-                tc::tma_load_4d(smem + L::kK + st * L::kTile + c * 16384, &p.qk128, k_full + st,
-                                dcol + hc + 32 * c, row, b, 0);
-              ++kn;
-            }
-            if (pass) {  // V tile j (pass 2)
-              const uint32_t st = vn % L::kVStages, ph = (vn / L::kVStages) & 1;
-              if (!wait_or_abort(v_empty + st, ph ^ 1, abort_flag)) break;
-              tc::mbar_arrive_expect_tx(v_full + st, L::kTile);
-              last_v[st] = static_cast<int>(ph);
-#pragma unroll
-              for (int kb = 0; kb < 4; ++kb)
-#pragma unroll
-                for (int c = 0; c < DH / 32; ++c)
-                  tc::tma_load_4d(smem + L::kV + st * L::kTile + (kb * (DH / 32) + c) * 4096,
-                                  &p.qkv_mn, v_full + st, 2 * dcol + hc + 32 * c, row + 32 * kb,
-                                  b, 0);
-              ++vn;
-            }
+                tc::tma_load_4d(smem + L::kV + st * L::kTile + (kb * (DH / 32) + c) * 4096,
+                                &p.qkv_mn, v_full + st, 2 * dcol + hc + 32 * c, row + 32 * kb, b,
+                                0);
+            ++vn;
           }
         }
       }
-      if (last_q >= 0 && !tc::mbar_wait(q_full, last_q)) record_error();
+      // Every load issued must have landed before the CTA exits.
+      for (int x = 0; x < 2; ++x)
+        if (last_q[x] >= 0 && !tc::mbar_wait(q_full + x, last_q[x])) record_error();
       for (uint32_t s = 0; s < L::kKStages; ++s)
         if (last_k[s] >= 0 && !tc::mbar_wait(k_full + s, last_k[s])) record_error();
       for (uint32_t s = 0; s < L::kVStages; ++s)
@@ -325,69 +415,70 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       const uint32_t q_addr = tc::smem_u32(smem + L::kQ);
       const uint32_t k_addr = tc::smem_u32(smem + L::kK);
       const uint32_t v_addr = tc::smem_u32(smem + L::kV);
-      uint32_t kn = 0, vn = 0, sn = 0, pn = 0, item = 0;
-      // An S buffer is freed by the softmax warps after a pass-1 use (s_read) and by the P V
-      // product after a pass-2 use (s_used); per buffer: which freed it last, and how many
-      // completions each barrier has had.
-      uint32_t reads[2] = {0, 0}, useds[2] = {0, 0}, last[2] = {0, 0};
+      uint32_t kn = 0, vn = 0, qn[2] = {0, 0}, on[2] = {0, 0}, gbase = 0;
       bool ok = true;
-      // S[sn & 1] = Q K^T for the next K tile of the ring; the K stage is free once it is read.
-      auto issue_s = [&](uint32_t pass) -> bool {
-        const uint32_t st = kn % L::kKStages, sb = sn & 1;
-        if (!wait_or_abort(k_full + st, (kn / L::kKStages) & 1, abort_flag)) return false;
-        if (last[sb] == 1 && !wait_or_abort(s_read + sb, (reads[sb] - 1) & 1, abort_flag))
-          return false;
-        if (last[sb] == 2 && !wait_or_abort(s_used + sb, (useds[sb] - 1) & 1, abort_flag))
-          return false;
-        tc::tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < DH / 8; ++ks)
-          tc::mma_tf32(tmem + sb * 128, kmajor_desc(q_addr, 16384, ks),
-                       kmajor_desc(k_addr + st * L::kTile, 16384, ks), idesc_s, ks > 0);
-        tc::mma_commit(s_full + sb);
-        tc::mma_commit(k_empty + st);
-        ++kn;
-        if (pass == 0) {
-          last[sb] = 1;
-          ++reads[sb];
-        } else {
-          last[sb] = 2;
-          ++useds[sb];
+      for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x) {
+        const PairItem it = decode_pair(p, idx);
+        const uint32_t n[2] = {it.na, it.nb};
+        const uint32_t njobs = it.na + it.nb;
+        for (int x = it.na ? 0 : 1; x < 2 && ok; ++x) {
+          ok = wait_or_abort(q_full + x, qn[x] & 1, abort_flag);
+          ++qn[x];
         }
-        ++sn;
-        return true;
-      };
-      for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x, ++item) {
-        const Item it = decode(p, idx, true);
-        const uint32_t nkv = it.t + 1;
-        if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
-        tc::tc_fence_after();
-        for (uint32_t j = 0; j < nkv && ok; ++j)  // pass 1
-          ok = issue_s(0);
-        if (!ok) break;
-        // pass 2: S_{j+1} is issued before O += P_j V_j so the softmax of tile j+1 overlaps it.
-        const uint32_t sn0 = sn;
-        if (!(ok = issue_s(1))) break;
-        for (uint32_t j = 0; j < nkv && ok; ++j) {
-          if (j + 1 < nkv) {
-            if (!(ok = issue_s(1))) break;
+        int k_ready = -1, v_ready = -1;  // key tiles whose K / V stage has been waited for
+        uint32_t is = 0;                 // S jobs issued (P V jobs: ip)
+        for (uint32_t ip = 0; ip < njobs && ok; ++ip) {
+          // S jobs up to three ahead: job g reuses the buffer of job g - 3, so that job's P V
+          // product must have read it.
+          while (is < njobs && is < ip + kSBufs && ok) {
+            uint32_t x, j;
+            job_of(it, is, x, j);
+            const uint32_t g = gbase + is, buf = g % kSBufs;
+            if (g >= kSBufs && !(ok = wait_or_abort(s_used + buf, (g / kSBufs - 1) & 1, abort_flag)))
+              break;
+            const uint32_t kst = (kn + j) % L::kKStages;
+            if (static_cast<int>(j) > k_ready) {
+              if (!(ok = wait_or_abort(k_full + kst, ((kn + j) / L::kKStages) & 1, abort_flag))) break;
+              k_ready = static_cast<int>(j);
+            }
+            tc::tc_fence_after();
+            const uint32_t qa = q_addr + x * L::kTile;
+#pragma unroll
+            for (int ks = 0; ks < DH / 8; ++ks)
+              tc::mma_tf32(tmem + buf * 128, kmajor_desc(qa, 16384, ks),
+                           kmajor_desc(k_addr + kst * L::kTile, 16384, ks), idesc_s, ks > 0);
+            tc::mma_commit(s_full + x * kSBufs + buf);
+            if (j + 1 == n[x]) tc::mma_commit(q_empty + x);  // Q_X no longer read this item
+            if (x == 1) tc::mma_commit(k_empty + kst);       // (B, j) is K_j's last product
+            ++is;
           }
-          if (j + 1 == nkv) tc::mma_commit(q_empty);  // Q is no longer read in this item
-          if (!(ok = wait_or_abort(p_full + (pn & 1), (pn >> 1) & 1, abort_flag))) break;
-          ++pn;
-          if (j == 0 && !(ok = wait_or_abort(o_empty, (item & 1) ^ 1, abort_flag))) break;
-          const uint32_t vst = vn % L::kVStages, sb = (sn0 + j) & 1;
-          if (!(ok = wait_or_abort(v_full + vst, (vn / L::kVStages) & 1, abort_flag))) break;
+          if (!ok) break;
+          uint32_t x, j;
+          job_of(it, ip, x, j);
+          const uint32_t g = gbase + ip, buf = g % kSBufs;
+          if (!(ok = wait_or_abort(p_full + buf, (g / kSBufs) & 1, abort_flag))) break;
+          if (j == 0 && !(ok = wait_or_abort(o_empty + x, (on[x] & 1) ^ 1, abort_flag))) break;
+          const uint32_t vst = (vn + j) % L::kVStages;
+          if (static_cast<int>(j) > v_ready) {
+            if (!(ok = wait_or_abort(v_full + vst, ((vn + j) / L::kVStages) & 1, abort_flag))) break;
+            v_ready = static_cast<int>(j);
+          }
           tc::tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < 16; ++ks)
-            tc::mma_tf32_ts(tmem + 256, tmem + sb * 128 + ks * 8,
+            tc::mma_tf32_ts(tmem + 384 + x * 64, tmem + buf * 128 + ks * 8,
                             mnmajor_desc<DH>(v_addr + vst * L::kTile, ks), idesc_o, (j | ks) != 0);
-          tc::mma_commit(s_used + sb);
-          tc::mma_commit(v_empty + vst);
-          ++vn;
+          tc::mma_commit(s_used + buf);
+          tc::mma_commit(o_pv + x);
+          if (j + 1 == n[x]) {
+            tc::mma_commit(o_full + x);
+            ++on[x];
+          }
+          if (x == 1) tc::mma_commit(v_empty + vst);  // (B, j) is V_j's last product
         }
-        if (ok) tc::mma_commit(o_full);
+        kn += it.nb;
+        vn += it.nb;
+        gbase += njobs;
       }
       tc::mma_commit(drain);
       if (!tc::mbar_wait(drain, 0)) record_error();
@@ -395,103 +486,110 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     __syncwarp();
   } else {
     // -------------------------------------------------------------- softmax + epilogue
-    // Thread (r, grp) owns columns [64*grp, 64*grp + 64) of row r of every 128 x 128 score tile.
-    const SoftThread th(warp, lane, tmem);
-    const uint32_t r = th.r, grp = th.grp;
-    uint8_t* stg = smem + L::kStg + th.quarter * 4096;
-    float* xmax = reinterpret_cast<float*>(smem + L::kX);  // [2][128]
-    float* xsum = xmax + 256;                              // [2][128]
-    uint32_t sn = 0, pn = 0, item = 0, xphase = 0;
+    // Warps 2-5 serve tile A, warps 6-9 tile B; thread = row r of its tile (TMEM lane).
+    const uint32_t x = static_cast<uint32_t>(warp - 2) >> 2;
+    const uint32_t quarter = warp & 3;
+    const uint32_t r = quarter * 32 + lane;
+    const uint32_t lanes = tmem + ((quarter * 32) << 16);
+    const uint32_t o_col = lanes + 384 + x * 64;
+    uint32_t gbase = 0, pv_done = 0, on = 0, scnt[kSBufs] = {0, 0, 0};  // this tile's uses per buffer
     bool ok = true;
-    for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
-      const Item it = decode(p, idx, true);
-      const uint32_t nkv = it.t + 1;
-      const uint32_t qrow = it.t * 128 + r;
-      float vmax = -INFINITY;  // max of the raw scores (scale > 0 commutes with max)
-      for (uint32_t j = 0; j < nkv && ok; ++j, ++sn) {  // pass 1: row maxima
-        if (!(ok = wait_or_abort(s_full + (sn & 1), (sn >> 1) & 1, abort_flag))) break;
+    for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x) {
+      const PairItem it = decode_pair(p, idx);
+      const uint32_t njobs = it.na + it.nb;
+      const uint32_t n = x ? it.nb : it.na;
+      const uint32_t t = x ? it.tb : it.ta;
+      float m = -INFINITY, sum = 0.f;
+      for (uint32_t j = 0; j < n && ok; ++j) {
+        const uint32_t g = gbase + job_index(it, x, j), buf = g % kSBufs;
+        const uint32_t s_col = lanes + buf * 128;
+        if (!(ok = wait_or_abort(s_full + x * kSBufs + buf, scnt[buf] & 1, abort_flag))) break;
+        ++scnt[buf];
         tc::tc_fence_after();
+        // Scores in two 64-column halves (64 registers each): half 0 is read for its maximum
+        // only, half 1 is kept, turned into P first, and half 0 is read again. Eight running
+        // maxima and four sums keep the dependent chains short.
         uint32_t v0[32], v1[32];
-        const uint32_t base = th.lanes + (sn & 1) * 128 + grp * 64;
-        tc::tmem_load_2x32(base, base + 32, v0, v1);
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(s_read + (sn & 1));
-        if (j != it.t) {
+        const bool diag = j == t;
+        float mxs[8];
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            vmax = fmaxf(vmax, fmaxf(__uint_as_float(v0[e]), __uint_as_float(v1[e])));
-        } else {  // diagonal tile: keys up to the row only
-          const uint32_t c0 = grp * 64;
+        for (int i = 0; i < 8; ++i) mxs[i] = -INFINITY;
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          tc::tmem_load_2x32(s_col + 64 * half, s_col + 64 * half + 32, v0, v1);
+          if (diag) row_max64<true>(v0, v1, 64 * half, r, mxs);
+          else row_max64<false>(v0, v1, 64 * half, r, mxs);
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                               fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        const float mx2 = mx * p.scale_log2;
+        if (j == 0) {
+          m = mx2;
+        } else {
+          const bool move = mx2 > m + kRescaleLog2;
+          if (__any_sync(0xffffffffu, move)) {
+            // O_X and the row sum follow the new maximum: the last O_X += P V must be done.
+            if (!(ok = wait_or_abort(o_pv + x, (pv_done + j - 1) & 1, abort_flag))) break;
+            tc::tc_fence_after();
+            const float f = move ? ex2(m - mx2) : 1.f;
+#pragma unroll 1
+            for (int c = 0; c < DH / 32; ++c) {
+              uint32_t o[32];
+              tc::tmem_load_32x32(o_col + c * 32, o);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            if (c0 + e <= r) vmax = fmaxf(vmax, __uint_as_float(v0[e]));
-            if (c0 + 32 + e <= r) vmax = fmaxf(vmax, __uint_as_float(v1[e]));
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+              tc::tmem_store_32x32(o_col + c * 32, o);
+            }
+            sum *= f;
+            if (move) m = mx2;
           }
         }
-      }
-      if (!ok) break;
-      xmax[grp * 128 + r] = vmax;
-      if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
-      const float mx = fmaxf(xmax[r], xmax[128 + r]) * p.scale_log2;
-      float sum = 0.f;
-      for (uint32_t j = 0; j < nkv && ok; ++j, ++sn) {  // pass 2: probabilities
-        if (!(ok = wait_or_abort(s_full + (sn & 1), (sn >> 1) & 1, abort_flag))) break;
-        tc::tc_fence_after();
-        uint32_t v0[32], v1[32];
-        const uint32_t base = th.lanes + (sn & 1) * 128 + grp * 64;
-        tc::tmem_load_2x32(base, base + 32, v0, v1);
-        const bool diag = j == it.t;
-        const uint32_t c0 = grp * 64;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float p0 = ex2(fmaf(__uint_as_float(v0[e]), p.scale_log2, -mx));
-          float p1 = ex2(fmaf(__uint_as_float(v1[e]), p.scale_log2, -mx));
-          if (diag && c0 + e > r) p0 = 0.f;
-          if (diag && c0 + 32 + e > r) p1 = 0.f;
-          sum += p0 + p1;
+        float sums[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int half = 1; half >= 0; --half) {
+          if (half == 0) tc::tmem_load_2x32(s_col, s_col + 32, v0, v1);
+          const uint32_t c0 = static_cast<uint32_t>(half) * 64;
           // The P V operand, rounded to nearest instead of truncated.
-          v0[e] = __float_as_uint(round_tf32(p0));
-          v1[e] = __float_as_uint(round_tf32(p1));
+          if (diag) probs64<true>(v0, v1, p.scale_log2, m, c0, r, sums);
+          else probs64<false>(v0, v1, p.scale_log2, m, c0, r, sums);
+          tc::tmem_store_2x32(s_col + c0, s_col + c0 + 32, v0, v1);
         }
-        tc::tmem_store_2x32(base, base + 32, v0, v1);  // P over S: the A operand of O += P V
+        sum += (sums[0] + sums[1]) + (sums[2] + sums[3]);
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(p_full + (pn & 1));
-        ++pn;
+        if (lane == 0) tc::mbar_arrive(p_full + buf);
       }
       if (!ok) break;
-      if (!(ok = wait_or_abort(o_full, item & 1, abort_flag))) break;
+      gbase += njobs;
+      if (n == 0) continue;  // no tile A in this item
+      pv_done += n;
+      if (!(ok = wait_or_abort(o_full + x, on & 1, abort_flag))) break;
+      ++on;
       tc::tc_fence_after();
-      xsum[grp * 128 + r] = sum;
-      if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
-      const float inv = 1.f / (xsum[r] + xsum[128 + r]);
-      if (grp == 0) {  // the four warps of column group 0 store O, one 32-column box at a time
-#pragma unroll 1
-        for (int c = 0; c < DH / 32; ++c) {
-          uint32_t v[32];
-          tc::tmem_load_32x32(th.lanes + 256 + c * 32, v);
-          float o[32];
+      const float inv = 1.f / sum;
+      const uint32_t qrow = t * 128 + r;
+      float* dst = p.o_out + (static_cast<uint64_t>(it.b) * p.seq + qrow) * p.ld_o + it.h * DH;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]) * inv;
-          if (lane == 0) tc::bulk_wait_read<0>();  // this warp's staging box is free again
-          __syncwarp();
-          store_box(&p.out, stg, o, static_cast<int>(it.h * DH + 32 * c),
-                    static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
-          if (lane == 0) tc::bulk_commit();
+      for (int c = 0; c < DH / 32; ++c) {
+        uint32_t o[32];
+        tc::tmem_load_32x32(o_col + c * 32, o);
+        if (qrow < p.seq) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(dst + c * 32 + e) =
+                make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                            __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
         }
       }
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(o_empty);
-      if (grp == 0 && qrow < p.seq) {
+      if (lane == 0) tc::mbar_arrive(o_empty + x);
+      if (qrow < p.seq) {
         const uint64_t s = static_cast<uint64_t>(it.b * p.heads + it.h) * p.seq + qrow;
-        p.row_max[s] = mx;
+        p.row_max[s] = m;
         p.row_inv[s] = inv;
       }
     }
-    if (lane == 0) tc::bulk_wait_all();
-    __syncwarp();
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -1125,13 +1223,13 @@ cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_ma
   base_params(p, batch, seq, heads, head_dim);
   const uint64_t d = heads * head_dim;
   if (!make_map(&p.qk128, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 128, false) ||
-      !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true) ||
-      !make_map(&p.out, ctx, d, seq, batch, 1, d, seq * d, 0, 32, false))
+      !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true))
     return cudaErrorInvalidValue;
+  p.o_out = ctx;
   p.row_max = row_max;
   p.row_inv = row_inv;
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
-  p.total = p.tiles * p.bh;
+  p.total = (p.tiles + 1) / 2 * p.bh;  // pairs of query tiles
   static bool cfg32[64] = {}, cfg64[64] = {};
   return head_dim == 64 ? launch_attn(attn_fwd_kernel<64>, Fwd<64>::kSmem, p, device, stream, cfg64)
                         : launch_attn(attn_fwd_kernel<32>, Fwd<32>::kSmem, p, device, stream, cfg32);

@@ -71,22 +71,53 @@ def test_attention_is_deterministic(cuda):
 
 
 def test_attention_statistics(cuda):
-    """row_max * ln 2 is the row maximum of the scaled scores; 1 / row_inv the sum of
-    exp(scaled score - max) over the causal keys."""
+    """The saved statistics reproduce the softmax: exp(scaled score - row_max * ln 2) * row_inv sums
+    to 1 over the causal keys, and row_max (a running maximum that only moves when a key tile
+    exceeds it by more than 8 in log2 units) lies within [max - 8 ln 2, max] of the scaled scores."""
     import torch
     from spar_b200 import ops
 
-    b, t, h, dh = 1, 96, 2, 32
+    b, t, h, dh = 1, 300, 2, 32
     r = np.random.default_rng(9)
     qkv = r.standard_normal((b, t, 3 * h * dh)).astype(np.float32)
+    qkv[..., h * dh:2 * h * dh] *= (1.0 + np.arange(t) / 40.0)[None, :, None]  # later keys larger
+    qkv = rn_tf32(qkv)  # exact TF32 operands, so the scores below are the kernel's to fp32 rounding
     ctx, row_max, row_inv = ops.attention_forward(torch.from_numpy(qkv).to(cuda), h)
     d = h * dh
     q = qkv[..., :d].reshape(b, t, h, dh).transpose(0, 2, 1, 3).astype(np.float64)
     k = qkv[..., d:2 * d].reshape(b, t, h, dh).transpose(0, 2, 1, 3).astype(np.float64)
     s = np.where(np.triu(np.ones((t, t), bool), 1), -np.inf, q @ k.transpose(0, 1, 3, 2) / np.sqrt(dh))
     m = s.max(-1)
-    assert rel_l2(row_max.cpu().numpy() * np.log(2.0), m) <= 2e-3
-    assert rel_l2(1.0 / row_inv.cpu().numpy(), np.exp(s - m[..., None]).sum(-1)) <= 2e-3
+    used = row_max.cpu().numpy().astype(np.float64) * np.log(2.0)
+    assert np.all(used <= m + 1e-3 * np.abs(m) + 1e-4)
+    assert np.all(used >= m - 8 * np.log(2.0) - 1e-3 * np.abs(m) - 1e-4)
+    total = (np.exp(s - used[..., None]).sum(-1)) * row_inv.cpu().numpy()
+    np.testing.assert_allclose(total, 1.0, rtol=1e-4)
+
+
+def test_attention_running_max_rescale(cuda):
+    """Keys that grow along the sequence make later key tiles exceed the running maximum, so the
+    forward rescales O and the row sums mid-row; results still match the oracle."""
+    import torch
+    from spar_b200 import ops
+
+    b, t, h, dh = 2, 512, 2, 64
+    d = h * dh
+    r = np.random.default_rng(77)
+    qkv = r.standard_normal((b, t, 3 * d)).astype(np.float32)
+    qkv[..., d:2 * d] *= (1.0 + np.arange(t) / 48.0)[None, :, None]
+    qkv = rn_tf32(qkv)
+    dctx = rn_tf32(r.standard_normal((b, t, d)).astype(np.float32))
+    q = torch.from_numpy(qkv).to(cuda)
+    ctx, row_max, row_inv = ops.attention_forward(q, h)
+    dqkv = ops.attention_backward(torch.from_numpy(dctx).to(cuda), q, ctx, row_max, row_inv, h)
+    torch.cuda.synchronize()
+    assert ops.attention_error(0) == 0
+    ref_ctx, ref_dqkv = O.attention_forward_backward(qkv, h, dctx)
+    assert rel_l2(ctx.cpu().numpy(), ref_ctx) <= 2e-3
+    got = dqkv.cpu().numpy()
+    for part, name in enumerate(("dq", "dk", "dv")):
+        assert rel_l2(got[..., part * d:(part + 1) * d], ref_dqkv[..., part * d:(part + 1) * d]) <= 2e-3, name
 
 
 def test_attention_invalid_arguments(cuda):
