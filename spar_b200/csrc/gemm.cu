@@ -130,7 +130,27 @@ struct EpiState {
   uint64_t* aux_bar;  // this warp's two mbarriers for aux-tile loads
   uint32_t aux_phase[2];
   uint32_t sel;
+  bool prefetched;    // the aux box of the next epilogue_box call is already on its way
 };
+
+__device__ __forceinline__ bool epilogue_needs_aux(const GemmParams& p) {
+  return p.kparts == 1 &&
+         (p.epilogue == SPAR_B200_EPI_BIAS_ADD || p.epilogue == SPAR_B200_EPI_GELU_BWD);
+}
+
+// Starts the TMA load of the aux box that the next epilogue_box call (box at col0, row0) reads,
+// into the staging box it will use, so the load overlaps the current box's work. That staging
+// box was last written by the store two boxes back: wait until at most one store still reads.
+__device__ __forceinline__ void aux_prefetch(const GemmParams& p, EpiState& st, uint32_t col0,
+                                             uint32_t row0, uint32_t b1, uint32_t b0) {
+  if (!epilogue_needs_aux(p) || st.prefetched) return;
+  if ((threadIdx.x & 31) == 0) {
+    tc::bulk_wait_read<1>();
+    tc::mbar_arrive_expect_tx(st.aux_bar + st.sel, 4096);
+    tc::tma_load_4d(st.bufs + st.sel * 4096, &p.aux_map, st.aux_bar + st.sel, col0, row0, b1, b0);
+  }
+  st.prefetched = true;
+}
 
 // Epilogue of one 32 x 32 box (this warp's 32 accumulator rows x 32 columns): optional aux tile
 // brought in by TMA, alpha/bias/GELU/GELU'/residual applied in registers (thread = row), the
@@ -167,12 +187,13 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
     else tc::bulk_wait_read<1>();
   }
   __syncwarp();
-  if (needs_aux) {
+  if (needs_aux && !st.prefetched) {
     if (lane == 0) {
       tc::mbar_arrive_expect_tx(st.aux_bar + st.sel, 4096);
       tc::tma_load_4d(buf, &p.aux_map, st.aux_bar + st.sel, col0, row0, b1, b0);
     }
   }
+  st.prefetched = false;
 #pragma unroll
   for (int e = 0; e < 32; ++e) v[e] *= p.alpha;
   if (p.bias && (p.epilogue == SPAR_B200_EPI_BIAS || p.epilogue == SPAR_B200_EPI_BIAS_GELU ||
@@ -444,6 +465,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
     st.aux_bar = aux_bars + ew * 2;
     st.aux_phase[0] = st.aux_phase[1] = 0;
     st.sel = 0;
+    st.prefetched = false;
     bool ok = true;
     uint32_t acc = 0, acc_phase = 0;
     for (uint32_t idx = blockIdx.x; idx < p.total_tiles && ok; idx += gridDim.x) {
@@ -453,6 +475,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
       const uint32_t row0 = t.mt * BM + quarter * 32;
       const uint32_t lane_base = tmem_base + ((quarter * 32) << 16);
       if constexpr (!CHUNKED) {
+        if (t.nt * BN + chunk0 * 32 < p.n) aux_prefetch(p, st, t.nt * BN + chunk0 * 32, row0, t.b1, t.b0);
         if (!tc::mbar_wait(tfull + acc, acc_phase)) {
           record_error();
           *abort_flag = 1;
@@ -469,6 +492,8 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
           epilogue_box(p, st, v, col0, row0, t.b1, t.b0, t.ks, ok);
+          if (chunk + 1 < chunk0 + kChunks && col0 + 32 < p.n)
+            aux_prefetch(p, st, col0 + 32, row0, t.b1, t.b0);
         }
         tc::tc_fence_before();
         __syncwarp();
@@ -519,6 +544,8 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
       }
     }
     if (!ok) *abort_flag = 1;
+    // A prefetched aux load left unused (the loop was abandoned) must land before the CTA exits.
+    if (st.prefetched && !tc::mbar_wait(st.aux_bar + st.sel, st.aux_phase[st.sel])) record_error();
     // All staged stores must have finished before the CTA (and its shared memory) goes away.
     if (lane == 0) tc::bulk_wait_all();
     __syncwarp();
@@ -724,6 +751,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __g
     st.aux_bar = aux_bars + ew * 2;
     st.aux_phase[0] = st.aux_phase[1] = 0;
     st.sel = 0;
+    st.prefetched = false;
     bool ok = true;
     uint32_t acc = 0, acc_phase = 0;
     const uint32_t tempty_leader = tc::map_to_rank(tc::smem_u32(tempty), 0);
@@ -733,6 +761,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __g
       if (*abort_flag) break;
       const uint32_t row0 = t.mt * 256 + rank * BM + quarter * 32;
       const uint32_t lane_base = tmem_base + ((quarter * 32) << 16);
+      if (t.nt * BN + chunk0 * 32 < p.n) aux_prefetch(p, st, t.nt * BN + chunk0 * 32, row0, t.b1, t.b0);
       if (!tc::mbar_wait_cluster(tfull + acc, acc_phase)) {
         record_error();
         *abort_flag = 1;
@@ -749,6 +778,8 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __g
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
         epilogue_box(p, st, v, col0, row0, t.b1, t.b0, t.ks, ok);
+        if (chunk + 1 < chunk0 + kChunks && col0 + 32 < p.n)
+          aux_prefetch(p, st, col0 + 32, row0, t.b1, t.b0);
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -759,6 +790,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __g
       }
     }
     if (!ok) *abort_flag = 1;
+    if (st.prefetched && !tc::mbar_wait(st.aux_bar + st.sel, st.aux_phase[st.sel])) record_error();
     if (lane == 0) tc::bulk_wait_all();
     __syncwarp();
   }
