@@ -223,7 +223,8 @@ class LMTrainer {
     uint64_t launches;
   };
   std::map<uint64_t, StepGraph> graphs;
-  bool graphs_enabled = true;
+  // SPAR_B200_GRAPHS=0 keeps every step eager (for per-kernel profiling of the step).
+  bool graphs_enabled = !(getenv("SPAR_B200_GRAPHS") && getenv("SPAR_B200_GRAPHS")[0] == '0');
   uint64_t eager_steps = 0;
   cudaStream_t exec_stream = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;

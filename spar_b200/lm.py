@@ -202,3 +202,37 @@ def smoke_step(device) -> None:
     if not (np.isfinite(loss) and np.isfinite(norm)) or flags != (0, 0):
         raise SparError("smoke", _lib.SparCudaStatus(2, 0))
     lm.close()
+
+
+def _main() -> None:
+    """`python -m spar_b200.lm --micro-batch MB --steps S`: S training steps of the C5 decoder on one
+    GPU, with rank 0's share of the 64-sequence global batch for 16 / MB ranks (4 accumulation
+    micro-steps of MB sequences), synthetic weights and ids; prints the loss and step time."""
+    import argparse
+    import time
+    from dataclasses import replace
+
+    import torch
+
+    from .data import rank_share
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--micro-batch", type=int, default=16, choices=[1, 2, 4, 8, 16])
+    ap.add_argument("--steps", type=int, default=2)
+    a = ap.parse_args()
+    cfg = replace(C5, micro_batch=a.micro_batch)
+    lm = DecoderLM(cfg, 0)
+    lm.init_normal(0x5EED0005, 0.02)
+    ids = torch.from_numpy(rank_share(0x5EED1005, 64, 4, cfg.seq, cfg.vocab, 0,
+                                      16 // a.micro_batch)).cuda()
+    for s in range(a.steps):
+        t0 = time.perf_counter()
+        loss, norm, flags = lm.train_step(ids, 3e-4, step=s + 1)
+        torch.cuda.synchronize()
+        print(f"step {s + 1}: loss {loss:.4f} grad-norm {norm:.4f} flags {flags} "
+              f"{(time.perf_counter() - t0) * 1e3:.1f} ms", flush=True)
+    lm.close()
+
+
+if __name__ == "__main__":
+    _main()
