@@ -193,7 +193,15 @@ class LMTrainer {
   bool fused_attention = false;
   float *ln_ws = nullptr, *col_ws = nullptr, *split_ws = nullptr, *rope_tab = nullptr;
   float* splitk_ws = nullptr;  // split-K partial tiles of the small weight-gradient GEMMs
+  float* splitk_ws2 = nullptr;  // the same for products on the weight-gradient stream
   uint64_t splitk_floats = 0;
+  // Weight gradients on a second stream: in the backward, dW = X^T dY and dX = dY W^T only share
+  // their input, so the dW products (and the bias column sums) run beside the dX chain and fill
+  // the SMs the other product leaves idle (a 2048-row product fills under half a wave of SM pairs).
+  // Forks and joins are events (captured as graph edges). TF32 mode, not while profiling.
+  cudaStream_t wgrad_stream = nullptr;
+  cudaEvent_t wg_fork[5] = {}, wg_join[4] = {};
+  bool wgrad_enabled = !(getenv("SPAR_B200_WGRAD_STREAM") && getenv("SPAR_B200_WGRAD_STREAM")[0] == '0');
   void* emb_scratch = nullptr;
   float* row_loss = nullptr;     // [N]
   float* loss_sums = nullptr;    // [kMaxMicro]
@@ -255,6 +263,11 @@ LMTrainer::~LMTrainer() {
   if (tail_ev) cudaEventDestroy(tail_ev);
   if (comm_done) cudaEventDestroy(comm_done);
   if (comm_stream) cudaStreamDestroy(comm_stream);
+  for (auto ev : wg_fork)
+    if (ev) cudaEventDestroy(ev);
+  for (auto ev : wg_join)
+    if (ev) cudaEventDestroy(ev);
+  if (wgrad_stream) cudaStreamDestroy(wgrad_stream);
   for (auto& g : graphs) cudaGraphExecDestroy(g.second.exec);
   if (exec_stream) cudaStreamDestroy(exec_stream);
   if (ev_in) cudaEventDestroy(ev_in);
@@ -386,7 +399,10 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
       g.precision = c.precision;
       splitk_floats = std::max(splitk_floats, gemm_splitk_workspace_floats(g, device));
     }
-    if (splitk_floats) f(&splitk_ws, splitk_floats);
+    if (splitk_floats) {
+      f(&splitk_ws, splitk_floats);
+      f(&splitk_ws2, splitk_floats);
+    }
   }
   uint64_t total = 0;
   for (auto& pb : plan) total += (pb.second + 255) / 256 * 256;
@@ -399,6 +415,11 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   }
   e = cudaMemset(flags, 0, 64);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&exec_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&wgrad_stream, cudaStreamNonBlocking);
+  for (auto& ev : wg_fork)
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  for (auto& ev : wg_join)
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
   if (e == cudaSuccess)
@@ -456,7 +477,8 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
   // Never let a split copy run past the workspace sized in init().
   if (cfg.precision == SPAR_B200_TF32X3 && gemm_split_workspace_floats(g) > split_floats)
     return cudaErrorInvalidValue;
-  if (!profiling) return gemm_launch(g, split_ws, device, s, splitk_ws, splitk_floats);
+  float* kws = s == wgrad_stream ? splitk_ws2 : splitk_ws;
+  if (!profiling) return gemm_launch(g, split_ws, device, s, kws, splitk_floats);
   if (ev_used == ev_pool.size()) {
     std::pair<cudaEvent_t, cudaEvent_t> pr;
     SPAR_TRY_RAW(cudaEventCreate(&pr.first));
@@ -469,7 +491,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
   auto& pr = ev_pool[ev_used++];
   ev_flops.push_back(fl);
   SPAR_TRY_RAW(cudaEventRecord(pr.first, s));
-  SPAR_TRY_RAW(gemm_launch(g, split_ws, device, s, splitk_ws, splitk_floats));
+  SPAR_TRY_RAW(gemm_launch(g, split_ws, device, s, kws, splitk_floats));
   return cudaEventRecord(pr.second, s);
 }
 
@@ -567,9 +589,16 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
                                   flags, device, s));
   SPAR_CHECK(sum_launch(loss_sums + micro, row_loss, N, s));
   // ---------------------------------------------------------------- backward
-  // dE += dlogits^T hf ; dhf = dlogits E
+  // dE += dlogits^T hf (weight-gradient stream) ; dhf = dlogits E
+  const bool conc = wgrad_enabled && !profiling && cfg.precision == SPAR_B200_TF32;
+  cudaStream_t w = conc ? wgrad_stream : s;
+  if (conc) {
+    SPAR_CHECK(cudaEventRecord(wg_fork[4], s));
+    SPAR_CHECK(cudaStreamWaitEvent(w, wg_fork[4], 0));
+  }
   SPAR_CHECK(gemm(V, d, N, logits, Vp, true, hf, d, false, G + off_E, d, true, SPAR_B200_EPI_NONE,
-                  nullptr, nullptr, 0, s));
+                  nullptr, nullptr, 0, w));
+  if (conc) SPAR_CHECK(cudaEventRecord(wg_join[3], w));
   SPAR_CHECK(gemm(N, d, V, logits, Vp, false, P + off_E, d, false, dtmp, d, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // The final norm's dx is dL/d(last block output): its column sums are that block's b2 gradient.
@@ -580,6 +609,9 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
     SPAR_CHECK(layer_backward(l, s));
   }
   launches += 5;
+  // dE's tied-embedding scatter below adds into G + off_E, and the next micro-step rewrites the
+  // logits and hf that the dE product reads.
+  if (conc) SPAR_CHECK(cudaStreamWaitEvent(s, wg_join[3], 0));
   SPAR_CHECK(embedding_backward_launch(G + off_E, dres, ids, N, V, d, emb_scratch, device, s));
   if (comm && last_micro) {
     // Tied embedding and final norm (first and last gradients of the sweep), then join.
@@ -632,25 +664,41 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   float* P = params;
   float* G = grads;
   launches += 2 * 2 + 2 * 2 + 1 + (cfg.use_rope && !fused_attention ? 1 : 0);  // col sums, LN bwd, softmax bwd, rope
+  // Weight gradients on the second stream (forks: event on s, wait on w; joins: the reverse).
+  const bool conc = wgrad_enabled && !profiling && cfg.precision == SPAR_B200_TF32;
+  cudaStream_t w = conc ? wgrad_stream : s;
+  auto fork = [&](int i) -> cudaError_t {
+    if (!conc) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(wg_fork[i], s);
+    return e == cudaSuccess ? cudaStreamWaitEvent(w, wg_fork[i], 0) : e;
+  };
+  auto mark = [&](int i) -> cudaError_t { return conc ? cudaEventRecord(wg_join[i], w) : cudaSuccess; };
+  auto join = [&](int i) -> cudaError_t { return conc ? cudaStreamWaitEvent(s, wg_join[i], 0) : cudaSuccess; };
   // dres = dL/d(layer output) = dL/d(h1 + mlp)
   // MLP: mlp = g W2 + b2, g = gelu(u), u = a2 W1 + b1. The b2 gradient (column sums of dres)
   // came out of the LayerNorm backward that produced dres (the next block's LN1, or the final
   // norm).
+  SPAR_TRY(fork(0));
   SPAR_TRY(gemm(F, d, N, A.g, F, true, dres, d, false, G + lo.w2, d, true, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s));
+                nullptr, nullptr, 0, w));
+  SPAR_TRY(mark(0));  // dW2 has read dres
   SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, du, F, false, SPAR_B200_EPI_GELU_BWD,
                 nullptr, A.u, F, s));
+  SPAR_TRY(fork(1));
   SPAR_TRY(gemm(d, F, N, A.a2, d, true, du, F, false, G + lo.w1, F, true, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s));
-  SPAR_TRY(column_sum_launch(G + lo.b1, du, N, F, F, 1, col_ws, device, s));
+                nullptr, nullptr, 0, w));
+  SPAR_TRY(column_sum_launch(G + lo.b1, du, N, F, F, 1, col_ws, device, w));
   SPAR_TRY(gemm(N, d, F, du, F, false, P + lo.w1, F, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
-  // dres += LN2 backward  ->  dL/dh1, whose column sums are the bo gradient
+  // dres += LN2 backward  ->  dL/dh1, whose column sums are the bo gradient (dW2 read dres first)
+  SPAR_TRY(join(0));
   SPAR_TRY(layernorm_backward_launch(dres, G + lo.ln2_g, G + lo.ln2_b, dtmp, A.h1, P + lo.ln2_g,
                                      A.mean2, A.rstd2, N, d, 1, 1, ln_ws, device, s, G + lo.bo));
   // out projection: h1 = x + ctx Wo + bo
+  SPAR_TRY(fork(2));
   SPAR_TRY(gemm(d, d, N, A.ctx, d, true, dres, d, false, G + lo.wo, d, true, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s));
+                nullptr, nullptr, 0, w));
+  SPAR_TRY(mark(1));  // dWo has read dres
   SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
                 fused_attention));
@@ -661,16 +709,21 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   if (cfg.use_rope && !fused_attention)
     SPAR_TRY(rope_apply_launch(dqkv, rope_tab, N, T, 2 * H, dh, ld, 1, device, s));
   // QKV projection
+  SPAR_TRY(fork(3));
   SPAR_TRY(gemm(d, 3 * d, N, A.a1, d, true, dqkv, ld, false, G + lo.wqkv, ld, true,
-                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
-  SPAR_TRY(column_sum_launch(G + lo.bqkv, dqkv, N, 3 * d, ld, 1, col_ws, device, s));
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, w));
+  SPAR_TRY(column_sum_launch(G + lo.bqkv, dqkv, N, 3 * d, ld, 1, col_ws, device, w));
+  SPAR_TRY(mark(2));  // every product of this layer on the weight-gradient stream is done
   SPAR_TRY(gemm(N, d, 3 * d, dqkv, ld, false, P + lo.wqkv, ld, true, dtmp, d, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // dres += LN1 backward -> dL/dx = dL/d(previous block output): its column sums are the
-  // previous block's b2 gradient
+  // previous block's b2 gradient (dWo read dres first)
+  SPAR_TRY(join(1));
   SPAR_TRY(layernorm_backward_launch(dres, G + lo.ln1_g, G + lo.ln1_b, dtmp, A.x, P + lo.ln1_g,
                                      A.mean1, A.rstd1, N, d, 1, 1, ln_ws, device, s,
                                      l > 0 ? G + lay[l - 1].b2 : nullptr));
+  // The next layer rewrites du and dqkv, and this layer's gradients are complete.
+  SPAR_TRY(join(2));
   if (comm && last_micro) {
     // This layer's gradients are final: reduce them on the communication stream while the
     // remaining layers run backward (bucket = one block's contiguous parameter range).
