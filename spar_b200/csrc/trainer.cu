@@ -63,6 +63,21 @@ __global__ void init_normal_kernel(float* dst, uint64_t rows, uint64_t cols, uin
   }
 }
 
+// a += b, n float4 (the second lane's gradients into the first, one fixed order).
+__global__ void add_into_kernel(float4* __restrict__ a, const float4* __restrict__ b, uint64_t n) {
+  pdl_begin();
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float4 x = a[i];
+    const float4 y = b[i];
+    x.x += y.x;
+    x.y += y.y;
+    x.z += y.z;
+    x.w += y.w;
+    a[i] = x;
+  }
+}
+
 __global__ void fill_kernel(float* dst, uint64_t n, float v) {
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
@@ -202,6 +217,42 @@ class LMTrainer {
   cudaStream_t wgrad_stream = nullptr;
   cudaEvent_t wg_fork[5] = {}, wg_join[4] = {};
   bool wgrad_enabled = !(getenv("SPAR_B200_WGRAD_STREAM") && getenv("SPAR_B200_WGRAD_STREAM")[0] == '0');
+  // Two micro-steps in flight at small micro-batches ("lanes"): each lane owns a full set of
+  // activation and workspace buffers, a stream pair and a gradient arena. Lane 1 runs every other
+  // micro-step beside lane 0, so two narrow micro-steps fill the SMs like one twice as wide;
+  // lane 1's gradients are added into lane 0's in a fixed order (per all-reduce bucket ahead of
+  // the data-parallel reduction, or once after the last micro-step), so steps stay deterministic.
+  // The working members above (acts, dres, ..., grads, wgrad_stream) are the selected lane's.
+  struct Lane {
+    std::vector<LayerActs> acts;
+    float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
+    float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
+    float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *splitk_ws2 = nullptr;
+    float *row_loss = nullptr, *grads = nullptr;
+    void* emb_scratch = nullptr;
+    cudaStream_t stream = nullptr, wgrad_stream = nullptr;
+    cudaEvent_t wg_fork[5] = {}, wg_join[4] = {};
+    std::vector<cudaEvent_t> layer_ev;  // data parallel: block l done in the lane's last micro-step
+    cudaEvent_t tail_ev = nullptr;
+  };
+  Lane lanes[2];
+  int lanes_alloc = 1;  // lanes with buffers (2 when the micro-batch is small)
+  int cur_lane = 0, step_lanes = 1, comm_lane = 0;
+  cudaEvent_t lane_fork = nullptr, lane_join = nullptr;
+  // SPAR_B200_LANES: 0 = never, 2 = at any micro-batch, unset / 1 = micro-batches of <= 4 sequences.
+  int lanes_mode = getenv("SPAR_B200_LANES") ? getenv("SPAR_B200_LANES")[0] - '0' : 1;
+  void select_lane(int i) {
+    Lane& ln = lanes[i];
+    acts = ln.acts;
+    xL = ln.xL; meanf = ln.meanf; rstdf = ln.rstdf; hf = ln.hf; logits = ln.logits;
+    dres = ln.dres; dtmp = ln.dtmp; dqkv = ln.dqkv; dS = ln.dS; du = ln.du;
+    ln_ws = ln.ln_ws; col_ws = ln.col_ws; splitk_ws = ln.splitk_ws; splitk_ws2 = ln.splitk_ws2;
+    row_loss = ln.row_loss; grads = ln.grads; emb_scratch = ln.emb_scratch;
+    wgrad_stream = ln.wgrad_stream;
+    for (int k = 0; k < 5; ++k) wg_fork[k] = ln.wg_fork[k];
+    for (int k = 0; k < 4; ++k) wg_join[k] = ln.wg_join[k];
+    cur_lane = i;
+  }
   void* emb_scratch = nullptr;
   float* row_loss = nullptr;     // [N]
   float* loss_sums = nullptr;    // [kMaxMicro]
@@ -254,6 +305,12 @@ class LMTrainer {
   cudaError_t attention_forward(LayerActs& A, cudaStream_t s);
   cudaError_t attention_backward(LayerActs& A, cudaStream_t s);
   cudaError_t layer_backward(uint64_t l, cudaStream_t s);
+  // Data-parallel reduction of buckets [b0, b1) on the communication stream once the gradients in
+  // them are final on stream s. With two lanes, each lane records lane_ev after its last
+  // micro-step has produced them; the lane that issues last (comm_lane) then adds lane 1's
+  // buckets into lane 0's and reduces lane 0's.
+  cudaError_t reduce_buckets(size_t b0, size_t b1, cudaEvent_t ev0, cudaEvent_t ev1,
+                             cudaEvent_t single_ev, cudaStream_t s);
 };
 
 LMTrainer::~LMTrainer() {
@@ -263,11 +320,18 @@ LMTrainer::~LMTrainer() {
   if (tail_ev) cudaEventDestroy(tail_ev);
   if (comm_done) cudaEventDestroy(comm_done);
   if (comm_stream) cudaStreamDestroy(comm_stream);
-  for (auto ev : wg_fork)
-    if (ev) cudaEventDestroy(ev);
-  for (auto ev : wg_join)
-    if (ev) cudaEventDestroy(ev);
-  if (wgrad_stream) cudaStreamDestroy(wgrad_stream);
+  for (Lane& ln : lanes) {
+    for (auto ev : ln.wg_fork)
+      if (ev) cudaEventDestroy(ev);
+    for (auto ev : ln.wg_join)
+      if (ev) cudaEventDestroy(ev);
+    for (auto ev : ln.layer_ev) cudaEventDestroy(ev);
+    if (ln.tail_ev) cudaEventDestroy(ln.tail_ev);
+    if (ln.wgrad_stream) cudaStreamDestroy(ln.wgrad_stream);
+    if (&ln != &lanes[0] && ln.stream) cudaStreamDestroy(ln.stream);  // lane 0 borrows the step's
+  }
+  if (lane_fork) cudaEventDestroy(lane_fork);
+  if (lane_join) cudaEventDestroy(lane_join);
   for (auto& g : graphs) cudaGraphExecDestroy(g.second.exec);
   if (exec_stream) cudaStreamDestroy(exec_stream);
   if (ev_in) cudaEventDestroy(ev_in);
@@ -327,40 +391,47 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   for (uint64_t w : {d, 3 * d, F})
     col_floats = std::max<uint64_t>(col_floats, static_cast<uint64_t>(column_sum_parts(N, w, device)) * w);
   std::vector<std::pair<void**, uint64_t>> plan;  // (pointer slot, bytes)
-  acts.resize(L);
   auto f = [&](float** p, uint64_t n) { plan.push_back({reinterpret_cast<void**>(p), n * 4}); };
-  for (uint64_t l = 0; l < L; ++l) {
-    LayerActs& A = acts[l];
-    f(&A.x, N * d);
-    f(&A.mean1, N);
-    f(&A.rstd1, N);
-    f(&A.a1, N * d);
-    f(&A.qkv, N * 3 * d);
-    f(fused_attention ? &A.stats : &A.p, PS);
-    f(&A.ctx, N * d);
-    f(&A.h1, N * d);
-    f(&A.mean2, N);
-    f(&A.rstd2, N);
-    f(&A.a2, N * d);
-    f(&A.u, N * F);
-    f(&A.g, N * F);
+  // Two lanes (two micro-steps in flight) when a micro-step is too narrow to fill the GPU.
+  lanes_alloc = (c.precision == SPAR_B200_TF32 && (lanes_mode == 2 || (lanes_mode == 1 && B <= 4))) ? 2 : 1;
+  for (int li = 0; li < lanes_alloc; ++li) {
+    Lane& ln = lanes[li];
+    ln.acts.resize(L);
+    for (uint64_t l = 0; l < L; ++l) {
+      LayerActs& A = ln.acts[l];
+      f(&A.x, N * d);
+      f(&A.mean1, N);
+      f(&A.rstd1, N);
+      f(&A.a1, N * d);
+      f(&A.qkv, N * 3 * d);
+      f(fused_attention ? &A.stats : &A.p, PS);
+      f(&A.ctx, N * d);
+      f(&A.h1, N * d);
+      f(&A.mean2, N);
+      f(&A.rstd2, N);
+      f(&A.a2, N * d);
+      f(&A.u, N * F);
+      f(&A.g, N * F);
+    }
+    f(&ln.xL, N * d);
+    f(&ln.meanf, N);
+    f(&ln.rstdf, N);
+    f(&ln.hf, N * d);
+    f(&ln.logits, N * Vp);
+    f(&ln.dres, N * d);
+    f(&ln.dtmp, N * d);
+    f(&ln.dqkv, N * 3 * d);
+    f(&ln.dS, fused_attention ? B * H * T : PS);
+    f(&ln.du, N * F);
+    f(&ln.ln_ws, 3ull * ln_parts * d);  // dgamma, dbeta and dx column-sum partials
+    f(&ln.col_ws, col_floats);
+    f(&ln.row_loss, N);
+    plan.push_back({reinterpret_cast<void**>(&ln.emb_scratch), embedding_backward_scratch(N, V)});
+    if (li > 0) f(&ln.grads, flat);  // lane 0 accumulates into the trainer's gradient arena
   }
-  f(&xL, N * d);
-  f(&meanf, N);
-  f(&rstdf, N);
-  f(&hf, N * d);
-  f(&logits, N * Vp);
-  f(&dres, N * d);
-  f(&dtmp, N * d);
-  f(&dqkv, N * 3 * d);
-  f(&dS, fused_attention ? B * H * T : PS);
-  f(&du, N * F);
-  f(&ln_ws, 3ull * ln_parts * d);  // dgamma, dbeta and dx column-sum partials
-  f(&col_ws, col_floats);
+  lanes[0].grads = grads;
   f(&rope_tab, T * dh);
-  f(&row_loss, N);
   f(&loss_sums, kMaxMicro);
-  plan.push_back({reinterpret_cast<void**>(&emb_scratch), embedding_backward_scratch(N, V)});
   plan.push_back({reinterpret_cast<void**>(&norm_state), kNormStateDoubles * sizeof(double)});
   plan.push_back({reinterpret_cast<void**>(&flags), 64});
   plan.push_back({reinterpret_cast<void**>(&opt_args), sizeof(AdamWArgs)});
@@ -399,10 +470,11 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
       g.precision = c.precision;
       splitk_floats = std::max(splitk_floats, gemm_splitk_workspace_floats(g, device));
     }
-    if (splitk_floats) {
-      f(&splitk_ws, splitk_floats);
-      f(&splitk_ws2, splitk_floats);
-    }
+    if (splitk_floats)
+      for (int li = 0; li < lanes_alloc; ++li) {
+        f(&lanes[li].splitk_ws, splitk_floats);
+        f(&lanes[li].splitk_ws2, splitk_floats);
+      }
   }
   uint64_t total = 0;
   for (auto& pb : plan) total += (pb.second + 255) / 256 * 256;
@@ -415,11 +487,18 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   }
   e = cudaMemset(flags, 0, 64);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&exec_stream, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&wgrad_stream, cudaStreamNonBlocking);
-  for (auto& ev : wg_fork)
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-  for (auto& ev : wg_join)
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  for (int li = 0; li < lanes_alloc; ++li) {
+    Lane& ln = lanes[li];
+    if (li > 0 && e == cudaSuccess) e = cudaStreamCreateWithFlags(&ln.stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ln.wgrad_stream, cudaStreamNonBlocking);
+    for (auto& ev : ln.wg_fork)
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    for (auto& ev : ln.wg_join)
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  }
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&lane_fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&lane_join, cudaEventDisableTiming);
+  select_lane(0);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
   if (e == cudaSuccess)
@@ -525,14 +604,68 @@ cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
 // One whole optimiser step on stream s with the token ids already in ids_dev: zero the gradient
 // arena, the micro-step sweeps, the global-norm pass and clip + AdamW (scalars by value, or from
 // opt_args when the launches are being captured for replay).
+cudaError_t LMTrainer::reduce_buckets(size_t b0, size_t b1, cudaEvent_t ev0, cudaEvent_t ev1,
+                                      cudaEvent_t single_ev, cudaStream_t s) {
+  if (step_lanes == 1) {
+    SPAR_TRY_RAW(cudaEventRecord(single_ev, s));
+    SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, single_ev, 0));
+    for (size_t i = b0; i < b1; ++i)
+      SPAR_TRY_RAW(comm_allreduce_sum(comm, grads + buckets[i].first, buckets[i].second, comm_stream));
+    return cudaSuccess;
+  }
+  SPAR_TRY_RAW(cudaEventRecord(cur_lane == 0 ? ev0 : ev1, s));
+  if (cur_lane != comm_lane) return cudaSuccess;  // the other lane issues the reduction
+  // The other lane's last micro-step was issued earlier, so both events are recorded.
+  SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, ev0, 0));
+  SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, ev1, 0));
+  for (size_t i = b0; i < b1; ++i) {
+    const uint64_t off = buckets[i].first, cnt = buckets[i].second;
+    launches += 1;
+    SPAR_TRY_RAW(launch(add_into_kernel, dim3(grid_for(cnt / 4, 256, sm_count(device) * 8)),
+                        dim3(256), 0, comm_stream, reinterpret_cast<float4*>(lanes[0].grads + off),
+                        reinterpret_cast<const float4*>(lanes[1].grads + off), cnt / 4));
+    SPAR_TRY_RAW(comm_allreduce_sum(comm, lanes[0].grads + off, cnt, comm_stream));
+  }
+  return cudaSuccess;
+}
+
 SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, double lr,
                                     uint64_t step, cudaStream_t s, bool device_args) {
-  cudaError_t e = cudaMemsetAsync(grads, 0, flat * sizeof(float), s);
+  step_lanes = (lanes_alloc == 2 && micro_steps >= 2 && !profiling) ? 2 : 1;
+  comm_lane = static_cast<int>((micro_steps - 1) % step_lanes);  // issues last, runs the reduction
+  lanes[0].stream = s;
+  cudaError_t e = cudaMemsetAsync(lanes[0].grads, 0, flat * sizeof(float), s);
+  if (e == cudaSuccess && step_lanes == 2)
+    e = cudaMemsetAsync(lanes[1].grads, 0, flat * sizeof(float), s);
+  if (e == cudaSuccess && step_lanes == 2) {  // lane 1 starts after the zeroing, on its stream
+    e = cudaEventRecord(lane_fork, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(lanes[1].stream, lane_fork, 0);
+  }
   if (e != cudaSuccess) return runtime(e);
   for (uint64_t m = 0; m < micro_steps; ++m) {
-    last_micro = m + 1 == micro_steps;
-    const SparCudaStatus st = forward_backward(ids_dev + m * N, grad_scale, m, s);
-    if (st.code != 0) return st;
+    const int li = static_cast<int>(m % step_lanes);
+    select_lane(li);
+    last_micro = m + step_lanes >= micro_steps;  // the lane's last micro-step
+    const SparCudaStatus st = forward_backward(ids_dev + m * N, grad_scale, m, lanes[li].stream);
+    if (st.code != 0) {
+      select_lane(0);
+      lanes[0].stream = nullptr;
+      return st;
+    }
+  }
+  select_lane(0);
+  lanes[0].stream = nullptr;  // borrowed for this step only
+  if (step_lanes == 2) {
+    e = cudaEventRecord(lane_join, lanes[1].stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, lane_join, 0);
+    // Without a communicator the lanes' gradients are added here (with one, per bucket).
+    if (e == cudaSuccess && !comm) {
+      launches += 1;
+      e = launch(add_into_kernel, dim3(grid_for(flat / 4, 256, sm_count(device) * 8)), dim3(256), 0,
+                 s, reinterpret_cast<float4*>(lanes[0].grads),
+                 reinterpret_cast<const float4*>(lanes[1].grads), flat / 4);
+    }
+    if (e != cudaSuccess) return runtime(e);
   }
   Slice slice{params, grads, m1, m2, flat};
   launches += 3;
@@ -615,12 +748,11 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   SPAR_CHECK(embedding_backward_launch(G + off_E, dres, ids, N, V, d, emb_scratch, device, s));
   if (comm && last_micro) {
     // Tied embedding and final norm (first and last gradients of the sweep), then join.
-    SPAR_CHECK(cudaEventRecord(tail_ev, s));
-    SPAR_CHECK(cudaStreamWaitEvent(comm_stream, tail_ev, 0));
-    for (size_t i = L; i < buckets.size(); ++i)
-      SPAR_CHECK(comm_allreduce_sum(comm, G + buckets[i].first, buckets[i].second, comm_stream));
-    SPAR_CHECK(cudaEventRecord(comm_done, comm_stream));
-    SPAR_CHECK(cudaStreamWaitEvent(s, comm_done, 0));
+    SPAR_CHECK(reduce_buckets(L, buckets.size(), lanes[0].tail_ev, lanes[1].tail_ev, tail_ev, s));
+    if (step_lanes == 1 || cur_lane == comm_lane) {
+      SPAR_CHECK(cudaEventRecord(comm_done, comm_stream));
+      SPAR_CHECK(cudaStreamWaitEvent(s, comm_done, 0));
+    }
   }
   return ok();
 #undef SPAR_CHECK
@@ -727,10 +859,8 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   if (comm && last_micro) {
     // This layer's gradients are final: reduce them on the communication stream while the
     // remaining layers run backward (bucket = one block's contiguous parameter range).
-    SPAR_TRY(cudaEventRecord(layer_ev[l], s));
-    SPAR_TRY(cudaStreamWaitEvent(comm_stream, layer_ev[l], 0));
-    const auto& bk = buckets[L - 1 - l];  // == [lo.begin, lo.end)
-    SPAR_TRY(comm_allreduce_sum(comm, G + bk.first, bk.second, comm_stream));
+    SPAR_TRY(reduce_buckets(L - 1 - l, L - l, lanes[0].layer_ev.empty() ? nullptr : lanes[0].layer_ev[l],
+                            lanes[1].layer_ev.empty() ? nullptr : lanes[1].layer_ev[l], layer_ev[l], s));
   }
   return cudaSuccess;
 }
@@ -854,6 +984,9 @@ extern "C" SparCudaStatus spar_b200_lm_forward_backward(void* handle, const int3
   DeviceScope scope(t->device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   t->last_micro = last_micro != 0;
+  t->step_lanes = 1;  // a caller-driven micro-step always runs on lane 0
+  t->comm_lane = 0;
+  t->select_lane(0);
   return t->forward_backward(ids, grad_scale, micro_index, static_cast<cudaStream_t>(stream));
 }
 
@@ -982,6 +1115,13 @@ extern "C" SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int wo
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&t->tail_ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&t->comm_done, cudaEventDisableTiming);
+    for (int li = 0; li < t->lanes_alloc; ++li) {
+      LMTrainer::Lane& ln = t->lanes[li];
+      ln.layer_ev.resize(t->L);
+      for (auto& ev : ln.layer_ev)
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ln.tail_ev, cudaEventDisableTiming);
+    }
     if (e != cudaSuccess) return runtime(e);
   }
   return ok();
