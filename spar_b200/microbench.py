@@ -27,14 +27,20 @@ def peaks():
     return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0) / 2.0
 
 
+EAGER = False  # --eager: plain launches, no graph (for per-kernel profilers)
+
+
 def timed(fn, iters=10, warmup=3):
     """Milliseconds per call: `iters` calls captured in one CUDA graph and replayed, so host-side
-    launch and allocation overhead is not timed (eager timing if the call cannot be captured)."""
+    launch and allocation overhead is not timed (eager timing if the call cannot be captured, or
+    with --eager)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     try:
+        if EAGER:
+            raise RuntimeError("eager timing requested")
         s = torch.cuda.Stream()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
@@ -164,7 +170,10 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--epi", default="none", choices=sorted(EPILOGUES))
     ap.add_argument("--batch", type=int, default=16, help="attention: sequences (C5: 16)")
+    ap.add_argument("--eager", action="store_true", help="time plain launches (no CUDA graph)")
     a = ap.parse_args()
+    global EAGER
+    EAGER = a.eager
     if a.kernel == "gemm":
         run_gemm(a.m, a.n, a.k, a.at, a.bt, a.x3, a.iters, a.epi)
     elif a.kernel == "all":
