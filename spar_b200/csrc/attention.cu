@@ -72,6 +72,7 @@ struct AttnParams {
   uint64_t ld_o;  // row stride of O and dO
   float scale, scale_log2;
   uint32_t tiles;  // stationary tiles per (batch, head)
+  uint32_t adjacent_pairs;  // forward: items pair query tiles (2p, 2p+1), heaviest first
   uint32_t total;  // work items
 };
 
@@ -217,8 +218,10 @@ __device__ __forceinline__ void probs64(uint32_t (&v0)[32], uint32_t (&v1)[32], 
 }
 
 // ============================================================================ forward
-// Work item = (batch, head, pair of query tiles t and T-1-t): the two tiles need T+1 key-tile
-// products together, the same for every item, so the causal triangle balances across SMs.
+// Work item = (batch, head, pair of query tiles): t and T-1-t (T+1 key-tile products per item,
+// the same for every item, so the causal triangle balances across SMs at any batch), or, with
+// at least four items per SM, the adjacent tiles 2q and 2q+1 heaviest first (the two tiles' key
+// counts differ by one, so both softmax groups work side by side for the whole item).
 // Four softmax warps per query tile (thread = query row, all 128 scores of its row).
 // The item is a list of jobs: for each key tile j, (A, j) while j <= t, then (B, j). Job g
 // (counted over the CTA's items) computes S = Q_X K_j^T into TMEM score buffer g % 3, its
@@ -258,8 +261,17 @@ __device__ __forceinline__ PairItem decode_pair(const AttnParams& p, uint32_t id
   PairItem it;
   it.b = bh / p.heads;
   it.h = bh - it.b * p.heads;
-  it.ta = pair;
-  it.tb = p.tiles - 1 - pair;
+  if (p.adjacent_pairs) {
+    // Tiles 2q and 2q+1 (q = the pair counted from the end, so the heaviest items come first):
+    // the two tiles' key counts differ by one, so both softmax groups stay busy until the last
+    // key tile. Used when there are enough items per SM to balance their unequal sizes.
+    const uint32_t q = (p.tiles + 1) / 2 - 1 - pair;
+    it.ta = 2 * q;
+    it.tb = min(2 * q + 1, p.tiles - 1);
+  } else {  // tiles t and T-1-t: every item the same T+1 key tiles (balanced at any batch)
+    it.ta = pair;
+    it.tb = p.tiles - 1 - pair;
+  }
   it.na = it.ta != it.tb ? it.ta + 1 : 0;
   it.nb = it.tb + 1;
   return it;
@@ -1230,6 +1242,7 @@ cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_ma
   p.row_inv = row_inv;
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
   p.total = (p.tiles + 1) / 2 * p.bh;  // pairs of query tiles
+  p.adjacent_pairs = p.total >= 4u * static_cast<uint32_t>(sm_count(device)) ? 1u : 0u;
   static bool cfg32[64] = {}, cfg64[64] = {};
   return head_dim == 64 ? launch_attn(attn_fwd_kernel<64>, Fwd<64>::kSmem, p, device, stream, cfg64)
                         : launch_attn(attn_fwd_kernel<32>, Fwd<32>::kSmem, p, device, stream, cfg32);

@@ -1053,13 +1053,23 @@ bool splittable(const SparB200Gemm& g) {
          g.batch[1] <= 1 && g.n % 4 == 0;
 }
 
+// SPAR_B200_SPLITK_MAX caps the K splits the planner may choose (1: never split); default 8.
+uint32_t max_splits() {
+  static const uint32_t v = [] {
+    const char* e = getenv("SPAR_B200_SPLITK_MAX");
+    const int n = e ? atoi(e) : 8;
+    return static_cast<uint32_t>(n < 1 ? 1 : (n > 8 ? 8 : n));
+  }();
+  return v;
+}
+
 // Fewest modelled microseconds over K splits 1..8 (at least 8 k-blocks per split) for tile model t.
 uint32_t best_parts(const SparB200Gemm& g, const TileModel& t, double* best_us) {
   const uint64_t kblocks = (g.k + BK - 1) / BK;
   uint32_t best = 1;
   double us = model_us(g, t, 1);
   if (splittable(g))
-    for (uint32_t parts = 2; parts <= 8 && parts * 8 <= kblocks; ++parts) {
+    for (uint32_t parts = 2; parts <= max_splits() && parts * 8 <= kblocks; ++parts) {
       const double u = model_us(g, t, parts);
       if (u < 0.97 * us) {
         us = u;

@@ -55,6 +55,18 @@ def test_attention_matches_oracle(cuda, b, t, h, dh):
         assert rel_l2(got, ref) <= 2e-3, name
 
 
+def test_attention_adjacent_tile_pairs_match_oracle(cuda):
+    """Enough work items (four or more per SM) switch the forward to adjacent query-tile pairs,
+    heaviest first; an odd tile count leaves one unpaired tile per head."""
+    b, t, h, dh = 24, 384, 16, 64
+    ctx, dqkv, ref_ctx, ref_dqkv, d = _run(cuda, b, t, h, dh, seed=4242)
+    assert rel_l2(ctx, ref_ctx) <= 2e-3
+    for part, name in enumerate(("dq", "dk", "dv")):
+        got = dqkv[..., part * d:(part + 1) * d]
+        ref = ref_dqkv[..., part * d:(part + 1) * d]
+        assert rel_l2(got, ref) <= 2e-3, name
+
+
 def test_attention_is_deterministic(cuda):
     import torch
     from spar_b200 import ops
