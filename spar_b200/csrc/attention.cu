@@ -1252,7 +1252,8 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       const float* row_max, const float* row_inv, float* delta,
                                       float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
                                       uint64_t head_dim, int device, cudaStream_t stream,
-                                      const float* rope_table) {
+                                      const float* rope_table, cudaStream_t key_stream,
+                                      cudaEvent_t fork, cudaEvent_t join) {
   AttnParams p;
   base_params(p, batch, seq, heads, head_dim);
   const uint64_t d = heads * head_dim;
@@ -1280,12 +1281,24 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
   if (e != cudaSuccess) return e;
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
   p.total = p.tiles * p.bh;
+  // The query and key kernels only share inputs (they write dq and dk / dv): on a second stream
+  // the key kernel's CTAs take the SMs that the query kernel's last items leave idle.
+  cudaStream_t ks = stream;
+  if (key_stream && fork && join) {
+    e = cudaEventRecord(fork, stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(key_stream, fork, 0);
+    if (e != cudaSuccess) return e;
+    ks = key_stream;
+  }
   e = head_dim == 64
           ? launch_attn(attn_bwd_q_kernel<64>, BwdQ<64>::kSmem, p, device, stream, q64)
-                      : launch_attn(attn_bwd_q_kernel<32>, BwdQ<32>::kSmem, p, device, stream, q32);
+          : launch_attn(attn_bwd_q_kernel<32>, BwdQ<32>::kSmem, p, device, stream, q32);
   if (e != cudaSuccess) return e;
-  return head_dim == 64 ? launch_attn(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, p, device, stream, k64)
-                        : launch_attn(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, p, device, stream, k32);
+  e = head_dim == 64 ? launch_attn(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, p, device, ks, k64)
+                     : launch_attn(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, p, device, ks, k32);
+  if (e != cudaSuccess || ks == stream) return e;
+  e = cudaEventRecord(join, ks);
+  return e == cudaSuccess ? cudaStreamWaitEvent(stream, join, 0) : e;
 }
 
 namespace {

@@ -28,7 +28,9 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       const float* row_max, const float* row_inv, float* delta,
                                       float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
                                       uint64_t head_dim, int device, cudaStream_t stream,
-                                      const float* rope_table = nullptr);
+                                      const float* rope_table = nullptr,
+                                      cudaStream_t key_stream = nullptr, cudaEvent_t fork = nullptr,
+                                      cudaEvent_t join = nullptr);
 
 // Spar's stable sigmoid (src/ops/unary.cpp:55-61 / cuda_kernels.cu:105-111), in fp32.
 __device__ __forceinline__ float stable_sigmoid(float v) {

@@ -232,6 +232,8 @@ class LMTrainer {
     void* emb_scratch = nullptr;
     cudaStream_t stream = nullptr, wgrad_stream = nullptr;
     cudaEvent_t wg_fork[5] = {}, wg_join[4] = {};
+    cudaStream_t key_stream = nullptr;  // the attention backward's key kernel
+    cudaEvent_t key_fork = nullptr, key_join = nullptr;
     std::vector<cudaEvent_t> layer_ev;  // data parallel: block l done in the lane's last micro-step
     cudaEvent_t tail_ev = nullptr;
   };
@@ -326,6 +328,9 @@ LMTrainer::~LMTrainer() {
     for (auto ev : ln.wg_join)
       if (ev) cudaEventDestroy(ev);
     for (auto ev : ln.layer_ev) cudaEventDestroy(ev);
+    if (ln.key_fork) cudaEventDestroy(ln.key_fork);
+    if (ln.key_join) cudaEventDestroy(ln.key_join);
+    if (ln.key_stream) cudaStreamDestroy(ln.key_stream);
     if (ln.tail_ev) cudaEventDestroy(ln.tail_ev);
     if (ln.wgrad_stream) cudaStreamDestroy(ln.wgrad_stream);
     if (&ln != &lanes[0] && ln.stream) cudaStreamDestroy(ln.stream);  // lane 0 borrows the step's
@@ -491,6 +496,9 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     Lane& ln = lanes[li];
     if (li > 0 && e == cudaSuccess) e = cudaStreamCreateWithFlags(&ln.stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ln.wgrad_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ln.key_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ln.key_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ln.key_join, cudaEventDisableTiming);
     for (auto& ev : ln.wg_fork)
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
     for (auto& ev : ln.wg_join)
@@ -763,8 +771,12 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
 cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
   if (fused_attention) {
     launches += 1;  // query and key kernels (one counted with the softmax in layer_backward)
+    const Lane& ln = lanes[cur_lane];
+    const bool two = !profiling;
     return attention_backward_launch(A.qkv, A.ctx, dtmp, A.stats, A.stats + B * H * T, dS, dqkv,
-                                     B, T, H, dh, device, s, cfg.use_rope ? rope_tab : nullptr);
+                                     B, T, H, dh, device, s, cfg.use_rope ? rope_tab : nullptr,
+                                     two ? ln.key_stream : nullptr, two ? ln.key_fork : nullptr,
+                                     two ? ln.key_join : nullptr);
   }
   const uint64_t ld = 3 * d;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
