@@ -63,17 +63,24 @@ __global__ void init_normal_kernel(float* dst, uint64_t rows, uint64_t cols, uin
   }
 }
 
-// a += b, n float4 (the second lane's gradients into the first, one fixed order).
-__global__ void add_into_kernel(float4* __restrict__ a, const float4* __restrict__ b, uint64_t n) {
+// a += b (+ c (+ d)), n float4, summed in that order: the other lanes' gradients into lane 0's.
+__global__ void add_lanes_kernel(float4* __restrict__ a, const float4* __restrict__ b,
+                                 const float4* __restrict__ c, const float4* __restrict__ d,
+                                 uint64_t n) {
   pdl_begin();
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
     float4 x = a[i];
-    const float4 y = b[i];
-    x.x += y.x;
-    x.y += y.y;
-    x.z += y.z;
-    x.w += y.w;
+    const float4* src[3] = {b, c, d};
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      if (!src[k]) break;
+      const float4 y = src[k][i];
+      x.x += y.x;
+      x.y += y.y;
+      x.z += y.z;
+      x.w += y.w;
+    }
     a[i] = x;
   }
 }
@@ -217,11 +224,11 @@ class LMTrainer {
   cudaStream_t wgrad_stream = nullptr;
   cudaEvent_t wg_fork[5] = {}, wg_join[4] = {};
   bool wgrad_enabled = !(getenv("SPAR_B200_WGRAD_STREAM") && getenv("SPAR_B200_WGRAD_STREAM")[0] == '0');
-  // Two micro-steps in flight at small micro-batches ("lanes"): each lane owns a full set of
-  // activation and workspace buffers, a stream pair and a gradient arena. Lane 1 runs every other
-  // micro-step beside lane 0, so two narrow micro-steps fill the SMs like one twice as wide;
-  // lane 1's gradients are added into lane 0's in a fixed order (per all-reduce bucket ahead of
-  // the data-parallel reduction, or once after the last micro-step), so steps stay deterministic.
+  // Several micro-steps in flight at small micro-batches ("lanes"): each lane owns a full set of
+  // activation and workspace buffers, its streams and a gradient arena. Micro-step m runs on lane
+  // m % lanes beside the others, so narrow micro-steps fill the SMs like one wider one; the other
+  // lanes' gradients are added into lane 0's in lane order (per all-reduce bucket ahead of the
+  // data-parallel reduction, or once after the last micro-step), so steps stay deterministic.
   // The working members above (acts, dres, ..., grads, wgrad_stream) are the selected lane's.
   struct Lane {
     std::vector<LayerActs> acts;
@@ -234,14 +241,16 @@ class LMTrainer {
     cudaEvent_t wg_fork[5] = {}, wg_join[4] = {};
     cudaStream_t key_stream = nullptr;  // the attention backward's key kernel
     cudaEvent_t key_fork = nullptr, key_join = nullptr;
+    cudaEvent_t done = nullptr;  // the lane's last micro-step finished (join into the step)
     std::vector<cudaEvent_t> layer_ev;  // data parallel: block l done in the lane's last micro-step
     cudaEvent_t tail_ev = nullptr;
   };
-  Lane lanes[2];
-  int lanes_alloc = 1;  // lanes with buffers (2 when the micro-batch is small)
+  static constexpr int kMaxLanes = 4;
+  Lane lanes[kMaxLanes];
+  int lanes_alloc = 1;  // lanes with buffers (2 or 4 when the micro-batch is small)
   int cur_lane = 0, step_lanes = 1, comm_lane = 0;
-  cudaEvent_t lane_fork = nullptr, lane_join = nullptr;
-  // SPAR_B200_LANES: 0 = never, 2 = at any micro-batch, unset / 1 = micro-batches of <= 4 sequences.
+  cudaEvent_t lane_fork = nullptr, lane_join[kMaxLanes] = {};
+  // SPAR_B200_LANES: 0 = never, 2 / 4 = that many at any micro-batch, unset / 1 = by micro-batch.
   int lanes_mode = getenv("SPAR_B200_LANES") ? getenv("SPAR_B200_LANES")[0] - '0' : 1;
   void select_lane(int i) {
     Lane& ln = lanes[i];
@@ -311,8 +320,10 @@ class LMTrainer {
   // them are final on stream s. With two lanes, each lane records lane_ev after its last
   // micro-step has produced them; the lane that issues last (comm_lane) then adds lane 1's
   // buckets into lane 0's and reduces lane 0's.
-  cudaError_t reduce_buckets(size_t b0, size_t b1, cudaEvent_t ev0, cudaEvent_t ev1,
-                             cudaEvent_t single_ev, cudaStream_t s);
+  cudaError_t reduce_buckets(size_t b0, size_t b1, int layer, cudaEvent_t single_ev,
+                             cudaStream_t s);
+  // lanes[0].grads[off, off + count) += the other step lanes' gradients, in lane order.
+  cudaError_t merge_lanes(uint64_t off, uint64_t count, cudaStream_t s);
 };
 
 LMTrainer::~LMTrainer() {
@@ -336,7 +347,8 @@ LMTrainer::~LMTrainer() {
     if (&ln != &lanes[0] && ln.stream) cudaStreamDestroy(ln.stream);  // lane 0 borrows the step's
   }
   if (lane_fork) cudaEventDestroy(lane_fork);
-  if (lane_join) cudaEventDestroy(lane_join);
+  for (auto ev : lane_join)
+    if (ev) cudaEventDestroy(ev);
   for (auto& g : graphs) cudaGraphExecDestroy(g.second.exec);
   if (exec_stream) cudaStreamDestroy(exec_stream);
   if (ev_in) cudaEventDestroy(ev_in);
@@ -398,7 +410,14 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   std::vector<std::pair<void**, uint64_t>> plan;  // (pointer slot, bytes)
   auto f = [&](float** p, uint64_t n) { plan.push_back({reinterpret_cast<void**>(p), n * 4}); };
   // Two lanes (two micro-steps in flight) when a micro-step is too narrow to fill the GPU.
-  lanes_alloc = (c.precision == SPAR_B200_TF32 && (lanes_mode == 2 || (lanes_mode == 1 && B <= 4))) ? 2 : 1;
+  // Two lanes at micro-batches of <= 4 sequences (SPAR_B200_LANES=2 / 4 force two / four at any
+  // micro-batch; four measured no faster than two at micro-batch 2: the merge grows, the SMs
+  // are already shared).
+  lanes_alloc = 1;
+  if (c.precision == SPAR_B200_TF32) {
+    if (lanes_mode == 2 || lanes_mode == 4) lanes_alloc = lanes_mode;
+    else if (lanes_mode == 1) lanes_alloc = B <= 4 ? 2 : 1;
+  }
   for (int li = 0; li < lanes_alloc; ++li) {
     Lane& ln = lanes[li];
     ln.acts.resize(L);
@@ -505,7 +524,8 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
   }
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&lane_fork, cudaEventDisableTiming);
-  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&lane_join, cudaEventDisableTiming);
+  for (int li = 0; li < lanes_alloc; ++li)
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&lane_join[li], cudaEventDisableTiming);
   select_lane(0);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
@@ -612,8 +632,16 @@ cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
 // One whole optimiser step on stream s with the token ids already in ids_dev: zero the gradient
 // arena, the micro-step sweeps, the global-norm pass and clip + AdamW (scalars by value, or from
 // opt_args when the launches are being captured for replay).
-cudaError_t LMTrainer::reduce_buckets(size_t b0, size_t b1, cudaEvent_t ev0, cudaEvent_t ev1,
-                                      cudaEvent_t single_ev, cudaStream_t s) {
+cudaError_t LMTrainer::merge_lanes(uint64_t off, uint64_t count, cudaStream_t s) {
+  const float4* src[3] = {nullptr, nullptr, nullptr};
+  for (int li = 1; li < step_lanes; ++li) src[li - 1] = reinterpret_cast<const float4*>(lanes[li].grads + off);
+  launches += 1;
+  return launch(add_lanes_kernel, dim3(grid_for(count / 4, 256, sm_count(device) * 8)), dim3(256), 0,
+                s, reinterpret_cast<float4*>(lanes[0].grads + off), src[0], src[1], src[2], count / 4);
+}
+
+cudaError_t LMTrainer::reduce_buckets(size_t b0, size_t b1, int layer, cudaEvent_t single_ev,
+                                      cudaStream_t s) {
   if (step_lanes == 1) {
     SPAR_TRY_RAW(cudaEventRecord(single_ev, s));
     SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, single_ev, 0));
@@ -621,17 +649,14 @@ cudaError_t LMTrainer::reduce_buckets(size_t b0, size_t b1, cudaEvent_t ev0, cud
       SPAR_TRY_RAW(comm_allreduce_sum(comm, grads + buckets[i].first, buckets[i].second, comm_stream));
     return cudaSuccess;
   }
-  SPAR_TRY_RAW(cudaEventRecord(cur_lane == 0 ? ev0 : ev1, s));
-  if (cur_lane != comm_lane) return cudaSuccess;  // the other lane issues the reduction
-  // The other lane's last micro-step was issued earlier, so both events are recorded.
-  SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, ev0, 0));
-  SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, ev1, 0));
+  auto ev = [&](int li) { return layer >= 0 ? lanes[li].layer_ev[layer] : lanes[li].tail_ev; };
+  SPAR_TRY_RAW(cudaEventRecord(ev(cur_lane), s));
+  if (cur_lane != comm_lane) return cudaSuccess;  // the lane issued last runs the reduction
+  // Every other lane's last micro-step was issued earlier, so all events are recorded.
+  for (int li = 0; li < step_lanes; ++li) SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, ev(li), 0));
   for (size_t i = b0; i < b1; ++i) {
     const uint64_t off = buckets[i].first, cnt = buckets[i].second;
-    launches += 1;
-    SPAR_TRY_RAW(launch(add_into_kernel, dim3(grid_for(cnt / 4, 256, sm_count(device) * 8)),
-                        dim3(256), 0, comm_stream, reinterpret_cast<float4*>(lanes[0].grads + off),
-                        reinterpret_cast<const float4*>(lanes[1].grads + off), cnt / 4));
+    SPAR_TRY_RAW(merge_lanes(off, cnt, comm_stream));
     SPAR_TRY_RAW(comm_allreduce_sum(comm, lanes[0].grads + off, cnt, comm_stream));
   }
   return cudaSuccess;
@@ -639,15 +664,18 @@ cudaError_t LMTrainer::reduce_buckets(size_t b0, size_t b1, cudaEvent_t ev0, cud
 
 SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, double lr,
                                     uint64_t step, cudaStream_t s, bool device_args) {
-  step_lanes = (lanes_alloc == 2 && micro_steps >= 2 && !profiling) ? 2 : 1;
+  step_lanes = (lanes_alloc > 1 && micro_steps >= 2 && !profiling)
+                   ? static_cast<int>(std::min<uint64_t>(lanes_alloc, micro_steps))
+                   : 1;
   comm_lane = static_cast<int>((micro_steps - 1) % step_lanes);  // issues last, runs the reduction
   lanes[0].stream = s;
-  cudaError_t e = cudaMemsetAsync(lanes[0].grads, 0, flat * sizeof(float), s);
-  if (e == cudaSuccess && step_lanes == 2)
-    e = cudaMemsetAsync(lanes[1].grads, 0, flat * sizeof(float), s);
-  if (e == cudaSuccess && step_lanes == 2) {  // lane 1 starts after the zeroing, on its stream
+  cudaError_t e = cudaSuccess;
+  for (int li = 0; li < step_lanes && e == cudaSuccess; ++li)
+    e = cudaMemsetAsync(lanes[li].grads, 0, flat * sizeof(float), s);
+  if (e == cudaSuccess && step_lanes > 1) {  // the other lanes start after the zeroing
     e = cudaEventRecord(lane_fork, s);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(lanes[1].stream, lane_fork, 0);
+    for (int li = 1; li < step_lanes && e == cudaSuccess; ++li)
+      e = cudaStreamWaitEvent(lanes[li].stream, lane_fork, 0);
   }
   if (e != cudaSuccess) return runtime(e);
   for (uint64_t m = 0; m < micro_steps; ++m) {
@@ -663,16 +691,13 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
   }
   select_lane(0);
   lanes[0].stream = nullptr;  // borrowed for this step only
-  if (step_lanes == 2) {
-    e = cudaEventRecord(lane_join, lanes[1].stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, lane_join, 0);
-    // Without a communicator the lanes' gradients are added here (with one, per bucket).
-    if (e == cudaSuccess && !comm) {
-      launches += 1;
-      e = launch(add_into_kernel, dim3(grid_for(flat / 4, 256, sm_count(device) * 8)), dim3(256), 0,
-                 s, reinterpret_cast<float4*>(lanes[0].grads),
-                 reinterpret_cast<const float4*>(lanes[1].grads), flat / 4);
+  if (step_lanes > 1) {
+    for (int li = 1; li < step_lanes && e == cudaSuccess; ++li) {
+      e = cudaEventRecord(lane_join[li], lanes[li].stream);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(s, lane_join[li], 0);
     }
+    // Without a communicator the lanes' gradients are added here (with one, per bucket).
+    if (e == cudaSuccess && !comm) e = merge_lanes(0, flat, s);
     if (e != cudaSuccess) return runtime(e);
   }
   Slice slice{params, grads, m1, m2, flat};
@@ -756,7 +781,7 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   SPAR_CHECK(embedding_backward_launch(G + off_E, dres, ids, N, V, d, emb_scratch, device, s));
   if (comm && last_micro) {
     // Tied embedding and final norm (first and last gradients of the sweep), then join.
-    SPAR_CHECK(reduce_buckets(L, buckets.size(), lanes[0].tail_ev, lanes[1].tail_ev, tail_ev, s));
+    SPAR_CHECK(reduce_buckets(L, buckets.size(), -1, tail_ev, s));
     if (step_lanes == 1 || cur_lane == comm_lane) {
       SPAR_CHECK(cudaEventRecord(comm_done, comm_stream));
       SPAR_CHECK(cudaStreamWaitEvent(s, comm_done, 0));
@@ -871,8 +896,7 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   if (comm && last_micro) {
     // This layer's gradients are final: reduce them on the communication stream while the
     // remaining layers run backward (bucket = one block's contiguous parameter range).
-    SPAR_TRY(reduce_buckets(L - 1 - l, L - l, lanes[0].layer_ev.empty() ? nullptr : lanes[0].layer_ev[l],
-                            lanes[1].layer_ev.empty() ? nullptr : lanes[1].layer_ev[l], layer_ev[l], s));
+    SPAR_TRY(reduce_buckets(L - 1 - l, L - l, static_cast<int>(l), layer_ev[l], s));
   }
   return cudaSuccess;
 }

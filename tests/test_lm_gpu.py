@@ -163,11 +163,11 @@ def _lanes_cfg():
 
     from spar_b200.lm import C1
 
-    return replace(C1, precision=0, micro_batch=2)  # small micro-batch: two lanes in flight
+    return replace(C1, precision=0, micro_batch=2)  # small micro-batch: several lanes in flight
 
 
-def test_two_lanes_match_oracle(cuda):
-    """Micro-batch 2 runs two micro-steps at once (lanes with their own buffers and gradient
+def test_lanes_match_oracle(cuda):
+    """Micro-batch 2 runs its micro-steps side by side (lanes with their own buffers and gradient
     arenas, added in a fixed order): one step of 4 micro-steps against the oracle."""
     cfg = _lanes_cfg()
     (loss, _, flags, grads, new), (o_loss, o_grads, o_new) = _run(cfg, 4)
@@ -178,7 +178,7 @@ def test_two_lanes_match_oracle(cuda):
     assert rel_l2(_flat(new, names), _flat(o_new, names)) <= 2e-3
 
 
-def test_two_lanes_match_one_lane_and_repeat(cuda, monkeypatch):
+def test_lanes_match_one_lane_and_repeat(cuda, monkeypatch):
     """The same steps with lanes switched off (SPAR_B200_LANES=0) differ only by the order of the
     gradient sums; with lanes, repeated runs (eager first step, then graph replays) are bitwise
     equal."""
