@@ -241,7 +241,6 @@ class LMTrainer {
     cudaEvent_t wg_fork[5] = {}, wg_join[4] = {};
     cudaStream_t key_stream = nullptr;  // the attention backward's key kernel
     cudaEvent_t key_fork = nullptr, key_join = nullptr;
-    cudaEvent_t done = nullptr;  // the lane's last micro-step finished (join into the step)
     std::vector<cudaEvent_t> layer_ev;  // data parallel: block l done in the lane's last micro-step
     cudaEvent_t tail_ev = nullptr;
   };
