@@ -1135,13 +1135,20 @@ done:
 }
 
 // Attaches a communicator from spar_b200_comm_init: gradients of each block are then summed
-// across ranks during the last micro-step's backward pass.
+// across ranks during the last micro-step's backward pass. A one-rank communicator is accepted
+// (the bucket reductions then run as identities); comm == nullptr with world_size 1 detaches.
 extern "C" SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int world_size) {
   if (!handle || world_size < 1 || (world_size > 1 && !comm)) return invalid();
   LMTrainer* t = as_trainer(handle);
   DeviceScope scope(t->device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
-  t->comm = world_size > 1 ? comm : nullptr;
+  if (t->comm != comm && !t->graphs.empty()) {  // captured steps hold the old reductions
+    cudaError_t e = cudaDeviceSynchronize();
+    for (auto& g : t->graphs) cudaGraphExecDestroy(g.second.exec);
+    t->graphs.clear();
+    if (e != cudaSuccess) return runtime(e);
+  }
+  t->comm = comm;
   t->world = world_size;
   if (t->comm && !t->comm_stream) {
     cudaError_t e = cudaStreamCreateWithFlags(&t->comm_stream, cudaStreamNonBlocking);

@@ -202,3 +202,52 @@ def test_lanes_match_one_lane_and_repeat(cuda, monkeypatch):
     assert a_l == b_l and np.array_equal(a, b)
     assert rel_l2(a, c) <= 1e-5
     np.testing.assert_allclose(a_l, c_l, rtol=1e-5)
+
+
+def _one_rank_comm():
+    import ctypes
+
+    from spar_b200 import _lib
+
+    lib = _lib.load()
+    uid = ctypes.create_string_buffer(128)
+    _lib.check("spar_b200_comm_unique_id", lib.spar_b200_comm_unique_id(uid, 128))
+    comm = ctypes.c_void_p()
+    _lib.check("spar_b200_comm_init", lib.spar_b200_comm_init(uid, 0, 1, 0, ctypes.byref(comm)))
+    return lib, comm
+
+
+@pytest.mark.parametrize("lanes", ["0", "2", "4"])
+def test_one_rank_communicator_matches_no_communicator(cuda, monkeypatch, lanes):
+    """A one-rank NCCL communicator drives the data-parallel path on one GPU: per-layer bucket
+    reductions on the communication stream during the last micro-steps, with the lanes' gradients
+    merged per bucket (lanes on) instead of once at step end. The all-reduce over one rank is an
+    identity and the merge order is the same, so every step is bitwise equal to the same steps
+    without a communicator (eager first step, then graph replays)."""
+    from spar_b200.lm import DecoderLM
+
+    monkeypatch.setenv("SPAR_B200_LANES", lanes)
+    cfg = _lanes_cfg()
+    params, ids = _setup(cfg, 4)
+
+    def steps(with_comm):
+        lm = DecoderLM(cfg, 0)
+        lm.load_state_dict(params)
+        lib = comm = None
+        if with_comm:
+            lib, comm = _one_rank_comm()
+            lm.attach_comm(comm, 1)
+        out = [lm.train_step(ids, 3e-4, step=s) for s in range(1, 4)]
+        state = _flat(lm.state_dict(), lm.names)
+        grads = _flat(lm.state_dict("grad"), lm.names)
+        lm.close()
+        if comm is not None:
+            lib.spar_b200_comm_destroy(comm, 0)
+        return out, state, grads
+
+    a_out, a, a_g = steps(False)
+    b_out, b, b_g = steps(True)
+    assert [o[2] for o in b_out] == [(0, 0)] * 3
+    assert [o[0] for o in a_out] == [o[0] for o in b_out]
+    assert [o[1] for o in a_out] == [o[1] for o in b_out]
+    assert np.array_equal(a_g, b_g) and np.array_equal(a, b)
