@@ -304,6 +304,12 @@ struct SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* ids, 
                                               double* grad_norm_out, int32_t* flags_out,
                                               void* stream);
 struct SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int world_size);
+/* Sharded optimiser (data parallel, on by default when world_size > 1): after a train step each */
+/* rank's arenas hold only its own pieces of the reduced gradients, the updated moments and (until */
+/* the next step's start) the updated parameters. spar_b200_lm_gather, called by EVERY rank in   */
+/* the same order, all-gathers one arena (which as in flat_buffer) ordered on `stream`; until     */
+/* then spar_b200_lm_parameter_copy refuses reads of it (code 1, cuda_error cudaErrorNotReady).   */
+struct SparCudaStatus spar_b200_lm_gather(void* handle, int which, void* stream);
 /* Host-only queries of the parameter-arena layout a config produces (no device work, usable   */
 /* without a GPU): flat size in floats, the named tensors (Spar's names, offset into the arena, */
 /* rows x cols with row stride ld; cols == 0 for vectors) and the gradient all-reduce buckets    */
@@ -317,6 +323,13 @@ struct SparCudaStatus spar_b200_lm_layout_tensor(const struct SparB200LMConfig* 
                                                  uint64_t* ld);
 struct SparCudaStatus spar_b200_lm_layout_bucket(const struct SparB200LMConfig* config,
                                                  uint64_t index, uint64_t* offset, uint64_t* count);
+/* Rank `rank` of `world` under the sharded optimiser: of bucket `index`, the reduce-scattered    */
+/* piece [own_offset, own_offset + shard) it updates (shard a multiple of 64 floats) and the      */
+/* uneven tail [tail_offset, tail_offset + tail_count) all-reduced and updated on every rank.     */
+struct SparCudaStatus spar_b200_lm_layout_shard(const struct SparB200LMConfig* config,
+                                                uint64_t index, int world, int rank,
+                                                uint64_t* own_offset, uint64_t* shard,
+                                                uint64_t* tail_offset, uint64_t* tail_count);
 struct SparCudaStatus spar_b200_lm_read_losses(void* handle, float* host, uint64_t count);
 /* Event timing of every tensor-core GEMM launch (for roofline accounting) and a kernel-launch */
 /* counter; profile_read synchronises the device.                                              */

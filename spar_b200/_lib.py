@@ -92,10 +92,13 @@ SIGNATURES = {
     "spar_b200_lm_train_step": (S, [p, p, i, u64, d, u64, POINTER(c_float), POINTER(c_double),
                                     POINTER(c_int32), p]),
     "spar_b200_lm_set_comm": (S, [p, p, i]),
+    "spar_b200_lm_gather": (S, [p, i, p]),
     "spar_b200_lm_layout": (S, [p, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
     "spar_b200_lm_layout_tensor": (S, [p, u64, c_char_p, u64, POINTER(c_uint64), POINTER(c_uint64),
                                        POINTER(c_uint64), POINTER(c_uint64)]),
     "spar_b200_lm_layout_bucket": (S, [p, u64, POINTER(c_uint64), POINTER(c_uint64)]),
+    "spar_b200_lm_layout_shard": (S, [p, u64, i, i, POINTER(c_uint64), POINTER(c_uint64),
+                                      POINTER(c_uint64), POINTER(c_uint64)]),
     "spar_b200_lm_read_losses": (S, [p, p, u64]),
     "spar_b200_warmup_cosine": (d, [d, d, u64, u64, u64]),
     "spar_b200_lm_profile": (S, [p, i]),

@@ -22,6 +22,10 @@ struct NcclApi {
   ncclResult_t (*init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*reduce_scatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                                 ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
   ncclResult_t (*destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*abort)(ncclComm_t) = nullptr;
   ncclResult_t (*async_error)(ncclComm_t, ncclResult_t*) = nullptr;
@@ -39,11 +43,14 @@ const NcclApi& api() {
     a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
     a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.reduce_scatter = reinterpret_cast<decltype(a.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
     a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
     a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
     a.async_error = reinterpret_cast<decltype(a.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
-    a.ok = a.get_unique_id && a.init_rank && a.all_reduce && a.destroy && a.abort;
+    a.ok = a.get_unique_id && a.init_rank && a.all_reduce && a.reduce_scatter && a.all_gather &&
+           a.destroy && a.abort;
   });
   return a;
 }
@@ -64,6 +71,35 @@ cudaError_t comm_allreduce_sum(void* comm, float* data, uint64_t count, cudaStre
   const ncclResult_t r = api().all_reduce(data, data, count, ncclFloat32, ncclSum, c->nccl, stream);
   return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
 }
+
+cudaError_t comm_allreduce_sum_f64(void* comm, double* data, uint64_t count, cudaStream_t stream) {
+  const Comm* c = static_cast<const Comm*>(comm);
+  if (!c || !api().ok) return cudaErrorInvalidValue;
+  const ncclResult_t r = api().all_reduce(data, data, count, ncclFloat64, ncclSum, c->nccl, stream);
+  return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+// In place: data[world * shard] in, the sum of every rank's data[rank * shard, + shard) lands
+// there (the rest of data is left unspecified).
+cudaError_t comm_reduce_scatter_sum(void* comm, float* data, uint64_t shard, cudaStream_t stream) {
+  const Comm* c = static_cast<const Comm*>(comm);
+  if (!c || !api().ok) return cudaErrorInvalidValue;
+  const ncclResult_t r = api().reduce_scatter(data, data + static_cast<uint64_t>(c->rank) * shard,
+                                              shard, ncclFloat32, ncclSum, c->nccl, stream);
+  return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+// In place: every rank's data[rank * shard, + shard) is copied to the same place on all ranks.
+cudaError_t comm_all_gather(void* comm, float* data, uint64_t shard, cudaStream_t stream) {
+  const Comm* c = static_cast<const Comm*>(comm);
+  if (!c || !api().ok) return cudaErrorInvalidValue;
+  const ncclResult_t r = api().all_gather(data + static_cast<uint64_t>(c->rank) * shard, data,
+                                          shard, ncclFloat32, c->nccl, stream);
+  return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+int comm_rank(void* comm) { return comm ? static_cast<const Comm*>(comm)->rank : 0; }
+int comm_size(void* comm) { return comm ? static_cast<const Comm*>(comm)->world : 1; }
 
 }  // namespace spar_b200
 

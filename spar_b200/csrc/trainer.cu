@@ -33,6 +33,11 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
 uint64_t gemm_split_workspace_floats(const SparB200Gemm& g);
 uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device);
 cudaError_t comm_allreduce_sum(void* comm, float* data, uint64_t count, cudaStream_t stream);
+cudaError_t comm_allreduce_sum_f64(void* comm, double* data, uint64_t count, cudaStream_t stream);
+cudaError_t comm_reduce_scatter_sum(void* comm, float* data, uint64_t shard, cudaStream_t stream);
+cudaError_t comm_all_gather(void* comm, float* data, uint64_t shard, cudaStream_t stream);
+int comm_rank(void* comm);
+int comm_size(void* comm);
 
 namespace {
 
@@ -128,6 +133,24 @@ struct ParamLayout {
     return b;
   }
 };
+
+// One rank's part of a gradient bucket [off, off + count) under the sharded optimiser: `world`
+// pieces of `shard` floats (a multiple of 64, so every piece stays 256-byte aligned) are
+// reduce-scattered, piece `rank` (at own_off) is this rank's to update, and the tail that does not
+// split evenly, [rem_off, rem_off + rem_count), is all-reduced and updated on every rank.
+struct BucketShard {
+  uint64_t off, shard, own_off, rem_off, rem_count;
+};
+
+BucketShard shard_bucket(uint64_t off, uint64_t count, int world, int rank) {
+  BucketShard b;
+  b.off = off;
+  b.shard = count / static_cast<uint64_t>(world) / kAlign * kAlign;
+  b.own_off = off + static_cast<uint64_t>(rank) * b.shard;
+  b.rem_off = off + static_cast<uint64_t>(world) * b.shard;
+  b.rem_count = off + count - b.rem_off;
+  return b;
+}
 
 SparCudaStatus plan_params(const SparB200LMConfig& c, ParamLayout& pl) {
   const uint64_t V = c.vocab_size, d = c.model_dim, F = c.hidden_dim, L = c.num_layers,
@@ -276,6 +299,31 @@ class LMTrainer {
   cudaStream_t comm_stream = nullptr;
   std::vector<cudaEvent_t> layer_ev;
   cudaEvent_t tail_ev = nullptr, comm_done = nullptr;
+  // Sharded optimiser state (data parallel): each bucket's gradients are reduce-scattered instead
+  // of all-reduced, and every rank runs the norm pass (its partial sum of squares all-reduced)
+  // and AdamW on its own piece of each bucket only: 1 / world of the optimiser's HBM traffic. The
+  // updated parameter pieces are all-gathered at the start of the next step, bucket by bucket in
+  // the order the forward pass first reads them (embedding, blocks 0.., final norm), and each
+  // micro-step's forward waits for a bucket only where it first reads it, so the gathers overlap
+  // the forward pass as the reductions overlap the backward. Moments stay sharded; gradients,
+  // moments and parameters read back through the C ABI need spar_b200_lm_gather on every rank.
+  // SPAR_B200_SHARD_OPT=0 keeps the replicated all-reduce + whole-arena AdamW; =1 shards with a
+  // one-rank communicator too (the path's test on one GPU); default: world > 1.
+  int shard_mode = getenv("SPAR_B200_SHARD_OPT") ? getenv("SPAR_B200_SHARD_OPT")[0] - '0' : -1;
+  bool sharded = false;       // a communicator is attached and the optimiser is sharded
+  bool sharded_step = false;  // the step being issued reduce-scatters (train_step only)
+  int rank = 0;
+  std::vector<BucketShard> shard_plan;    // per bucket, issue order
+  std::vector<Slice> own_slices, norm_slices;
+  std::vector<cudaEvent_t> gather_ev;     // per bucket: its parameters gathered
+  cudaEvent_t gather_fork = nullptr;
+  bool stale[4] = {};  // arena (parameters, gradients, moments) holds other ranks' pieces stale
+  cudaError_t gather_params(cudaStream_t s);
+  cudaError_t gather_arena(int which, cudaStream_t s);
+  cudaError_t reduce_bucket(size_t i, float* g);
+  cudaError_t wait_gather(size_t bucket, cudaStream_t s) {
+    return sharded_step ? cudaStreamWaitEvent(s, gather_ev[bucket], 0) : cudaSuccess;
+  }
   uint64_t split_floats = 0;
   // Live profiling of the tensor-core GEMMs (CUDA events around every launch on its stream).
   bool profiling = false;
@@ -329,6 +377,8 @@ LMTrainer::~LMTrainer() {
   DeviceScope scope(device);
   cudaDeviceSynchronize();
   for (auto ev : layer_ev) cudaEventDestroy(ev);
+  for (auto ev : gather_ev) cudaEventDestroy(ev);
+  if (gather_fork) cudaEventDestroy(gather_fork);
   if (tail_ev) cudaEventDestroy(tail_ev);
   if (comm_done) cudaEventDestroy(comm_done);
   if (comm_stream) cudaStreamDestroy(comm_stream);
@@ -644,8 +694,7 @@ cudaError_t LMTrainer::reduce_buckets(size_t b0, size_t b1, int layer, cudaEvent
   if (step_lanes == 1) {
     SPAR_TRY_RAW(cudaEventRecord(single_ev, s));
     SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, single_ev, 0));
-    for (size_t i = b0; i < b1; ++i)
-      SPAR_TRY_RAW(comm_allreduce_sum(comm, grads + buckets[i].first, buckets[i].second, comm_stream));
+    for (size_t i = b0; i < b1; ++i) SPAR_TRY_RAW(reduce_bucket(i, grads));
     return cudaSuccess;
   }
   auto ev = [&](int li) { return layer >= 0 ? lanes[li].layer_ev[layer] : lanes[li].tail_ev; };
@@ -656,8 +705,49 @@ cudaError_t LMTrainer::reduce_buckets(size_t b0, size_t b1, int layer, cudaEvent
   for (size_t i = b0; i < b1; ++i) {
     const uint64_t off = buckets[i].first, cnt = buckets[i].second;
     SPAR_TRY_RAW(merge_lanes(off, cnt, comm_stream));
-    SPAR_TRY_RAW(comm_allreduce_sum(comm, lanes[0].grads + off, cnt, comm_stream));
+    SPAR_TRY_RAW(reduce_bucket(i, lanes[0].grads));
   }
+  return cudaSuccess;
+}
+
+// Bucket i of gradient arena g summed across ranks on the communication stream: all-reduced, or
+// (sharded optimiser) reduce-scattered with its uneven tail all-reduced.
+cudaError_t LMTrainer::reduce_bucket(size_t i, float* g) {
+  if (!sharded_step) return comm_allreduce_sum(comm, g + buckets[i].first, buckets[i].second, comm_stream);
+  const BucketShard& b = shard_plan[i];
+  if (b.shard) SPAR_TRY_RAW(comm_reduce_scatter_sum(comm, g + b.off, b.shard, comm_stream));
+  if (b.rem_count) SPAR_TRY_RAW(comm_allreduce_sum(comm, g + b.rem_off, b.rem_count, comm_stream));
+  return cudaSuccess;
+}
+
+// Start of a sharded step: the parameter pieces the other ranks updated in the previous step are
+// all-gathered on the communication stream (after everything already on s), in the order the
+// forward pass first reads the buckets; gather_ev[i] marks bucket i complete.
+cudaError_t LMTrainer::gather_params(cudaStream_t s) {
+  SPAR_TRY_RAW(cudaEventRecord(gather_fork, s));
+  SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, gather_fork, 0));
+  auto issue = [&](size_t i) -> cudaError_t {
+    const BucketShard& b = shard_plan[i];
+    if (b.shard) SPAR_TRY_RAW(comm_all_gather(comm, params + b.off, b.shard, comm_stream));
+    return cudaEventRecord(gather_ev[i], comm_stream);
+  };
+  SPAR_TRY_RAW(issue(L));  // embedding
+  for (uint64_t l = 0; l < L; ++l) SPAR_TRY_RAW(issue(L - 1 - l));
+  return issue(L + 1);  // final norm
+}
+
+// Every bucket's pieces of arena `which` (0 parameters, 1 gradients, 2 / 3 moments) gathered onto
+// every rank, ordered after the work on s, which waits for the gather. Collective.
+cudaError_t LMTrainer::gather_arena(int which, cudaStream_t s) {
+  if (!sharded || !stale[which]) return cudaSuccess;
+  float* base = params + static_cast<uint64_t>(which) * flat;
+  SPAR_TRY_RAW(cudaEventRecord(gather_fork, s));
+  SPAR_TRY_RAW(cudaStreamWaitEvent(comm_stream, gather_fork, 0));
+  for (const BucketShard& b : shard_plan)
+    if (b.shard) SPAR_TRY_RAW(comm_all_gather(comm, base + b.off, b.shard, comm_stream));
+  SPAR_TRY_RAW(cudaEventRecord(comm_done, comm_stream));
+  SPAR_TRY_RAW(cudaStreamWaitEvent(s, comm_done, 0));
+  stale[which] = false;
   return cudaSuccess;
 }
 
@@ -668,7 +758,12 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
                    : 1;
   comm_lane = static_cast<int>((micro_steps - 1) % step_lanes);  // issues last, runs the reduction
   lanes[0].stream = s;
-  cudaError_t e = cudaSuccess;
+  sharded_step = sharded && comm;
+  struct Reset {  // the caller-driven micro-steps never shard
+    bool& f;
+    ~Reset() { f = false; }
+  } reset{sharded_step};
+  cudaError_t e = sharded_step ? gather_params(s) : cudaSuccess;
   for (int li = 0; li < step_lanes && e == cudaSuccess; ++li)
     e = cudaMemsetAsync(lanes[li].grads, 0, flat * sizeof(float), s);
   if (e == cudaSuccess && step_lanes > 1) {  // the other lanes start after the zeroing
@@ -700,6 +795,22 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
     if (e != cudaSuccess) return runtime(e);
   }
   Slice slice{params, grads, m1, m2, flat};
+  if (sharded_step) {
+    // This rank's pieces: sum of squares, summed over ranks (the non-finite flags too), then
+    // clip + AdamW on the pieces.
+    launches += norm_slices.size() + 1 + own_slices.size();
+    e = grad_norm_launch(norm_state, norm_slices.data(), norm_slices.size(), device, s);
+    if (e == cudaSuccess) e = cudaEventRecord(gather_fork, s);  // collectives stay on comm_stream
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(comm_stream, gather_fork, 0);
+    if (e == cudaSuccess) e = comm_allreduce_sum_f64(comm, norm_state, 2, comm_stream);
+    if (e == cudaSuccess) e = cudaEventRecord(comm_done, comm_stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, comm_done, 0);
+    if (e == cudaSuccess)
+      e = adamw_launch(own_slices.data(), own_slices.size(), norm_state, cfg.max_grad_norm, lr,
+                       cfg.beta1, cfg.beta2, cfg.adam_epsilon, cfg.weight_decay, step, flags + 1,
+                       device, s, device_args ? opt_args : nullptr);
+    return e == cudaSuccess ? ok() : runtime(e);
+  }
   launches += 3;
   e = grad_norm_launch(norm_state, &slice, 1, device, s);
   if (e == cudaSuccess)
@@ -721,11 +832,13 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   float* G = grads;
   // ---------------------------------------------------------------- forward
   launches += 1;
+  SPAR_CHECK(wait_gather(L, s));  // sharded optimiser: the embedding's bucket is gathered
   SPAR_CHECK(embedding_forward_launch(acts[0].x, P + off_E, ids, N, V, d, flags, device, s));
   for (uint64_t l = 0; l < L; ++l) {
     LayerActs& A = acts[l];
     const LayerOffsets& lo = lay[l];
     float* out = l + 1 < L ? acts[l + 1].x : xL;
+    SPAR_CHECK(wait_gather(L - 1 - l, s));
     launches += 2 + 1;  // 2 LayerNorms, softmax (or fused attention)
     SPAR_CHECK(layernorm_forward_launch(A.a1, A.mean1, A.rstd1, A.x, P + lo.ln1_g, P + lo.ln1_b,
                                         N, d, eps, device, s));
@@ -745,6 +858,7 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
                     SPAR_B200_EPI_BIAS_ADD, P + lo.b2, A.h1, d, s));
   }
   launches += 1 + 2 + 2;  // final LayerNorm, cross-entropy + loss sum, final LayerNorm backward
+  SPAR_CHECK(wait_gather(L + 1, s));
   SPAR_CHECK(layernorm_forward_launch(hf, meanf, rstdf, xL, P + off_lnf_g, P + off_lnf_b, N, d,
                                       eps, device, s));
   SPAR_CHECK(gemm(N, V, d, hf, d, false, P + off_E, d, true, logits, Vp, false,
@@ -963,6 +1077,8 @@ extern "C" SparCudaStatus spar_b200_lm_parameter_copy(void* handle, uint64_t ind
   LMTrainer* t = as_trainer(handle);
   if (index >= t->named.size()) return invalid();
   const NamedTensor& n = t->named[index];
+  // Sharded optimiser: other ranks' pieces are out of date until spar_b200_lm_gather.
+  if (!to_device && t->stale[which]) return {1, static_cast<int>(cudaErrorNotReady)};
   DeviceScope scope(t->device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   float* dev = t->params + static_cast<uint64_t>(which) * t->flat + n.offset;
@@ -1004,6 +1120,7 @@ extern "C" SparCudaStatus spar_b200_lm_zero_grad(void* handle, void* stream) {
   DeviceScope scope(t->device);
   const cudaError_t e = cudaMemsetAsync(t->grads, 0, t->flat * sizeof(float),
                                         static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) t->stale[1] = false;
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
@@ -1022,6 +1139,10 @@ extern "C" SparCudaStatus spar_b200_lm_forward_backward(void* handle, const int3
   t->step_lanes = 1;  // a caller-driven micro-step always runs on lane 0
   t->comm_lane = 0;
   t->select_lane(0);
+  // After a sharded train step: whole parameters and gradients (collective, like the step).
+  cudaError_t e = t->gather_arena(0, static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = t->gather_arena(1, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return runtime(e);
   return t->forward_backward(ids, grad_scale, micro_index, static_cast<cudaStream_t>(stream));
 }
 
@@ -1035,8 +1156,11 @@ extern "C" SparCudaStatus spar_b200_lm_optimizer_step(void* handle, double learn
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   Slice slice{t->params, t->grads, t->m1, t->m2, t->flat};
+  cudaError_t e = cudaSuccess;
+  for (int w = 0; w < 4 && e == cudaSuccess; ++w) e = t->gather_arena(w, s);  // whole arenas
+  if (e != cudaSuccess) return runtime(e);
   t->launches += 3;
-  cudaError_t e = grad_norm_launch(t->norm_state, &slice, 1, t->device, s);
+  e = grad_norm_launch(t->norm_state, &slice, 1, t->device, s);
   if (e == cudaSuccess)
     e = adamw_launch(&slice, 1, t->norm_state, t->cfg.max_grad_norm, learning_rate, t->cfg.beta1,
                      t->cfg.beta2, t->cfg.adam_epsilon, t->cfg.weight_decay, step, t->flags + 1,
@@ -1115,6 +1239,8 @@ extern "C" SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* i
     t->launches += it->second.launches;
   }
 done:
+  if (t->sharded && t->comm)  // only this rank's pieces were reduced and updated
+    for (auto& st : t->stale) st = true;
   float sums[LMTrainer::kMaxMicro];
   double norm_state[2];
   int32_t flags[2];
@@ -1142,6 +1268,8 @@ extern "C" SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int wo
   LMTrainer* t = as_trainer(handle);
   DeviceScope scope(t->device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
+  // Arenas left sharded by the current communicator must be gathered through it first.
+  if (t->comm != comm && (t->stale[0] || t->stale[1] || t->stale[2] || t->stale[3])) return invalid();
   if (t->comm != comm && !t->graphs.empty()) {  // captured steps hold the old reductions
     cudaError_t e = cudaDeviceSynchronize();
     for (auto& g : t->graphs) cudaGraphExecDestroy(g.second.exec);
@@ -1166,7 +1294,54 @@ extern "C" SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int wo
     }
     if (e != cudaSuccess) return runtime(e);
   }
+  // Sharded optimiser: this rank's piece of every bucket (and the uneven tails, which every rank
+  // updates; rank 0 alone counts them in the norm).
+  t->sharded = t->comm && (t->shard_mode == 1 || (t->shard_mode < 0 && world_size > 1));
+  if (t->sharded && comm_size(t->comm) != world_size) return invalid();
+  t->rank = t->sharded ? comm_rank(t->comm) : 0;
+  t->shard_plan.clear();
+  t->own_slices.clear();
+  t->norm_slices.clear();
+  if (t->sharded) {
+    cudaError_t e = cudaSuccess;
+    if (!t->gather_fork) e = cudaEventCreateWithFlags(&t->gather_fork, cudaEventDisableTiming);
+    while (e == cudaSuccess && t->gather_ev.size() < t->buckets.size()) {
+      cudaEvent_t ev = nullptr;
+      e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+      if (e == cudaSuccess) t->gather_ev.push_back(ev);
+    }
+    if (e != cudaSuccess) return runtime(e);
+    auto slice = [t](uint64_t off, uint64_t count) {
+      return Slice{t->params + off, t->grads + off, t->m1 + off, t->m2 + off, count};
+    };
+    for (const auto& bk : t->buckets) {
+      const BucketShard b = shard_bucket(bk.first, bk.second, world_size, t->rank);
+      t->shard_plan.push_back(b);
+      if (b.shard) {
+        t->own_slices.push_back(slice(b.own_off, b.shard));
+        t->norm_slices.push_back(slice(b.own_off, b.shard));
+      }
+      if (b.rem_count) {
+        t->own_slices.push_back(slice(b.rem_off, b.rem_count));
+        if (t->rank == 0) t->norm_slices.push_back(slice(b.rem_off, b.rem_count));
+      }
+    }
+  }
   return ok();
+}
+
+// Sharded optimiser: gathers every rank's pieces of arena `which` (0 parameters, 1 gradients,
+// 2 first moments, 3 second moments) onto every rank, ordered on `stream` (which waits for it).
+// After a sharded train step the arenas hold only this rank's pieces up to date; this call (made
+// by every rank, in the same order) brings one whole arena up to date for reading. No-op when the
+// arena is current or the optimiser is not sharded.
+extern "C" SparCudaStatus spar_b200_lm_gather(void* handle, int which, void* stream) {
+  if (!handle || which < 0 || which > 3) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const cudaError_t e = t->gather_arena(which, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : runtime(e);
 }
 
 // Mean loss of the micro-steps run since the last train step (host read, synchronous).
@@ -1275,5 +1450,25 @@ extern "C" SparCudaStatus spar_b200_lm_layout_bucket(const SparB200LMConfig* con
   if (index >= b.size()) return invalid();
   *offset = b[index].first;
   *count = b[index].second;
+  return ok();
+}
+
+extern "C" SparCudaStatus spar_b200_lm_layout_shard(const SparB200LMConfig* config, uint64_t index,
+                                                    int world, int rank, uint64_t* own_offset,
+                                                    uint64_t* shard, uint64_t* tail_offset,
+                                                    uint64_t* tail_count) {
+  if (!config || !own_offset || !shard || !tail_offset || !tail_count || world < 1 || rank < 0 ||
+      rank >= world)
+    return invalid();
+  ParamLayout pl;
+  const SparCudaStatus st = plan_params(*config, pl);
+  if (st.code) return st;
+  const auto b = pl.buckets();
+  if (index >= b.size()) return invalid();
+  const BucketShard s = shard_bucket(b[index].first, b[index].second, world, rank);
+  *own_offset = s.own_off;
+  *shard = s.shard;
+  *tail_offset = s.rem_off;
+  *tail_count = s.rem_count;
   return ok();
 }

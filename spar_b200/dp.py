@@ -6,8 +6,12 @@ sequences (`spar_b200.data.rank_share`); the loss gradient of each rank is scale
 of the mean loss over the global batch. The runtime sums them with one NCCL all-reduce per
 bucket, issued during the last micro-step's backward in the order of `buckets()`: each block's
 contiguous parameter range as soon as its backward finishes (last block first), then the tied
-embedding and the final norm. This module exposes that plan, queried from the runtime itself
-(host-only C-ABI calls, no GPU needed), and packs / unpacks per-tensor gradients along it.
+embedding and the final norm. With the sharded optimiser (the default at world > 1) each bucket
+is reduce-scattered instead: rank r keeps the sum of piece r (`shards`), runs the norm pass and
+AdamW on its pieces only (the sums of squares all-reduced), and the next step starts by
+all-gathering the updated parameter pieces. This module exposes that plan, queried from the
+runtime itself (host-only C-ABI calls, no GPU needed), and packs / unpacks per-tensor gradients
+along it.
 """
 from __future__ import annotations
 
@@ -63,6 +67,32 @@ def layout(cfg: LMConfig):
                                                   ctypes.byref(cnt)))
         buckets.append((off.value, cnt.value))
     return flat.value, tensors, buckets
+
+
+@dataclass(frozen=True)
+class BucketShard:
+    """One rank's part of a bucket under the sharded optimiser: the reduce-scattered piece
+    [own_offset, own_offset + shard) it updates, and the uneven tail [tail_offset, + tail_count)
+    that is all-reduced and updated on every rank."""
+    own_offset: int
+    shard: int
+    tail_offset: int
+    tail_count: int
+
+
+def shards(cfg: LMConfig, world: int, rank: int) -> list[BucketShard]:
+    """The runtime's piece of every bucket (issue order) for `rank` of `world` (host-only query)."""
+    lib = _lib.load()
+    c = native_config(cfg)
+    _, _, buckets = layout(cfg)
+    vals = [ctypes.c_uint64() for _ in range(4)]
+    out = []
+    for i in range(len(buckets)):
+        _lib.check("spar_b200_lm_layout_shard",
+                   lib.spar_b200_lm_layout_shard(ctypes.byref(c), i, world, rank,
+                                                 *[ctypes.byref(v) for v in vals]))
+        out.append(BucketShard(*[v.value for v in vals]))
+    return out
 
 
 def to_arena(grads: dict, flat: int, tensors, dtype=np.float64) -> np.ndarray:

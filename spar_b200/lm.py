@@ -150,6 +150,11 @@ class DecoderLM:
     def attach_comm(self, comm, world_size: int):
         check("spar_b200_lm_set_comm", self.lib.spar_b200_lm_set_comm(self.handle, comm, world_size))
 
+    def gather(self, which: str = "param", stream: int = 0):
+        """Sharded optimiser: all-gathers one arena's pieces from every rank so that it can be read
+        (get / state_dict). Collective: every rank calls it, in the same order."""
+        check("spar_b200_lm_gather", self.lib.spar_b200_lm_gather(self.handle, WHICH[which], stream))
+
     def train_step(self, ids, lr: float, step: int | None = None, stream: int = 0):
         """ids: int32 array [micro_steps, micro_batch, seq] in host memory (numpy or pinned
         torch tensor), or a CUDA int32 tensor of that shape. Returns (loss, grad_norm, flags)."""

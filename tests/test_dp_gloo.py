@@ -120,3 +120,106 @@ def test_gloo_two_ranks_sum_to_full_batch_gradient():
     for name, ref in full.items():
         err = np.linalg.norm(got[name] - ref) / max(np.linalg.norm(ref), 1e-300)
         assert err <= 1e-12, (name, err)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 5, 8])
+def test_shard_plan_tiles_every_bucket(world):
+    """Sharded optimiser: the ranks' pieces of each bucket (equal, 64-float multiples, in rank
+    order) and the all-reduced tail tile the bucket exactly."""
+    from spar_b200 import dp
+    from spar_b200.lm import C5
+
+    for cfg in (_cfg(1), C5):
+        _, _, buckets = dp.layout(cfg)
+        plans = [dp.shards(cfg, world, r) for r in range(world)]
+        for i, (off, cnt) in enumerate(buckets):
+            pieces = [p[i] for p in plans]
+            shard = pieces[0].shard
+            assert shard % 64 == 0 and all(p.shard == shard for p in pieces)
+            assert [p.own_offset for p in pieces] == [off + r * shard for r in range(world)]
+            assert all(p.tail_offset == off + world * shard for p in pieces)
+            assert pieces[0].tail_offset + pieces[0].tail_count == off + cnt
+            assert pieces[0].tail_count < world * 64  # only what does not split evenly
+    # C5's buckets split evenly over 2, 4 and 8 ranks: nothing is all-reduced there.
+    if world in (2, 8):
+        assert all(p.tail_count == 0 for p in dp.shards(C5, world, 0))
+
+
+OPT = dict(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1)
+
+
+def _sharded_worker(rank, world, port, out_dir, max_norm):
+    """One rank of the sharded optimiser step, restated on the host: reduce (all-reduce, then
+    keep this rank's pieces: the reduce-scatter result), norm of the own pieces (+ the tails on
+    rank 0) all-reduced, AdamW on the own pieces and the tails, all-gather of the parameters."""
+    import torch
+    import torch.distributed as dist
+
+    from spar_b200 import dp
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120))
+    cfg = _cfg(1)
+    flat, _, buckets = dp.layout(cfg)
+    rng = np.random.default_rng(7)
+    p = rng.normal(0, 0.02, flat).astype(np.float32)
+    m = rng.normal(0, 1e-3, flat).astype(np.float32)
+    v = np.abs(rng.normal(0, 1e-6, flat)).astype(np.float32)
+    g = np.random.default_rng(100 + rank).normal(0, 1e-2, flat).astype(np.float32)
+    t = torch.from_numpy(g)
+    dist.all_reduce(t)
+    g = t.numpy()
+    plan = dp.shards(cfg, world, rank)
+    own = [(b.own_offset, b.shard) for b in plan if b.shard]
+    tails = [(b.tail_offset, b.tail_count) for b in plan if b.tail_count]
+    counted = own + (tails if rank == 0 else [])
+    ssq = torch.tensor([sum(float(np.dot(g[o:o + c].astype(np.float64), g[o:o + c].astype(np.float64)))
+                            for o, c in counted)], dtype=torch.float64)
+    dist.all_reduce(ssq)
+    clip = O.clip_factor(float(np.sqrt(ssq.item())), max_norm)
+    for o, c in own + tails:
+        p[o:o + c], m[o:o + c], v[o:o + c] = O.adamw_update(p[o:o + c], g[o:o + c], m[o:o + c],
+                                                            v[o:o + c], 3, clip=clip, **OPT)
+    for b in plan:
+        if b.shard:
+            piece = torch.from_numpy(p[b.own_offset:b.own_offset + b.shard].copy())
+            parts = [torch.empty_like(piece) for _ in range(world)]
+            dist.all_gather(parts, piece)
+            start = b.own_offset - rank * b.shard
+            p[start:start + world * b.shard] = torch.cat(parts).numpy()
+    np.save(os.path.join(out_dir, f"p{rank}.npy"), p)
+    np.save(os.path.join(out_dir, f"g{rank}.npy"), g)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,max_norm", [(2, 1e30), (3, 1e30), (3, 1e-3)])
+def test_gloo_sharded_optimizer_matches_replicated(world, max_norm):
+    """The sharded optimiser step over `world` gloo ranks (3: uneven tails) gives every rank the
+    parameters of the replicated step: bitwise without clipping, and to 1e-6 with clipping active
+    (the norm's double sum runs in another order)."""
+    import torch.multiprocessing as mp
+
+    from spar_b200 import dp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(_sharded_worker, args=(world, port, out, max_norm), nprocs=world,
+                           join=True, start_method="spawn")
+        ps = [np.load(os.path.join(out, f"p{r}.npy")) for r in range(world)]
+        g = np.load(os.path.join(out, "g0.npy"))
+    for r in range(1, world):
+        assert np.array_equal(ps[0], ps[r])
+    flat, _, _ = dp.layout(_cfg(1))
+    rng = np.random.default_rng(7)
+    p = rng.normal(0, 0.02, flat).astype(np.float32)
+    m = rng.normal(0, 1e-3, flat).astype(np.float32)
+    v = np.abs(rng.normal(0, 1e-6, flat)).astype(np.float32)
+    clip = O.clip_factor(O.global_grad_norm([g]), max_norm)
+    want, _, _ = O.adamw_update(p, g, m, v, 3, clip=clip, **OPT)
+    if clip == 1.0:
+        assert np.array_equal(ps[0], want)
+    else:
+        np.testing.assert_allclose(ps[0], want, rtol=1e-6, atol=1e-9)

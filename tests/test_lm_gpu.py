@@ -251,3 +251,52 @@ def test_one_rank_communicator_matches_no_communicator(cuda, monkeypatch, lanes)
     assert [o[0] for o in a_out] == [o[0] for o in b_out]
     assert [o[1] for o in a_out] == [o[1] for o in b_out]
     assert np.array_equal(a_g, b_g) and np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("lanes", ["0", "2"])
+def test_sharded_optimizer_one_rank_matches_replicated(cuda, monkeypatch, lanes):
+    """The sharded optimiser path on one GPU (SPAR_B200_SHARD_OPT=1 with a one-rank communicator):
+    reduce-scatter per bucket, norm pass and AdamW per bucket piece, parameter all-gather at the
+    next step's start. Over one rank the collectives are identities, so three steps match the
+    replicated steps without a communicator: losses and parameters bitwise, the norm to double
+    rounding. Reads need the collective gather first."""
+    from spar_b200._lib import SparError
+    from spar_b200.lm import DecoderLM
+
+    monkeypatch.setenv("SPAR_B200_LANES", lanes)
+    monkeypatch.setenv("SPAR_B200_SHARD_OPT", "1")
+    cfg = _lanes_cfg()
+    params, ids = _setup(cfg, 4)
+
+    def steps(with_comm):
+        lm = DecoderLM(cfg, 0)
+        lm.load_state_dict(params)
+        lib = comm = None
+        if with_comm:
+            lib, comm = _one_rank_comm()
+            lm.attach_comm(comm, 1)
+        out = [lm.train_step(ids, 3e-4, step=s) for s in range(1, 4)]
+        if with_comm:
+            with pytest.raises(SparError):
+                lm.get(lm.names[0])
+            for which in ("param", "grad", "m", "v"):
+                lm.gather(which)
+        state = [_flat(lm.state_dict(w), lm.names) for w in ("param", "grad", "m", "v")]
+        lm.close()
+        if comm is not None:
+            lib.spar_b200_comm_destroy(comm, 0)
+        return out, state
+
+    a_out, a = steps(False)
+    b_out, b = steps(True)
+    assert [o[2] for o in b_out] == [(0, 0)] * 3
+    np.testing.assert_allclose([o[1] for o in a_out], [o[1] for o in b_out], rtol=1e-12)
+    # A clip factor from a norm that differs in its last double bit can move a clipped fp32
+    # gradient by one ulp (rarely); with identical norms the steps are bitwise equal.
+    exact = [o[1] for o in a_out] == [o[1] for o in b_out]
+    if exact:
+        assert [o[0] for o in a_out] == [o[0] for o in b_out]
+    else:
+        np.testing.assert_allclose([o[0] for o in a_out], [o[0] for o in b_out], rtol=1e-6)
+    for x, y in zip(a, b):
+        assert np.array_equal(x, y) if exact else rel_l2(x, y) <= 1e-6
