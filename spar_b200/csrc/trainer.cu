@@ -678,9 +678,6 @@ cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
   return cudaSuccess;
 }
 
-// One whole optimiser step on stream s with the token ids already in ids_dev: zero the gradient
-// arena, the micro-step sweeps, the global-norm pass and clip + AdamW (scalars by value, or from
-// opt_args when the launches are being captured for replay).
 cudaError_t LMTrainer::merge_lanes(uint64_t off, uint64_t count, cudaStream_t s) {
   const float4* src[3] = {nullptr, nullptr, nullptr};
   for (int li = 1; li < step_lanes; ++li) src[li - 1] = reinterpret_cast<const float4*>(lanes[li].grads + off);
@@ -751,6 +748,9 @@ cudaError_t LMTrainer::gather_arena(int which, cudaStream_t s) {
   return cudaSuccess;
 }
 
+// One whole optimiser step on stream s with the token ids already in ids_dev: (sharded: gather the
+// parameters,) zero the gradient arenas, the micro-step sweeps, the global-norm pass and
+// clip + AdamW (scalars by value, or from opt_args when the launches are being captured).
 SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, double lr,
                                     uint64_t step, cudaStream_t s, bool device_args) {
   step_lanes = (lanes_alloc > 1 && micro_steps >= 2 && !profiling)
