@@ -56,6 +56,60 @@ struct SparCudaStatus spar_b200_layernorm_backward_noalloc(
     int accumulate_dx, int device, void* stream);
 
 /* ------------------------------------------------------------------------------------------ */
+/* RMSNorm over the last axis of x[rows, cols] (cols % 4 == 0, cols <= 2048):                   */
+/* y = x / sqrt(mean(x^2) + epsilon) * weight, replacing nn::RMSNorm::forward                   */
+/* (src/nn/rmsnorm.cpp:40-53: mean(square), add_scalar, sqrt, divide, multiply(weight)); the    */
+/* divide is taken as a multiply by rstd. rstd [rows] = 1 / sqrt(mean(x^2) + epsilon) is saved.  */
+struct SparCudaStatus spar_b200_rmsnorm_forward(float* y, float* rstd, const float* x,
+                                                const float* weight, uint64_t rows, uint64_t cols,
+                                                double epsilon, int device, void* stream);
+/* dx and dweight of the RMSNorm above in one pass over (x, dy) (the autograd sweep of that      */
+/* chain): dx = rstd * (g - xhat * mean(g * xhat)), g = dy * weight, xhat = x * rstd;           */
+/* dweight = sum over rows of dy * xhat, reduced deterministically. accumulate_params /         */
+/* accumulate_dx add to the existing dweight / dx as in spar_b200_layernorm_backward.           */
+struct SparCudaStatus spar_b200_rmsnorm_backward(float* dx, float* dweight, const float* dy,
+                                                 const float* x, const float* weight,
+                                                 const float* rstd, uint64_t rows, uint64_t cols,
+                                                 int accumulate_params, int accumulate_dx,
+                                                 int device, void* stream);
+
+/* qk-norm, replacing the q_norm / k_norm RMSNorm(head_dim) of nn::SelfAttention               */
+/* (src/nn/attention.cpp:183-186, 212-213) on the head-major view of the projections: RMSNorm   */
+/* over each head's head_dim features where x[tokens, ld] holds `heads` consecutive heads from   */
+/* column 0 of each row (pass the packed projection output + the q or k part's column offset). */
+/* y and x share the layout and may be the same buffer (each head row is read before it is     */
+/* written); rstd [tokens * heads] (token-major). head_dim % 4 == 0, ld % 4 == 0, 16-byte       */
+/* aligned pointers.                                                                            */
+struct SparCudaStatus spar_b200_head_rmsnorm_forward(float* y, const float* x, uint64_t ld,
+                                                     uint64_t tokens, uint64_t heads,
+                                                     uint64_t head_dim, const float* weight,
+                                                     float* rstd, double epsilon, int device,
+                                                     void* stream);
+/* dx (same layout; may be dy's buffer) and dweight of the qk-norm above.                       */
+struct SparCudaStatus spar_b200_head_rmsnorm_backward(float* dx, float* dweight, const float* dy,
+                                                      const float* x, uint64_t ld,
+                                                      uint64_t tokens, uint64_t heads,
+                                                      uint64_t head_dim, const float* weight,
+                                                      const float* rstd, int accumulate_params,
+                                                      int device, void* stream);
+
+/* SwiGLU gate, replacing nn::swiglu (src/nn/functional.cpp:9-11) as used by SwiGLUMLP          */
+/* (src/nn/mlp.cpp:33-46): h = silu(gate) * value, silu(x) = x * sigmoid(x) with Spar's stable   */
+/* sigmoid (src/ops/unary.cpp:55-61, 150-152), over rows x cols with row strides (ld*, in        */
+/* floats), so gate and value may be the two column halves of one fused projection output.      */
+struct SparCudaStatus spar_b200_swiglu_forward(float* h, uint64_t ldh, const float* gate,
+                                               uint64_t ldg, const float* value, uint64_t ldv,
+                                               uint64_t rows, uint64_t cols, int device,
+                                               void* stream);
+/* d gate = (dh * value) * (s + gate * (s * (1 - s))), d value = dh * silu(gate), s = sigmoid(gate) */
+/* (silu's local derivative, src/ops/unary.cpp:155-160, through multiply's backward).             */
+struct SparCudaStatus spar_b200_swiglu_backward(float* dgate, uint64_t lddg, float* dvalue,
+                                                uint64_t lddv, const float* dh, uint64_t lddh,
+                                                const float* gate, uint64_t ldg,
+                                                const float* value, uint64_t ldv, uint64_t rows,
+                                                uint64_t cols, int device, void* stream);
+
+/* ------------------------------------------------------------------------------------------ */
 /* GELU, tanh form: gelu(x) = x * sigmoid(2*sqrt(2/pi)*(x + 0.044715 x^3)), the identity that  */
 /* writes the tanh form with Spar's stable sigmoid (src/ops/unary.cpp:137-148).                 */
 struct SparCudaStatus spar_b200_gelu_forward(float* y, const float* x, uint64_t count, int device,

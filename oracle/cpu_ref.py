@@ -32,6 +32,8 @@ def load():
         sig = {
             "ref_layernorm": [F, F, F, F, c_int64, c_int64, c_double, F, F, F, F],
             "ref_gelu": [F, F, c_int64, F, F],
+            "ref_rmsnorm": [F, F, F, c_int64, c_int64, c_double, F, F, F],
+            "ref_swiglu": [F, F, F, c_int64, F, F, F],
             "ref_causal_softmax": [F, F, c_int64, c_int64, c_double, F, F],
             "ref_cross_entropy": [F, I32, c_int64, c_int64, c_int64, F, F],
             "ref_matmul": [F, F, F, c_int64, c_int64, c_int64, F, F, F],
@@ -75,6 +77,21 @@ def layernorm(x, gamma, beta, dy, eps=1e-5):
     _check(load().ref_layernorm(_p(x), _p(gamma), _p(beta), _p(dy), rows, cols, eps, _p(y), _p(dx),
                                 _p(dg), _p(db)))
     return y, dx, dg, db
+
+
+def rmsnorm(x, weight, dy, eps=1e-5):
+    x, weight, dy = map(_f, (x, weight, dy))
+    rows, cols = x.shape
+    y, dx, dw = np.empty_like(x), np.empty_like(x), np.empty(cols, np.float32)
+    _check(load().ref_rmsnorm(_p(x), _p(weight), _p(dy), rows, cols, eps, _p(y), _p(dx), _p(dw)))
+    return y, dx, dw
+
+
+def swiglu(gate, value, dh):
+    gate, value, dh = map(_f, (gate, value, dh))
+    h, dg, dv = np.empty_like(gate), np.empty_like(gate), np.empty_like(gate)
+    _check(load().ref_swiglu(_p(gate), _p(value), _p(dh), gate.size, _p(h), _p(dg), _p(dv)))
+    return h, dg, dv
 
 
 def gelu(x, dy):

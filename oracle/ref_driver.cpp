@@ -162,6 +162,37 @@ int ref_layernorm(const float* x, const float* gamma, const float* beta, const f
   });
 }
 
+// nn::RMSNorm (src/nn/rmsnorm.cpp:40-53) with the given weight; dx, dweight for upstream dy.
+int ref_rmsnorm(const float* x, const float* weight, const float* dy, int64_t rows, int64_t cols,
+                double eps, float* y, float* dx, float* dweight) {
+  return guarded([&] {
+    nn::RMSNorm norm{static_cast<std::size_t>(cols), DType::Float32, eps};
+    load(norm.weight(), weight);
+    Tensor tx = from_host(x, {rows, cols}, true);
+    Tensor out = norm.forward(tx);
+    to_host(out, y);
+    Tensor loss = weighted_sum(out, dy);
+    loss.backward();
+    to_host(tx.grad(), dx);
+    to_host(norm.weight().tensor().grad(), dweight);
+  });
+}
+
+// nn::swiglu (src/nn/functional.cpp:9-11): h = silu(gate) * value; d gate, d value for dh.
+int ref_swiglu(const float* gate, const float* value, const float* dh, int64_t n, float* h,
+               float* dgate, float* dvalue) {
+  return guarded([&] {
+    Tensor tg = from_host(gate, {n}, true);
+    Tensor tv = from_host(value, {n}, true);
+    Tensor out = nn::swiglu(tg, tv);
+    to_host(out, h);
+    Tensor loss = weighted_sum(out, dh);
+    loss.backward();
+    to_host(tg.grad(), dgate);
+    to_host(tv.grad(), dvalue);
+  });
+}
+
 int ref_gelu(const float* x, const float* dy, int64_t n, float* y, float* dx) {
   return guarded([&] {
     Tensor tx = from_host(x, {n}, true);

@@ -113,6 +113,29 @@ def layer_norm_backward(dy, x, gamma, eps=1e-5, dtype=np.float64):
     return dx, (dy * xhat).sum(axis=red), dy.sum(axis=red)
 
 
+# ------------------------------------------------------------------------------ RMSNorm
+def rms_norm_forward(x, weight, eps=1e-5, dtype=np.float32):
+    """nn::RMSNorm::forward (src/nn/rmsnorm.cpp:40-53): mean(square(x)) over the last axis,
+    add_scalar(eps), sqrt, divide, multiply(weight); returns y and rstd = 1 / sqrt(ms + eps)."""
+    x = np.asarray(x, dtype)
+    ms = (x * x).mean(axis=-1, keepdims=True, dtype=dtype)
+    denom = np.sqrt(ms + dtype(eps))
+    y = x / denom * np.asarray(weight, dtype)
+    return y.astype(dtype), (1.0 / denom[..., 0]).astype(dtype)
+
+
+def rms_norm_backward(dy, x, weight, eps=1e-5, dtype=np.float64):
+    """Closed form of the reverse-mode sweep over the chain above: with xhat = x * rstd and
+    g = dy * weight, dx = rstd * (g - xhat * mean(g * xhat)), dweight = sum_rows dy * xhat."""
+    x = np.asarray(x, dtype)
+    dy = np.asarray(dy, dtype)
+    rstd = 1.0 / np.sqrt((x * x).mean(axis=-1, keepdims=True) + eps)
+    xhat = x * rstd
+    gy = dy * np.asarray(weight, dtype)
+    dx = rstd * (gy - xhat * (gy * xhat).mean(axis=-1, keepdims=True))
+    return dx, (dy * xhat).sum(axis=tuple(range(dy.ndim - 1)))
+
+
 # ------------------------------------------------------------------------------ GELU
 def stable_sigmoid(v):
     """src/ops/unary.cpp:55-61."""
@@ -140,6 +163,24 @@ def gelu_derivative(x, dtype=np.float64):
     u = (x + (x * x * x) * GELU_B) * GELU_A
     s = stable_sigmoid(u)
     return s + x * s * (1.0 - s) * GELU_A * (1.0 + 3.0 * GELU_B * x * x)
+
+
+# ------------------------------------------------------------------------------ SwiGLU
+def swiglu_forward(gate, value, dtype=np.float32):
+    """nn::swiglu (src/nn/functional.cpp:9-11): silu(gate) * value, silu(x) = x * sigmoid(x)
+    with the stable sigmoid (src/ops/unary.cpp:55-61, 150-152)."""
+    g = np.asarray(gate, dtype)
+    return (g * stable_sigmoid(g) * np.asarray(value, dtype)).astype(dtype)
+
+
+def swiglu_backward(dh, gate, value, dtype=np.float64):
+    """d gate = dh * value * (s + gate * s * (1 - s)), d value = dh * gate * s, s = sigmoid(gate)
+    (silu's local derivative, src/ops/unary.cpp:155-160, through multiply's backward)."""
+    g = np.asarray(gate, dtype)
+    v = np.asarray(value, dtype)
+    d = np.asarray(dh, dtype)
+    sg = stable_sigmoid(g)
+    return d * v * (sg + g * (sg * (1.0 - sg))), d * (g * sg)
 
 
 # ------------------------------------------------------------------------------ softmax

@@ -58,6 +58,12 @@ SIGNATURES = {
     "spar_b200_layernorm_forward": (S, [p, p, p, p, p, p, u64, u64, d, i, p]),
     "spar_b200_layernorm_backward": (S, [p, p, p, p, p, p, p, p, u64, u64, i, i, i, p]),
     "spar_b200_layernorm_backward_noalloc": (S, [p, p, p, p, p, p, p, p, u64, u64, i, i, i, p]),
+    "spar_b200_rmsnorm_forward": (S, [p, p, p, p, u64, u64, d, i, p]),
+    "spar_b200_rmsnorm_backward": (S, [p, p, p, p, p, p, u64, u64, i, i, i, p]),
+    "spar_b200_head_rmsnorm_forward": (S, [p, p, u64, u64, u64, u64, p, p, d, i, p]),
+    "spar_b200_head_rmsnorm_backward": (S, [p, p, p, p, u64, u64, u64, u64, p, p, i, i, p]),
+    "spar_b200_swiglu_forward": (S, [p, u64, p, u64, p, u64, u64, u64, i, p]),
+    "spar_b200_swiglu_backward": (S, [p, u64, p, u64, p, u64, p, u64, p, u64, u64, u64, i, p]),
     "spar_b200_gelu_forward": (S, [p, p, u64, i, p]),
     "spar_b200_gelu_backward": (S, [p, p, p, u64, i, p]),
     "spar_b200_causal_softmax_forward": (S, [p, p, u64, u64, u64, f, u64, i, p]),

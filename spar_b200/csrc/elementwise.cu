@@ -1,11 +1,17 @@
-// GELU forward/backward, rotary embedding, column sums and a deterministic total sum.
+// GELU and SwiGLU forward/backward, rotary embedding, column sums and a deterministic total sum.
 //
 // GELU: Spar has no GELU op; the harness writes the tanh form exactly through Spar's stable
 // sigmoid (src/ops/unary.cpp:137-148, branch form of cuda_kernels.cu:105-111):
 //   gelu(x) = x * sigmoid(u),  u = 2*sqrt(2/pi)*(x + 0.044715 x^3)   (tanh(z) = 2 sigmoid(2z) - 1)
 //   gelu'(x) = s + x * s * (1 - s) * du/dx,  du/dx = 2*sqrt(2/pi)*(1 + 3*0.044715 x^2)
+// SwiGLU: nn::swiglu (src/nn/functional.cpp:9-11) h = silu(gate) * value, silu(x) = x * s(x) with
+// the stable sigmoid; backward through multiply and silu's local derivative s + x s (1 - s)
+// (src/ops/unary.cpp:150-160): d gate = (dh * value) * (s + gate * (s * (1 - s))),
+// d value = dh * silu(gate), in that operation order.
 // RoPE: interleaved pairs (2i, 2i+1) as Spar's apply_rope (src/nn/rope.cpp:35-66); the angle table
 // is computed once in double and rounded to fp32 exactly as the reference does per element.
+#include <initializer_list>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -43,6 +49,77 @@ __global__ void gelu_tail_kernel(float* y, const float* dy, const float* x, uint
   const uint64_t i = begin + threadIdx.x;
   if (i >= n) return;
   y[i] = backward ? dy[i] * gelu_derivative(x[i]) : gelu_value(x[i]);
+}
+
+__device__ __forceinline__ float silu_value(float g) { return g * stable_sigmoid(g); }
+
+__device__ __forceinline__ void swiglu_grads(float d, float g, float v, float& dg, float& dv) {
+  const float sg = stable_sigmoid(g);
+  dg = (d * v) * (sg + g * (sg * (1.f - sg)));
+  dv = d * (g * sg);
+}
+
+// Row-strided SwiGLU over rows x cols. Vector path: every leading dimension and pointer allows
+// float4 access (cols % 4 == 0). No per-element index division: the forward gives block (x, y)
+// 256 consecutive float4 (or float) columns of rows y, y + gridDim.y, ... with four rows' loads in
+// flight per thread; the backward (five streams) cuts the rows into 256-column segments that
+// blocks take in grid-stride order, so consecutive blocks stream consecutive memory (each layout
+// measured the faster for its kernel).
+template <bool kVec>
+__global__ void swiglu_forward_kernel(float* __restrict__ h, uint64_t ldh,
+                                      const float* __restrict__ gate, uint64_t ldg,
+                                      const float* __restrict__ value, uint64_t ldv, uint64_t rows,
+                                      uint64_t cols) {
+  pdl_begin();
+  const uint64_t per_row = kVec ? cols / 4 : cols;
+  const uint64_t c = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= per_row) return;
+#pragma unroll 4
+  for (uint64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    if constexpr (kVec) {
+      const float4 g = ld_stream(reinterpret_cast<const float4*>(gate + r * ldg) + c);
+      const float4 v = ld_stream(reinterpret_cast<const float4*>(value + r * ldv) + c);
+      reinterpret_cast<float4*>(h + r * ldh)[c] =
+          make_float4(silu_value(g.x) * v.x, silu_value(g.y) * v.y, silu_value(g.z) * v.z,
+                      silu_value(g.w) * v.w);
+    } else {
+      h[r * ldh + c] = silu_value(gate[r * ldg + c]) * value[r * ldv + c];
+    }
+  }
+}
+
+template <bool kVec>
+__global__ void swiglu_backward_kernel(float* __restrict__ dgate, uint64_t lddg,
+                                       float* __restrict__ dvalue, uint64_t lddv,
+                                       const float* __restrict__ dh, uint64_t lddh,
+                                       const float* __restrict__ gate, uint64_t ldg,
+                                       const float* __restrict__ value, uint64_t ldv,
+                                       uint64_t rows, uint64_t cols) {
+  pdl_begin();
+  const uint64_t per_row = kVec ? cols / 4 : cols;
+  const uint64_t segs_per_row = (per_row + 255) / 256, segs = rows * segs_per_row;
+  for (uint64_t seg = blockIdx.x; seg < segs; seg += gridDim.x) {
+    const uint64_t r = seg / segs_per_row;
+    const uint64_t c = (seg - r * segs_per_row) * 256 + threadIdx.x;
+    if (c >= per_row) continue;
+    if constexpr (kVec) {
+      const float4 d = ld_stream(reinterpret_cast<const float4*>(dh + r * lddh) + c);
+      const float4 g = ld_stream(reinterpret_cast<const float4*>(gate + r * ldg) + c);
+      const float4 v = ld_stream(reinterpret_cast<const float4*>(value + r * ldv) + c);
+      float4 a, b;
+      swiglu_grads(d.x, g.x, v.x, a.x, b.x);
+      swiglu_grads(d.y, g.y, v.y, a.y, b.y);
+      swiglu_grads(d.z, g.z, v.z, a.z, b.z);
+      swiglu_grads(d.w, g.w, v.w, a.w, b.w);
+      reinterpret_cast<float4*>(dgate + r * lddg)[c] = a;
+      reinterpret_cast<float4*>(dvalue + r * lddv)[c] = b;
+    } else {
+      float a, b;
+      swiglu_grads(dh[r * lddh + c], gate[r * ldg + c], value[r * ldv + c], a, b);
+      dgate[r * lddg + c] = a;
+      dvalue[r * lddv + c] = b;
+    }
+  }
 }
 
 // One thread per (position, pair): cos/sin of pos * theta^(-2i/D), computed in double.
@@ -227,6 +304,77 @@ extern "C" SparCudaStatus spar_b200_gelu_backward(float* dx, const float* dy, co
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   const cudaError_t e = gelu_launch(dx, dy, x, count, 1, device, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+namespace {
+// float4 access is possible when cols and every leading dimension are multiples of 4 and every
+// pointer is 16-byte aligned.
+bool swiglu_vec(uint64_t cols, std::initializer_list<uint64_t> lds,
+                std::initializer_list<const void*> ptrs) {
+  if (cols % 4) return false;
+  for (uint64_t ld : lds)
+    if (ld % 4) return false;
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15) return false;
+  return true;
+}
+
+// Forward: 256-wide column blocks x enough row slots for about eight blocks per SM.
+dim3 swiglu_forward_grid(uint64_t rows, uint64_t per_row, int device) {
+  const uint64_t gx = (per_row + 255) / 256;
+  uint64_t gy = (static_cast<uint64_t>(sm_count(device)) * 8 + gx - 1) / gx;
+  if (gy > rows) gy = rows;
+  if (gy > 65535) gy = 65535;
+  if (gy < 1) gy = 1;
+  return dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+}
+
+// Backward: one 256-thread block per 256-column segment, at most eight blocks per SM.
+dim3 swiglu_backward_grid(uint64_t rows, uint64_t per_row, int device) {
+  return dim3(grid_for(rows * ((per_row + 255) / 256), 1, sm_count(device) * 8));
+}
+}  // namespace
+
+extern "C" SparCudaStatus spar_b200_swiglu_forward(float* h, uint64_t ldh, const float* gate,
+                                                   uint64_t ldg, const float* value, uint64_t ldv,
+                                                   uint64_t rows, uint64_t cols, int device,
+                                                   void* stream) {
+  if (rows == 0 || cols == 0) return ok();
+  if (!h || !gate || !value || ldh < cols || ldg < cols || ldv < cols) return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const bool vec = swiglu_vec(cols, {ldh, ldg, ldv}, {h, gate, value});
+  const dim3 grid = swiglu_forward_grid(rows, vec ? cols / 4 : cols, device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec) launch(swiglu_forward_kernel<true>, dim3(grid), dim3(256), 0, s, h, ldh, gate, ldg, value, ldv, rows, cols);
+  else launch(swiglu_forward_kernel<false>, dim3(grid), dim3(256), 0, s, h, ldh, gate, ldg, value, ldv, rows, cols);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" SparCudaStatus spar_b200_swiglu_backward(float* dgate, uint64_t lddg, float* dvalue,
+                                                    uint64_t lddv, const float* dh, uint64_t lddh,
+                                                    const float* gate, uint64_t ldg,
+                                                    const float* value, uint64_t ldv,
+                                                    uint64_t rows, uint64_t cols, int device,
+                                                    void* stream) {
+  if (rows == 0 || cols == 0) return ok();
+  if (!dgate || !dvalue || !dh || !gate || !value || lddg < cols || lddv < cols || lddh < cols ||
+      ldg < cols || ldv < cols)
+    return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const bool vec = swiglu_vec(cols, {lddg, lddv, lddh, ldg, ldv}, {dgate, dvalue, dh, gate, value});
+  const dim3 grid = swiglu_backward_grid(rows, vec ? cols / 4 : cols, device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec)
+    launch(swiglu_backward_kernel<true>, dim3(grid), dim3(256), 0, s, dgate, lddg, dvalue, lddv,
+           dh, lddh, gate, ldg, value, ldv, rows, cols);
+  else
+    launch(swiglu_backward_kernel<false>, dim3(grid), dim3(256), 0, s, dgate, lddg, dvalue, lddv,
+           dh, lddh, gate, ldg, value, ldv, rows, cols);
+  const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? ok() : runtime(e);
 }
 

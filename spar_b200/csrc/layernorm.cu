@@ -4,16 +4,22 @@
 //   mean(x) -> subtract -> square -> mean -> add_scalar(eps) -> sqrt -> divide -> multiply(gamma)
 //   -> add(beta)
 // which is the RMSNorm pattern of src/nn/rmsnorm.cpp:50-52 with a centring step; the forward here
-// evaluates that chain with the same operation order per element (divide by sqrt(var + eps), not
-// multiply by a reciprocal). The backward is the closed form of that chain's autograd:
+// evaluates that chain per element with the division by sqrt(var + eps) taken as a multiply by
+// rstd = 1 / sqrt(var + eps) (within an ulp of the divide). The backward is the closed form of
+// that chain's autograd:
 //   xhat = (x - mean) * rstd, g = dy * gamma
 //   dx = rstd * (g - mean(g) - xhat * mean(g * xhat)), dgamma = sum_rows dy * xhat, dbeta = sum dy
+// RMSNorm itself (nn::RMSNorm, src/nn/rmsnorm.cpp:40-53: mean(square(x)), add_scalar(eps), sqrt,
+// divide, multiply(weight)) is the same kernels without the centring and the bias (kRms):
+//   y = x * rstd * w, rstd = 1 / sqrt(mean(x^2) + eps)
+//   dx = rstd * (g - xhat * mean(g * xhat)) with xhat = x * rstd, dw = sum_rows dy * xhat
 //
 // Layout: one warp per row, the row held in registers as float4 (lane l owns float4 columns
 // l, l + 32, ...), so x and dy are read from HBM exactly once per pass. dgamma/dbeta are
 // accumulated per warp in shared memory, reduced over the block's warps in a fixed order and
 // written as one partial row per block; a second kernel sums the partials in a fixed order
 // (deterministic, no atomics).
+#include <cmath>
 #include <mutex>
 
 #include "common.cuh"
@@ -23,15 +29,26 @@ namespace {
 
 constexpr int kWarps = 8;  // rows in flight per block
 
+// Where row r of x / y / dy / dx starts: rows of `cols` floats, `group` consecutive rows per
+// stride of `ld` floats (group 1, ld = cols: a plain [rows, cols] matrix; group = heads,
+// ld = the projection's row stride: the heads of one token inside a packed q / k projection).
+struct RowMap {
+  uint64_t ld;
+  uint32_t group;
+  __device__ __forceinline__ uint64_t operator()(uint64_t row, int cols) const {
+    return group == 1 ? row * ld : (row / group) * ld + (row % group) * static_cast<uint64_t>(cols);
+  }
+};
+
 // One warp per row, the row in registers (VPL float4 per lane); gamma and beta are read per use
 // (L1-resident, the same for every row) rather than held, which keeps the registers low enough
 // for three blocks (24 rows in flight) per SM.
-template <int VPL>
+template <int VPL, bool kRms>
 __global__ void __launch_bounds__(kWarps * 32, 3)
 layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
                          float* __restrict__ rstd_out, const float* __restrict__ x,
                          const float* __restrict__ gamma, const float* __restrict__ beta,
-                         uint64_t rows, int cols, float eps) {
+                         uint64_t rows, int cols, float eps, RowMap rm) {
   pdl_begin();
   const int lane = threadIdx.x & 31;
   const int vec_cols = cols >> 2;
@@ -41,7 +58,7 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
   const uint64_t warp_global = (static_cast<uint64_t>(blockIdx.x) * kWarps) + (threadIdx.x >> 5);
   const uint64_t warp_stride = static_cast<uint64_t>(gridDim.x) * kWarps;
   for (uint64_t row = warp_global; row < rows; row += warp_stride) {
-    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+    const float4* xr = reinterpret_cast<const float4*>(x + rm(row, cols));
     float4 v[VPL];
     float s = 0.f;
 #pragma unroll
@@ -49,10 +66,11 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
       const int f = lane + 32 * j;
       if (f < vec_cols) {
         v[j] = ld_stream(xr + f);
-        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+        if constexpr (!kRms) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
       }
     }
-    const float mean = warp_sum(s) * inv_cols;
+    float mean = 0.f;
+    if constexpr (!kRms) mean = warp_sum(s) * inv_cols;
     float q = 0.f;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
@@ -64,35 +82,41 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
     }
     const float var = warp_sum(q) * inv_cols;
     const float rstd = 1.0f / sqrtf(var + eps);
-    float4* yr = reinterpret_cast<float4*>(y + row * cols);
+    float4* yr = reinterpret_cast<float4*>(y + rm(row, cols));
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int f = lane + 32 * j;
       if (f < vec_cols) {
-        const float4 g = __ldg(g4 + f), b = __ldg(b4 + f);
+        const float4 g = __ldg(g4 + f);
         float4 o;
-        o.x = (v[j].x - mean) * rstd * g.x + b.x;
-        o.y = (v[j].y - mean) * rstd * g.y + b.y;
-        o.z = (v[j].z - mean) * rstd * g.z + b.z;
-        o.w = (v[j].w - mean) * rstd * g.w + b.w;
+        if constexpr (kRms) {
+          o = make_float4(v[j].x * rstd * g.x, v[j].y * rstd * g.y, v[j].z * rstd * g.z,
+                          v[j].w * rstd * g.w);
+        } else {
+          const float4 b = __ldg(b4 + f);
+          o.x = (v[j].x - mean) * rstd * g.x + b.x;
+          o.y = (v[j].y - mean) * rstd * g.y + b.y;
+          o.z = (v[j].z - mean) * rstd * g.z + b.z;
+          o.w = (v[j].w - mean) * rstd * g.w + b.w;
+        }
         yr[f] = o;  // read next by the projection GEMM: left in L2
       }
     }
     if (lane == 0) {
-      mean_out[row] = mean;
+      if constexpr (!kRms) mean_out[row] = mean;
       rstd_out[row] = rstd;
     }
   }
 }
 
-template <int VPL>
+template <int VPL, bool kRms>
 __global__ void __launch_bounds__(kWarps * 32, VPL <= 8 ? 2 : 1)
 layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dgamma,
                           float* __restrict__ partial_dbeta, float* __restrict__ partial_dsum,
                           const float* __restrict__ dy, const float* __restrict__ x,
                           const float* __restrict__ gamma, const float* __restrict__ mean_in,
                           const float* __restrict__ rstd_in, uint64_t rows, int cols,
-                          uint64_t rows_per_block, int accumulate_dx) {
+                          uint64_t rows_per_block, int accumulate_dx, RowMap rm) {
   pdl_begin();
   // Per-warp dgamma / dbeta accumulators live in shared memory ([kWarps][cols] twice; lane l
   // owns float4 columns l, l + 32, ... of its warp's slice), which keeps the registers for the
@@ -103,15 +127,16 @@ layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dg
   const int vec_cols = cols >> 2;
   const float inv_cols = 1.0f / static_cast<float>(cols);
   const bool with_sum = partial_dsum != nullptr;
+  constexpr int kSumSlice = kRms ? 1 : 2;  // RMSNorm has no dbeta slice
   float4* acc_g = reinterpret_cast<float4*>(smem + warp * cols);
   float4* acc_b = reinterpret_cast<float4*>(smem + (kWarps + warp) * cols);
-  float4* acc_s = reinterpret_cast<float4*>(smem + (2 * kWarps + warp) * cols);
+  float4* acc_s = reinterpret_cast<float4*>(smem + (kSumSlice * kWarps + warp) * cols);
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int f = lane + 32 * j;
     if (f < vec_cols) {
       acc_g[f] = make_float4(0.f, 0.f, 0.f, 0.f);
-      acc_b[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (!kRms) acc_b[f] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (with_sum) acc_s[f] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
@@ -120,10 +145,11 @@ layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dg
   uint64_t row_end = row_begin + rows_per_block;
   if (row_end > rows) row_end = rows;
   for (uint64_t row = row_begin + warp; row < row_end; row += kWarps) {
-    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
-    const float4* dyr = reinterpret_cast<const float4*>(dy + row * cols);
-    float4* dxr = reinterpret_cast<float4*>(dx + row * cols);
-    const float mean = mean_in[row], rstd = rstd_in[row];
+    const uint64_t off = rm(row, cols);
+    const float4* xr = reinterpret_cast<const float4*>(x + off);
+    const float4* dyr = reinterpret_cast<const float4*>(dy + off);
+    float4* dxr = reinterpret_cast<float4*>(dx + off);
+    const float mean = kRms ? 0.f : mean_in[row], rstd = rstd_in[row];
     float4 xh[VPL], d[VPL], prev[VPL];
     // Issue every load of the row (x, dy and the dx being accumulated into) before any use.
 #pragma unroll
@@ -144,22 +170,26 @@ layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dg
                             (xh[j].z - mean) * rstd, (xh[j].w - mean) * rstd);
         const float4 g = __ldg(g4 + f);
         const float g0 = d[j].x * g.x, g1 = d[j].y * g.y, g2 = d[j].z * g.z, g3 = d[j].w * g.w;
-        sg += (g0 + g1) + (g2 + g3);
+        if constexpr (!kRms) sg += (g0 + g1) + (g2 + g3);
         sgx += (g0 * xh[j].x + g1 * xh[j].y) + (g2 * xh[j].z + g3 * xh[j].w);
-        float4 ag = acc_g[f], ab = acc_b[f];
+        float4 ag = acc_g[f];
         ag.x += d[j].x * xh[j].x;
         ag.y += d[j].y * xh[j].y;
         ag.z += d[j].z * xh[j].z;
         ag.w += d[j].w * xh[j].w;
-        ab.x += d[j].x;
-        ab.y += d[j].y;
-        ab.z += d[j].z;
-        ab.w += d[j].w;
         acc_g[f] = ag;
-        acc_b[f] = ab;
+        if constexpr (!kRms) {
+          float4 ab = acc_b[f];
+          ab.x += d[j].x;
+          ab.y += d[j].y;
+          ab.z += d[j].z;
+          ab.w += d[j].w;
+          acc_b[f] = ab;
+        }
       }
     }
-    const float mg = warp_sum(sg) * inv_cols;
+    float mg = 0.f;
+    if constexpr (!kRms) mg = warp_sum(sg) * inv_cols;
     const float mgx = warp_sum(sgx) * inv_cols;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
@@ -193,17 +223,17 @@ layernorm_backward_kernel(float* __restrict__ dx, float* __restrict__ partial_dg
   __syncthreads();
   const float* sg_ = smem;
   const float* sb_ = smem + kWarps * cols;
-  const float* ss_ = smem + 2 * kWarps * cols;
+  const float* ss_ = smem + kSumSlice * kWarps * cols;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
     float a = 0.f, bsum = 0.f, ssum = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       a += sg_[w * cols + c];
-      bsum += sb_[w * cols + c];
+      if constexpr (!kRms) bsum += sb_[w * cols + c];
       if (with_sum) ssum += ss_[w * cols + c];
     }
     partial_dgamma[static_cast<uint64_t>(blockIdx.x) * cols + c] = a;
-    partial_dbeta[static_cast<uint64_t>(blockIdx.x) * cols + c] = bsum;
+    if constexpr (!kRms) partial_dbeta[static_cast<uint64_t>(blockIdx.x) * cols + c] = bsum;
     if (with_sum) partial_dsum[static_cast<uint64_t>(blockIdx.x) * cols + c] = ssum;
   }
 }
@@ -280,7 +310,7 @@ cudaError_t layernorm_forward_launch(float* y, float* mean, float* rstd, const f
   switch (vectors_per_lane(cols)) {
 #define SPAR_LN_FWD(V) \
   case V:              \
-    launch(layernorm_forward_kernel<V>, dim3(grid), dim3(kWarps * 32), 0, stream, y, mean, rstd, x, gamma, beta, rows, c, eps); \
+    launch(layernorm_forward_kernel<V, false>, dim3(grid), dim3(kWarps * 32), 0, stream, y, mean, rstd, x, gamma, beta, rows, c, eps, RowMap{cols, 1}); \
     break;
     SPAR_LN_FWD(1) SPAR_LN_FWD(2) SPAR_LN_FWD(4) SPAR_LN_FWD(6) SPAR_LN_FWD(8) SPAR_LN_FWD(12)
     SPAR_LN_FWD(16)
@@ -307,11 +337,11 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
   switch (vectors_per_lane(cols)) {
 #define SPAR_LN_BWD(V)                                                                          \
   case V: {                                                                                    \
-    auto k = layernorm_backward_kernel<V>;                                                     \
+    auto k = layernorm_backward_kernel<V, false>;                                              \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                                static_cast<int>(smem));                         \
     launch(k, dim3(parts), dim3(kWarps * 32), smem, stream, dx, pa, pb, ps, dy, x, gamma, mean, \
-           rstd, rows, c, rows_per_block, accumulate_dx);                                       \
+           rstd, rows, c, rows_per_block, accumulate_dx, RowMap{cols, 1});                      \
     break;                                                                                     \
   }
     SPAR_LN_BWD(1) SPAR_LN_BWD(2) SPAR_LN_BWD(4) SPAR_LN_BWD(6) SPAR_LN_BWD(8) SPAR_LN_BWD(12)
@@ -324,6 +354,60 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
   if (e != cudaSuccess) return e;
   PartialJobs jobs = {{dgamma, dbeta, dsum}, {pa, pb, ps}, {accumulate_params, accumulate_params, 1}};
   return launch(reduce_partials_kernel, dim3((c + 31) / 32, arrays), dim3(kReduceWarps * 32), 0,
+                stream, jobs, parts, c);
+}
+
+cudaError_t rmsnorm_forward_launch(float* y, float* rstd, const float* x, const float* weight,
+                                   uint64_t rows, uint64_t cols, float eps, int device,
+                                   cudaStream_t stream, uint64_t ld = 0, uint32_t group = 1) {
+  const RowMap rm{ld ? ld : cols, group};
+  const unsigned grid = grid_for(rows, kWarps, sm_count(device) * 8);
+  const int c = static_cast<int>(cols);
+  switch (vectors_per_lane(cols)) {
+#define SPAR_RMS_FWD(V) \
+  case V:               \
+    launch(layernorm_forward_kernel<V, true>, dim3(grid), dim3(kWarps * 32), 0, stream, y, nullptr, rstd, x, weight, nullptr, rows, c, eps, rm); \
+    break;
+    SPAR_RMS_FWD(1) SPAR_RMS_FWD(2) SPAR_RMS_FWD(4) SPAR_RMS_FWD(6) SPAR_RMS_FWD(8) SPAR_RMS_FWD(12)
+    SPAR_RMS_FWD(16)
+#undef SPAR_RMS_FWD
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// workspace: layernorm_backward_parts(rows) x cols floats (the per-block dweight partial rows).
+cudaError_t rmsnorm_backward_launch(float* dx, float* dweight, const float* dy, const float* x,
+                                    const float* weight, const float* rstd, uint64_t rows,
+                                    uint64_t cols, int accumulate_params, int accumulate_dx,
+                                    float* workspace, int device, cudaStream_t stream,
+                                    uint64_t ld = 0, uint32_t group = 1) {
+  const RowMap rm{ld ? ld : cols, group};
+  const int parts = layernorm_backward_parts(rows, device);
+  const uint64_t rows_per_block = (rows + parts - 1) / parts;
+  const int c = static_cast<int>(cols);
+  const size_t smem = kWarps * cols * sizeof(float);
+  switch (vectors_per_lane(cols)) {
+#define SPAR_RMS_BWD(V)                                                                         \
+  case V: {                                                                                    \
+    auto k = layernorm_backward_kernel<V, true>;                                               \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                               static_cast<int>(smem));                         \
+    launch(k, dim3(parts), dim3(kWarps * 32), smem, stream, dx, workspace, nullptr, nullptr, dy, \
+           x, weight, nullptr, rstd, rows, c, rows_per_block, accumulate_dx, rm);               \
+    break;                                                                                     \
+  }
+    SPAR_RMS_BWD(1) SPAR_RMS_BWD(2) SPAR_RMS_BWD(4) SPAR_RMS_BWD(6) SPAR_RMS_BWD(8)
+    SPAR_RMS_BWD(12) SPAR_RMS_BWD(16)
+#undef SPAR_RMS_BWD
+    default:
+      return cudaErrorInvalidValue;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  PartialJobs jobs = {{dweight, nullptr, nullptr}, {workspace, nullptr, nullptr}, {accumulate_params, 0, 0}};
+  return launch(reduce_partials_kernel, dim3((c + 31) / 32, 1), dim3(kReduceWarps * 32), 0,
                 stream, jobs, parts, c);
 }
 
@@ -374,6 +458,109 @@ extern "C" SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma,
   if (e != cudaSuccess) return runtime(e);
   e = layernorm_backward_launch(dx, dgamma, dbeta, dy, x, gamma, mean, rstd, rows, cols,
                                 accumulate_params, accumulate_dx, workspace, device, s, nullptr);
+  const cudaError_t f = cudaFreeAsync(workspace, s);
+  if (e != cudaSuccess) return runtime(e);
+  return f == cudaSuccess ? ok() : runtime(f);
+}
+
+// RMSNorm (nn::RMSNorm, src/nn/rmsnorm.cpp:40-53): the LayerNorm kernels without centring/bias.
+extern "C" SparCudaStatus spar_b200_rmsnorm_forward(float* y, float* rstd, const float* x,
+                                                    const float* weight, uint64_t rows,
+                                                    uint64_t cols, double epsilon, int device,
+                                                    void* stream) {
+  if (rows == 0) return ok();
+  // RMSNorm's constructor checks (rmsnorm.cpp:17-28): positive size, finite positive epsilon.
+  if (cols == 0 || cols % 4 != 0 || vectors_per_lane(cols) == 0 || !y || !rstd || !x || !weight ||
+      !(epsilon > 0.0) || !std::isfinite(epsilon))
+    return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const cudaError_t e = rmsnorm_forward_launch(y, rstd, x, weight, rows, cols,
+                                               static_cast<float>(epsilon), device,
+                                               static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" SparCudaStatus spar_b200_rmsnorm_backward(float* dx, float* dweight, const float* dy,
+                                                     const float* x, const float* weight,
+                                                     const float* rstd, uint64_t rows,
+                                                     uint64_t cols, int accumulate_params,
+                                                     int accumulate_dx, int device, void* stream) {
+  if (cols == 0 || cols % 4 != 0 || vectors_per_lane(cols) == 0 || !dweight || !weight)
+    return invalid();
+  if (rows != 0 && (!dx || !dy || !x || !rstd)) return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (accumulate_params) return ok();
+    const cudaError_t e = cudaMemsetAsync(dweight, 0, cols * sizeof(float), s);
+    return e == cudaSuccess ? ok() : runtime(e);
+  }
+  const int parts = layernorm_backward_parts(rows, device);
+  float* workspace = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&workspace),
+                                  static_cast<uint64_t>(parts) * cols * sizeof(float), s);
+  if (e != cudaSuccess) return runtime(e);
+  e = rmsnorm_backward_launch(dx, dweight, dy, x, weight, rstd, rows, cols, accumulate_params,
+                              accumulate_dx, workspace, device, s);
+  const cudaError_t f = cudaFreeAsync(workspace, s);
+  if (e != cudaSuccess) return runtime(e);
+  return f == cudaSuccess ? ok() : runtime(f);
+}
+
+// qk-norm: RMSNorm(head_dim) over each head of the q or k part of a packed projection output,
+// addressed in place in the [tokens, ld] layout (head h of token t at t * ld + h * head_dim).
+extern "C" SparCudaStatus spar_b200_head_rmsnorm_forward(float* y, const float* x, uint64_t ld,
+                                                         uint64_t tokens, uint64_t heads,
+                                                         uint64_t head_dim, const float* weight,
+                                                         float* rstd, double epsilon, int device,
+                                                         void* stream) {
+  if (tokens == 0) return ok();
+  if (head_dim == 0 || head_dim % 4 != 0 || vectors_per_lane(head_dim) == 0 || heads == 0 ||
+      heads > 0xFFFFFFFFull || ld % 4 != 0 || ld < heads * head_dim || !y || !x || !weight ||
+      !rstd || !(epsilon > 0.0) || !std::isfinite(epsilon) ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15))
+    return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const cudaError_t e = rmsnorm_forward_launch(y, rstd, x, weight, tokens * heads, head_dim,
+                                               static_cast<float>(epsilon), device,
+                                               static_cast<cudaStream_t>(stream), ld,
+                                               static_cast<uint32_t>(heads));
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" SparCudaStatus spar_b200_head_rmsnorm_backward(float* dx, float* dweight,
+                                                          const float* dy, const float* x,
+                                                          uint64_t ld, uint64_t tokens,
+                                                          uint64_t heads, uint64_t head_dim,
+                                                          const float* weight, const float* rstd,
+                                                          int accumulate_params, int device,
+                                                          void* stream) {
+  if (head_dim == 0 || head_dim % 4 != 0 || vectors_per_lane(head_dim) == 0 || heads == 0 ||
+      heads > 0xFFFFFFFFull || ld % 4 != 0 || ld < heads * head_dim || !dweight || !weight)
+    return invalid();
+  if (tokens != 0 && (!dx || !dy || !x || !rstd ||
+                      ((reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dy) |
+                        reinterpret_cast<uintptr_t>(x)) & 15)))
+    return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (tokens == 0) {
+    if (accumulate_params) return ok();
+    const cudaError_t e = cudaMemsetAsync(dweight, 0, head_dim * sizeof(float), s);
+    return e == cudaSuccess ? ok() : runtime(e);
+  }
+  const uint64_t rows = tokens * heads;
+  const int parts = layernorm_backward_parts(rows, device);
+  float* workspace = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&workspace),
+                                  static_cast<uint64_t>(parts) * head_dim * sizeof(float), s);
+  if (e != cudaSuccess) return runtime(e);
+  e = rmsnorm_backward_launch(dx, dweight, dy, x, weight, rstd, rows, head_dim, accumulate_params,
+                              0, workspace, device, s, ld, static_cast<uint32_t>(heads));
   const cudaError_t f = cudaFreeAsync(workspace, s);
   if (e != cudaSuccess) return runtime(e);
   return f == cudaSuccess ? ok() : runtime(f);

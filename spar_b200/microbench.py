@@ -3,7 +3,7 @@ than L2, warm-up first) with the achieved rate against the B200 peaks.
 
   python -m spar_b200.microbench all
   python -m spar_b200.microbench gemm --m 8192 --n 4096 --k 4096 [--at] [--bt] [--x3]
-  python -m spar_b200.microbench layernorm_bwd|gelu_bwd|softmax_bwd|cross_entropy|adamw|attention
+  python -m spar_b200.microbench layernorm_bwd|rmsnorm|swiglu|gelu_bwd|softmax_bwd|cross_entropy|adamw|attention
 
 Bandwidth kernels report algorithmic bytes / time (GB/s); GEMMs report 2mnk / time (TFLOP/s).
 """
@@ -124,6 +124,32 @@ def run_bandwidth(name, iters=10):
                       timed(lambda: ops.layer_norm_backward(dy, x, g, mean, rstd, dg, db, dx,
                                                             accumulate_dx=True), iters),
                       16 * x.numel(), "GB/s", hbm)
+    if name == "rmsnorm":
+        x = torch.randn(65536, 1024, device=dev)  # 256 MB: larger than L2
+        dy = torch.randn_like(x)
+        w = torch.ones(1024, device=dev)
+        _, rstd = ops.rms_norm_forward(x, w)
+        report("rmsnorm_fwd 65536x1024", timed(lambda: ops.rms_norm_forward(x, w), iters),
+               8 * x.numel(), "GB/s", hbm)
+        dx = torch.zeros_like(x)
+        dw = torch.empty_like(w)
+        return report("rmsnorm_bwd 65536x1024",
+                      timed(lambda: ops.rms_norm_backward(dy, x, w, rstd, dw, dx,
+                                                          accumulate_dx=True), iters),
+                      16 * x.numel(), "GB/s", hbm)
+    if name == "swiglu":
+        # gate | value as the two halves of one fused [16384, 2 x 4096] projection output
+        gv = torch.randn(16384, 8192, device=dev)
+        gate, value = gv[:, :4096], gv[:, 4096:]
+        h = torch.empty(16384, 4096, device=dev)
+        dh = torch.randn_like(h)
+        dgv = torch.empty_like(gv)
+        report("swiglu_fwd 16384x4096", timed(lambda: ops.swiglu_forward(gate, value, out=h), iters),
+               12 * h.numel(), "GB/s", hbm)
+        return report("swiglu_bwd 16384x4096",
+                      timed(lambda: ops.swiglu_backward(dh, gate, value, dgv[:, :4096],
+                                                        dgv[:, 4096:]), iters),
+                      20 * h.numel(), "GB/s", hbm)
     if name == "gelu_bwd":
         x = torch.randn(16384, 4096, device=dev)
         dy = torch.randn_like(x)
@@ -183,7 +209,8 @@ def main():
                                   (16384, 32768, 1024, 0, 1)]:
             run_gemm(m, n, k, bool(at), bool(bt), False, a.iters)
         run_attention(iters=a.iters)
-        for name in ("layernorm_bwd", "gelu_bwd", "softmax_bwd", "cross_entropy", "adamw"):
+        for name in ("layernorm_bwd", "rmsnorm", "swiglu", "gelu_bwd", "softmax_bwd",
+                     "cross_entropy", "adamw"):
             run_bandwidth(name, a.iters)
     elif a.kernel == "attention":
         run_attention(b=a.batch, iters=a.iters)

@@ -68,6 +68,89 @@ def layer_norm_backward(dy, x, gamma, mean, rstd, dgamma=None, dbeta=None, dx=No
     return dx, dgamma, dbeta
 
 
+# ------------------------------------------------------------------------------- RMSNorm
+def rms_norm_forward(x, weight, eps: float = 1e-5):
+    _f32(x, "x")
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    y = torch.empty_like(x)
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+    call("spar_b200_rmsnorm_forward", y.data_ptr(), rstd.data_ptr(), x.data_ptr(),
+         _f32(weight, "weight").data_ptr(), rows, cols, eps, _dev(x), _stream(x))
+    return y, rstd
+
+
+def rms_norm_backward(dy, x, weight, rstd, dweight=None, dx=None, accumulate_params=False,
+                      accumulate_dx=False):
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    dx = torch.empty_like(x) if dx is None else dx
+    dweight = torch.empty(cols, device=x.device, dtype=torch.float32) if dweight is None else dweight
+    call("spar_b200_rmsnorm_backward", dx.data_ptr(), dweight.data_ptr(), _f32(dy, "dy").data_ptr(),
+         _f32(x, "x").data_ptr(), weight.data_ptr(), rstd.data_ptr(), rows, cols,
+         int(accumulate_params), int(accumulate_dx), _dev(x), _stream(x))
+    return dx, dweight
+
+
+def head_rms_norm_forward(x, heads: int, head_dim: int, weight, eps: float = 1e-5, out=None):
+    """qk-norm over the first heads * head_dim columns of each row of x (a 2-D view whose rows
+    may be strided, e.g. qkv[:, 0:d] for q); out=x normalises in place."""
+    tokens, _, ld = _rows_view(x, "x")
+    if out is None:  # same row stride as x
+        out = torch.empty(tokens, ld, device=x.device)[:, :heads * head_dim]
+    y = out
+    if y.stride(0) != ld:
+        raise ValueError("out must have the row stride of x")
+    rstd = torch.empty(tokens * heads, device=x.device, dtype=torch.float32)
+    call("spar_b200_head_rmsnorm_forward", y.data_ptr(), x.data_ptr(), ld, tokens, heads, head_dim,
+         _f32(weight, "weight").data_ptr(), rstd.data_ptr(), eps, _dev(x), _stream(x))
+    return y, rstd
+
+
+def head_rms_norm_backward(dy, x, heads: int, head_dim: int, weight, rstd, dweight=None,
+                           out=None, accumulate_params=False):
+    tokens, _, ld = _rows_view(x, "x")
+    if dy.stride(0) != ld:
+        raise ValueError("dy must have the row stride of x")
+    dx = torch.empty(tokens, ld, device=x.device)[:, :heads * head_dim] if out is None else out
+    dweight = torch.empty(head_dim, device=x.device) if dweight is None else dweight
+    call("spar_b200_head_rmsnorm_backward", dx.data_ptr(), dweight.data_ptr(), dy.data_ptr(),
+         x.data_ptr(), ld, tokens, heads, head_dim, weight.data_ptr(), rstd.data_ptr(),
+         int(accumulate_params), _dev(x), _stream(x))
+    return dx, dweight
+
+
+# ------------------------------------------------------------------------------- SwiGLU
+def _rows_view(t, name):
+    """(rows, cols, row stride) of a 2-D float32 tensor whose rows may be strided (a column
+    slice of a wider matrix)."""
+    if t.dtype != torch.float32 or t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D float32 tensor with unit column stride")
+    return t.shape[0], t.shape[1], t.stride(0)
+
+
+def swiglu_forward(gate, value, out=None):
+    rows, cols, ldg = _rows_view(gate, "gate")
+    _, _, ldv = _rows_view(value, "value")
+    h = torch.empty(rows, cols, device=gate.device, dtype=torch.float32) if out is None else out
+    call("spar_b200_swiglu_forward", h.data_ptr(), _rows_view(h, "h")[2], gate.data_ptr(), ldg,
+         value.data_ptr(), ldv, rows, cols, _dev(gate), _stream(gate))
+    return h
+
+
+def swiglu_backward(dh, gate, value, dgate=None, dvalue=None):
+    rows, cols, ldg = _rows_view(gate, "gate")
+    _, _, ldv = _rows_view(value, "value")
+    _, _, lddh = _rows_view(dh, "dh")
+    new = lambda: torch.empty(rows, cols, device=gate.device, dtype=torch.float32)  # noqa: E731
+    dgate = new() if dgate is None else dgate
+    dvalue = new() if dvalue is None else dvalue
+    call("spar_b200_swiglu_backward", dgate.data_ptr(), _rows_view(dgate, "dgate")[2],
+         dvalue.data_ptr(), _rows_view(dvalue, "dvalue")[2], dh.data_ptr(), lddh,
+         gate.data_ptr(), ldg, value.data_ptr(), ldv, rows, cols, _dev(gate), _stream(gate))
+    return dgate, dvalue
+
+
 # ------------------------------------------------------------------------------- GELU
 def gelu_forward(x):
     y = torch.empty_like(_f32(x, "x"))

@@ -7,7 +7,8 @@ CPU oracle and the CUDA path are pinned to the reference's behaviour.
 Inputs are regenerated from seeds (SplitMix64 streams of oracle/spar_oracle.py, which the tests
 also use); each .npz stores the inputs it needs and the reference outputs.
 
-Usage: python tests/golden/make_golden.py   (takes a few minutes: the reference is slow)
+Usage: python tests/golden/make_golden.py [name ...]   (all fixtures take a few minutes: the
+reference is slow; names restrict the writes, e.g. `rmsnorm swiglu`)
 """
 from __future__ import annotations
 
@@ -34,7 +35,15 @@ def save(name, **arrays):
     print(name, {k: v.shape for k, v in arrays.items()})
 
 
-def main():
+def main(only=()):
+    """Writes every fixture, or only those named in `only` (the .npz stems)."""
+    global save
+    if only:
+        write = save
+
+        def save(name, **arrays):  # noqa: F811 - restrict the writes to the names asked for
+            if name in only:
+                write(name, **arrays)
     # LayerNorm (composed from Spar ops), incl. a wide-range row
     x = normal(1, (24, 64))
     x[3] *= 100.0
@@ -43,6 +52,23 @@ def main():
     dy = normal(4, (24, 64))
     y, dx, dg, db = R.layernorm(x, g, b, dy, 1e-5)
     save("layernorm", x=x, gamma=g, beta=b, dy=dy, y=y, dx=dx, dgamma=dg, dbeta=db)
+
+    # RMSNorm (nn::RMSNorm), incl. a wide-range row and a zero row
+    x = normal(30, (24, 96))
+    x[5] *= 100.0
+    x[9] = 0.0
+    w = 1.0 + normal(31, (96,), 0.1)
+    dy = normal(32, (24, 96))
+    y, dx, dw = R.rmsnorm(x, w, dy, 1e-5)
+    save("rmsnorm", x=x, weight=w, dy=dy, y=y, dx=dx, dweight=dw)
+
+    # SwiGLU (nn::swiglu), incl. large |gate| and zero
+    gt = np.concatenate([normal(33, (500,), 3.0),
+                         np.array([0.0, -30.0, 30.0, 1e-6, -1e-6, -90.0, 90.0], np.float32)])
+    vl = normal(34, gt.shape)
+    dh = normal(35, gt.shape)
+    h, dgt, dvl = R.swiglu(gt, vl, dh)
+    save("swiglu", gate=gt, value=vl, dh=dh, h=h, dgate=dgt, dvalue=dvl)
 
     # GELU through Spar's sigmoid, incl. large |x| and zero
     x = np.concatenate([normal(5, (500,), 3.0), np.array([0.0, -30.0, 30.0, 1e-6, -1e-6, 15.0],
@@ -120,4 +146,4 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]))

@@ -38,6 +38,21 @@ def test_oracle_gelu_matches_reference():
     assert rel_err(f["dx"], f["dy"] * O.gelu_derivative(f["x"])) <= TOL
 
 
+def test_oracle_rmsnorm_matches_reference():
+    f = load("rmsnorm")
+    y, _ = O.rms_norm_forward(f["x"], f["weight"], 1e-5, np.float64)
+    dx, dw = O.rms_norm_backward(f["dy"], f["x"], f["weight"], 1e-5)
+    assert rel_err(f["y"], y) <= TOL
+    assert rel_err(f["dx"], dx) <= TOL and rel_err(f["dweight"], dw) <= TOL
+
+
+def test_oracle_swiglu_matches_reference():
+    f = load("swiglu")
+    assert rel_err(f["h"], O.swiglu_forward(f["gate"], f["value"], np.float64)) <= TOL
+    dg, dv = O.swiglu_backward(f["dh"], f["gate"], f["value"])
+    assert rel_err(f["dgate"], dg) <= TOL and rel_err(f["dvalue"], dv) <= TOL
+
+
 def test_oracle_causal_softmax_matches_reference():
     f = load("causal_softmax")
     scale = float(f["scale"])
@@ -142,6 +157,16 @@ def test_reference_library_agrees_with_oracle_when_built():
     y, dx, _, _ = cpu_ref.layernorm(x, g, b, dy)
     assert rel_err(y, O.layer_norm_forward(x, g, b, 1e-5, np.float64)[0]) <= TOL
     assert rel_err(dx, O.layer_norm_backward(dy, x, g)[0]) <= TOL
+    w = (1 + 0.1 * r.standard_normal(40)).astype(np.float32)
+    y, dx, dw = cpu_ref.rmsnorm(x, w, dy)
+    assert rel_err(y, O.rms_norm_forward(x, w, 1e-5, np.float64)[0]) <= TOL
+    rdx, rdw = O.rms_norm_backward(dy, x, w)
+    assert rel_err(dx, rdx) <= TOL and rel_err(dw, rdw) <= TOL
+    v = r.standard_normal((7, 40)).astype(np.float32)
+    h, dg, dv = cpu_ref.swiglu(4 * x, v, dy)
+    assert rel_err(h, O.swiglu_forward(4 * x, v, np.float64)) <= TOL
+    odg, odv = O.swiglu_backward(dy, 4 * x, v)
+    assert rel_err(dg, odg) <= TOL and rel_err(dv, odv) <= TOL
 
 
 # ------------------------------------------------------------------------------ CUDA (GPU)
@@ -184,6 +209,28 @@ def test_cuda_ops_match_reference_fixtures(cuda):
     n_lm = len(f4["lm_ids"]) // seq * (seq - 1)
     assert abs(lml.cpu().numpy().astype(np.float64).sum() / n_lm - f4["lm_loss"]) <= TOL * f4["lm_loss"]
     assert rel_err(xr.cpu().numpy(), f5["out"]) <= TOL and rel_err(dr.cpu().numpy(), f5["dx"]) <= TOL
+
+
+@pytest.mark.gpu
+def test_cuda_rmsnorm_swiglu_match_reference_fixtures(cuda):
+    import torch
+    from spar_b200 import ops
+
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    f = load("rmsnorm")
+    y, rstd = ops.rms_norm_forward(T(f["x"]), T(f["weight"]))
+    dx, dw = ops.rms_norm_backward(T(f["dy"]), T(f["x"]), T(f["weight"]), rstd)
+    g = load("swiglu")
+    n = g["gate"].size
+    h = ops.swiglu_forward(T(g["gate"]).view(1, n), T(g["value"]).view(1, n))
+    dg, dv = ops.swiglu_backward(T(g["dh"]).view(1, n), T(g["gate"]).view(1, n),
+                                 T(g["value"]).view(1, n))
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), f["y"]) <= TOL and rel_err(dx.cpu().numpy(), f["dx"]) <= TOL
+    assert rel_err(dw.cpu().numpy(), f["dweight"]) <= TOL
+    assert rel_err(h.cpu().numpy().ravel(), g["h"]) <= TOL
+    assert rel_err(dg.cpu().numpy().ravel(), g["dgate"]) <= TOL
+    assert rel_err(dv.cpu().numpy().ravel(), g["dvalue"]) <= TOL
 
 
 @pytest.mark.gpu

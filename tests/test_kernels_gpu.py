@@ -60,6 +60,114 @@ def test_layernorm_backward_accumulate_and_deterministic(cuda):
     assert torch.allclose(dg3, 2 * dg1, rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("rows,cols", [(64, 128), (257, 768), (2048, 1024), (33, 2048), (7, 4)])
+def test_rmsnorm_forward_backward(cuda, rows, cols):
+    import torch
+    from spar_b200 import ops
+
+    r = _rng(rows * cols + 1)
+    x = r.standard_normal((rows, cols)).astype(np.float32)
+    x[0] *= 50.0
+    w = (1 + 0.1 * r.standard_normal(cols)).astype(np.float32)
+    dy = r.standard_normal((rows, cols)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    y, rstd = ops.rms_norm_forward(t(x), t(w), 1e-5)
+    dx, dw = ops.rms_norm_backward(t(dy), t(x), t(w), rstd)
+    torch.cuda.synchronize()
+    y64, rstd64 = O.rms_norm_forward(x, w, 1e-5, np.float64)
+    dx64, dw64 = O.rms_norm_backward(dy, x, w, 1e-5)
+    assert rel_err(y.cpu().numpy(), y64) <= TOL and rel_err(rstd.cpu().numpy(), rstd64) <= TOL
+    assert rel_err(dx.cpu().numpy(), dx64) <= TOL
+    assert rel_err(dw.cpu().numpy(), dw64) <= TOL
+
+
+def test_rmsnorm_backward_accumulate_deterministic_and_empty(cuda):
+    import torch
+    from spar_b200 import ops
+
+    r = _rng(6)
+    x = torch.from_numpy(r.standard_normal((1000, 1024)).astype(np.float32)).to(cuda)
+    dy = torch.from_numpy(r.standard_normal((1000, 1024)).astype(np.float32)).to(cuda)
+    w = torch.ones(1024, device=cuda)
+    _, rstd = ops.rms_norm_forward(x, w)
+    dx1, dw1 = ops.rms_norm_backward(dy, x, w, rstd)
+    dx2, dw2 = ops.rms_norm_backward(dy, x, w, rstd)
+    assert torch.equal(dw1, dw2) and torch.equal(dx1, dx2)
+    dw3, dx3 = dw1.clone(), dx1.clone()
+    ops.rms_norm_backward(dy, x, w, rstd, dweight=dw3, dx=dx3, accumulate_params=True,
+                          accumulate_dx=True)
+    torch.cuda.synchronize()
+    assert torch.allclose(dw3, 2 * dw1, rtol=1e-6, atol=1e-6)
+    assert torch.allclose(dx3, 2 * dx1, rtol=1e-6, atol=1e-6)
+    # No rows: the weight gradient is zero (or left alone when accumulating).
+    e = torch.empty(0, 1024, device=cuda)
+    dwz = torch.full((1024,), 5.0, device=cuda)
+    ops.rms_norm_backward(e, e, w, torch.empty(0, device=cuda), dweight=dwz)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(dwz).item() == 0
+
+
+@pytest.mark.parametrize("tokens,heads,head_dim", [(2048, 16, 64), (37, 4, 32), (5, 3, 128)])
+def test_head_rmsnorm_qk_norm(cuda, tokens, heads, head_dim):
+    """qk-norm on the q and k parts of a packed [tokens, 3d] projection, in place, against the
+    oracle RMSNorm over each head's features; the v part is untouched."""
+    import torch
+    from spar_b200 import ops
+
+    d = heads * head_dim
+    r = _rng(tokens * heads + head_dim)
+    qkv = (2 * r.standard_normal((tokens, 3 * d))).astype(np.float32)
+    w = (1 + 0.1 * r.standard_normal(head_dim)).astype(np.float32)
+    dy = r.standard_normal((tokens, 3 * d)).astype(np.float32)
+    t = torch.from_numpy(qkv.copy()).to(cuda)
+    wt = torch.from_numpy(w).to(cuda)
+    dyt = torch.from_numpy(dy).to(cuda)
+    q, k = t[:, :d], t[:, d:2 * d]
+    saved = t.clone()  # the inputs, with the packed row stride
+    x_q, x_k = saved[:, :d], saved[:, d:2 * d]
+    _, rq = ops.head_rms_norm_forward(q, heads, head_dim, wt, out=q)
+    yk, rk = ops.head_rms_norm_forward(k, heads, head_dim, wt)
+    dxq, dwq = ops.head_rms_norm_backward(dyt[:, :d], x_q, heads, head_dim, wt, rq)
+    dxk, dwk = ops.head_rms_norm_backward(dyt[:, d:2 * d], x_k, heads, head_dim, wt, rk)
+    torch.cuda.synchronize()
+    out = t.cpu().numpy()
+    assert np.array_equal(out[:, 2 * d:], qkv[:, 2 * d:]) and np.array_equal(out[:, d:2 * d], qkv[:, d:2 * d])
+    for part, y, dx, dw in ((0, out[:, :d], dxq, dwq), (1, yk.cpu().numpy(), dxk, dwk)):
+        xs = qkv[:, part * d:(part + 1) * d].reshape(tokens * heads, head_dim)
+        dys = dy[:, part * d:(part + 1) * d].reshape(tokens * heads, head_dim)
+        y64, _ = O.rms_norm_forward(xs, w, 1e-5, np.float64)
+        dx64, dw64 = O.rms_norm_backward(dys, xs, w, 1e-5)
+        assert rel_err(np.asarray(y).reshape(tokens * heads, head_dim), y64) <= TOL
+        assert rel_err(dx.cpu().numpy().reshape(tokens * heads, head_dim), dx64) <= TOL
+        assert rel_err(dw.cpu().numpy(), dw64) <= TOL
+
+
+@pytest.mark.parametrize("rows,cols,fused", [(2048, 4096, True), (2048, 4096, False), (3, 7, True),
+                                             (1, 1, False), (513, 1028, True)])
+def test_swiglu(cuda, rows, cols, fused):
+    """gate / value as the two column halves of one [rows, 2 cols] projection (row stride 2 cols)
+    or as separate tensors; odd widths take the scalar path."""
+    import torch
+    from spar_b200 import ops
+
+    r = _rng(rows * cols + int(fused))
+    gv = (3 * r.standard_normal((rows, 2 * cols))).astype(np.float32)
+    gv[0, :4 if cols >= 4 else 1] = [0.0, -40.0, 40.0, 1e-6][:4 if cols >= 4 else 1]
+    dh = r.standard_normal((rows, cols)).astype(np.float32)
+    t = torch.from_numpy(gv).to(cuda)
+    if fused:
+        gate, value = t[:, :cols], t[:, cols:]
+    else:
+        gate, value = t[:, :cols].contiguous(), t[:, cols:].contiguous()
+    h = ops.swiglu_forward(gate, value)
+    dg, dv = ops.swiglu_backward(torch.from_numpy(dh).to(cuda), gate, value)
+    torch.cuda.synchronize()
+    g64, v64 = gv[:, :cols], gv[:, cols:]
+    assert rel_err(h.cpu().numpy(), O.swiglu_forward(g64, v64, np.float64)) <= TOL
+    odg, odv = O.swiglu_backward(dh, g64, v64)
+    assert rel_err(dg.cpu().numpy(), odg) <= TOL and rel_err(dv.cpu().numpy(), odv) <= TOL
+
+
 @pytest.mark.parametrize("n", [1, 7, 4096, 1 << 20])
 def test_gelu(cuda, n):
     import torch
