@@ -309,6 +309,19 @@ struct SparCudaStatus spar_b200_attention_backward(const float* qkv, const float
                                                    uint64_t batch, uint64_t seq, uint64_t heads,
                                                    uint64_t head_dim, const float* rope_table,
                                                    int device, void* stream);
+/* Grouped-query attention (SelfAttention with num_kv_heads < num_query_heads,                  */
+/* src/nn/attention.cpp:168-186; repeat_kv_heads :77-94): query head h attends with key / value  */
+/* head h / (heads / kv_heads), without materialising the repeated heads. qkv and dqkv rows are  */
+/* [Q (heads) | K (kv_heads) | V (kv_heads)] x head_dim; dK / dV sum over each head's group      */
+/* (deterministic). kv_heads must divide heads; kv_heads == heads is the call above.            */
+struct SparCudaStatus spar_b200_attention_forward_gqa(const float* qkv, float* ctx, float* row_max,
+                                                      float* row_inv, uint64_t batch, uint64_t seq,
+                                                      uint64_t heads, uint64_t kv_heads,
+                                                      uint64_t head_dim, int device, void* stream);
+struct SparCudaStatus spar_b200_attention_backward_gqa(
+    const float* qkv, const float* ctx, const float* dctx, const float* row_max,
+    const float* row_inv, float* delta, float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
+    uint64_t kv_heads, uint64_t head_dim, const float* rope_table, int device, void* stream);
 /* As spar_b200_gemm_error, for the attention kernels' bounded waits. */
 int spar_b200_attention_error(int device, int clear);
 

@@ -34,6 +34,7 @@ def load():
             "ref_gelu": [F, F, c_int64, F, F],
             "ref_rmsnorm": [F, F, F, c_int64, c_int64, c_double, F, F, F],
             "ref_swiglu": [F, F, F, c_int64, F, F, F],
+            "ref_attention": [F, F, F, F] + [c_int64] * 5 + [F, F, F, F],
             "ref_causal_softmax": [F, F, c_int64, c_int64, c_double, F, F],
             "ref_cross_entropy": [F, I32, c_int64, c_int64, c_int64, F, F],
             "ref_matmul": [F, F, F, c_int64, c_int64, c_int64, F, F, F],
@@ -92,6 +93,18 @@ def swiglu(gate, value, dh):
     h, dg, dv = np.empty_like(gate), np.empty_like(gate), np.empty_like(gate)
     _check(load().ref_swiglu(_p(gate), _p(value), _p(dh), gate.size, _p(h), _p(dg), _p(dv)))
     return h, dg, dv
+
+
+def attention(q, k, v, d_out):
+    """Causal scaled_dot_product_attention; q [b, h, t, dh], k / v [b, kvh, t, dh]."""
+    q, k, v, d_out = map(_f, (q, k, v, d_out))
+    b, h, t, dh = q.shape
+    kvh = k.shape[1]
+    out, dq = np.empty_like(q), np.empty_like(q)
+    dk, dv = np.empty_like(k), np.empty_like(v)
+    _check(load().ref_attention(_p(q), _p(k), _p(v), _p(d_out), b, h, kvh, t, dh, _p(out), _p(dq),
+                                _p(dk), _p(dv)))
+    return out, dq, dk, dv
 
 
 def gelu(x, dy):

@@ -193,6 +193,25 @@ int ref_swiglu(const float* gate, const float* value, const float* dh, int64_t n
   });
 }
 
+// nn::scaled_dot_product_attention (src/nn/attention.cpp:121-135), causal, with key / value of
+// kv_heads heads (repeat_kv_heads inside): q [b, heads, t, dh], k / v [b, kv_heads, t, dh].
+int ref_attention(const float* q, const float* k, const float* v, const float* d_out, int64_t b,
+                  int64_t heads, int64_t kv_heads, int64_t t, int64_t dh, float* out, float* dq,
+                  float* dk, float* dv) {
+  return guarded([&] {
+    Tensor tq = from_host(q, {b, heads, t, dh}, true);
+    Tensor tk = from_host(k, {b, kv_heads, t, dh}, true);
+    Tensor tv = from_host(v, {b, kv_heads, t, dh}, true);
+    Tensor o = nn::scaled_dot_product_attention(tq, tk, tv, true);
+    to_host(o, out);
+    Tensor loss = weighted_sum(o, d_out);
+    loss.backward();
+    to_host(tq.grad(), dq);
+    to_host(tk.grad(), dk);
+    to_host(tv.grad(), dv);
+  });
+}
+
 int ref_gelu(const float* x, const float* dy, int64_t n, float* y, float* dx) {
   return guarded([&] {
     Tensor tx = from_host(x, {n}, true);

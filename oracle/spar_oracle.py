@@ -208,25 +208,37 @@ def causal_softmax_backward(dp, p, scale, dtype=np.float64):
     return np.where(mask, p * (dp - dot) * scale, 0.0)
 
 
-def attention_forward_backward(qkv, heads, dctx=None, dtype=np.float64):
-    """Causal self-attention over a packed projection buffer qkv [B, T, 3d] (Q | K | V thirds,
-    head h at columns h*dh of each): scaled_dot_product_attention (src/nn/attention.cpp:121-135:
-    matmul(Q, K^T) * 1/sqrt(dh), + causal_mask, softmax over keys, matmul(P, V)) and, given
-    dctx [B, T, d], the autograd backward of that chain (matmul backward, softmax backward
-    src/ops/softmax.cpp:110-150, scalar-multiply backward). Returns (ctx, dqkv or None)."""
+def attention_forward_backward(qkv, heads, dctx=None, dtype=np.float64, kv_heads=None):
+    """Causal self-attention over a packed projection buffer qkv [B, T, (H + 2 KVH) dh] (Q | K | V,
+    head h at columns h*dh of each part; KVH = kv_heads, default H): scaled_dot_product_attention
+    (src/nn/attention.cpp:121-135: matmul(Q, K^T) * 1/sqrt(dh), + causal_mask, softmax over keys,
+    matmul(P, V)) after repeat_kv_heads (:77-94: kv head j serves query heads j*G .. j*G+G-1,
+    G = H / KVH) and, given dctx [B, T, H dh], the autograd backward of that chain (matmul
+    backward, softmax backward src/ops/softmax.cpp:110-150, scalar-multiply backward; the repeat's
+    backward sums each group's dK / dV). Returns (ctx, dqkv or None)."""
     qkv = np.asarray(qkv, dtype)
-    b, t, d3 = qkv.shape
-    d = d3 // 3
-    dh = d // heads
+    kvh = heads if kv_heads is None else kv_heads
+    b, t, width = qkv.shape
+    dh = width // (heads + 2 * kvh)
+    d, dk_w = heads * dh, kvh * dh
+    group = heads // kvh
     scale = 1.0 / math.sqrt(dh)
 
-    def split(x):  # [B, T, d] -> [B, H, T, dh]
-        return x.reshape(b, t, heads, dh).transpose(0, 2, 1, 3)
+    def split(x, n):  # [B, T, n dh] -> [B, n, T, dh]
+        return x.reshape(b, t, n, dh).transpose(0, 2, 1, 3)
 
     def merge(x):
-        return x.transpose(0, 2, 1, 3).reshape(b, t, d)
+        return x.transpose(0, 2, 1, 3).reshape(b, t, -1)
 
-    q, k, v = split(qkv[..., :d]), split(qkv[..., d:2 * d]), split(qkv[..., 2 * d:])
+    def repeat(x):  # repeat_kv_heads: [B, KVH, T, dh] -> [B, H, T, dh]
+        return np.repeat(x, group, axis=1)
+
+    def group_sum(x):  # backward of repeat: [B, H, T, dh] -> [B, KVH, T, dh]
+        return x.reshape(b, kvh, group, t, dh).sum(axis=2)
+
+    q = split(qkv[..., :d], heads)
+    k = repeat(split(qkv[..., d:d + dk_w], kvh))
+    v = repeat(split(qkv[..., d + dk_w:], kvh))
     mask = np.triu(np.ones((t, t), dtype=bool), 1)
     s = np.where(mask, -np.inf, (q @ k.transpose(0, 1, 3, 2)) * scale)
     e = np.exp(s - s.max(-1, keepdims=True))
@@ -234,13 +246,13 @@ def attention_forward_backward(qkv, heads, dctx=None, dtype=np.float64):
     ctx = merge(pr @ v)
     if dctx is None:
         return ctx, None
-    do = split(np.asarray(dctx, dtype))
+    do = split(np.asarray(dctx, dtype), heads)
     dp = do @ v.transpose(0, 1, 3, 2)
     dv = pr.transpose(0, 1, 3, 2) @ do
     ds = pr * (dp - (dp * pr).sum(-1, keepdims=True)) * scale
     dq = ds @ k
     dk = ds.transpose(0, 1, 3, 2) @ q
-    return ctx, np.concatenate([merge(dq), merge(dk), merge(dv)], axis=-1)
+    return ctx, np.concatenate([merge(dq), merge(group_sum(dk)), merge(group_sum(dv))], axis=-1)
 
 
 # ------------------------------------------------------------------------------ cross-entropy

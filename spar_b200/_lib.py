@@ -83,6 +83,9 @@ SIGNATURES = {
     "spar_b200_gemm_error": (c_int, [i, i]),
     "spar_b200_attention_forward": (S, [p, p, p, p, u64, u64, u64, u64, i, p]),
     "spar_b200_attention_backward": (S, [p, p, p, p, p, p, p, u64, u64, u64, u64, p, i, p]),
+    "spar_b200_attention_forward_gqa": (S, [p, p, p, p, u64, u64, u64, u64, u64, i, p]),
+    "spar_b200_attention_backward_gqa": (S, [p, p, p, p, p, p, p, u64, u64, u64, u64, u64, p, i,
+                                             p]),
     "spar_b200_attention_error": (c_int, [i, i]),
     "spar_b200_lm_create": (S, [POINTER(SparB200LMConfig), i, POINTER(c_void_p)]),
     "spar_b200_lm_destroy": (None, [p]),

@@ -5,7 +5,11 @@
 // This computes what Spar's scaled_dot_product_attention does (src/nn/attention.cpp:121-135:
 // scores = (Q K^T) * 1/sqrt(head_dim), causal -inf mask, softmax over the last axis, P V) and its
 // autograd backward (matmul / softmax backward), for the packed projection buffer
-// qkv [batch, seq, 3*model_dim] (Q | K | V, head h at columns h*head_dim of each third).
+// qkv [batch, seq, (heads + 2 kv_heads) * head_dim] (Q | K | V, head h at columns h*head_dim of
+// each part). With kv_heads < heads (grouped-query attention, repeat_kv_heads of
+// src/nn/attention.cpp:77-94) query head h reads key / value head h / (heads / kv_heads); the key
+// kernel's items are (batch, key/value head, key tile) and sweep every query head of the group,
+// so dK / dV come out summed over the group without the repeated heads ever existing.
 //
 // Forward (one CTA per SM, persistent; work item = (batch, head, query tiles t and T-1-t), so
 // every item costs the same T+1 key-tile products): the two query tiles alternate on the tensor
@@ -69,6 +73,10 @@ struct AttnParams {
   float* delta;        // [batch*heads, seq]: D
   const float2* rope;  // optional RoPE table [seq, head_dim / 2]: dQ, dK leave inverse-rotated
   uint32_t heads, seq, model_dim, bh;
+  // Grouped-query attention (repeat_kv_heads, src/nn/attention.cpp:77-94): query head h reads
+  // key / value head h / group; K and V start at columns kcol and vcol of each qkv / dqkv row
+  // (group 1: kcol = model_dim, vcol = 2 * model_dim).
+  uint32_t group, kv_heads, kv_bh, kcol, vcol;
   uint64_t ld_o;  // row stride of O and dO
   float scale, scale_log2;
   uint32_t tiles;  // stationary tiles per (batch, head)
@@ -131,6 +139,17 @@ __device__ __forceinline__ void inverse_rope(float (&o)[32], const float2* tab) 
 struct Item {
   uint32_t b, h, t;
 };
+
+// Key-side items of the backward: (batch, key/value head, 128-key tile).
+__device__ __forceinline__ Item decode_kv(const AttnParams& p, uint32_t idx) {
+  const uint32_t tile = idx / p.kv_bh;
+  const uint32_t bh = idx - tile * p.kv_bh;
+  Item it;
+  it.b = bh / p.kv_heads;
+  it.h = bh - it.b * p.kv_heads;
+  it.t = tile;
+  return it;
+}
 
 __device__ __forceinline__ Item decode(const AttnParams& p, uint32_t idx, bool descending) {
   const uint32_t tile = idx / p.bh;
@@ -354,7 +373,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_begin();  // set-up done; global memory from here on
-  const int dcol = static_cast<int>(p.model_dim);
 
   if (warp == 0) {
     // -------------------------------------------------------------- TMA producer
@@ -368,6 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x) {
         const PairItem it = decode_pair(p, idx);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
+        const int kvc = static_cast<int>(it.h / p.group * DH);
+        const int kc = static_cast<int>(p.kcol) + kvc, vc = static_cast<int>(p.vcol) + kvc;
         bool ok = true;
         for (int x = it.na ? 0 : 1; x < 2 && ok; ++x) {
           const uint32_t t = x ? it.tb : it.ta;
@@ -391,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 #pragma unroll
             for (int c = 0; c < DH / 32; ++c)
               tc::tma_load_4d(smem + L::kK + st * L::kTile + c * 16384, &p.qk128, k_full + st,
-                              dcol + hc + 32 * c, row, b, 0);
+                              kc + 32 * c, row, b, 0);
             ++kn;
           }
           {
@@ -404,8 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 #pragma unroll
               for (int c = 0; c < DH / 32; ++c)
                 tc::tma_load_4d(smem + L::kV + st * L::kTile + (kb * (DH / 32) + c) * 4096,
-                                &p.qkv_mn, v_full + st, 2 * dcol + hc + 32 * c, row + 32 * kb, b,
-                                0);
+                                &p.qkv_mn, v_full + st, vc + 32 * c, row + 32 * kb, b, 0);
             ++vn;
           }
         }
@@ -673,7 +692,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_begin();  // set-up done; global memory from here on
-  const int dcol = static_cast<int>(p.model_dim);
   const uint32_t seq = p.seq;
 
   if (warp == 0) {
@@ -684,6 +702,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
         const Item it = decode(p, idx, true);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
+        const int kvc = static_cast<int>(it.h / p.group * DH);
+        const int kc = static_cast<int>(p.kcol) + kvc, vc = static_cast<int>(p.vcol) + kvc;
         if (!wait_or_abort(q_empty, (item & 1) ^ 1, abort_flag)) break;
         tc::mbar_arrive_expect_tx(q_full, 2 * L::kTile128);
         last_q = item & 1;
@@ -702,16 +722,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
           const int row = static_cast<int>(j * 64);
 #pragma unroll
           for (int c = 0; c < DH / 32; ++c) {
-            tc::tma_load_4d(s + c * 8192, &p.qk64, kv_full + st, dcol + hc + 32 * c, row, b, 0);
-            tc::tma_load_4d(s + L::kTile64 + c * 8192, &p.qk64, kv_full + st,
-                            2 * dcol + hc + 32 * c, row, b, 0);
+            tc::tma_load_4d(s + c * 8192, &p.qk64, kv_full + st, kc + 32 * c, row, b, 0);
+            tc::tma_load_4d(s + L::kTile64 + c * 8192, &p.qk64, kv_full + st, vc + 32 * c, row, b,
+                            0);
           }
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
             for (int c = 0; c < DH / 32; ++c)
               tc::tma_load_4d(s + 2 * L::kTile64 + (kb * (DH / 32) + c) * 4096, &p.qkv_mn,
-                              kv_full + st, dcol + hc + 32 * c, row + 32 * kb, b, 0);
+                              kv_full + st, kc + 32 * c, row + 32 * kb, b, 0);
           if (++st == L::kStages) {
             st = 0;
             ph ^= 1;
@@ -944,7 +964,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_begin();  // set-up done; global memory from here on
-  const int dcol = static_cast<int>(p.model_dim);
   const uint32_t seq = p.seq;
   const uint32_t nq_all = (seq + 63) / 64;
 
@@ -953,19 +972,23 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       uint32_t n = 0, item = 0;
       int last_kv = -1, last_kq[2] = {-1, -1}, last_mn[2] = {-1, -1};
       for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
-        const Item it = decode(p, idx, false);
-        const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
+        const Item it = decode_kv(p, idx);  // it.h: the key / value head
+        const int b = static_cast<int>(it.b);
+        const int kc = static_cast<int>(p.kcol + it.h * DH), vc = static_cast<int>(p.vcol + it.h * DH);
         if (!wait_or_abort(kv_empty, (item & 1) ^ 1, abort_flag)) break;
         tc::mbar_arrive_expect_tx(kv_full, 2 * L::kTile128);
         last_kv = item & 1;
         const int k0 = static_cast<int>(it.t * 128);
 #pragma unroll
         for (int c = 0; c < DH / 32; ++c) {
-          tc::tma_load_4d(smem + L::kK + c * 16384, &p.qk128, kv_full, dcol + hc + 32 * c, k0, b, 0);
-          tc::tma_load_4d(smem + L::kV + c * 16384, &p.qk128, kv_full, 2 * dcol + hc + 32 * c, k0,
-                          b, 0);
+          tc::tma_load_4d(smem + L::kK + c * 16384, &p.qk128, kv_full, kc + 32 * c, k0, b, 0);
+          tc::tma_load_4d(smem + L::kV + c * 16384, &p.qk128, kv_full, vc + 32 * c, k0, b, 0);
         }
-        for (uint32_t i = 2 * it.t; i < nq_all; ++i, ++n) {
+        // Every query head of the group, each over the query tiles at or after the key tile.
+        const uint32_t steps = nq_all - 2 * it.t;
+        for (uint32_t j = 0; j < steps * p.group; ++j, ++n) {
+          const uint32_t i = 2 * it.t + j % steps;
+          const int hc = static_cast<int>((it.h * p.group + j / steps) * DH);
           const uint32_t st = n & 1, ph = (n >> 1) & 1;
           const int row = static_cast<int>(i * 64);
           if (!wait_or_abort(kq_empty + st, ph ^ 1, abort_flag)) break;
@@ -1028,8 +1051,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         return true;
       };
       for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x, ++item) {
-        const Item it = decode(p, idx, false);
-        const uint32_t steps = nq_all - 2 * it.t;  // >= 1: every 128-key tile starts below seq
+        const Item it = decode_kv(p, idx);
+        // >= 1 query tile per head (every 128-key tile starts below seq), for each head of the group
+        const uint32_t steps = (nq_all - 2 * it.t) * p.group;
         if (!(ok = wait_or_abort(kv_full, item & 1, abort_flag))) break;
         tc::tc_fence_after();
         const uint32_t n0 = n, sn0 = sn;
@@ -1080,17 +1104,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       return (u < 192 && q < seq) ? __ldg(src + sbase + q) : 0.f;
     };
     for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
-      const Item it = decode(p, idx, false);
+      const Item it = decode_kv(p, idx);
       const uint32_t i0 = 2 * it.t;
-      const uint32_t steps = nq_all - i0;
+      const uint32_t per_head = nq_all - i0;
+      const uint32_t steps = per_head * p.group;
       const uint32_t kv = it.t * 128 + r;
-      const uint64_t sbase = static_cast<uint64_t>(it.b * p.heads + it.h) * seq;
-      float next = fetch(sbase, i0 * 64);
-      for (uint32_t i = 0; i < steps && ok; ++i, ++n) {
+      // Statistics of query head it.h * group + j / per_head, query tile i0 + j % per_head.
+      auto stat_base = [&](uint32_t j) {
+        return static_cast<uint64_t>(it.b * p.heads + it.h * p.group + j / per_head) * seq;
+      };
+      float next = fetch(stat_base(0), i0 * 64);
+      for (uint32_t j = 0; j < steps && ok; ++j, ++n) {
+        const uint32_t i = j % per_head;  // query tile i0 + i
         float* st = stats + (n & 1) * 192;
         if (u < 192) st[u] = next;
         if (!(ok = soft_sync(xbar, xphase, abort_flag))) break;
-        if (i + 1 < steps) next = fetch(sbase, (i0 + i + 1) * 64);
+        if (j + 1 < steps) next = fetch(stat_base(j + 1), (i0 + (j + 1) % per_head) * 64);
         if (!(ok = wait_or_abort(s_full + (n & 1), (n >> 1) & 1, abort_flag))) break;
         tc::tc_fence_after();
         uint32_t sv[32], pv[32];
@@ -1135,7 +1164,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         __syncwarp();
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);  // dV
-        store_box(&p.out, stg, o, static_cast<int>(2 * p.model_dim + it.h * DH + 32 * grp), row,
+        store_box(&p.out, stg, o, static_cast<int>(p.vcol + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
         if (lane == 0) {
           tc::bulk_commit();
@@ -1145,7 +1174,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(w[e]);  // dK
         if (p.rope && kv < seq) inverse_rope(o, p.rope + static_cast<uint64_t>(kv) * (DH / 2) + grp * 16);
-        store_box(&p.out, stg, o, static_cast<int>(p.model_dim + it.h * DH + 32 * grp), row,
+        store_box(&p.out, stg, o, static_cast<int>(p.kcol + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
         if (lane == 0) tc::bulk_commit();
       }
@@ -1211,12 +1240,18 @@ cudaError_t launch_attn(K kernel, uint32_t smem, const AttnParams& p, int device
   return launch(kernel, dim3(grid), dim3(kThreads), smem, stream, p);
 }
 
-void base_params(AttnParams& p, uint64_t batch, uint64_t seq, uint64_t heads, uint64_t head_dim) {
+void base_params(AttnParams& p, uint64_t batch, uint64_t seq, uint64_t heads, uint64_t head_dim,
+                 uint64_t kv_heads) {
   memset(&p, 0, sizeof(p));
   p.heads = static_cast<uint32_t>(heads);
   p.seq = static_cast<uint32_t>(seq);
   p.model_dim = static_cast<uint32_t>(heads * head_dim);
   p.bh = static_cast<uint32_t>(batch * heads);
+  p.kv_heads = static_cast<uint32_t>(kv_heads);
+  p.kv_bh = static_cast<uint32_t>(batch * kv_heads);
+  p.group = static_cast<uint32_t>(heads / kv_heads);
+  p.kcol = p.model_dim;
+  p.vcol = static_cast<uint32_t>((heads + kv_heads) * head_dim);
   p.ld_o = heads * head_dim;
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)));
   p.scale_log2 = p.scale * kLog2e;
@@ -1230,12 +1265,14 @@ bool attention_supported(uint64_t head_dim) { return head_dim == 32 || head_dim 
 
 cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_max, float* row_inv,
                                      uint64_t batch, uint64_t seq, uint64_t heads,
-                                     uint64_t head_dim, int device, cudaStream_t stream) {
+                                     uint64_t head_dim, int device, cudaStream_t stream,
+                                     uint64_t kv_heads) {
+  if (kv_heads == 0) kv_heads = heads;
   AttnParams p;
-  base_params(p, batch, seq, heads, head_dim);
-  const uint64_t d = heads * head_dim;
-  if (!make_map(&p.qk128, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 128, false) ||
-      !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true))
+  base_params(p, batch, seq, heads, head_dim, kv_heads);
+  const uint64_t w = (heads + 2 * kv_heads) * head_dim;  // packed q | k | v row
+  if (!make_map(&p.qk128, qkv, w, seq, batch, 1, w, seq * w, 0, 128, false) ||
+      !make_map(&p.qkv_mn, qkv, w, seq, batch, 1, w, seq * w, 0, 32, true))
     return cudaErrorInvalidValue;
   p.o_out = ctx;
   p.row_max = row_max;
@@ -1253,17 +1290,19 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
                                       uint64_t head_dim, int device, cudaStream_t stream,
                                       const float* rope_table, cudaStream_t key_stream,
-                                      cudaEvent_t fork, cudaEvent_t join) {
+                                      cudaEvent_t fork, cudaEvent_t join, uint64_t kv_heads) {
+  if (kv_heads == 0) kv_heads = heads;
   AttnParams p;
-  base_params(p, batch, seq, heads, head_dim);
+  base_params(p, batch, seq, heads, head_dim, kv_heads);
   const uint64_t d = heads * head_dim;
-  if (!make_map(&p.qk128, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 128, false) ||
-      !make_map(&p.qk64, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 64, false) ||
-      !make_map(&p.qkv_mn, qkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, true) ||
+  const uint64_t w = (heads + 2 * kv_heads) * head_dim;  // packed q | k | v row
+  if (!make_map(&p.qk128, qkv, w, seq, batch, 1, w, seq * w, 0, 128, false) ||
+      !make_map(&p.qk64, qkv, w, seq, batch, 1, w, seq * w, 0, 64, false) ||
+      !make_map(&p.qkv_mn, qkv, w, seq, batch, 1, w, seq * w, 0, 32, true) ||
       !make_map(&p.do128, dctx, d, seq, batch, 1, d, seq * d, 0, 128, false) ||
       !make_map(&p.do64, dctx, d, seq, batch, 1, d, seq * d, 0, 64, false) ||
       !make_map(&p.do_mn, dctx, d, seq, batch, 1, d, seq * d, 0, 32, true) ||
-      !make_map(&p.out, dqkv, 3 * d, seq, batch, 1, 3 * d, seq * 3 * d, 0, 32, false))
+      !make_map(&p.out, dqkv, w, seq, batch, 1, w, seq * w, 0, 32, false))
     return cudaErrorInvalidValue;
   p.o = ctx;
   p.d_o = dctx;
@@ -1294,6 +1333,7 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
           ? launch_attn(attn_bwd_q_kernel<64>, BwdQ<64>::kSmem, p, device, stream, q64)
           : launch_attn(attn_bwd_q_kernel<32>, BwdQ<32>::kSmem, p, device, stream, q32);
   if (e != cudaSuccess) return e;
+  p.total = p.tiles * p.kv_bh;  // key-side items: one per key / value head
   e = head_dim == 64 ? launch_attn(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, p, device, ks, k64)
                      : launch_attn(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, p, device, ks, k32);
   if (e != cudaSuccess || ks == stream) return e;
@@ -1303,11 +1343,15 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
 
 namespace {
 SparCudaStatus attention_validate(const float* const* ptrs, int count, uint64_t batch,
-                                  uint64_t seq, uint64_t heads, uint64_t head_dim) {
+                                  uint64_t seq, uint64_t heads, uint64_t head_dim,
+                                  uint64_t kv_heads) {
   for (int i = 0; i < count; ++i)
     if (!ptrs[i] || !aligned16(ptrs[i])) return invalid();
   if (batch == 0 || seq == 0 || heads == 0 || !attention_supported(head_dim)) return invalid();
-  if (batch * heads > (1ull << 31) || seq > (1ull << 31) || batch * seq * 3 * heads * head_dim >= (1ull << 40))
+  // repeat_kv_heads' requirement (src/nn/attention.cpp:26-75): kv heads divide the query heads.
+  if (kv_heads == 0 || kv_heads > heads || heads % kv_heads != 0) return invalid();
+  if (batch * heads > (1ull << 31) || seq > (1ull << 31) ||
+      batch * seq * (heads + 2 * kv_heads) * head_dim >= (1ull << 40))
     return invalid();
   return ok();
 }
@@ -1317,17 +1361,45 @@ SparCudaStatus attention_validate(const float* const* ptrs, int count, uint64_t 
 
 using namespace spar_b200;
 
-extern "C" SparCudaStatus spar_b200_attention_forward(const float* qkv, float* ctx, float* row_max,
-                                                      float* row_inv, uint64_t batch, uint64_t seq,
-                                                      uint64_t heads, uint64_t head_dim, int device,
-                                                      void* stream) {
+extern "C" SparCudaStatus spar_b200_attention_forward_gqa(const float* qkv, float* ctx,
+                                                          float* row_max, float* row_inv,
+                                                          uint64_t batch, uint64_t seq,
+                                                          uint64_t heads, uint64_t kv_heads,
+                                                          uint64_t head_dim, int device,
+                                                          void* stream) {
   const float* ptrs[4] = {qkv, ctx, row_max, row_inv};
-  const SparCudaStatus v = attention_validate(ptrs, 4, batch, seq, heads, head_dim);
+  const SparCudaStatus v = attention_validate(ptrs, 4, batch, seq, heads, head_dim, kv_heads);
   if (v.code) return v;
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   const cudaError_t e = attention_forward_launch(qkv, ctx, row_max, row_inv, batch, seq, heads,
-                                                 head_dim, device, static_cast<cudaStream_t>(stream));
+                                                 head_dim, device, static_cast<cudaStream_t>(stream),
+                                                 kv_heads);
+  return e == cudaSuccess ? ok() : runtime(e);
+}
+
+extern "C" SparCudaStatus spar_b200_attention_forward(const float* qkv, float* ctx, float* row_max,
+                                                      float* row_inv, uint64_t batch, uint64_t seq,
+                                                      uint64_t heads, uint64_t head_dim, int device,
+                                                      void* stream) {
+  return spar_b200_attention_forward_gqa(qkv, ctx, row_max, row_inv, batch, seq, heads, heads,
+                                         head_dim, device, stream);
+}
+
+extern "C" SparCudaStatus spar_b200_attention_backward_gqa(
+    const float* qkv, const float* ctx, const float* dctx, const float* row_max,
+    const float* row_inv, float* delta, float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
+    uint64_t kv_heads, uint64_t head_dim, const float* rope_table, int device, void* stream) {
+  const float* ptrs[7] = {qkv, ctx, dctx, row_max, row_inv, delta, dqkv};
+  const SparCudaStatus v = attention_validate(ptrs, 7, batch, seq, heads, head_dim, kv_heads);
+  if (v.code) return v;
+  if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7)) return invalid();
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  const cudaError_t e = attention_backward_launch(qkv, ctx, dctx, row_max, row_inv, delta, dqkv,
+                                                  batch, seq, heads, head_dim, device,
+                                                  static_cast<cudaStream_t>(stream), rope_table,
+                                                  nullptr, nullptr, nullptr, kv_heads);
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
@@ -1338,16 +1410,8 @@ extern "C" SparCudaStatus spar_b200_attention_backward(const float* qkv, const f
                                                        uint64_t heads, uint64_t head_dim,
                                                        const float* rope_table, int device,
                                                        void* stream) {
-  const float* ptrs[7] = {qkv, ctx, dctx, row_max, row_inv, delta, dqkv};
-  const SparCudaStatus v = attention_validate(ptrs, 7, batch, seq, heads, head_dim);
-  if (v.code) return v;
-  if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7)) return invalid();
-  DeviceScope scope(device);
-  if (scope.error() != cudaSuccess) return runtime(scope.error());
-  const cudaError_t e = attention_backward_launch(qkv, ctx, dctx, row_max, row_inv, delta, dqkv,
-                                                  batch, seq, heads, head_dim, device,
-                                                  static_cast<cudaStream_t>(stream), rope_table);
-  return e == cudaSuccess ? ok() : runtime(e);
+  return spar_b200_attention_backward_gqa(qkv, ctx, dctx, row_max, row_inv, delta, dqkv, batch,
+                                          seq, heads, heads, head_dim, rope_table, device, stream);
 }
 
 extern "C" int spar_b200_attention_error(int device, int clear) {

@@ -22,7 +22,8 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows
 bool attention_supported(uint64_t head_dim);
 cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_max, float* row_inv,
                                      uint64_t batch, uint64_t seq, uint64_t heads,
-                                     uint64_t head_dim, int device, cudaStream_t stream);
+                                     uint64_t head_dim, int device, cudaStream_t stream,
+                                     uint64_t kv_heads = 0);  // 0: heads (no grouping)
 // dqkv (every column of the rows < seq written) from dctx; delta [batch * heads * seq] scratch.
 cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const float* dctx,
                                       const float* row_max, const float* row_inv, float* delta,
@@ -30,7 +31,7 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       uint64_t head_dim, int device, cudaStream_t stream,
                                       const float* rope_table = nullptr,
                                       cudaStream_t key_stream = nullptr, cudaEvent_t fork = nullptr,
-                                      cudaEvent_t join = nullptr);
+                                      cudaEvent_t join = nullptr, uint64_t kv_heads = 0);
 
 // Spar's stable sigmoid (src/ops/unary.cpp:55-61 / cuda_kernels.cu:105-111), in fp32.
 __device__ __forceinline__ float stable_sigmoid(float v) {

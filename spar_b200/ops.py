@@ -186,32 +186,37 @@ def causal_softmax_backward(dp, p, scale: float, zero_fill_block: int = 0, out=N
 
 
 # ------------------------------------------------------------------------------- attention
-def attention_forward(qkv, heads: int):
-    """Fused causal attention over the packed projection buffer qkv [batch, seq, 3*d].
+def attention_forward(qkv, heads: int, kv_heads: int | None = None):
+    """Fused causal attention over the packed projection buffer qkv [batch, seq, (H + 2 KVH) dh]
+    (KVH = kv_heads, default H: grouped-query attention when smaller).
 
-    Returns (ctx [batch, seq, d], row_max [batch, heads, seq], row_inv [batch, heads, seq])."""
+    Returns (ctx [batch, seq, H dh], row_max [batch, heads, seq], row_inv [batch, heads, seq])."""
     _f32(qkv, "qkv")
-    batch, seq, d3 = qkv.shape
-    d = d3 // 3
-    ctx = torch.empty(batch, seq, d, device=qkv.device, dtype=torch.float32)
+    kvh = heads if kv_heads is None else kv_heads
+    batch, seq, width = qkv.shape
+    dh = width // (heads + 2 * kvh)
+    ctx = torch.empty(batch, seq, heads * dh, device=qkv.device, dtype=torch.float32)
     row_max = torch.empty(batch, heads, seq, device=qkv.device, dtype=torch.float32)
     row_inv = torch.empty_like(row_max)
-    call("spar_b200_attention_forward", qkv.data_ptr(), ctx.data_ptr(), row_max.data_ptr(),
-         row_inv.data_ptr(), batch, seq, heads, d // heads, _dev(qkv), _stream(qkv))
+    call("spar_b200_attention_forward_gqa", qkv.data_ptr(), ctx.data_ptr(), row_max.data_ptr(),
+         row_inv.data_ptr(), batch, seq, heads, kvh, dh, _dev(qkv), _stream(qkv))
     return ctx, row_max, row_inv
 
 
-def attention_backward(dctx, qkv, ctx, row_max, row_inv, heads: int, rope_table=None):
-    """dqkv [batch, seq, 3*d] of the fused causal attention (q, k thirds rotated back by the
-    RoPE table when one is given)."""
-    batch, seq, d3 = qkv.shape
-    d = d3 // 3
+def attention_backward(dctx, qkv, ctx, row_max, row_inv, heads: int, rope_table=None,
+                       kv_heads: int | None = None):
+    """dqkv (the layout of qkv) of the fused causal attention (q, k parts rotated back by the RoPE
+    table when one is given; dK / dV summed over each key/value head's query group)."""
+    kvh = heads if kv_heads is None else kv_heads
+    batch, seq, width = qkv.shape
+    dh = width // (heads + 2 * kvh)
     dqkv = torch.empty_like(qkv)
     delta = torch.empty(batch, heads, seq, device=qkv.device, dtype=torch.float32)
-    call("spar_b200_attention_backward", _f32(qkv, "qkv").data_ptr(), _f32(ctx, "ctx").data_ptr(),
-         _f32(dctx, "dctx").data_ptr(), _f32(row_max, "row_max").data_ptr(),
-         _f32(row_inv, "row_inv").data_ptr(), delta.data_ptr(), dqkv.data_ptr(), batch, seq, heads,
-         d // heads, _ptr(rope_table), _dev(qkv), _stream(qkv))
+    call("spar_b200_attention_backward_gqa", _f32(qkv, "qkv").data_ptr(),
+         _f32(ctx, "ctx").data_ptr(), _f32(dctx, "dctx").data_ptr(),
+         _f32(row_max, "row_max").data_ptr(), _f32(row_inv, "row_inv").data_ptr(),
+         delta.data_ptr(), dqkv.data_ptr(), batch, seq, heads, kvh, dh, _ptr(rope_table),
+         _dev(qkv), _stream(qkv))
     return dqkv
 
 

@@ -70,6 +70,14 @@ def main(only=()):
     h, dgt, dvl = R.swiglu(gt, vl, dh)
     save("swiglu", gate=gt, value=vl, dh=dh, h=h, dgate=dgt, dvalue=dvl)
 
+    # Grouped-query causal attention (4 query heads sharing 2 key/value heads), head_dim 32
+    qa = normal(36, (1, 4, 40, 32))
+    ka = normal(37, (1, 2, 40, 32))
+    va = normal(38, (1, 2, 40, 32))
+    doa = normal(39, (1, 4, 40, 32))
+    oa, dqa, dka, dva = R.attention(qa, ka, va, doa)
+    save("attention_gqa", q=qa, k=ka, v=va, d_out=doa, out=oa, dq=dqa, dk=dka, dv=dva)
+
     # GELU through Spar's sigmoid, incl. large |x| and zero
     x = np.concatenate([normal(5, (500,), 3.0), np.array([0.0, -30.0, 30.0, 1e-6, -1e-6, 15.0],
                                                           np.float32)])

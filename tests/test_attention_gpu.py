@@ -179,3 +179,58 @@ def test_attention_c5_shape_repeated_without_timeouts(cuda):
     torch.cuda.synchronize()
     assert ops.attention_error(0) == 0
     assert torch.isfinite(ctx).all() and torch.isfinite(dqkv).all()
+
+
+@pytest.mark.parametrize("b,t,h,kvh,dh", [(2, 384, 8, 2, 64), (1, 200, 4, 1, 32), (3, 256, 6, 3, 64),
+                                          (2, 1024, 16, 4, 64)])
+def test_gqa_matches_oracle(cuda, b, t, h, kvh, dh):
+    """Grouped-query attention: query head i reads key/value head i // (h / kvh); the backward's
+    dK / dV are summed over each group. Against the float64 oracle (repeat_kv_heads + the MHA
+    chain) at the TF32 tolerance of the other attention tests."""
+    import torch
+    from spar_b200 import ops
+
+    r = np.random.default_rng(b * t + h * 10 + kvh)
+    w = (h + 2 * kvh) * dh
+    qkv = r.standard_normal((b, t, w)).astype(np.float32)
+    do = r.standard_normal((b, t, h * dh)).astype(np.float32)
+    qt = torch.from_numpy(rn_tf32(qkv)).to(cuda)
+    ctx, mx, inv = ops.attention_forward(qt, h, kv_heads=kvh)
+    dqkv = ops.attention_backward(torch.from_numpy(rn_tf32(do)).to(cuda), qt, ctx, mx, inv, h,
+                                  kv_heads=kvh)
+    torch.cuda.synchronize()
+    assert ops.attention_error(0) == 0
+    o_ctx, o_d = O.attention_forward_backward(qkv, h, do, kv_heads=kvh)
+    assert rel_l2(ctx.cpu().numpy(), o_ctx) <= 2e-3
+    got = dqkv.cpu().numpy()
+    d, dkv = h * dh, kvh * dh
+    for lo, hi in ((0, d), (d, d + dkv), (d + dkv, w)):
+        assert rel_l2(got[..., lo:hi], o_d[..., lo:hi]) <= 2e-3, (lo, hi)
+
+
+def test_gqa_with_one_group_is_the_mha_call(cuda):
+    """kv_heads == heads through the grouped entry points is bitwise the plain entry points."""
+    import torch
+    from spar_b200 import _lib, ops
+
+    r = np.random.default_rng(5)
+    b, t, h, dh = 2, 256, 4, 64
+    qkv = torch.from_numpy(r.standard_normal((b, t, 3 * h * dh)).astype(np.float32)).to(cuda)
+    do = torch.from_numpy(r.standard_normal((b, t, h * dh)).astype(np.float32)).to(cuda)
+    ctx, mx, inv = ops.attention_forward(qkv, h, kv_heads=h)
+    d1 = ops.attention_backward(do, qkv, ctx, mx, inv, h, kv_heads=h)
+    lib = _lib.load()
+    ctx2 = torch.empty_like(ctx)
+    mx2, inv2 = torch.empty_like(mx), torch.empty_like(inv)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check("spar_b200_attention_forward",
+               lib.spar_b200_attention_forward(qkv.data_ptr(), ctx2.data_ptr(), mx2.data_ptr(),
+                                               inv2.data_ptr(), b, t, h, dh, 0, stream))
+    d2 = torch.empty_like(qkv)
+    delta = torch.empty_like(mx)
+    _lib.check("spar_b200_attention_backward",
+               lib.spar_b200_attention_backward(qkv.data_ptr(), ctx2.data_ptr(), do.data_ptr(),
+                                                mx2.data_ptr(), inv2.data_ptr(), delta.data_ptr(),
+                                                d2.data_ptr(), b, t, h, dh, None, 0, stream))
+    torch.cuda.synchronize()
+    assert torch.equal(ctx, ctx2) and torch.equal(d1, d2)

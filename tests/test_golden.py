@@ -53,6 +53,23 @@ def test_oracle_swiglu_matches_reference():
     assert rel_err(f["dgate"], dg) <= TOL and rel_err(f["dvalue"], dv) <= TOL
 
 
+def _packed_gqa(f):
+    """The fixture's head-major q / k / v as one packed [B, T, (H + 2 KVH) dh] projection."""
+    pack = lambda x: x.transpose(0, 2, 1, 3).reshape(x.shape[0], x.shape[2], -1)
+    return np.concatenate([pack(f["q"]), pack(f["k"]), pack(f["v"])], axis=-1), pack(f["d_out"])
+
+
+def test_oracle_gqa_attention_matches_reference():
+    f = load("attention_gqa")
+    qkv, do = _packed_gqa(f)
+    heads, kvh = f["q"].shape[1], f["k"].shape[1]
+    ctx, dqkv = O.attention_forward_backward(qkv, heads, do, kv_heads=kvh)
+    pack = lambda x: x.transpose(0, 2, 1, 3).reshape(x.shape[0], x.shape[2], -1)
+    want = np.concatenate([pack(f["dq"]), pack(f["dk"]), pack(f["dv"])], axis=-1)
+    assert rel_err(f["out"].transpose(0, 2, 1, 3).reshape(ctx.shape), ctx) <= TOL
+    assert rel_err(want, dqkv) <= TOL
+
+
 def test_oracle_causal_softmax_matches_reference():
     f = load("causal_softmax")
     scale = float(f["scale"])
@@ -231,6 +248,27 @@ def test_cuda_rmsnorm_swiglu_match_reference_fixtures(cuda):
     assert rel_err(h.cpu().numpy().ravel(), g["h"]) <= TOL
     assert rel_err(dg.cpu().numpy().ravel(), g["dgate"]) <= TOL
     assert rel_err(dv.cpu().numpy().ravel(), g["dvalue"]) <= TOL
+
+
+@pytest.mark.gpu
+def test_cuda_gqa_attention_matches_reference_fixture(cuda):
+    """The fused grouped-query attention against the reference's own sdpa + repeat_kv_heads
+    (TF32 products: relative L2 <= 2e-3, the attention bar)."""
+    import torch
+    from spar_b200 import ops
+
+    f = load("attention_gqa")
+    qkv, do = _packed_gqa(f)
+    heads, kvh = f["q"].shape[1], f["k"].shape[1]
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(cuda)
+    ctx, mx, inv = ops.attention_forward(T(qkv), heads, kv_heads=kvh)
+    dqkv = ops.attention_backward(T(do), T(qkv), ctx, mx, inv, heads, kv_heads=kvh)
+    torch.cuda.synchronize()
+    assert ops.attention_error(0) == 0
+    pack = lambda x: x.transpose(0, 2, 1, 3).reshape(x.shape[0], x.shape[2], -1)
+    assert rel_l2(ctx.cpu().numpy(), pack(f["out"])) <= 2e-3
+    want = np.concatenate([pack(f["dq"]), pack(f["dk"]), pack(f["dv"])], axis=-1)
+    assert rel_l2(dqkv.cpu().numpy(), want) <= 2e-3
 
 
 @pytest.mark.gpu
