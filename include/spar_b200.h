@@ -335,15 +335,27 @@ int spar_b200_attention_error(int device, int clear);
 /* (src/autograd/autograd.cpp:201-265), training::clip_grad_norm (gradients.cpp:176-190) and    */
 /* optim::AdamW::step (src/optim/adamw.cpp:83-170), scheduled on one CUDA stream.               */
 /* Parameters are exposed under Spar's named_parameters names (src/nn/parameters.cpp:51-132).   */
+/* family (the fields after max_grad_norm; a zero-initialised tail is family 0):                */
+/*   SPAR_B200_FAMILY_LN_GELU (0): the benchmark decoder above.                                  */
+/*   SPAR_B200_FAMILY_SPAR (1): Spar's own nn::DecoderLM (src/nn/decoder.cpp, transformer.cpp:   */
+/*   53-69, attention.cpp:168-225, mlp.cpp:33-46): RMSNorm pre-norms and final norm, no biases,  */
+/*   num_kv_heads key/value heads (grouped-query attention), optional RMSNorm of each q / k head */
+/*   before RoPE (qk_norm, qk_norm_epsilon), SwiGLU MLP (gate, up, down), tied logits. Names as */
+/*   nn::named_parameters (src/nn/parameters.cpp:51-132); TF32 only, head_dim 32 or 64.         */
+enum { SPAR_B200_FAMILY_LN_GELU = 0, SPAR_B200_FAMILY_SPAR = 1 };
 struct SparB200LMConfig {
   uint64_t vocab_size, model_dim, hidden_dim, num_layers, num_heads, sequence_length;
   uint64_t micro_batch; /* sequences per micro-step */
-  double norm_epsilon;  /* LayerNorm epsilon (Spar's norm default 1e-5) */
+  double norm_epsilon;  /* LayerNorm / RMSNorm epsilon (Spar's norm default 1e-5) */
   double rope_theta;    /* 10000 in Spar */
   int use_rope;
   int precision; /* SparB200Precision of every GEMM */
   double beta1, beta2, adam_epsilon, weight_decay;
   double max_grad_norm; /* < 0: no clipping */
+  int family;           /* SPAR_B200_FAMILY_* */
+  int qk_norm;          /* family 1 */
+  uint64_t num_kv_heads; /* family 1; 0 = num_heads */
+  double qk_norm_epsilon; /* family 1 (Spar's default 1e-6) */
 };
 struct SparCudaStatus spar_b200_lm_create(const struct SparB200LMConfig* config, int device,
                                           void** handle);

@@ -35,6 +35,11 @@ def load():
             "ref_rmsnorm": [F, F, F, c_int64, c_int64, c_double, F, F, F],
             "ref_swiglu": [F, F, F, c_int64, F, F, F],
             "ref_attention": [F, F, F, F] + [c_int64] * 5 + [F, F, F, F],
+            "ref_spar_param_info": [c_int64] * 8 + [c_char_p, c_int64, POINTER(c_int64)],
+            "ref_spar_lm_step": [c_int64] * 10 + [c_double, c_double, POINTER(F), I32, c_double,
+                                                  c_double, c_double, c_double, c_double,
+                                                  c_double, F, POINTER(c_double), POINTER(F),
+                                                  POINTER(F)],
             "ref_causal_softmax": [F, F, c_int64, c_int64, c_double, F, F],
             "ref_cross_entropy": [F, I32, c_int64, c_int64, c_int64, F, F],
             "ref_matmul": [F, F, F, c_int64, c_int64, c_int64, F, F, F],
@@ -177,6 +182,44 @@ def lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
                               arr(ps), ids.ctypes.data_as(I32), lr, opt["beta1"], opt["beta2"],
                               opt["eps"], opt["weight_decay"], opt["max_grad_norm"], _p(loss),
                               ctypes.byref(norm), arr(gs), arr(outs)))
+    return float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs))
+
+
+def _spar_dims(cfg):
+    return (cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"],
+            cfg.get("kv_heads", cfg["heads"]), int(cfg.get("qk_norm", 0)))
+
+
+def spar_param_info(cfg: dict):
+    """[(name, numel)] of nn::DecoderLM's named_parameters for cfg (the reference's own order)."""
+    lib = load()
+    n = c_int64(0)
+    buf = ctypes.create_string_buffer(256)
+    _check(lib.ref_spar_param_info(*_spar_dims(cfg), -1, buf, 256, ctypes.byref(n)))
+    out = []
+    for i in range(n.value):
+        k = c_int64(0)
+        _check(lib.ref_spar_param_info(*_spar_dims(cfg), i, buf, 256, ctypes.byref(k)))
+        out.append((buf.value.decode(), k.value))
+    return out
+
+
+def spar_lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
+    """One training step of the reference's nn::DecoderLM; ids [micro, batch, t].
+    Returns (loss, norm, grads, new) keyed by the reference's parameter names."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    micro, batch, t = ids.shape
+    ps = [_f(params[n]) for n in names]
+    gs = [np.empty_like(p) for p in ps]
+    outs = [np.empty_like(p) for p in ps]
+    arr = lambda lst: (F * len(lst))(*[_p(a) for a in lst])
+    loss = np.zeros(1, np.float32)
+    norm = c_double(0.0)
+    _check(load().ref_spar_lm_step(*_spar_dims(cfg), batch, t, micro, cfg.get("eps", 1e-5),
+                                   cfg.get("rope_theta", 1e4), arr(ps), ids.ctypes.data_as(I32),
+                                   lr, opt["beta1"], opt["beta2"], opt["eps"],
+                                   opt["weight_decay"], opt["max_grad_norm"], _p(loss),
+                                   ctypes.byref(norm), arr(gs), arr(outs)))
     return float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs))
 
 

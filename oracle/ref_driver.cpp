@@ -10,6 +10,7 @@
 #include "spar.hpp"
 
 #include <chrono>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <utility>
@@ -327,6 +328,72 @@ int ref_lm_step(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t hea
     for (int64_t mi = 0; mi < micro; ++mi) {
       Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t});
       Tensor loss = loss::language_model_cross_entropy(model.logits(tid), tid);
+      total += std::as_const(loss).span<float>()[0];
+      Tensor scaled = multiply_scalar(loss, 1.0 / static_cast<double>(micro));
+      scaled.backward();
+    }
+    *loss_out = static_cast<float>(total / static_cast<double>(micro));
+    for (std::size_t i = 0; i < ps.size(); ++i) to_host(ps[i].grad(), grads[i]);
+    *norm_out = training::clip_grad_norm(ps, max_norm).total_norm;
+    optim::AdamW opt{ps, lr, beta1, beta2, adam_eps, wd};
+    opt.step();
+    for (std::size_t i = 0; i < ps.size(); ++i) to_host(ps[i].tensor(), out_params[i]);
+  });
+}
+
+// Spar's own decoder (nn::DecoderLM, src/nn/decoder.cpp: RMSNorm, RoPE self-attention with
+// num_kv_heads key/value heads and optional q/k RMSNorm, SwiGLU MLP, no biases, tied logits).
+nn::DecoderConfig spar_config(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t heads,
+                              int64_t kv_heads, int64_t qk_norm, double eps, double theta) {
+  nn::DecoderConfig c;
+  c.vocab_size = static_cast<std::size_t>(vocab);
+  c.model_dim = static_cast<std::size_t>(d);
+  c.hidden_dim = static_cast<std::size_t>(f);
+  c.num_layers = static_cast<std::size_t>(layers);
+  c.num_query_heads = static_cast<std::size_t>(heads);
+  c.num_kv_heads = static_cast<std::size_t>(kv_heads);
+  c.norm_epsilon = eps;
+  c.rope_theta = theta;
+  c.qk_norm = qk_norm != 0;
+  return c;
+}
+
+// Name and element count of named parameter `index` of that decoder (named_parameters order).
+int ref_spar_param_info(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t heads,
+                        int64_t kv_heads, int64_t qk_norm, int64_t index, char* name,
+                        int64_t capacity, int64_t* numel) {
+  return guarded([&] {
+    Random rng{1};
+    nn::DecoderLM model{spar_config(vocab, d, f, layers, heads, kv_heads, qk_norm, 1e-5, 1e4), rng};
+    const auto named = nn::named_parameters(model);
+    if (index < 0) {
+      *numel = static_cast<int64_t>(named.size());
+      return;
+    }
+    const auto& np = named.at(static_cast<std::size_t>(index));
+    std::snprintf(name, static_cast<std::size_t>(capacity), "%s", np.name.c_str());
+    *numel = static_cast<int64_t>(np.parameter.tensor().numel());
+  });
+}
+
+// One optimiser step of nn::DecoderLM: as ref_lm_step (micro-batches, mean loss, backward,
+// clip_grad_norm, AdamW), parameters in named_parameters order.
+int ref_spar_lm_step(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t heads,
+                     int64_t kv_heads, int64_t qk_norm, int64_t batch, int64_t t, int64_t micro,
+                     double eps, double theta, const float* const* params, const int32_t* ids,
+                     double lr, double beta1, double beta2, double adam_eps, double wd,
+                     double max_norm, float* loss_out, double* norm_out, float** grads,
+                     float** out_params) {
+  return guarded([&] {
+    Random rng{1};
+    nn::DecoderLM model{spar_config(vocab, d, f, layers, heads, kv_heads, qk_norm, eps, theta), rng};
+    std::vector<nn::Parameter> ps;
+    for (auto& np : nn::named_parameters(model)) ps.push_back(np.parameter);
+    for (std::size_t i = 0; i < ps.size(); ++i) load(ps[i], params[i]);
+    double total = 0.0;
+    for (int64_t mi = 0; mi < micro; ++mi) {
+      Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t});
+      Tensor loss = loss::language_model_cross_entropy(model.forward(tid), tid);
       total += std::as_const(loss).span<float>()[0];
       Tensor scaled = multiply_scalar(loss, 1.0 / static_cast<double>(micro));
       scaled.backward();

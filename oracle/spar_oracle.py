@@ -403,6 +403,46 @@ def init_parameters(cfg, seed, std=0.02):
     return params
 
 
+def spar_family_shapes(cfg):
+    """Shapes of nn::DecoderLM's named parameters (src/nn/parameters.cpp:61-108, Linear weights
+    [in, out], linear.cpp:33-35) in order, for cfg {vocab, dim, hidden, layers, heads, kv_heads,
+    qk_norm}."""
+    v, d, f, n_l, h = cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"]
+    kvh = cfg.get("kv_heads") or h
+    dh = d // h
+    shapes = {"token_embedding.weight": (v, d)}
+    for i in range(n_l):
+        p = f"blocks.{i}."
+        shapes[p + "attention_norm.weight"] = (d,)
+        shapes[p + "attention.q_proj.weight"] = (d, h * dh)
+        shapes[p + "attention.k_proj.weight"] = (d, kvh * dh)
+        shapes[p + "attention.v_proj.weight"] = (d, kvh * dh)
+        shapes[p + "attention.out_proj.weight"] = (d, d)
+        if cfg.get("qk_norm"):
+            shapes[p + "attention.q_norm.weight"] = (dh,)
+            shapes[p + "attention.k_norm.weight"] = (dh,)
+        shapes[p + "mlp_norm.weight"] = (d,)
+        shapes[p + "mlp.gate_proj.weight"] = (d, f)
+        shapes[p + "mlp.up_proj.weight"] = (d, f)
+        shapes[p + "mlp.down_proj.weight"] = (f, d)
+    shapes["final_norm.weight"] = (d,)
+    return shapes
+
+
+def spar_family_parameters(cfg, seed, std=0.02, norm_std=0.1):
+    """Test parameters for nn::DecoderLM: matrices N(0, std), norm weights 1 + N(0, norm_std),
+    drawn in named-parameter order from one Random(seed) stream."""
+    rng = Random(seed)
+    out = {}
+    for name, shape in spar_family_shapes(cfg).items():
+        n = int(np.prod(shape))
+        if len(shape) == 2:
+            out[name] = rng.normal(n, std).reshape(shape)
+        else:
+            out[name] = (1.0 + rng.normal(n, norm_std)).astype(np.float32).reshape(shape)
+    return out
+
+
 def lm_forward_backward(params, ids, cfg, dtype=np.float64):
     """One forward + backward of the pre-LN decoder (DecoderLM::forward, src/nn/decoder.cpp:
     73-90; TransformerBlock::forward, transformer.cpp:53-69; SelfAttention::forward,

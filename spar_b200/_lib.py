@@ -47,6 +47,8 @@ class SparB200LMConfig(ctypes.Structure):
         ("use_rope", c_int), ("precision", c_int),
         ("beta1", c_double), ("beta2", c_double), ("adam_epsilon", c_double),
         ("weight_decay", c_double), ("max_grad_norm", c_double),
+        ("family", c_int), ("qk_norm", c_int), ("num_kv_heads", c_uint64),
+        ("qk_norm_epsilon", c_double),
     ]
 
 

@@ -307,6 +307,7 @@ extern "C" SparCudaStatus spar_b200_gelu_backward(float* dx, const float* dy, co
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
+namespace spar_b200 {
 namespace {
 // float4 access is possible when cols and every leading dimension are multiples of 4 and every
 // pointer is 16-byte aligned.
@@ -336,6 +337,32 @@ dim3 swiglu_backward_grid(uint64_t rows, uint64_t per_row, int device) {
 }
 }  // namespace
 
+cudaError_t swiglu_forward_launch(float* h, uint64_t ldh, const float* gate, uint64_t ldg,
+                                  const float* value, uint64_t ldv, uint64_t rows, uint64_t cols,
+                                  int device, cudaStream_t s) {
+  const bool vec = swiglu_vec(cols, {ldh, ldg, ldv}, {h, gate, value});
+  const dim3 grid = swiglu_forward_grid(rows, vec ? cols / 4 : cols, device);
+  if (vec) return launch(swiglu_forward_kernel<true>, grid, dim3(256), 0, s, h, ldh, gate, ldg, value, ldv, rows, cols);
+  return launch(swiglu_forward_kernel<false>, grid, dim3(256), 0, s, h, ldh, gate, ldg, value, ldv, rows, cols);
+}
+
+cudaError_t swiglu_backward_launch(float* dgate, uint64_t lddg, float* dvalue, uint64_t lddv,
+                                   const float* dh, uint64_t lddh, const float* gate, uint64_t ldg,
+                                   const float* value, uint64_t ldv, uint64_t rows, uint64_t cols,
+                                   int device, cudaStream_t s) {
+  const bool vec = swiglu_vec(cols, {lddg, lddv, lddh, ldg, ldv}, {dgate, dvalue, dh, gate, value});
+  const dim3 grid = swiglu_backward_grid(rows, vec ? cols / 4 : cols, device);
+  if (vec)
+    return launch(swiglu_backward_kernel<true>, grid, dim3(256), 0, s, dgate, lddg, dvalue, lddv,
+                  dh, lddh, gate, ldg, value, ldv, rows, cols);
+  return launch(swiglu_backward_kernel<false>, grid, dim3(256), 0, s, dgate, lddg, dvalue, lddv,
+                dh, lddh, gate, ldg, value, ldv, rows, cols);
+}
+
+}  // namespace spar_b200
+
+using namespace spar_b200;
+
 extern "C" SparCudaStatus spar_b200_swiglu_forward(float* h, uint64_t ldh, const float* gate,
                                                    uint64_t ldg, const float* value, uint64_t ldv,
                                                    uint64_t rows, uint64_t cols, int device,
@@ -344,12 +371,8 @@ extern "C" SparCudaStatus spar_b200_swiglu_forward(float* h, uint64_t ldh, const
   if (!h || !gate || !value || ldh < cols || ldg < cols || ldv < cols) return invalid();
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
-  const bool vec = swiglu_vec(cols, {ldh, ldg, ldv}, {h, gate, value});
-  const dim3 grid = swiglu_forward_grid(rows, vec ? cols / 4 : cols, device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec) launch(swiglu_forward_kernel<true>, dim3(grid), dim3(256), 0, s, h, ldh, gate, ldg, value, ldv, rows, cols);
-  else launch(swiglu_forward_kernel<false>, dim3(grid), dim3(256), 0, s, h, ldh, gate, ldg, value, ldv, rows, cols);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = swiglu_forward_launch(h, ldh, gate, ldg, value, ldv, rows, cols, device,
+                                              static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
@@ -365,16 +388,9 @@ extern "C" SparCudaStatus spar_b200_swiglu_backward(float* dgate, uint64_t lddg,
     return invalid();
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
-  const bool vec = swiglu_vec(cols, {lddg, lddv, lddh, ldg, ldv}, {dgate, dvalue, dh, gate, value});
-  const dim3 grid = swiglu_backward_grid(rows, vec ? cols / 4 : cols, device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec)
-    launch(swiglu_backward_kernel<true>, dim3(grid), dim3(256), 0, s, dgate, lddg, dvalue, lddv,
-           dh, lddh, gate, ldg, value, ldv, rows, cols);
-  else
-    launch(swiglu_backward_kernel<false>, dim3(grid), dim3(256), 0, s, dgate, lddg, dvalue, lddv,
-           dh, lddh, gate, ldg, value, ldv, rows, cols);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = swiglu_backward_launch(dgate, lddg, dvalue, lddv, dh, lddh, gate, ldg,
+                                               value, ldv, rows, cols, device,
+                                               static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? ok() : runtime(e);
 }
 

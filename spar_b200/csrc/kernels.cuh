@@ -103,6 +103,25 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
                                       const float* rstd, uint64_t rows, uint64_t cols,
                                       int accumulate_params, int accumulate_dx, float* workspace,
                                       int device, cudaStream_t stream, float* dsum = nullptr);
+// RMSNorm (the LayerNorm kernels without centring / bias). Rows of `cols` floats, `group`
+// consecutive rows per `ld` floats (ld 0: cols; group = heads for qk-norm inside a projection).
+// Backward workspace: layernorm_backward_parts(rows) * cols floats.
+cudaError_t rmsnorm_forward_launch(float* y, float* rstd, const float* x, const float* weight,
+                                   uint64_t rows, uint64_t cols, float eps, int device,
+                                   cudaStream_t stream, uint64_t ld = 0, uint32_t group = 1);
+cudaError_t rmsnorm_backward_launch(float* dx, float* dweight, const float* dy, const float* x,
+                                    const float* weight, const float* rstd, uint64_t rows,
+                                    uint64_t cols, int accumulate_params, int accumulate_dx,
+                                    float* workspace, int device, cudaStream_t stream,
+                                    uint64_t ld = 0, uint32_t group = 1);
+// SwiGLU h = silu(gate) * value and its backward over rows x cols with row strides (floats).
+cudaError_t swiglu_forward_launch(float* h, uint64_t ldh, const float* gate, uint64_t ldg,
+                                  const float* value, uint64_t ldv, uint64_t rows, uint64_t cols,
+                                  int device, cudaStream_t stream);
+cudaError_t swiglu_backward_launch(float* dgate, uint64_t lddg, float* dvalue, uint64_t lddv,
+                                   const float* dh, uint64_t lddh, const float* gate, uint64_t ldg,
+                                   const float* value, uint64_t ldv, uint64_t rows, uint64_t cols,
+                                   int device, cudaStream_t stream);
 
 cudaError_t gelu_launch(float* y, const float* dy, const float* x, uint64_t n, int backward,
                         int device, cudaStream_t stream);

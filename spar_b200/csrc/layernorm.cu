@@ -23,6 +23,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace spar_b200 {
 namespace {
@@ -359,7 +360,7 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
 
 cudaError_t rmsnorm_forward_launch(float* y, float* rstd, const float* x, const float* weight,
                                    uint64_t rows, uint64_t cols, float eps, int device,
-                                   cudaStream_t stream, uint64_t ld = 0, uint32_t group = 1) {
+                                   cudaStream_t stream, uint64_t ld, uint32_t group) {
   const RowMap rm{ld ? ld : cols, group};
   const unsigned grid = grid_for(rows, kWarps, sm_count(device) * 8);
   const int c = static_cast<int>(cols);
@@ -382,7 +383,7 @@ cudaError_t rmsnorm_backward_launch(float* dx, float* dweight, const float* dy, 
                                     const float* weight, const float* rstd, uint64_t rows,
                                     uint64_t cols, int accumulate_params, int accumulate_dx,
                                     float* workspace, int device, cudaStream_t stream,
-                                    uint64_t ld = 0, uint32_t group = 1) {
+                                    uint64_t ld, uint32_t group) {
   const RowMap rm{ld ? ld : cols, group};
   const int parts = layernorm_backward_parts(rows, device);
   const uint64_t rows_per_block = (rows + parts - 1) / parts;

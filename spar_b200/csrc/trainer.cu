@@ -19,6 +19,7 @@
 // the named-parameter view below splits them back into Spar's q_proj/k_proj/v_proj tensors.
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <string>
 #include <vector>
@@ -90,6 +91,20 @@ __global__ void add_lanes_kernel(float4* __restrict__ a, const float4* __restric
   }
 }
 
+// dst[r * ld + c] = src[r * ld + c] rounded to nearest TF32 for c < cols (the value part of the
+// projection after the q / k norms: it only feeds tensor-core products).
+__global__ void copy_round_kernel(float* __restrict__ dst, const float* __restrict__ src,
+                                  uint64_t rows, uint64_t cols, uint64_t ld) {
+  pdl_begin();
+  const uint64_t total = rows * cols;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const uint64_t r = i / cols, c = i - r * cols;
+    dst[r * ld + c] = round_tf32(src[r * ld + c]);
+  }
+}
+
 __global__ void fill_kernel(float* dst, uint64_t n, float v) {
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
@@ -106,12 +121,16 @@ struct NamedTensor {
 
 struct LayerOffsets {
   uint64_t ln1_g, ln1_b, wqkv, bqkv, wo, bo, ln2_g, ln2_b, w1, b1, w2, b2, begin, end;
+  uint64_t qn, kn;  // Spar family with qk_norm: q_norm / k_norm weights [head_dim]
 };
 
 struct LayerActs {
   float *x, *mean1, *rstd1, *a1, *qkv, *ctx, *h1, *mean2, *rstd2, *a2, *u, *g;
   float* p;      // attention probabilities [B, H, T, T] (unfused path only)
   float* stats;  // fused attention softmax statistics: row max [B*H*T], 1 / row sum [B*H*T]
+  // Spar family: u = [gate | up] projection [N, 2F], g = swiglu output [N, F]; with qk_norm the
+  // projection before the q / k norms (qkv_raw) and their 1 / rms (qk_rstd [N * (H + KVH)]).
+  float *qkv_raw, *qk_rstd;
 };
 
 }  // namespace
@@ -152,6 +171,54 @@ BucketShard shard_bucket(uint64_t off, uint64_t count, int world, int rank) {
   return b;
 }
 
+// Spar's own decoder (family 1): nn::named_parameters order of DecoderLM (src/nn/parameters.cpp:
+// 61-108): embedding; per block attention_norm, q / k / v / out projections (q_norm, k_norm),
+// mlp_norm, gate / up / down projections; final_norm. q | k | v are stored as one [d, (H + 2 KVH)
+// dh] matrix and gate | up as one [d, 2F] matrix (column views under Spar's names), so each
+// projection is one product.
+void plan_spar_family(const SparB200LMConfig& c, ParamLayout& pl, uint64_t& o,
+                      const std::function<uint64_t(uint64_t)>& take) {
+  const uint64_t V = c.vocab_size, d = c.model_dim, F = c.hidden_dim, L = c.num_layers,
+                 H = c.num_heads, dh = d / H, KVH = c.num_kv_heads ? c.num_kv_heads : H;
+  const uint64_t wq = (H + 2 * KVH) * dh;
+  pl.off_E = take(V * d);
+  pl.named.push_back({"token_embedding.weight", pl.off_E, V, d, d, true});
+  for (uint64_t l = 0; l < L; ++l) {
+    LayerOffsets lo{};
+    lo.begin = o;
+    lo.ln1_g = take(d);
+    lo.wqkv = take(d * wq);
+    lo.wo = take(d * d);
+    if (c.qk_norm) {
+      lo.qn = take(dh);
+      lo.kn = take(dh);
+    }
+    lo.ln2_g = take(d);
+    lo.w1 = take(d * 2 * F);
+    lo.w2 = take(F * d);
+    lo.end = o;
+    pl.lay.push_back(lo);
+    const std::string p = "blocks." + std::to_string(l) + ".";
+    pl.named.push_back({p + "attention_norm.weight", lo.ln1_g, d, 0, 0, false});
+    pl.named.push_back({p + "attention.q_proj.weight", lo.wqkv, d, H * dh, wq, true});
+    pl.named.push_back({p + "attention.k_proj.weight", lo.wqkv + H * dh, d, KVH * dh, wq, true});
+    pl.named.push_back({p + "attention.v_proj.weight", lo.wqkv + (H + KVH) * dh, d, KVH * dh, wq,
+                        true});
+    pl.named.push_back({p + "attention.out_proj.weight", lo.wo, d, d, d, true});
+    if (c.qk_norm) {
+      pl.named.push_back({p + "attention.q_norm.weight", lo.qn, dh, 0, 0, false});
+      pl.named.push_back({p + "attention.k_norm.weight", lo.kn, dh, 0, 0, false});
+    }
+    pl.named.push_back({p + "mlp_norm.weight", lo.ln2_g, d, 0, 0, false});
+    pl.named.push_back({p + "mlp.gate_proj.weight", lo.w1, d, F, 2 * F, true});
+    pl.named.push_back({p + "mlp.up_proj.weight", lo.w1 + F, d, F, 2 * F, true});
+    pl.named.push_back({p + "mlp.down_proj.weight", lo.w2, F, d, d, true});
+  }
+  pl.off_lnf_g = take(d);
+  pl.off_lnf_b = pl.off_lnf_g;  // no bias: the final-norm bucket is [off_lnf_g, flat)
+  pl.named.push_back({"final_norm.weight", pl.off_lnf_g, d, 0, 0, false});
+}
+
 SparCudaStatus plan_params(const SparB200LMConfig& c, ParamLayout& pl) {
   const uint64_t V = c.vocab_size, d = c.model_dim, F = c.hidden_dim, L = c.num_layers,
                  H = c.num_heads, T = c.sequence_length, B = c.micro_batch;
@@ -160,6 +227,7 @@ SparCudaStatus plan_params(const SparB200LMConfig& c, ParamLayout& pl) {
   const uint64_t dh = d / H;
   if (d % 32 != 0 || F % 4 != 0 || dh % 32 != 0 || T % 4 != 0) return invalid();
   if (c.precision != SPAR_B200_TF32 && c.precision != SPAR_B200_TF32X3) return invalid();
+  if (c.family != SPAR_B200_FAMILY_LN_GELU && c.family != SPAR_B200_FAMILY_SPAR) return invalid();
   // ---- parameter arena in Spar's named_parameters order (src/nn/parameters.cpp:51-132)
   uint64_t o = 0;
   auto take = [&](uint64_t n) {
@@ -167,6 +235,17 @@ SparCudaStatus plan_params(const SparB200LMConfig& c, ParamLayout& pl) {
     o = align_up(o + n);
     return at;
   };
+  if (c.family == SPAR_B200_FAMILY_SPAR) {
+    // DecoderLM's checks (src/nn/decoder.cpp:17-49) and this runtime's: TF32 with the fused
+    // attention (head_dim 32 or 64).
+    const uint64_t kvh = c.num_kv_heads ? c.num_kv_heads : H;
+    if (kvh > H || H % kvh != 0 || c.precision != SPAR_B200_TF32 || (dh != 32 && dh != 64) ||
+        (c.qk_norm && !(c.qk_norm_epsilon > 0.0)) || F % 32 != 0)
+      return invalid();
+    plan_spar_family(c, pl, o, take);
+    pl.flat = o;
+    return ok();
+  }
   pl.off_E = take(V * d);
   pl.named.push_back({"token_embedding.weight", pl.off_E, V, d, d, true});
   for (uint64_t l = 0; l < L; ++l) {
@@ -222,6 +301,11 @@ class LMTrainer {
   SparB200LMConfig cfg;
   int device = 0;
   uint64_t V, d, F, L, H, T, B, N, dh, Vp;
+  // Model family (SPAR_B200_FAMILY_*); Spar family: KVH key/value heads, qkv rows of Wq =
+  // (H + 2 KVH) dh floats, [gate | up] rows of Fu = 2F floats (LN family: KVH = H, Wq = 3d, Fu = F).
+  int family = SPAR_B200_FAMILY_LN_GELU;
+  uint64_t KVH = 0, Wq = 0, Fu = 0;
+  bool qk_norm = false;
   uint64_t flat = 0;  // parameter floats (with alignment padding)
   std::vector<NamedTensor> named;
   std::vector<LayerOffsets> lay;
@@ -233,6 +317,7 @@ class LMTrainer {
   std::vector<LayerActs> acts;
   float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
   float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
+  float* dh_buf = nullptr;  // Spar family: d(swiglu output) [N, F]
   // Fused attention (TF32 mode, head_dim 32 / 64): no [T, T] buffers; dS holds the backward's
   // D = rowsum(dO o O) [B*H*T] instead of dS.
   bool fused_attention = false;
@@ -257,6 +342,7 @@ class LMTrainer {
     std::vector<LayerActs> acts;
     float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
     float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
+    float* dh_buf = nullptr;
     float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *splitk_ws2 = nullptr;
     float *row_loss = nullptr, *grads = nullptr;
     void* emb_scratch = nullptr;
@@ -278,7 +364,7 @@ class LMTrainer {
     Lane& ln = lanes[i];
     acts = ln.acts;
     xL = ln.xL; meanf = ln.meanf; rstdf = ln.rstdf; hf = ln.hf; logits = ln.logits;
-    dres = ln.dres; dtmp = ln.dtmp; dqkv = ln.dqkv; dS = ln.dS; du = ln.du;
+    dres = ln.dres; dtmp = ln.dtmp; dqkv = ln.dqkv; dS = ln.dS; du = ln.du; dh_buf = ln.dh_buf;
     ln_ws = ln.ln_ws; col_ws = ln.col_ws; splitk_ws = ln.splitk_ws; splitk_ws2 = ln.splitk_ws2;
     row_loss = ln.row_loss; grads = ln.grads; emb_scratch = ln.emb_scratch;
     wgrad_stream = ln.wgrad_stream;
@@ -363,6 +449,9 @@ class LMTrainer {
   cudaError_t attention_forward(LayerActs& A, cudaStream_t s);
   cudaError_t attention_backward(LayerActs& A, cudaStream_t s);
   cudaError_t layer_backward(uint64_t l, cudaStream_t s);
+  // Spar family (nn::DecoderLM): one block forward / backward.
+  cudaError_t layer_forward_spar(uint64_t l, float* out, cudaStream_t s);
+  cudaError_t layer_backward_spar(uint64_t l, cudaStream_t s);
   // Data-parallel reduction of buckets [b0, b1) on the communication stream once the gradients in
   // them are final on stream s. With two lanes, each lane records lane_ev after its last
   // micro-step has produced them; the lane that issues last (comm_lane) then adds lane 1's
@@ -422,6 +511,11 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   dh = d / H;
   N = B * T;
   Vp = (V + 3) / 4 * 4;
+  family = c.family;
+  KVH = (family == SPAR_B200_FAMILY_SPAR && c.num_kv_heads) ? c.num_kv_heads : H;
+  Wq = (H + 2 * KVH) * (d / H);
+  Fu = family == SPAR_B200_FAMILY_SPAR ? 2 * F : F;
+  qk_norm = family == SPAR_B200_FAMILY_SPAR && c.qk_norm != 0;
   if (d % 32 != 0 || F % 4 != 0 || dh % 32 != 0 || T % 4 != 0) return invalid();
   if (c.precision != SPAR_B200_TF32 && c.precision != SPAR_B200_TF32X3) return invalid();
 
@@ -476,14 +570,18 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
       f(&A.mean1, N);
       f(&A.rstd1, N);
       f(&A.a1, N * d);
-      f(&A.qkv, N * 3 * d);
+      f(&A.qkv, N * Wq);
+      if (qk_norm) {
+        f(&A.qkv_raw, N * Wq);
+        f(&A.qk_rstd, N * (H + KVH));
+      }
       f(fused_attention ? &A.stats : &A.p, PS);
       f(&A.ctx, N * d);
       f(&A.h1, N * d);
       f(&A.mean2, N);
       f(&A.rstd2, N);
       f(&A.a2, N * d);
-      f(&A.u, N * F);
+      f(&A.u, N * Fu);
       f(&A.g, N * F);
     }
     f(&ln.xL, N * d);
@@ -493,9 +591,10 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     f(&ln.logits, N * Vp);
     f(&ln.dres, N * d);
     f(&ln.dtmp, N * d);
-    f(&ln.dqkv, N * 3 * d);
+    f(&ln.dqkv, N * Wq);
     f(&ln.dS, fused_attention ? B * H * T : PS);
-    f(&ln.du, N * F);
+    f(&ln.du, N * Fu);
+    if (family == SPAR_B200_FAMILY_SPAR) f(&ln.dh_buf, N * F);
     f(&ln.ln_ws, 3ull * ln_parts * d);  // dgamma, dbeta and dx column-sum partials
     f(&ln.col_ws, col_floats);
     f(&ln.row_loss, N);
@@ -534,9 +633,9 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     // Partial tiles of every product of the step that may be split along K (few output tiles
     // for the SMs: the weight gradients, and the token-dimension products at small batches).
     struct Shape { uint64_t m, n, k; };
-    const Shape shapes[] = {{N, 3 * d, d}, {N, d, d},     {N, F, d},  {N, d, F}, {N, V, d},
-                            {V, d, N},     {N, d, V},     {F, d, N},  {d, F, N}, {d, d, N},
-                            {d, 3 * d, N}, {N, d, 3 * d}};
+    const Shape shapes[] = {{N, Wq, d}, {N, d, d},  {N, Fu, d}, {N, d, F}, {N, V, d},
+                            {V, d, N},  {N, d, V},  {F, d, N},  {d, Fu, N}, {d, d, N},
+                            {d, Wq, N}, {N, d, Wq}, {N, F, d},  {N, d, Fu}};
     for (const Shape& sh : shapes) {
       SparB200Gemm g{};
       g.m = sh.m; g.n = sh.n; g.k = sh.k; g.batch[0] = g.batch[1] = 1;
@@ -627,7 +726,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
     g.rope_table = rope_tab;
     g.rope_seq = T;
     g.rope_dim = dh;
-    g.rope_cols = 2 * d;
+    g.rope_cols = Wq - KVH * dh;  // the q and k parts
   }
   launches += cfg.precision == SPAR_B200_TF32X3 ? 3 : 1;
   // Never let a split copy run past the workspace sized in init().
@@ -661,7 +760,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
 cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
   if (fused_attention)
     return attention_forward_launch(A.qkv, A.ctx, A.stats, A.stats + B * H * T, B, T, H, dh,
-                                    device, s);
+                                    device, s, KVH);
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
   const uint64_t ld = 3 * d;
   const uint64_t qkv_bs[2] = {T * ld, dh};
@@ -839,6 +938,10 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
     const LayerOffsets& lo = lay[l];
     float* out = l + 1 < L ? acts[l + 1].x : xL;
     SPAR_CHECK(wait_gather(L - 1 - l, s));
+    if (family == SPAR_B200_FAMILY_SPAR) {
+      SPAR_CHECK(layer_forward_spar(l, out, s));
+      continue;
+    }
     launches += 2 + 1;  // 2 LayerNorms, softmax (or fused attention)
     SPAR_CHECK(layernorm_forward_launch(A.a1, A.mean1, A.rstd1, A.x, P + lo.ln1_g, P + lo.ln1_b,
                                         N, d, eps, device, s));
@@ -859,8 +962,11 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   }
   launches += 1 + 2 + 2;  // final LayerNorm, cross-entropy + loss sum, final LayerNorm backward
   SPAR_CHECK(wait_gather(L + 1, s));
-  SPAR_CHECK(layernorm_forward_launch(hf, meanf, rstdf, xL, P + off_lnf_g, P + off_lnf_b, N, d,
-                                      eps, device, s));
+  if (family == SPAR_B200_FAMILY_SPAR)
+    SPAR_CHECK(rmsnorm_forward_launch(hf, rstdf, xL, P + off_lnf_g, N, d, eps, device, s));
+  else
+    SPAR_CHECK(layernorm_forward_launch(hf, meanf, rstdf, xL, P + off_lnf_g, P + off_lnf_b, N, d,
+                                        eps, device, s));
   SPAR_CHECK(gemm(N, V, d, hf, d, false, P + off_E, d, true, logits, Vp, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // Fused log-softmax + NLL + mean backward; dlogits overwrite the logits in place.
@@ -881,11 +987,15 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   SPAR_CHECK(gemm(N, d, V, logits, Vp, false, P + off_E, d, false, dtmp, d, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // The final norm's dx is dL/d(last block output): its column sums are that block's b2 gradient.
-  SPAR_CHECK(layernorm_backward_launch(dres, G + off_lnf_g, G + off_lnf_b, dtmp, xL,
-                                       P + off_lnf_g, meanf, rstdf, N, d, 1, 0, ln_ws, device, s,
-                                       G + lay[L - 1].b2));
+  if (family == SPAR_B200_FAMILY_SPAR)
+    SPAR_CHECK(rmsnorm_backward_launch(dres, G + off_lnf_g, dtmp, xL, P + off_lnf_g, rstdf, N, d,
+                                       1, 0, ln_ws, device, s));
+  else
+    SPAR_CHECK(layernorm_backward_launch(dres, G + off_lnf_g, G + off_lnf_b, dtmp, xL,
+                                         P + off_lnf_g, meanf, rstdf, N, d, 1, 0, ln_ws, device, s,
+                                         G + lay[L - 1].b2));
   for (uint64_t l = L; l-- > 0;) {
-    SPAR_CHECK(layer_backward(l, s));
+    SPAR_CHECK(family == SPAR_B200_FAMILY_SPAR ? layer_backward_spar(l, s) : layer_backward(l, s));
   }
   launches += 5;
   // dE's tied-embedding scatter below adds into G + off_E, and the next micro-step rewrites the
@@ -904,6 +1014,118 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
 #undef SPAR_CHECK
 }
 
+// One block of Spar's decoder (TransformerBlock::forward, src/nn/transformer.cpp:53-69):
+//   a1 = RMSNorm(x); qkv = a1 [Wq | Wk | Wv]; (qk_norm: RMSNorm of each q / k head); RoPE on q, k;
+//   ctx = attention (key/value heads shared by query groups); h1 = x + ctx Wo;
+//   a2 = RMSNorm(h1); [gate | up] = a2 [Wgate | Wup]; g = silu(gate) * up; out = h1 + g Wdown.
+cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s) {
+  LayerActs& A = acts[l];
+  const LayerOffsets& lo = lay[l];
+  float* P = params;
+  const float eps = static_cast<float>(cfg.norm_epsilon);
+  launches += 2 + 1 + 1;  // 2 RMSNorms, attention, SwiGLU
+  SPAR_TRY(rmsnorm_forward_launch(A.a1, A.rstd1, A.x, P + lo.ln1_g, N, d, eps, device, s));
+  if (!qk_norm) {
+    // RoPE on the q and k parts in the epilogue; q, k, v stored rounded to nearest TF32.
+    SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, P + lo.wqkv, Wq, false, A.qkv, Wq, false,
+                  SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1,
+                  nullptr, nullptr, nullptr, true, cfg.use_rope != 0));
+  } else {
+    // The q / k norms come before RoPE (attention.cpp:212-215): project, normalise each head
+    // into qkv, copy v, then rotate q and k (rounded to nearest TF32).
+    launches += 3 + (cfg.use_rope ? 1 : 0);
+    const float qeps = static_cast<float>(cfg.qk_norm_epsilon);
+    SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, P + lo.wqkv, Wq, false, A.qkv_raw, Wq, false,
+                  SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+    SPAR_TRY(rmsnorm_forward_launch(A.qkv, A.qk_rstd, A.qkv_raw, P + lo.qn, N * H, dh, qeps,
+                                    device, s, Wq, static_cast<uint32_t>(H)));
+    SPAR_TRY(rmsnorm_forward_launch(A.qkv + H * dh, A.qk_rstd + N * H, A.qkv_raw + H * dh,
+                                    P + lo.kn, N * KVH, dh, qeps, device, s, Wq,
+                                    static_cast<uint32_t>(KVH)));
+    const uint64_t vc = (H + KVH) * dh;
+    SPAR_TRY(launch(copy_round_kernel, dim3(grid_for(N * KVH * dh, 256, sm_count(device) * 8)),
+                    dim3(256), 0, s, A.qkv + vc, static_cast<const float*>(A.qkv_raw + vc), N,
+                    KVH * dh, Wq));
+    if (cfg.use_rope)
+      SPAR_TRY(rope_apply_launch(A.qkv, rope_tab, N, T, H + KVH, dh, Wq, 0, device, s, 1));
+  }
+  SPAR_TRY(attention_forward(A, s));
+  SPAR_TRY(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
+                SPAR_B200_EPI_BIAS_ADD, nullptr, A.x, d, s));
+  SPAR_TRY(rmsnorm_forward_launch(A.a2, A.rstd2, A.h1, P + lo.ln2_g, N, d, eps, device, s));
+  SPAR_TRY(gemm(N, Fu, d, A.a2, d, false, P + lo.w1, Fu, false, A.u, Fu, false,
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+  SPAR_TRY(swiglu_forward_launch(A.g, F, A.u, Fu, A.u + F, Fu, N, F, device, s));
+  return gemm(N, d, F, A.g, F, false, P + lo.w2, d, false, out, d, false, SPAR_B200_EPI_BIAS_ADD,
+              nullptr, A.h1, d, s);
+}
+
+// Backward of that block, dres = dL/d(block output) in, dres = dL/d(block input) out; weight
+// gradients accumulate, on the weight-gradient stream beside the dX chain as in layer_backward.
+cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
+  LayerActs& A = acts[l];
+  const LayerOffsets& lo = lay[l];
+  float* P = params;
+  float* G = grads;
+  launches += 2 * 2 + 1 + 1 + (qk_norm ? 4 : 0);  // RMSNorm bwd, attention, SwiGLU bwd, qk norms
+  const bool conc = wgrad_enabled && !profiling;
+  cudaStream_t w = conc ? wgrad_stream : s;
+  auto fork = [&](int i) -> cudaError_t {
+    if (!conc) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(wg_fork[i], s);
+    return e == cudaSuccess ? cudaStreamWaitEvent(w, wg_fork[i], 0) : e;
+  };
+  auto mark = [&](int i) -> cudaError_t { return conc ? cudaEventRecord(wg_join[i], w) : cudaSuccess; };
+  auto join = [&](int i) -> cudaError_t { return conc ? cudaStreamWaitEvent(s, wg_join[i], 0) : cudaSuccess; };
+  // MLP: out = h1 + g Wdown, g = silu(gate) * up, [gate | up] = a2 [Wgate | Wup]
+  SPAR_TRY(fork(0));
+  SPAR_TRY(gemm(F, d, N, A.g, F, true, dres, d, false, G + lo.w2, d, true, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, w));
+  SPAR_TRY(mark(0));  // dWdown has read dres
+  SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, dh_buf, F, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s));
+  SPAR_TRY(swiglu_backward_launch(du, Fu, du + F, Fu, dh_buf, F, A.u, Fu, A.u + F, Fu, N, F,
+                                  device, s));
+  SPAR_TRY(fork(1));
+  SPAR_TRY(gemm(d, Fu, N, A.a2, d, true, du, Fu, false, G + lo.w1, Fu, true, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, w));
+  SPAR_TRY(gemm(N, d, Fu, du, Fu, false, P + lo.w1, Fu, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s));
+  // dres += RMSNorm backward -> dL/dh1 (dWdown read dres first)
+  SPAR_TRY(join(0));
+  SPAR_TRY(rmsnorm_backward_launch(dres, G + lo.ln2_g, dtmp, A.h1, P + lo.ln2_g, A.rstd2, N, d, 1,
+                                   1, ln_ws, device, s));
+  // out projection: h1 = x + ctx Wo
+  SPAR_TRY(fork(2));
+  SPAR_TRY(gemm(d, d, N, A.ctx, d, true, dres, d, false, G + lo.wo, d, true, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, w));
+  SPAR_TRY(mark(1));  // dWo has read dres
+  SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
+                true));
+  // attention: dctx (dtmp) -> dqkv, dq / dk already rotated back through RoPE
+  SPAR_TRY(attention_backward(A, s));
+  if (qk_norm) {  // through the q / k norms, in place (weight gradients accumulate)
+    SPAR_TRY(rmsnorm_backward_launch(dqkv, G + lo.qn, dqkv, A.qkv_raw, P + lo.qn, A.qk_rstd, N * H,
+                                     dh, 1, 0, ln_ws, device, s, Wq, static_cast<uint32_t>(H)));
+    SPAR_TRY(rmsnorm_backward_launch(dqkv + H * dh, G + lo.kn, dqkv + H * dh, A.qkv_raw + H * dh,
+                                     P + lo.kn, A.qk_rstd + N * H, N * KVH, dh, 1, 0, ln_ws,
+                                     device, s, Wq, static_cast<uint32_t>(KVH)));
+  }
+  SPAR_TRY(fork(3));
+  SPAR_TRY(gemm(d, Wq, N, A.a1, d, true, dqkv, Wq, false, G + lo.wqkv, Wq, true,
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, w));
+  SPAR_TRY(mark(2));
+  SPAR_TRY(gemm(N, d, Wq, dqkv, Wq, false, P + lo.wqkv, Wq, true, dtmp, d, false,
+                SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
+  SPAR_TRY(join(1));
+  SPAR_TRY(rmsnorm_backward_launch(dres, G + lo.ln1_g, dtmp, A.x, P + lo.ln1_g, A.rstd1, N, d, 1,
+                                   1, ln_ws, device, s));
+  SPAR_TRY(join(2));
+  if (comm && last_micro) SPAR_TRY(reduce_buckets(L - 1 - l, L - l, static_cast<int>(l), layer_ev[l], s));
+  return cudaSuccess;
+}
+
 // dqkv from dctx (in dtmp): fused kernels, or the six batched GEMMs around the materialised
 // probabilities and the softmax backward.
 cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
@@ -914,7 +1136,7 @@ cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
     return attention_backward_launch(A.qkv, A.ctx, dtmp, A.stats, A.stats + B * H * T, dS, dqkv,
                                      B, T, H, dh, device, s, cfg.use_rope ? rope_tab : nullptr,
                                      two ? ln.key_stream : nullptr, two ? ln.key_fork : nullptr,
-                                     two ? ln.key_join : nullptr);
+                                     two ? ln.key_join : nullptr, KVH);
   }
   const uint64_t ld = 3 * d;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));

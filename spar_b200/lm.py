@@ -38,6 +38,10 @@ class LMConfig:
     adam_eps: float = 1e-8
     weight_decay: float = 0.1
     max_grad_norm: float = 1.0
+    family: int = 0  # 0: LayerNorm / GELU benchmark decoder, 1: Spar's nn::DecoderLM
+    kv_heads: int = 0  # family 1: key/value heads (0 = heads)
+    qk_norm: bool = False  # family 1
+    qk_eps: float = 1e-6  # family 1
 
     def oracle_dict(self):
         return {"vocab": self.vocab, "dim": self.dim, "hidden": self.hidden, "layers": self.layers,
@@ -59,7 +63,8 @@ def native_config(cfg: LMConfig) -> SparB200LMConfig:
     return SparB200LMConfig(cfg.vocab, cfg.dim, cfg.hidden, cfg.layers, cfg.heads, cfg.seq,
                             cfg.micro_batch, cfg.eps, cfg.rope_theta, int(cfg.use_rope),
                             cfg.precision, cfg.beta1, cfg.beta2, cfg.adam_eps, cfg.weight_decay,
-                            cfg.max_grad_norm)
+                            cfg.max_grad_norm, cfg.family, int(cfg.qk_norm), cfg.kv_heads,
+                            cfg.qk_eps)
 
 
 class DecoderLM:

@@ -152,6 +152,31 @@ def main(only=()):
         samp["gnorm/" + n] = np.float64(np.linalg.norm(grads[n].astype(np.float64)))
     save("lm_c1", ids=ids, loss=np.float32(loss), norm=np.float64(norm), **samp)
 
+    save("lm_spar", **spar_family_fixture())
+
+
+def spar_family_fixture():
+    """Spar's own nn::DecoderLM (RMSNorm, grouped-query attention with q/k norms, SwiGLU, no
+    biases): one optimiser step of two micro-batches; loss, norm, per-tensor gradient norms and 64
+    sampled entries of every gradient / updated parameter."""
+    cfg = {"vocab": 64, "dim": 128, "hidden": 256, "layers": 2, "heads": 4, "kv_heads": 2,
+           "qk_norm": 1}
+    opt = {"beta1": 0.9, "beta2": 0.95, "eps": 1e-8, "weight_decay": 0.1, "max_grad_norm": 1.0}
+    names = [n for n, _ in R.spar_param_info(cfg)]
+    assert names == list(O.spar_family_shapes(cfg)), names
+    params = O.spar_family_parameters(cfg, 0x5EED0301)
+    ids = O.Random(0x5EED1301).bounded(2 * 2 * 32, 64).reshape(2, 2, 32).astype(np.int32)
+    loss, norm, grads, new = R.spar_lm_step(params, names, ids, cfg, 3e-4, opt)
+    samp = {}
+    rng = np.random.default_rng(1)
+    for n in names:
+        idx = rng.choice(grads[n].size, size=min(64, grads[n].size), replace=False)
+        samp["idx/" + n] = idx
+        samp["grad/" + n] = grads[n].ravel()[idx]
+        samp["new/" + n] = new[n].ravel()[idx]
+        samp["gnorm/" + n] = np.float64(np.linalg.norm(grads[n].astype(np.float64)))
+    return dict(ids=ids, loss=np.float32(loss), norm=np.float64(norm), **samp)
+
 
 if __name__ == "__main__":
     main(tuple(sys.argv[1:]))

@@ -313,3 +313,54 @@ def test_cuda_c1_step_matches_reference_fixture(cuda, precision, tol):
     for n in O.parameter_names(2):
         gn = float(f["gnorm/" + n])
         assert abs(np.linalg.norm(grads[n].astype(np.float64)) - gn) <= 10 * tol * gn + 1e-12, n
+
+
+SPAR_FAMILY = dict(vocab=64, dim=128, hidden=256, layers=2, heads=4, kv_heads=2, qk_norm=1)
+
+
+def test_oracle_spar_family_names_match_reference_fixture():
+    """The parameter plan the runtime and the tests share names every tensor of the fixture."""
+    f = load("lm_spar")
+    names = list(O.spar_family_shapes(SPAR_FAMILY))
+    assert sorted(k[len("grad/"):] for k in f if k.startswith("grad/")) == sorted(names)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("lanes", ["0", "2"])
+def test_cuda_spar_family_step_matches_reference_fixture(cuda, monkeypatch, lanes):
+    """One training step of Spar's own nn::DecoderLM (RMSNorm, grouped-query attention with q/k
+    norms and RoPE, SwiGLU, no biases, tied logits; two micro-batches, clip, AdamW) on the runtime
+    against the reference run on the same parameters and ids: loss and norm to the TF32 bar
+    (2e-3), per-tensor gradient norms and sampled gradient entries to relative L2 2e-2. Sampled
+    updated parameters: the first AdamW step moves every parameter by about lr * sign(g), so a
+    near-zero gradient entry whose sign TF32 flips lands 2 lr away; no entry may differ by more
+    than that, and the median entry must agree to 1e-5 of the weights' scale."""
+    from spar_b200.lm import DecoderLM, LMConfig
+
+    monkeypatch.setenv("SPAR_B200_LANES", lanes)
+    c = SPAR_FAMILY
+    cfg = LMConfig(vocab=c["vocab"], dim=c["dim"], hidden=c["hidden"], layers=c["layers"],
+                   heads=c["heads"], seq=32, micro_batch=2, family=1, kv_heads=c["kv_heads"],
+                   qk_norm=bool(c["qk_norm"]))
+    f = load("lm_spar")
+    lm = DecoderLM(cfg, 0)
+    assert lm.names == list(O.spar_family_shapes(c))
+    lm.load_state_dict(O.spar_family_parameters(c, 0x5EED0301))
+    loss, norm, flags = lm.train_step(f["ids"], 3e-4, step=1)
+    grads = lm.state_dict("grad")
+    new = lm.state_dict("param")
+    lm.close()
+    from spar_b200 import ops
+
+    assert ops.gemm_error(0) == 0 and ops.attention_error(0) == 0
+    assert flags == (0, 0)
+    assert abs(loss - f["loss"]) <= 2e-3 * abs(f["loss"])
+    assert abs(norm - f["norm"]) <= 2e-3 * f["norm"]
+    for n in lm.names:
+        gn = float(f["gnorm/" + n])
+        assert abs(np.linalg.norm(grads[n].astype(np.float64)) - gn) <= 2e-2 * gn + 1e-12, n
+        idx = f["idx/" + n]
+        assert rel_l2(grads[n].ravel()[idx], f["grad/" + n]) <= 2e-2, n
+        diff = np.abs(new[n].ravel()[idx].astype(np.float64) - f["new/" + n])
+        assert diff.max() <= 2.02 * 3e-4 + 1e-7, n
+        assert np.median(diff) <= 1e-5 * np.abs(f["new/" + n]).max(), n
