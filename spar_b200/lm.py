@@ -215,9 +215,11 @@ def smoke_step(device) -> None:
 
 
 def _main() -> None:
-    """`python -m spar_b200.lm --micro-batch MB --steps S`: S training steps of the C5 decoder on one
-    GPU, with rank 0's share of the 64-sequence global batch for 16 / MB ranks (4 accumulation
-    micro-steps of MB sequences), synthetic weights and ids; prints the loss and step time."""
+    """`python -m spar_b200.lm --micro-batch MB --steps S [--family spar --kv-heads K --qk-norm]`:
+    S training steps of the C5 decoder (or, with --family spar, Spar's own nn::DecoderLM at the C5
+    dimensions: RMSNorm, K key/value heads, SwiGLU with the same hidden size) on one GPU, with
+    rank 0's share of the 64-sequence global batch for 16 / MB ranks (4 accumulation micro-steps
+    of MB sequences), synthetic weights and ids; prints the loss and step time."""
     import argparse
     import time
     from dataclasses import replace
@@ -229,18 +231,25 @@ def _main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--micro-batch", type=int, default=16, choices=[1, 2, 4, 8, 16])
     ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--family", default="ln", choices=["ln", "spar"])
+    ap.add_argument("--kv-heads", type=int, default=4)
+    ap.add_argument("--qk-norm", action="store_true")
     a = ap.parse_args()
     cfg = replace(C5, micro_batch=a.micro_batch)
+    if a.family == "spar":
+        cfg = replace(cfg, family=1, kv_heads=a.kv_heads, qk_norm=a.qk_norm)
     lm = DecoderLM(cfg, 0)
     lm.init_normal(0x5EED0005, 0.02)
     ids = torch.from_numpy(rank_share(0x5EED1005, 64, 4, cfg.seq, cfg.vocab, 0,
                                       16 // a.micro_batch)).cuda()
+    tokens = ids.numel()
     for s in range(a.steps):
         t0 = time.perf_counter()
         loss, norm, flags = lm.train_step(ids, 3e-4, step=s + 1)
         torch.cuda.synchronize()
-        print(f"step {s + 1}: loss {loss:.4f} grad-norm {norm:.4f} flags {flags} "
-              f"{(time.perf_counter() - t0) * 1e3:.1f} ms", flush=True)
+        ms = (time.perf_counter() - t0) * 1e3
+        print(f"step {s + 1}: loss {loss:.4f} grad-norm {norm:.4f} flags {flags} {ms:.1f} ms "
+              f"({tokens / ms * 1e3:.0f} tokens/s)", flush=True)
     lm.close()
 
 
