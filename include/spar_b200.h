@@ -389,6 +389,38 @@ struct SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int world_
 /* the same order, all-gathers one arena (which as in flat_buffer) ordered on `stream`; until     */
 /* then spar_b200_lm_parameter_copy refuses reads of it (code 1, cuda_error cudaErrorNotReady).   */
 struct SparCudaStatus spar_b200_lm_gather(void* handle, int which, void* stream);
+/* Training checkpoints in Spar's SPARCKPT v1 format (src/checkpoint/checkpoint.cpp:18-475:    */
+/* save_training_checkpoint / load_training_checkpoint), family 1 only (the format stores a      */
+/* DecoderConfig): model parameters and AdamW moments by name, progress, RNG state, optimiser    */
+/* hyper-parameters. adam_step: completed AdamW steps (0: no optimiser state; the next          */
+/* train_step is then step adam_step + 1). The writer writes `path`.tmp, then renames it.        */
+struct SparB200Checkpoint {
+  uint64_t global_step, tokens_seen; /* TrainingProgress */
+  uint64_t rng_state;                /* Random::state() of the caller's data RNG */
+  double learning_rate;              /* the optimiser's current learning rate */
+  uint64_t adam_step;
+};
+/* Device state -> file (synchronises the device). With a sharded optimiser this is collective:  */
+/* every rank calls it (path NULL on ranks that only take part in the gather).                   */
+struct SparCudaStatus spar_b200_lm_save_checkpoint(void* handle, const char* path,
+                                                   const struct SparB200Checkpoint* meta);
+/* File -> device state (parameters and moments; gradients untouched). Code 1 when the file does */
+/* not match the handle's config (dimensions, norms, AdamW hyper-parameters) or is malformed.   */
+struct SparCudaStatus spar_b200_lm_load_checkpoint(void* handle, const char* path,
+                                                   struct SparB200Checkpoint* meta);
+/* The same format from / to host arrays, without a GPU: one contiguous row-major float array    */
+/* per named tensor of `config` (spar_b200_lm_layout_tensor order and shapes).                  */
+struct SparCudaStatus spar_b200_checkpoint_write(const char* path,
+                                                 const struct SparB200LMConfig* config,
+                                                 const struct SparB200Checkpoint* meta,
+                                                 const float* const* values,
+                                                 const float* const* first_moments,
+                                                 const float* const* second_moments);
+struct SparCudaStatus spar_b200_checkpoint_read(const char* path,
+                                                const struct SparB200LMConfig* config,
+                                                struct SparB200Checkpoint* meta,
+                                                float* const* values, float* const* first_moments,
+                                                float* const* second_moments);
 /* Host-only queries of the parameter-arena layout a config produces (no device work, usable   */
 /* without a GPU): flat size in floats, the named tensors (Spar's names, offset into the arena, */
 /* rows x cols with row stride ld; cols == 0 for vectors) and the gradient all-reduce buckets    */

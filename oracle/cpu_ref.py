@@ -36,6 +36,10 @@ def load():
             "ref_swiglu": [F, F, F, c_int64, F, F, F],
             "ref_attention": [F, F, F, F] + [c_int64] * 5 + [F, F, F, F],
             "ref_spar_param_info": [c_int64] * 8 + [c_char_p, c_int64, POINTER(c_int64)],
+            "ref_spar_ckpt_save": [c_char_p] + [c_int64] * 7 + [c_double] * 3 +
+                                  [POINTER(F)] * 3 + [c_uint64] * 4 + [c_double] * 5,
+            "ref_spar_ckpt_load": [c_char_p] + [POINTER(F)] * 3 + [POINTER(c_uint64)] * 4 +
+                                  [POINTER(c_double)],
             "ref_spar_lm_step": [c_int64] * 10 + [c_double, c_double, POINTER(F), I32, c_double,
                                                   c_double, c_double, c_double, c_double,
                                                   c_double, F, POINTER(c_double), POINTER(F),
@@ -221,6 +225,34 @@ def spar_lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
                                    opt["weight_decay"], opt["max_grad_norm"], _p(loss),
                                    ctypes.byref(norm), arr(gs), arr(outs)))
     return float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs))
+
+
+def spar_ckpt_save(path, cfg: dict, params: list, m: list, v: list, adam_step: int,
+                   global_step: int, tokens: int, rng_state: int, lr: float, opt: dict):
+    """checkpoint::save_training_checkpoint of the reference's nn::DecoderLM (params / m / v in
+    named-parameter order)."""
+    arr = lambda lst: (F * len(lst))(*[_p(_f(a)) for a in lst])
+    keep = [_f(a) for a in params + m + v]  # noqa: F841 - alive during the call
+    _check(load().ref_spar_ckpt_save(str(path).encode(), *_spar_dims(cfg), cfg.get("eps", 1e-5),
+                                     cfg.get("rope_theta", 1e4), cfg.get("qk_eps", 1e-6),
+                                     arr(params), arr(m), arr(v), adam_step, global_step, tokens,
+                                     rng_state, lr, opt["beta1"], opt["beta2"], opt["eps"],
+                                     opt["weight_decay"]))
+
+
+def spar_ckpt_load(path, cfg: dict):
+    """checkpoint::load_training_checkpoint: (params, m, v, adam_step, global_step, tokens,
+    rng_state, lr) with arrays in named-parameter order."""
+    sizes = [k for _, k in spar_param_info(cfg)]
+    ps = [np.empty(k, np.float32) for k in sizes]
+    ms = [np.empty(k, np.float32) for k in sizes]
+    vs = [np.empty(k, np.float32) for k in sizes]
+    arr = lambda lst: (F * len(lst))(*[_p(a) for a in lst])
+    u = [c_uint64() for _ in range(4)]
+    lr = c_double()
+    _check(load().ref_spar_ckpt_load(str(path).encode(), arr(ps), arr(ms), arr(vs),
+                                     *[ctypes.byref(x) for x in u], ctypes.byref(lr)))
+    return ps, ms, vs, u[0].value, u[1].value, u[2].value, u[3].value, lr.value
 
 
 def _sample_worker(args):

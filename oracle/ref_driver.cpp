@@ -407,6 +407,66 @@ int ref_spar_lm_step(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_
   });
 }
 
+// checkpoint::save_training_checkpoint of nn::DecoderLM with the given parameters, an AdamW whose
+// every parameter state is (m, v, adam_step) (none when adam_step == 0), a Random at rng_state.
+int ref_spar_ckpt_save(const char* path, int64_t vocab, int64_t d, int64_t f, int64_t layers,
+                       int64_t heads, int64_t kv_heads, int64_t qk_norm, double eps, double theta,
+                       double qk_eps, const float* const* params, const float* const* m,
+                       const float* const* v, uint64_t adam_step, uint64_t global_step,
+                       uint64_t tokens, uint64_t rng_state, double lr, double beta1, double beta2,
+                       double adam_eps, double wd) {
+  return guarded([&] {
+    Random rng{1};
+    nn::DecoderConfig c = spar_config(vocab, d, f, layers, heads, kv_heads, qk_norm, eps, theta);
+    c.qk_norm_epsilon = qk_eps;
+    nn::DecoderLM model{c, rng};
+    std::vector<nn::Parameter> ps;
+    for (auto& np : nn::named_parameters(model)) ps.push_back(np.parameter);
+    for (std::size_t i = 0; i < ps.size(); ++i) load(ps[i], params[i]);
+    optim::AdamW opt{ps, lr, beta1, beta2, adam_eps, wd};
+    if (adam_step)
+      for (std::size_t i = 0; i < ps.size(); ++i) {
+        const auto shape = ps[i].tensor().shape();
+        std::vector<dim> dims(shape.dimensions().begin(), shape.dimensions().end());
+        opt.set_parameter_state(ps[i], optim::AdamWParameterState{from_host(m[i], dims, false),
+                                                                  from_host(v[i], dims, false),
+                                                                  adam_step});
+      }
+    Random random{0};
+    random.set_state(rng_state);
+    checkpoint::save_training_checkpoint(path, model, opt, random, {global_step, tokens});
+  });
+}
+
+// checkpoint::load_training_checkpoint: parameters, moments (zero without state), the AdamW step
+// of the first parameter, progress, RNG state and learning rate.
+int ref_spar_ckpt_load(const char* path, float** params, float** m, float** v,
+                       uint64_t* adam_step, uint64_t* global_step, uint64_t* tokens,
+                       uint64_t* rng_state, double* lr) {
+  return guarded([&] {
+    auto loaded = checkpoint::load_training_checkpoint(path);
+    const auto named = nn::named_parameters(loaded.model);
+    *adam_step = 0;
+    for (std::size_t i = 0; i < named.size(); ++i) {
+      to_host(named[i].parameter.tensor(), params[i]);
+      const auto st = loaded.optimizer.parameter_state(named[i].parameter);
+      const std::size_t n = named[i].parameter.tensor().numel();
+      if (st) {
+        to_host(st->first_moment, m[i]);
+        to_host(st->second_moment, v[i]);
+        if (i == 0) *adam_step = st->step;
+      } else {
+        std::memset(m[i], 0, n * sizeof(float));
+        std::memset(v[i], 0, n * sizeof(float));
+      }
+    }
+    *global_step = loaded.progress.global_step;
+    *tokens = loaded.progress.tokens_seen;
+    *rng_state = loaded.random.state();
+    *lr = loaded.optimizer.learning_rate();
+  });
+}
+
 // Seconds for `iters` training steps (forward, loss, backward, clip, AdamW) of a one-block
 // decoder with the given dimensions on [1, t] token ids: the bounded CPU-baseline sample.
 double ref_train_sample_seconds(int64_t vocab, int64_t d, int64_t f, int64_t heads, int64_t t,

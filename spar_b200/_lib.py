@@ -39,6 +39,11 @@ class SparB200Gemm(ctypes.Structure):
     ]
 
 
+class SparB200Checkpoint(ctypes.Structure):
+    _fields_ = [("global_step", c_uint64), ("tokens_seen", c_uint64), ("rng_state", c_uint64),
+                ("learning_rate", c_double), ("adam_step", c_uint64)]
+
+
 class SparB200LMConfig(ctypes.Structure):
     _fields_ = [
         ("vocab_size", c_uint64), ("model_dim", c_uint64), ("hidden_dim", c_uint64),
@@ -104,6 +109,12 @@ SIGNATURES = {
                                     POINTER(c_int32), p]),
     "spar_b200_lm_set_comm": (S, [p, p, i]),
     "spar_b200_lm_gather": (S, [p, i, p]),
+    "spar_b200_lm_save_checkpoint": (S, [p, c_char_p, POINTER(SparB200Checkpoint)]),
+    "spar_b200_lm_load_checkpoint": (S, [p, c_char_p, POINTER(SparB200Checkpoint)]),
+    "spar_b200_checkpoint_write": (S, [c_char_p, POINTER(SparB200LMConfig),
+                                       POINTER(SparB200Checkpoint), p, p, p]),
+    "spar_b200_checkpoint_read": (S, [c_char_p, POINTER(SparB200LMConfig),
+                                      POINTER(SparB200Checkpoint), p, p, p]),
     "spar_b200_lm_layout": (S, [p, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
     "spar_b200_lm_layout_tensor": (S, [p, u64, c_char_p, u64, POINTER(c_uint64), POINTER(c_uint64),
                                        POINTER(c_uint64), POINTER(c_uint64)]),

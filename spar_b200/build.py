@@ -30,6 +30,7 @@ SOURCES = [
     "compat.cu",
     "trainer.cu",
     "comm.cpp",
+    "checkpoint.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -24,6 +24,7 @@
 #include <string>
 #include <vector>
 
+#include "checkpoint.h"
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -1549,6 +1550,104 @@ extern "C" SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int wo
       }
     }
   }
+  return ok();
+}
+
+// ---------------------------------------------------------------- checkpoints (SPARCKPT v1)
+namespace spar_b200 {
+// Named tensors (name, shape) of a Spar-family config, in named-parameter order.
+bool checkpoint_tensors(const SparB200LMConfig& c, std::vector<CkptTensor>& out) {
+  if (c.family != SPAR_B200_FAMILY_SPAR) return false;
+  ParamLayout pl;
+  if (plan_params(c, pl).code != 0) return false;
+  out.clear();
+  for (const NamedTensor& n : pl.named)
+    out.push_back({n.name, n.cols ? std::vector<uint64_t>{n.rows, n.cols}
+                                  : std::vector<uint64_t>{n.rows}});
+  return true;
+}
+}  // namespace spar_b200
+
+namespace {
+// Device arena `which` of every named tensor <-> contiguous host arrays.
+cudaError_t stage_tensors(LMTrainer* t, int which, std::vector<std::vector<float>>& host,
+                          bool to_device) {
+  if (!to_device) host.assign(t->named.size(), {});
+  for (size_t i = 0; i < t->named.size(); ++i) {
+    const NamedTensor& n = t->named[i];
+    const uint64_t cols = n.cols ? n.cols : n.rows, rows = n.cols ? n.rows : 1;
+    const uint64_t ld = n.cols ? n.ld : n.rows;
+    float* dev = t->params + static_cast<uint64_t>(which) * t->flat + n.offset;
+    if (!to_device) host[i].resize(rows * cols);
+    const cudaError_t e =
+        to_device ? cudaMemcpy2D(dev, ld * 4, host[i].data(), cols * 4, cols * 4, rows,
+                                 cudaMemcpyHostToDevice)
+                  : cudaMemcpy2D(host[i].data(), cols * 4, dev, ld * 4, cols * 4, rows,
+                                 cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+std::vector<const float*> cptrs(const std::vector<std::vector<float>>& h) {
+  std::vector<const float*> p;
+  for (const auto& x : h) p.push_back(x.data());
+  return p;
+}
+std::vector<float*> ptrs(std::vector<std::vector<float>>& h) {
+  std::vector<float*> p;
+  for (auto& x : h) p.push_back(x.data());
+  return p;
+}
+}  // namespace
+
+extern "C" SparCudaStatus spar_b200_lm_save_checkpoint(void* handle, const char* path,
+                                                       const SparB200Checkpoint* meta) {
+  if (!handle || !meta) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  if (t->family != SPAR_B200_FAMILY_SPAR) return invalid();
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaError_t e = cudaDeviceSynchronize();
+  for (int w : {0, 2, 3})  // sharded optimiser: whole parameters and moments (collective)
+    if (e == cudaSuccess) e = t->gather_arena(w, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return runtime(e);
+  if (!path) return ok();
+  std::vector<std::vector<float>> p, m, v;
+  e = stage_tensors(t, 0, p, false);
+  if (e == cudaSuccess && meta->adam_step) e = stage_tensors(t, 2, m, false);
+  if (e == cudaSuccess && meta->adam_step) e = stage_tensors(t, 3, v, false);
+  if (e != cudaSuccess) return runtime(e);
+  const auto pp = cptrs(p), mp = cptrs(m), vp = cptrs(v);
+  return checkpoint_write(path, t->cfg, *meta, pp.data(), meta->adam_step ? mp.data() : nullptr,
+                          meta->adam_step ? vp.data() : nullptr);
+}
+
+extern "C" SparCudaStatus spar_b200_lm_load_checkpoint(void* handle, const char* path,
+                                                       SparB200Checkpoint* meta) {
+  if (!handle || !path || !meta) return invalid();
+  LMTrainer* t = as_trainer(handle);
+  if (t->family != SPAR_B200_FAMILY_SPAR) return invalid();
+  std::vector<std::vector<float>> p(t->named.size()), m(t->named.size()), v(t->named.size());
+  for (size_t i = 0; i < t->named.size(); ++i) {
+    const NamedTensor& n = t->named[i];
+    const uint64_t numel = n.cols ? n.rows * n.cols : n.rows;
+    p[i].resize(numel);
+    m[i].resize(numel);
+    v[i].resize(numel);
+  }
+  auto pp = ptrs(p), mp = ptrs(m), vp = ptrs(v);
+  const SparCudaStatus st = checkpoint_read(path, t->cfg, *meta, pp.data(), mp.data(), vp.data());
+  if (st.code != 0) return st;
+  DeviceScope scope(t->device);
+  if (scope.error() != cudaSuccess) return runtime(scope.error());
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = stage_tensors(t, 0, p, true);
+  if (e == cudaSuccess) e = stage_tensors(t, 2, m, true);
+  if (e == cudaSuccess) e = stage_tensors(t, 3, v, true);
+  if (e != cudaSuccess) return runtime(e);
+  for (int w : {0, 2, 3}) t->stale[w] = false;  // every rank loads the whole state
   return ok();
 }
 

@@ -155,6 +155,22 @@ class DecoderLM:
     def attach_comm(self, comm, world_size: int):
         check("spar_b200_lm_set_comm", self.lib.spar_b200_lm_set_comm(self.handle, comm, world_size))
 
+    def save_checkpoint(self, path, global_step: int, tokens_seen: int, rng_state: int,
+                        learning_rate: float, adam_step: int):
+        """SPARCKPT v1 training checkpoint (Spar-family models; collective with a sharded
+        optimiser: every rank calls it, path None on ranks that only take part in the gather)."""
+        meta = _lib.SparB200Checkpoint(global_step, tokens_seen, rng_state, learning_rate, adam_step)
+        check("spar_b200_lm_save_checkpoint", self.lib.spar_b200_lm_save_checkpoint(
+            self.handle, None if path is None else str(path).encode(), ctypes.byref(meta)))
+
+    def load_checkpoint(self, path) -> dict:
+        """Loads parameters and AdamW moments; returns the progress fields (adam_step: the
+        next train_step is step adam_step + 1)."""
+        meta = _lib.SparB200Checkpoint()
+        check("spar_b200_lm_load_checkpoint", self.lib.spar_b200_lm_load_checkpoint(
+            self.handle, str(path).encode(), ctypes.byref(meta)))
+        return {k: getattr(meta, k) for k, _ in meta._fields_}
+
     def gather(self, which: str = "param", stream: int = 0):
         """Sharded optimiser: all-gathers one arena's pieces from every rank so that it can be read
         (get / state_dict). Collective: every rank calls it, in the same order."""
@@ -184,6 +200,37 @@ class DecoderLM:
                                                ctypes.byref(loss), ctypes.byref(norm), flags, stream))
         self.step_count = step
         return loss.value, norm.value, (flags[0], flags[1])
+
+
+def write_checkpoint(path, cfg: LMConfig, values: list, first_moments: list | None,
+                     second_moments: list | None, global_step: int = 0, tokens_seen: int = 0,
+                     rng_state: int = 0, learning_rate: float = 0.0, adam_step: int = 0):
+    """SPARCKPT v1 from host arrays (one per named tensor, layout order), no GPU needed."""
+    lib = _lib.load()
+    c = native_config(cfg)
+    meta = _lib.SparB200Checkpoint(global_step, tokens_seen, rng_state, learning_rate, adam_step)
+    keep = [np.ascontiguousarray(a, np.float32) for a in values]
+    arr = lambda lst: (ctypes.c_void_p * len(lst))(*[a.ctypes.data for a in lst])  # noqa: E731
+    km = [np.ascontiguousarray(a, np.float32) for a in (first_moments or [])]
+    kv = [np.ascontiguousarray(a, np.float32) for a in (second_moments or [])]
+    check("spar_b200_checkpoint_write",
+          lib.spar_b200_checkpoint_write(str(path).encode(), ctypes.byref(c), ctypes.byref(meta),
+                                         arr(keep), arr(km) if km else None,
+                                         arr(kv) if kv else None))
+
+
+def read_checkpoint(path, cfg: LMConfig, sizes: list):
+    """(values, first moments, second moments, meta dict) of a SPARCKPT v1 file for cfg;
+    sizes: element counts of the named tensors in layout order."""
+    lib = _lib.load()
+    c = native_config(cfg)
+    meta = _lib.SparB200Checkpoint()
+    vals, ms, vs = ([np.empty(k, np.float32) for k in sizes] for _ in range(3))
+    arr = lambda lst: (ctypes.c_void_p * len(lst))(*[a.ctypes.data for a in lst])  # noqa: E731
+    check("spar_b200_checkpoint_read",
+          lib.spar_b200_checkpoint_read(str(path).encode(), ctypes.byref(c), ctypes.byref(meta),
+                                        arr(vals), arr(ms), arr(vs)))
+    return vals, ms, vs, {k: getattr(meta, k) for k, _ in meta._fields_}
 
 
 def warmup_cosine(peak: float, minimum: float, warmup: int, decay: int, step: int) -> float:

@@ -300,3 +300,32 @@ def test_sharded_optimizer_one_rank_matches_replicated(cuda, monkeypatch, lanes)
         np.testing.assert_allclose([o[0] for o in a_out], [o[0] for o in b_out], rtol=1e-6)
     for x, y in zip(a, b):
         assert np.array_equal(x, y) if exact else rel_l2(x, y) <= 1e-6
+
+
+def test_spar_family_checkpoint_exact_resume(cuda, tmp_path):
+    """Spar-family runtime: two steps, a SPARCKPT v1 checkpoint (parameters + AdamW moments), a new
+    runtime that loads it, then the same third step on both: bitwise equal losses and weights."""
+    from spar_b200.lm import DecoderLM, LMConfig
+
+    c = dict(vocab=64, dim=128, hidden=256, layers=2, heads=4, kv_heads=2, qk_norm=1)
+    cfg = LMConfig(vocab=64, dim=128, hidden=256, layers=2, heads=4, seq=32, micro_batch=2,
+                   family=1, kv_heads=2, qk_norm=True)
+    ids = O.Random(0x5EED1401).bounded(3 * 2 * 2 * 32, 64).reshape(3, 2, 2, 32).astype(np.int32)
+    a = DecoderLM(cfg, 0)
+    a.load_state_dict(O.spar_family_parameters(c, 0x5EED0401))
+    for s in (1, 2):
+        a.train_step(ids[s - 1], 3e-4, step=s)
+    path = tmp_path / "step2.sparckpt"
+    a.save_checkpoint(path, global_step=2, tokens_seen=2 * 128, rng_state=99, learning_rate=3e-4,
+                      adam_step=2)
+    b = DecoderLM(cfg, 0)
+    meta = b.load_checkpoint(path)
+    assert meta == {"global_step": 2, "tokens_seen": 256, "rng_state": 99,
+                    "learning_rate": 3e-4, "adam_step": 2}
+    la = a.train_step(ids[2], 3e-4, step=3)
+    lb = b.train_step(ids[2], 3e-4, step=3)
+    pa, pb = _flat(a.state_dict(), a.names), _flat(b.state_dict(), b.names)
+    a.close()
+    b.close()
+    assert la == lb
+    assert np.array_equal(pa, pb)
