@@ -389,6 +389,35 @@ struct SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int world_
 /* the same order, all-gathers one arena (which as in flat_buffer) ordered on `stream`; until     */
 /* then spar_b200_lm_parameter_copy refuses reads of it (code 1, cuda_error cudaErrorNotReady).   */
 struct SparCudaStatus spar_b200_lm_gather(void* handle, int which, void* stream);
+/* Input pipeline, replacing data::LMBatchIterator (src/data/batch_iterator.cpp:56-143) over    */
+/* data::WindowDataset (src/data/tokenized_corpus.cpp:49-80): window i = tokens [i * stride,     */
+/* i * stride + sequence_length) of a packed corpus held in device memory; each epoch visits the  */
+/* windows in Spar's (optionally Fisher-Yates shuffled, derive_epoch_seed) order, batch_size at a */
+/* time (the last batch shorter unless drop_last). For data parallelism rank r of world receives */
+/* rows [r n / world, (r + 1) n / world) of every n-row batch. next gathers this rank's rows as   */
+/* int32 ids [rows, sequence_length] into `ids` (device) on `stream`; rows = 0: epoch finished.   */
+struct SparCudaStatus spar_b200_batches_create(const int32_t* tokens, uint64_t token_count,
+                                               uint64_t sequence_length, uint64_t stride,
+                                               uint64_t batch_size, int shuffle,
+                                               uint64_t shuffle_seed, int drop_last, int rank,
+                                               int world, int device, void** handle);
+struct SparCudaStatus spar_b200_batches_next(void* handle, int32_t* ids, uint64_t* rows,
+                                             uint64_t* global_rows, void* stream);
+struct SparCudaStatus spar_b200_batches_next_epoch(void* handle);
+/* BatchIteratorState: epoch and windows of its order consumed (set_state rebuilds the order). */
+struct SparCudaStatus spar_b200_batches_state(void* handle, uint64_t* epoch, uint64_t* cursor,
+                                              uint64_t* windows);
+struct SparCudaStatus spar_b200_batches_set_state(void* handle, uint64_t epoch, uint64_t cursor);
+void spar_b200_batches_destroy(void* handle);
+/* Host-only, no GPU: this rank's window start offsets (token index) of the batch at (epoch,     */
+/* cursor), its row counts and the cursor after it.                                              */
+struct SparCudaStatus spar_b200_batch_windows(uint64_t token_count, uint64_t sequence_length,
+                                              uint64_t stride, uint64_t batch_size, int shuffle,
+                                              uint64_t shuffle_seed, int drop_last, uint64_t epoch,
+                                              uint64_t cursor, int rank, int world,
+                                              uint64_t* starts, uint64_t* rows,
+                                              uint64_t* global_rows, uint64_t* next_cursor);
+
 /* Training checkpoints in Spar's SPARCKPT v1 format (src/checkpoint/checkpoint.cpp:18-475:    */
 /* save_training_checkpoint / load_training_checkpoint), family 1 only (the format stores a      */
 /* DecoderConfig): model parameters and AdamW moments by name, progress, RNG state, optimiser    */

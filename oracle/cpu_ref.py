@@ -35,6 +35,9 @@ def load():
             "ref_rmsnorm": [F, F, F, c_int64, c_int64, c_double, F, F, F],
             "ref_swiglu": [F, F, F, c_int64, F, F, F],
             "ref_attention": [F, F, F, F] + [c_int64] * 5 + [F, F, F, F],
+            "ref_batches": [c_char_p, POINTER(c_int64), c_int64, c_int64, c_int64, c_int64,
+                            c_int64, c_uint64, c_int64, c_int64, I32, POINTER(c_int64), I32,
+                            POINTER(c_int64), POINTER(c_int64)],
             "ref_spar_param_info": [c_int64] * 8 + [c_char_p, c_int64, POINTER(c_int64)],
             "ref_spar_ckpt_save": [c_char_p] + [c_int64] * 7 + [c_double] * 3 +
                                   [POINTER(F)] * 3 + [c_uint64] * 4 + [c_double] * 5,
@@ -253,6 +256,29 @@ def spar_ckpt_load(path, cfg: dict):
     _check(load().ref_spar_ckpt_load(str(path).encode(), arr(ps), arr(ms), arr(vs),
                                      *[ctypes.byref(x) for x in u], ctypes.byref(lr)))
     return ps, ms, vs, u[0].value, u[1].value, u[2].value, u[3].value, lr.value
+
+
+def batches(documents: list, seq: int, stride: int, batch: int, shuffle: bool, seed: int,
+            drop_last: bool, epochs: int):
+    """The reference's LMBatchIterator over its byte-level TokenizedCorpus of `documents`
+    (bytes): (corpus tokens int32, [batch arrays [rows, seq] int32 in order])."""
+    blob = b"".join(documents)
+    lens = (c_int64 * len(documents))(*[len(d) for d in documents])
+    ntok = len(blob) + len(documents)
+    windows = max(0, 1 + (ntok - seq) // stride) if ntok >= seq else 0
+    toks = np.empty(ntok, np.int32)
+    out = np.empty((max(1, windows * epochs), seq), np.int32)
+    rows = np.empty(max(1, windows * epochs), np.int64)
+    tc, nb = c_int64(), c_int64()
+    _check(load().ref_batches(blob, lens, len(documents), seq, stride, batch, int(shuffle), seed,
+                              int(drop_last), epochs, toks.ctypes.data_as(I32), ctypes.byref(tc),
+                              out.ctypes.data_as(I32), rows.ctypes.data_as(POINTER(c_int64)),
+                              ctypes.byref(nb)))
+    res, r0 = [], 0
+    for k in range(nb.value):
+        res.append(out[r0:r0 + rows[k]].copy())
+        r0 += rows[k]
+    return toks[:tc.value], res
 
 
 def _sample_worker(args):

@@ -467,6 +467,44 @@ int ref_spar_ckpt_load(const char* path, float** params, float** m, float** v,
   });
 }
 
+// data::LMBatchIterator over data::WindowDataset of the TokenizedCorpus of `ndocs` documents
+// (bytes `docs`, lengths `lens`) under the byte-level ByteBPETokenizer: the packed corpus tokens
+// (tokens_out, *token_count) and every batch of `epochs` epochs, rows concatenated in batches_out
+// ([sum rows, seq] int32), rows per batch in rows_out, *n_batches batches.
+int ref_batches(const char* docs, const int64_t* lens, int64_t ndocs, int64_t seq, int64_t stride,
+                int64_t batch, int64_t shuffle, uint64_t seed, int64_t drop_last, int64_t epochs,
+                int32_t* tokens_out, int64_t* token_count, int32_t* batches_out, int64_t* rows_out,
+                int64_t* n_batches) {
+  return guarded([&] {
+    std::vector<std::string> documents;
+    const char* p = docs;
+    for (int64_t i = 0; i < ndocs; ++i) {
+      documents.emplace_back(p, static_cast<std::size_t>(lens[i]));
+      p += lens[i];
+    }
+    tokenizer::ByteBPETokenizer tok;
+    data::TokenizedCorpus corpus{documents, tok};
+    const auto toks = corpus.tokens();
+    for (std::size_t i = 0; i < toks.size(); ++i) tokens_out[i] = static_cast<int32_t>(toks[i]);
+    *token_count = static_cast<int64_t>(toks.size());
+    data::WindowDataset windows{corpus, {static_cast<std::size_t>(seq), static_cast<std::size_t>(stride)}};
+    data::BatchConfig bc{static_cast<std::size_t>(batch), DType::Int32, shuffle != 0, seed,
+                         drop_last != 0};
+    data::LMBatchIterator it{windows, bc};
+    int64_t nb = 0, row = 0;
+    for (int64_t e = 0; e < epochs; ++e) {
+      if (e > 0) it.next_epoch();
+      while (auto b = it.next_batch()) {
+        const auto v = std::as_const(*b).span<int32_t>();
+        std::memcpy(batches_out + row * seq, v.data(), v.size() * sizeof(int32_t));
+        rows_out[nb++] = b->shape()[0];
+        row += b->shape()[0];
+      }
+    }
+    *n_batches = nb;
+  });
+}
+
 // Seconds for `iters` training steps (forward, loss, backward, clip, AdamW) of a one-block
 // decoder with the given dimensions on [1, t] token ids: the bounded CPU-baseline sample.
 double ref_train_sample_seconds(int64_t vocab, int64_t d, int64_t f, int64_t heads, int64_t t,

@@ -109,6 +109,15 @@ SIGNATURES = {
                                     POINTER(c_int32), p]),
     "spar_b200_lm_set_comm": (S, [p, p, i]),
     "spar_b200_lm_gather": (S, [p, i, p]),
+    "spar_b200_batches_create": (S, [p, u64, u64, u64, u64, i, u64, i, i, i, i,
+                                     POINTER(c_void_p)]),
+    "spar_b200_batches_next": (S, [p, p, POINTER(c_uint64), POINTER(c_uint64), p]),
+    "spar_b200_batches_next_epoch": (S, [p]),
+    "spar_b200_batches_state": (S, [p, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
+    "spar_b200_batches_set_state": (S, [p, u64, u64]),
+    "spar_b200_batches_destroy": (None, [p]),
+    "spar_b200_batch_windows": (S, [u64, u64, u64, u64, i, u64, i, u64, u64, i, i, p,
+                                    POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
     "spar_b200_lm_save_checkpoint": (S, [p, c_char_p, POINTER(SparB200Checkpoint)]),
     "spar_b200_lm_load_checkpoint": (S, [p, c_char_p, POINTER(SparB200Checkpoint)]),
     "spar_b200_checkpoint_write": (S, [c_char_p, POINTER(SparB200LMConfig),

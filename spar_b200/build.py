@@ -31,6 +31,7 @@ SOURCES = [
     "trainer.cu",
     "comm.cpp",
     "checkpoint.cpp",
+    "batches.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -57,3 +57,97 @@ def rank_share(seed: int, global_seqs: int, accum: int, seq: int, vocab: int, ra
     per = global_seqs // world
     mine = ids[rank * per:(rank + 1) * per]
     return np.ascontiguousarray(mine.reshape(accum, per // accum, seq).astype(np.int32))
+
+
+def batch_windows(token_count: int, seq: int, stride: int, batch: int, shuffle: bool, seed: int,
+                  drop_last: bool, epoch: int, cursor: int, rank: int = 0, world: int = 1):
+    """Host-only (no GPU): this rank's window start offsets of the batch at (epoch, cursor) of
+    Spar's LMBatchIterator order, the batch's row count and the cursor after it."""
+    import ctypes
+
+    from . import _lib
+
+    lib = _lib.load()
+    starts = np.empty(max(batch, 1), np.uint64)
+    rows, grows, nxt = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+    _lib.check("spar_b200_batch_windows",
+               lib.spar_b200_batch_windows(token_count, seq, stride, batch, int(shuffle), seed,
+                                           int(drop_last), epoch, cursor, rank, world,
+                                           starts.ctypes.data, ctypes.byref(rows),
+                                           ctypes.byref(grows), ctypes.byref(nxt)))
+    return starts[:rows.value].copy(), grows.value, nxt.value
+
+
+class BatchIterator:
+    """Spar's LMBatchIterator over a packed token corpus held in device memory: each `next`
+    gathers this rank's rows of the next batch as int32 ids [rows, seq] on the device."""
+
+    def __init__(self, tokens, seq: int, stride: int, batch: int, shuffle: bool = True,
+                 seed: int = 0, drop_last: bool = False, rank: int = 0, world: int = 1,
+                 device: int = 0):
+        import ctypes
+
+        from . import _lib
+
+        self.lib = _lib.load()
+        self.seq, self.device, self._batch = seq, device, batch
+        self.handle = None
+        toks = np.ascontiguousarray(tokens, np.int32)
+        h = ctypes.c_void_p()
+        _lib.check("spar_b200_batches_create",
+                   self.lib.spar_b200_batches_create(toks.ctypes.data, toks.size, seq, stride,
+                                                     batch, int(shuffle), seed, int(drop_last),
+                                                     rank, world, device, ctypes.byref(h)))
+        self.handle = h
+
+    def next(self, out=None):
+        """(ids tensor [rows, seq] on the device, or None at the end of the epoch)."""
+        import ctypes
+
+        import torch
+
+        from . import _lib
+
+        rows, grows = ctypes.c_uint64(), ctypes.c_uint64()
+        dev = torch.device("cuda", self.device)
+        buf = out if out is not None else torch.empty(self._batch, self.seq, dtype=torch.int32,
+                                                      device=dev)
+        _lib.check("spar_b200_batches_next",
+                   self.lib.spar_b200_batches_next(self.handle, buf.data_ptr(), ctypes.byref(rows),
+                                                   ctypes.byref(grows),
+                                                   torch.cuda.current_stream(dev).cuda_stream))
+        if grows.value == 0:
+            return None
+        return buf[:rows.value]
+
+    def next_epoch(self):
+        from . import _lib
+
+        _lib.check("spar_b200_batches_next_epoch", self.lib.spar_b200_batches_next_epoch(self.handle))
+
+    def state(self):
+        import ctypes
+
+        from . import _lib
+
+        e, c, w = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        _lib.check("spar_b200_batches_state", self.lib.spar_b200_batches_state(
+            self.handle, ctypes.byref(e), ctypes.byref(c), ctypes.byref(w)))
+        return e.value, c.value
+
+    def set_state(self, epoch: int, cursor: int):
+        from . import _lib
+
+        _lib.check("spar_b200_batches_set_state",
+                   self.lib.spar_b200_batches_set_state(self.handle, epoch, cursor))
+
+    def close(self):
+        if self.handle:
+            self.lib.spar_b200_batches_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
