@@ -329,3 +329,40 @@ def test_spar_family_checkpoint_exact_resume(cuda, tmp_path):
     b.close()
     assert la == lb
     assert np.array_equal(pa, pb)
+
+
+def test_spar_family_sharded_one_rank_matches_replicated(cuda, monkeypatch):
+    """The data-parallel path (bucket reduce-scatter, per-piece AdamW, parameter all-gather) with
+    the Spar-family runtime on a one-rank communicator: the same steps as without one."""
+    from spar_b200.lm import DecoderLM, LMConfig
+
+    monkeypatch.setenv("SPAR_B200_SHARD_OPT", "1")
+    c = dict(vocab=64, dim=128, hidden=256, layers=2, heads=4, kv_heads=1, qk_norm=0)
+    cfg = LMConfig(vocab=64, dim=128, hidden=256, layers=2, heads=4, seq=32, micro_batch=2,
+                   family=1, kv_heads=1)
+    ids = O.Random(0x5EED1501).bounded(4 * 2 * 32, 64).reshape(4, 2, 32).astype(np.int32)
+
+    def steps(with_comm):
+        lm = DecoderLM(cfg, 0)
+        lm.load_state_dict(O.spar_family_parameters(c, 0x5EED0501))
+        lib = comm = None
+        if with_comm:
+            lib, comm = _one_rank_comm()
+            lm.attach_comm(comm, 1)
+        out = [lm.train_step(ids, 3e-4, step=s) for s in range(1, 4)]
+        if with_comm:
+            lm.gather("param")
+        state = _flat(lm.state_dict(), lm.names)
+        lm.close()
+        if comm is not None:
+            lib.spar_b200_comm_destroy(comm, 0)
+        return out, state
+
+    a_out, a = steps(False)
+    b_out, b = steps(True)
+    assert [o[2] for o in b_out] == [(0, 0)] * 3
+    np.testing.assert_allclose([o[1] for o in a_out], [o[1] for o in b_out], rtol=1e-12)
+    if [o[1] for o in a_out] == [o[1] for o in b_out]:
+        assert [o[0] for o in a_out] == [o[0] for o in b_out] and np.array_equal(a, b)
+    else:
+        assert rel_l2(a, b) <= 1e-6
