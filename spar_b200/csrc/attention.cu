@@ -39,7 +39,11 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <queue>
+#include <tuple>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -77,6 +81,11 @@ struct AttnParams {
   // key / value head h / group; K and V start at columns kcol and vcol of each qkv / dqkv row
   // (group 1: kcol = model_dim, vcol = 2 * model_dim).
   uint32_t group, kv_heads, kv_bh, kcol, vcol;
+  // Backward work lists: CTA c processes items sched[sched[c] .. sched[c + 1]) of the item array
+  // at sched + grid + 1 (an item idx decodes as tile idx / bh, (batch, head) idx % bh); built on
+  // the host by longest-processing-time-first over the items' costs (see backward_schedule).
+  const uint32_t* sched;
+  uint32_t sched_grid;
   uint64_t ld_o;  // row stride of O and dO
   float scale, scale_log2;
   uint32_t tiles;  // stationary tiles per (batch, head)
@@ -139,6 +148,13 @@ __device__ __forceinline__ void inverse_rope(float (&o)[32], const float2* tab) 
 struct Item {
   uint32_t b, h, t;
 };
+
+// Backward item list of this CTA: [begin, end) into the schedule, and the k-th item there.
+__device__ __forceinline__ uint32_t sched_begin(const AttnParams& p) { return p.sched[blockIdx.x]; }
+__device__ __forceinline__ uint32_t sched_end(const AttnParams& p) { return p.sched[blockIdx.x + 1]; }
+__device__ __forceinline__ uint32_t sched_item(const AttnParams& p, uint32_t k) {
+  return p.sched[p.sched_grid + 1 + k];
+}
 
 // Key-side items of the backward: (batch, key/value head, 128-key tile).
 __device__ __forceinline__ Item decode_kv(const AttnParams& p, uint32_t idx) {
@@ -699,8 +715,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       uint32_t n = 0, item = 0, st = 0, ph = 0;
       int last_q = -1, last_kv[L::kStages];
       for (uint32_t i = 0; i < L::kStages; ++i) last_kv[i] = -1;
-      for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
-        const Item it = decode(p, idx, true);
+      for (uint32_t k = sched_begin(p); k < sched_end(p) && !*abort_flag; ++k, ++item) {
+        const uint32_t idx = sched_item(p, k);
+        const Item it = decode(p, idx, false);
         const int hc = static_cast<int>(it.h * DH), b = static_cast<int>(it.b);
         const int kvc = static_cast<int>(it.h / p.group * DH);
         const int kc = static_cast<int>(p.kcol) + kvc, vc = static_cast<int>(p.vcol) + kvc;
@@ -770,8 +787,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
         ++sn;
         return true;
       };
-      for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x, ++item) {
-        const Item it = decode(p, idx, true);
+      for (uint32_t k = sched_begin(p); k < sched_end(p) && ok && !*abort_flag; ++k, ++item) {
+        const uint32_t idx = sched_item(p, k);
+        const Item it = decode(p, idx, false);
         const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
         if (!(ok = wait_or_abort(q_full, item & 1, abort_flag))) break;
         tc::tc_fence_after();
@@ -810,8 +828,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
     uint8_t* dsbuf = smem + L::kDS;
     uint32_t sn = 0, item = 0;
     bool ok = true;
-    for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
-      const Item it = decode(p, idx, true);
+    for (uint32_t k = sched_begin(p); k < sched_end(p) && ok; ++k, ++item) {
+        const uint32_t idx = sched_item(p, k);
+      const Item it = decode(p, idx, false);
       const uint32_t nkv = (min(seq, it.t * 128 + 128) + 63) / 64;
       const uint32_t q = it.t * 128 + r;
       const bool valid = q < seq;
@@ -971,7 +990,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
     if (tc::elect_one()) {
       uint32_t n = 0, item = 0;
       int last_kv = -1, last_kq[2] = {-1, -1}, last_mn[2] = {-1, -1};
-      for (uint32_t idx = blockIdx.x; idx < p.total && !*abort_flag; idx += gridDim.x, ++item) {
+      for (uint32_t k = sched_begin(p); k < sched_end(p) && !*abort_flag; ++k, ++item) {
+        const uint32_t idx = sched_item(p, k);
         const Item it = decode_kv(p, idx);  // it.h: the key / value head
         const int b = static_cast<int>(it.b);
         const int kc = static_cast<int>(p.kcol + it.h * DH), vc = static_cast<int>(p.vcol + it.h * DH);
@@ -1050,7 +1070,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         ++sn;
         return true;
       };
-      for (uint32_t idx = blockIdx.x; idx < p.total && ok && !*abort_flag; idx += gridDim.x, ++item) {
+      for (uint32_t k = sched_begin(p); k < sched_end(p) && ok && !*abort_flag; ++k, ++item) {
+        const uint32_t idx = sched_item(p, k);
         const Item it = decode_kv(p, idx);
         // >= 1 query tile per head (every 128-key tile starts below seq), for each head of the group
         const uint32_t steps = (nq_all - 2 * it.t) * p.group;
@@ -1103,7 +1124,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       const uint32_t q = q0 + (u & 63);
       return (u < 192 && q < seq) ? __ldg(src + sbase + q) : 0.f;
     };
-    for (uint32_t idx = blockIdx.x; idx < p.total && ok; idx += gridDim.x, ++item) {
+    for (uint32_t k = sched_begin(p); k < sched_end(p) && ok; ++k, ++item) {
+        const uint32_t idx = sched_item(p, k);
       const Item it = decode_kv(p, idx);
       const uint32_t i0 = 2 * it.t;
       const uint32_t per_head = nq_all - i0;
@@ -1235,9 +1257,81 @@ cudaError_t launch_attn(K kernel, uint32_t smem, const AttnParams& p, int device
     if (e != cudaSuccess) return e;
     configured[device] = true;
   }
-  const unsigned grid = std::min<uint32_t>(p.total, static_cast<uint32_t>(sm_count(device)));
+  const unsigned grid =
+      p.sched ? p.sched_grid : std::min<uint32_t>(p.total, static_cast<uint32_t>(sm_count(device)));
   if (grid == 0) return cudaSuccess;
   return launch(kernel, dim3(grid), dim3(kThreads), smem, stream, p);
+}
+
+// Work lists for the persistent backward kernels, longest processing time first: the items
+// (tile, batch-head) are sorted by cost (the 64-row steps the item loops over: key tiles up to the
+// query tile's end for the query kernel, query tiles from the key tile on times the query group for
+// the key kernel), then each goes to the CTA with the least cost assigned so far. Round-robin over
+// tiles in cost order left CTAs with one heavy and one medium item beside others with one light
+// item (at 2 sequences x 16 heads x 8 tiles, 24 steps on the busiest CTA against 15.6 on average).
+// That is for the two kernels run one after the other (18 % faster at 2 x 16 x 1024 x 64). When
+// they run side by side on two streams (lpt = false, the training runtime), the CTAs that finish
+// early in cost-ordered round robin hand their SMs to the other kernel, which measured as good or
+// slightly better than balanced lists, so that order is kept there.
+// Stored as CSR in device memory [grid + 1 offsets | items], built once per (device, side, shape,
+// kind): the first backward call of a shape allocates, so make it before any stream capture.
+cudaError_t backward_schedule(int device, bool key_side, uint32_t bh, uint32_t tiles, uint32_t seq,
+                              uint32_t group, bool lpt, const uint32_t** out, uint32_t* grid_out) {
+  using Key = std::tuple<int, bool, uint32_t, uint32_t, uint32_t, uint32_t, bool>;
+  static std::mutex mu;
+  static std::map<Key, std::pair<uint32_t*, uint32_t>> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const Key key{device, key_side, bh, tiles, seq, group, lpt};
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    const uint32_t total = bh * tiles;
+    const uint32_t grid = std::min<uint32_t>(total, static_cast<uint32_t>(sm_count(device)));
+    const uint32_t nq_all = (seq + 63) / 64;
+    auto cost = [&](uint32_t t) -> uint64_t {
+      if (key_side) return static_cast<uint64_t>(nq_all - 2 * t) * group;
+      return (std::min<uint64_t>(seq, 128ull * t + 128) + 63) / 64;
+    };
+    std::vector<uint32_t> items(total);
+    for (uint32_t i = 0; i < total; ++i) items[i] = i;
+    std::stable_sort(items.begin(), items.end(), [&](uint32_t a, uint32_t b) {
+      return cost(a / bh) > cost(b / bh);
+    });
+    using Slot = std::pair<uint64_t, uint32_t>;  // (assigned cost, cta)
+    std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> heap;
+    for (uint32_t c = 0; c < grid; ++c) heap.push({0, c});
+    std::vector<std::vector<uint32_t>> lists(grid);
+    for (uint32_t k = 0; k < total; ++k) {  // !lpt: CTA c takes items c, c + grid, ...
+      const uint32_t i = items[k];
+      if (!lpt) {
+        lists[k % grid].push_back(i);
+        continue;
+      }
+      Slot sl = heap.top();
+      heap.pop();
+      lists[sl.second].push_back(i);
+      sl.first += cost(i / bh);
+      heap.push(sl);
+    }
+    std::vector<uint32_t> host(grid + 1 + total);
+    uint32_t pos = 0;
+    for (uint32_t c = 0; c < grid; ++c) {
+      host[c] = pos;
+      for (uint32_t i : lists[c]) host[grid + 1 + pos++] = i;
+    }
+    host[grid] = pos;
+    uint32_t* dev = nullptr;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&dev), host.size() * sizeof(uint32_t));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(dev, host.data(), host.size() * sizeof(uint32_t), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(dev);
+      return e;
+    }
+    it = cache.emplace(key, std::make_pair(dev, grid)).first;
+  }
+  *out = it->second.first;
+  *grid_out = it->second.second;
+  return cudaSuccess;
 }
 
 void base_params(AttnParams& p, uint64_t batch, uint64_t seq, uint64_t heads, uint64_t head_dim,
@@ -1320,6 +1414,15 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
   if (e != cudaSuccess) return e;
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
   p.total = p.tiles * p.bh;
+  AttnParams pk = p;  // the key kernel's items: one per key / value head
+  pk.total = p.tiles * p.kv_bh;
+  const bool side_by_side = key_stream && fork && join;
+  e = backward_schedule(device, false, p.bh, p.tiles, p.seq, p.group, !side_by_side, &p.sched,
+                        &p.sched_grid);
+  if (e == cudaSuccess)
+    e = backward_schedule(device, true, pk.kv_bh, pk.tiles, pk.seq, pk.group, !side_by_side,
+                          &pk.sched, &pk.sched_grid);
+  if (e != cudaSuccess) return e;
   // The query and key kernels only share inputs (they write dq and dk / dv): on a second stream
   // the key kernel's CTAs take the SMs that the query kernel's last items leave idle.
   cudaStream_t ks = stream;
@@ -1333,9 +1436,8 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
           ? launch_attn(attn_bwd_q_kernel<64>, BwdQ<64>::kSmem, p, device, stream, q64)
           : launch_attn(attn_bwd_q_kernel<32>, BwdQ<32>::kSmem, p, device, stream, q32);
   if (e != cudaSuccess) return e;
-  p.total = p.tiles * p.kv_bh;  // key-side items: one per key / value head
-  e = head_dim == 64 ? launch_attn(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, p, device, ks, k64)
-                     : launch_attn(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, p, device, ks, k32);
+  e = head_dim == 64 ? launch_attn(attn_bwd_kv_kernel<64>, BwdKV<64>::kSmem, pk, device, ks, k64)
+                     : launch_attn(attn_bwd_kv_kernel<32>, BwdKV<32>::kSmem, pk, device, ks, k32);
   if (e != cudaSuccess || ks == stream) return e;
   e = cudaEventRecord(join, ks);
   return e == cudaSuccess ? cudaStreamWaitEvent(stream, join, 0) : e;
