@@ -54,7 +54,13 @@ class LMConfig:
     def flops_per_token(self) -> float:
         """6 * matmul params + attention (12 * L * d * T, half of it under the causal mask is
         skipped by the kernels but counted here as the standard estimate)."""
-        n_mm = self.layers * (4 * self.dim * self.dim + 2 * self.dim * self.hidden) + self.vocab * self.dim
+        if self.family == 1:  # q | k | v with kv_heads, out, gate | up | down
+            kvh = self.kv_heads or self.heads
+            qkv = self.dim * (self.dim + 2 * kvh * (self.dim // self.heads))
+            per_layer = qkv + self.dim * self.dim + 3 * self.dim * self.hidden
+        else:
+            per_layer = 4 * self.dim * self.dim + 2 * self.dim * self.hidden
+        n_mm = self.layers * per_layer + self.vocab * self.dim
         return 6.0 * n_mm + 12.0 * self.layers * self.dim * self.seq
 
 
