@@ -32,6 +32,7 @@ SOURCES = [
     "comm.cpp",
     "checkpoint.cpp",
     "batches.cu",
+    "qknorm.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -114,6 +114,21 @@ cudaError_t rmsnorm_backward_launch(float* dx, float* dweight, const float* dy, 
                                     uint64_t cols, int accumulate_params, int accumulate_dx,
                                     float* workspace, int device, cudaStream_t stream,
                                     uint64_t ld = 0, uint32_t group = 1);
+// qk-norm + RoPE of the Spar-family projection (qknorm.cu): out (q | k | v rows of ld floats,
+// TF32-rounded) from raw; rstd [tokens * heads] then [tokens * kv_heads]; rope_table may be null.
+cudaError_t qk_norm_rope_launch(float* out, const float* raw, uint64_t tokens, uint64_t seq,
+                                uint64_t heads, uint64_t kv_heads, uint64_t head_dim, uint64_t ld,
+                                const float* wq, const float* wk, float* rstd,
+                                const float* rope_table, float eps, int device,
+                                cudaStream_t stream);
+// Backward in place over the dq | dk part of dqk; dwq / dwk (+)= the weight gradients; workspace
+// qk_norm_backward_parts(tokens) * 2 * head_dim floats.
+int qk_norm_backward_parts(uint64_t tokens, int device);
+cudaError_t qk_norm_backward_launch(float* dqk, const float* raw, uint64_t tokens, uint64_t heads,
+                                    uint64_t kv_heads, uint64_t head_dim, uint64_t ld,
+                                    const float* wq, const float* wk, const float* rstd,
+                                    float* dwq, float* dwk, int accumulate, float* workspace,
+                                    int device, cudaStream_t stream);
 // SwiGLU h = silu(gate) * value and its backward over rows x cols with row strides (floats).
 cudaError_t swiglu_forward_launch(float* h, uint64_t ldh, const float* gate, uint64_t ldg,
                                   const float* value, uint64_t ldv, uint64_t rows, uint64_t cols,

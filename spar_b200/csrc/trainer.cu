@@ -92,20 +92,6 @@ __global__ void add_lanes_kernel(float4* __restrict__ a, const float4* __restric
   }
 }
 
-// dst[r * ld + c] = src[r * ld + c] rounded to nearest TF32 for c < cols (the value part of the
-// projection after the q / k norms: it only feeds tensor-core products).
-__global__ void copy_round_kernel(float* __restrict__ dst, const float* __restrict__ src,
-                                  uint64_t rows, uint64_t cols, uint64_t ld) {
-  pdl_begin();
-  const uint64_t total = rows * cols;
-  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += stride) {
-    const uint64_t r = i / cols, c = i - r * cols;
-    dst[r * ld + c] = round_tf32(src[r * ld + c]);
-  }
-}
-
 __global__ void fill_kernel(float* dst, uint64_t n, float v) {
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
@@ -1032,23 +1018,14 @@ cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1,
                   nullptr, nullptr, nullptr, true, cfg.use_rope != 0));
   } else {
-    // The q / k norms come before RoPE (attention.cpp:212-215): project, normalise each head
-    // into qkv, copy v, then rotate q and k (rounded to nearest TF32).
-    launches += 3 + (cfg.use_rope ? 1 : 0);
-    const float qeps = static_cast<float>(cfg.qk_norm_epsilon);
+    // The q / k norms come before RoPE (attention.cpp:212-215): project, then one pass per
+    // token normalises each q / k head, rotates it and writes q | k | v rounded to TF32.
+    launches += 1;
     SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, P + lo.wqkv, Wq, false, A.qkv_raw, Wq, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
-    SPAR_TRY(rmsnorm_forward_launch(A.qkv, A.qk_rstd, A.qkv_raw, P + lo.qn, N * H, dh, qeps,
-                                    device, s, Wq, static_cast<uint32_t>(H)));
-    SPAR_TRY(rmsnorm_forward_launch(A.qkv + H * dh, A.qk_rstd + N * H, A.qkv_raw + H * dh,
-                                    P + lo.kn, N * KVH, dh, qeps, device, s, Wq,
-                                    static_cast<uint32_t>(KVH)));
-    const uint64_t vc = (H + KVH) * dh;
-    SPAR_TRY(launch(copy_round_kernel, dim3(grid_for(N * KVH * dh, 256, sm_count(device) * 8)),
-                    dim3(256), 0, s, A.qkv + vc, static_cast<const float*>(A.qkv_raw + vc), N,
-                    KVH * dh, Wq));
-    if (cfg.use_rope)
-      SPAR_TRY(rope_apply_launch(A.qkv, rope_tab, N, T, H + KVH, dh, Wq, 0, device, s, 1));
+    SPAR_TRY(qk_norm_rope_launch(A.qkv, A.qkv_raw, N, T, H, KVH, dh, Wq, P + lo.qn, P + lo.kn,
+                                 A.qk_rstd, cfg.use_rope ? rope_tab : nullptr,
+                                 static_cast<float>(cfg.qk_norm_epsilon), device, s));
   }
   SPAR_TRY(attention_forward(A, s));
   SPAR_TRY(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
@@ -1068,7 +1045,7 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
   const LayerOffsets& lo = lay[l];
   float* P = params;
   float* G = grads;
-  launches += 2 * 2 + 1 + 1 + (qk_norm ? 4 : 0);  // RMSNorm bwd, attention, SwiGLU bwd, qk norms
+  launches += 2 * 2 + 1 + 1 + (qk_norm ? 2 : 0);  // RMSNorm bwd, attention, SwiGLU bwd, qk norms
   const bool conc = wgrad_enabled && !profiling;
   cudaStream_t w = conc ? wgrad_stream : s;
   auto fork = [&](int i) -> cudaError_t {
@@ -1106,13 +1083,9 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
                 true));
   // attention: dctx (dtmp) -> dqkv, dq / dk already rotated back through RoPE
   SPAR_TRY(attention_backward(A, s));
-  if (qk_norm) {  // through the q / k norms, in place (weight gradients accumulate)
-    SPAR_TRY(rmsnorm_backward_launch(dqkv, G + lo.qn, dqkv, A.qkv_raw, P + lo.qn, A.qk_rstd, N * H,
-                                     dh, 1, 0, ln_ws, device, s, Wq, static_cast<uint32_t>(H)));
-    SPAR_TRY(rmsnorm_backward_launch(dqkv + H * dh, G + lo.kn, dqkv + H * dh, A.qkv_raw + H * dh,
-                                     P + lo.kn, A.qk_rstd + N * H, N * KVH, dh, 1, 0, ln_ws,
-                                     device, s, Wq, static_cast<uint32_t>(KVH)));
-  }
+  if (qk_norm)  // through the q / k norms, in place (weight gradients accumulate)
+    SPAR_TRY(qk_norm_backward_launch(dqkv, A.qkv_raw, N, H, KVH, dh, Wq, P + lo.qn, P + lo.kn,
+                                     A.qk_rstd, G + lo.qn, G + lo.kn, 1, ln_ws, device, s));
   SPAR_TRY(fork(3));
   SPAR_TRY(gemm(d, Wq, N, A.a1, d, true, dqkv, Wq, false, G + lo.wqkv, Wq, true,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, w));
