@@ -418,6 +418,11 @@ struct SparCudaStatus spar_b200_batch_windows(uint64_t token_count, uint64_t seq
                                               uint64_t* starts, uint64_t* rows,
                                               uint64_t* global_rows, uint64_t* next_cursor);
 
+/* data::split_documents (src/data/batch_iterator.cpp:144-162), host-only: `order` receives the  */
+/* document_count indices in Spar's shuffled order; the first validation_count are validation.   */
+struct SparCudaStatus spar_b200_split_documents(uint64_t document_count, uint64_t validation_count,
+                                                uint64_t seed, uint64_t* order);
+
 /* Training checkpoints in Spar's SPARCKPT v1 format (src/checkpoint/checkpoint.cpp:18-475:    */
 /* save_training_checkpoint / load_training_checkpoint), family 1 only (the format stores a      */
 /* DecoderConfig): model parameters and AdamW moments by name, progress, RNG state, optimiser    */

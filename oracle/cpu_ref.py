@@ -35,6 +35,7 @@ def load():
             "ref_rmsnorm": [F, F, F, c_int64, c_int64, c_double, F, F, F],
             "ref_swiglu": [F, F, F, c_int64, F, F, F],
             "ref_attention": [F, F, F, F] + [c_int64] * 5 + [F, F, F, F],
+            "ref_split_documents": [c_int64, c_int64, c_uint64, POINTER(c_int64)],
             "ref_batches": [c_char_p, POINTER(c_int64), c_int64, c_int64, c_int64, c_int64,
                             c_int64, c_uint64, c_int64, c_int64, I32, POINTER(c_int64), I32,
                             POINTER(c_int64), POINTER(c_int64)],
@@ -256,6 +257,14 @@ def spar_ckpt_load(path, cfg: dict):
     _check(load().ref_spar_ckpt_load(str(path).encode(), arr(ps), arr(ms), arr(vs),
                                      *[ctypes.byref(x) for x in u], ctypes.byref(lr)))
     return ps, ms, vs, u[0].value, u[1].value, u[2].value, u[3].value, lr.value
+
+
+def split_documents(count: int, validation: int, seed: int):
+    """The reference's data::split_documents: (train indices, validation indices)."""
+    out = np.empty(max(count, 1), np.int64)
+    _check(load().ref_split_documents(count, validation, seed,
+                                      out.ctypes.data_as(POINTER(c_int64))))
+    return out[validation:count], out[:validation]
 
 
 def batches(documents: list, seq: int, stride: int, batch: int, shuffle: bool, seed: int,

@@ -505,6 +505,17 @@ int ref_batches(const char* docs, const int64_t* lens, int64_t ndocs, int64_t se
   });
 }
 
+// data::split_documents: validation indices then training indices into `out`.
+int ref_split_documents(int64_t count, int64_t validation, uint64_t seed, int64_t* out) {
+  return guarded([&] {
+    const auto split = data::split_documents(static_cast<std::size_t>(count),
+                                             static_cast<std::size_t>(validation), seed);
+    std::size_t k = 0;
+    for (std::size_t i : split.validation_indices) out[k++] = static_cast<int64_t>(i);
+    for (std::size_t i : split.train_indices) out[k++] = static_cast<int64_t>(i);
+  });
+}
+
 // Seconds for `iters` training steps (forward, loss, backward, clip, AdamW) of a one-block
 // decoder with the given dimensions on [1, t] token ids: the bounded CPU-baseline sample.
 double ref_train_sample_seconds(int64_t vocab, int64_t d, int64_t f, int64_t heads, int64_t t,

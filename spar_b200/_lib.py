@@ -116,6 +116,7 @@ SIGNATURES = {
     "spar_b200_batches_state": (S, [p, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
     "spar_b200_batches_set_state": (S, [p, u64, u64]),
     "spar_b200_batches_destroy": (None, [p]),
+    "spar_b200_split_documents": (S, [u64, u64, u64, p]),
     "spar_b200_batch_windows": (S, [u64, u64, u64, u64, i, u64, i, u64, u64, i, i, p,
                                     POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
     "spar_b200_lm_save_checkpoint": (S, [p, c_char_p, POINTER(SparB200Checkpoint)]),

@@ -52,14 +52,23 @@ uint64_t bounded_index(SplitMix& r, uint64_t bound) {
   return v % bound;
 }
 
+// Fisher-Yates over iota(n) with a Random seeded `seed` (batch_iterator.cpp:34-40).
+void shuffled(std::vector<uint64_t>& order, uint64_t n, uint64_t seed) {
+  order.resize(n);
+  std::iota(order.begin(), order.end(), uint64_t{0});
+  SplitMix r{seed};
+  for (uint64_t remaining = n; remaining > 1; --remaining)
+    std::swap(order[remaining - 1], order[bounded_index(r, remaining)]);
+}
+
 void epoch_order(std::vector<uint64_t>& order, uint64_t windows, bool shuffle, uint64_t seed,
                  uint64_t epoch) {
+  if (shuffle) {
+    shuffled(order, windows, derive_epoch_seed(seed, epoch));
+    return;
+  }
   order.resize(windows);
   std::iota(order.begin(), order.end(), uint64_t{0});
-  if (!shuffle) return;
-  SplitMix r{derive_epoch_seed(seed, epoch)};
-  for (uint64_t remaining = windows; remaining > 1; --remaining)
-    std::swap(order[remaining - 1], order[bounded_index(r, remaining)]);
 }
 
 // This rank's rows of the batch starting at `cursor`: window starts into `starts`; returns the
@@ -251,5 +260,18 @@ extern "C" SparCudaStatus spar_b200_batch_windows(uint64_t token_count, uint64_t
   if (*rows && !starts) return invalid();
   for (uint64_t r = r0; r < r1; ++r) starts[r - r0] = order[cursor + r] * stride;
   *next_cursor = *global_rows ? cursor + *global_rows : windows;
+  return ok();
+}
+
+// data::split_documents (batch_iterator.cpp:144-162): the document indices shuffled by Random(seed);
+// the first validation_count are the validation documents, the rest (in that order) the training
+// ones. order: document_count entries. Host-only.
+extern "C" SparCudaStatus spar_b200_split_documents(uint64_t document_count,
+                                                    uint64_t validation_count, uint64_t seed,
+                                                    uint64_t* order) {
+  if (validation_count > document_count || (document_count && !order)) return invalid();
+  std::vector<uint64_t> o;
+  shuffled(o, document_count, seed);
+  if (document_count) std::memcpy(order, o.data(), document_count * sizeof(uint64_t));
   return ok();
 }

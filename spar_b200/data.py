@@ -78,6 +78,18 @@ def batch_windows(token_count: int, seq: int, stride: int, batch: int, shuffle: 
     return starts[:rows.value].copy(), grows.value, nxt.value
 
 
+def split_documents(document_count: int, validation_count: int, seed: int):
+    """Spar's data::split_documents: (train indices, validation indices)."""
+    from . import _lib
+
+    order = np.empty(max(document_count, 1), np.uint64)
+    _lib.check("spar_b200_split_documents",
+               _lib.load().spar_b200_split_documents(document_count, validation_count, seed,
+                                                     order.ctypes.data))
+    order = order[:document_count].astype(np.int64)
+    return order[validation_count:], order[:validation_count]
+
+
 class BatchIterator:
     """Spar's LMBatchIterator over a packed token corpus held in device memory: each `next`
     gathers this rank's rows of the next batch as int32 ids [rows, seq] on the device."""

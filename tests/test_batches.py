@@ -56,6 +56,17 @@ def test_rank_shares_partition_each_batch():
         assert len(got) == len(ref) and all(np.array_equal(a, b) for a, b in zip(got, ref))
 
 
+@pytest.mark.skipif(not cpu_ref.available(), reason="oracle/_ref not built here")
+@pytest.mark.parametrize("count,validation,seed", [(10, 3, 1), (1, 0, 5), (0, 0, 9),
+                                                   (1000, 100, 0x5EED), (7, 7, 2)])
+def test_split_documents_matches_reference(count, validation, seed):
+    from spar_b200.data import split_documents
+
+    got = split_documents(count, validation, seed)
+    ref = cpu_ref.split_documents(count, validation, seed)
+    assert all(np.array_equal(a, b) for a, b in zip(got, ref))
+
+
 @pytest.mark.gpu
 def test_device_batches_match_host_order(cuda):
     """The device iterator (resident corpus, window gather kernel) gives the host-order batches,
