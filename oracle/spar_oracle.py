@@ -545,6 +545,105 @@ def lm_forward_backward(params, ids, cfg, dtype=np.float64):
     return float(loss), grads
 
 
+def spar_lm_forward_backward(params, ids, cfg, dtype=np.float64):
+    """One forward + backward of Spar's own nn::DecoderLM (decoder.cpp:73-90; TransformerBlock
+    transformer.cpp:53-69 with RMSNorm pre-norms; SelfAttention attention.cpp:188-225 without
+    biases, num_kv_heads key/value heads repeated over query groups (repeat_kv_heads :77-94), q /
+    k RMSNorm(head_dim) before RoPE when qk_norm; SwiGLUMLP mlp.cpp:33-46: down(silu(gate) * up);
+    final RMSNorm, tied logits) and the LM cross-entropy. Returns (loss, grads dict)."""
+    v, d, f, layers, heads = cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"]
+    kvh = cfg.get("kv_heads") or heads
+    eps, qeps = cfg.get("eps", 1e-5), cfg.get("qk_eps", 1e-6)
+    qk = bool(cfg.get("qk_norm"))
+    b, t = ids.shape
+    dh = d // heads
+    group = heads // kvh
+    scale = 1.0 / math.sqrt(dh)
+    P = {k: np.asarray(val, dtype) for k, val in params.items()}
+    cos, sin = rope_table(t, dh, cfg.get("rope_theta", 10000.0))
+    cos, sin = cos.astype(dtype), sin.astype(dtype)
+    E = P["token_embedding.weight"]
+    h = E[ids.reshape(-1)]
+
+    def rms(x, w, e):
+        return x / np.sqrt((x * x).mean(-1, keepdims=True) + e) * w
+
+    def heads_of(x, n):  # [BT, n dh] -> [B, n, T, dh]
+        return x.reshape(b, t, n, dh).transpose(0, 2, 1, 3)
+
+    def merge(x):  # [B, n, T, dh] -> [BT, n dh]
+        return x.transpose(0, 2, 1, 3).reshape(b * t, -1)
+
+    mask = np.triu(np.ones((t, t), dtype=bool), 1)
+    cache = []
+    for i in range(layers):
+        pre = f"blocks.{i}."
+        x = h
+        a = rms(x, P[pre + "attention_norm.weight"], eps)
+        qr = heads_of(a @ P[pre + "attention.q_proj.weight"], heads)
+        kr = heads_of(a @ P[pre + "attention.k_proj.weight"], kvh)
+        vh = heads_of(a @ P[pre + "attention.v_proj.weight"], kvh)
+        qn = rms(qr, P[pre + "attention.q_norm.weight"], qeps) if qk else qr
+        kn = rms(kr, P[pre + "attention.k_norm.weight"], qeps) if qk else kr
+        qh, kh = rope_apply(qn, cos, sin), rope_apply(kn, cos, sin)
+        kx, vx = np.repeat(kh, group, axis=1), np.repeat(vh, group, axis=1)
+        sc = np.where(mask, -np.inf, (qh @ kx.transpose(0, 1, 3, 2)) * scale)
+        pr = np.exp(sc - sc.max(-1, keepdims=True))
+        pr = pr / pr.sum(-1, keepdims=True)
+        ctx = merge(pr @ vx)
+        h1 = x + ctx @ P[pre + "attention.out_proj.weight"]
+        a2 = rms(h1, P[pre + "mlp_norm.weight"], eps)
+        gate = a2 @ P[pre + "mlp.gate_proj.weight"]
+        up = a2 @ P[pre + "mlp.up_proj.weight"]
+        hid = swiglu_forward(gate, up, dtype)
+        h = h1 + hid @ P[pre + "mlp.down_proj.weight"]
+        cache.append((x, a, qr, kr, qh, kh, vh, kx, vx, pr, ctx, h1, a2, gate, up, hid))
+    hf = rms(h, P["final_norm.weight"], eps)
+    logits = hf @ E.T
+    rows, targets = lm_targets(ids)
+    loss, _, dlogits = cross_entropy_forward_backward(logits, targets, rows, dtype)
+
+    grads = {name: np.zeros_like(val) for name, val in P.items()}
+    grads["token_embedding.weight"] += dlogits.T @ hf
+    dres, dwf = rms_norm_backward(dlogits @ E, h, P["final_norm.weight"], eps, dtype)
+    grads["final_norm.weight"] += dwf
+    group_sum = lambda z: z.reshape(b, kvh, group, t, dh).sum(axis=2)  # noqa: E731
+    for i in reversed(range(layers)):
+        pre = f"blocks.{i}."
+        x, a, qr, kr, qh, kh, vh, kx, vx, pr, ctx, h1, a2, gate, up, hid = cache[i]
+        grads[pre + "mlp.down_proj.weight"] += hid.T @ dres
+        dgate, dup = swiglu_backward(dres @ P[pre + "mlp.down_proj.weight"].T, gate, up, dtype)
+        grads[pre + "mlp.gate_proj.weight"] += a2.T @ dgate
+        grads[pre + "mlp.up_proj.weight"] += a2.T @ dup
+        da2 = dgate @ P[pre + "mlp.gate_proj.weight"].T + dup @ P[pre + "mlp.up_proj.weight"].T
+        dx2, dw2 = rms_norm_backward(da2, h1, P[pre + "mlp_norm.weight"], eps, dtype)
+        grads[pre + "mlp_norm.weight"] += dw2
+        dh1 = dres + dx2
+        grads[pre + "attention.out_proj.weight"] += ctx.T @ dh1
+        dctx = heads_of(dh1 @ P[pre + "attention.out_proj.weight"].T, heads)
+        dpr = dctx @ vx.transpose(0, 1, 3, 2)
+        dvh = group_sum(pr.transpose(0, 1, 3, 2) @ dctx)
+        ds = pr * (dpr - (dpr * pr).sum(-1, keepdims=True)) * scale
+        dqn = rope_apply(ds @ kx, cos, sin, inverse=True)
+        dkn = rope_apply(group_sum(ds.transpose(0, 1, 3, 2) @ qh), cos, sin, inverse=True)
+        if qk:
+            dqr, dwq = rms_norm_backward(dqn, qr, P[pre + "attention.q_norm.weight"], qeps, dtype)
+            dkr, dwk = rms_norm_backward(dkn, kr, P[pre + "attention.k_norm.weight"], qeps, dtype)
+            grads[pre + "attention.q_norm.weight"] += dwq
+            grads[pre + "attention.k_norm.weight"] += dwk
+        else:
+            dqr, dkr = dqn, dkn
+        da = np.zeros_like(a)
+        for proj, dy in (("q_proj", merge(dqr)), ("k_proj", merge(dkr)), ("v_proj", merge(dvh))):
+            grads[pre + f"attention.{proj}.weight"] += a.T @ dy
+            da += dy @ P[pre + f"attention.{proj}.weight"].T
+        dx1, dw1 = rms_norm_backward(da, x, P[pre + "attention_norm.weight"], eps, dtype)
+        grads[pre + "attention_norm.weight"] += dw1
+        dres = dh1 + dx1
+    np.add.at(grads["token_embedding.weight"], ids.reshape(-1), dres)
+    return float(loss), grads
+
+
 def lm_train_step(params, moments, ids_list, cfg, step, lr, opt, dtype=np.float64):
     """One optimiser step with gradient accumulation over the micro-batches in ids_list: grads
     summed over micro-steps of the per-micro-batch mean loss divided by the micro-step count,

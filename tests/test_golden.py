@@ -325,6 +325,25 @@ def test_oracle_spar_family_names_match_reference_fixture():
     assert sorted(k[len("grad/"):] for k in f if k.startswith("grad/")) == sorted(names)
 
 
+def test_oracle_spar_family_step_matches_reference_fixture():
+    """The float64 restatement of nn::DecoderLM's step (spar_lm_forward_backward) against the
+    reference's own fp32 step: loss, norm, every gradient's norm and the sampled gradients."""
+    f = load("lm_spar")
+    params = O.spar_family_parameters(SPAR_FAMILY, 0x5EED0301)
+    total, loss = None, 0.0
+    for ids in f["ids"]:
+        lo, g = O.spar_lm_forward_backward(params, ids, SPAR_FAMILY)
+        loss += lo / len(f["ids"])
+        total = g if total is None else {k: total[k] + g[k] for k in g}
+    grads = {k: v / len(f["ids"]) for k, v in total.items()}
+    assert abs(loss - f["loss"]) <= TOL * abs(f["loss"])
+    assert abs(O.global_grad_norm(list(grads.values())) - f["norm"]) <= TOL * f["norm"]
+    for n, gr in grads.items():
+        gn = float(f["gnorm/" + n])
+        assert abs(np.linalg.norm(gr) - gn) <= 1e-4 * gn + 1e-12, n
+        assert rel_l2(gr.ravel()[f["idx/" + n]], f["grad/" + n]) <= 1e-4, n
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("lanes", ["0", "2"])
 def test_cuda_spar_family_step_matches_reference_fixture(cuda, monkeypatch, lanes):

@@ -366,3 +366,34 @@ def test_spar_family_sharded_one_rank_matches_replicated(cuda, monkeypatch):
         assert [o[0] for o in a_out] == [o[0] for o in b_out] and np.array_equal(a, b)
     else:
         assert rel_l2(a, b) <= 1e-6
+
+
+@pytest.mark.parametrize("kv_heads,qk_norm", [(2, True), (4, False), (1, True)])
+def test_spar_family_grads_match_oracle(cuda, kv_heads, qk_norm):
+    """Every gradient and updated parameter of one Spar-family step (two micro-steps, clip,
+    AdamW) against the float64 restatement, relative L2 <= 2e-3 (TF32)."""
+    from spar_b200.lm import DecoderLM, LMConfig
+
+    c = dict(vocab=64, dim=128, hidden=256, layers=2, heads=4, kv_heads=kv_heads,
+             qk_norm=int(qk_norm))
+    cfg = LMConfig(vocab=64, dim=128, hidden=256, layers=2, heads=4, seq=64, micro_batch=2,
+                   family=1, kv_heads=kv_heads, qk_norm=qk_norm)
+    params = O.spar_family_parameters(c, 0x5EED0601 + kv_heads)
+    ids = O.Random(0x5EED1601).bounded(2 * 2 * 64, 64).reshape(2, 2, 64).astype(np.int32)
+    lm = DecoderLM(cfg, 0)
+    lm.load_state_dict(params)
+    loss, norm, flags = lm.train_step(ids, 3e-4, step=1)
+    grads = lm.state_dict("grad")
+    lm.close()
+    total, o_loss = None, 0.0
+    for m in ids:
+        lo, g = O.spar_lm_forward_backward(params, m, c)
+        o_loss += lo / len(ids)
+        total = g if total is None else {k: total[k] + g[k] for k in g}
+    o_grads = {k: v / len(ids) for k, v in total.items()}
+    assert flags == (0, 0)
+    assert abs(loss - o_loss) <= 2e-3 * abs(o_loss)
+    names = list(o_grads)
+    assert rel_l2(_flat(grads, names), _flat(o_grads, names)) <= 2e-3
+    for n in names:
+        assert rel_l2(grads[n], o_grads[n]) <= 1e-2, n
