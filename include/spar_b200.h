@@ -395,7 +395,8 @@ struct SparCudaStatus spar_b200_lm_gather(void* handle, int which, void* stream)
 /* windows in Spar's (optionally Fisher-Yates shuffled, derive_epoch_seed) order, batch_size at a */
 /* time (the last batch shorter unless drop_last). For data parallelism rank r of world receives */
 /* rows [r n / world, (r + 1) n / world) of every n-row batch. next gathers this rank's rows as   */
-/* int32 ids [rows, sequence_length] into `ids` (device) on `stream`; rows = 0: epoch finished.   */
+/* int32 ids [rows, sequence_length] into `ids` (device) on `stream`; global_rows = 0 means the  */
+/* epoch is finished (rows alone can be 0 for a rank whose share of a short last batch is empty). */
 struct SparCudaStatus spar_b200_batches_create(const int32_t* tokens, uint64_t token_count,
                                                uint64_t sequence_length, uint64_t stride,
                                                uint64_t batch_size, int shuffle,

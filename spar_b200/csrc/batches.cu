@@ -169,8 +169,9 @@ extern "C" SparCudaStatus spar_b200_batches_create(const int32_t* tokens, uint64
 }
 
 // Gathers this rank's rows of the next batch into ids (device, [rows, sequence_length] int32,
-// ordered on `stream`); *rows = 0 when the epoch is finished (call next_epoch). *global_rows
-// (optional) receives the whole batch's row count.
+// ordered on `stream`). *global_rows (optional) receives the whole batch's row count, 0 when the
+// epoch is finished (call next_epoch); *rows alone is 0 also for a rank whose share of a short
+// last batch is empty.
 extern "C" SparCudaStatus spar_b200_batches_next(void* handle, int32_t* ids, uint64_t* rows,
                                                  uint64_t* global_rows, void* stream) {
   if (!handle || !rows) return invalid();
