@@ -89,3 +89,26 @@ def test_checkpoint_without_optimizer_state_and_rejections(tmp_path):
     ours = tmp_path / "ours.sparckpt"
     write_checkpoint(ours, _cfg(), vals, None, None, rng_state=5, learning_rate=3e-4)
     assert ours.read_bytes() == path.read_bytes()  # byte-identical to the reference's file
+
+
+@pytest.mark.parametrize("kv_heads,qk_norm", [(4, 0), (2, 1), (1, 1)])
+def test_spar_family_layout_matches_reference_parameters(kv_heads, qk_norm):
+    """The runtime's named tensors for Spar-family configs (host-only layout query) are the
+    reference nn::DecoderLM's named_parameters: same names, order and element counts."""
+    from spar_b200 import dp
+
+    cfg = _cfg(kv_heads=kv_heads, qk_norm=qk_norm)
+    _, tensors, buckets = dp.layout(cfg)
+    ref = cpu_ref.spar_param_info(dict(CFG, kv_heads=kv_heads, qk_norm=qk_norm))
+    assert [t.name for t in tensors] == [n for n, _ in ref]
+    assert [t.rows * (t.cols or 1) for t in tensors] == [k for _, k in ref]
+    assert len(buckets) == cfg.layers + 2
+    spans = sorted(buckets)
+    for (o0, c0), (o1, _) in zip(spans, spans[1:]):
+        assert o0 + c0 == o1
+    for world in (2, 4):  # the sharded optimiser's pieces tile every bucket of this family too
+        plans = [dp.shards(cfg, world, r) for r in range(world)]
+        for i, (off, cnt) in enumerate(buckets):
+            p0 = plans[0][i]
+            assert p0.tail_offset + p0.tail_count == off + cnt
+            assert [p[i].own_offset for p in plans] == [off + r * p0.shard for r in range(world)]
