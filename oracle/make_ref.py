@@ -16,7 +16,8 @@ directory under oracle/_ref/ (removed after the build; only objects and the .so 
 Nothing else is changed. The CUDA backend is disabled (SPAR_ENABLE_CUDA=0): the path pinned here
 is the reference's CPU path. oracle/ref_driver.cpp (ours) exposes a C API over Spar's public API.
 
-Usage: python oracle/make_ref.py [--src /root/reference/src] [--jobs N]
+Usage: python oracle/make_ref.py [--src <reference checkout>/src] [--jobs N]
+(default: $SPAR_REFERENCE_SRC, else the reference checkout this build environment provides)
 """
 from __future__ import annotations
 
