@@ -49,7 +49,10 @@ struct SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma, flo
 /* Scratch is a static device array shared by all calls: cols <= 2048, at most 296 partial rows */
 /* (4.85 MB per GPU, held until exit); rejects larger sizes with code 1. The first call on a    */
 /* device looks up the array's address (make it before any stream capture); calls that overlap */
-/* on the GPU race and must be serialised by the caller.                                        */
+/* on the GPU race and must be serialised by the caller. The looked-up address is cached for   */
+/* the process's life and does not survive cudaDeviceReset (or another teardown of the device's */
+/* primary context): do not call this entry point again after one. x, dy, dx and gamma must be   */
+/* 16-byte aligned (code 1 otherwise), as for spar_b200_layernorm_backward.                     */
 struct SparCudaStatus spar_b200_layernorm_backward_noalloc(
     float* dx, float* dgamma, float* dbeta, const float* dy, const float* x, const float* gamma,
     const float* mean, const float* rstd, uint64_t rows, uint64_t cols, int accumulate_params,
@@ -281,6 +284,17 @@ struct SparB200Gemm {
 };
 struct SparCudaStatus spar_b200_gemm(const struct SparB200Gemm* gemm, int device, void* stream);
 
+/* Contiguous batched matmul of any shape: C[b] = A[b] B[b] for b < batch, row-major            */
+/* [batch, m, k] x [batch, k, n] -> [batch, m, n], dtype SPAR_CUDA_FLOAT32 (tcgen05, precision  */
+/* SparB200Precision; shapes or pointers the tensor-core GEMM cannot address directly are staged */
+/* through zero-padded copies) or SPAR_CUDA_FLOAT64 (SIMT, precision ignored). The body of the   */
+/* replacement for Spar's cuBLAS seam spar::detail::cuda_blas::matmul (reference                 */
+/* src/backend/cuda_blas.cppm:122-194, which loops cublasSgemm / cublasDgemm over the batch).    */
+/* k == 0 writes zeros; asynchronous on `stream`.                                               */
+struct SparCudaStatus spar_b200_matmul(const void* a, const void* b, void* c, uint64_t batch,
+                                       uint64_t m, uint64_t k, uint64_t n, int dtype,
+                                       int precision, int device, void* stream);
+
 /* Returns 1 if a GEMM on `device` gave up on a bounded pipeline wait (the kernel records the    */
 /* event and exits instead of hanging), 0 otherwise, -1 on a CUDA error; clear != 0 resets it.  */
 int spar_b200_gemm_error(int device, int clear);
@@ -324,6 +338,12 @@ struct SparCudaStatus spar_b200_attention_backward_gqa(
     uint64_t kv_heads, uint64_t head_dim, const float* rope_table, int device, void* stream);
 /* As spar_b200_gemm_error, for the attention kernels' bounded waits. */
 int spar_b200_attention_error(int device, int clear);
+/* Host-side fault injection for tests of the error path (no counterpart in the reference): sets  */
+/* (value != 0) or clears the bounded-wait flag of the GEMM (kernel 0) or attention (kernel 1)    */
+/* kernels on `device` without running a kernel. A training step that finds either flag set      */
+/* updates nothing and returns {2, cudaErrorTimeout}. Returns 0, or -1 on a bad argument / CUDA   */
+/* error.                                                                                         */
+int spar_b200_set_wait_error(int device, int kernel, int value);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Training-step runtime for the pre-LN / GELU decoder LM (BASELINE's model family): tied token */
@@ -377,6 +397,10 @@ struct SparCudaStatus spar_b200_lm_forward_backward(void* handle, const int32_t*
                                                     int last_micro, void* stream);
 struct SparCudaStatus spar_b200_lm_optimizer_step(void* handle, double learning_rate,
                                                   uint64_t step, void* stream);
+/* One whole optimiser step (zero grads, micro-steps, reduction, clip + AdamW); synchronises      */
+/* `stream` and reads back the mean loss, the pre-clip norm and flags [invalid id, non-finite      */
+/* norm]. If a GEMM or attention kernel of the step gave up a bounded wait (on any rank), nothing  */
+/* is updated and the call returns {2, cudaErrorTimeout}; see spar_b200_gemm_error.                */
 struct SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* ids, int ids_on_host,
                                               uint64_t micro_steps, double learning_rate,
                                               uint64_t step, float* loss_out,

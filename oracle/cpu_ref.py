@@ -11,23 +11,31 @@ from pathlib import Path
 
 import numpy as np
 
-LIB = Path(__file__).resolve().parent / "_ref" / "libspar_ref.so"
-_lib = None
+REF = Path(__file__).resolve().parent / "_ref"
+LIB = REF / "libspar_ref.so"
+# Builds of the same reference sources (oracle/make_ref.py): "cpu" the CPU path; "b200" Spar with
+# its CUDA backend on libspar_b200.so (the drop-in); "stock" Spar's own CUDA backend + cuBLAS.
+VARIANT_LIBS = {"cpu": LIB, "b200": REF / "libspar_ref_b200.so", "stock": REF / "libspar_ref_stock.so"}
+_libs: dict = {}
 
 F = POINTER(c_float)
 I32 = POINTER(ctypes.c_int32)
 
 
-def available() -> bool:
-    return LIB.exists()
+def available(variant: str = "cpu") -> bool:
+    return VARIANT_LIBS[variant].exists()
 
 
-def load():
-    global _lib
-    if _lib is None:
-        if not LIB.exists():
-            raise FileNotFoundError(f"{LIB} not built (python oracle/make_ref.py)")
-        lib = ctypes.CDLL(str(LIB))
+def load(variant: str = "cpu"):
+    if variant not in _libs:
+        path = VARIANT_LIBS[variant]
+        if not path.exists():
+            raise FileNotFoundError(f"{path} not built (python oracle/make_ref.py)")
+        if variant == "b200":  # its spar_cuda_* / spar_b200_* come from the in-tree product build
+            import spar_b200._lib as product
+
+            product.load()
+        lib = ctypes.CDLL(str(path))
         lib.ref_last_error.restype = c_char_p
         sig = {
             "ref_layernorm": [F, F, F, F, c_int64, c_int64, c_double, F, F, F, F],
@@ -47,7 +55,7 @@ def load():
             "ref_spar_lm_step": [c_int64] * 10 + [c_double, c_double, POINTER(F), I32, c_double,
                                                   c_double, c_double, c_double, c_double,
                                                   c_double, F, POINTER(c_double), POINTER(F),
-                                                  POINTER(F)],
+                                                  POINTER(F), c_int64],
             "ref_causal_softmax": [F, F, c_int64, c_int64, c_double, F, F],
             "ref_cross_entropy": [F, I32, c_int64, c_int64, c_int64, F, F],
             "ref_matmul": [F, F, F, c_int64, c_int64, c_int64, F, F, F],
@@ -56,7 +64,7 @@ def load():
             "ref_rope": [F, F, c_int64, c_int64, c_int64, c_double, F, F],
             "ref_lm_step": [c_int64] * 8 + [c_double, c_double, POINTER(F), I32, c_double,
                                             c_double, c_double, c_double, c_double, c_double, F,
-                                            POINTER(c_double), POINTER(F), POINTER(F)],
+                                            POINTER(c_double), POINTER(F), POINTER(F), c_int64],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)
@@ -66,8 +74,12 @@ def load():
         lib.ref_warmup_cosine.restype = c_double
         lib.ref_train_sample_seconds.argtypes = [c_int64] * 6
         lib.ref_train_sample_seconds.restype = c_double
-        _lib = lib
-    return _lib
+        lib.ref_lm_step_seconds.argtypes = [c_int64] * 10
+        lib.ref_lm_step_seconds.restype = c_double
+        lib.ref_matmul_seconds.argtypes = [c_int64] * 5
+        lib.ref_matmul_seconds.restype = c_double
+        _libs[variant] = lib
+    return _libs[variant]
 
 
 def _f(a):
@@ -78,9 +90,9 @@ def _p(a):
     return a.ctypes.data_as(F)
 
 
-def _check(rc):
+def _check(rc, lib=None):
     if rc != 0:
-        raise RuntimeError("reference: " + load().ref_last_error().decode())
+        raise RuntimeError("reference: " + (lib or load()).ref_last_error().decode())
 
 
 def layernorm(x, gamma, beta, dy, eps=1e-5):
@@ -175,8 +187,10 @@ def rope(x, dy, theta=10000.0):
     return out, dx
 
 
-def lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
-    """One reference training step; ids [micro, batch, t]. Returns (loss, norm, grads, new)."""
+def lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict, device: int = -1,
+            variant: str = "cpu"):
+    """One reference training step; ids [micro, batch, t]. Returns (loss, norm, grads, new).
+    device >= 0 runs it on that CUDA device (variants "b200" / "stock")."""
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     micro, batch, t = ids.shape
     ps = [_f(params[n]) for n in names]
@@ -185,11 +199,12 @@ def lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
     arr = lambda lst: (F * len(lst))(*[_p(a) for a in lst])
     loss = np.zeros(1, np.float32)
     norm = c_double(0.0)
-    _check(load().ref_lm_step(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"],
-                              batch, t, micro, cfg.get("eps", 1e-5), cfg.get("rope_theta", 1e4),
-                              arr(ps), ids.ctypes.data_as(I32), lr, opt["beta1"], opt["beta2"],
-                              opt["eps"], opt["weight_decay"], opt["max_grad_norm"], _p(loss),
-                              ctypes.byref(norm), arr(gs), arr(outs)))
+    lib = load(variant)
+    _check(lib.ref_lm_step(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"],
+                           batch, t, micro, cfg.get("eps", 1e-5), cfg.get("rope_theta", 1e4),
+                           arr(ps), ids.ctypes.data_as(I32), lr, opt["beta1"], opt["beta2"],
+                           opt["eps"], opt["weight_decay"], opt["max_grad_norm"], _p(loss),
+                           ctypes.byref(norm), arr(gs), arr(outs), device), lib)
     return float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs))
 
 
@@ -212,9 +227,11 @@ def spar_param_info(cfg: dict):
     return out
 
 
-def spar_lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
+def spar_lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict, device: int = -1,
+                 variant: str = "cpu"):
     """One training step of the reference's nn::DecoderLM; ids [micro, batch, t].
-    Returns (loss, norm, grads, new) keyed by the reference's parameter names."""
+    Returns (loss, norm, grads, new) keyed by the reference's parameter names. device >= 0 runs
+    it on that CUDA device (variants "b200" / "stock")."""
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     micro, batch, t = ids.shape
     ps = [_f(params[n]) for n in names]
@@ -223,11 +240,12 @@ def spar_lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict):
     arr = lambda lst: (F * len(lst))(*[_p(a) for a in lst])
     loss = np.zeros(1, np.float32)
     norm = c_double(0.0)
-    _check(load().ref_spar_lm_step(*_spar_dims(cfg), batch, t, micro, cfg.get("eps", 1e-5),
-                                   cfg.get("rope_theta", 1e4), arr(ps), ids.ctypes.data_as(I32),
-                                   lr, opt["beta1"], opt["beta2"], opt["eps"],
-                                   opt["weight_decay"], opt["max_grad_norm"], _p(loss),
-                                   ctypes.byref(norm), arr(gs), arr(outs)))
+    lib = load(variant)
+    _check(lib.ref_spar_lm_step(*_spar_dims(cfg), batch, t, micro, cfg.get("eps", 1e-5),
+                                cfg.get("rope_theta", 1e4), arr(ps), ids.ctypes.data_as(I32),
+                                lr, opt["beta1"], opt["beta2"], opt["eps"],
+                                opt["weight_decay"], opt["max_grad_norm"], _p(loss),
+                                ctypes.byref(norm), arr(gs), arr(outs), device), lib)
     return float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs))
 
 
@@ -293,6 +311,26 @@ def batches(documents: list, seq: int, stride: int, batch: int, shuffle: bool, s
 def _sample_worker(args):
     vocab, d, f, heads, t, iters = args
     return load().ref_train_sample_seconds(vocab, d, f, heads, t, iters)
+
+
+def lm_step_seconds(cfg, batch: int, warmup: int, iters: int, device: int = 0,
+                    variant: str = "stock") -> float:
+    """Seconds per full training step of the LN/GELU decoder `cfg` (an LMConfig) on [batch, seq]
+    ids through the given build's backend (default: the reference's own CUDA path)."""
+    v = load(variant).ref_lm_step_seconds(cfg.vocab, cfg.dim, cfg.hidden, cfg.layers, cfg.heads,
+                                          batch, cfg.seq, warmup, iters, device)
+    if v <= 0:
+        _check(1, load(variant))
+    return v
+
+
+def matmul_seconds(m: int, k: int, n: int, iters: int, device: int = 0,
+                   variant: str = "stock") -> float:
+    """Seconds per Spar matmul [m, k] x [k, n] (fp32) through the given build's cuda_blas seam."""
+    v = load(variant).ref_matmul_seconds(m, k, n, iters, device)
+    if v <= 0:
+        _check(1, load(variant))
+    return v
 
 
 def default_processes() -> int:

@@ -13,11 +13,12 @@ directory under oracle/_ref/ (removed after the build; only objects and the .so 
     definitions (the backend modules' bodies) become a translation unit `X.iface.cpp`;
   * each implementation unit `*.cpp`: `module X;` becomes #include "X.hpp" and imports become
     includes.
-Nothing else is changed. The CUDA backend is disabled (SPAR_ENABLE_CUDA=0): the path pinned here
-is the reference's CPU path. oracle/ref_driver.cpp (ours) exposes a C API over Spar's public API.
+Nothing else is changed. Three libraries come out of the same sources (VARIANTS below): the CPU
+path (SPAR_ENABLE_CUDA=0), the drop-in build on libspar_b200.so, and the unchanged reference GPU
+path. oracle/ref_driver.cpp (ours) exposes a C API over Spar's public API in each.
 
 Usage: python oracle/make_ref.py [--src <reference checkout>/src] [--jobs N]
-(default: $SPAR_REFERENCE_SRC, else the reference checkout this build environment provides)
+(default: $SPAR_REFERENCE_SRC, else the src/ of a `reference` checkout beside this repository)
 """
 from __future__ import annotations
 
@@ -155,44 +156,104 @@ def convert_unit(path: Path, build: Path) -> Path:
     return out
 
 
-def compile_one(src: Path, obj: Path, include: Path) -> None:
-    subprocess.run([CXX, *FLAGS, f"-I{include}", "-c", str(src), "-o", str(obj)], check=True)
+def compile_one(src: Path, obj: Path, include: Path, flags: list[str]) -> None:
+    subprocess.run([CXX, *flags, f"-I{include}", "-c", str(src), "-o", str(obj)], check=True)
+
+
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+REPO = HERE.parent
+
+# Variants (all TEST INFRASTRUCTURE, outputs under oracle/_ref/):
+#   cpu   libspar_ref.so        the reference's CPU path (SPAR_ENABLE_CUDA=0): the oracle's pin and
+#                               the CPU baseline.
+#   b200  libspar_ref_b200.so   the reference built with SPAR_ENABLE_CUDA=1 as a Spar build that
+#                               adopts the drop-in would be: src/backend/cuda_kernels.cu left out and
+#                               libspar_b200.so linked in its place (its spar_cuda_* entry points),
+#                               and the product's spar_b200/spar/cuda_blas.cppm compiled in place of
+#                               src/backend/cuda_blas.cppm. Every other reference source unchanged.
+#   stock libspar_ref_stock.so  the unchanged reference GPU path (its own cuda_kernels.cu, built
+#                               with nvcc for sm_100a, and cuBLAS): the GPU bar, timed only.
+VARIANTS = {"cpu": "libspar_ref.so", "b200": "libspar_ref_b200.so", "stock": "libspar_ref_stock.so"}
+
+
+def _inputs(src: Path, variant: str) -> list[Path]:
+    files = [*src.rglob("*.cppm"), *src.rglob("*.cpp"), *src.rglob("*.cu"), *src.rglob("*.hpp"),
+             HERE / "ref_driver.cpp", Path(__file__)]
+    if variant == "b200":
+        files += [REPO / "spar_b200" / "spar" / "cuda_blas.cppm", *(REPO / "include").glob("*.h")]
+    return files
+
+
+def build_variant(src: Path, variant: str, jobs: int) -> Path:
+    lib = OUT / VARIANTS[variant]
+    inputs = _inputs(src, variant)
+    if lib.exists() and lib.stat().st_mtime >= max(f.stat().st_mtime for f in inputs):
+        return lib
+    objdir = OUT / ("obj" if variant == "cpu" else f"obj_{variant}")
+    objdir.mkdir(parents=True, exist_ok=True)
+    build = Path(tempfile.mkdtemp(prefix="conv_", dir=OUT))
+    flags = list(FLAGS)
+    link: list[str] = []
+    try:
+        units = []
+        glue = REPO / "spar_b200" / "spar" / "cuda_blas.cppm"
+        for cppm in sorted(src.rglob("*.cppm")):
+            if variant == "b200" and cppm.relative_to(src).as_posix() == "backend/cuda_blas.cppm":
+                cppm = glue  # the product's module in place of the reference's cuBLAS seam
+            _, tu = convert_interface(cppm, build)
+            if tu:
+                units.append(tu)
+        for cpp in sorted(src.rglob("*.cpp")):
+            units.append(convert_unit(cpp, build))
+        objs = [objdir / (u.stem + ".o") for u in units]
+        if variant != "cpu":
+            flags = [f for f in flags if not f.startswith("-DSPAR_ENABLE_CUDA")]
+            flags += ["-DSPAR_ENABLE_CUDA=1", f"-I{CUDA_HOME / 'include'}"]
+            link += [f"-L{CUDA_HOME / 'lib64'}", f"-Wl,-rpath,{CUDA_HOME / 'lib64'}", "-lcudart"]
+        if variant == "b200":
+            # cuda_ops.cppm includes "cuda_kernels.hpp": here it resolves to the product's header.
+            (build / "cuda_kernels.hpp").write_text('#include "spar_cuda_kernels.h"\n')
+            flags += [f"-I{REPO / 'include'}"]
+            link = [f"-L{REPO / 'spar_b200'}", "-l:libspar_b200.so",
+                    "-Wl,-rpath,$ORIGIN/../../spar_b200", *link]
+        if variant == "stock":
+            flags += [f"-I{src / 'backend'}"]
+            kernels_obj = objdir / "cuda_kernels.o"
+            subprocess.run([str(CUDA_HOME / "bin" / "nvcc"), "-gencode",
+                            "arch=compute_100a,code=sm_100a", "-O2", "-std=c++20", "-Xcompiler",
+                            "-fPIC", "-c", str(src / "backend" / "cuda_kernels.cu"), "-o",
+                            str(kernels_obj)], check=True)
+            objs.append(kernels_obj)
+            link += ["-lcublas"]
+        driver = HERE / "ref_driver.cpp"
+        with concurrent.futures.ThreadPoolExecutor(max_workers=jobs) as pool:
+            futs = [pool.submit(compile_one, u, o, build, flags)
+                    for u, o in zip(units, objs) if u.suffix != ".o"]
+            futs.append(pool.submit(compile_one, driver, objdir / "ref_driver.o", build, flags))
+            for f in futs:
+                f.result()
+        subprocess.run([CXX, "-shared", "-Wl,-Bsymbolic", "-o", str(lib), *map(str, objs),
+                        str(objdir / "ref_driver.o"), *link], check=True)
+    finally:
+        shutil.rmtree(build, ignore_errors=True)
+    return lib
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", default=os.environ.get("SPAR_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--src", default=os.environ.get("SPAR_REFERENCE_SRC") or
+                    str(HERE.parents[1] / "reference" / "src"))
     ap.add_argument("--jobs", type=int, default=os.cpu_count() or 4)
+    ap.add_argument("--variant", action="append", choices=sorted(VARIANTS),
+                    help="default: all three")
     args = ap.parse_args()
     src = Path(args.src)
     if not src.is_dir():
         print(f"reference sources not found at {src}", file=sys.stderr)
         return 1
     OUT.mkdir(exist_ok=True)
-    objdir = OUT / "obj"
-    objdir.mkdir(exist_ok=True)
-    build = Path(tempfile.mkdtemp(prefix="conv_", dir=OUT))
-    try:
-        units = []
-        for cppm in sorted(src.rglob("*.cppm")):
-            _, tu = convert_interface(cppm, build)
-            if tu:
-                units.append(tu)
-        for cpp in sorted(src.rglob("*.cpp")):
-            units.append(convert_unit(cpp, build))
-        driver = HERE / "ref_driver.cpp"
-        objs = [objdir / (u.stem + ".o") for u in units]
-        with concurrent.futures.ThreadPoolExecutor(max_workers=args.jobs) as pool:
-            futs = [pool.submit(compile_one, u, o, build) for u, o in zip(units, objs)]
-            futs.append(pool.submit(compile_one, driver, objdir / "ref_driver.o", build))
-            for f in futs:
-                f.result()
-        lib = OUT / "libspar_ref.so"
-        subprocess.run([CXX, "-shared", "-o", str(lib), *map(str, objs),
-                        str(objdir / "ref_driver.o")], check=True)
-        print(lib)
-    finally:
-        shutil.rmtree(build, ignore_errors=True)
+    for variant in args.variant or ["cpu", "b200", "stock"]:
+        print(build_variant(src, variant, args.jobs))
     return 0
 
 

@@ -39,8 +39,19 @@ Tensor ids_from_host(const int32_t* data, std::vector<dim> shape) {
   return t;
 }
 
+// device < 0: the CPU; otherwise Device::cuda(device) (builds with SPAR_ENABLE_CUDA=1).
+Device device_of(int64_t device) {
+  return device < 0 ? Device::cpu() : Device::cuda(static_cast<std::int32_t>(device));
+}
+
+// The value of a one-element float tensor on any device.
+float scalar_of(const Tensor& t) {
+  const Tensor c = t.detach().to(Device::cpu());
+  return c.span<float>()[0];
+}
+
 void to_host(const Tensor& t, float* out) {
-  const Tensor c = t.detach().contiguous();
+  const Tensor c = t.detach().to(Device::cpu()).contiguous();
   auto s = std::as_const(c).span<float>();
   std::memcpy(out, s.data(), s.size() * sizeof(float));
 }
@@ -314,21 +325,25 @@ int ref_rope(const float* x, const float* dy, int64_t outer, int64_t t, int64_t 
 // mean-of-micro-batch-means loss, Spar backward, clip_grad_norm, AdamW. params/grads/out_params
 // are arrays of pointers in named-parameter order (embedding, per block: ln1 w/b, q/k/v/out
 // w/b, ln2 w/b, up w/b, down w/b; final ln w/b). grads are the pre-clip gradients.
+// `device` (last argument): < 0 runs on the CPU, otherwise the parameters are moved to
+// Device::cuda(device) (nn::move_to) and the whole step runs through Spar's CUDA backend.
 int ref_lm_step(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t heads, int64_t batch,
                 int64_t t, int64_t micro, double eps, double theta, const float* const* params,
                 const int32_t* ids, double lr, double beta1, double beta2, double adam_eps,
                 double wd, double max_norm, float* loss_out, double* norm_out, float** grads,
-                float** out_params) {
+                float** out_params, int64_t device) {
   return guarded([&] {
     Random rng{1};
     Model model(vocab, d, f, layers, heads, theta, eps, rng);
     std::vector<nn::Parameter> ps = model.parameters();
     for (std::size_t i = 0; i < ps.size(); ++i) load(ps[i], params[i]);
+    const Device dev = device_of(device);
+    nn::move_to(std::span<nn::Parameter>{ps}, dev);
     double total = 0.0;
     for (int64_t mi = 0; mi < micro; ++mi) {
-      Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t});
+      Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t}).to(dev);
       Tensor loss = loss::language_model_cross_entropy(model.logits(tid), tid);
-      total += std::as_const(loss).span<float>()[0];
+      total += scalar_of(loss);
       Tensor scaled = multiply_scalar(loss, 1.0 / static_cast<double>(micro));
       scaled.backward();
     }
@@ -383,18 +398,20 @@ int ref_spar_lm_step(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_
                      double eps, double theta, const float* const* params, const int32_t* ids,
                      double lr, double beta1, double beta2, double adam_eps, double wd,
                      double max_norm, float* loss_out, double* norm_out, float** grads,
-                     float** out_params) {
+                     float** out_params, int64_t device) {
   return guarded([&] {
     Random rng{1};
     nn::DecoderLM model{spar_config(vocab, d, f, layers, heads, kv_heads, qk_norm, eps, theta), rng};
     std::vector<nn::Parameter> ps;
     for (auto& np : nn::named_parameters(model)) ps.push_back(np.parameter);
     for (std::size_t i = 0; i < ps.size(); ++i) load(ps[i], params[i]);
+    const Device dev = device_of(device);
+    nn::move_to(model, dev);
     double total = 0.0;
     for (int64_t mi = 0; mi < micro; ++mi) {
-      Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t});
+      Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t}).to(dev);
       Tensor loss = loss::language_model_cross_entropy(model.forward(tid), tid);
-      total += std::as_const(loss).span<float>()[0];
+      total += scalar_of(loss);
       Tensor scaled = multiply_scalar(loss, 1.0 / static_cast<double>(micro));
       scaled.backward();
     }
@@ -538,6 +555,66 @@ double ref_train_sample_seconds(int64_t vocab, int64_t d, int64_t f, int64_t hea
       opt.step();
     }
     seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  });
+  return seconds;
+}
+
+// Seconds per training step (forward, LM loss, backward, clip, AdamW) of the LN/GELU decoder
+// with N(0, 0.02) weights on [batch, t] ids, on `device` (< 0: CPU), after `warmup` untimed
+// steps, averaged over `iters` steps. Each step ends with the loss read back to the host. Used to
+// time the reference's own GPU path (reported beside the product's numbers, never a parity
+// check).
+double ref_lm_step_seconds(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t heads,
+                           int64_t batch, int64_t t, int64_t warmup, int64_t iters,
+                           int64_t device) {
+  double seconds = -1.0;
+  guarded([&] {
+    Random rng{11};
+    Model model(vocab, d, f, layers, heads, 10000.0, 1e-5, rng);
+    std::vector<nn::Parameter> ps = model.parameters();
+    const Device dev = device_of(device);
+    nn::move_to(std::span<nn::Parameter>{ps}, dev);
+    optim::AdamW opt{ps, 3e-4, 0.9, 0.95, 1e-8, 0.1};
+    Tensor host_ids{Shape{batch, t}, DType::Int32};
+    auto s = host_ids.span<int32_t>();
+    for (int64_t i = 0; i < batch * t; ++i) s[i] = static_cast<int32_t>((i * 7919 + 13) % vocab);
+    const Tensor tid = host_ids.to(dev);
+    auto one = [&] {
+      for (auto& p : ps) p.zero_grad();
+      Tensor loss = loss::language_model_cross_entropy(model.logits(tid), tid);
+      loss.backward();
+      (void)training::clip_grad_norm(ps, 1.0);
+      opt.step();
+      (void)scalar_of(loss);
+    };
+    for (int64_t i = 0; i < warmup; ++i) one();
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int64_t i = 0; i < iters; ++i) one();
+    seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() /
+              static_cast<double>(iters);
+  });
+  return seconds;
+}
+
+// Seconds per Spar matmul (forward only, the cuda_blas seam on a CUDA device) of [m, k] x [k, n]
+// fp32 N(0, 1) operands, averaged over `iters` calls after one warm-up call.
+double ref_matmul_seconds(int64_t m, int64_t k, int64_t n, int64_t iters, int64_t device) {
+  double seconds = -1.0;
+  guarded([&] {
+    const Device dev = device_of(device);
+    auto pattern = [](Tensor t) {  // deterministic values spread over [-0.5, 0.5)
+      auto v = t.span<float>();
+      for (std::size_t i = 0; i < v.size(); ++i)
+        v[i] = static_cast<float>((i * 2654435761ull) % 1000003ull) / 1000003.0f - 0.5f;
+      return t;
+    };
+    Tensor a = pattern(Tensor{Shape{m, k}, DType::Float32}).to(dev);
+    Tensor b = pattern(Tensor{Shape{k, n}, DType::Float32}).to(dev);
+    (void)matmul(a, b);
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int64_t i = 0; i < iters; ++i) (void)matmul(a, b);
+    seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() /
+              static_cast<double>(iters);
   });
   return seconds;
 }

@@ -269,16 +269,23 @@ def cross_entropy_forward_backward(logits, targets, rows=None, dtype=np.float64)
     """log_softmax (softmax.cpp:342-404) + NLL gather (cross_entropy.cpp:52-64) + mean; the
     gradient of the mean loss is (exp(logp) - onehot)/N on selected rows (nll_gradient :66-78,
     log_softmax_gradient softmax.cpp:406-444). Returns (mean loss, per-row loss, dlogits)."""
-    z = np.asarray(logits, dtype).reshape(-1, logits.shape[-1])
+    z = np.asarray(logits).reshape(-1, logits.shape[-1])
     if rows is None:
         rows = np.arange(z.shape[0])
-    m = z.max(axis=-1, keepdims=True)
-    logp = (z - m) - np.log(np.exp(z - m).sum(axis=-1, keepdims=True))
+    rows = np.asarray(rows)
+    # One working copy of the selected rows, shifted by the row maximum, exponentiated in place
+    # (large vocabularies: a single [rows, V] float64 array instead of several).
+    d = np.zeros((z.shape[0], z.shape[1]), dtype)
+    w = z[rows].astype(dtype)
+    w -= w.max(axis=-1, keepdims=True)
+    shifted_target = w[np.arange(len(rows)), targets].copy()
+    np.exp(w, out=w)
+    total = w.sum(axis=-1)
     n = len(rows)
     row_loss = np.zeros(z.shape[0], dtype)
-    row_loss[rows] = -logp[rows, targets]
-    d = np.zeros_like(z)
-    d[rows] = np.exp(logp[rows]) / n
+    row_loss[rows] = np.log(total) - shifted_target  # -log softmax at the target
+    w *= (1.0 / n) / total[:, None]
+    d[rows] = w
     d[rows, targets] -= 1.0 / n
     return row_loss[rows].mean(), row_loss, d
 

@@ -88,12 +88,14 @@ SIGNATURES = {
     "spar_b200_rope_apply": (S, [p, p, u64, u64, u64, u64, u64, i, i, p]),
     "spar_b200_gemm": (S, [POINTER(SparB200Gemm), i, p]),
     "spar_b200_gemm_error": (c_int, [i, i]),
+    "spar_b200_matmul": (S, [p, p, p, u64, u64, u64, u64, i, i, i, p]),
     "spar_b200_attention_forward": (S, [p, p, p, p, u64, u64, u64, u64, i, p]),
     "spar_b200_attention_backward": (S, [p, p, p, p, p, p, p, u64, u64, u64, u64, p, i, p]),
     "spar_b200_attention_forward_gqa": (S, [p, p, p, p, u64, u64, u64, u64, u64, i, p]),
     "spar_b200_attention_backward_gqa": (S, [p, p, p, p, p, p, p, u64, u64, u64, u64, u64, p, i,
                                              p]),
     "spar_b200_attention_error": (c_int, [i, i]),
+    "spar_b200_set_wait_error": (c_int, [i, i, i]),
     "spar_b200_lm_create": (S, [POINTER(SparB200LMConfig), i, POINTER(c_void_p)]),
     "spar_b200_lm_destroy": (None, [p]),
     "spar_b200_lm_parameter_count": (u64, [p]),

@@ -26,6 +26,7 @@ SOURCES = [
     "adamw.cu",
     "embedding.cu",
     "gemm.cu",
+    "matmul.cu",
     "attention.cu",
     "compat.cu",
     "trainer.cu",

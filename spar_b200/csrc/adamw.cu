@@ -75,7 +75,7 @@ norm_partial_kernel(double* __restrict__ state, const float* __restrict__ g, uin
   }
 }
 
-__global__ void norm_final_kernel(double* state, int parts) {
+__global__ void norm_final_kernel(double* state, int parts, const int* wait_a, const int* wait_b) {
   pdl_begin();
   if (threadIdx.x != 0) return;
   double s = 0.0, bad = 0.0;
@@ -84,6 +84,10 @@ __global__ void norm_final_kernel(double* state, int parts) {
     s += partial[p];
     bad = fmax(bad, partial[parts + p]);
   }
+  // A kernel of this step gave up a bounded wait: its outputs are not trustworthy.
+  if ((wait_a && *reinterpret_cast<const volatile int*>(wait_a)) ||
+      (wait_b && *reinterpret_cast<const volatile int*>(wait_b)))
+    bad += kWaitErrorMark;
   state[0] = s;
   state[1] = bad;
 }
@@ -147,7 +151,8 @@ adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restri
 }  // namespace
 
 cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t slice_count,
-                             int device, cudaStream_t stream) {
+                             int device, cudaStream_t stream, const int* wait_flag_a,
+                             const int* wait_flag_b) {
   const int parts = norm_blocks(device);
   bool first = true;
   for (uint64_t i = 0; i < slice_count; ++i) {
@@ -156,12 +161,9 @@ cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t s
                                                    slices[i].count, first ? 1 : 0);
     first = false;
   }
-  if (first) {  // nothing to reduce: norm 0
-    const cudaError_t e = cudaMemsetAsync(norm_state, 0, 2 * sizeof(double), stream);
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
-  }
-  launch(norm_final_kernel, dim3(1), dim3(32), 0, stream, norm_state, parts);
+  // Nothing to reduce: norm 0 (the final pass still reads the wait flags).
+  launch(norm_final_kernel, dim3(1), dim3(32), 0, stream, norm_state, first ? 0 : parts,
+         wait_flag_a, wait_flag_b);
   return cudaGetLastError();
 }
 

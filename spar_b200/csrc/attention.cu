@@ -1516,6 +1516,24 @@ extern "C" SparCudaStatus spar_b200_attention_backward(const float* qkv, const f
                                           seq, heads, heads, head_dim, rope_table, device, stream);
 }
 
+namespace spar_b200 {
+int* attention_wait_flag(int device) {
+  static std::mutex mu;
+  static int* addr[64] = {};
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[device]) {
+    DeviceScope scope(device);
+    void* p = nullptr;
+    if (scope.error() == cudaSuccess && cudaGetSymbolAddress(&p, g_attn_error) == cudaSuccess)
+      addr[device] = static_cast<int*>(p);
+    else
+      cudaGetLastError();
+  }
+  return addr[device];
+}
+}  // namespace spar_b200
+
 extern "C" int spar_b200_attention_error(int device, int clear) {
   DeviceScope scope(device);
   int v = 0;

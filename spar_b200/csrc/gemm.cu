@@ -1344,6 +1344,24 @@ extern "C" SparCudaStatus spar_b200_gemm(const SparB200Gemm* gemm, int device, v
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
+namespace spar_b200 {
+int* gemm_wait_flag(int device) {
+  static std::mutex mu;
+  static int* addr[64] = {};
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[device]) {
+    DeviceScope scope(device);
+    void* p = nullptr;
+    if (scope.error() == cudaSuccess && cudaGetSymbolAddress(&p, g_gemm_error) == cudaSuccess)
+      addr[device] = static_cast<int*>(p);
+    else
+      cudaGetLastError();
+  }
+  return addr[device];
+}
+}  // namespace spar_b200
+
 extern "C" int spar_b200_gemm_error(int device, int clear) {
   DeviceScope scope(device);
   int v = 0;
@@ -1353,4 +1371,18 @@ extern "C" int spar_b200_gemm_error(int device, int clear) {
     cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int));
   }
   return v;
+}
+
+// Host-side fault injection for tests of the error path: sets (or clears) the flag that a GEMM
+// (kernel 0) or attention (kernel 1) kernel raises when one of its bounded waits expires, without
+// running a kernel that waits. No GPU work is left in an undefined state.
+extern "C" int spar_b200_set_wait_error(int device, int kernel, int value) {
+  if (kernel != 0 && kernel != 1) return -1;
+  DeviceScope scope(device);
+  if (scope.error() != cudaSuccess) return -1;
+  const int v = value ? 1 : 0;
+  int* flag = kernel == 0 ? gemm_wait_flag(device) : attention_wait_flag(device);
+  if (!flag) return -1;
+  const cudaError_t e = cudaMemcpy(flag, &v, sizeof(int), cudaMemcpyHostToDevice);
+  return e == cudaSuccess ? 0 : -1;
 }

@@ -170,8 +170,17 @@ struct Slice {
   float* second_moment;
   uint64_t count;
 };
+// Device addresses of the flags a GEMM / attention kernel sets when one of its bounded waits
+// expires (looked up once per device with that device current); nullptr if the lookup failed.
+int* gemm_wait_flag(int device);
+int* attention_wait_flag(int device);
+// Added to norm_state[1] by the norm pass when a wait flag given to it is set: AdamW then updates
+// nothing (as for a non-finite norm) and the step reports cudaErrorTimeout. A non-finite gradient
+// adds at most 1 per rank, so the mark stays recognisable after the flags are summed over ranks.
+constexpr double kWaitErrorMark = 1024.0;
 cudaError_t grad_norm_launch(double* norm_state, const Slice* slices, uint64_t slice_count,
-                             int device, cudaStream_t stream);
+                             int device, cudaStream_t stream, const int* wait_flag_a = nullptr,
+                             const int* wait_flag_b = nullptr);
 // AdamW scalars for one step (bias corrections c1 = 1 - beta1^step, c2 = 1 - beta2^step).
 struct AdamWArgs {
   double lr, beta1, beta2, eps, decay_factor, c1, c2, max_norm;

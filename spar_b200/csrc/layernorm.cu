@@ -433,6 +433,16 @@ extern "C" SparCudaStatus spar_b200_layernorm_forward(float* y, float* mean, flo
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
+namespace {
+// The backward kernel reads x, dy and gamma and writes dx as float4 (rows are cols floats apart,
+// cols a multiple of 4), so those base pointers must be 16-byte aligned.
+bool backward_pointers_aligned(const float* dx, const float* dy, const float* x,
+                               const float* gamma) {
+  return ((reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dy) |
+           reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma)) & 15) == 0;
+}
+}  // namespace
+
 extern "C" SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma, float* dbeta,
                                                        const float* dy, const float* x,
                                                        const float* gamma, const float* mean,
@@ -443,6 +453,7 @@ extern "C" SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma,
   if (cols == 0 || cols % 4 != 0 || vectors_per_lane(cols) == 0 || !dgamma || !dbeta || !gamma)
     return invalid();
   if (rows != 0 && (!dx || !dy || !x || !mean || !rstd)) return invalid();
+  if (!backward_pointers_aligned(dx, dy, x, gamma)) return invalid();
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -605,7 +616,9 @@ cudaError_t scratch_address(int device, float** out) {
 
 // Same arguments and results as spar_b200_layernorm_backward; allocates nothing.
 // The first call on a device looks up the scratch address (make that first call before any
-// stream capture). All calls share one scratch array, so calls that overlap on the GPU (two
+// stream capture). The address is cached for the life of the process: it does not survive
+// cudaDeviceReset (or any other teardown of the device's primary context), after which this entry
+// point must not be called again in that process. All calls share one scratch array, so calls that overlap on the GPU (two
 // streams, or two host threads on one device) race; serialise them. The array keeps the previous
 // call's partials, which is harmless: every partial row a call reads is written earlier in the
 // same call, so nothing has to start at zero.
@@ -616,6 +629,7 @@ extern "C" SparCudaStatus spar_b200_layernorm_backward_noalloc(
   if (cols == 0 || cols % 4 != 0 || !dgamma || !dbeta || !gamma) return invalid();
   if (cols > kNoAllocMaxCols) return invalid();  // beyond the static scratch size
   if (rows != 0 && (!dx || !dy || !x || !mean || !rstd)) return invalid();
+  if (!backward_pointers_aligned(dx, dy, x, gamma)) return invalid();
   DeviceScope scope(device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -885,7 +885,8 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
     // This rank's pieces: sum of squares, summed over ranks (the non-finite flags too), then
     // clip + AdamW on the pieces.
     launches += norm_slices.size() + 1 + own_slices.size();
-    e = grad_norm_launch(norm_state, norm_slices.data(), norm_slices.size(), device, s);
+    e = grad_norm_launch(norm_state, norm_slices.data(), norm_slices.size(), device, s,
+                         gemm_wait_flag(device), attention_wait_flag(device));
     if (e == cudaSuccess) e = cudaEventRecord(gather_fork, s);  // collectives stay on comm_stream
     if (e == cudaSuccess) e = cudaStreamWaitEvent(comm_stream, gather_fork, 0);
     if (e == cudaSuccess) e = comm_allreduce_sum_f64(comm, norm_state, 2, comm_stream);
@@ -898,7 +899,8 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
     return e == cudaSuccess ? ok() : runtime(e);
   }
   launches += 3;
-  e = grad_norm_launch(norm_state, &slice, 1, device, s);
+  e = grad_norm_launch(norm_state, &slice, 1, device, s, gemm_wait_flag(device),
+                       attention_wait_flag(device));
   if (e == cudaSuccess)
     e = adamw_launch(&slice, 1, norm_state, cfg.max_grad_norm, lr, cfg.beta1, cfg.beta2,
                      cfg.adam_epsilon, cfg.weight_decay, step, flags + 1, device, s,
@@ -1356,7 +1358,8 @@ extern "C" SparCudaStatus spar_b200_lm_optimizer_step(void* handle, double learn
   for (int w = 0; w < 4 && e == cudaSuccess; ++w) e = t->gather_arena(w, s);  // whole arenas
   if (e != cudaSuccess) return runtime(e);
   t->launches += 3;
-  e = grad_norm_launch(t->norm_state, &slice, 1, t->device, s);
+  e = grad_norm_launch(t->norm_state, &slice, 1, t->device, s, gemm_wait_flag(t->device),
+                       attention_wait_flag(t->device));
   if (e == cudaSuccess)
     e = adamw_launch(&slice, 1, t->norm_state, t->cfg.max_grad_norm, learning_rate, t->cfg.beta1,
                      t->cfg.beta2, t->cfg.adam_epsilon, t->cfg.weight_decay, step, t->flags + 1,
@@ -1453,6 +1456,10 @@ done:
     flags_out[0] = flags[0];
     flags_out[1] = flags[1];
   }
+  // A GEMM or attention kernel of this step (on any rank) gave up one of its bounded waits: the
+  // gradients are not trustworthy and AdamW updated nothing. The flags stay set until cleared
+  // (spar_b200_gemm_error / spar_b200_attention_error with clear = 1), so later steps also refuse.
+  if (norm_state[1] >= kWaitErrorMark) return runtime(cudaErrorTimeout);
   return ok();
 }
 

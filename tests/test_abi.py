@@ -57,6 +57,22 @@ def test_invalid_arguments_rejected_without_gpu():
     assert st.code == 1
 
 
+def test_layernorm_backward_rejects_misaligned_pointers_without_gpu():
+    """The LayerNorm backward reads x, dy, gamma and writes dx as float4: a base pointer that is
+    not 16-byte aligned is an invalid argument (code 1), checked before any CUDA call."""
+    from spar_b200 import _lib
+
+    lib = _lib.load()
+    good, bad = 1 << 20, (1 << 20) + 4  # never dereferenced: validation fails first
+    for fn in (lib.spar_b200_layernorm_backward, lib.spar_b200_layernorm_backward_noalloc):
+        for k in range(4):  # dx, dy, x, gamma in turn
+            ptrs = [good] * 4
+            ptrs[k] = bad
+            dx, dy, x, g = ptrs
+            st = fn(dx, good, good, dy, x, g, good, good, 8, 64, 0, 0, 0, None)
+            assert st.code == 1, (fn, k)
+
+
 def test_zero_count_calls_succeed():
     """Zero-count calls return success without launching (reference cuda_kernels.cu convention)."""
     from spar_b200 import _lib

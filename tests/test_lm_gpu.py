@@ -133,6 +133,38 @@ def test_nonfinite_gradient_skips_update(cuda):
         np.testing.assert_array_equal(after[n], bad[n])
 
 
+@pytest.mark.parametrize("kernel", [0, 1])
+def test_wait_error_fails_the_step_and_skips_the_update(cuda, kernel):
+    """A GEMM (0) or attention (1) kernel that gives up one of its bounded waits raises a device
+    flag. The flag is set here from the host (no kernel is made to wait); the norm pass reads it,
+    AdamW updates nothing, and the step returns {2, cudaErrorTimeout}, eagerly and in graph
+    replay. Once the flag is cleared the next step updates as usual."""
+    from spar_b200 import _lib, ops
+    from spar_b200._lib import SparError
+    from spar_b200.lm import C1, DecoderLM
+
+    lib = _lib.load()
+    params, ids = _setup(C1, 1)
+    lm = DecoderLM(C1, 0)
+    lm.load_state_dict(params)
+    try:
+        for step in (1, 2, 3):  # step 1 eager, 2 captured, 3 replayed
+            if step > 1:
+                before = _flat(lm.state_dict(), lm.names)
+                assert lib.spar_b200_set_wait_error(0, kernel, 1) == 0
+                with pytest.raises(SparError) as err:
+                    lm.train_step(ids, 3e-4, step=step)
+                assert (err.value.code, err.value.cuda_error) == (2, 909)
+                assert np.array_equal(_flat(lm.state_dict(), lm.names), before)
+                assert lib.spar_b200_set_wait_error(0, kernel, 0) == 0
+            _, _, flags = lm.train_step(ids, 3e-4, step=step)
+            assert flags == (0, 0)
+    finally:
+        lib.spar_b200_set_wait_error(0, kernel, 0)
+        lm.close()
+    assert ops.gemm_error(0) == 0 and ops.attention_error(0) == 0
+
+
 def test_graph_replay_matches_eager_steps(cuda):
     """train_step runs its first step eagerly, captures the second into a CUDA graph and replays
     it afterwards (AdamW scalars refreshed from device memory): three steps must give the same

@@ -1,0 +1,146 @@
+"""One training step at the benchmark's widths against the float64 oracle.
+
+The C1 step tests run the tiny model only; the headline bench runs code paths that C1 never
+reaches: paired-SM 256-column GEMM tiles and split-K with epilogues, the weight-gradient stream,
+two micro-steps in flight (lanes, micro-batches of <= 4 sequences), the streaming cross-entropy
+(vocabularies > 2048), padded logits (V = 50257) and the attention scheduling at T = 1024. Here
+one full step (embedding, blocks, final norm, tied logits, LM cross-entropy
+(src/loss/cross_entropy.cpp:176-214), backward, clip, AdamW) runs through
+spar_b200_lm_train_step at the C5 widths (d 1024, 16 heads, F 4096, T 1024, V 32768) and the C4
+widths (d 768, 12 heads, F 3072, V 50257), two blocks deep, and is compared with
+oracle.spar_oracle.lm_train_step (float64; DecoderLM::forward, src/nn/decoder.cpp:73-90) on the
+same seeded weights and ids. Biases, LayerNorm gains and shifts are drawn non-trivially so their
+gradients are tested at non-identity values.
+
+Bars (north star): per-tensor gradient relative L2 <= 2e-3 in TF32 and <= 1e-5 in 3xTF32, loss
+and gradient norm at the same bars.
+
+The update is checked in two parts, because at step 1 AdamW's update is
+lr * g / (|g| + eps) (plus decay), i.e. lr * sign(g) wherever |g| >> eps: comparing it with an
+independently computed float64 step would only test the signs of near-zero gradient elements.
+(1) The update applied is exactly AdamW of the GPU's own gradients: the parameter delta equals
+the oracle's AdamW (src/optim/adamw.cpp:37-63, clip of src/training/gradients.cpp:176-190) fed
+with those gradients and the GPU's norm, to 1e-6 relative L2 (fp32 rounding of the clipped
+gradient). (2) Where the oracle gradient is well conditioned (|g| >= 5 % of the tensor's RMS),
+the delta equals the float64 oracle's delta within the same bar as the gradients.
+"""
+import numpy as np
+import pytest
+
+from _util import rel_l2
+from oracle import spar_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LR = 3e-4
+
+
+def _cfg(name, micro_batch, precision):
+    from dataclasses import replace
+
+    from spar_b200.lm import C4, C5
+
+    base = {"c5": C5, "c4": C4}[name]
+    return replace(base, layers=2, micro_batch=micro_batch, precision=precision)
+
+
+_CACHE = {}
+
+
+def _inputs(cfg, micro_steps):
+    """Weights N(0, 0.02) from the device initialiser (the oracle's stream, tested against it at
+    C1), biases N(0, 0.02), norm gains 1 + N(0, 0.1), norm shifts N(0, 0.1); ids by the oracle's
+    bounded sampler. Cached per model so the TF32 and 3xTF32 runs share inputs and oracle."""
+    from spar_b200.lm import DecoderLM
+
+    key = (cfg.vocab, cfg.dim, cfg.micro_batch, micro_steps)
+    if key in _CACHE:
+        return _CACHE[key]
+    lm = DecoderLM(cfg, 0)
+    lm.init_normal(0x5EED0000 + cfg.dim, 0.02)
+    params = lm.state_dict()
+    lm.close()
+    r = np.random.default_rng(cfg.dim)
+    for n, v in params.items():
+        if v.ndim == 1:
+            if n.endswith("norm.weight"):
+                params[n] = (1.0 + 0.1 * r.standard_normal(v.shape)).astype(np.float32)
+            elif "norm" in n:
+                params[n] = (0.1 * r.standard_normal(v.shape)).astype(np.float32)
+            else:
+                params[n] = (0.02 * r.standard_normal(v.shape)).astype(np.float32)
+    ids = O.Random(0x5EED1000 + cfg.dim).bounded(micro_steps * cfg.micro_batch * cfg.seq, cfg.vocab)
+    ids = ids.reshape(micro_steps, cfg.micro_batch, cfg.seq).astype(np.int32)
+    o_loss, o_grads, o_new, _ = O.lm_train_step(params, {}, list(ids), cfg.oracle_dict(), 1, LR,
+                                                cfg.opt_dict())
+    _CACHE[key] = (params, ids, (o_loss, o_grads, o_new))
+    return _CACHE[key]
+
+
+def _step(cfg, params, ids):
+    from spar_b200 import ops
+    from spar_b200.lm import DecoderLM
+
+    lm = DecoderLM(cfg, 0)
+    try:
+        lm.load_state_dict(params)
+        loss, norm, flags = lm.train_step(ids, LR, step=1)
+        assert ops.gemm_error(0) == 0 and ops.attention_error(0) == 0
+        return loss, norm, flags, lm.state_dict("grad"), lm.state_dict("param")
+    finally:
+        lm.close()
+
+
+def _check(cfg, micro_steps, tol):
+    params, ids, (o_loss, o_grads, o_new) = _inputs(cfg, micro_steps)
+    loss, norm, flags, grads, new = _step(cfg, params, ids)
+    names = list(o_grads)
+    o_norm = O.global_grad_norm([o_grads[n] for n in names])
+    report = []
+    for n in names:
+        report.append((rel_l2(grads[n], o_grads[n]), n))
+    worst = sorted(report, reverse=True)[:6]
+    print(f"\n{cfg.dim}x{cfg.vocab} mb{cfg.micro_batch}x{micro_steps} precision {cfg.precision}: "
+          f"loss {loss:.6f} / {o_loss:.6f}, norm {norm:.6f} / {o_norm:.6f}; worst gradients "
+          + ", ".join(f"{n} {e:.2e}" for e, n in worst))
+    assert flags == (0, 0)
+    assert abs(loss - o_loss) <= tol * abs(o_loss)
+    assert abs(norm - o_norm) <= tol * o_norm
+    for e, n in report:
+        assert e <= tol, (n, e)
+    # (1) the applied update is AdamW of the GPU's own gradients and norm.
+    clip = O.clip_factor(norm, cfg.max_grad_norm)
+    for n in names:
+        want, _, _ = O.adamw_update(params[n], grads[n], np.zeros_like(params[n]),
+                                    np.zeros_like(params[n]), 1, LR, cfg.beta1, cfg.beta2,
+                                    cfg.adam_eps, cfg.weight_decay, clip)
+        d_gpu = new[n].astype(np.float64) - params[n]
+        d_ref = want.astype(np.float64) - params[n]
+        assert rel_l2(d_gpu, d_ref) <= 1e-6, n
+    # (2) on well-conditioned elements the delta is the float64 oracle's.
+    for n in names:
+        g = np.asarray(o_grads[n], np.float64)
+        mask = np.abs(g) >= 0.05 * np.sqrt(np.mean(g * g))
+        d_gpu = new[n].astype(np.float64) - params[n]
+        d_ref = o_new[n].astype(np.float64) - params[n]
+        assert rel_l2(d_gpu[mask], d_ref[mask]) <= tol, n
+
+
+@pytest.mark.parametrize("precision,tol", [(0, 2e-3), (1, 1e-5)])
+def test_c5_widths_micro_batch_16(cuda, precision, tol):
+    """The bench's micro-step (16 sequences of 1024 tokens): paired 256x256 tiles, split-K weight
+    gradients, the weight-gradient stream (TF32), the streaming cross-entropy over 32768 classes."""
+    _check(_cfg("c5", 16, precision), 1, tol)
+
+
+def test_c5_widths_micro_batch_2_lanes(cuda, monkeypatch):
+    """Rank 0's share of the 64-sequence batch on eight GPUs: four micro-steps of two sequences,
+    run two at a time (lanes) with their gradient arenas merged in a fixed order."""
+    monkeypatch.setenv("SPAR_B200_LANES", "2")
+    _check(_cfg("c5", 2, 0), 4, 2e-3)
+
+
+@pytest.mark.parametrize("precision,tol", [(0, 2e-3), (1, 1e-5)])
+def test_c4_widths_padded_vocabulary(cuda, precision, tol):
+    """GPT-2-small widths: 50257 classes (logits padded to a multiple of 4 columns), 12 heads."""
+    _check(_cfg("c4", 8, precision), 1, tol)
