@@ -91,6 +91,7 @@ struct AttnParams {
   uint32_t tiles;  // stationary tiles per (batch, head)
   uint32_t adjacent_pairs;  // forward: items pair query tiles (2p, 2p+1), heaviest first
   uint32_t total;  // work items
+  uint32_t round_out;  // store ctx / dqkv rounded to nearest TF32 (they only feed TF32 products)
 };
 
 __device__ __forceinline__ void record_error() { atomicExch(&g_attn_error, 1); }
@@ -175,6 +176,11 @@ __device__ __forceinline__ Item decode(const AttnParams& p, uint32_t idx, bool d
   it.h = bh - it.b * p.heads;
   it.t = descending ? p.tiles - 1 - tile : tile;
   return it;
+}
+
+__device__ __forceinline__ void round_box(float (&v)[32]) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = round_tf32(v[e]);
 }
 
 // Stages one 32-row x 32-column fp32 box (this warp's rows) and stores it through `map`.
@@ -622,10 +628,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         tc::tmem_load_32x32(o_col + c * 32, o);
         if (qrow < p.seq) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4*>(dst + c * 32 + e) =
-                make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
-                            __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+          for (int e = 0; e < 32; e += 4) {
+            float4 w = make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                                   __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+            if (p.round_out)
+              w = make_float4(round_tf32(w.x), round_tf32(w.y), round_tf32(w.z), round_tf32(w.w));
+            *reinterpret_cast<float4*>(dst + c * 32 + e) = w;
+          }
         }
       }
       tc::tc_fence_before();
@@ -890,6 +899,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);
           if (p.rope && valid) inverse_rope(o, p.rope + static_cast<uint64_t>(q) * (DH / 2) + c * 16);
+          if (p.round_out) round_box(o);
           if (c > 0) {
             if (lane == 0) tc::bulk_wait_read<0>();
             __syncwarp();
@@ -1186,6 +1196,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         __syncwarp();
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);  // dV
+        if (p.round_out) round_box(o);
         store_box(&p.out, stg, o, static_cast<int>(p.vcol + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
         if (lane == 0) {
@@ -1196,6 +1207,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(w[e]);  // dK
         if (p.rope && kv < seq) inverse_rope(o, p.rope + static_cast<uint64_t>(kv) * (DH / 2) + grp * 16);
+        if (p.round_out) round_box(o);
         store_box(&p.out, stg, o, static_cast<int>(p.kcol + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
         if (lane == 0) tc::bulk_commit();
@@ -1360,10 +1372,11 @@ bool attention_supported(uint64_t head_dim) { return head_dim == 32 || head_dim 
 cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_max, float* row_inv,
                                      uint64_t batch, uint64_t seq, uint64_t heads,
                                      uint64_t head_dim, int device, cudaStream_t stream,
-                                     uint64_t kv_heads) {
+                                     uint64_t kv_heads, bool round_out) {
   if (kv_heads == 0) kv_heads = heads;
   AttnParams p;
   base_params(p, batch, seq, heads, head_dim, kv_heads);
+  p.round_out = round_out ? 1u : 0u;
   const uint64_t w = (heads + 2 * kv_heads) * head_dim;  // packed q | k | v row
   if (!make_map(&p.qk128, qkv, w, seq, batch, 1, w, seq * w, 0, 128, false) ||
       !make_map(&p.qkv_mn, qkv, w, seq, batch, 1, w, seq * w, 0, 32, true))
@@ -1384,10 +1397,12 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       float* dqkv, uint64_t batch, uint64_t seq, uint64_t heads,
                                       uint64_t head_dim, int device, cudaStream_t stream,
                                       const float* rope_table, cudaStream_t key_stream,
-                                      cudaEvent_t fork, cudaEvent_t join, uint64_t kv_heads) {
+                                      cudaEvent_t fork, cudaEvent_t join, uint64_t kv_heads,
+                                      bool round_out) {
   if (kv_heads == 0) kv_heads = heads;
   AttnParams p;
   base_params(p, batch, seq, heads, head_dim, kv_heads);
+  p.round_out = round_out ? 1u : 0u;
   const uint64_t d = heads * head_dim;
   const uint64_t w = (heads + 2 * kv_heads) * head_dim;  // packed q | k | v row
   if (!make_map(&p.qk128, qkv, w, seq, batch, 1, w, seq * w, 0, 128, false) ||

@@ -10,6 +10,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <map>
+#include <mutex>
 #include <utility>
 
 #include "spar_b200.h"
@@ -103,6 +105,24 @@ inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Raises (never lowers) the dynamic shared memory `kernel` may be launched with on `device`.
+// A kernel launched with different sizes must never have its limit lowered by a smaller launch:
+// a CUDA graph captured earlier with the larger size re-issues that launch later (and a profiler
+// replaying the graph's nodes re-launches them one by one) under the limit in force at that time,
+// and a launch above the limit fails.
+inline cudaError_t raise_dynamic_smem(const void* kernel, int device, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> limit;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& current = limit[{kernel, device}];
+  if (current >= bytes) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) current = bytes;
+  return e;
 }
 
 // ---------------------------------------------------------------- device reductions

@@ -431,7 +431,11 @@ __global__ void scale_k(T* v, uint64_t n, double f) {
 
 template <typename T>
 __global__ void adamw_k(T* p, const T* g, T* m, T* v, uint64_t n, double lr, double b1, double b2,
-                        double eps, double decay, double c1, double c2) {
+                        double eps, double wd, double c1, double c2) {
+  // The decay factor is formed on the device, as the reference does: a host-side 1 - lr * wd
+  // rounds twice where the device's contracted multiply-add rounds once, which moves float64
+  // parameters by an ulp.
+  const double decay = 1.0 - lr * wd;
   GRID_LOOP(i, n) {
     const double gd = static_cast<double>(g[i]);
     m[i] = static_cast<T>(b1 * static_cast<double>(m[i]) + (1.0 - b1) * gd);
@@ -880,11 +884,10 @@ extern "C" SparCudaStatus spar_cuda_launch_adamw(void* parameter, const void* gr
   if (count == 0) return ok();
   SPAR_SCOPE(device);
   const unsigned g = blocks_for(count, device);
-  const double decay = 1.0 - learning_rate * weight_decay;
   if (dtype == SPAR_CUDA_FLOAT32)
-    adamw_k<float><<<g, 256>>>(tp<float>(parameter), ctp<float>(gradient), tp<float>(first_moment), tp<float>(second_moment), count, learning_rate, beta1, beta2, epsilon, decay, first_correction, second_correction);
+    adamw_k<float><<<g, 256>>>(tp<float>(parameter), ctp<float>(gradient), tp<float>(first_moment), tp<float>(second_moment), count, learning_rate, beta1, beta2, epsilon, weight_decay, first_correction, second_correction);
   else
-    adamw_k<double><<<g, 256>>>(tp<double>(parameter), ctp<double>(gradient), tp<double>(first_moment), tp<double>(second_moment), count, learning_rate, beta1, beta2, epsilon, decay, first_correction, second_correction);
+    adamw_k<double><<<g, 256>>>(tp<double>(parameter), ctp<double>(gradient), tp<double>(first_moment), tp<double>(second_moment), count, learning_rate, beta1, beta2, epsilon, weight_decay, first_correction, second_correction);
   return finish();
 }
 

@@ -43,10 +43,14 @@ __device__ __forceinline__ void ms_combine(float& m, float& s, float m2, float s
   m = mn;
 }
 
+__device__ __forceinline__ float4 round4(float4 v) {
+  return make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+}
+
 __global__ void __launch_bounds__(kCeThreads, 3)
 ce_stream_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                  const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes, uint64_t ld,
-                 uint64_t seq, float grad_scale, int32_t* invalid) {
+                 uint64_t seq, float grad_scale, int32_t* invalid, int round_out) {
   pdl_begin();
   __shared__ float part_m[kCeThreads / 32], part_s[kCeThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -123,6 +127,7 @@ ce_stream_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                            : target == c + 2 ? x[u].z : x[u].w;
             loss[r] = -((zt - M) - log_sum);
           }
+          if (round_out) o = round4(o);
           st_stream(dr + f, o);
         }
       }
@@ -135,7 +140,7 @@ template <int VPL>
 __global__ void __launch_bounds__(256)
 ce_warp_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes, uint64_t ld,
-               uint64_t seq, float grad_scale, int32_t* invalid) {
+               uint64_t seq, float grad_scale, int32_t* invalid, int round_out) {
   pdl_begin();
   const int lane = threadIdx.x & 31;
   const uint64_t vec = classes / 4;
@@ -190,6 +195,7 @@ ce_warp_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                          : target == c + 2 ? v[j].z : v[j].w;
           loss[r] = -((zt - m) - log_sum);
         }
+        if (round_out) o = round4(o);
         dr[f] = o;
       }
     }
@@ -200,7 +206,7 @@ ce_warp_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
 __global__ void __launch_bounds__(256)
 ce_generic_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
                   const int32_t* __restrict__ targets, uint64_t rows, uint64_t classes,
-                  uint64_t ld, uint64_t seq, float grad_scale, int32_t* invalid) {
+                  uint64_t ld, uint64_t seq, float grad_scale, int32_t* invalid, int round_out) {
   pdl_begin();
   __shared__ float scratch[32];
   for (uint64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -226,8 +232,10 @@ ce_generic_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
     const float log_sum = logf(s);
     const float zt = zr[target];
     __syncthreads();
-    for (uint64_t c = threadIdx.x; c < classes; c += blockDim.x)
-      dr[c] = grad_scale * (expf((zr[c] - m) - log_sum) - (c == (uint64_t)target ? 1.f : 0.f));
+    for (uint64_t c = threadIdx.x; c < classes; c += blockDim.x) {
+      const float d = grad_scale * (expf((zr[c] - m) - log_sum) - (c == (uint64_t)target ? 1.f : 0.f));
+      dr[c] = round_out ? round_tf32(d) : d;
+    }
     if (threadIdx.x == 0) loss[r] = -((zt - m) - log_sum);
     __syncthreads();
   }
@@ -238,26 +246,28 @@ ce_generic_kernel(float* __restrict__ loss, float* dlogits, const float* logits,
 cudaError_t cross_entropy_launch(float* loss, float* dlogits, const float* logits,
                                  const int32_t* targets, uint64_t rows, uint64_t classes,
                                  uint64_t ld, uint64_t seq, float grad_scale,
-                                 int32_t* invalid, int device, cudaStream_t stream) {
+                                 int32_t* invalid, int device, cudaStream_t stream,
+                                 bool round_out) {
   const bool vec_ok = classes % 4 == 0 && ld % 4 == 0;
+  const int rnd = round_out ? 1 : 0;
   const uint64_t vec = classes / 4;
   const int sms = sm_count(device);
   if (vec_ok && vec <= 32 * 16) {
     const uint64_t v = (vec + 31) / 32;
     const unsigned grid = grid_for(rows, 8, sms * 16);
     switch (v <= 1 ? 1 : v <= 2 ? 2 : v <= 4 ? 4 : v <= 8 ? 8 : 16) {
-#define SPAR_CE_W(V) case V: launch(ce_warp_kernel<V>, dim3(grid), dim3(256), 0, stream, loss, dlogits, logits, targets, rows, classes, ld, seq, grad_scale, invalid); break;
+#define SPAR_CE_W(V) case V: launch(ce_warp_kernel<V>, dim3(grid), dim3(256), 0, stream, loss, dlogits, logits, targets, rows, classes, ld, seq, grad_scale, invalid, rnd); break;
       SPAR_CE_W(1) SPAR_CE_W(2) SPAR_CE_W(4) SPAR_CE_W(8) SPAR_CE_W(16)
 #undef SPAR_CE_W
     }
   } else if (vec_ok) {
     const unsigned grid = grid_for(rows, 1, sms * 3);
     launch(ce_stream_kernel, dim3(grid), dim3(kCeThreads), 0, stream, loss, dlogits, logits,
-           targets, rows, classes, ld, seq, grad_scale, invalid);
+           targets, rows, classes, ld, seq, grad_scale, invalid, rnd);
   } else {
     const unsigned grid = grid_for(rows, 1, sms * 8);
     launch(ce_generic_kernel, dim3(grid), dim3(256), 0, stream, loss, dlogits, logits, targets, rows, classes, ld,
-                                                seq, grad_scale, invalid);
+                                                seq, grad_scale, invalid, rnd);
   }
   return cudaGetLastError();
 }

@@ -23,7 +23,8 @@ bool attention_supported(uint64_t head_dim);
 cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_max, float* row_inv,
                                      uint64_t batch, uint64_t seq, uint64_t heads,
                                      uint64_t head_dim, int device, cudaStream_t stream,
-                                     uint64_t kv_heads = 0);  // 0: heads (no grouping)
+                                     uint64_t kv_heads = 0,  // 0: heads (no grouping)
+                                     bool round_out = false);  // ctx rounded to nearest TF32
 // dqkv (every column of the rows < seq written) from dctx; delta [batch * heads * seq] scratch.
 cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const float* dctx,
                                       const float* row_max, const float* row_inv, float* delta,
@@ -31,7 +32,8 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       uint64_t head_dim, int device, cudaStream_t stream,
                                       const float* rope_table = nullptr,
                                       cudaStream_t key_stream = nullptr, cudaEvent_t fork = nullptr,
-                                      cudaEvent_t join = nullptr, uint64_t kv_heads = 0);
+                                      cudaEvent_t join = nullptr, uint64_t kv_heads = 0,
+                                      bool round_out = false);  // dqkv rounded to nearest TF32
 
 // Spar's stable sigmoid (src/ops/unary.cpp:55-61 / cuda_kernels.cu:105-111), in fp32.
 __device__ __forceinline__ float stable_sigmoid(float v) {
@@ -94,9 +96,12 @@ __device__ __forceinline__ float gelu_derivative_fast(float x) {
 }
 
 // ---------------------------------------------------------------- launchers (async, on stream)
+// round_out: store y rounded to nearest TF32 (for outputs that only feed TF32 products, which
+// would otherwise truncate them: a systematic shrink of about 2^-11 per operand).
 cudaError_t layernorm_forward_launch(float* y, float* mean, float* rstd, const float* x,
                                      const float* gamma, const float* beta, uint64_t rows,
-                                     uint64_t cols, float eps, int device, cudaStream_t stream);
+                                     uint64_t cols, float eps, int device, cudaStream_t stream,
+                                     bool round_out = false);
 int layernorm_backward_parts(uint64_t rows, int device);
 cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, const float* dy,
                                       const float* x, const float* gamma, const float* mean,
@@ -108,7 +113,8 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
 // Backward workspace: layernorm_backward_parts(rows) * cols floats.
 cudaError_t rmsnorm_forward_launch(float* y, float* rstd, const float* x, const float* weight,
                                    uint64_t rows, uint64_t cols, float eps, int device,
-                                   cudaStream_t stream, uint64_t ld = 0, uint32_t group = 1);
+                                   cudaStream_t stream, uint64_t ld = 0, uint32_t group = 1,
+                                   bool round_out = false);
 cudaError_t rmsnorm_backward_launch(float* dx, float* dweight, const float* dy, const float* x,
                                     const float* weight, const float* rstd, uint64_t rows,
                                     uint64_t cols, int accumulate_params, int accumulate_dx,
@@ -156,10 +162,12 @@ cudaError_t causal_softmax_launch(float* out, const float* in, const float* p, u
                                   uint64_t t, uint64_t ld, float scale, uint64_t zero_fill_block,
                                   int backward, cudaStream_t stream);
 
+// round_out: dlogits stored rounded to nearest TF32 (they only feed TF32 products).
 cudaError_t cross_entropy_launch(float* loss, float* dlogits, const float* logits,
                                  const int32_t* targets, uint64_t rows, uint64_t classes,
                                  uint64_t ld, uint64_t sequence_length, float grad_scale,
-                                 int32_t* invalid_target, int device, cudaStream_t stream);
+                                 int32_t* invalid_target, int device, cudaStream_t stream,
+                                 bool round_out = false);
 
 // Multi-slice gradient norm + clipped AdamW. `norm_state` holds kNormStateDoubles doubles.
 constexpr int kNormStateDoubles = 1024;

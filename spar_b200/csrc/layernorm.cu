@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
 layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
                          float* __restrict__ rstd_out, const float* __restrict__ x,
                          const float* __restrict__ gamma, const float* __restrict__ beta,
-                         uint64_t rows, int cols, float eps, RowMap rm) {
+                         uint64_t rows, int cols, float eps, RowMap rm, int round_out) {
   pdl_begin();
   const int lane = threadIdx.x & 31;
   const int vec_cols = cols >> 2;
@@ -99,6 +99,12 @@ layernorm_forward_kernel(float* __restrict__ y, float* __restrict__ mean_out,
           o.y = (v[j].y - mean) * rstd * g.y + b.y;
           o.z = (v[j].z - mean) * rstd * g.z + b.z;
           o.w = (v[j].w - mean) * rstd * g.w + b.w;
+        }
+        if (round_out) {  // the output only feeds TF32 products: round to nearest once here
+          o.x = round_tf32(o.x);
+          o.y = round_tf32(o.y);
+          o.z = round_tf32(o.z);
+          o.w = round_tf32(o.w);
         }
         yr[f] = o;  // read next by the projection GEMM: left in L2
       }
@@ -305,13 +311,14 @@ int layernorm_backward_parts(uint64_t rows, int device) {
 
 cudaError_t layernorm_forward_launch(float* y, float* mean, float* rstd, const float* x,
                                      const float* gamma, const float* beta, uint64_t rows,
-                                     uint64_t cols, float eps, int device, cudaStream_t stream) {
+                                     uint64_t cols, float eps, int device, cudaStream_t stream,
+                                     bool round_out) {
   const unsigned grid = grid_for(rows, kWarps, sm_count(device) * 8);
   const int c = static_cast<int>(cols);
   switch (vectors_per_lane(cols)) {
 #define SPAR_LN_FWD(V) \
   case V:              \
-    launch(layernorm_forward_kernel<V, false>, dim3(grid), dim3(kWarps * 32), 0, stream, y, mean, rstd, x, gamma, beta, rows, c, eps, RowMap{cols, 1}); \
+    launch(layernorm_forward_kernel<V, false>, dim3(grid), dim3(kWarps * 32), 0, stream, y, mean, rstd, x, gamma, beta, rows, c, eps, RowMap{cols, 1}, round_out ? 1 : 0); \
     break;
     SPAR_LN_FWD(1) SPAR_LN_FWD(2) SPAR_LN_FWD(4) SPAR_LN_FWD(6) SPAR_LN_FWD(8) SPAR_LN_FWD(12)
     SPAR_LN_FWD(16)
@@ -339,8 +346,8 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
 #define SPAR_LN_BWD(V)                                                                          \
   case V: {                                                                                    \
     auto k = layernorm_backward_kernel<V, false>;                                              \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                               static_cast<int>(smem));                         \
+    const cudaError_t se = raise_dynamic_smem(reinterpret_cast<const void*>(k), device, smem);  \
+    if (se != cudaSuccess) return se;                                                          \
     launch(k, dim3(parts), dim3(kWarps * 32), smem, stream, dx, pa, pb, ps, dy, x, gamma, mean, \
            rstd, rows, c, rows_per_block, accumulate_dx, RowMap{cols, 1});                      \
     break;                                                                                     \
@@ -360,14 +367,15 @@ cudaError_t layernorm_backward_launch(float* dx, float* dgamma, float* dbeta, co
 
 cudaError_t rmsnorm_forward_launch(float* y, float* rstd, const float* x, const float* weight,
                                    uint64_t rows, uint64_t cols, float eps, int device,
-                                   cudaStream_t stream, uint64_t ld, uint32_t group) {
+                                   cudaStream_t stream, uint64_t ld, uint32_t group,
+                                   bool round_out) {
   const RowMap rm{ld ? ld : cols, group};
   const unsigned grid = grid_for(rows, kWarps, sm_count(device) * 8);
   const int c = static_cast<int>(cols);
   switch (vectors_per_lane(cols)) {
 #define SPAR_RMS_FWD(V) \
   case V:               \
-    launch(layernorm_forward_kernel<V, true>, dim3(grid), dim3(kWarps * 32), 0, stream, y, nullptr, rstd, x, weight, nullptr, rows, c, eps, rm); \
+    launch(layernorm_forward_kernel<V, true>, dim3(grid), dim3(kWarps * 32), 0, stream, y, nullptr, rstd, x, weight, nullptr, rows, c, eps, rm, round_out ? 1 : 0); \
     break;
     SPAR_RMS_FWD(1) SPAR_RMS_FWD(2) SPAR_RMS_FWD(4) SPAR_RMS_FWD(6) SPAR_RMS_FWD(8) SPAR_RMS_FWD(12)
     SPAR_RMS_FWD(16)
@@ -393,8 +401,8 @@ cudaError_t rmsnorm_backward_launch(float* dx, float* dweight, const float* dy, 
 #define SPAR_RMS_BWD(V)                                                                         \
   case V: {                                                                                    \
     auto k = layernorm_backward_kernel<V, true>;                                               \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                               static_cast<int>(smem));                         \
+    const cudaError_t se = raise_dynamic_smem(reinterpret_cast<const void*>(k), device, smem);  \
+    if (se != cudaSuccess) return se;                                                          \
     launch(k, dim3(parts), dim3(kWarps * 32), smem, stream, dx, workspace, nullptr, nullptr, dy, \
            x, weight, nullptr, rstd, rows, c, rows_per_block, accumulate_dx, rm);               \
     break;                                                                                     \

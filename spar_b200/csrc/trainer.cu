@@ -745,9 +745,9 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
 
 // S = QK^T (lower tiles), P = causal softmax in place, ctx = P V (k <= row).
 cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
-  if (fused_attention)
+  if (fused_attention)  // TF32 mode: ctx only feeds TF32 products, stored rounded to nearest
     return attention_forward_launch(A.qkv, A.ctx, A.stats, A.stats + B * H * T, B, T, H, dh,
-                                    device, s, KVH);
+                                    device, s, KVH, cfg.precision == SPAR_B200_TF32);
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
   const uint64_t ld = 3 * d;
   const uint64_t qkv_bs[2] = {T * ld, dh};
@@ -849,7 +849,9 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
     bool& f;
     ~Reset() { f = false; }
   } reset{sharded_step};
-  cudaError_t e = sharded_step ? gather_params(s) : cudaSuccess;
+  // The error flags describe this step only (a skipped update does not taint the next step).
+  cudaError_t e = cudaMemsetAsync(flags, 0, 2 * sizeof(int32_t), s);
+  if (e == cudaSuccess && sharded_step) e = gather_params(s);
   for (int li = 0; li < step_lanes && e == cudaSuccess; ++li)
     e = cudaMemsetAsync(lanes[li].grads, 0, flat * sizeof(float), s);
   if (e == cudaSuccess && step_lanes > 1) {  // the other lanes start after the zeroing
@@ -916,6 +918,7 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
     if (e_ != cudaSuccess) return runtime(e_);        \
   } while (0)
   const float eps = static_cast<float>(cfg.norm_epsilon);
+  const bool rn = cfg.precision == SPAR_B200_TF32;
   float* P = params;
   float* G = grads;
   // ---------------------------------------------------------------- forward
@@ -932,8 +935,10 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
       continue;
     }
     launches += 2 + 1;  // 2 LayerNorms, softmax (or fused attention)
+    // TF32 mode: the norm outputs, g, ctx, dlogits, du and dqkv only feed TF32 products and are
+    // stored rounded to nearest TF32 (the tensor cores would truncate them: a bias toward zero).
     SPAR_CHECK(layernorm_forward_launch(A.a1, A.mean1, A.rstd1, A.x, P + lo.ln1_g, P + lo.ln1_b,
-                                        N, d, eps, device, s));
+                                        N, d, eps, device, s, rn));
     // qkv = a1 Wqkv + b, RoPE on the q and k thirds in the epilogue. q, k, v only feed
     // attention products: with fused attention they are stored rounded to nearest TF32.
     SPAR_CHECK(gemm(N, 3 * d, d, A.a1, d, false, P + lo.wqkv, 3 * d, false, A.qkv, 3 * d, false,
@@ -943,24 +948,26 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
     SPAR_CHECK(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
                     SPAR_B200_EPI_BIAS_ADD, P + lo.bo, A.x, d, s));
     SPAR_CHECK(layernorm_forward_launch(A.a2, A.mean2, A.rstd2, A.h1, P + lo.ln2_g, P + lo.ln2_b,
-                                        N, d, eps, device, s));
+                                        N, d, eps, device, s, rn));
     SPAR_CHECK(gemm(N, F, d, A.a2, d, false, P + lo.w1, F, false, A.g, F, false,
-                    SPAR_B200_EPI_BIAS_GELU, P + lo.b1, A.u, F, s));
+                    SPAR_B200_EPI_BIAS_GELU, P + lo.b1, A.u, F, s, SPAR_B200_CAUSAL_NONE, 1, 1,
+                    nullptr, nullptr, nullptr, rn));
     SPAR_CHECK(gemm(N, d, F, A.g, F, false, P + lo.w2, d, false, out, d, false,
                     SPAR_B200_EPI_BIAS_ADD, P + lo.b2, A.h1, d, s));
   }
   launches += 1 + 2 + 2;  // final LayerNorm, cross-entropy + loss sum, final LayerNorm backward
   SPAR_CHECK(wait_gather(L + 1, s));
   if (family == SPAR_B200_FAMILY_SPAR)
-    SPAR_CHECK(rmsnorm_forward_launch(hf, rstdf, xL, P + off_lnf_g, N, d, eps, device, s));
+    SPAR_CHECK(rmsnorm_forward_launch(hf, rstdf, xL, P + off_lnf_g, N, d, eps, device, s, 0, 1,
+                                      rn));
   else
     SPAR_CHECK(layernorm_forward_launch(hf, meanf, rstdf, xL, P + off_lnf_g, P + off_lnf_b, N, d,
-                                        eps, device, s));
+                                        eps, device, s, rn));
   SPAR_CHECK(gemm(N, V, d, hf, d, false, P + off_E, d, true, logits, Vp, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // Fused log-softmax + NLL + mean backward; dlogits overwrite the logits in place.
   SPAR_CHECK(cross_entropy_launch(row_loss, logits, logits, ids, N, V, Vp, T, grad_scale,
-                                  flags, device, s));
+                                  flags, device, s, rn));
   SPAR_CHECK(sum_launch(loss_sums + micro, row_loss, N, s));
   // ---------------------------------------------------------------- backward
   // dE += dlogits^T hf (weight-gradient stream) ; dhf = dlogits E
@@ -1013,7 +1020,9 @@ cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s
   float* P = params;
   const float eps = static_cast<float>(cfg.norm_epsilon);
   launches += 2 + 1 + 1;  // 2 RMSNorms, attention, SwiGLU
-  SPAR_TRY(rmsnorm_forward_launch(A.a1, A.rstd1, A.x, P + lo.ln1_g, N, d, eps, device, s));
+  const bool rn = cfg.precision == SPAR_B200_TF32;  // norm outputs only feed TF32 products
+  SPAR_TRY(rmsnorm_forward_launch(A.a1, A.rstd1, A.x, P + lo.ln1_g, N, d, eps, device, s, 0, 1,
+                                  rn));
   if (!qk_norm) {
     // RoPE on the q and k parts in the epilogue; q, k, v stored rounded to nearest TF32.
     SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, P + lo.wqkv, Wq, false, A.qkv, Wq, false,
@@ -1032,7 +1041,8 @@ cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s
   SPAR_TRY(attention_forward(A, s));
   SPAR_TRY(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
                 SPAR_B200_EPI_BIAS_ADD, nullptr, A.x, d, s));
-  SPAR_TRY(rmsnorm_forward_launch(A.a2, A.rstd2, A.h1, P + lo.ln2_g, N, d, eps, device, s));
+  SPAR_TRY(rmsnorm_forward_launch(A.a2, A.rstd2, A.h1, P + lo.ln2_g, N, d, eps, device, s, 0, 1,
+                                  rn));
   SPAR_TRY(gemm(N, Fu, d, A.a2, d, false, P + lo.w1, Fu, false, A.u, Fu, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   SPAR_TRY(swiglu_forward_launch(A.g, F, A.u, Fu, A.u + F, Fu, N, F, device, s));
@@ -1112,7 +1122,8 @@ cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
     return attention_backward_launch(A.qkv, A.ctx, dtmp, A.stats, A.stats + B * H * T, dS, dqkv,
                                      B, T, H, dh, device, s, cfg.use_rope ? rope_tab : nullptr,
                                      two ? ln.key_stream : nullptr, two ? ln.key_fork : nullptr,
-                                     two ? ln.key_join : nullptr, KVH);
+                                     two ? ln.key_join : nullptr, KVH,
+                                     cfg.precision == SPAR_B200_TF32);
   }
   const uint64_t ld = 3 * d;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
@@ -1163,7 +1174,8 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
                 nullptr, nullptr, 0, w));
   SPAR_TRY(mark(0));  // dW2 has read dres
   SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, du, F, false, SPAR_B200_EPI_GELU_BWD,
-                nullptr, A.u, F, s));
+                nullptr, A.u, F, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
+                cfg.precision == SPAR_B200_TF32));
   SPAR_TRY(fork(1));
   SPAR_TRY(gemm(d, F, N, A.a2, d, true, du, F, false, G + lo.w1, F, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, w));
@@ -1316,8 +1328,11 @@ extern "C" SparCudaStatus spar_b200_lm_zero_grad(void* handle, void* stream) {
   if (!handle) return invalid();
   LMTrainer* t = as_trainer(handle);
   DeviceScope scope(t->device);
-  const cudaError_t e = cudaMemsetAsync(t->grads, 0, t->flat * sizeof(float),
-                                        static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaMemsetAsync(t->grads, 0, t->flat * sizeof(float),
+                                  static_cast<cudaStream_t>(stream));
+  // A new accumulation window: the error flags start clear.
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(t->flags, 0, 2 * sizeof(int32_t), static_cast<cudaStream_t>(stream));
   if (e == cudaSuccess) t->stale[1] = false;
   return e == cudaSuccess ? ok() : runtime(e);
 }

@@ -35,12 +35,11 @@ namespace {
 
 #if SPAR_ENABLE_CUDA
 
+// Read on every call (next to a synchronous matmul the lookup costs nothing), so a process can
+// switch modes between steps.
 int float32_precision() {
-  static const int precision = [] {
-    const char* v = std::getenv("SPAR_B200_MATMUL_PRECISION");
-    return (v != nullptr && std::string_view{v} == "tf32") ? SPAR_B200_TF32 : SPAR_B200_TF32X3;
-  }();
-  return precision;
+  const char* v = std::getenv("SPAR_B200_MATMUL_PRECISION");
+  return (v != nullptr && std::string_view{v} == "tf32") ? SPAR_B200_TF32 : SPAR_B200_TF32X3;
 }
 
 [[noreturn]] void fail(std::string_view operation, Device device, SparCudaStatus status) {
@@ -94,18 +93,21 @@ Tensor matmul(const Tensor& a, const Tensor& b, Shape output_shape, std::size_t 
     fail("spar_b200_matmul", device, status);
   }
   int previous{0};
-  if (cudaGetDevice(&previous) == cudaSuccess) {
+  cudaError_t synced{cudaGetDevice(&previous)};
+  if (synced == cudaSuccess) {
     const bool switched{previous != static_cast<int>(device.index())};
     if (switched) {
-      static_cast<void>(cudaSetDevice(static_cast<int>(device.index())));
+      synced = cudaSetDevice(static_cast<int>(device.index()));
     }
-    const cudaError_t synced{cudaDeviceSynchronize()};
+    if (synced == cudaSuccess) {
+      synced = cudaDeviceSynchronize();
+    }
     if (switched) {
       static_cast<void>(cudaSetDevice(previous));
     }
-    if (synced != cudaSuccess) {
-      fail("CUDA matmul synchronization", device, SparCudaStatus{2, static_cast<int>(synced)});
-    }
+  }
+  if (synced != cudaSuccess) {
+    fail("CUDA matmul synchronization", device, SparCudaStatus{2, static_cast<int>(synced)});
   }
   return output;
 #else

@@ -1,0 +1,83 @@
+"""Data-parallel training on several GPUs equals one GPU on the same global batch.
+
+tests/dp_parity_run.py runs two optimiser steps of the runtime under torchrun on 2 GPUs (NCCL
+bucket reduction inside the last micro-step's backward; with the sharded optimiser, the default,
+reduce-scatter + per-piece norm and AdamW + parameter all-gather; SPAR_B200_SHARD_OPT=0 the
+replicated all-reduce path) and in one process on one GPU (16-sequence micro-steps). The mean loss
+of the global batch, the gradient norm of each step, and after step 2 every gradient and first
+moment must agree within the parity bars: relative L2 <= 1e-5 per tensor in 3xTF32; in TF32 (the
+two runs use different micro-batch sizes, hence different tile plans and TF32 rounding) <= 2e-3
+overall and <= 1e-2 per tensor. Parameter updates are compared where the first moment is well
+conditioned (|m| >= 5 % of the tensor's RMS; AdamW's update lr * m / sqrt(v) only tests a sign
+where m cancels to near zero).
+
+Needs two GPUs (skipped otherwise); run with `gpurun --gpus 2`.
+"""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from _util import rel_l2
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _launch(out, precision, world, env):
+    cmd = [sys.executable, os.path.join(HERE, "dp_parity_run.py"), "--out", out,
+           "--precision", str(precision)]
+    if world > 1:
+        cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+               "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
+               "--master-port", str(_free_port()), *cmd[1:]]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=700)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    return dict(np.load(out))
+
+
+@pytest.mark.parametrize("shard", ["1", "0"])
+@pytest.mark.parametrize("precision", [1, 0])
+def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, shard):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, SPAR_B200_SHARD_OPT=shard, NCCL_NVLS_ENABLE="0")
+    one = _launch(str(tmp_path / "one.npz"), precision, 1, env)
+    two = _launch(str(tmp_path / "two.npz"), precision, 2, env)
+    assert int(two["world"]) == 2
+    tol_all, tol_each = (1e-5, 1e-5) if precision == 1 else (2e-3, 1e-2)
+    np.testing.assert_allclose(two["losses"], one["losses"], rtol=tol_all)
+    np.testing.assert_allclose(two["norms"], one["norms"], rtol=tol_all)
+    names = sorted(k.split(":", 1)[1] for k in one if k.startswith("param:"))
+    for kind in ("grad", "m"):
+        flat1 = np.concatenate([one[f"{kind}:{n}"].ravel() for n in names])
+        flat2 = np.concatenate([two[f"{kind}:{n}"].ravel() for n in names])
+        assert rel_l2(flat2, flat1) <= tol_all, kind
+        for n in names:
+            assert rel_l2(two[f"{kind}:{n}"], one[f"{kind}:{n}"]) <= tol_each, (kind, n)
+    from spar_b200.lm import DecoderLM
+
+    sys.path.insert(0, HERE)
+    import dp_parity_run
+
+    lm = DecoderLM(dp_parity_run.config(1, precision), 0)
+    lm.init_normal(0x5EED0009, 0.02)
+    init = lm.state_dict()
+    lm.close()
+    for n in names:
+        m = one[f"m:{n}"].astype(np.float64)
+        mask = np.abs(m) >= 0.05 * np.sqrt(np.mean(m * m))
+        d1 = one[f"param:{n}"].astype(np.float64) - init[n]
+        d2 = two[f"param:{n}"].astype(np.float64) - init[n]
+        assert rel_l2(d2[mask], d1[mask]) <= tol_each, n

@@ -31,10 +31,15 @@ def libs(cuda):
         pytest.skip("reference GPU build absent (python oracle/make_ref.py --variant stock)")
     prod = _lib.load()
     ref = ctypes.CDLL(str(cpu_ref.VARIANT_LIBS["stock"]))
-    for name, (res, args) in _lib.SIGNATURES.items():
-        if name.startswith("spar_cuda_"):
-            fn = getattr(ref, name)
-            fn.restype, fn.argtypes = res, args
+    # Both libraries get the same ctypes signatures (pointers as 64-bit, sizes as uint64): a call
+    # without them would pass pointers as 32-bit C ints.
+    table = {**_lib.SIGNATURES, **_lib.EXTRA_SIGNATURES}
+    names = [n for n in table if n.startswith("spar_cuda_")]
+    assert len(names) == 23
+    for name in names:
+        fn = getattr(ref, name)
+        fn.restype, fn.argtypes = table[name]
+        assert getattr(prod, name).argtypes is not None
     return prod, ref
 
 
@@ -49,8 +54,10 @@ def _both(libs, name, make_args, outs):
     arrays giving each output's initial contents. Returns ([ours], [reference]) host arrays."""
     results = []
     for lib in libs:
+        fn = getattr(lib, name)
+        assert fn.argtypes is not None and fn.restype is not None, name
         dev = [_dev(o.copy()) for o in outs]
-        st = getattr(lib, name)(*make_args(dev))
+        st = fn(*make_args(dev))
         assert (st.code, st.cuda_error) == (0, 0), (name, st.code, st.cuda_error)
         results.append([d.cpu().numpy() for d in dev])
     return results
@@ -192,12 +199,17 @@ def test_embedding_and_targets(libs, dtype, index_dtype):
     bad[77] = vocab + 5
     bad[99] = -1
     gb = _dev(bad)
-    for name, args in (("spar_cuda_launch_validate_embedding_indices",
-                        lambda o: (_ptr(o[0]), _ptr(gb), count, vocab, index_dtype, 0)),
-                       ("spar_cuda_validate_targets",
-                        lambda o: (_ptr(o[0]), _ptr(gb), count, vocab, index_dtype, 0))):
-        ours, ref = _both(libs, name, args, [np.zeros(1, np.int32)])
-        assert ours[0][0] == ref[0][0] == 1, name
+    ours, ref = _both(libs, "spar_cuda_launch_validate_embedding_indices",
+                      lambda o: (_ptr(o[0]), _ptr(gb), count, vocab, index_dtype, 0),
+                      [np.zeros(1, np.int32)])
+    assert ours[0][0] == ref[0][0] == 1
+    # validate_targets reports through a HOST int32 (the reference copies its flag back).
+    for ids_dev, want in ((gi, 0), (gb, 1)):
+        for lib in libs:
+            flag = ctypes.c_int32(7)
+            st = lib.spar_cuda_validate_targets(ctypes.byref(flag), _ptr(ids_dev), count, vocab,
+                                                index_dtype, 0)
+            assert (st.code, flag.value) == (0, want)
 
 
 @pytest.mark.parametrize("language_model", [0, 1])
@@ -273,8 +285,10 @@ def test_strided_copy_and_broadcast_reduce(libs, element_size):
     gext = (ctypes.c_uint64 * 4)(4, 5, 6, 7)
     oext = (ctypes.c_uint64 * 3)(5, 1, 7)
     ostr = (ctypes.c_uint64 * 3)(7, 7, 1)
+    # count is the GRADIENT's element count (the reference loops over gradient elements).
     ours, ref = _both(libs, "spar_cuda_launch_broadcast_reduce",
-                      lambda o: (_ptr(o[0]), _ptr(grad), 4, gext, 3, oext, ostr, 5 * 7, dtype, 0),
+                      lambda o: (_ptr(o[0]), _ptr(grad), 4, gext, 3, oext, ostr, 4 * 5 * 6 * 7,
+                                 dtype, 0),
                       [np.zeros(5 * 7, DT[dtype])])
     _close(ours[0], ref[0], 20 * RTOL[dtype])  # reduction order differs (reference: atomics)
 
@@ -286,6 +300,8 @@ def test_norm_summary_and_adamw(libs, dtype):
     r = np.random.default_rng(19 + dtype)
     n = (1 << 20) + 3
     g = (1e-3 * r.standard_normal(n)).astype(DT[dtype])
+    for lib in libs:
+        assert lib.spar_cuda_gradient_norm_summary.argtypes is not None
     for case in ("finite", "inf", "nan"):
         gg = g.copy()
         if case == "inf":
@@ -330,5 +346,6 @@ def test_invalid_arguments_match_reference(libs):
         ("spar_cuda_launch_strided_copy", (1, 1, 0, None, None, 0, 4, 2, 0)),  # element size
     ]
     for name, args in cases:
+        assert getattr(prod, name).argtypes is not None and getattr(ref, name).argtypes is not None
         a, b = getattr(prod, name)(*args), getattr(ref, name)(*args)
         assert a.code == b.code == 1, (name, a.code, b.code)

@@ -326,3 +326,36 @@ def test_gemm_split_k_with_epilogues(cuda, epi):
     torch.cuda.synchronize()
     assert ops.gemm_error(0) == 0
     assert rel_l2(got.cpu().numpy(), expect) <= tol
+
+
+@pytest.mark.parametrize("dtype", [0, 1])  # SPAR_CUDA_FLOAT32, SPAR_CUDA_FLOAT64
+@pytest.mark.parametrize("shape", [(3, 128, 64, 96), (2, 5, 7, 3), (4, 33, 17, 9), (1, 300, 1, 1),
+                                   (6, 64, 64, 64), (2, 1, 130, 3)])
+def test_contiguous_matmul_any_shape(cuda, shape, dtype):
+    """spar_b200_matmul, the body behind Spar's cuda_blas seam: batched contiguous products of any
+    shape (k or n not a multiple of 4 go through zero-padded staging), float32 in both precisions
+    against float64, float64 (SIMT kernel) to double rounding."""
+    import torch
+    from spar_b200 import _lib
+
+    lib = _lib.load()
+    batch, m, k, n = shape
+    r = np.random.default_rng(sum(shape) + dtype)
+    npt = np.float32 if dtype == 0 else np.float64
+    a = r.standard_normal((batch, m, k)).astype(npt)
+    b = r.standard_normal((batch, k, n)).astype(npt)
+    ref = np.einsum("bmk,bkn->bmn", a.astype(np.float64), b.astype(np.float64))
+    ga, gb = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    for precision, tol in ((0, 2e-3), (1, 1e-5)) if dtype == 0 else ((0, 1e-13),):
+        gc = torch.full((batch, m, n), float("nan"), dtype=ga.dtype, device=cuda)
+        st = lib.spar_b200_matmul(ga.data_ptr(), gb.data_ptr(), gc.data_ptr(), batch, m, k, n,
+                                  dtype, precision, 0, None)
+        assert st.code == 0
+        torch.cuda.synchronize()
+        assert rel_l2(gc.cpu().numpy(), ref) <= tol, (precision, rel_l2(gc.cpu().numpy(), ref))
+    # k == 0: zeros, as the reference seam returns
+    gc = torch.full((batch, m, n), 5.0, dtype=ga.dtype, device=cuda)
+    assert lib.spar_b200_matmul(ga.data_ptr(), gb.data_ptr(), gc.data_ptr(), batch, m, 0, n, dtype,
+                                1, 0, None).code == 0
+    torch.cuda.synchronize()
+    assert not gc.cpu().numpy().any()

@@ -100,9 +100,12 @@ def _check(cfg, micro_steps, tol):
     for n in names:
         report.append((rel_l2(grads[n], o_grads[n]), n))
     worst = sorted(report, reverse=True)[:6]
+    overall = rel_l2(np.concatenate([np.asarray(grads[n], np.float64).ravel() for n in names]),
+                     np.concatenate([np.asarray(o_grads[n], np.float64).ravel() for n in names]))
     print(f"\n{cfg.dim}x{cfg.vocab} mb{cfg.micro_batch}x{micro_steps} precision {cfg.precision}: "
-          f"loss {loss:.6f} / {o_loss:.6f}, norm {norm:.6f} / {o_norm:.6f}; worst gradients "
-          + ", ".join(f"{n} {e:.2e}" for e, n in worst))
+          f"loss {loss:.6f} / {o_loss:.6f}, norm {norm:.6f} / {o_norm:.6f}, all gradients "
+          f"{overall:.2e}; worst tensors " + ", ".join(f"{n} {e:.2e}" for e, n in worst))
+    assert overall <= tol
     assert flags == (0, 0)
     assert abs(loss - o_loss) <= tol * abs(o_loss)
     assert abs(norm - o_norm) <= tol * o_norm
