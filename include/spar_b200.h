@@ -281,6 +281,12 @@ struct SparB200Gemm {
   uint64_t rope_seq;
   uint64_t rope_dim;  /* even */
   uint64_t rope_cols; /* multiple of rope_dim */
+  /* Optional, unbatched GEMMs only: per 32-row block column sums of this product's epilogue     */
+  /* output (before accumulation into C and before output rounding; rows past m count as zero),  */
+  /* written to column_partials[(row / 32) * n + col], a [ceil(m / 32), n] array. Summing its    */
+  /* rows gives the column sums of the result (a bias gradient) without re-reading C. K is then   */
+  /* never split.                                                                               */
+  float* column_partials;
 };
 struct SparCudaStatus spar_b200_gemm(const struct SparB200Gemm* gemm, int device, void* stream);
 

@@ -35,7 +35,7 @@ class SparB200Gemm(ctypes.Structure):
         ("alpha", c_float), ("accumulate", c_int), ("epilogue", c_int), ("bias", c_void_p),
         ("aux", c_void_p), ("ldaux", c_uint64), ("precision", c_int), ("causal", c_int),
         ("round_output", c_int), ("rope_table", c_void_p), ("rope_seq", c_uint64),
-        ("rope_dim", c_uint64), ("rope_cols", c_uint64),
+        ("rope_dim", c_uint64), ("rope_cols", c_uint64), ("column_partials", c_void_p),
     ]
 
 

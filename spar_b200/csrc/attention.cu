@@ -92,6 +92,10 @@ struct AttnParams {
   uint32_t adjacent_pairs;  // forward: items pair query tiles (2p, 2p+1), heaviest first
   uint32_t total;  // work items
   uint32_t round_out;  // store ctx / dqkv rounded to nearest TF32 (they only feed TF32 products)
+  // Backward, optional (seq a multiple of 32): per 32-row block column sums of dqkv (the qkv
+  // bias gradient's partials), [batch * seq / 32, width of a packed row].
+  float* colpart;
+  uint32_t colpart_ld;
 };
 
 __device__ __forceinline__ void record_error() { atomicExch(&g_attn_error, 1); }
@@ -176,6 +180,15 @@ __device__ __forceinline__ Item decode(const AttnParams& p, uint32_t idx, bool d
   it.h = bh - it.b * p.heads;
   it.t = descending ? p.tiles - 1 - tile : tile;
   return it;
+}
+
+// Column sums of one stored 32 x 32 box of dqkv (before rounding) into the partials array.
+__device__ __forceinline__ void box_partials(const AttnParams& p, const float (&v)[32], int col,
+                                             int row, int b) {
+  if (!p.colpart || static_cast<uint32_t>(row) >= p.seq) return;
+  const float cs = box_column_sum(v, true);
+  const uint64_t block = (static_cast<uint64_t>(b) * p.seq + static_cast<uint32_t>(row)) / 32;
+  p.colpart[block * p.colpart_ld + static_cast<uint32_t>(col) + (threadIdx.x & 31)] = cs;
 }
 
 __device__ __forceinline__ void round_box(float (&v)[32]) {
@@ -899,6 +912,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);
           if (p.rope && valid) inverse_rope(o, p.rope + static_cast<uint64_t>(q) * (DH / 2) + c * 16);
+          box_partials(p, o, static_cast<int>(it.h * DH + 32 * c),
+                       static_cast<int>(it.t * 128 + th.quarter * 32), static_cast<int>(it.b));
           if (p.round_out) round_box(o);
           if (c > 0) {
             if (lane == 0) tc::bulk_wait_read<0>();
@@ -1196,6 +1211,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
         __syncwarp();
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(v[e]);  // dV
+        box_partials(p, o, static_cast<int>(p.vcol + it.h * DH + 32 * grp), row,
+                     static_cast<int>(it.b));
         if (p.round_out) round_box(o);
         store_box(&p.out, stg, o, static_cast<int>(p.vcol + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
@@ -1207,6 +1224,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(w[e]);  // dK
         if (p.rope && kv < seq) inverse_rope(o, p.rope + static_cast<uint64_t>(kv) * (DH / 2) + grp * 16);
+        box_partials(p, o, static_cast<int>(p.kcol + it.h * DH + 32 * grp), row,
+                     static_cast<int>(it.b));
         if (p.round_out) round_box(o);
         store_box(&p.out, stg, o, static_cast<int>(p.kcol + it.h * DH + 32 * grp), row,
                   static_cast<int>(it.b));
@@ -1398,11 +1417,14 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       uint64_t head_dim, int device, cudaStream_t stream,
                                       const float* rope_table, cudaStream_t key_stream,
                                       cudaEvent_t fork, cudaEvent_t join, uint64_t kv_heads,
-                                      bool round_out) {
+                                      bool round_out, float* column_partials) {
   if (kv_heads == 0) kv_heads = heads;
+  if (column_partials && seq % 32) return cudaErrorInvalidValue;
   AttnParams p;
   base_params(p, batch, seq, heads, head_dim, kv_heads);
   p.round_out = round_out ? 1u : 0u;
+  p.colpart = column_partials;
+  p.colpart_ld = static_cast<uint32_t>((heads + 2 * kv_heads) * head_dim);
   const uint64_t d = heads * head_dim;
   const uint64_t w = (heads + 2 * kv_heads) * head_dim;  // packed q | k | v row
   if (!make_map(&p.qk128, qkv, w, seq, batch, 1, w, seq * w, 0, 128, false) ||

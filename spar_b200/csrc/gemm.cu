@@ -69,6 +69,7 @@ struct GemmParams {
   int round_out;    // round the stored C to nearest TF32
   const float2* rope;  // optional RoPE table [rope_seq, rope_half]
   uint32_t rope_seq, rope_half, rope_dim, rope_cols;
+  float* colpart;  // optional [ceil(m / 32), n] per-32-row-block column sums of the output
 };
 
 struct TileCoord {
@@ -253,6 +254,10 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
       v[2 * i] = x0 * cs.x - x1 * cs.y;
       v[2 * i + 1] = x0 * cs.y + x1 * cs.x;
     }
+  }
+  if (p.colpart) {  // this box's column sums (a bias gradient's partials), before rounding
+    const float cs = box_column_sum(v, row0 + lane < p.m);
+    if (col0 + lane < p.n) p.colpart[static_cast<uint64_t>(row0 / 32) * p.n + col0 + lane] = cs;
   }
   if (p.round_out) {
 #pragma unroll
@@ -1120,8 +1125,15 @@ GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
   return pl;
 }
 
+// Column partials are written by the GEMM's own epilogue, which a K split hands to the reduction.
+GemmPlan gemm_plan_for(const SparB200Gemm& g, int device) {
+  GemmPlan pl = gemm_plan(g, device);
+  if (g.column_partials) pl.kparts = 1;
+  return pl;
+}
+
 uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device) {
-  const GemmPlan pl = gemm_plan(g, device);
+  const GemmPlan pl = gemm_plan_for(g, device);
   return pl.kparts > 1 ? static_cast<uint64_t>(pl.kparts) * g.m * ((g.n + 3) / 4 * 4) : 0;
 }
 
@@ -1133,7 +1145,7 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
   const bool split = g.precision == SPAR_B200_TF32X3;
   // 3xTF32 keeps its running sums in registers (one 64-column row segment per thread).
-  const GemmPlan plan = gemm_plan(g, device);
+  const GemmPlan plan = gemm_plan_for(g, device);
   const int bn = plan.bn;
   p.sections = split ? 3 : 1;
   p.a_mn_major = g.a_transposed ? 1 : 0;
@@ -1205,6 +1217,7 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
   p.kchunk = 4;  // 4 k-blocks = 128 K elements x 3 sections per hardware-accumulated chunk
   p.kparts = 1;
   p.round_out = g.round_output != 0;
+  p.colpart = g.column_partials;
   if (g.rope_table) {
     p.rope = reinterpret_cast<const float2*>(g.rope_table);
     p.rope_seq = static_cast<uint32_t>(g.rope_seq);
@@ -1313,6 +1326,7 @@ SparCudaStatus gemm_validate(const SparB200Gemm* g) {
     return invalid();
   if ((x.causal == SPAR_B200_CAUSAL_K_UPTO || x.causal == SPAR_B200_CAUSAL_K_FROM) && x.m != x.k)
     return invalid();
+  if (x.column_partials && (b0 * b1 != 1 || x.causal != SPAR_B200_CAUSAL_NONE)) return invalid();
   return ok();
 }
 

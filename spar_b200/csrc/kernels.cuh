@@ -33,7 +33,10 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
                                       const float* rope_table = nullptr,
                                       cudaStream_t key_stream = nullptr, cudaEvent_t fork = nullptr,
                                       cudaEvent_t join = nullptr, uint64_t kv_heads = 0,
-                                      bool round_out = false);  // dqkv rounded to nearest TF32
+                                      bool round_out = false,  // dqkv rounded to nearest TF32
+                                      // optional [batch * seq / 32, packed width] per-32-row
+                                      // column sums of dqkv (seq % 32 == 0)
+                                      float* column_partials = nullptr);
 
 // Spar's stable sigmoid (src/ops/unary.cpp:55-61 / cuda_kernels.cu:105-111), in fp32.
 __device__ __forceinline__ float stable_sigmoid(float v) {
@@ -56,6 +59,45 @@ __device__ __forceinline__ float round_tf32(float v) {
   const uint32_t b = __float_as_uint(v);
   if ((b & 0x7f800000u) == 0x7f800000u) return v;  // inf / nan unchanged
   return __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
+}
+
+// Column sums of a warp's 32 x 32 register box (lane = row, v[c] = column c; rows with
+// live == false count as zero): a transposing butterfly over the warp, after which lane l holds
+// the sum of column l over the 32 rows. 31 shuffles and adds per lane, no shared memory.
+__device__ __forceinline__ float box_column_sum(const float (&v)[32], bool live) {
+  const uint32_t lane = threadIdx.x & 31;
+  float a[16];
+  {
+    const bool up = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float lo = live ? v[i] : 0.f, hi = live ? v[i + 16] : 0.f;
+      a[i] = (up ? hi : lo) + __shfl_xor_sync(0xffffffffu, up ? lo : hi, 16);
+    }
+  }
+  float b[8];
+  {
+    const bool up = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      b[i] = (up ? a[i + 8] : a[i]) + __shfl_xor_sync(0xffffffffu, up ? a[i] : a[i + 8], 8);
+  }
+  float c[4];
+  {
+    const bool up = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      c[i] = (up ? b[i + 4] : b[i]) + __shfl_xor_sync(0xffffffffu, up ? b[i] : b[i + 4], 4);
+  }
+  float d[2];
+  {
+    const bool up = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      d[i] = (up ? c[i + 2] : c[i]) + __shfl_xor_sync(0xffffffffu, up ? c[i] : c[i + 2], 2);
+  }
+  const bool up = lane & 1;
+  return (up ? d[1] : d[0]) + __shfl_xor_sync(0xffffffffu, up ? d[0] : d[1], 1);
 }
 
 __device__ __forceinline__ float gelu_value(float x) {

@@ -305,6 +305,9 @@ class LMTrainer {
   float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
   float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
   float* dh_buf = nullptr;  // Spar family: d(swiglu output) [N, F]
+  // Bias-gradient partials written by the producers of du and dqkv (per 32-row block column
+  // sums, [N / 32, F] then [N / 32, 3d]), so the bias gradients never re-read du or dqkv.
+  float* colpart = nullptr;
   // Fused attention (TF32 mode, head_dim 32 / 64): no [T, T] buffers; dS holds the backward's
   // D = rowsum(dO o O) [B*H*T] instead of dS.
   bool fused_attention = false;
@@ -330,6 +333,7 @@ class LMTrainer {
     float *xL = nullptr, *meanf = nullptr, *rstdf = nullptr, *hf = nullptr, *logits = nullptr;
     float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
     float* dh_buf = nullptr;
+    float* colpart = nullptr;
     float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *splitk_ws2 = nullptr;
     float *row_loss = nullptr, *grads = nullptr;
     void* emb_scratch = nullptr;
@@ -352,6 +356,7 @@ class LMTrainer {
     acts = ln.acts;
     xL = ln.xL; meanf = ln.meanf; rstdf = ln.rstdf; hf = ln.hf; logits = ln.logits;
     dres = ln.dres; dtmp = ln.dtmp; dqkv = ln.dqkv; dS = ln.dS; du = ln.du; dh_buf = ln.dh_buf;
+    colpart = ln.colpart;
     ln_ws = ln.ln_ws; col_ws = ln.col_ws; splitk_ws = ln.splitk_ws; splitk_ws2 = ln.splitk_ws2;
     row_loss = ln.row_loss; grads = ln.grads; emb_scratch = ln.emb_scratch;
     wgrad_stream = ln.wgrad_stream;
@@ -432,7 +437,8 @@ class LMTrainer {
                    bool accumulate, int epi, const float* bias, float* aux, uint64_t ldaux,
                    cudaStream_t s, int causal = SPAR_B200_CAUSAL_NONE, uint64_t b0 = 1,
                    uint64_t b1 = 1, const uint64_t* a_bs = nullptr, const uint64_t* b_bs = nullptr,
-                   const uint64_t* c_bs = nullptr, bool round_out = false, bool rope = false);
+                   const uint64_t* c_bs = nullptr, bool round_out = false, bool rope = false,
+                   float* column_partials = nullptr);
   cudaError_t attention_forward(LayerActs& A, cudaStream_t s);
   cudaError_t attention_backward(LayerActs& A, cudaStream_t s);
   cudaError_t layer_backward(uint64_t l, cudaStream_t s);
@@ -582,6 +588,7 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     f(&ln.dS, fused_attention ? B * H * T : PS);
     f(&ln.du, N * Fu);
     if (family == SPAR_B200_FAMILY_SPAR) f(&ln.dh_buf, N * F);
+    else f(&ln.colpart, (N + 31) / 32 * (F + Wq));
     f(&ln.ln_ws, 3ull * ln_parts * d);  // dgamma, dbeta and dx column-sum partials
     f(&ln.col_ws, col_floats);
     f(&ln.row_loss, N);
@@ -682,7 +689,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
                             bool accumulate, int epi, const float* bias, float* aux,
                             uint64_t ldaux, cudaStream_t s, int causal, uint64_t b0, uint64_t b1,
                             const uint64_t* a_bs, const uint64_t* b_bs, const uint64_t* c_bs,
-                            bool round_out, bool rope) {
+                            bool round_out, bool rope, float* column_partials) {
   SparB200Gemm g{};
   g.m = m;
   g.n = n;
@@ -709,6 +716,7 @@ cudaError_t LMTrainer::gemm(uint64_t m, uint64_t n, uint64_t k, const float* a, 
   g.precision = cfg.precision;
   g.causal = causal;
   g.round_output = round_out;
+  g.column_partials = column_partials;
   if (rope) {  // RoPE on the q and k thirds of the fused projection output
     g.rope_table = rope_tab;
     g.rope_seq = T;
@@ -1123,7 +1131,10 @@ cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
                                      B, T, H, dh, device, s, cfg.use_rope ? rope_tab : nullptr,
                                      two ? ln.key_stream : nullptr, two ? ln.key_fork : nullptr,
                                      two ? ln.key_join : nullptr, KVH,
-                                     cfg.precision == SPAR_B200_TF32);
+                                     cfg.precision == SPAR_B200_TF32,
+                                     family == SPAR_B200_FAMILY_SPAR || T % 32
+                                         ? nullptr
+                                         : colpart + (N + 31) / 32 * F);
   }
   const uint64_t ld = 3 * d;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
@@ -1173,13 +1184,15 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   SPAR_TRY(gemm(F, d, N, A.g, F, true, dres, d, false, G + lo.w2, d, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, w));
   SPAR_TRY(mark(0));  // dW2 has read dres
+  // du = (dres W2^T) o gelu'(u); its epilogue also leaves the b1 gradient's column partials.
   SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, du, F, false, SPAR_B200_EPI_GELU_BWD,
                 nullptr, A.u, F, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
-                cfg.precision == SPAR_B200_TF32));
+                cfg.precision == SPAR_B200_TF32, false, colpart));
   SPAR_TRY(fork(1));
   SPAR_TRY(gemm(d, F, N, A.a2, d, true, du, F, false, G + lo.w1, F, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, w));
-  SPAR_TRY(column_sum_launch(G + lo.b1, du, N, F, F, 1, col_ws, device, w));
+  const uint64_t blocks = (N + 31) / 32;
+  SPAR_TRY(column_sum_launch(G + lo.b1, colpart, blocks, F, F, 1, col_ws, device, w));
   SPAR_TRY(gemm(N, d, F, du, F, false, P + lo.w1, F, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
   // dres += LN2 backward  ->  dL/dh1, whose column sums are the bo gradient (dW2 read dres first)
@@ -1204,7 +1217,11 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   SPAR_TRY(fork(3));
   SPAR_TRY(gemm(d, 3 * d, N, A.a1, d, true, dqkv, ld, false, G + lo.wqkv, ld, true,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, w));
-  SPAR_TRY(column_sum_launch(G + lo.bqkv, dqkv, N, 3 * d, ld, 1, col_ws, device, w));
+  if (fused_attention && T % 32 == 0)  // partials left by the attention backward
+    SPAR_TRY(column_sum_launch(G + lo.bqkv, colpart + blocks * F, blocks, 3 * d, 3 * d, 1, col_ws,
+                               device, w));
+  else
+    SPAR_TRY(column_sum_launch(G + lo.bqkv, dqkv, N, 3 * d, ld, 1, col_ws, device, w));
   SPAR_TRY(mark(2));  // every product of this layer on the weight-gradient stream is done
   SPAR_TRY(gemm(N, d, 3 * d, dqkv, ld, false, P + lo.wqkv, ld, true, dtmp, d, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));

@@ -267,12 +267,52 @@ def smoke_step(device) -> None:
     lm.close()
 
 
+def _measure(cfg: "LMConfig", micro: int, steps: int, warmup: int, precision: int) -> None:
+    """Tokens/s of `steps` graph-replayed training steps of `cfg` (after `warmup` steps), timed
+    with CUDA events on the step's stream; one JSON line."""
+    import json
+    from dataclasses import replace
+
+    import torch
+
+    cfg = replace(cfg, precision=precision)
+    lm = DecoderLM(cfg, 0)
+    lm.init_normal(0x5EED0000 + cfg.dim, 0.02)
+    rng = np.random.default_rng(cfg.vocab)
+    ids = torch.from_numpy(rng.integers(0, cfg.vocab, (micro, cfg.micro_batch, cfg.seq))
+                           .astype(np.int32)).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    for s in range(warmup):
+        lm.train_step(ids, 3e-4, step=s + 1, stream=stream)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(steps):
+        _, _, flags = lm.train_step(ids, 3e-4, step=warmup + s + 1, stream=stream)
+    b.record()
+    torch.cuda.synchronize()
+    lm.close()
+    ms = a.elapsed_time(b) / steps
+    tokens = micro * cfg.micro_batch * cfg.seq
+    print(json.dumps({"config": {"vocab": cfg.vocab, "dim": cfg.dim, "layers": cfg.layers,
+                                 "heads": cfg.heads, "seq": cfg.seq, "micro_batch": cfg.micro_batch,
+                                 "micro_steps": micro},
+                      "precision": "tf32x3" if precision else "tf32", "ms_per_step": round(ms, 3),
+                      "tokens_per_s": round(tokens / ms * 1e3, 1),
+                      "model_tflops": round(tokens * cfg.flops_per_token() / ms / 1e9, 1),
+                      "flags": list(flags)}), flush=True)
+
+
 def _main() -> None:
     """`python -m spar_b200.lm --micro-batch MB --steps S [--family spar --kv-heads K --qk-norm]`:
     S training steps of the C5 decoder (or, with --family spar, Spar's own nn::DecoderLM at the C5
     dimensions: RMSNorm, K key/value heads, SwiGLU with the same hidden size) on one GPU, with
     rank 0's share of the 64-sequence global batch for 16 / MB ranks (4 accumulation micro-steps
-    of MB sequences), synthetic weights and ids; prints the loss and step time."""
+    of MB sequences), synthetic weights and ids; prints the loss and step time.
+
+    `python -m spar_b200.lm --config c1|c4 [--precision tf32x3] [--steps S]`: the step rate of the
+    C1 tiny model (batch 8 x 64 tokens) or the C4 GPT-2-small-shaped model (batch 8 x 1024 tokens,
+    vocabulary 50257), one micro-step per optimiser step, timed on the device."""
     import argparse
     import time
     from dataclasses import replace
@@ -287,7 +327,13 @@ def _main() -> None:
     ap.add_argument("--family", default="ln", choices=["ln", "spar"])
     ap.add_argument("--kv-heads", type=int, default=4)
     ap.add_argument("--qk-norm", action="store_true")
+    ap.add_argument("--config", default="c5", choices=["c1", "c4", "c5"])
+    ap.add_argument("--precision", default="tf32", choices=["tf32", "tf32x3"])
     a = ap.parse_args()
+    if a.config != "c5":
+        _measure(C1 if a.config == "c1" else C4, 1, max(a.steps, 5), 3,
+                 1 if a.precision == "tf32x3" else 0)
+        return
     cfg = replace(C5, micro_batch=a.micro_batch)
     if a.family == "spar":
         cfg = replace(cfg, family=1, kv_heads=a.kv_heads, qk_norm=a.qk_norm)

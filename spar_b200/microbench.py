@@ -3,6 +3,7 @@ than L2, warm-up first) with the achieved rate against the B200 peaks.
 
   python -m spar_b200.microbench all
   python -m spar_b200.microbench gemm --m 8192 --n 4096 --k 4096 [--at] [--bt] [--x3]
+  python -m spar_b200.microbench c3        (the C3 Linear table, TF32 and 3xTF32)
   python -m spar_b200.microbench layernorm_bwd|rmsnorm|swiglu|gelu_bwd|softmax_bwd|cross_entropy|adamw|attention
 
 Bandwidth kernels report algorithmic bytes / time (GB/s); GEMMs report 2mnk / time (TFLOP/s).
@@ -88,6 +89,39 @@ def run_gemm(m, n, k, at=False, bt=False, x3=False, iters=10, epi="none"):
     _, tf = peaks()
     return report(f"gemm {m}x{n}x{k} a_t={int(at)} b_t={int(bt)} {'3xtf32' if x3 else 'tf32'} "
                   f"epi={epi}", ms, 2.0 * m * n * k, "TFLOP/s", tf)
+
+
+def run_c3(iters=10):
+    """The isolated Linear forward and backward products of config C3 (X [8192, K] ~ N(0, 1),
+    W [K, N] ~ N(0, 0.02), dY [8192, N] ~ N(0, 1)) at W = 4096 x 4096, 4096 x 16384 and
+    16384 x 4096, in TF32 and 3xTF32: Y = X W + b (bias epilogue), dX = dY W^T (W read
+    transposed in place), dW = X^T dY (X read transposed in place), and db = column sums of dY
+    (bandwidth: 4 B per element of dY)."""
+    dev = torch.device("cuda")
+    hbm, tf = peaks()
+    m = 8192
+    for k, n in ((4096, 4096), (4096, 16384), (16384, 4096)):
+        x = torch.randn(m, k, device=dev)
+        w = torch.randn(k, n, device=dev) * 0.02
+        dy = torch.randn(m, n, device=dev)
+        bias = torch.randn(n, device=dev) * 0.02
+        y = torch.empty(m, n, device=dev)
+        dx = torch.empty(m, k, device=dev)
+        dw = torch.empty(k, n, device=dev)
+        for prec, tag in ((ops.TF32, "tf32"), (ops.TF32X3, "3xtf32")):
+            fl = 2.0 * m * n * k
+            report(f"c3 Y=XW+b {m}x{k}x{n} {tag}", timed(lambda: ops.matmul(
+                x, w, out=y, precision=prec, epilogue=ops.EPI_BIAS, bias=bias), iters),
+                fl, "TFLOP/s", tf)
+            report(f"c3 dX=dY.W^T {m}x{n}x{k} {tag}", timed(lambda: ops.matmul(
+                dy, w, b_t=True, out=dx, precision=prec), iters), fl, "TFLOP/s", tf)
+            report(f"c3 dW=X^T.dY {k}x{m}x{n} {tag}", timed(lambda: ops.matmul(
+                x, dy, a_t=True, out=dw, precision=prec), iters), fl, "TFLOP/s", tf)
+        db = torch.empty(n, device=dev)
+        report(f"c3 db=sum(dY) {m}x{n}", timed(lambda: ops.column_sum(dy, out=db), iters),
+               4.0 * m * n, "GB/s", hbm)
+        del x, w, dy, y, dx, dw
+        torch.cuda.empty_cache()
 
 
 def run_attention(b=16, t=1024, h=16, dh=64, iters=10):
@@ -212,6 +246,8 @@ def main():
         for name in ("layernorm_bwd", "rmsnorm", "swiglu", "gelu_bwd", "softmax_bwd",
                      "cross_entropy", "adamw"):
             run_bandwidth(name, a.iters)
+    elif a.kernel == "c3":
+        run_c3(a.iters)
     elif a.kernel == "attention":
         run_attention(b=a.batch, iters=a.iters)
     else:

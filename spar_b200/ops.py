@@ -327,10 +327,12 @@ def rope_apply_(x, table, batch: int, t: int, heads: int, d: int, ld: int, inver
 def gemm_desc(m, n, k, a, lda, b, ldb, c, ldc, *, a_t=False, b_t=False, alpha=1.0,
               accumulate=False, epilogue=EPI_NONE, bias=None, aux=None, ldaux=0,
               precision=TF32, causal=CAUSAL_NONE, batch=(1, 1), a_bs=(0, 0), b_bs=(0, 0),
-              c_bs=(0, 0), round_output=False, rope=None) -> SparB200Gemm:
-    """rope = (table, seq, dim, cols) applies RoPE to columns < cols in the epilogue."""
+              c_bs=(0, 0), round_output=False, rope=None, column_partials=None) -> SparB200Gemm:
+    """rope = (table, seq, dim, cols) applies RoPE to columns < cols in the epilogue;
+    column_partials = a device pointer to [ceil(m / 32), n] floats for per-32-row column sums."""
     g = SparB200Gemm()
     g.round_output = int(round_output)
+    g.column_partials = column_partials
     if rope is not None:
         g.rope_table, g.rope_seq, g.rope_dim, g.rope_cols = rope[0].data_ptr(), *rope[1:]
     g.m, g.n, g.k = m, n, k
@@ -352,10 +354,13 @@ def gemm_run(desc: SparB200Gemm, device: int, stream: int) -> None:
 
 
 def matmul(a, b, *, a_t=False, b_t=False, out=None, alpha=1.0, accumulate=False,
-           epilogue=EPI_NONE, bias=None, aux=None, precision=TF32, round_output=False, rope=None):
+           epilogue=EPI_NONE, bias=None, aux=None, precision=TF32, round_output=False, rope=None,
+           column_partials=None):
     """C = alpha * op(a) @ op(b) (+ epilogue) for 2-D row-major float32 tensors.
 
     op(a) = a.T when a_t (a stored [k, m]); op(b) = b.T when b_t (b stored [n, k]).
+    column_partials: optional float32 tensor [ceil(m / 32), n] receiving per-32-row-block column
+    sums of the epilogue output (its rows sum to the column sums of the result).
     """
     _f32(a, "a")
     _f32(b, "b")
@@ -368,7 +373,8 @@ def matmul(a, b, *, a_t=False, b_t=False, out=None, alpha=1.0, accumulate=False,
                      c.shape[1], a_t=a_t, b_t=b_t, alpha=alpha, accumulate=accumulate,
                      epilogue=epilogue, bias=_ptr(bias), aux=_ptr(aux),
                      ldaux=(aux.shape[1] if aux is not None else 0), precision=precision,
-                     round_output=round_output, rope=rope)
+                     round_output=round_output, rope=rope,
+                     column_partials=_ptr(column_partials))
     gemm_run(desc, _dev(a), _stream(a))
     return c
 

@@ -359,3 +359,32 @@ def test_contiguous_matmul_any_shape(cuda, shape, dtype):
                                 1, 0, None).code == 0
     torch.cuda.synchronize()
     assert not gc.cpu().numpy().any()
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+@pytest.mark.parametrize("epi", ["gelu_bwd", "bias", "none"])
+@pytest.mark.parametrize("shape", [(2048, 4096, 1024), (300, 200, 96), (16384, 3072, 256)])
+def test_gemm_column_partials(cuda, shape, epi, precision):
+    """The epilogue's per-32-row column sums (the bias gradient of a product without re-reading
+    its output): their row sums equal the column sums of C (float64 reference) to fp32
+    summation error, whatever tile kernel and epilogue the plan picks; K is never split."""
+    import torch
+    from spar_b200 import ops
+
+    m, n, k = shape
+    r = np.random.default_rng(m + n + k)
+    a = torch.from_numpy(r.standard_normal((m, k)).astype(np.float32)).to(cuda)
+    b = torch.from_numpy((0.02 * r.standard_normal((k, n))).astype(np.float32)).to(cuda)
+    bias = torch.from_numpy(r.standard_normal(n).astype(np.float32)).to(cuda)
+    aux = torch.from_numpy(r.standard_normal((m, n)).astype(np.float32)).to(cuda)
+    e = {"gelu_bwd": ops.EPI_GELU_BWD, "bias": ops.EPI_BIAS, "none": ops.EPI_NONE}[epi]
+    parts = torch.full(((m + 31) // 32, n), float("nan"), device=cuda)
+    c = ops.matmul(a, b, epilogue=e, bias=bias if epi == "bias" else None,
+                   aux=aux if epi == "gelu_bwd" else None, precision=precision,
+                   column_partials=parts)
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+    got = parts.cpu().numpy().astype(np.float64).sum(0)
+    want = c.cpu().numpy().astype(np.float64).sum(0)
+    scale = np.abs(c.cpu().numpy()).astype(np.float64).sum(0)
+    assert np.all(np.abs(got - want) <= 1e-5 * scale + 1e-30)
