@@ -526,6 +526,15 @@ struct SparCudaStatus spar_b200_comm_allreduce_sum(void* comm, float* data, uint
                                                    void* stream);
 struct SparCudaStatus spar_b200_comm_check(void* comm);
 struct SparCudaStatus spar_b200_comm_destroy(void* comm, int abort);
+/* Failure path (no counterpart in the reference, which has no collectives; its error contract   */
+/* is the status code, src/backend/cuda_ops.cppm:194-206). spar_b200_comm_wait waits for         */
+/* `stream` with a deadline, polling the stream and NCCL's asynchronous error state; after an    */
+/* asynchronous error or at the deadline it aborts the communicator (ncclCommAbort) and returns  */
+/* {3, ncclResult}. spar_b200_lm_train_step uses it for its final wait when a communicator is    */
+/* attached, so a rank whose peer left gets code 3 instead of hanging. The deadline is           */
+/* $SPAR_B200_COMM_TIMEOUT_S (default 600 s) or set per communicator.                            */
+struct SparCudaStatus spar_b200_comm_set_timeout(void* comm, double seconds);
+struct SparCudaStatus spar_b200_comm_wait(void* comm, void* stream);
 
 /* Library version string. */
 const char* spar_b200_version(void);

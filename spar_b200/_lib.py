@@ -143,6 +143,8 @@ SIGNATURES = {
     "spar_b200_comm_allreduce_sum": (S, [p, p, u64, p]),
     "spar_b200_comm_check": (S, [p]),
     "spar_b200_comm_destroy": (S, [p, i]),
+    "spar_b200_comm_set_timeout": (S, [p, d]),
+    "spar_b200_comm_wait": (S, [p, p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -9,8 +9,11 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "spar_b200.h"
 
@@ -55,9 +58,20 @@ const NcclApi& api() {
   return a;
 }
 
+// Seconds a bounded wait on a step's collectives may take before the communicator is aborted:
+// $SPAR_B200_COMM_TIMEOUT_S, default 600 (well above any step; a peer that left or hung is the
+// only way to reach it).
+double default_timeout() {
+  const char* e = getenv("SPAR_B200_COMM_TIMEOUT_S");
+  const double v = e ? atof(e) : 0.0;
+  return v > 0.0 ? v : 600.0;
+}
+
 struct Comm {
   ncclComm_t nccl = nullptr;
   int rank = 0, world = 1, device = 0;
+  double timeout_s = default_timeout();
+  bool aborted = false;
 };
 
 // Status for a failed NCCL call: code 3, the ncclResult_t in cuda_error.
@@ -67,14 +81,14 @@ SparCudaStatus nccl_status(ncclResult_t r) { return {r == ncclSuccess ? 0 : 3, s
 
 cudaError_t comm_allreduce_sum(void* comm, float* data, uint64_t count, cudaStream_t stream) {
   const Comm* c = static_cast<const Comm*>(comm);
-  if (!c || !api().ok) return cudaErrorInvalidValue;
+  if (!c || !api().ok || c->aborted) return cudaErrorInvalidValue;
   const ncclResult_t r = api().all_reduce(data, data, count, ncclFloat32, ncclSum, c->nccl, stream);
   return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
 }
 
 cudaError_t comm_allreduce_sum_f64(void* comm, double* data, uint64_t count, cudaStream_t stream) {
   const Comm* c = static_cast<const Comm*>(comm);
-  if (!c || !api().ok) return cudaErrorInvalidValue;
+  if (!c || !api().ok || c->aborted) return cudaErrorInvalidValue;
   const ncclResult_t r = api().all_reduce(data, data, count, ncclFloat64, ncclSum, c->nccl, stream);
   return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
 }
@@ -83,7 +97,7 @@ cudaError_t comm_allreduce_sum_f64(void* comm, double* data, uint64_t count, cud
 // there (the rest of data is left unspecified).
 cudaError_t comm_reduce_scatter_sum(void* comm, float* data, uint64_t shard, cudaStream_t stream) {
   const Comm* c = static_cast<const Comm*>(comm);
-  if (!c || !api().ok) return cudaErrorInvalidValue;
+  if (!c || !api().ok || c->aborted) return cudaErrorInvalidValue;
   const ncclResult_t r = api().reduce_scatter(data, data + static_cast<uint64_t>(c->rank) * shard,
                                               shard, ncclFloat32, ncclSum, c->nccl, stream);
   return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
@@ -92,10 +106,50 @@ cudaError_t comm_reduce_scatter_sum(void* comm, float* data, uint64_t shard, cud
 // In place: every rank's data[rank * shard, + shard) is copied to the same place on all ranks.
 cudaError_t comm_all_gather(void* comm, float* data, uint64_t shard, cudaStream_t stream) {
   const Comm* c = static_cast<const Comm*>(comm);
-  if (!c || !api().ok) return cudaErrorInvalidValue;
+  if (!c || !api().ok || c->aborted) return cudaErrorInvalidValue;
   const ncclResult_t r = api().all_gather(data + static_cast<uint64_t>(c->rank) * shard, data,
                                           shard, ncclFloat32, c->nccl, stream);
   return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+// Waits for `stream` (whose work includes this communicator's collectives) with a deadline,
+// polling the stream and NCCL's asynchronous error state. A collective whose peer left or failed
+// never completes: on an asynchronous error or at the deadline the communicator is aborted
+// (ncclCommAbort stops its kernels, so the stream drains) and {3, ncclResult} is returned; the
+// communicator is unusable afterwards. The communicator stays blocking (collective enqueues never
+// return ncclInProgress), which keeps the step's collectives capturable in a CUDA graph on the
+// calling thread; this wait is where a hang would otherwise show.
+SparCudaStatus comm_wait(void* comm, cudaStream_t stream) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c) return {1, static_cast<int>(cudaErrorInvalidValue)};
+  if (c->aborted) return {3, static_cast<int>(ncclInvalidUsage)};
+  const auto start = std::chrono::steady_clock::now();
+  auto sleep_us = std::chrono::microseconds(20);
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(stream);
+    if (q == cudaSuccess) return {0, 0};
+    if (q != cudaErrorNotReady) return {2, static_cast<int>(q)};
+    ncclResult_t async = ncclSuccess;
+    if (api().async_error) {
+      const ncclResult_t r = api().async_error(c->nccl, &async);
+      if (r != ncclSuccess) async = r;
+    }
+    const double waited =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+    if ((async != ncclSuccess && async != ncclInProgress) || waited > c->timeout_s) {
+      api().abort(c->nccl);  // its kernels see the abort flag and return
+      c->nccl = nullptr;
+      c->aborted = true;
+      const auto stop = std::chrono::steady_clock::now();
+      while (cudaStreamQuery(stream) == cudaErrorNotReady &&
+             std::chrono::steady_clock::now() - stop < std::chrono::seconds(30))
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+      cudaGetLastError();
+      return {3, static_cast<int>(async != ncclSuccess ? async : ncclRemoteError)};
+    }
+    std::this_thread::sleep_for(sleep_us);
+    if (sleep_us < std::chrono::microseconds(1000)) sleep_us *= 2;
+  }
 }
 
 int comm_rank(void* comm) { return comm ? static_cast<const Comm*>(comm)->rank : 0; }
@@ -145,6 +199,7 @@ extern "C" SparCudaStatus spar_b200_comm_allreduce_sum(void* comm, float* data, 
   if (!comm || (count && !data)) return {1, static_cast<int>(cudaErrorInvalidValue)};
   if (count == 0) return {0, 0};
   const Comm* c = static_cast<const Comm*>(comm);
+  if (c->aborted) return {3, static_cast<int>(ncclInvalidUsage)};
   const ncclResult_t r = api().all_reduce(data, data, count, ncclFloat32, ncclSum, c->nccl,
                                           static_cast<cudaStream_t>(stream));
   return nccl_status(r);
@@ -154,17 +209,35 @@ extern "C" SparCudaStatus spar_b200_comm_allreduce_sum(void* comm, float* data, 
 extern "C" SparCudaStatus spar_b200_comm_check(void* comm) {
   if (!comm) return {1, static_cast<int>(cudaErrorInvalidValue)};
   const Comm* c = static_cast<const Comm*>(comm);
+  if (c->aborted) return {3, static_cast<int>(ncclRemoteError)};
   if (!api().async_error) return {0, 0};
   ncclResult_t async = ncclSuccess;
   const ncclResult_t r = api().async_error(c->nccl, &async);
   return nccl_status(r != ncclSuccess ? r : async);
 }
 
-// Tears the communicator down; abort != 0 cancels outstanding operations (failure path).
+// Tears the communicator down; abort != 0 cancels outstanding operations (failure path). A
+// communicator already aborted by a bounded wait only frees its handle.
 extern "C" SparCudaStatus spar_b200_comm_destroy(void* comm, int abort) {
   if (!comm) return {0, 0};
   Comm* c = static_cast<Comm*>(comm);
-  const ncclResult_t r = abort ? api().abort(c->nccl) : api().destroy(c->nccl);
+  const ncclResult_t r = c->aborted ? ncclSuccess
+                         : abort    ? api().abort(c->nccl)
+                                    : api().destroy(c->nccl);
   delete c;
   return nccl_status(r);
+}
+
+// Deadline of the bounded waits on this communicator's collectives (seconds, > 0).
+extern "C" SparCudaStatus spar_b200_comm_set_timeout(void* comm, double seconds) {
+  if (!comm || !(seconds > 0.0)) return {1, static_cast<int>(cudaErrorInvalidValue)};
+  static_cast<Comm*>(comm)->timeout_s = seconds;
+  return {0, 0};
+}
+
+// Bounded wait for `stream` (see comm_wait): {0,0} when it finished, {3, ncclResult} after an
+// asynchronous NCCL error or the deadline (the communicator is then aborted), {2, cudaError} for
+// a CUDA error.
+extern "C" SparCudaStatus spar_b200_comm_wait(void* comm, void* stream) {
+  return comm_wait(comm, static_cast<cudaStream_t>(stream));
 }

@@ -40,6 +40,7 @@ cudaError_t comm_reduce_scatter_sum(void* comm, float* data, uint64_t shard, cud
 cudaError_t comm_all_gather(void* comm, float* data, uint64_t shard, cudaStream_t stream);
 int comm_rank(void* comm);
 int comm_size(void* comm);
+SparCudaStatus comm_wait(void* comm, cudaStream_t stream);
 
 namespace {
 
@@ -1478,8 +1479,15 @@ done:
   e = cudaMemcpyAsync(sums, t->loss_sums, micro_steps * sizeof(float), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaMemcpyAsync(norm_state, t->norm_state, 2 * sizeof(double), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaMemcpyAsync(flags, t->flags, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return runtime(e);
+  if (t->comm) {
+    // Bounded: a peer that left makes the step's collectives wait forever; the communicator is
+    // then aborted and the step reports code 3 (the caller destroys the communicator).
+    const SparCudaStatus w = comm_wait(t->comm, s);
+    if (w.code != 0) return w;
+  } else if ((e = cudaStreamSynchronize(s)) != cudaSuccess) {
+    return runtime(e);
+  }
   double total = 0.0;
   for (uint64_t m = 0; m < micro_steps; ++m) total += sums[m];
   if (loss_out) *loss_out = static_cast<float>(total / (rows / t->world));

@@ -128,3 +128,47 @@ def allreduce_sum(arena: np.ndarray, buckets, reduce_fn) -> np.ndarray:
     for off, cnt in buckets:
         reduce_fn(arena[off:off + cnt])
     return arena
+
+
+class RankLost(RuntimeError):
+    """A data-parallel peer did not reach the next step (it exited or stopped between steps)."""
+
+    def __init__(self, step: int, missing: list[int], left: list[int]):
+        self.step, self.missing, self.left = step, missing, left
+        super().__init__(f"step {step}: ranks {missing} did not arrive"
+                         + (f" (ranks {left} left)" if left else ""))
+
+
+class Heartbeat:
+    """Host-side liveness check between optimiser steps, through the process group's key-value
+    store (no collective, no GPU work). Before launching step s every rank records that it reached
+    s and waits, with a deadline, until every rank has; a rank that exited or stopped between
+    steps is named in RankLost before any collective of step s is launched, so no rank blocks in
+    a collective whose peer is gone. A rank leaving on purpose calls leave(), which lets the
+    others fail at once instead of at the deadline. (Inside a step, a peer that dies is caught by
+    the runtime's bounded wait: spar_b200_comm_wait, code 3.)"""
+
+    def __init__(self, store, rank: int, world: int, timeout: float = 60.0, poll: float = 0.01,
+                 prefix: str = "spar_b200/heartbeat"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout, self.poll, self.prefix = timeout, poll, prefix
+
+    def leave(self) -> None:
+        self.store.set(f"{self.prefix}/left/{self.rank}", "1")
+
+    def arrive(self, step: int) -> None:
+        """Records this rank at `step`, then waits for all ranks (RankLost at the deadline, or
+        as soon as a missing rank has left)."""
+        import time
+
+        self.store.set(f"{self.prefix}/{step}/{self.rank}", "1")
+        deadline = time.monotonic() + self.timeout
+        while True:
+            missing = [r for r in range(self.world)
+                       if not self.store.check([f"{self.prefix}/{step}/{r}"])]
+            if not missing:
+                return
+            left = [r for r in missing if self.store.check([f"{self.prefix}/left/{r}"])]
+            if left or time.monotonic() > deadline:
+                raise RankLost(step, missing, left)
+            time.sleep(self.poll)

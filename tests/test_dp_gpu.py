@@ -81,3 +81,25 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, shard):
         d1 = one[f"param:{n}"].astype(np.float64) - init[n]
         d2 = two[f"param:{n}"].astype(np.float64) - init[n]
         assert rel_l2(d2[mask], d1[mask]) <= tol_each, n
+
+
+def test_peer_missing_a_step_gets_code_3(cuda, tmp_path):
+    """A peer that stays alive but skips a step: the other rank's collectives can never complete;
+    the runtime's bounded wait (5 s here) aborts the communicator and the step returns code 3,
+    the device context stays usable. Two GPUs, NVLS off."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = str(tmp_path / "seen.txt")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port",
+           str(_free_port()), os.path.join(HERE, "dp_failure_run.py"), "--out", out]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    seen = open(out).read()
+    assert seen.startswith("code 3 after"), seen
+    waited = float(seen.split("after ")[1].split("s")[0])
+    assert 4.5 <= waited < 60.0
+    assert seen.endswith("device ok 12")
