@@ -168,7 +168,7 @@ cudaError_t qk_norm_rope_launch(float* out, const float* raw, uint64_t tokens, u
                                 uint64_t heads, uint64_t kv_heads, uint64_t head_dim, uint64_t ld,
                                 const float* wq, const float* wk, float* rstd,
                                 const float* rope_table, float eps, int device,
-                                cudaStream_t stream);
+                                cudaStream_t stream, bool round_out = true);
 // Backward in place over the dq | dk part of dqk; dwq / dwk (+)= the weight gradients; workspace
 // qk_norm_backward_parts(tokens) * 2 * head_dim floats.
 int qk_norm_backward_parts(uint64_t tokens, int device);
@@ -252,5 +252,15 @@ cudaError_t embedding_backward_launch(float* grad_weight, const float* grad_out,
                                       const int32_t* ids, uint64_t count, uint64_t vocab,
                                       uint64_t dim, void* scratch, int device,
                                       cudaStream_t stream);
+
+// Grouped-query attention on the unfused path: k | v (kv_heads heads at column kcol of the
+// packed [tokens, ld] projection) expanded to `heads` heads in out [tokens, 2 * heads * dh], and
+// the reverse group sum of d(expanded) into dqkv's k | v columns.
+cudaError_t repeat_kv_launch(float* out, const float* qkv, uint64_t tokens, uint64_t heads,
+                             uint64_t kv_heads, uint64_t dh, uint64_t ld, uint64_t kcol,
+                             int device, cudaStream_t stream);
+cudaError_t group_sum_launch(float* dqkv, const float* drep, uint64_t tokens, uint64_t heads,
+                             uint64_t kv_heads, uint64_t dh, uint64_t ld, uint64_t kcol,
+                             int device, cudaStream_t stream);
 
 }  // namespace spar_b200

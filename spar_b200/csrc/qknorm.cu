@@ -25,7 +25,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 qk_norm_rope_kernel(float* __restrict__ out, const float* __restrict__ raw, uint64_t tokens,
                     uint32_t seq, uint32_t heads, uint32_t kv_heads, uint64_t ld,
                     const float* __restrict__ wq, const float* __restrict__ wk,
-                    float* __restrict__ rstd, const float2* __restrict__ rope, float eps) {
+                    float* __restrict__ rstd, const float2* __restrict__ rope, float eps,
+                    int round_out) {
   pdl_begin();
   constexpr uint32_t kLanes = DH / 4;  // lanes per head
   const uint32_t lane = threadIdx.x & 31;
@@ -48,8 +49,10 @@ qk_norm_rope_kernel(float* __restrict__ out, const float* __restrict__ raw, uint
 #pragma unroll
       for (uint32_t o = kLanes / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (!active) continue;
-      if (h >= qk_heads) {  // value head: rounded copy
-        dst[j] = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+      if (h >= qk_heads) {  // value head: copy (rounded to nearest TF32 in TF32 mode)
+        dst[j] = round_out ? make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z),
+                                         round_tf32(v.w))
+                           : v;
         continue;
       }
       const float r = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(DH)) + eps);
@@ -62,7 +65,9 @@ qk_norm_rope_kernel(float* __restrict__ out, const float* __restrict__ raw, uint
         y = make_float4(y.x * c0.x - y.y * c0.y, y.x * c0.y + y.y * c0.x, y.z * c1.x - y.w * c1.y,
                         y.z * c1.y + y.w * c1.x);
       }
-      dst[j] = make_float4(round_tf32(y.x), round_tf32(y.y), round_tf32(y.z), round_tf32(y.w));
+      dst[j] = round_out ? make_float4(round_tf32(y.x), round_tf32(y.y), round_tf32(y.z),
+                                       round_tf32(y.w))
+                         : y;
       if (c == 0)
         rstd[is_q ? t * heads + h : tokens * heads + t * kv_heads + (h - heads)] = r;
     }
@@ -162,17 +167,17 @@ cudaError_t qk_norm_rope_launch(float* out, const float* raw, uint64_t tokens, u
                                 uint64_t heads, uint64_t kv_heads, uint64_t head_dim, uint64_t ld,
                                 const float* wq, const float* wk, float* rstd,
                                 const float* rope_table, float eps, int device,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, bool round_out) {
   const unsigned grid = grid_for(tokens, kWarps, sm_count(device) * 8);
   const float2* rope = reinterpret_cast<const float2*>(rope_table);
   const uint32_t s = static_cast<uint32_t>(seq), h = static_cast<uint32_t>(heads),
                  kv = static_cast<uint32_t>(kv_heads);
   if (head_dim == 64)
     return launch(qk_norm_rope_kernel<64>, dim3(grid), dim3(kWarps * 32), 0, stream, out, raw,
-                  tokens, s, h, kv, ld, wq, wk, rstd, rope, eps);
+                  tokens, s, h, kv, ld, wq, wk, rstd, rope, eps, round_out ? 1 : 0);
   if (head_dim == 32)
     return launch(qk_norm_rope_kernel<32>, dim3(grid), dim3(kWarps * 32), 0, stream, out, raw,
-                  tokens, s, h, kv, ld, wq, wk, rstd, rope, eps);
+                  tokens, s, h, kv, ld, wq, wk, rstd, rope, eps, round_out ? 1 : 0);
   return cudaErrorInvalidValue;
 }
 
@@ -196,6 +201,62 @@ cudaError_t qk_norm_backward_launch(float* dqk, const float* raw, uint64_t token
   return launch(qk_weight_sum_kernel, dim3(1), dim3(128), 0, stream, dwq, dwk,
                 static_cast<const float*>(workspace), parts, static_cast<int>(head_dim),
                 accumulate);
+}
+
+// Grouped-query attention on the unfused (3xTF32) path, as Spar's repeat_kv_heads
+// (src/nn/attention.cpp:77-94) and its backward: k | v of kv_heads heads, read from the packed
+// projection [tokens, ld] at column kcol, expanded to `heads` heads ([tokens, 2 * heads * dh],
+// query head h reading key / value head h / group); and the reverse, each key / value head's
+// gradient the sum of its group's heads in head order (deterministic).
+__global__ void repeat_kv_kernel(float* __restrict__ out, const float* __restrict__ qkv,
+                                 uint64_t tokens, uint32_t heads, uint32_t kv_heads, uint32_t dh,
+                                 uint64_t ld, uint64_t kcol) {
+  pdl_begin();
+  const uint32_t group = heads / kv_heads;
+  const uint64_t d = static_cast<uint64_t>(heads) * dh, per_token = 2 * d;
+  const uint64_t n = tokens * per_token;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t t = i / per_token, c = i % per_token;
+    const uint64_t part = c / d, h = (c % d) / dh, e = c % dh;  // part 0 = k, 1 = v
+    out[i] = qkv[t * ld + kcol + part * kv_heads * dh + (h / group) * dh + e];
+  }
+}
+
+__global__ void group_sum_kernel(float* __restrict__ dqkv, const float* __restrict__ drep,
+                                 uint64_t tokens, uint32_t heads, uint32_t kv_heads, uint32_t dh,
+                                 uint64_t ld, uint64_t kcol) {
+  pdl_begin();
+  const uint32_t group = heads / kv_heads;
+  const uint64_t d = static_cast<uint64_t>(heads) * dh, kvd = static_cast<uint64_t>(kv_heads) * dh;
+  const uint64_t n = tokens * 2 * kvd;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t t = i / (2 * kvd), c = i % (2 * kvd);
+    const uint64_t part = c / kvd, kh = (c % kvd) / dh, e = c % dh;
+    const float* src = drep + t * 2 * d + part * d + kh * group * dh + e;
+    float acc = 0.f;
+    for (uint32_t g = 0; g < group; ++g) acc += src[static_cast<uint64_t>(g) * dh];
+    dqkv[t * ld + kcol + c] = acc;
+  }
+}
+
+cudaError_t repeat_kv_launch(float* out, const float* qkv, uint64_t tokens, uint64_t heads,
+                             uint64_t kv_heads, uint64_t dh, uint64_t ld, uint64_t kcol,
+                             int device, cudaStream_t stream) {
+  const uint64_t n = tokens * 2 * heads * dh;
+  return launch(repeat_kv_kernel, dim3(grid_for(n, 256, sm_count(device) * 16)), dim3(256), 0,
+                stream, out, qkv, tokens, static_cast<uint32_t>(heads),
+                static_cast<uint32_t>(kv_heads), static_cast<uint32_t>(dh), ld, kcol);
+}
+
+cudaError_t group_sum_launch(float* dqkv, const float* drep, uint64_t tokens, uint64_t heads,
+                             uint64_t kv_heads, uint64_t dh, uint64_t ld, uint64_t kcol,
+                             int device, cudaStream_t stream) {
+  const uint64_t n = tokens * 2 * kv_heads * dh;
+  return launch(group_sum_kernel, dim3(grid_for(n, 256, sm_count(device) * 16)), dim3(256), 0,
+                stream, dqkv, drep, tokens, static_cast<uint32_t>(heads),
+                static_cast<uint32_t>(kv_heads), static_cast<uint32_t>(dh), ld, kcol);
 }
 
 }  // namespace spar_b200

@@ -227,7 +227,7 @@ SparCudaStatus plan_params(const SparB200LMConfig& c, ParamLayout& pl) {
     // DecoderLM's checks (src/nn/decoder.cpp:17-49) and this runtime's: TF32 with the fused
     // attention (head_dim 32 or 64).
     const uint64_t kvh = c.num_kv_heads ? c.num_kv_heads : H;
-    if (kvh > H || H % kvh != 0 || c.precision != SPAR_B200_TF32 || (dh != 32 && dh != 64) ||
+    if (kvh > H || H % kvh != 0 || (dh != 32 && dh != 64) ||
         (c.qk_norm && !(c.qk_norm_epsilon > 0.0)) || F % 32 != 0)
       return invalid();
     plan_spar_family(c, pl, o, take);
@@ -309,6 +309,9 @@ class LMTrainer {
   // Bias-gradient partials written by the producers of du and dqkv (per 32-row block column
   // sums, [N / 32, F] then [N / 32, 3d]), so the bias gradients never re-read du or dqkv.
   float* colpart = nullptr;
+  // Spar family on the unfused (3xTF32) attention path with grouped key / value heads: k | v
+  // expanded to the query heads [N, 2d] (rebuilt in the backward), and its gradient.
+  float *kvrep = nullptr, *dkvrep = nullptr;
   // Fused attention (TF32 mode, head_dim 32 / 64): no [T, T] buffers; dS holds the backward's
   // D = rowsum(dO o O) [B*H*T] instead of dS.
   bool fused_attention = false;
@@ -335,6 +338,7 @@ class LMTrainer {
     float *dres = nullptr, *dtmp = nullptr, *dqkv = nullptr, *dS = nullptr, *du = nullptr;
     float* dh_buf = nullptr;
     float* colpart = nullptr;
+    float *kvrep = nullptr, *dkvrep = nullptr;
     float *ln_ws = nullptr, *col_ws = nullptr, *splitk_ws = nullptr, *splitk_ws2 = nullptr;
     float *row_loss = nullptr, *grads = nullptr;
     void* emb_scratch = nullptr;
@@ -358,6 +362,8 @@ class LMTrainer {
     xL = ln.xL; meanf = ln.meanf; rstdf = ln.rstdf; hf = ln.hf; logits = ln.logits;
     dres = ln.dres; dtmp = ln.dtmp; dqkv = ln.dqkv; dS = ln.dS; du = ln.du; dh_buf = ln.dh_buf;
     colpart = ln.colpart;
+    kvrep = ln.kvrep;
+    dkvrep = ln.dkvrep;
     ln_ws = ln.ln_ws; col_ws = ln.col_ws; splitk_ws = ln.splitk_ws; splitk_ws2 = ln.splitk_ws2;
     row_loss = ln.row_loss; grads = ln.grads; emb_scratch = ln.emb_scratch;
     wgrad_stream = ln.wgrad_stream;
@@ -590,6 +596,10 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
     f(&ln.du, N * Fu);
     if (family == SPAR_B200_FAMILY_SPAR) f(&ln.dh_buf, N * F);
     else f(&ln.colpart, (N + 31) / 32 * (F + Wq));
+    if (!fused_attention && KVH != H) {
+      f(&ln.kvrep, N * 2 * d);
+      f(&ln.dkvrep, N * 2 * d);
+    }
     f(&ln.ln_ws, 3ull * ln_parts * d);  // dgamma, dbeta and dx column-sum partials
     f(&ln.col_ws, col_floats);
     f(&ln.row_loss, N);
@@ -615,6 +625,9 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
         {N, d, F, 0, 1, 1, 1},      {d, d, N, 1, 0, 1, 1},   {N, d, d, 0, 1, 1, 1},
         {T, dh, T, 1, 0, B, H},     {T, T, dh, 0, 1, B, H},  {T, dh, T, 0, 0, B, H},
         {T, dh, T, 1, 0, B, H},     {d, 3 * d, N, 1, 0, 1, 1}, {N, d, 3 * d, 0, 1, 1, 1},
+        // Spar family: packed q | k | v rows of Wq, gate | up rows of Fu
+        {N, Wq, d, 0, 0, 1, 1},     {d, Wq, N, 1, 0, 1, 1},  {N, d, Wq, 0, 1, 1, 1},
+        {N, Fu, d, 0, 0, 1, 1},     {d, Fu, N, 1, 0, 1, 1},  {N, d, Fu, 0, 1, 1, 1},
     };
     for (const Shape& sh : shapes) {
       SparB200Gemm g{};
@@ -758,18 +771,28 @@ cudaError_t LMTrainer::attention_forward(LayerActs& A, cudaStream_t s) {
     return attention_forward_launch(A.qkv, A.ctx, A.stats, A.stats + B * H * T, B, T, H, dh,
                                     device, s, KVH, cfg.precision == SPAR_B200_TF32);
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
-  const uint64_t ld = 3 * d;
-  const uint64_t qkv_bs[2] = {T * ld, dh};
+  // q from the packed projection (rows of Wq floats); k, v from it too, or (grouped key / value
+  // heads) from their expansion to the query heads, rows of 2d floats.
+  const uint64_t ldq = Wq;
+  uint64_t ldkv = Wq;
+  const float* k = A.qkv + d;
+  const float* v = A.qkv + 2 * d;
+  if (KVH != H) {
+    SPAR_TRY(repeat_kv_launch(kvrep, A.qkv, N, H, KVH, dh, Wq, d, device, s));
+    ldkv = 2 * d;
+    k = kvrep;
+    v = kvrep + d;
+  }
+  const uint64_t q_bs[2] = {T * ldq, dh};
+  const uint64_t kv_bs[2] = {T * ldkv, dh};
   const uint64_t p_bs[2] = {H * T * T, T * T};
   const uint64_t ctx_bs[2] = {T * d, dh};
   const float* q = A.qkv;
-  const float* k = A.qkv + d;
-  const float* v = A.qkv + 2 * d;
-  SPAR_TRY(gemm(T, T, dh, q, ld, false, k, ld, true, A.p, T, false, SPAR_B200_EPI_NONE, nullptr,
-                nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, qkv_bs, qkv_bs, p_bs));
+  SPAR_TRY(gemm(T, T, dh, q, ldq, false, k, ldkv, true, A.p, T, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, q_bs, kv_bs, p_bs));
   SPAR_TRY(causal_softmax_launch(A.p, A.p, nullptr, B * H, T, T, scale, 128, 0, s));
-  SPAR_TRY(gemm(T, dh, T, A.p, T, false, v, ld, false, A.ctx, d, false, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, qkv_bs, ctx_bs));
+  SPAR_TRY(gemm(T, dh, T, A.p, T, false, v, ldkv, false, A.ctx, d, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, kv_bs, ctx_bs));
   return cudaSuccess;
 }
 
@@ -1036,7 +1059,7 @@ cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s
     // RoPE on the q and k parts in the epilogue; q, k, v stored rounded to nearest TF32.
     SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, P + lo.wqkv, Wq, false, A.qkv, Wq, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1,
-                  nullptr, nullptr, nullptr, true, cfg.use_rope != 0));
+                  nullptr, nullptr, nullptr, rn, cfg.use_rope != 0));
   } else {
     // The q / k norms come before RoPE (attention.cpp:212-215): project, then one pass per
     // token normalises each q / k head, rotates it and writes q | k | v rounded to TF32.
@@ -1045,7 +1068,7 @@ cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
     SPAR_TRY(qk_norm_rope_launch(A.qkv, A.qkv_raw, N, T, H, KVH, dh, Wq, P + lo.qn, P + lo.kn,
                                  A.qk_rstd, cfg.use_rope ? rope_tab : nullptr,
-                                 static_cast<float>(cfg.qk_norm_epsilon), device, s));
+                                 static_cast<float>(cfg.qk_norm_epsilon), device, s, rn));
   }
   SPAR_TRY(attention_forward(A, s));
   SPAR_TRY(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
@@ -1067,7 +1090,8 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
   float* P = params;
   float* G = grads;
   launches += 2 * 2 + 1 + 1 + (qk_norm ? 2 : 0);  // RMSNorm bwd, attention, SwiGLU bwd, qk norms
-  const bool conc = wgrad_enabled && !profiling;
+  // (3xTF32 keeps one stream: its hi / lo operand workspace is shared by the products.)
+  const bool conc = wgrad_enabled && !profiling && cfg.precision == SPAR_B200_TF32;
   cudaStream_t w = conc ? wgrad_stream : s;
   auto fork = [&](int i) -> cudaError_t {
     if (!conc) return cudaSuccess;
@@ -1101,9 +1125,12 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
   SPAR_TRY(mark(1));  // dWo has read dres
   SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
-                true));
-  // attention: dctx (dtmp) -> dqkv, dq / dk already rotated back through RoPE
+                cfg.precision == SPAR_B200_TF32));
+  // attention: dctx (dtmp) -> dqkv; the fused kernels rotate dq / dk back through RoPE, the
+  // unfused path does it after the products (q and k heads are consecutive in each row).
   SPAR_TRY(attention_backward(A, s));
+  if (cfg.use_rope && !fused_attention)
+    SPAR_TRY(rope_apply_launch(dqkv, rope_tab, N, T, H + KVH, dh, Wq, 1, device, s));
   if (qk_norm)  // through the q / k norms, in place (weight gradients accumulate)
     SPAR_TRY(qk_norm_backward_launch(dqkv, A.qkv_raw, N, H, KVH, dh, Wq, P + lo.qn, P + lo.kn,
                                      A.qk_rstd, G + lo.qn, G + lo.kn, 1, ln_ws, device, s));
@@ -1137,27 +1164,35 @@ cudaError_t LMTrainer::attention_backward(LayerActs& A, cudaStream_t s) {
                                          ? nullptr
                                          : colpart + (N + 31) / 32 * F);
   }
-  const uint64_t ld = 3 * d;
   const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
-  const uint64_t qkv_bs[2] = {T * ld, dh};
+  // Grouped key / value heads: the products run on the expansion to the query heads (rebuilt
+  // here), their k / v gradients land in dkvrep and are summed per group into dqkv.
+  const bool grouped = KVH != H;
+  const uint64_t ldq = Wq, ldkv = grouped ? 2 * d : Wq;
+  if (grouped) SPAR_TRY(repeat_kv_launch(kvrep, A.qkv, N, H, KVH, dh, Wq, d, device, s));
+  const uint64_t q_bs[2] = {T * ldq, dh};
+  const uint64_t kv_bs[2] = {T * ldkv, dh};
   const uint64_t p_bs[2] = {H * T * T, T * T};
   const uint64_t ctx_bs[2] = {T * d, dh};
   const float* q = A.qkv;
-  const float* k = A.qkv + d;
-  const float* v = A.qkv + 2 * d;
+  const float* k = grouped ? kvrep : A.qkv + d;
+  const float* v = grouped ? kvrep + d : A.qkv + 2 * d;
+  float* dk = grouped ? dkvrep : dqkv + d;
+  float* dv = grouped ? dkvrep + d : dqkv + 2 * d;
   // dV = P^T dctx (k >= row)
-  SPAR_TRY(gemm(T, dh, T, A.p, T, true, dtmp, d, false, dqkv + 2 * d, ld, false,
+  SPAR_TRY(gemm(T, dh, T, A.p, T, true, dtmp, d, false, dv, ldkv, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs,
-                ctx_bs, qkv_bs));
+                ctx_bs, kv_bs));
   // dP = dctx V^T (lower tiles), dS = softmax backward (scaled) in place
-  SPAR_TRY(gemm(T, T, dh, dtmp, d, false, v, ld, true, dS, T, false, SPAR_B200_EPI_NONE, nullptr,
-                nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, ctx_bs, qkv_bs, p_bs));
+  SPAR_TRY(gemm(T, T, dh, dtmp, d, false, v, ldkv, true, dS, T, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_LOWER, B, H, ctx_bs, kv_bs, p_bs));
   SPAR_TRY(causal_softmax_launch(dS, dS, A.p, B * H, T, T, scale, 128, 1, s));
   // dQ = dS K (k <= row), dK = dS^T Q (k >= row)
-  SPAR_TRY(gemm(T, dh, T, dS, T, false, k, ld, false, dqkv, ld, false, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, qkv_bs, qkv_bs));
-  SPAR_TRY(gemm(T, dh, T, dS, T, true, q, ld, false, dqkv + d, ld, false, SPAR_B200_EPI_NONE,
-                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs, qkv_bs, qkv_bs));
+  SPAR_TRY(gemm(T, dh, T, dS, T, false, k, ldkv, false, dqkv, ldq, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_UPTO, B, H, p_bs, kv_bs, q_bs));
+  SPAR_TRY(gemm(T, dh, T, dS, T, true, q, ldq, false, dk, ldkv, false, SPAR_B200_EPI_NONE,
+                nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_K_FROM, B, H, p_bs, q_bs, kv_bs));
+  if (grouped) SPAR_TRY(group_sum_launch(dqkv, dkvrep, N, H, KVH, dh, Wq, d, device, s));
   return cudaSuccess;
 }
 

@@ -400,8 +400,9 @@ def test_spar_family_sharded_one_rank_matches_replicated(cuda, monkeypatch):
         assert rel_l2(a, b) <= 1e-6
 
 
-@pytest.mark.parametrize("kv_heads,qk_norm", [(2, True), (4, False), (1, True)])
-def test_spar_family_grads_match_oracle(cuda, kv_heads, qk_norm):
+@pytest.mark.parametrize("kv_heads,qk_norm,precision", [(2, True, 0), (4, False, 0), (1, True, 0),
+                                                     (2, True, 1), (4, False, 1)])
+def test_spar_family_grads_match_oracle(cuda, kv_heads, qk_norm, precision):
     """Every gradient of one Spar-family step (two micro-steps) against the float64
     restatement: relative L2 over all gradients <= 3e-3, per tensor <= 1e-2 (TF32 products; with
     one key/value head for four query heads each dK / dV entry sums four heads' TF32 products,
@@ -411,7 +412,7 @@ def test_spar_family_grads_match_oracle(cuda, kv_heads, qk_norm):
     c = dict(vocab=64, dim=128, hidden=256, layers=2, heads=4, kv_heads=kv_heads,
              qk_norm=int(qk_norm))
     cfg = LMConfig(vocab=64, dim=128, hidden=256, layers=2, heads=4, seq=64, micro_batch=2,
-                   family=1, kv_heads=kv_heads, qk_norm=qk_norm)
+                   family=1, kv_heads=kv_heads, qk_norm=qk_norm, precision=precision)
     params = O.spar_family_parameters(c, 0x5EED0601 + kv_heads)
     ids = O.Random(0x5EED1601).bounded(2 * 2 * 64, 64).reshape(2, 2, 64).astype(np.int32)
     lm = DecoderLM(cfg, 0)
@@ -426,8 +427,10 @@ def test_spar_family_grads_match_oracle(cuda, kv_heads, qk_norm):
         total = g if total is None else {k: total[k] + g[k] for k in g}
     o_grads = {k: v / len(ids) for k, v in total.items()}
     assert flags == (0, 0)
-    assert abs(loss - o_loss) <= 2e-3 * abs(o_loss)
+    # 3xTF32 (unfused attention, grouped heads expanded and summed back): the 1e-5 bar.
+    tol_loss, tol_all, tol_each = (2e-3, 3e-3, 1e-2) if precision == 0 else (1e-5, 1e-5, 1e-5)
+    assert abs(loss - o_loss) <= tol_loss * abs(o_loss)
     names = list(o_grads)
-    assert rel_l2(_flat(grads, names), _flat(o_grads, names)) <= 3e-3
+    assert rel_l2(_flat(grads, names), _flat(o_grads, names)) <= tol_all
     for n in names:
-        assert rel_l2(grads[n], o_grads[n]) <= 1e-2, n
+        assert rel_l2(grads[n], o_grads[n]) <= tol_each, n
