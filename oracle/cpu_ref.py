@@ -72,6 +72,13 @@ def load(variant: str = "cpu"):
             fn.restype = c_int
         lib.ref_warmup_cosine.argtypes = [c_double, c_double, c_uint64, c_uint64, c_uint64]
         lib.ref_warmup_cosine.restype = c_double
+        if hasattr(lib, "ref_lm_step_fused"):  # the drop-in build only
+            lib.ref_lm_step_fused.argtypes = (
+                [c_int64] * 8 + [c_double, c_double, POINTER(F), I32, c_double, c_double, c_double,
+                                 c_double, c_double, c_double, F, POINTER(c_double), POINTER(F),
+                                 POINTER(F), c_int64, POINTER(c_int64), POINTER(c_double),
+                                 POINTER(c_int64)])
+            lib.ref_lm_step_fused.restype = c_int
         lib.ref_train_sample_seconds.argtypes = [c_int64] * 6
         lib.ref_train_sample_seconds.restype = c_double
         lib.ref_lm_step_seconds.argtypes = [c_int64] * 10
@@ -206,6 +213,35 @@ def lm_step(params: dict, names, ids, cfg: dict, lr, opt: dict, device: int = -1
                            opt["eps"], opt["weight_decay"], opt["max_grad_norm"], _p(loss),
                            ctypes.byref(norm), arr(gs), arr(outs), device), lib)
     return float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs))
+
+
+def lm_step_fused(params: dict, names, ids, cfg: dict, lr, opt: dict, device: int = 0):
+    """ref_lm_step with the product's fused operations recorded on Spar's tape (drop-in build):
+    (loss, norm, grads, new, hook_calls, hook_norms, hook_order) for the grad_ready slots (per
+    block: ln1 gain, ln2 gain, up-projection weight)."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    micro, batch, t = ids.shape
+    ps = [_f(params[n]) for n in names]
+    gs = [np.empty_like(p) for p in ps]
+    outs = [np.empty_like(p) for p in ps]
+    arr = lambda lst: (F * len(lst))(*[_p(a) for a in lst])
+    loss = np.zeros(1, np.float32)
+    norm = c_double(0.0)
+    slots = 3 * cfg["layers"]
+    calls = np.zeros(slots, np.int64)
+    norms = np.zeros(slots, np.float64)
+    order = np.full(slots * micro, -1, np.int64)
+    lib = load("b200")
+    _check(lib.ref_lm_step_fused(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"],
+                                 cfg["heads"], batch, t, micro, cfg.get("eps", 1e-5),
+                                 cfg.get("rope_theta", 1e4), arr(ps), ids.ctypes.data_as(I32), lr,
+                                 opt["beta1"], opt["beta2"], opt["eps"], opt["weight_decay"],
+                                 opt["max_grad_norm"], _p(loss), ctypes.byref(norm), arr(gs),
+                                 arr(outs), device, calls.ctypes.data_as(POINTER(c_int64)),
+                                 norms.ctypes.data_as(POINTER(c_double)),
+                                 order.ctypes.data_as(POINTER(c_int64))), lib)
+    return (float(loss[0]), norm.value, dict(zip(names, gs)), dict(zip(names, outs)), calls, norms,
+            order)
 
 
 def _spar_dims(cfg):

@@ -170,7 +170,8 @@ REPO = HERE.parent
 #                               adopts the drop-in would be: src/backend/cuda_kernels.cu left out and
 #                               libspar_b200.so linked in its place (its spar_cuda_* entry points),
 #                               and the product's spar_b200/spar/cuda_blas.cppm compiled in place of
-#                               src/backend/cuda_blas.cppm. Every other reference source unchanged.
+#                               src/backend/cuda_blas.cppm; the product's spar_b200/spar/fused.cppm
+#                               (module spar.b200) added. Every other reference source unchanged.
 #   stock libspar_ref_stock.so  the unchanged reference GPU path (its own cuda_kernels.cu, built
 #                               with nvcc for sm_100a, and cuBLAS): the GPU bar, timed only.
 VARIANTS = {"cpu": "libspar_ref.so", "b200": "libspar_ref_b200.so", "stock": "libspar_ref_stock.so"}
@@ -180,7 +181,8 @@ def _inputs(src: Path, variant: str) -> list[Path]:
     files = [*src.rglob("*.cppm"), *src.rglob("*.cpp"), *src.rglob("*.cu"), *src.rglob("*.hpp"),
              HERE / "ref_driver.cpp", Path(__file__)]
     if variant == "b200":
-        files += [REPO / "spar_b200" / "spar" / "cuda_blas.cppm", *(REPO / "include").glob("*.h")]
+        files += [REPO / "spar_b200" / "spar" / "cuda_blas.cppm",
+                  REPO / "spar_b200" / "spar" / "fused.cppm", *(REPO / "include").glob("*.h")]
     return files
 
 
@@ -197,8 +199,12 @@ def build_variant(src: Path, variant: str, jobs: int) -> Path:
     try:
         units = []
         glue = REPO / "spar_b200" / "spar" / "cuda_blas.cppm"
-        for cppm in sorted(src.rglob("*.cppm")):
-            if variant == "b200" and cppm.relative_to(src).as_posix() == "backend/cuda_blas.cppm":
+        interfaces = sorted(src.rglob("*.cppm"))
+        if variant == "b200":  # the product's fused differentiable operations (module spar.b200)
+            interfaces.append(REPO / "spar_b200" / "spar" / "fused.cppm")
+        for cppm in interfaces:
+            if variant == "b200" and cppm.is_relative_to(src) and \
+                    cppm.relative_to(src).as_posix() == "backend/cuda_blas.cppm":
                 cppm = glue  # the product's module in place of the reference's cuBLAS seam
             _, tu = convert_interface(cppm, build)
             if tu:
@@ -213,7 +219,7 @@ def build_variant(src: Path, variant: str, jobs: int) -> Path:
         if variant == "b200":
             # cuda_ops.cppm includes "cuda_kernels.hpp": here it resolves to the product's header.
             (build / "cuda_kernels.hpp").write_text('#include "spar_cuda_kernels.h"\n')
-            flags += [f"-I{REPO / 'include'}"]
+            flags += [f"-I{REPO / 'include'}", "-DSPAR_B200_FUSED=1"]
             link = [f"-L{REPO / 'spar_b200'}", "-l:libspar_b200.so",
                     "-Wl,-rpath,$ORIGIN/../../spar_b200", *link]
         if variant == "stock":

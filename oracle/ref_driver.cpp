@@ -8,6 +8,9 @@
 // SelfAttention (bias, RoPE) and Linear modules, Spar's autograd, LM cross-entropy,
 // clip_grad_norm, AdamW and warmup-cosine schedule.
 #include "spar.hpp"
+#ifdef SPAR_B200_FUSED
+#include "spar.b200.hpp"  // the product's fused differentiable operations (drop-in build only)
+#endif
 
 #include <chrono>
 #include <cstdio>
@@ -132,6 +135,29 @@ struct Model {
     p.push_back(lnf_b);
     return p;
   }
+#ifdef SPAR_B200_FUSED
+  // The same decoder with the product's fused operations recorded on Spar's tape: LayerNorm,
+  // the MLP's up projection + bias + GELU, and (in the caller) the LM cross-entropy. Every
+  // up-projection weight and LayerNorm gain passes through b200::grad_ready with `hook`.
+  Tensor logits_fused(const Tensor& ids,
+                      const std::function<void(int, const Tensor&)>& hook) {
+    int slot = 0;
+    auto ready = [&](const nn::Parameter& p) {
+      const int id = slot++;
+      return b200::grad_ready(p.tensor(), [id, &hook](const Tensor& g) { hook(id, g); });
+    };
+    Tensor h = embedding.forward(ids);
+    for (Block& b : blocks) {
+      const Tensor a1 = b200::layer_norm(h, ready(b.ln1_g), b.ln1_b.tensor(), eps);
+      const Tensor h1 = add(h, b.attn.forward(a1));
+      const Tensor a2 = b200::layer_norm(h1, ready(b.ln2_g), b.ln2_b.tensor(), eps);
+      const Tensor g = b200::linear_gelu(a2, ready(b.up.weight()), b.up.bias()->tensor());
+      h = add(h1, b.down.forward(g));
+    }
+    const Tensor hf = b200::layer_norm(h, lnf_g.tensor(), lnf_b.tensor(), eps);
+    return matmul(hf, embedding.weight().tensor().transpose(0, 1));
+  }
+#endif
   Tensor logits(const Tensor& ids) {
     Tensor h = embedding.forward(ids);
     for (Block& b : blocks) {
@@ -558,6 +584,54 @@ double ref_train_sample_seconds(int64_t vocab, int64_t d, int64_t f, int64_t hea
   });
   return seconds;
 }
+
+#ifdef SPAR_B200_FUSED
+// ref_lm_step with the product's fused operations (logits_fused + b200::language_model_cross_
+// entropy) on Device::cuda(device), through Spar's own autograd, clip and AdamW. hook_calls[i]
+// and hook_norms[i] report how often grad_ready slot i fired and the norm of the gradient it saw
+// (slots: per block ln1 gain, ln2 gain, up-projection weight); hook_order lists the slots in
+// firing order (3 * layers * micro entries).
+int ref_lm_step_fused(int64_t vocab, int64_t d, int64_t f, int64_t layers, int64_t heads,
+                      int64_t batch, int64_t t, int64_t micro, double eps, double theta,
+                      const float* const* params, const int32_t* ids, double lr, double beta1,
+                      double beta2, double adam_eps, double wd, double max_norm, float* loss_out,
+                      double* norm_out, float** grads, float** out_params, int64_t device,
+                      int64_t* hook_calls, double* hook_norms, int64_t* hook_order) {
+  return guarded([&] {
+    Random rng{1};
+    Model model(vocab, d, f, layers, heads, theta, eps, rng);
+    std::vector<nn::Parameter> ps = model.parameters();
+    for (std::size_t i = 0; i < ps.size(); ++i) load(ps[i], params[i]);
+    const Device dev = device_of(device);
+    nn::move_to(std::span<nn::Parameter>{ps}, dev);
+    const int64_t slots = 3 * layers;
+    for (int64_t i = 0; i < slots; ++i) hook_calls[i] = 0;
+    int64_t fired = 0;
+    auto hook = [&](int id, const Tensor& g) {
+      ++hook_calls[id];
+      hook_order[fired++] = id;
+      const Tensor c = g.detach().to(Device::cpu()).contiguous();
+      double s = 0.0;
+      for (float v : std::as_const(c).span<float>()) s += static_cast<double>(v) * v;
+      hook_norms[id] = std::sqrt(s);
+    };
+    double total = 0.0;
+    for (int64_t mi = 0; mi < micro; ++mi) {
+      Tensor tid = ids_from_host(ids + mi * batch * t, {batch, t}).to(dev);
+      Tensor loss = b200::language_model_cross_entropy(model.logits_fused(tid, hook), tid);
+      total += scalar_of(loss);
+      Tensor scaled = multiply_scalar(loss, 1.0 / static_cast<double>(micro));
+      scaled.backward();
+    }
+    *loss_out = static_cast<float>(total / static_cast<double>(micro));
+    for (std::size_t i = 0; i < ps.size(); ++i) to_host(ps[i].grad(), grads[i]);
+    *norm_out = training::clip_grad_norm(ps, max_norm).total_norm;
+    optim::AdamW opt{ps, lr, beta1, beta2, adam_eps, wd};
+    opt.step();
+    for (std::size_t i = 0; i < ps.size(); ++i) to_host(ps[i].tensor(), out_params[i]);
+  });
+}
+#endif
 
 // Seconds per training step (forward, LM loss, backward, clip, AdamW) of the LN/GELU decoder
 // with N(0, 0.02) weights on [batch, t] ids, on `device` (< 0: CPU), after `warmup` untimed

@@ -108,7 +108,8 @@ __device__ __forceinline__ void adamw_element(float& p, float g, float& m, float
 __global__ void __launch_bounds__(256)
 adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
              float* __restrict__ v, uint64_t count, const double* __restrict__ state,
-             AdamWArgs args, const AdamWArgs* __restrict__ args_dev, int32_t* nonfinite_flag) {
+             AdamWArgs args, const AdamWArgs* __restrict__ args_dev, int32_t* nonfinite_flag,
+             float* __restrict__ rounded) {
   pdl_begin();
   // Scalars by value, or (args_dev != nullptr) from device memory, which a replayed CUDA graph
   // reads afresh every step.
@@ -124,7 +125,8 @@ adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restri
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   const uint64_t start = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const bool aligned = ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
-                         reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15) == 0;
+                         reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v) |
+                         reinterpret_cast<uintptr_t>(rounded)) & 15) == 0;
   const uint64_t n4 = aligned ? count / 4 : 0;
   for (uint64_t i = start; i < n4; i += stride) {
     float4 pv = reinterpret_cast<float4*>(p)[i];
@@ -138,6 +140,9 @@ adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restri
     reinterpret_cast<float4*>(p)[i] = pv;
     reinterpret_cast<float4*>(m)[i] = mv;
     reinterpret_cast<float4*>(v)[i] = vv;
+    if (rounded)
+      reinterpret_cast<float4*>(rounded)[i] =
+          make_float4(round_tf32(pv.x), round_tf32(pv.y), round_tf32(pv.z), round_tf32(pv.w));
   }
   for (uint64_t i = n4 * 4 + start; i < count; i += stride) {
     float pv = p[i], mv = m[i], vv = v[i];
@@ -145,6 +150,7 @@ adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restri
     p[i] = pv;
     m[i] = mv;
     v[i] = vv;
+    if (rounded) rounded[i] = round_tf32(pv);
   }
 }
 
@@ -184,17 +190,38 @@ AdamWArgs adamw_args(double max_norm, double lr, double beta1, double beta2, dou
 cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double* norm_state,
                          double max_norm, double lr, double beta1, double beta2, double eps,
                          double weight_decay, uint64_t step, int32_t* nonfinite_flag, int device,
-                         cudaStream_t stream, const AdamWArgs* args_dev) {
+                         cudaStream_t stream, const AdamWArgs* args_dev,
+                         const float* param_base, float* rounded_base) {
   const AdamWArgs a = adamw_args(max_norm, lr, beta1, beta2, eps, weight_decay, step);
   const int sms = sm_count(device);
   for (uint64_t i = 0; i < slice_count; ++i) {
     const Slice& s = slices[i];
     if (s.count == 0) continue;
     const unsigned grid = grid_for((s.count + 3) / 4, 256, sms * 8);
+    float* rounded = rounded_base ? rounded_base + (s.parameter - param_base) : nullptr;
     launch(adamw_kernel, dim3(grid), dim3(256), 0, stream, s.parameter, s.gradient, s.first_moment,
                                            s.second_moment, s.count, norm_state, a, args_dev,
-                                           nonfinite_flag);
+                                           nonfinite_flag, rounded);
   }
+  return cudaGetLastError();
+}
+
+namespace {
+__global__ void round_copy_kernel(float* __restrict__ dst, const float* __restrict__ src,
+                                  uint64_t count) {
+  pdl_begin();
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += stride)
+    dst[i] = round_tf32(src[i]);
+}
+}  // namespace
+
+cudaError_t round_copy_launch(float* dst, const float* src, uint64_t count, int device,
+                              cudaStream_t stream) {
+  if (count == 0) return cudaSuccess;
+  launch(round_copy_kernel, dim3(grid_for(count, 256, sm_count(device) * 16)), dim3(256), 0,
+         stream, dst, src, count);
   return cudaGetLastError();
 }
 

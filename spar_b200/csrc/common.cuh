@@ -107,6 +107,30 @@ inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// cudaMallocAsync from the current device's memory pool, which is first told (once per device)
+// to keep freed memory reserved instead of returning it to the driver at every synchronisation:
+// with the default release threshold of 0, each synchronous call that takes a large workspace
+// (the 3xTF32 operand splits: 1.6 GB for an 8192 x 16384 x 4096 product) would map and unmap it
+// again, which measured slower than the product itself. Memory stays with the pool up to its peak.
+inline cudaError_t stream_alloc(void** ptr, size_t bytes, cudaStream_t stream) {
+  static std::mutex mu;
+  static bool done[64] = {};
+  int device = 0;
+  if (cudaGetDevice(&device) == cudaSuccess && device >= 0 && device < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[device]) {
+      cudaMemPool_t pool = nullptr;
+      if (cudaDeviceGetMemPool(&pool, device) == cudaSuccess) {
+        uint64_t keep = ~0ull;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      }
+      cudaGetLastError();
+      done[device] = true;
+    }
+  }
+  return cudaMallocAsync(ptr, bytes, stream);
+}
+
 // Raises (never lowers) the dynamic shared memory `kernel` may be launched with on `device`.
 // A kernel launched with different sizes must never have its limit lowered by a smaller launch:
 // a CUDA graph captured earlier with the larger size re-issues that launch later (and a profiler

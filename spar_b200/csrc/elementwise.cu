@@ -435,7 +435,7 @@ extern "C" SparCudaStatus spar_b200_column_sum(float* out, const float* x, uint6
   }
   const int parts = column_sum_parts(rows, cols, device);
   float* ws = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), parts * cols * sizeof(float), s);
+  cudaError_t e = stream_alloc(reinterpret_cast<void**>(&ws), parts * cols * sizeof(float), s);
   if (e != cudaSuccess) return runtime(e);
   e = column_sum_launch(out, x, rows, cols, ld, accumulate, ws, device, s);
   const cudaError_t f = cudaFreeAsync(ws, s);

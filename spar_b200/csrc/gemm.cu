@@ -255,7 +255,9 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, EpiState& st, 
       v[2 * i + 1] = x0 * cs.y + x1 * cs.x;
     }
   }
-  if (p.colpart) {  // this box's column sums (a bias gradient's partials), before rounding
+  // This box's column sums (a bias gradient's partials), before rounding. Boxes wholly below
+  // row m (the rest of a tile that overhangs the matrix) have no row of the partials array.
+  if (p.colpart && row0 < p.m) {
     const float cs = box_column_sum(v, row0 + lane < p.m);
     if (col0 + lane < p.n) p.colpart[static_cast<uint64_t>(row0 / 32) * p.n + col0 + lane] = cs;
   }
@@ -833,6 +835,61 @@ __global__ void split_tf32_kernel(float* __restrict__ hi, float* __restrict__ lo
   }
 }
 
+// 3xTF32 as one TF32 product of depth 3 kp (kp = k rounded up to a multiple of 4): the operands
+// are written with their three K sections side by side, A' = [hi | hi | lo] and B' = [hi; lo; hi]
+// (sections zero-padded from k to kp), so A' B' = hi hi + hi lo + lo hi accumulated in fp32 by the
+// fast TF32 kernels (paired-SM 256-column tiles, split-K, every epilogue) instead of a dedicated
+// three-section kernel. `k_inner`: K runs along the source rows' contiguous dimension (the
+// section offset s * kp is added to the column; otherwise to the row). parts: 0 = (hi, hi, lo),
+// 1 = (hi, lo, hi).
+__global__ void split_concat_kernel(float* __restrict__ dst, const float* __restrict__ src,
+                                    uint64_t inner, uint64_t rows, uint64_t ld, uint64_t out_ld,
+                                    uint64_t kp, int k_inner, int parts) {
+  pdl_begin();
+  // Covers the padded extent along K (kp instead of k) so the pad is written as zeros.
+  const uint64_t inner_p = k_inner ? kp : inner, rows_p = k_inner ? rows : kp;
+  const uint64_t total = inner_p * rows_p;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const uint64_t x = i % inner_p, r = i / inner_p;
+    const bool real = x < inner && r < rows;
+    const float v = real ? src[r * ld + x] : 0.f;
+    const float h = round_tf32(v);
+    const float l = round_tf32(v - h);
+    const float sec[3] = {h, parts == 0 ? h : l, parts == 0 ? l : h};
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const uint64_t o = k_inner ? r * out_ld + q * kp + x : (q * kp + r) * out_ld + x;
+      dst[o] = sec[q];
+    }
+  }
+}
+
+// Whether a 3xTF32 product runs as one TF32 product over K-concatenated split operands (unbatched,
+// non-causal) rather than in the three-section kernel.
+bool concat_x3(const SparB200Gemm& g) {
+  return g.precision == SPAR_B200_TF32X3 && (g.batch[0] ? g.batch[0] : 1) == 1 &&
+         (g.batch[1] ? g.batch[1] : 1) == 1 && g.causal == SPAR_B200_CAUSAL_NONE;
+}
+
+// The operand layouts of that product: A' and B' sizes in floats and their leading dimensions.
+struct ConcatShape {
+  uint64_t kp, a_ld, a_floats, b_ld, b_floats;
+};
+ConcatShape concat_shape(const SparB200Gemm& g) {
+  auto pad = [](uint64_t x) { return (x + 3) & ~3ull; };
+  ConcatShape c;
+  c.kp = pad(g.k);
+  // A logical [m, k]: stored [m, k] (K inner) or [k, m] (K along rows).
+  c.a_ld = g.a_transposed ? pad(g.m) : 3 * c.kp;
+  c.a_floats = g.a_transposed ? 3 * c.kp * c.a_ld : g.m * c.a_ld;
+  // B logical [k, n]: stored [k, n] (K along rows) or [n, k] (K inner).
+  c.b_ld = g.b_transposed ? 3 * c.kp : pad(g.n);
+  c.b_floats = g.b_transposed ? g.n * c.b_ld : 3 * c.kp * c.b_ld;
+  return c;
+}
+
 // Split-K reduction and epilogue: the partial tiles [kparts][m][ldp] are summed in split order
 // (deterministic), then the GEMM's epilogue is applied exactly as the tile epilogue does it
 // (alpha, bias, residual / GELU' aux, bias + GELU with the pre-activation to aux, RoPE,
@@ -1019,6 +1076,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 }  // namespace
 
 uint64_t gemm_split_workspace_floats(const SparB200Gemm& g) {
+  if (concat_x3(g)) {
+    const ConcatShape c = concat_shape(g);
+    return c.a_floats + c.b_floats;
+  }
   const uint64_t b = g.batch[0] * g.batch[1];
   const uint64_t a_inner = g.a_transposed ? g.m : g.k, a_rows = g.a_transposed ? g.k : g.m;
   const uint64_t b_inner = g.b_transposed ? g.k : g.n, b_rows = g.b_transposed ? g.n : g.k;
@@ -1133,6 +1194,12 @@ GemmPlan gemm_plan_for(const SparB200Gemm& g, int device) {
 }
 
 uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device) {
+  if (concat_x3(g)) {  // planned as the TF32 product it becomes
+    SparB200Gemm t = g;
+    t.precision = SPAR_B200_TF32;
+    t.k = 3 * concat_shape(g).kp;
+    return gemm_splitk_workspace_floats(t, device);
+  }
   const GemmPlan pl = gemm_plan_for(g, device);
   return pl.kparts > 1 ? static_cast<uint64_t>(pl.kparts) * g.m * ((g.n + 3) / 4 * 4) : 0;
 }
@@ -1140,6 +1207,28 @@ uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device) {
 cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
                         cudaStream_t stream, float* splitk_workspace = nullptr,
                         uint64_t splitk_floats = 0) {
+  if (concat_x3(g)) {
+    const ConcatShape c = concat_shape(g);
+    float* a2 = split_workspace;
+    float* b2 = split_workspace + c.a_floats;
+    const int sms = sm_count(device);
+    const uint64_t a_inner = g.a_transposed ? g.m : g.k, a_rows = g.a_transposed ? g.k : g.m;
+    const uint64_t b_inner = g.b_transposed ? g.k : g.n, b_rows = g.b_transposed ? g.n : g.k;
+    cudaError_t e = launch(split_concat_kernel, dim3(sms * 8), dim3(256), 0, stream, a2, g.a,
+                           a_inner, a_rows, g.lda, c.a_ld, c.kp, g.a_transposed ? 0 : 1, 0);
+    if (e == cudaSuccess)
+      e = launch(split_concat_kernel, dim3(sms * 8), dim3(256), 0, stream, b2, g.b, b_inner,
+                 b_rows, g.ldb, c.b_ld, c.kp, g.b_transposed ? 1 : 0, 1);
+    if (e != cudaSuccess) return e;
+    SparB200Gemm t = g;
+    t.precision = SPAR_B200_TF32;
+    t.k = 3 * c.kp;
+    t.a = a2;
+    t.lda = c.a_ld;
+    t.b = b2;
+    t.ldb = c.b_ld;
+    return gemm_launch(t, nullptr, device, stream, splitk_workspace, splitk_floats);
+  }
   GemmParams p;
   memset(&p, 0, sizeof(p));
   const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
@@ -1343,13 +1432,13 @@ extern "C" SparCudaStatus spar_b200_gemm(const SparB200Gemm* gemm, int device, v
   float* ws = nullptr;
   float* kws = nullptr;
   if (gemm->precision == SPAR_B200_TF32X3) {
-    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws),
+    const cudaError_t e = stream_alloc(reinterpret_cast<void**>(&ws),
                                           gemm_split_workspace_floats(*gemm) * sizeof(float), s);
     if (e != cudaSuccess) return runtime(e);
   }
   const uint64_t kfloats = gemm_splitk_workspace_floats(*gemm, device);
   if (kfloats) {
-    const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&kws), kfloats * sizeof(float), s);
+    const cudaError_t e = stream_alloc(reinterpret_cast<void**>(&kws), kfloats * sizeof(float), s);
     if (e != cudaSuccess) return runtime(e);
   }
   const cudaError_t e = gemm_launch(*gemm, ws, device, s, kws, kfloats);

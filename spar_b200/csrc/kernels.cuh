@@ -239,10 +239,16 @@ AdamWArgs adamw_args(double max_norm, double lr, double beta1, double beta2, dou
                      double weight_decay, uint64_t step);
 // args_dev != nullptr: the kernels read the scalars from that device struct instead of the
 // values given (so a captured launch can be replayed for later steps).
+// rounded_base != nullptr: each updated parameter is also written, rounded to nearest TF32, at the
+// same offset from rounded_base as it has from param_base (the copy the TF32 GEMMs read).
 cudaError_t adamw_launch(const Slice* slices, uint64_t slice_count, const double* norm_state,
                          double max_norm, double lr, double beta1, double beta2, double eps,
                          double weight_decay, uint64_t step, int32_t* nonfinite_flag, int device,
-                         cudaStream_t stream, const AdamWArgs* args_dev = nullptr);
+                         cudaStream_t stream, const AdamWArgs* args_dev = nullptr,
+                         const float* param_base = nullptr, float* rounded_base = nullptr);
+// dst[i] = src[i] rounded to nearest TF32, i < count.
+cudaError_t round_copy_launch(float* dst, const float* src, uint64_t count, int device,
+                              cudaStream_t stream);
 
 cudaError_t embedding_forward_launch(float* out, const float* weight, const int32_t* ids,
                                      uint64_t count, uint64_t vocab, uint64_t dim,

@@ -473,7 +473,7 @@ extern "C" SparCudaStatus spar_b200_layernorm_backward(float* dx, float* dgamma,
   }
   const int parts = layernorm_backward_parts(rows, device);
   float* workspace = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&workspace),
+  cudaError_t e = stream_alloc(reinterpret_cast<void**>(&workspace),
                                   2ull * parts * cols * sizeof(float), s);
   if (e != cudaSuccess) return runtime(e);
   e = layernorm_backward_launch(dx, dgamma, dbeta, dy, x, gamma, mean, rstd, rows, cols,
@@ -519,7 +519,7 @@ extern "C" SparCudaStatus spar_b200_rmsnorm_backward(float* dx, float* dweight, 
   }
   const int parts = layernorm_backward_parts(rows, device);
   float* workspace = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&workspace),
+  cudaError_t e = stream_alloc(reinterpret_cast<void**>(&workspace),
                                   static_cast<uint64_t>(parts) * cols * sizeof(float), s);
   if (e != cudaSuccess) return runtime(e);
   e = rmsnorm_backward_launch(dx, dweight, dy, x, weight, rstd, rows, cols, accumulate_params,
@@ -576,7 +576,7 @@ extern "C" SparCudaStatus spar_b200_head_rmsnorm_backward(float* dx, float* dwei
   const uint64_t rows = tokens * heads;
   const int parts = layernorm_backward_parts(rows, device);
   float* workspace = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&workspace),
+  cudaError_t e = stream_alloc(reinterpret_cast<void**>(&workspace),
                                   static_cast<uint64_t>(parts) * head_dim * sizeof(float), s);
   if (e != cudaSuccess) return runtime(e);
   e = rmsnorm_backward_launch(dx, dweight, dy, x, weight, rstd, rows, head_dim, accumulate_params,

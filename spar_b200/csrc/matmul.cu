@@ -144,7 +144,7 @@ extern "C" SparCudaStatus spar_b200_matmul(const void* a, const void* b, void* c
   float* pb = nullptr;
   float* pc = nullptr;
   const uint64_t fa = batch * m * k4, fb = batch * k4 * n4, fc = batch * m * n4;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&pa), (fa + fb + fc) * sizeof(float), s);
+  cudaError_t e = stream_alloc(reinterpret_cast<void**>(&pa), (fa + fb + fc) * sizeof(float), s);
   if (e != cudaSuccess) return runtime(e);
   pb = pa + fa;
   pc = pb + fb;

@@ -300,6 +300,13 @@ class LMTrainer {
   uint64_t off_E = 0, off_lnf_g = 0, off_lnf_b = 0;
   std::vector<std::pair<uint64_t, uint64_t>> buckets;  // all-reduce buckets in issue order
   float *params = nullptr, *grads = nullptr, *m1 = nullptr, *m2 = nullptr;
+  // TF32 mode: the parameters rounded to nearest TF32, which every GEMM reads as its weight
+  // operand (the tensor cores would otherwise truncate the fp32 master weights: a systematic
+  // shrink of every product). Kept current by AdamW (it writes both), by the sharded optimiser's
+  // parameter gather, and, after host writes (wround_dirty), by a rounding pass before the step.
+  float* wround = nullptr;
+  bool wround_dirty = true;
+  cudaError_t refresh_rounded(cudaStream_t s);
   // activations
   char* act_base = nullptr;
   std::vector<LayerActs> acts;
@@ -493,7 +500,16 @@ LMTrainer::~LMTrainer() {
   if (ev_out) cudaEventDestroy(ev_out);
   if (opt_args_host) cudaFreeHost(opt_args_host);
   cudaFree(params);
+  if (wround) cudaFree(wround);
   cudaFree(act_base);
+}
+
+// The rounded weight copy after host-side parameter writes (not captured into a step graph).
+cudaError_t LMTrainer::refresh_rounded(cudaStream_t s) {
+  if (!wround || !wround_dirty) return cudaSuccess;
+  const cudaError_t e = round_copy_launch(wround, params, flat, device, s);
+  if (e == cudaSuccess) wround_dirty = false;
+  return e;
 }
 
 SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
@@ -539,6 +555,11 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   m2 = m1 + flat;
   e = cudaMemset(params, 0, 4 * flat * sizeof(float));
   if (e != cudaSuccess) return runtime(e);
+  if (c.precision == SPAR_B200_TF32) {
+    e = cudaMalloc(reinterpret_cast<void**>(&wround), flat * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(wround, 0, flat * sizeof(float));
+    if (e != cudaSuccess) return runtime(e);
+  }
 
   // ---- activation arena
   fused_attention = c.precision == SPAR_B200_TF32 && attention_supported(dh);
@@ -844,6 +865,12 @@ cudaError_t LMTrainer::gather_params(cudaStream_t s) {
   auto issue = [&](size_t i) -> cudaError_t {
     const BucketShard& b = shard_plan[i];
     if (b.shard) SPAR_TRY_RAW(comm_all_gather(comm, params + b.off, b.shard, comm_stream));
+    if (wround && b.shard) {  // the other ranks' pieces arrive unrounded
+      launches += 1;
+      SPAR_TRY_RAW(round_copy_launch(wround + b.off, params + b.off,
+                                     static_cast<uint64_t>(comm_size(comm)) * b.shard, device,
+                                     comm_stream));
+    }
     return cudaEventRecord(gather_ev[i], comm_stream);
   };
   SPAR_TRY_RAW(issue(L));  // embedding
@@ -863,6 +890,7 @@ cudaError_t LMTrainer::gather_arena(int which, cudaStream_t s) {
   SPAR_TRY_RAW(cudaEventRecord(comm_done, comm_stream));
   SPAR_TRY_RAW(cudaStreamWaitEvent(s, comm_done, 0));
   stale[which] = false;
+  if (which == 0) wround_dirty = true;  // the gathered pieces reach the rounded copy next step
   return cudaSuccess;
 }
 
@@ -929,7 +957,7 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
     if (e == cudaSuccess)
       e = adamw_launch(own_slices.data(), own_slices.size(), norm_state, cfg.max_grad_norm, lr,
                        cfg.beta1, cfg.beta2, cfg.adam_epsilon, cfg.weight_decay, step, flags + 1,
-                       device, s, device_args ? opt_args : nullptr);
+                       device, s, device_args ? opt_args : nullptr, params, wround);
     return e == cudaSuccess ? ok() : runtime(e);
   }
   launches += 3;
@@ -938,7 +966,7 @@ SparCudaStatus LMTrainer::step_body(uint64_t micro_steps, float grad_scale, doub
   if (e == cudaSuccess)
     e = adamw_launch(&slice, 1, norm_state, cfg.max_grad_norm, lr, cfg.beta1, cfg.beta2,
                      cfg.adam_epsilon, cfg.weight_decay, step, flags + 1, device, s,
-                     device_args ? opt_args : nullptr);
+                     device_args ? opt_args : nullptr, params, wround);
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
@@ -952,6 +980,8 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   const float eps = static_cast<float>(cfg.norm_epsilon);
   const bool rn = cfg.precision == SPAR_B200_TF32;
   float* P = params;
+  // Weights as the GEMMs read them: the copy rounded to nearest TF32 in TF32 mode.
+  const float* Wt = wround ? wround : params;
   float* G = grads;
   // ---------------------------------------------------------------- forward
   launches += 1;
@@ -973,18 +1003,18 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
                                         N, d, eps, device, s, rn));
     // qkv = a1 Wqkv + b, RoPE on the q and k thirds in the epilogue. q, k, v only feed
     // attention products: with fused attention they are stored rounded to nearest TF32.
-    SPAR_CHECK(gemm(N, 3 * d, d, A.a1, d, false, P + lo.wqkv, 3 * d, false, A.qkv, 3 * d, false,
+    SPAR_CHECK(gemm(N, 3 * d, d, A.a1, d, false, Wt + lo.wqkv, 3 * d, false, A.qkv, 3 * d, false,
                     SPAR_B200_EPI_BIAS, P + lo.bqkv, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1,
                     nullptr, nullptr, nullptr, fused_attention, cfg.use_rope != 0));
     SPAR_CHECK(attention_forward(A, s));
-    SPAR_CHECK(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
+    SPAR_CHECK(gemm(N, d, d, A.ctx, d, false, Wt + lo.wo, d, false, A.h1, d, false,
                     SPAR_B200_EPI_BIAS_ADD, P + lo.bo, A.x, d, s));
     SPAR_CHECK(layernorm_forward_launch(A.a2, A.mean2, A.rstd2, A.h1, P + lo.ln2_g, P + lo.ln2_b,
                                         N, d, eps, device, s, rn));
-    SPAR_CHECK(gemm(N, F, d, A.a2, d, false, P + lo.w1, F, false, A.g, F, false,
+    SPAR_CHECK(gemm(N, F, d, A.a2, d, false, Wt + lo.w1, F, false, A.g, F, false,
                     SPAR_B200_EPI_BIAS_GELU, P + lo.b1, A.u, F, s, SPAR_B200_CAUSAL_NONE, 1, 1,
                     nullptr, nullptr, nullptr, rn));
-    SPAR_CHECK(gemm(N, d, F, A.g, F, false, P + lo.w2, d, false, out, d, false,
+    SPAR_CHECK(gemm(N, d, F, A.g, F, false, Wt + lo.w2, d, false, out, d, false,
                     SPAR_B200_EPI_BIAS_ADD, P + lo.b2, A.h1, d, s));
   }
   launches += 1 + 2 + 2;  // final LayerNorm, cross-entropy + loss sum, final LayerNorm backward
@@ -995,7 +1025,7 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   else
     SPAR_CHECK(layernorm_forward_launch(hf, meanf, rstdf, xL, P + off_lnf_g, P + off_lnf_b, N, d,
                                         eps, device, s, rn));
-  SPAR_CHECK(gemm(N, V, d, hf, d, false, P + off_E, d, true, logits, Vp, false,
+  SPAR_CHECK(gemm(N, V, d, hf, d, false, Wt + off_E, d, true, logits, Vp, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // Fused log-softmax + NLL + mean backward; dlogits overwrite the logits in place.
   SPAR_CHECK(cross_entropy_launch(row_loss, logits, logits, ids, N, V, Vp, T, grad_scale,
@@ -1012,7 +1042,7 @@ SparCudaStatus LMTrainer::forward_backward(const int32_t* ids, float grad_scale,
   SPAR_CHECK(gemm(V, d, N, logits, Vp, true, hf, d, false, G + off_E, d, true, SPAR_B200_EPI_NONE,
                   nullptr, nullptr, 0, w));
   if (conc) SPAR_CHECK(cudaEventRecord(wg_join[3], w));
-  SPAR_CHECK(gemm(N, d, V, logits, Vp, false, P + off_E, d, false, dtmp, d, false,
+  SPAR_CHECK(gemm(N, d, V, logits, Vp, false, Wt + off_E, d, false, dtmp, d, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // The final norm's dx is dL/d(last block output): its column sums are that block's b2 gradient.
   if (family == SPAR_B200_FAMILY_SPAR)
@@ -1050,6 +1080,8 @@ cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s
   LayerActs& A = acts[l];
   const LayerOffsets& lo = lay[l];
   float* P = params;
+  // Weights as the GEMMs read them: the copy rounded to nearest TF32 in TF32 mode.
+  const float* Wt = wround ? wround : params;
   const float eps = static_cast<float>(cfg.norm_epsilon);
   launches += 2 + 1 + 1;  // 2 RMSNorms, attention, SwiGLU
   const bool rn = cfg.precision == SPAR_B200_TF32;  // norm outputs only feed TF32 products
@@ -1057,28 +1089,28 @@ cudaError_t LMTrainer::layer_forward_spar(uint64_t l, float* out, cudaStream_t s
                                   rn));
   if (!qk_norm) {
     // RoPE on the q and k parts in the epilogue; q, k, v stored rounded to nearest TF32.
-    SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, P + lo.wqkv, Wq, false, A.qkv, Wq, false,
+    SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, Wt + lo.wqkv, Wq, false, A.qkv, Wq, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1,
                   nullptr, nullptr, nullptr, rn, cfg.use_rope != 0));
   } else {
     // The q / k norms come before RoPE (attention.cpp:212-215): project, then one pass per
     // token normalises each q / k head, rotates it and writes q | k | v rounded to TF32.
     launches += 1;
-    SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, P + lo.wqkv, Wq, false, A.qkv_raw, Wq, false,
+    SPAR_TRY(gemm(N, Wq, d, A.a1, d, false, Wt + lo.wqkv, Wq, false, A.qkv_raw, Wq, false,
                   SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
     SPAR_TRY(qk_norm_rope_launch(A.qkv, A.qkv_raw, N, T, H, KVH, dh, Wq, P + lo.qn, P + lo.kn,
                                  A.qk_rstd, cfg.use_rope ? rope_tab : nullptr,
                                  static_cast<float>(cfg.qk_norm_epsilon), device, s, rn));
   }
   SPAR_TRY(attention_forward(A, s));
-  SPAR_TRY(gemm(N, d, d, A.ctx, d, false, P + lo.wo, d, false, A.h1, d, false,
+  SPAR_TRY(gemm(N, d, d, A.ctx, d, false, Wt + lo.wo, d, false, A.h1, d, false,
                 SPAR_B200_EPI_BIAS_ADD, nullptr, A.x, d, s));
   SPAR_TRY(rmsnorm_forward_launch(A.a2, A.rstd2, A.h1, P + lo.ln2_g, N, d, eps, device, s, 0, 1,
                                   rn));
-  SPAR_TRY(gemm(N, Fu, d, A.a2, d, false, P + lo.w1, Fu, false, A.u, Fu, false,
+  SPAR_TRY(gemm(N, Fu, d, A.a2, d, false, Wt + lo.w1, Fu, false, A.u, Fu, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   SPAR_TRY(swiglu_forward_launch(A.g, F, A.u, Fu, A.u + F, Fu, N, F, device, s));
-  return gemm(N, d, F, A.g, F, false, P + lo.w2, d, false, out, d, false, SPAR_B200_EPI_BIAS_ADD,
+  return gemm(N, d, F, A.g, F, false, Wt + lo.w2, d, false, out, d, false, SPAR_B200_EPI_BIAS_ADD,
               nullptr, A.h1, d, s);
 }
 
@@ -1088,6 +1120,8 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
   LayerActs& A = acts[l];
   const LayerOffsets& lo = lay[l];
   float* P = params;
+  // Weights as the GEMMs read them: the copy rounded to nearest TF32 in TF32 mode.
+  const float* Wt = wround ? wround : params;
   float* G = grads;
   launches += 2 * 2 + 1 + 1 + (qk_norm ? 2 : 0);  // RMSNorm bwd, attention, SwiGLU bwd, qk norms
   // (3xTF32 keeps one stream: its hi / lo operand workspace is shared by the products.)
@@ -1105,14 +1139,14 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
   SPAR_TRY(gemm(F, d, N, A.g, F, true, dres, d, false, G + lo.w2, d, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, w));
   SPAR_TRY(mark(0));  // dWdown has read dres
-  SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, dh_buf, F, false, SPAR_B200_EPI_NONE,
+  SPAR_TRY(gemm(N, F, d, dres, d, false, Wt + lo.w2, d, true, dh_buf, F, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
   SPAR_TRY(swiglu_backward_launch(du, Fu, du + F, Fu, dh_buf, F, A.u, Fu, A.u + F, Fu, N, F,
                                   device, s));
   SPAR_TRY(fork(1));
   SPAR_TRY(gemm(d, Fu, N, A.a2, d, true, du, Fu, false, G + lo.w1, Fu, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, w));
-  SPAR_TRY(gemm(N, d, Fu, du, Fu, false, P + lo.w1, Fu, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+  SPAR_TRY(gemm(N, d, Fu, du, Fu, false, Wt + lo.w1, Fu, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
   // dres += RMSNorm backward -> dL/dh1 (dWdown read dres first)
   SPAR_TRY(join(0));
@@ -1123,7 +1157,7 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
   SPAR_TRY(gemm(d, d, N, A.ctx, d, true, dres, d, false, G + lo.wo, d, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, w));
   SPAR_TRY(mark(1));  // dWo has read dres
-  SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+  SPAR_TRY(gemm(N, d, d, dres, d, false, Wt + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
                 cfg.precision == SPAR_B200_TF32));
   // attention: dctx (dtmp) -> dqkv; the fused kernels rotate dq / dk back through RoPE, the
@@ -1138,7 +1172,7 @@ cudaError_t LMTrainer::layer_backward_spar(uint64_t l, cudaStream_t s) {
   SPAR_TRY(gemm(d, Wq, N, A.a1, d, true, dqkv, Wq, false, G + lo.wqkv, Wq, true,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, w));
   SPAR_TRY(mark(2));
-  SPAR_TRY(gemm(N, d, Wq, dqkv, Wq, false, P + lo.wqkv, Wq, true, dtmp, d, false,
+  SPAR_TRY(gemm(N, d, Wq, dqkv, Wq, false, Wt + lo.wqkv, Wq, true, dtmp, d, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   SPAR_TRY(join(1));
   SPAR_TRY(rmsnorm_backward_launch(dres, G + lo.ln1_g, dtmp, A.x, P + lo.ln1_g, A.rstd1, N, d, 1,
@@ -1200,6 +1234,8 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   LayerActs& A = acts[l];
   const LayerOffsets& lo = lay[l];
   float* P = params;
+  // Weights as the GEMMs read them: the copy rounded to nearest TF32 in TF32 mode.
+  const float* Wt = wround ? wround : params;
   float* G = grads;
   launches += 2 * 2 + 2 * 2 + 1 + (cfg.use_rope && !fused_attention ? 1 : 0);  // col sums, LN bwd, softmax bwd, rope
   // Weight gradients on the second stream (forks: event on s, wait on w; joins: the reverse).
@@ -1221,7 +1257,7 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
                 nullptr, nullptr, 0, w));
   SPAR_TRY(mark(0));  // dW2 has read dres
   // du = (dres W2^T) o gelu'(u); its epilogue also leaves the b1 gradient's column partials.
-  SPAR_TRY(gemm(N, F, d, dres, d, false, P + lo.w2, d, true, du, F, false, SPAR_B200_EPI_GELU_BWD,
+  SPAR_TRY(gemm(N, F, d, dres, d, false, Wt + lo.w2, d, true, du, F, false, SPAR_B200_EPI_GELU_BWD,
                 nullptr, A.u, F, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
                 cfg.precision == SPAR_B200_TF32, false, colpart));
   SPAR_TRY(fork(1));
@@ -1229,7 +1265,7 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
                 nullptr, nullptr, 0, w));
   const uint64_t blocks = (N + 31) / 32;
   SPAR_TRY(column_sum_launch(G + lo.b1, colpart, blocks, F, F, 1, col_ws, device, w));
-  SPAR_TRY(gemm(N, d, F, du, F, false, P + lo.w1, F, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+  SPAR_TRY(gemm(N, d, F, du, F, false, Wt + lo.w1, F, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s));
   // dres += LN2 backward  ->  dL/dh1, whose column sums are the bo gradient (dW2 read dres first)
   SPAR_TRY(join(0));
@@ -1240,7 +1276,7 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   SPAR_TRY(gemm(d, d, N, A.ctx, d, true, dres, d, false, G + lo.wo, d, true, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, w));
   SPAR_TRY(mark(1));  // dWo has read dres
-  SPAR_TRY(gemm(N, d, d, dres, d, false, P + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
+  SPAR_TRY(gemm(N, d, d, dres, d, false, Wt + lo.wo, d, true, dtmp, d, false, SPAR_B200_EPI_NONE,
                 nullptr, nullptr, 0, s, SPAR_B200_CAUSAL_NONE, 1, 1, nullptr, nullptr, nullptr,
                 fused_attention));
   // attention core: dtmp = dctx [N, d] -> dqkv
@@ -1259,7 +1295,7 @@ cudaError_t LMTrainer::layer_backward(uint64_t l, cudaStream_t s) {
   else
     SPAR_TRY(column_sum_launch(G + lo.bqkv, dqkv, N, 3 * d, ld, 1, col_ws, device, w));
   SPAR_TRY(mark(2));  // every product of this layer on the weight-gradient stream is done
-  SPAR_TRY(gemm(N, d, 3 * d, dqkv, ld, false, P + lo.wqkv, ld, true, dtmp, d, false,
+  SPAR_TRY(gemm(N, d, 3 * d, dqkv, ld, false, Wt + lo.wqkv, ld, true, dtmp, d, false,
                 SPAR_B200_EPI_NONE, nullptr, nullptr, 0, s));
   // dres += LN1 backward -> dL/dx = dL/d(previous block output): its column sums are the
   // previous block's b2 gradient (dWo read dres first)
@@ -1348,6 +1384,7 @@ extern "C" SparCudaStatus spar_b200_lm_parameter_copy(void* handle, uint64_t ind
   const uint64_t cols = n.cols ? n.cols : n.rows, rows = n.cols ? n.rows : 1;
   const uint64_t ld = n.cols ? n.ld : n.rows;
   cudaError_t e = cudaDeviceSynchronize();
+  if (to_device && which == 0) t->wround_dirty = true;
   if (e == cudaSuccess) {
     if (to_device)
       e = cudaMemcpy2D(dev, ld * 4, host, cols * 4, cols * 4, rows, cudaMemcpyHostToDevice);
@@ -1363,6 +1400,7 @@ extern "C" SparCudaStatus spar_b200_lm_init_normal(void* handle, uint64_t seed, 
                                                    void* stream) {
   if (!handle) return invalid();
   LMTrainer* t = as_trainer(handle);
+  t->wround_dirty = true;
   DeviceScope scope(t->device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1408,6 +1446,7 @@ extern "C" SparCudaStatus spar_b200_lm_forward_backward(void* handle, const int3
   // After a sharded train step: whole parameters and gradients (collective, like the step).
   cudaError_t e = t->gather_arena(0, static_cast<cudaStream_t>(stream));
   if (e == cudaSuccess) e = t->gather_arena(1, static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = t->refresh_rounded(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return runtime(e);
   return t->forward_backward(ids, grad_scale, micro_index, static_cast<cudaStream_t>(stream));
 }
@@ -1431,7 +1470,7 @@ extern "C" SparCudaStatus spar_b200_lm_optimizer_step(void* handle, double learn
   if (e == cudaSuccess)
     e = adamw_launch(&slice, 1, t->norm_state, t->cfg.max_grad_norm, learning_rate, t->cfg.beta1,
                      t->cfg.beta2, t->cfg.adam_epsilon, t->cfg.weight_decay, step, t->flags + 1,
-                     t->device, s);
+                     t->device, s, nullptr, t->params, t->wround);
   return e == cudaSuccess ? ok() : runtime(e);
 }
 
@@ -1462,6 +1501,8 @@ extern "C" SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* i
   const double rows = static_cast<double>(t->B) * static_cast<double>(t->T - 1) *
                       static_cast<double>(micro_steps) * static_cast<double>(t->world);
   const float grad_scale = static_cast<float>(1.0 / rows);
+  e = t->refresh_rounded(s);  // host writes since the last step (eager, never in a graph)
+  if (e != cudaSuccess) return runtime(e);
   if (!t->graphs_enabled || t->profiling || t->eager_steps == 0) {
     const SparCudaStatus st = t->step_body(micro_steps, grad_scale, learning_rate, step, s, false);
     if (st.code != 0) return st;
@@ -1698,6 +1739,7 @@ extern "C" SparCudaStatus spar_b200_lm_load_checkpoint(void* handle, const char*
   DeviceScope scope(t->device);
   if (scope.error() != cudaSuccess) return runtime(scope.error());
   cudaError_t e = cudaDeviceSynchronize();
+  t->wround_dirty = true;
   if (e == cudaSuccess) e = stage_tensors(t, 0, p, true);
   if (e == cudaSuccess) e = stage_tensors(t, 2, m, true);
   if (e == cudaSuccess) e = stage_tensors(t, 3, v, true);

@@ -105,3 +105,38 @@ def test_ln_gelu_decoder_step_on_cuda_matches_cpu(ref, monkeypatch, precision, t
     cpu = ref.lm_step(params, names, ids, cfg, 3e-4, OPT, device=-1, variant="b200")
     gpu = ref.lm_step(params, names, ids, cfg, 3e-4, OPT, device=0, variant="b200")
     _compare(cpu, gpu, params, names, tol_all, tol_each)
+
+
+def test_fused_ops_on_spar_tape_match_composed_cpu_step(ref, monkeypatch):
+    """The product's differentiable fused operations (spar_b200/spar/fused.cppm, module spar.b200:
+    layer_norm, linear_gelu, language_model_cross_entropy, grad_ready) recorded on Spar's own
+    autograd tape through detail::record_operation, in the LN/GELU decoder on cuda:0, against the
+    CPU step built from Spar's composed ops: the same 1e-5 bars (3xTF32 products). grad_ready's
+    hooks fire once per backward pass per parameter, blocks in reverse order, each with the
+    parameter's whole gradient (one micro-step: the gradient it ends with)."""
+    monkeypatch.setenv("SPAR_B200_MATMUL_PRECISION", "tf32x3")
+    lib = ref.load("b200")
+    if not hasattr(lib, "ref_lm_step_fused"):
+        pytest.skip("drop-in build without the fused module")
+    cfg = {"vocab": 256, "dim": 128, "hidden": 512, "layers": 2, "heads": 4, "eps": 1e-5,
+           "rope_theta": 1e4}
+    params = O.init_parameters(cfg, 0x5EED0901)
+    r = np.random.default_rng(9)
+    for n, v in params.items():
+        if v.ndim == 1:
+            params[n] = ((1.0 if n.endswith("norm.weight") else 0.0)
+                         + 0.05 * r.standard_normal(v.shape)).astype(np.float32)
+    names = O.parameter_names(cfg["layers"])
+    ids = O.Random(0x5EED1901).bounded(1 * 4 * 64, 256).reshape(1, 4, 64).astype(np.int32)
+    cpu = ref.lm_step(params, names, ids, cfg, 3e-4, OPT, device=-1, variant="b200")
+    loss, norm, grads, new, calls, norms, order = ref.lm_step_fused(params, names, ids, cfg, 3e-4,
+                                                                    OPT, device=0)
+    _compare(cpu, (loss, norm, grads, new), params, names, 1e-5, 1e-5)
+    assert list(calls) == [1] * 6
+    # slots (block, kind): block 1's three fire before block 0's (reverse layer order)
+    assert sorted(order[:3]) == [3, 4, 5] and sorted(order[3:]) == [0, 1, 2]
+    hooked = [f"blocks.{b}.{k}" for b in range(2)
+              for k in ("attention_norm.weight", "mlp_norm.weight", "mlp.up_proj.weight")]
+    for slot, n in enumerate(hooked):
+        want = np.linalg.norm(grads[n].astype(np.float64))
+        assert abs(norms[slot] - want) <= 1e-6 * want, n
