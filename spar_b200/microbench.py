@@ -141,6 +141,9 @@ def run_attention(b=16, t=1024, h=16, dh=64, iters=10):
                   5 * half, "TFLOP/s", tf)
 
 
+ADAMW_PARAMS = 350_000_000  # --adamw-params: C2's AdamW size (smaller for profiler captures)
+
+
 def run_bandwidth(name, iters=10):
     dev = torch.device("cuda")
     hbm, _ = peaks()
@@ -204,7 +207,7 @@ def run_bandwidth(name, iters=10):
         return report("cross_entropy 8192x32768", timed(lambda: ops.cross_entropy_forward_backward(z, tg, in_place=True), iters),
                       8 * z.numel(), "GB/s", hbm)
     if name == "adamw":
-        n = 350_000_000
+        n = ADAMW_PARAMS
         p = torch.randn(n, device=dev) * 0.02
         g = torch.randn(n, device=dev) * 1e-3
         m = torch.zeros_like(p)
@@ -212,8 +215,8 @@ def run_bandwidth(name, iters=10):
         st = ops.grad_norm_squared([g])
         ms = timed(lambda: ops.adamw_clipped([p], [g], [m], [v], st, lr=3e-4, beta1=0.9, beta2=0.95,
                                              weight_decay=0.1, step=1, max_norm=1.0), min(iters, 5))
-        report("adamw 350M", ms, 28 * n, "GB/s", hbm)
-        return report("grad_norm 350M", timed(lambda: ops.grad_norm_squared([g], st), min(iters, 5)),
+        report(f"adamw {n / 1e6:.0f}M", ms, 28 * n, "GB/s", hbm)
+        return report(f"grad_norm {n / 1e6:.0f}M", timed(lambda: ops.grad_norm_squared([g], st), min(iters, 5)),
                       4 * n, "GB/s", hbm)
     raise SystemExit(f"unknown kernel {name}")
 
@@ -231,9 +234,11 @@ def main():
     ap.add_argument("--epi", default="none", choices=sorted(EPILOGUES))
     ap.add_argument("--batch", type=int, default=16, help="attention: sequences (C5: 16)")
     ap.add_argument("--eager", action="store_true", help="time plain launches (no CUDA graph)")
+    ap.add_argument("--adamw-params", type=int, default=350_000_000)
     a = ap.parse_args()
-    global EAGER
+    global EAGER, ADAMW_PARAMS
     EAGER = a.eager
+    ADAMW_PARAMS = a.adamw_params
     if a.kernel == "gemm":
         run_gemm(a.m, a.n, a.k, a.at, a.bt, a.x3, a.iters, a.epi)
     elif a.kernel == "all":
