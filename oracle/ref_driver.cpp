@@ -144,7 +144,8 @@ struct Model {
     int slot = 0;
     auto ready = [&](const nn::Parameter& p) {
       const int id = slot++;
-      return b200::grad_ready(p.tensor(), [id, &hook](const Tensor& g) { hook(id, g); });
+      // The hook is copied into the node: the node's backward runs after this call returns.
+      return b200::grad_ready(p.tensor(), [id, hook](const Tensor& g) { hook(id, g); });
     };
     Tensor h = embedding.forward(ids);
     for (Block& b : blocks) {

@@ -654,6 +654,9 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
       SparB200Gemm g{};
       g.m = sh.m; g.n = sh.n; g.k = sh.k; g.a_transposed = sh.at; g.b_transposed = sh.bt;
       g.batch[0] = sh.b0; g.batch[1] = sh.b1;
+      g.precision = SPAR_B200_TF32X3;  // the workspace depends on how the product is split
+      // The batched attention products are the causal ones (three-section kernel).
+      g.causal = sh.b0 * sh.b1 > 1 ? SPAR_B200_CAUSAL_LOWER : SPAR_B200_CAUSAL_NONE;
       split_floats = std::max(split_floats, gemm_split_workspace_floats(g));
     }
     f(&split_ws, split_floats);
