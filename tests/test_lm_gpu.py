@@ -211,9 +211,11 @@ def test_lanes_match_oracle(cuda):
 
 
 def test_lanes_match_one_lane_and_repeat(cuda, monkeypatch):
-    """The same steps with lanes switched off (SPAR_B200_LANES=0) differ only by the order of the
-    gradient sums; with lanes, repeated runs (eager first step, then graph replays) are bitwise
-    equal."""
+    """The same step with lanes switched off (SPAR_B200_LANES=0) differs only by the order of the
+    gradient sums (fp32 rounding: the gradients within 1e-6); with lanes, repeated runs (eager
+    first step, then graph replays) are bitwise equal. After the first update the two runs' weights
+    differ in their last bits, and the TF32 rounding of the weights the GEMMs read turns some of
+    those into TF32-ulp differences, so three steps are compared at 1e-4."""
     from spar_b200.lm import DecoderLM
 
     cfg = _lanes_cfg()
@@ -222,18 +224,21 @@ def test_lanes_match_one_lane_and_repeat(cuda, monkeypatch):
     def steps():
         lm = DecoderLM(cfg, 0)
         lm.load_state_dict(params)
-        ls = [lm.train_step(ids, 3e-4, step=s)[0] for s in range(1, 4)]
+        ls = [lm.train_step(ids, 3e-4, step=1)[0]]
+        g1 = _flat(lm.state_dict("grad"), lm.names)
+        ls += [lm.train_step(ids, 3e-4, step=s)[0] for s in range(2, 4)]
         out = _flat(lm.state_dict(), lm.names)
         lm.close()
-        return ls, out
+        return ls, g1, out
 
-    a_l, a = steps()
-    b_l, b = steps()
+    a_l, a_g, a = steps()
+    b_l, b_g, b = steps()
     monkeypatch.setenv("SPAR_B200_LANES", "0")
-    c_l, c = steps()
-    assert a_l == b_l and np.array_equal(a, b)
-    assert rel_l2(a, c) <= 1e-5
-    np.testing.assert_allclose(a_l, c_l, rtol=1e-5)
+    c_l, c_g, c = steps()
+    assert a_l == b_l and np.array_equal(a_g, b_g) and np.array_equal(a, b)
+    assert rel_l2(a_g, c_g) <= 1e-6 and abs(a_l[0] - c_l[0]) <= 1e-6 * abs(c_l[0])
+    assert rel_l2(a, c) <= 1e-4
+    np.testing.assert_allclose(a_l, c_l, rtol=1e-4)
 
 
 def _one_rank_comm():

@@ -12,8 +12,12 @@ oracle.spar_oracle.lm_train_step (float64; DecoderLM::forward, src/nn/decoder.cp
 same seeded weights and ids. Biases, LayerNorm gains and shifts are drawn non-trivially so their
 gradients are tested at non-identity values.
 
-Bars (north star): per-tensor gradient relative L2 <= 2e-3 in TF32 and <= 1e-5 in 3xTF32, loss
-and gradient norm at the same bars.
+Bars (north star): all gradients together and every tensor's gradient within relative L2
+<= 2e-3 in TF32 and <= 1e-5 in 3xTF32, loss and gradient norm at the same bars; with one
+exception in TF32, the key-projection biases (bar 4e-3): their gradient is the sum over keys of
+dK, and since every softmax row's dS sums to zero that sum cancels to almost nothing (exactly
+nothing without RoPE), so the TF32 rounding of dK, ~1e-3 of dK's own size, is ~2e-3 of that
+small remainder (3xTF32: 4e-6, also among the largest).
 
 The update is checked in two parts, because at step 1 AdamW's update is
 lr * g / (|g| + eps) (plus decay), i.e. lr * sign(g) wherever |g| >> eps: comparing it with an
@@ -110,7 +114,8 @@ def _check(cfg, micro_steps, tol):
     assert abs(loss - o_loss) <= tol * abs(o_loss)
     assert abs(norm - o_norm) <= tol * o_norm
     for e, n in report:
-        assert e <= tol, (n, e)
+        bar = 2 * tol if (cfg.precision == 0 and n.endswith("k_proj.bias")) else tol
+        assert e <= bar, (n, e)
     # (1) the applied update is AdamW of the GPU's own gradients and norm.
     clip = O.clip_factor(norm, cfg.max_grad_norm)
     for n in names:
