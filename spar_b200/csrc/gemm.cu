@@ -1186,27 +1186,47 @@ GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
   return pl;
 }
 
+// Longest K (in 32-element blocks) a concatenated 3xTF32 product accumulates in one tensor-core
+// accumulator. The accumulator's adds are not IEEE fp32 (measured: a C5-width training step's
+// gradients drifted 1.3e-4 from float64 with K' = 3 x 16384 in one accumulator, against 2.4e-6 when
+// sums moved to fp32 registers every 3 x 128); past this length the K dimension is split and the
+// partial tiles summed in fp32 by the reduction pass, as the three-section kernel's chunks are.
+constexpr uint32_t kX3MaxBlocks = 96;  // 3072 K elements = 3 sections of 1024
+
+uint32_t x3_min_parts(uint64_t k) {
+  const uint64_t kb = (k + BK - 1) / BK;
+  return static_cast<uint32_t>((kb + kX3MaxBlocks - 1) / kX3MaxBlocks);
+}
+
 // Column partials are written by the GEMM's own epilogue, which a K split hands to the reduction.
-GemmPlan gemm_plan_for(const SparB200Gemm& g, int device) {
+GemmPlan gemm_plan_for(const SparB200Gemm& g, int device, uint32_t min_parts = 1) {
   GemmPlan pl = gemm_plan(g, device);
+  if (pl.kparts < min_parts) {
+    pl.kparts = min_parts;
+    // every split non-empty: (parts - 1) full splits of ceil(kb / parts) blocks stay below kb
+    const uint64_t kb = (g.k + BK - 1) / BK;
+    while (pl.kparts > 1 && (pl.kparts - 1) * ((kb + pl.kparts - 1) / pl.kparts) >= kb)
+      --pl.kparts;
+  }
   if (g.column_partials) pl.kparts = 1;
   return pl;
 }
 
 uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device) {
+  uint32_t min_parts = 1;
+  SparB200Gemm t = g;
   if (concat_x3(g)) {  // planned as the TF32 product it becomes
-    SparB200Gemm t = g;
     t.precision = SPAR_B200_TF32;
     t.k = 3 * concat_shape(g).kp;
-    return gemm_splitk_workspace_floats(t, device);
+    min_parts = x3_min_parts(t.k);
   }
-  const GemmPlan pl = gemm_plan_for(g, device);
-  return pl.kparts > 1 ? static_cast<uint64_t>(pl.kparts) * g.m * ((g.n + 3) / 4 * 4) : 0;
+  const GemmPlan pl = gemm_plan_for(t, device, min_parts);
+  return pl.kparts > 1 ? static_cast<uint64_t>(pl.kparts) * t.m * ((t.n + 3) / 4 * 4) : 0;
 }
 
 cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
                         cudaStream_t stream, float* splitk_workspace = nullptr,
-                        uint64_t splitk_floats = 0) {
+                        uint64_t splitk_floats = 0, uint32_t min_parts = 1) {
   if (concat_x3(g)) {
     const ConcatShape c = concat_shape(g);
     float* a2 = split_workspace;
@@ -1227,14 +1247,15 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     t.lda = c.a_ld;
     t.b = b2;
     t.ldb = c.b_ld;
-    return gemm_launch(t, nullptr, device, stream, splitk_workspace, splitk_floats);
+    return gemm_launch(t, nullptr, device, stream, splitk_workspace, splitk_floats,
+                       x3_min_parts(t.k));
   }
   GemmParams p;
   memset(&p, 0, sizeof(p));
   const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
   const bool split = g.precision == SPAR_B200_TF32X3;
   // 3xTF32 keeps its running sums in registers (one 64-column row segment per thread).
-  const GemmPlan plan = gemm_plan_for(g, device);
+  const GemmPlan plan = gemm_plan_for(g, device, min_parts);
   const int bn = plan.bn;
   p.sections = split ? 3 : 1;
   p.a_mn_major = g.a_transposed ? 1 : 0;
