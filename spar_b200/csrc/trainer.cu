@@ -31,7 +31,8 @@
 namespace spar_b200 {
 
 cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
-                        cudaStream_t stream, float* splitk_workspace, uint64_t splitk_floats);
+                        cudaStream_t stream, float* splitk_workspace, uint64_t splitk_floats,
+                        uint32_t min_parts = 1);
 uint64_t gemm_split_workspace_floats(const SparB200Gemm& g);
 uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device);
 cudaError_t comm_allreduce_sum(void* comm, float* data, uint64_t count, cudaStream_t stream);
