@@ -304,7 +304,7 @@ def main():
     # with the bias + GELU epilogue, paired-SM kernel), from one ncu capture of that launch:
     # dram__bytes_read.sum + dram__bytes_write.sum. Its algorithmic bytes are 620.8 MB (A and B
     # read once, GELU output and pre-activation written once).
-    traffic = 184.3e6 + 478.7e6
+    traffic = 185.2e6 + 479.4e6
     result = {
         "metric": "train tokens/sec (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
