@@ -1187,11 +1187,12 @@ GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
 }
 
 // Longest K (in 32-element blocks) a concatenated 3xTF32 product accumulates in one tensor-core
-// accumulator. The accumulator's adds are not IEEE fp32 (measured: a C5-width training step's
-// gradients drifted 1.3e-4 from float64 with K' = 3 x 16384 in one accumulator, against 2.4e-6 when
-// sums moved to fp32 registers every 3 x 128); past this length the K dimension is split and the
-// partial tiles summed in fp32 by the reduction pass, as the three-section kernel's chunks are.
-constexpr uint32_t kX3MaxBlocks = 96;  // 3072 K elements = 3 sections of 1024
+// accumulator. The accumulator's adds are not round-to-nearest fp32: the error grows with the
+// number of K = 8 steps added into it. Measured on a C5-width training step against float64:
+// K' = 3 x 16384 in one accumulator 1.3e-4, at most 3072 per accumulator 1.9e-5, sums moved to fp32
+// registers every 3 x 128 (the three-section kernel) 2.4e-6. Past this length the K dimension is
+// split and the partial tiles are summed in fp32 by the reduction pass.
+constexpr uint32_t kX3MaxBlocks = 16;  // 512 K' elements (64 accumulator steps) per partial
 
 uint32_t x3_min_parts(uint64_t k) {
   const uint64_t kb = (k + BK - 1) / BK;

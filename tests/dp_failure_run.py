@@ -1,9 +1,12 @@
 """Worker for tests/test_dp_gpu.py::test_peer_missing_a_step_gets_code_3: one process per GPU
-under torchrun, NVLS off. Both ranks run step 1 of the training runtime with a NCCL communicator;
-then the last rank stays alive but does not join step 2 (it waits on the host until rank 0 is
-done, so none of its memory goes away while rank 0's collectives wait for it). Rank 0's step 2
-must end with status code 3 from the communicator's bounded wait (deadline 5 s) instead of
-hanging; its communicator is then aborted. Rank 0 writes what it saw to --out.
+under torchrun, NVLS off. Both ranks run steps 1 and 2 of the training runtime with a NCCL
+communicator (so every collective the step uses, including the sharded optimiser's parameter
+all-gather that step 1 does not need, has made its connections: NCCL connects lazily, and a first
+use whose peer is gone would block inside the enqueue, on the host); then the last rank stays
+alive but does not join step 3 (it waits on the host until rank 0 is done, so none of its memory
+goes away while rank 0's collectives wait for it). Rank 0's step 3 (a graph replay) must end with
+status code 3 from the communicator's bounded wait (deadline 5 s) instead of hanging; its
+communicator is then aborted. Rank 0 writes what it saw to --out.
 """
 from __future__ import annotations
 
@@ -48,10 +51,11 @@ def main(out: str) -> None:
                                                               ctypes.byref(comm)))
     _lib.check("spar_b200_comm_set_timeout", lib.spar_b200_comm_set_timeout(comm, 5.0))
     lm.attach_comm(comm, world)
-    ids = [rank_share(11 + s, 8, 1, cfg.seq, cfg.vocab, rank, world) for s in (1, 2)]
+    ids = [rank_share(11 + s, 8, 1, cfg.seq, cfg.vocab, rank, world) for s in (1, 2, 3)]
     lm.train_step(ids[0], 3e-4, step=1)
+    lm.train_step(ids[1], 3e-4, step=2)
     torch.cuda.synchronize()
-    dist.barrier()  # step 1 done everywhere
+    dist.barrier()  # steps 1 and 2 done everywhere
     if rank == world - 1:
         store.wait(["rank0_done"], datetime.timedelta(seconds=120))  # alive, but skips step 2
         lib.spar_b200_comm_destroy(comm, 1)
@@ -59,8 +63,8 @@ def main(out: str) -> None:
         return
     start = time.monotonic()
     try:
-        lm.train_step(ids[1], 3e-4, step=2)
-        seen = "step 2 completed"
+        lm.train_step(ids[2], 3e-4, step=3)
+        seen = "step 3 completed"
     except _lib.SparError as e:
         seen = f"code {e.code} after {time.monotonic() - start:.1f}s"
     # The context still works after the abort: a plain device computation.

@@ -84,9 +84,9 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, shard):
 
 
 def test_peer_missing_a_step_gets_code_3(cuda, tmp_path):
-    """A peer that stays alive but skips a step: the other rank's collectives can never complete;
-    the runtime's bounded wait (5 s here) aborts the communicator and the step returns code 3,
-    the device context stays usable. Two GPUs, NVLS off."""
+    """A peer that stays alive but skips a step (after two steps together): the other rank's
+    collectives can never complete; the runtime's bounded wait (5 s here) aborts the communicator
+    and the step returns code 3, the device context stays usable. Two GPUs, NVLS off."""
     import torch
 
     if torch.cuda.device_count() < 2:
