@@ -90,6 +90,10 @@ struct AttnParams {
   float scale, scale_log2;
   uint32_t tiles;  // stationary tiles per (batch, head)
   uint32_t adjacent_pairs;  // forward: items pair query tiles (2p, 2p+1), heaviest first
+  // Forward, balanced pairs only: the pairs of one (batch, head) are consecutive items, so the
+  // CTAs running at the same time share that head's K / V tiles through L2 (otherwise the items of
+  // one pair index run together over every head and each K / V tile is fetched once per pair).
+  uint32_t head_major;
   uint32_t total;  // work items
   uint32_t round_out;  // store ctx / dqkv rounded to nearest TF32 (they only feed TF32 products)
   // Backward, optional (seq a multiple of 32): per 32-row block column sums of dqkv (the qkv
@@ -310,8 +314,15 @@ struct PairItem {
 };
 
 __device__ __forceinline__ PairItem decode_pair(const AttnParams& p, uint32_t idx) {
-  const uint32_t pair = idx / p.bh;
-  const uint32_t bh = idx - pair * p.bh;
+  uint32_t pair, bh;
+  if (p.head_major) {
+    const uint32_t pairs = (p.tiles + 1) / 2;
+    bh = idx / pairs;
+    pair = idx - bh * pairs;
+  } else {
+    pair = idx / p.bh;
+    bh = idx - pair * p.bh;
+  }
   PairItem it;
   it.b = bh / p.heads;
   it.h = bh - it.b * p.heads;
@@ -1306,42 +1317,60 @@ cudaError_t launch_attn(K kernel, uint32_t smem, const AttnParams& p, int device
 // slightly better than balanced lists, so that order is kept there.
 // Stored as CSR in device memory [grid + 1 offsets | items], built once per (device, side, shape,
 // kind): the first backward call of a shape allocates, so make it before any stream capture.
+// With head_pairs (the kOrderHead order) the lists are instead made of tile pairs (T-1-t, t) of
+// one (batch, head), heavier tile first; pair k (counted head by head) goes to CTA k % grid. A
+// pair's cost is the same for every t (the triangle's rows and columns sum to T+1 tiles), so the
+// lists balance without sorting, and the CTAs that start together work on the same heads.
 cudaError_t backward_schedule(int device, bool key_side, uint32_t bh, uint32_t tiles, uint32_t seq,
-                              uint32_t group, bool lpt, const uint32_t** out, uint32_t* grid_out) {
-  using Key = std::tuple<int, bool, uint32_t, uint32_t, uint32_t, uint32_t, bool>;
+                              uint32_t group, bool lpt, const uint32_t** out, uint32_t* grid_out,
+                              bool head_pairs = false) {
+  using Key = std::tuple<int, bool, uint32_t, uint32_t, uint32_t, uint32_t, bool, bool>;
   static std::mutex mu;
   static std::map<Key, std::pair<uint32_t*, uint32_t>> cache;
   std::lock_guard<std::mutex> lock(mu);
-  const Key key{device, key_side, bh, tiles, seq, group, lpt};
+  const Key key{device, key_side, bh, tiles, seq, group, lpt, head_pairs};
   auto it = cache.find(key);
   if (it == cache.end()) {
     const uint32_t total = bh * tiles;
-    const uint32_t grid = std::min<uint32_t>(total, static_cast<uint32_t>(sm_count(device)));
+    const uint32_t pairs = (tiles + 1) / 2;
+    const uint32_t grid = std::min<uint32_t>(head_pairs ? bh * pairs : total,
+                                             static_cast<uint32_t>(sm_count(device)));
     const uint32_t nq_all = (seq + 63) / 64;
     auto cost = [&](uint32_t t) -> uint64_t {
       if (key_side) return static_cast<uint64_t>(nq_all - 2 * t) * group;
       return (std::min<uint64_t>(seq, 128ull * t + 128) + 63) / 64;
     };
-    std::vector<uint32_t> items(total);
-    for (uint32_t i = 0; i < total; ++i) items[i] = i;
-    std::stable_sort(items.begin(), items.end(), [&](uint32_t a, uint32_t b) {
-      return cost(a / bh) > cost(b / bh);
-    });
-    using Slot = std::pair<uint64_t, uint32_t>;  // (assigned cost, cta)
-    std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> heap;
-    for (uint32_t c = 0; c < grid; ++c) heap.push({0, c});
     std::vector<std::vector<uint32_t>> lists(grid);
-    for (uint32_t k = 0; k < total; ++k) {  // !lpt: CTA c takes items c, c + grid, ...
-      const uint32_t i = items[k];
-      if (!lpt) {
-        lists[k % grid].push_back(i);
-        continue;
+    if (head_pairs) {
+      for (uint32_t h = 0; h < bh; ++h)
+        for (uint32_t q = 0; q < pairs; ++q) {
+          const uint32_t lo = q, hi = tiles - 1 - q;
+          const uint32_t heavy = cost(lo) >= cost(hi) ? lo : hi, light = heavy == lo ? hi : lo;
+          std::vector<uint32_t>& l = lists[(h * pairs + q) % grid];
+          l.push_back(heavy * bh + h);
+          if (light != heavy) l.push_back(light * bh + h);
+        }
+    } else {
+      std::vector<uint32_t> items(total);
+      for (uint32_t i = 0; i < total; ++i) items[i] = i;
+      std::stable_sort(items.begin(), items.end(), [&](uint32_t a, uint32_t b) {
+        return cost(a / bh) > cost(b / bh);
+      });
+      using Slot = std::pair<uint64_t, uint32_t>;  // (assigned cost, cta)
+      std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> heap;
+      for (uint32_t c = 0; c < grid; ++c) heap.push({0, c});
+      for (uint32_t k = 0; k < total; ++k) {  // !lpt: CTA c takes items c, c + grid, ...
+        const uint32_t i = items[k];
+        if (!lpt) {
+          lists[k % grid].push_back(i);
+          continue;
+        }
+        Slot sl = heap.top();
+        heap.pop();
+        lists[sl.second].push_back(i);
+        sl.first += cost(i / bh);
+        heap.push(sl);
       }
-      Slot sl = heap.top();
-      heap.pop();
-      lists[sl.second].push_back(i);
-      sl.first += cost(i / bh);
-      heap.push(sl);
     }
     std::vector<uint32_t> host(grid + 1 + total);
     uint32_t pos = 0;
@@ -1384,6 +1413,23 @@ void base_params(AttnParams& p, uint64_t batch, uint64_t seq, uint64_t heads, ui
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Work orders of the persistent kernels. kOrderAuto: the forward pairs adjacent query tiles
+// heaviest first when there are at least four items per SM, else tiles t and T-1-t; the backward
+// lists are cost-ordered (longest first). kOrderHead: forward tiles t and T-1-t with the pairs of
+// one (batch, head) consecutive; backward lists of tile pairs (t, T-1-t) of one (batch, head)
+// handed to consecutive CTAs, so the CTAs that run together read the same head's tiles and L2
+// serves the repeats. SPAR_B200_ATTN_ORDER=head | auto overrides the default.
+enum AttnOrder { kOrderAuto = 0, kOrderHead = 1 };
+
+AttnOrder attn_order() {
+  static const AttnOrder order = [] {
+    const char* e = getenv("SPAR_B200_ATTN_ORDER");
+    if (e && std::strcmp(e, "head") == 0) return kOrderHead;
+    return kOrderAuto;
+  }();
+  return order;
+}
+
 }  // namespace
 
 bool attention_supported(uint64_t head_dim) { return head_dim == 32 || head_dim == 64; }
@@ -1405,7 +1451,10 @@ cudaError_t attention_forward_launch(const float* qkv, float* ctx, float* row_ma
   p.row_inv = row_inv;
   p.tiles = static_cast<uint32_t>((seq + 127) / 128);
   p.total = (p.tiles + 1) / 2 * p.bh;  // pairs of query tiles
-  p.adjacent_pairs = p.total >= 4u * static_cast<uint32_t>(sm_count(device)) ? 1u : 0u;
+  if (attn_order() == kOrderHead)
+    p.head_major = 1u;
+  else
+    p.adjacent_pairs = p.total >= 4u * static_cast<uint32_t>(sm_count(device)) ? 1u : 0u;
   static bool cfg32[64] = {}, cfg64[64] = {};
   return head_dim == 64 ? launch_attn(attn_fwd_kernel<64>, Fwd<64>::kSmem, p, device, stream, cfg64)
                         : launch_attn(attn_fwd_kernel<32>, Fwd<32>::kSmem, p, device, stream, cfg32);
@@ -1454,11 +1503,12 @@ cudaError_t attention_backward_launch(const float* qkv, const float* ctx, const 
   AttnParams pk = p;  // the key kernel's items: one per key / value head
   pk.total = p.tiles * p.kv_bh;
   const bool side_by_side = key_stream && fork && join;
+  const bool head_pairs = attn_order() == kOrderHead;
   e = backward_schedule(device, false, p.bh, p.tiles, p.seq, p.group, !side_by_side, &p.sched,
-                        &p.sched_grid);
+                        &p.sched_grid, head_pairs);
   if (e == cudaSuccess)
     e = backward_schedule(device, true, pk.kv_bh, pk.tiles, pk.seq, pk.group, !side_by_side,
-                          &pk.sched, &pk.sched_grid);
+                          &pk.sched, &pk.sched_grid, head_pairs);
   if (e != cudaSuccess) return e;
   // The query and key kernels only share inputs (they write dq and dk / dv): on a second stream
   // the key kernel's CTAs take the SMs that the query kernel's last items leave idle.

@@ -893,7 +893,10 @@ ConcatShape concat_shape(const SparB200Gemm& g) {
 // Split-K reduction and epilogue: the partial tiles [kparts][m][ldp] are summed in split order
 // (deterministic), then the GEMM's epilogue is applied exactly as the tile epilogue does it
 // (alpha, bias, residual / GELU' aux, bias + GELU with the pre-activation to aux, RoPE,
-// rounding to TF32, accumulate into C).
+// rounding to TF32, accumulate into C). A thread owns four adjacent columns of a row; the last
+// group of a row may hold fewer (n not a multiple of 4), and C / aux are accessed element by
+// element unless their rows are 16-byte aligned (`vec`). ldp is a multiple of 4, so the partials
+// are always read four at a time (the columns past n there are never used).
 struct SplitEpilogue {
   float* c;
   uint64_t ldc;
@@ -901,7 +904,7 @@ struct SplitEpilogue {
   uint64_t ldp;
   uint32_t kparts, m, n;
   float alpha;
-  int accumulate, epilogue, round_out;
+  int accumulate, epilogue, round_out, vec;
   const float* bias;
   float* aux;
   uint64_t ldaux;
@@ -911,7 +914,7 @@ struct SplitEpilogue {
 
 __global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
   pdl_begin();
-  const uint32_t n4 = q.n / 4;
+  const uint32_t n4 = (q.n + 3) / 4;
   const uint64_t total = static_cast<uint64_t>(q.m) * n4;
   const uint64_t plane = static_cast<uint64_t>(q.m) * q.ldp;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
@@ -922,6 +925,8 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
        i += stride) {
     const uint64_t r = i / n4;
     const uint32_t col = static_cast<uint32_t>(i % n4) * 4;
+    const uint32_t cnt = min(4u, q.n - col);  // columns of this group inside the matrix
+    const bool vec = q.vec && cnt == 4;
     const float* src = q.part + r * q.ldp + col;
     float4 acc = *reinterpret_cast<const float4*>(src);
     for (uint32_t s = 1; s < q.kparts; ++s) {
@@ -934,23 +939,33 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
     float v[4] = {q.alpha * acc.x, q.alpha * acc.y, q.alpha * acc.z, q.alpha * acc.w};
     if (bias) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] += __ldg(q.bias + col + e);
+      for (int e = 0; e < 4; ++e)
+        if (static_cast<uint32_t>(e) < cnt) v[e] += __ldg(q.bias + col + e);
     }
     float* auxp = q.aux ? q.aux + r * q.ldaux + col : nullptr;
     if (q.epilogue == SPAR_B200_EPI_BIAS_ADD || q.epilogue == SPAR_B200_EPI_GELU_BWD) {
-      const float4 x = *reinterpret_cast<const float4*>(auxp);
-      const float a4[4] = {x.x, x.y, x.z, x.w};
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+      if (vec) {
+        const float4 x = *reinterpret_cast<const float4*>(auxp);
+        a4[0] = x.x; a4[1] = x.y; a4[2] = x.z; a4[3] = x.w;
+      } else {
+        for (uint32_t e = 0; e < cnt; ++e) a4[e] = auxp[e];
+      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         if (q.epilogue == SPAR_B200_EPI_BIAS_ADD) v[e] += a4[e];
         else v[e] *= gelu_derivative_fast(a4[e]);
       }
     } else if (q.epilogue == SPAR_B200_EPI_BIAS_GELU) {
-      *reinterpret_cast<float4*>(auxp) = make_float4(v[0], v[1], v[2], v[3]);
+      if (vec) {
+        *reinterpret_cast<float4*>(auxp) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+        for (uint32_t e = 0; e < cnt; ++e) auxp[e] = v[e];
+      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = gelu_value_fast(v[e]);
     }
-    if (q.rope && col < q.rope_cols) {
+    if (q.rope && col < q.rope_cols) {  // rope_cols and the head width are even: whole pairs
       const float2* tab = q.rope + (r % q.rope_seq) * q.rope_half;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
@@ -964,16 +979,21 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = round_tf32(v[e]);
     }
-    float4* dst = reinterpret_cast<float4*>(q.c + r * q.ldc + col);
-    float4 o = make_float4(v[0], v[1], v[2], v[3]);
-    if (q.accumulate) {
-      const float4 prev = *dst;
-      o.x += prev.x;
-      o.y += prev.y;
-      o.z += prev.z;
-      o.w += prev.w;
+    float* out = q.c + r * q.ldc + col;
+    if (vec) {
+      float4* dst = reinterpret_cast<float4*>(out);
+      float4 o = make_float4(v[0], v[1], v[2], v[3]);
+      if (q.accumulate) {
+        const float4 prev = *dst;
+        o.x += prev.x;
+        o.y += prev.y;
+        o.z += prev.z;
+        o.w += prev.w;
+      }
+      *dst = o;
+    } else {
+      for (uint32_t e = 0; e < cnt; ++e) out[e] = q.accumulate ? out[e] + v[e] : v[e];
     }
-    *dst = o;
   }
 }
 
@@ -1365,12 +1385,16 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     q.bias = g.bias;
     q.aux = g.aux;
     q.ldaux = g.ldaux;
+    const auto rows16 = [](const void* ptr, uint64_t ld) {
+      return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 4 == 0;
+    };
+    q.vec = rows16(g.c, g.ldc) && (!g.aux || rows16(g.aux, g.ldaux)) ? 1 : 0;
     q.rope = p.rope;
     q.rope_seq = p.rope_seq;
     q.rope_dim = p.rope_dim;
     q.rope_cols = p.rope_cols;
     q.rope_half = p.rope_half;
-    const uint64_t work = g.m * (g.n / 4);
+    const uint64_t work = g.m * ((g.n + 3) / 4);
     return launch(splitk_reduce_kernel, dim3(grid_for(work, 256, sm_count(device) * 8)), dim3(256),
                   0, stream, q);
   }

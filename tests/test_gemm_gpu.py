@@ -388,3 +388,33 @@ def test_gemm_column_partials(cuda, shape, epi, precision):
     want = c.cpu().numpy().astype(np.float64).sum(0)
     scale = np.abs(c.cpu().numpy()).astype(np.float64).sum(0)
     assert np.all(np.abs(got - want) <= 1e-5 * scale + 1e-30)
+
+
+@pytest.mark.parametrize("precision,accumulate", [(0, False), (1, False), (1, True)])
+def test_gemm_split_k_ragged_columns(cuda, precision, accumulate):
+    """A K-split product whose column count is not a multiple of 4, stored with a padded row
+    stride (the tied LM head: logits [tokens, vocab] in rows of the padded vocabulary). The
+    reduction writes every column up to n, the bias included, and none of the padding."""
+    import torch
+    from spar_b200 import ops
+
+    m, n, k, ldc = 256, 301, 8192, 304
+    a, b, ref = _mats(m, n, k, False, True, seed=41)
+    bias = np.random.default_rng(42).standard_normal(n).astype(np.float32)
+    prev = np.random.default_rng(43).standard_normal((m, n)).astype(np.float32)
+    at, bt = torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda)
+    biast = torch.from_numpy(bias).to(cuda)
+    c = torch.full((m, ldc), float("nan"), device=cuda)
+    if accumulate:
+        c[:, :n] = torch.from_numpy(prev).to(cuda)
+    desc = ops.gemm_desc(m, n, k, at.data_ptr(), k, bt.data_ptr(), k, c.data_ptr(), ldc, b_t=True,
+                         accumulate=accumulate, epilogue=ops.EPI_BIAS, bias=biast.data_ptr(),
+                         precision=precision)
+    ops.gemm_run(desc, 0, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert ops.gemm_error(0) == 0
+    got = c.cpu().numpy()
+    assert np.isnan(got[:, n:]).all()  # padding untouched
+    expect = ref + bias + (prev if accumulate else 0.0)
+    assert not np.isnan(got[:, :n]).any()
+    assert rel_l2(got[:, :n], expect) <= (1e-5 if precision else 2e-3)
