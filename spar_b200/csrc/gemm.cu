@@ -910,90 +910,117 @@ struct SplitEpilogue {
   uint64_t ldaux;
   const float2* rope;
   uint32_t rope_seq, rope_dim, rope_cols, rope_half;
+  float* colpart;  // optional [ceil(m / 32)][n] column sums of each 32-row block
 };
 
-__global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
-  pdl_begin();
-  const uint32_t n4 = (q.n + 3) / 4;
-  const uint64_t total = static_cast<uint64_t>(q.m) * n4;
+// One row's group of up to four columns: the partial sums added in split order, the epilogue,
+// the store. `pre` receives the values before rounding (what the column partials sum).
+__device__ __forceinline__ void reduce_group(const SplitEpilogue& q, uint64_t r, uint32_t col,
+                                             float (&pre)[4]) {
+  const uint32_t cnt = min(4u, q.n - col);  // columns of this group inside the matrix
+  const bool vec = q.vec && cnt == 4;
   const uint64_t plane = static_cast<uint64_t>(q.m) * q.ldp;
-  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   const bool bias = q.bias && (q.epilogue == SPAR_B200_EPI_BIAS ||
                                q.epilogue == SPAR_B200_EPI_BIAS_GELU ||
                                q.epilogue == SPAR_B200_EPI_BIAS_ADD);
+  const float* src = q.part + r * q.ldp + col;
+  float4 acc = *reinterpret_cast<const float4*>(src);
+  for (uint32_t s = 1; s < q.kparts; ++s) {
+    const float4 x = *reinterpret_cast<const float4*>(src + s * plane);
+    acc.x += x.x;
+    acc.y += x.y;
+    acc.z += x.z;
+    acc.w += x.w;
+  }
+  float v[4] = {q.alpha * acc.x, q.alpha * acc.y, q.alpha * acc.z, q.alpha * acc.w};
+  if (bias) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (static_cast<uint32_t>(e) < cnt) v[e] += __ldg(q.bias + col + e);
+  }
+  float* auxp = q.aux ? q.aux + r * q.ldaux + col : nullptr;
+  if (q.epilogue == SPAR_B200_EPI_BIAS_ADD || q.epilogue == SPAR_B200_EPI_GELU_BWD) {
+    float a4[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec) {
+      const float4 x = *reinterpret_cast<const float4*>(auxp);
+      a4[0] = x.x; a4[1] = x.y; a4[2] = x.z; a4[3] = x.w;
+    } else {
+      for (uint32_t e = 0; e < cnt; ++e) a4[e] = auxp[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (q.epilogue == SPAR_B200_EPI_BIAS_ADD) v[e] += a4[e];
+      else v[e] *= gelu_derivative_fast(a4[e]);
+    }
+  } else if (q.epilogue == SPAR_B200_EPI_BIAS_GELU) {
+    if (vec) {
+      *reinterpret_cast<float4*>(auxp) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      for (uint32_t e = 0; e < cnt; ++e) auxp[e] = v[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = gelu_value_fast(v[e]);
+  }
+  if (q.rope && col < q.rope_cols) {  // rope_cols and the head width are even: whole pairs
+    const float2* tab = q.rope + (r % q.rope_seq) * q.rope_half;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float2 cs = __ldg(tab + ((col + 2 * k) % q.rope_dim) / 2);
+      const float x0 = v[2 * k], x1 = v[2 * k + 1];
+      v[2 * k] = x0 * cs.x - x1 * cs.y;
+      v[2 * k + 1] = x0 * cs.y + x1 * cs.x;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) pre[e] = static_cast<uint32_t>(e) < cnt ? v[e] : 0.f;
+  if (q.round_out) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = round_tf32(v[e]);
+  }
+  float* out = q.c + r * q.ldc + col;
+  if (vec) {
+    float4* dst = reinterpret_cast<float4*>(out);
+    float4 o = make_float4(v[0], v[1], v[2], v[3]);
+    if (q.accumulate) {
+      const float4 prev = *dst;
+      o.x += prev.x;
+      o.y += prev.y;
+      o.z += prev.z;
+      o.w += prev.w;
+    }
+    *dst = o;
+  } else {
+    for (uint32_t e = 0; e < cnt; ++e) out[e] = q.accumulate ? out[e] + v[e] : v[e];
+  }
+}
+
+// Thread = (row, four-column group); with column partials, thread = (32-row block, four-column
+// group), which walks the block's rows and writes the block's column sums of the epilogue output
+// (before rounding) to colpart[block][n], as the tile epilogue does for an unsplit product.
+__global__ void splitk_reduce_kernel(const __grid_constant__ SplitEpilogue q) {
+  pdl_begin();
+  const uint32_t n4 = (q.n + 3) / 4;
+  const uint64_t rows = q.colpart ? (static_cast<uint64_t>(q.m) + 31) / 32 : q.m;
+  const uint64_t total = rows * n4;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += stride) {
     const uint64_t r = i / n4;
     const uint32_t col = static_cast<uint32_t>(i % n4) * 4;
-    const uint32_t cnt = min(4u, q.n - col);  // columns of this group inside the matrix
-    const bool vec = q.vec && cnt == 4;
-    const float* src = q.part + r * q.ldp + col;
-    float4 acc = *reinterpret_cast<const float4*>(src);
-    for (uint32_t s = 1; s < q.kparts; ++s) {
-      const float4 x = *reinterpret_cast<const float4*>(src + s * plane);
-      acc.x += x.x;
-      acc.y += x.y;
-      acc.z += x.z;
-      acc.w += x.w;
+    float pre[4];
+    if (!q.colpart) {
+      reduce_group(q, r, col, pre);
+      continue;
     }
-    float v[4] = {q.alpha * acc.x, q.alpha * acc.y, q.alpha * acc.z, q.alpha * acc.w};
-    if (bias) {
+    float cs[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint64_t r1 = r * 32 + 32 < q.m ? r * 32 + 32 : q.m;
+    for (uint64_t row = r * 32; row < r1; ++row) {
+      reduce_group(q, row, col, pre);
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (static_cast<uint32_t>(e) < cnt) v[e] += __ldg(q.bias + col + e);
+      for (int e = 0; e < 4; ++e) cs[e] += pre[e];
     }
-    float* auxp = q.aux ? q.aux + r * q.ldaux + col : nullptr;
-    if (q.epilogue == SPAR_B200_EPI_BIAS_ADD || q.epilogue == SPAR_B200_EPI_GELU_BWD) {
-      float a4[4] = {0.f, 0.f, 0.f, 0.f};
-      if (vec) {
-        const float4 x = *reinterpret_cast<const float4*>(auxp);
-        a4[0] = x.x; a4[1] = x.y; a4[2] = x.z; a4[3] = x.w;
-      } else {
-        for (uint32_t e = 0; e < cnt; ++e) a4[e] = auxp[e];
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if (q.epilogue == SPAR_B200_EPI_BIAS_ADD) v[e] += a4[e];
-        else v[e] *= gelu_derivative_fast(a4[e]);
-      }
-    } else if (q.epilogue == SPAR_B200_EPI_BIAS_GELU) {
-      if (vec) {
-        *reinterpret_cast<float4*>(auxp) = make_float4(v[0], v[1], v[2], v[3]);
-      } else {
-        for (uint32_t e = 0; e < cnt; ++e) auxp[e] = v[e];
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = gelu_value_fast(v[e]);
-    }
-    if (q.rope && col < q.rope_cols) {  // rope_cols and the head width are even: whole pairs
-      const float2* tab = q.rope + (r % q.rope_seq) * q.rope_half;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const float2 cs = __ldg(tab + ((col + 2 * k) % q.rope_dim) / 2);
-        const float x0 = v[2 * k], x1 = v[2 * k + 1];
-        v[2 * k] = x0 * cs.x - x1 * cs.y;
-        v[2 * k + 1] = x0 * cs.y + x1 * cs.x;
-      }
-    }
-    if (q.round_out) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = round_tf32(v[e]);
-    }
-    float* out = q.c + r * q.ldc + col;
-    if (vec) {
-      float4* dst = reinterpret_cast<float4*>(out);
-      float4 o = make_float4(v[0], v[1], v[2], v[3]);
-      if (q.accumulate) {
-        const float4 prev = *dst;
-        o.x += prev.x;
-        o.y += prev.y;
-        o.z += prev.z;
-        o.w += prev.w;
-      }
-      *dst = o;
-    } else {
-      for (uint32_t e = 0; e < cnt; ++e) out[e] = q.accumulate ? out[e] + v[e] : v[e];
-    }
+    const uint32_t cnt = min(4u, q.n - col);
+    for (uint32_t e = 0; e < cnt; ++e) q.colpart[r * q.n + col + e] = cs[e];
   }
 }
 
@@ -1219,7 +1246,7 @@ uint32_t x3_min_parts(uint64_t k) {
   return static_cast<uint32_t>((kb + kX3MaxBlocks - 1) / kX3MaxBlocks);
 }
 
-// Column partials are written by the GEMM's own epilogue, which a K split hands to the reduction.
+// A K split hands the epilogue, column partials included, to the reduction kernel.
 GemmPlan gemm_plan_for(const SparB200Gemm& g, int device, uint32_t min_parts = 1) {
   GemmPlan pl = gemm_plan(g, device);
   if (pl.kparts < min_parts) {
@@ -1229,7 +1256,6 @@ GemmPlan gemm_plan_for(const SparB200Gemm& g, int device, uint32_t min_parts = 1
     while (pl.kparts > 1 && (pl.kparts - 1) * ((kb + pl.kparts - 1) / pl.kparts) >= kb)
       --pl.kparts;
   }
-  if (g.column_partials) pl.kparts = 1;
   return pl;
 }
 
@@ -1389,12 +1415,13 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
       return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 4 == 0;
     };
     q.vec = rows16(g.c, g.ldc) && (!g.aux || rows16(g.aux, g.ldaux)) ? 1 : 0;
+    q.colpart = g.column_partials;
     q.rope = p.rope;
     q.rope_seq = p.rope_seq;
     q.rope_dim = p.rope_dim;
     q.rope_cols = p.rope_cols;
     q.rope_half = p.rope_half;
-    const uint64_t work = g.m * ((g.n + 3) / 4);
+    const uint64_t work = (g.column_partials ? (g.m + 31) / 32 : g.m) * ((g.n + 3) / 4);
     return launch(splitk_reduce_kernel, dim3(grid_for(work, 256, sm_count(device) * 8)), dim3(256),
                   0, stream, q);
   }

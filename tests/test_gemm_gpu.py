@@ -363,11 +363,14 @@ def test_contiguous_matmul_any_shape(cuda, shape, dtype):
 
 @pytest.mark.parametrize("precision", [0, 1])
 @pytest.mark.parametrize("epi", ["gelu_bwd", "bias", "none"])
-@pytest.mark.parametrize("shape", [(2048, 4096, 1024), (300, 200, 96), (16384, 3072, 256)])
+@pytest.mark.parametrize("shape", [(2048, 4096, 1024), (300, 200, 96), (16384, 3072, 256),
+                                   (256, 300, 8192)])
 def test_gemm_column_partials(cuda, shape, epi, precision):
     """The epilogue's per-32-row column sums (the bias gradient of a product without re-reading
     its output): their row sums equal the column sums of C (float64 reference) to fp32
-    summation error, whatever tile kernel and epilogue the plan picks; K is never split."""
+    summation error, whatever tile kernel and epilogue the plan picks. With a K split (3xTF32
+    past 512 concatenated K elements; the last shape in either precision) the reduction kernel
+    writes them."""
     import torch
     from spar_b200 import ops
 
