@@ -261,7 +261,9 @@ struct SparB200Gemm {
   uint64_t b_batch_stride[2];
   int b_transposed;
   float* c;
-  uint64_t ldc;
+  uint64_t ldc; /* multiple of 4, like every leading dimension and batch stride here. Rows of C */
+                /* are stored in whole 16-byte chunks: when n is not a multiple of 4, the up to  */
+                /* 3 floats after column n - 1 of a row (inside ldc) may be overwritten.        */
   uint64_t c_batch_stride[2];
   float alpha;
   int accumulate; /* 1: C += result (beta = 1) */
@@ -284,8 +286,8 @@ struct SparB200Gemm {
   /* Optional, unbatched GEMMs only: per 32-row block column sums of this product's epilogue     */
   /* output (before accumulation into C and before output rounding; rows past m count as zero),  */
   /* written to column_partials[(row / 32) * n + col], a [ceil(m / 32), n] array. Summing its    */
-  /* rows gives the column sums of the result (a bias gradient) without re-reading C. K is then   */
-  /* never split.                                                                               */
+  /* rows gives the column sums of the result (a bias gradient) without re-reading C. With a K   */
+  /* split the split-K reduction writes them (summed row by row, same values to fp32 rounding).  */
   float* column_partials;
 };
 struct SparCudaStatus spar_b200_gemm(const struct SparB200Gemm* gemm, int device, void* stream);

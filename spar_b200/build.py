@@ -52,7 +52,9 @@ def _compile(src: Path, obj: Path, newest_header: float, verbose: bool) -> None:
     if src.suffix == ".cu":
         cmd = [NVCC, *ARCH, "-lineinfo", *COMMON, "-c", str(src), "-o", str(obj)]
     else:
-        cmd = [NVCC, *COMMON, "-x", "c++", "-c", str(src), "-o", str(obj)]
+        # host-only C++: no device code, so no target architecture to name
+        cmd = [NVCC, *COMMON, "-Wno-deprecated-gpu-targets", "-x", "c++", "-c", str(src), "-o",
+               str(obj)]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

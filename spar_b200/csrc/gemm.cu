@@ -577,9 +577,15 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_tf32_kernel(const __g
 // of the same name in both CTAs (two plain commits); both CTAs' epilogue warps arrive on the even
 // CTA's accumulator-empty barrier. Every wait is bounded; the closing cluster barrier keeps each
 // CTA (and its shared memory) alive until the even CTA has drained or given up.
-template <int BN, int STAGES, int EW>
+// DRAIN (concatenated 3xTF32 products): the tile's K range is accumulated in chunks of p.kchunk
+// k-blocks, alternating between the two TMEM accumulators; the epilogue warps add each chunk into
+// fp32 registers (round-to-nearest adds) and apply the epilogue to those sums after the last
+// chunk. The tensor cores' accumulation rounds toward zero, so the drift of a long hardware sum
+// is bounded by one chunk, without partial tiles in HBM.
+template <int BN, int STAGES, int EW, bool DRAIN = false>
 __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
   static_assert(BN == 256 || BN == 128, "paired tile N");
+  static_assert(!DRAIN || BN / 32 / (EW / 4) <= 2, "drained sums: at most 64 registers a thread");
   constexpr int BNH = BN / 2;  // B rows (N) staged by each CTA
   constexpr uint32_t A_BYTES = BM * BK * 4;
   constexpr uint32_t B_BYTES = BNH * BK * 4;
@@ -701,46 +707,50 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __g
         if (!decode_tile<BN>(p, idx, t)) continue;
         uint32_t kb0, kb1;
         k_range(p, t, kb0, kb1);
-        if (!tc::mbar_wait_cluster(tempty + acc, acc_phase ^ 1)) {
-          record_error();
-          *abort_flag = 1;
-          break;
-        }
-        tc::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (uint32_t kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
-          if (!tc::mbar_wait_cluster(full + stage, phase)) {
+        const uint32_t chunk = DRAIN ? p.kchunk : kb1 - kb0;
+        for (uint32_t c0 = kb0; c0 < kb1 && !*abort_flag; c0 += chunk) {
+          const uint32_t c1 = min(kb1, c0 + chunk);
+          if (!tc::mbar_wait_cluster(tempty + acc, acc_phase ^ 1)) {
             record_error();
             *abort_flag = 1;
             break;
           }
           tc::tc_fence_after();
-          const uint32_t a_addr = tc::smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t b_addr = a_addr + A_BYTES;
+          const uint32_t d_tmem = tmem_base + acc * BN;
+          for (uint32_t kb = c0; kb < c1 && !*abort_flag; ++kb) {
+            if (!tc::mbar_wait_cluster(full + stage, phase)) {
+              record_error();
+              *abort_flag = 1;
+              break;
+            }
+            tc::tc_fence_after();
+            const uint32_t a_addr = tc::smem_u32(smem + stage * STAGE_BYTES);
+            const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < BK / 8; ++ks) {
-            const uint64_t a_desc =
-                p.a_mn_major ? tc::smem_desc(a_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
-                             : tc::smem_desc(a_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
-            const uint64_t b_desc =
-                p.b_mn_major ? tc::smem_desc(b_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
-                             : tc::smem_desc(b_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
-            tc::mma_tf32_pair(d_tmem, a_desc, b_desc, idesc, (kb != kb0 || ks != 0) ? 1u : 0u);
+            for (int ks = 0; ks < BK / 8; ++ks) {
+              const uint64_t a_desc =
+                  p.a_mn_major ? tc::smem_desc(a_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                               : tc::smem_desc(a_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
+              const uint64_t b_desc =
+                  p.b_mn_major ? tc::smem_desc(b_addr + ks * 1024, 4096, 512, tc::kLayoutSw128Base32)
+                               : tc::smem_desc(b_addr + ks * 32, 16, 1024, tc::kLayoutSw128);
+              tc::mma_tf32_pair(d_tmem, a_desc, b_desc, idesc, (kb != c0 || ks != 0) ? 1u : 0u);
+            }
+            const uint32_t e = tc::smem_u32(empty + stage);
+            tc::mma_commit_pair(e);
+            tc::mma_commit_pair(tc::map_to_rank(e, peer));
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
-          const uint32_t e = tc::smem_u32(empty + stage);
-          tc::mma_commit_pair(e);
-          tc::mma_commit_pair(tc::map_to_rank(e, peer));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+          const uint32_t f = tc::smem_u32(tfull + acc);
+          tc::mma_commit_pair(f);
+          tc::mma_commit_pair(tc::map_to_rank(f, peer));
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
           }
-        }
-        const uint32_t f = tc::smem_u32(tfull + acc);
-        tc::mma_commit_pair(f);
-        tc::mma_commit_pair(tc::map_to_rank(f, peer));
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1;
         }
       }
       tc::mma_commit_pair(tc::smem_u32(drain));
@@ -769,6 +779,49 @@ __global__ void __launch_bounds__(threads_for(EW), 1) gemm_pair_kernel(const __g
       const uint32_t row0 = t.mt * 256 + rank * BM + quarter * 32;
       const uint32_t lane_base = tmem_base + ((quarter * 32) << 16);
       if (t.nt * BN + chunk0 * 32 < p.n) aux_prefetch(p, st, t.nt * BN + chunk0 * 32, row0, t.b1, t.b0);
+      if constexpr (DRAIN) {
+        constexpr int kC = kChunks;
+        uint32_t kb0, kb1;
+        k_range(p, t, kb0, kb1);
+        const uint32_t nchunks = (kb1 - kb0 + p.kchunk - 1) / p.kchunk;
+        float sum[kC][32];
+#pragma unroll
+        for (int c = 0; c < kC; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) sum[c][e] = 0.f;
+        for (uint32_t ci = 0; ci < nchunks; ++ci) {
+          if (!tc::mbar_wait_cluster(tfull + acc, acc_phase)) {
+            record_error();
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < kC; ++c) {
+            uint32_t r[32];
+            tc::tmem_load_32x32(lane_base + acc * BN + (chunk0 + c) * 32, r);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sum[c][e] += __uint_as_float(r[e]);
+          }
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive_cluster(tempty_leader + acc * 8);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < kC; ++c) {
+          const uint32_t col0 = t.nt * BN + (chunk0 + c) * 32;
+          if (col0 >= p.n) continue;
+          epilogue_box(p, st, sum[c], col0, row0, t.b1, t.b0, t.ks, ok);
+          if (c + 1 < kC && col0 + 32 < p.n) aux_prefetch(p, st, col0 + 32, row0, t.b1, t.b0);
+        }
+        continue;
+      }
       if (!tc::mbar_wait_cluster(tfull + acc, acc_phase)) {
         record_error();
         *abort_flag = 1;
@@ -1082,12 +1135,12 @@ cudaError_t launch_kernel(const GemmParams& p, int device, cudaStream_t stream) 
 }
 
 // Paired-SM launch: clusters of two CTAs, at most as many clusters as fit at once.
-template <int BN, int STAGES, int EW>
+template <int BN, int STAGES, int EW, bool DRAIN = false>
 cudaError_t launch_pair(const GemmParams& p, int device, cudaStream_t stream) {
   constexpr size_t smem = STAGES * (BM * BK * 4 + (BN / 2) * BK * 4) + epi_bytes(EW) + 1024 + 256;
   static_assert(smem <= 232448, "paired GEMM shared memory");
   static int max_clusters[64] = {0};
-  auto k = gemm_pair_kernel<BN, STAGES, EW>;
+  auto k = gemm_pair_kernel<BN, STAGES, EW, DRAIN>;
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -1202,7 +1255,7 @@ struct GemmPlan {
   uint32_t kparts;
 };
 
-GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
+GemmPlan gemm_plan(const SparB200Gemm& g, int device, bool narrow_only = false) {
   const bool x3 = g.precision == SPAR_B200_TF32X3;
   const uint64_t b = (g.batch[0] ? g.batch[0] : 1) * (g.batch[1] ? g.batch[1] : 1);
   const int sms = sm_count(device);
@@ -1216,7 +1269,7 @@ GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
     const TileModel narrow{256, 128, 7.0e12, 1.0, sms / 2};  // half the reuse of each A stage
     double us_wide = 1e30, us_narrow = 0.0;
     uint32_t parts_wide = 1;
-    if (g.n > 128) parts_wide = best_parts(g, wide, &us_wide);
+    if (g.n > 128 && !narrow_only) parts_wide = best_parts(g, wide, &us_wide);
     const uint32_t parts_narrow = best_parts(g, narrow, &us_narrow);
     pl.pair = true;
     if (us_wide <= us_narrow) {
@@ -1234,21 +1287,28 @@ GemmPlan gemm_plan(const SparB200Gemm& g, int device) {
 }
 
 // Longest K (in 32-element blocks) a concatenated 3xTF32 product accumulates in one tensor-core
-// accumulator. The accumulator's adds are not round-to-nearest fp32: the error grows with the
-// number of K = 8 steps added into it. Measured on a C5-width training step against float64:
-// K' = 3 x 16384 in one accumulator 1.3e-4, at most 3072 per accumulator 1.9e-5, sums moved to fp32
-// registers every 3 x 128 (the three-section kernel) 2.4e-6. Past this length the K dimension is
-// split and the partial tiles are summed in fp32 by the reduction pass.
-constexpr uint32_t kX3MaxBlocks = 16;  // 512 K' elements (64 accumulator steps) per partial
+// accumulator. The accumulator's adds round toward zero, so the error grows with the number of
+// K = 8 steps added into it. Measured on a C5-width training step against float64: K' = 3 x 16384
+// in one accumulator 1.3e-4, at most 3072 per accumulator 1.9e-5, sums moved to fp32 registers
+// every 3 x 128 (the three-section kernel) 2.4e-6. On SM pairs the kernel itself moves the sums
+// into fp32 registers every kX3DrainBlocks k-blocks (DRAIN); single-SM plans split K into parts of
+// at most kX3MaxBlocks k-blocks whose partial tiles the reduction pass sums in fp32.
+constexpr uint32_t kX3DrainBlocks = 8;  // 256 K' elements (32 accumulator steps) per drain
+constexpr uint32_t kX3MaxBlocks = 16;   // 512 K' elements (64 accumulator steps) per partial
 
 uint32_t x3_min_parts(uint64_t k) {
   const uint64_t kb = (k + BK - 1) / BK;
   return static_cast<uint32_t>((kb + kX3MaxBlocks - 1) / kX3MaxBlocks);
 }
 
+// The concatenated product t (TF32 over K' = 3 kp) drains its accumulator on SM pairs when the
+// plan puts it there (256 x 128 tiles, eight epilogue warps: 64 fp32 sums a thread).
+bool x3_drains(const SparB200Gemm& t, int device) { return gemm_plan(t, device, true).pair; }
+
 // A K split hands the epilogue, column partials included, to the reduction kernel.
-GemmPlan gemm_plan_for(const SparB200Gemm& g, int device, uint32_t min_parts = 1) {
-  GemmPlan pl = gemm_plan(g, device);
+GemmPlan gemm_plan_for(const SparB200Gemm& g, int device, uint32_t min_parts = 1,
+                       bool drain = false) {
+  GemmPlan pl = gemm_plan(g, device, drain);
   if (pl.kparts < min_parts) {
     pl.kparts = min_parts;
     // every split non-empty: (parts - 1) full splits of ceil(kb / parts) blocks stay below kb
@@ -1262,18 +1322,31 @@ GemmPlan gemm_plan_for(const SparB200Gemm& g, int device, uint32_t min_parts = 1
 uint64_t gemm_splitk_workspace_floats(const SparB200Gemm& g, int device) {
   uint32_t min_parts = 1;
   SparB200Gemm t = g;
+  bool drain = false;
   if (concat_x3(g)) {  // planned as the TF32 product it becomes
     t.precision = SPAR_B200_TF32;
     t.k = 3 * concat_shape(g).kp;
-    min_parts = x3_min_parts(t.k);
+    drain = x3_drains(t, device);
+    if (!drain) min_parts = x3_min_parts(t.k);
   }
-  const GemmPlan pl = gemm_plan_for(t, device, min_parts);
+  const GemmPlan pl = gemm_plan_for(t, device, min_parts, drain);
   return pl.kparts > 1 ? static_cast<uint64_t>(pl.kparts) * t.m * ((t.n + 3) / 4 * 4) : 0;
 }
+
+cudaError_t gemm_launch_plan(const SparB200Gemm& g, float* split_workspace, int device,
+                             cudaStream_t stream, float* splitk_workspace, uint64_t splitk_floats,
+                             uint32_t min_parts, bool drain);
 
 cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int device,
                         cudaStream_t stream, float* splitk_workspace = nullptr,
                         uint64_t splitk_floats = 0, uint32_t min_parts = 1) {
+  return gemm_launch_plan(g, split_workspace, device, stream, splitk_workspace, splitk_floats,
+                          min_parts, false);
+}
+
+cudaError_t gemm_launch_plan(const SparB200Gemm& g, float* split_workspace, int device,
+                             cudaStream_t stream, float* splitk_workspace, uint64_t splitk_floats,
+                             uint32_t min_parts, bool drain) {
   if (concat_x3(g)) {
     const ConcatShape c = concat_shape(g);
     float* a2 = split_workspace;
@@ -1294,16 +1367,18 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
     t.lda = c.a_ld;
     t.b = b2;
     t.ldb = c.b_ld;
-    return gemm_launch(t, nullptr, device, stream, splitk_workspace, splitk_floats,
-                       x3_min_parts(t.k));
+    const bool d = x3_drains(t, device);
+    return gemm_launch_plan(t, nullptr, device, stream, splitk_workspace, splitk_floats,
+                            d ? 1 : x3_min_parts(t.k), d);
   }
   GemmParams p;
   memset(&p, 0, sizeof(p));
   const uint64_t b1 = g.batch[1] ? g.batch[1] : 1, b0 = g.batch[0] ? g.batch[0] : 1;
   const bool split = g.precision == SPAR_B200_TF32X3;
   // 3xTF32 keeps its running sums in registers (one 64-column row segment per thread).
-  const GemmPlan plan = gemm_plan_for(g, device, min_parts);
+  const GemmPlan plan = gemm_plan_for(g, device, min_parts, drain);
   const int bn = plan.bn;
+  drain = drain && plan.pair && bn == 128;
   p.sections = split ? 3 : 1;
   p.a_mn_major = g.a_transposed ? 1 : 0;
   p.b_mn_major = g.b_transposed ? 0 : 1;
@@ -1390,7 +1465,9 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
       return cudaErrorInvalidValue;
     p.kparts = kparts;
     p.total_tiles *= kparts;
-    const cudaError_t e = pair      ? (bn == 256 ? launch_pair<256, 6, 4>(p, device, stream)
+    if (drain) p.kchunk = kX3DrainBlocks;
+    const cudaError_t e = drain     ? launch_pair<128, 6, 8, true>(p, device, stream)
+                        : pair      ? (bn == 256 ? launch_pair<256, 6, 4>(p, device, stream)
                                                  : launch_pair<128, 8, 4>(p, device, stream))
                         : bn == 256 ? launch_kernel<256, 4, false>(p, device, stream)
                         : bn == 128 ? launch_kernel<128, 6, false>(p, device, stream)
@@ -1426,6 +1503,10 @@ cudaError_t gemm_launch(const SparB200Gemm& g, float* split_workspace, int devic
                   0, stream, q);
   }
   if (split) return launch_kernel<64, 8, true>(p, device, stream);
+  if (drain) {
+    p.kchunk = kX3DrainBlocks;
+    return launch_pair<128, 6, 8, true>(p, device, stream);
+  }
   // Epilogues with per-element work beyond a bias add (GELU, GELU', residual / aux tiles, RoPE)
   // get eight epilogue warps (one fewer operand stage makes room for their staging boxes).
   const bool heavy = g.epilogue == SPAR_B200_EPI_BIAS_GELU || g.epilogue == SPAR_B200_EPI_GELU_BWD ||

@@ -337,6 +337,8 @@ def _main() -> None:
     cfg = replace(C5, micro_batch=a.micro_batch)
     if a.family == "spar":
         cfg = replace(cfg, family=1, kv_heads=a.kv_heads, qk_norm=a.qk_norm)
+    if a.precision == "tf32x3":
+        cfg = replace(cfg, precision=1)
     lm = DecoderLM(cfg, 0)
     lm.init_normal(0x5EED0005, 0.02)
     ids = torch.from_numpy(rank_share(0x5EED1005, 64, 4, cfg.seq, cfg.vocab, 0,

@@ -49,8 +49,11 @@ def test_gemm_tf32_layouts(cuda, shape, a_t, b_t):
 
 
 @pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False)])
-@pytest.mark.parametrize("shape", [(256, 512, 1024), (200, 300, 96), (1024, 1024, 2048)])
+@pytest.mark.parametrize("shape", [(256, 512, 1024), (200, 300, 96), (1024, 1024, 2048),
+                                   (512, 768, 24576), (128, 96, 24576)])
 def test_gemm_3xtf32(cuda, shape, a_t, b_t):
+    """The last two shapes have a long K: on SM pairs the accumulator is drained into fp32
+    registers every 256 concatenated K elements, on single SMs K is split into parts."""
     import torch
     from spar_b200 import ops
 
@@ -395,13 +398,14 @@ def test_gemm_column_partials(cuda, shape, epi, precision):
 
 @pytest.mark.parametrize("precision,accumulate", [(0, False), (1, False), (1, True)])
 def test_gemm_split_k_ragged_columns(cuda, precision, accumulate):
-    """A K-split product whose column count is not a multiple of 4, stored with a padded row
-    stride (the tied LM head: logits [tokens, vocab] in rows of the padded vocabulary). The
-    reduction writes every column up to n, the bias included, and none of the padding."""
+    """A product whose column count is not a multiple of 4, stored with a padded row stride (the
+    tied LM head: logits [tokens, vocab] in rows of the padded vocabulary), K split in 3xTF32.
+    Every column up to n is written, the bias included; the padding past the 16-byte chunk that
+    holds column n - 1 is untouched (tile stores write whole 16-byte chunks)."""
     import torch
     from spar_b200 import ops
 
-    m, n, k, ldc = 256, 301, 8192, 304
+    m, n, k, ldc = 256, 301, 8192, 320
     a, b, ref = _mats(m, n, k, False, True, seed=41)
     bias = np.random.default_rng(42).standard_normal(n).astype(np.float32)
     prev = np.random.default_rng(43).standard_normal((m, n)).astype(np.float32)
@@ -417,7 +421,7 @@ def test_gemm_split_k_ragged_columns(cuda, precision, accumulate):
     torch.cuda.synchronize()
     assert ops.gemm_error(0) == 0
     got = c.cpu().numpy()
-    assert np.isnan(got[:, n:]).all()  # padding untouched
+    assert np.isnan(got[:, (n + 3) // 4 * 4:]).all()  # padding untouched
     expect = ref + bias + (prev if accumulate else 0.0)
     assert not np.isnan(got[:, :n]).any()
     assert rel_l2(got[:, :n], expect) <= (1e-5 if precision else 2e-3)
