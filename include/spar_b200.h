@@ -534,7 +534,13 @@ struct SparCudaStatus spar_b200_comm_destroy(void* comm, int abort);
 /* asynchronous error or at the deadline it aborts the communicator (ncclCommAbort) and returns  */
 /* {3, ncclResult}. spar_b200_lm_train_step uses it for its final wait when a communicator is    */
 /* attached, so a rank whose peer left gets code 3 instead of hanging. The deadline is           */
-/* $SPAR_B200_COMM_TIMEOUT_S (default 600 s) or set per communicator.                            */
+/* $SPAR_B200_COMM_TIMEOUT_S (default 600 s) or set per communicator. The bound covers device   */
+/* work: the step's results are read into pinned host memory so no copy holds the host first.  */
+/* NCCL's host-side connection setup with the peers (inside the enqueue of a collective's first */
+/* use) is not covered; a peer lost before then is found between steps                          */
+/* (spar_b200.dp.Heartbeat). After code 3 the communicator is aborted (destroy it with abort =  */
+/* 1, which then only frees the handle), the trainer's captured steps are dropped without being */
+/* destroyed, and its sharded state holds only this rank's pieces: resume from a checkpoint.    */
 struct SparCudaStatus spar_b200_comm_set_timeout(void* comm, double seconds);
 struct SparCudaStatus spar_b200_comm_wait(void* comm, void* stream);
 

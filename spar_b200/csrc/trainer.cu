@@ -433,6 +433,15 @@ class LMTrainer {
     uint64_t launches;
   };
   std::map<uint64_t, StepGraph> graphs;
+  // A step's bounded wait aborted the communicator: the captured steps hold that communicator's
+  // collectives, whose resources the abort released, so they are dropped without being
+  // destroyed (destroying them would run the library's clean-up on the released communicator).
+  bool comm_aborted = false;
+  void drop_graphs() {
+    if (!comm_aborted)
+      for (auto& g : graphs) cudaGraphExecDestroy(g.second.exec);
+    graphs.clear();
+  }
   // SPAR_B200_GRAPHS=0 keeps every step eager (for per-kernel profiling of the step).
   bool graphs_enabled = !(getenv("SPAR_B200_GRAPHS") && getenv("SPAR_B200_GRAPHS")[0] == '0');
   uint64_t eager_steps = 0;
@@ -440,6 +449,15 @@ class LMTrainer {
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
   AdamWArgs* opt_args = nullptr;       // device
   AdamWArgs* opt_args_host = nullptr;  // pinned host
+  // Pinned host landing area of a step's results. A device-to-host copy into pageable memory
+  // returns only once the stream's earlier work has finished, which would hold the host inside
+  // the copy (before the communicator's bounded wait) when a peer never joins the step.
+  struct StepResults {
+    float sums[kMaxMicro];  // loss sum of each micro-step
+    double norm_state[2];
+    int32_t flags[2];
+  };
+  StepResults* results_host = nullptr;
   SparCudaStatus step_body(uint64_t micro_steps, float grad_scale, double lr, uint64_t step,
                            cudaStream_t s, bool device_args);
 
@@ -495,11 +513,12 @@ LMTrainer::~LMTrainer() {
   if (lane_fork) cudaEventDestroy(lane_fork);
   for (auto ev : lane_join)
     if (ev) cudaEventDestroy(ev);
-  for (auto& g : graphs) cudaGraphExecDestroy(g.second.exec);
+  drop_graphs();
   if (exec_stream) cudaStreamDestroy(exec_stream);
   if (ev_in) cudaEventDestroy(ev_in);
   if (ev_out) cudaEventDestroy(ev_out);
   if (opt_args_host) cudaFreeHost(opt_args_host);
+  if (results_host) cudaFreeHost(results_host);
   cudaFree(params);
   if (wround) cudaFree(wround);
   cudaFree(act_base);
@@ -712,6 +731,8 @@ SparCudaStatus LMTrainer::init(const SparB200LMConfig& c, int dev) {
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
   if (e == cudaSuccess)
     e = cudaMallocHost(reinterpret_cast<void**>(&opt_args_host), sizeof(AdamWArgs));
+  if (e == cudaSuccess)
+    e = cudaMallocHost(reinterpret_cast<void**>(&results_host), sizeof(StepResults));
   if (e == cudaSuccess) e = rope_table_launch(rope_tab, T, dh, c.rope_theta, 0, 0);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return runtime(e);
@@ -1553,28 +1574,31 @@ extern "C" SparCudaStatus spar_b200_lm_train_step(void* handle, const int32_t* i
 done:
   if (t->sharded && t->comm)  // only this rank's pieces were reduced and updated
     for (auto& st : t->stale) st = true;
-  float sums[LMTrainer::kMaxMicro];
-  double norm_state[2];
-  int32_t flags[2];
-  e = cudaMemcpyAsync(sums, t->loss_sums, micro_steps * sizeof(float), cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(norm_state, t->norm_state, 2 * sizeof(double), cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(flags, t->flags, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  LMTrainer::StepResults* r = t->results_host;
+  e = cudaMemcpyAsync(r->sums, t->loss_sums, micro_steps * sizeof(float), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(r->norm_state, t->norm_state, 2 * sizeof(double), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(r->flags, t->flags, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
   if (e != cudaSuccess) return runtime(e);
   if (t->comm) {
     // Bounded: a peer that left makes the step's collectives wait forever; the communicator is
     // then aborted and the step reports code 3 (the caller destroys the communicator).
     const SparCudaStatus w = comm_wait(t->comm, s);
+    if (w.code == 3) {
+      t->comm_aborted = true;
+      t->drop_graphs();
+    }
     if (w.code != 0) return w;
   } else if ((e = cudaStreamSynchronize(s)) != cudaSuccess) {
     return runtime(e);
   }
+  const double* norm_state = r->norm_state;
   double total = 0.0;
-  for (uint64_t m = 0; m < micro_steps; ++m) total += sums[m];
+  for (uint64_t m = 0; m < micro_steps; ++m) total += r->sums[m];
   if (loss_out) *loss_out = static_cast<float>(total / (rows / t->world));
   if (grad_norm_out) *grad_norm_out = std::sqrt(norm_state[0]);
   if (flags_out) {
-    flags_out[0] = flags[0];
-    flags_out[1] = flags[1];
+    flags_out[0] = r->flags[0];
+    flags_out[1] = r->flags[1];
   }
   // A GEMM or attention kernel of this step (on any rank) gave up one of its bounded waits: the
   // gradients are not trustworthy and AdamW updated nothing. The flags stay set until cleared
@@ -1595,8 +1619,7 @@ extern "C" SparCudaStatus spar_b200_lm_set_comm(void* handle, void* comm, int wo
   if (t->comm != comm && (t->stale[0] || t->stale[1] || t->stale[2] || t->stale[3])) return invalid();
   if (t->comm != comm && !t->graphs.empty()) {  // captured steps hold the old reductions
     cudaError_t e = cudaDeviceSynchronize();
-    for (auto& g : t->graphs) cudaGraphExecDestroy(g.second.exec);
-    t->graphs.clear();
+    t->drop_graphs();
     if (e != cudaSuccess) return runtime(e);
   }
   t->comm = comm;

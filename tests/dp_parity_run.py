@@ -25,14 +25,17 @@ if ROOT not in sys.path:
 GLOBAL_SEQS, ACCUM = 64, 4
 
 
-def config(world: int, precision: int):
+def config(world: int, precision: int, family: int = 0):
+    """family 0: the LayerNorm / GELU block; 1: Spar's own block (RMSNorm, SwiGLU, grouped-query
+    attention with two key / value heads, qk-norm)."""
     from spar_b200.lm import LMConfig
 
+    extra = dict(family=1, kv_heads=2, qk_norm=True) if family else {}
     return LMConfig(vocab=1000, dim=256, hidden=1024, layers=2, heads=4, seq=128,
-                    micro_batch=GLOBAL_SEQS // world // ACCUM, precision=precision)
+                    micro_batch=GLOBAL_SEQS // world // ACCUM, precision=precision, **extra)
 
 
-def run(out: str, precision: int, steps: int = 2) -> None:
+def run(out: str, precision: int, steps: int = 2, family: int = 0) -> None:
     import torch
 
     from spar_b200 import _lib
@@ -48,7 +51,7 @@ def run(out: str, precision: int, steps: int = 2) -> None:
         import torch.distributed as dist
 
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
-    cfg = config(world, precision)
+    cfg = config(world, precision, family)
     lm = DecoderLM(cfg, local)
     lm.init_normal(0x5EED0009, 0.02)
     lib = _lib.load()
@@ -95,5 +98,6 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
     ap.add_argument("--precision", type=int, default=0)
+    ap.add_argument("--family", type=int, default=0)
     a = ap.parse_args()
-    run(a.out, a.precision)
+    run(a.out, a.precision, family=a.family)

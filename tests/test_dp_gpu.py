@@ -4,12 +4,15 @@ tests/dp_parity_run.py runs two optimiser steps of the runtime under torchrun on
 bucket reduction inside the last micro-step's backward; with the sharded optimiser, the default,
 reduce-scatter + per-piece norm and AdamW + parameter all-gather; SPAR_B200_SHARD_OPT=0 the
 replicated all-reduce path) and in one process on one GPU (16-sequence micro-steps). The mean loss
-of the global batch, the gradient norm of each step, and after step 2 every gradient and first
-moment must agree within the parity bars: relative L2 <= 1e-5 per tensor in 3xTF32; in TF32 (the
-two runs use different micro-batch sizes, hence different tile plans and TF32 rounding) <= 2e-3
-overall and <= 1e-2 per tensor. Parameter updates are compared where the first moment is well
-conditioned (|m| >= 5 % of the tensor's RMS; AdamW's update lr * m / sqrt(v) only tests a sign
-where m cancels to near zero).
+of the global batch, the gradient norm of each step, every parameter after step 2 (relative L2
+<= 1e-5 in 3xTF32, <= 2e-3 in TF32), and every gradient and first moment must agree. The two runs
+use different micro-batch sizes, hence different tile plans and rounding; each is within the step
+parity bars of the float64 oracle, so by the triangle inequality they agree within twice those
+bars per tensor: 2e-5 in 3xTF32 (per-run 1e-5), 1e-2 for the LayerNorm / GELU block in TF32, 2e-2
+for Spar's own block in TF32 (its per-run bar against the oracle is 1e-2: grouped key / value heads
+sum several heads' TF32 products); all tensors together within the per-run bars (1e-5, 2e-3).
+Parameter updates are compared where the first moment is well conditioned (|m| >= 5 % of the
+tensor's RMS; AdamW's update lr * m / sqrt(v) only tests a sign where m cancels to near zero).
 
 Needs two GPUs (skipped otherwise); run with `gpurun --gpus 2`.
 """
@@ -33,9 +36,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _launch(out, precision, world, env):
+def _launch(out, precision, world, env, family=0):
     cmd = [sys.executable, os.path.join(HERE, "dp_parity_run.py"), "--out", out,
-           "--precision", str(precision)]
+           "--precision", str(precision), "--family", str(family)]
     if world > 1:
         cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
                "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
@@ -45,21 +48,27 @@ def _launch(out, precision, world, env):
     return dict(np.load(out))
 
 
-@pytest.mark.parametrize("shard", ["1", "0"])
+@pytest.mark.parametrize("family,shard", [(0, "1"), (0, "0"), (1, "1")])
 @pytest.mark.parametrize("precision", [1, 0])
-def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, shard):
+def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, family, shard):
+    """family 1 is Spar's own block (RMSNorm, SwiGLU, GQA, qk-norm) on its sharded path."""
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     env = dict(os.environ, SPAR_B200_SHARD_OPT=shard, NCCL_NVLS_ENABLE="0")
-    one = _launch(str(tmp_path / "one.npz"), precision, 1, env)
-    two = _launch(str(tmp_path / "two.npz"), precision, 2, env)
+    one = _launch(str(tmp_path / "one.npz"), precision, 1, env, family)
+    two = _launch(str(tmp_path / "two.npz"), precision, 2, env, family)
     assert int(two["world"]) == 2
-    tol_all, tol_each = (1e-5, 1e-5) if precision == 1 else (2e-3, 1e-2)
+    if precision == 1:
+        tol_all, tol_each = 1e-5, 2e-5
+    else:
+        tol_all, tol_each = 2e-3, (2e-2 if family else 1e-2)
     np.testing.assert_allclose(two["losses"], one["losses"], rtol=tol_all)
     np.testing.assert_allclose(two["norms"], one["norms"], rtol=tol_all)
     names = sorted(k.split(":", 1)[1] for k in one if k.startswith("param:"))
+    for n in names:
+        assert rel_l2(two[f"param:{n}"], one[f"param:{n}"]) <= tol_all, ("param", n)
     for kind in ("grad", "m"):
         flat1 = np.concatenate([one[f"{kind}:{n}"].ravel() for n in names])
         flat2 = np.concatenate([two[f"{kind}:{n}"].ravel() for n in names])
@@ -71,7 +80,7 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, shard):
     sys.path.insert(0, HERE)
     import dp_parity_run
 
-    lm = DecoderLM(dp_parity_run.config(1, precision), 0)
+    lm = DecoderLM(dp_parity_run.config(1, precision, family), 0)
     lm.init_normal(0x5EED0009, 0.02)
     init = lm.state_dict()
     lm.close()
