@@ -9,9 +9,12 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <thread>
 
@@ -72,7 +75,13 @@ struct Comm {
   int rank = 0, world = 1, device = 0;
   double timeout_s = default_timeout();
   bool aborted = false;
+  // The abort runs on its own thread (see comm_wait); set when ncclCommAbort has returned.
+  // While it has not, the handle is never freed (the thread still uses it).
+  std::shared_ptr<std::atomic<bool>> abort_done;
 };
+
+// Seconds comm_wait waits for ncclCommAbort to return before reporting the failure anyway.
+constexpr double kAbortWaitS = 20.0;
 
 // Status for a failed NCCL call: code 3, the ncclResult_t in cuda_error.
 SparCudaStatus nccl_status(ncclResult_t r) { return {r == ncclSuccess ? 0 : 3, static_cast<int>(r)}; }
@@ -119,6 +128,12 @@ cudaError_t comm_all_gather(void* comm, float* data, uint64_t shard, cudaStream_
 // communicator is unusable afterwards. The communicator stays blocking (collective enqueues never
 // return ncclInProgress), which keeps the step's collectives capturable in a CUDA graph on the
 // calling thread; this wait is where a hang would otherwise show.
+// SPAR_B200_COMM_TRACE=1: the failure path reports its stages on stderr.
+bool comm_trace() {
+  static const bool on = getenv("SPAR_B200_COMM_TRACE") && getenv("SPAR_B200_COMM_TRACE")[0] == '1';
+  return on;
+}
+
 SparCudaStatus comm_wait(void* comm, cudaStream_t stream) {
   Comm* c = static_cast<Comm*>(comm);
   if (!c) return {1, static_cast<int>(cudaErrorInvalidValue)};
@@ -137,14 +152,45 @@ SparCudaStatus comm_wait(void* comm, cudaStream_t stream) {
     const double waited =
         std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
     if ((async != ncclSuccess && async != ncclInProgress) || waited > c->timeout_s) {
-      api().abort(c->nccl);  // its kernels see the abort flag and return
-      c->nccl = nullptr;
+      if (comm_trace())
+        fprintf(stderr, "spar_b200 comm_wait: rank %d gives up after %.1f s (async %d), aborting\n",
+                c->rank, waited, static_cast<int>(async));
+      // ncclCommAbort stops the communicator's kernels (they see its abort flag and return), but
+      // it has been seen to block the calling thread while the step's captured collectives were
+      // in flight. It runs on a detached thread, waited for at most kAbortWaitS, so the step
+      // reports the failure within its bound either way.
       c->aborted = true;
+      c->abort_done = std::make_shared<std::atomic<bool>>(false);
+      {
+        ncclComm_t nc = c->nccl;
+        auto done = c->abort_done;
+        std::thread([nc, done] {
+          api().abort(nc);
+          done->store(true);
+        }).detach();
+      }
+      c->nccl = nullptr;
       const auto stop = std::chrono::steady_clock::now();
-      while (cudaStreamQuery(stream) == cudaErrorNotReady &&
-             std::chrono::steady_clock::now() - stop < std::chrono::seconds(30))
+      while (!c->abort_done->load() &&
+             std::chrono::steady_clock::now() - stop < std::chrono::duration<double>(kAbortWaitS))
         std::this_thread::sleep_for(std::chrono::milliseconds(1));
+      const bool returned = c->abort_done->load();
+      if (comm_trace())
+        fprintf(stderr, "spar_b200 comm_wait: rank %d abort %s\n", c->rank,
+                returned ? "returned" : "still running (the step's streams may not drain)");
+      cudaError_t q2 = cudaErrorNotReady;
+      if (returned) {
+        const auto drain = std::chrono::steady_clock::now();
+        while ((q2 = cudaStreamQuery(stream)) == cudaErrorNotReady &&
+               std::chrono::steady_clock::now() - drain < std::chrono::seconds(30))
+          std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        if (comm_trace())
+          fprintf(stderr, "spar_b200 comm_wait: rank %d stream after abort: %s\n", c->rank,
+                  q2 == cudaSuccess ? "drained" : cudaGetErrorString(q2));
+      }
       cudaGetLastError();
+      // ncclInProgress: the abort (or the drain) had not finished when the wait gave up.
+      if (!returned || q2 != cudaSuccess) return {3, static_cast<int>(ncclInProgress)};
       return {3, static_cast<int>(async != ncclSuccess ? async : ncclRemoteError)};
     }
     std::this_thread::sleep_for(sleep_us);
@@ -224,7 +270,7 @@ extern "C" SparCudaStatus spar_b200_comm_destroy(void* comm, int abort) {
   const ncclResult_t r = c->aborted ? ncclSuccess
                          : abort    ? api().abort(c->nccl)
                                     : api().destroy(c->nccl);
-  delete c;
+  delete c;  // the abort thread, if any, holds its own references
   return nccl_status(r);
 }
 

@@ -1,12 +1,15 @@
 """Worker for tests/test_dp_gpu.py: one process per GPU under torchrun.
 
 Two optimiser steps of the training runtime over a 64-sequence global batch, split across the
-ranks (spar_b200.data.rank_share: rank r takes sequences [r*per, (r+1)*per), four accumulation
-micro-steps), gradients reduced over NCCL by the runtime itself (bucket all-reduce, or
+ranks (spar_b200.data.rank_share: rank r takes sequences [r*per, (r+1)*per) as micro-steps of 8
+sequences), gradients reduced over NCCL by the runtime itself (bucket all-reduce, or
 reduce-scatter + per-piece AdamW + parameter all-gather with the sharded optimiser). Afterwards
 every arena is gathered (a collective) and rank 0 writes parameters, gradients and first
 moments, plus each step's mean loss over the global batch and norm, to --out. Run with world
-size 1 (no torchrun) it is the single-GPU run of the same global batch (16-sequence micro-steps).
+size 1 (no torchrun) it is the single-GPU run of the same global batch: the same 8-sequence
+micro-steps (eight of them), so every micro-step computes exactly what the matching micro-step of
+a rank computes, and the runs differ only in how the micro-steps' gradients are summed (in one
+arena, or per rank and then across ranks) and in the data-parallel optimiser path.
 """
 from __future__ import annotations
 
@@ -22,7 +25,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-GLOBAL_SEQS, ACCUM = 64, 4
+GLOBAL_SEQS, MICRO = 64, 8
+
+
+def accum(world: int) -> int:
+    return GLOBAL_SEQS // world // MICRO
 
 
 def config(world: int, precision: int, family: int = 0):
@@ -32,7 +39,7 @@ def config(world: int, precision: int, family: int = 0):
 
     extra = dict(family=1, kv_heads=2, qk_norm=True) if family else {}
     return LMConfig(vocab=1000, dim=256, hidden=1024, layers=2, heads=4, seq=128,
-                    micro_batch=GLOBAL_SEQS // world // ACCUM, precision=precision, **extra)
+                    micro_batch=MICRO, precision=precision, **extra)
 
 
 def run(out: str, precision: int, steps: int = 2, family: int = 0) -> None:
@@ -69,7 +76,8 @@ def run(out: str, precision: int, steps: int = 2, family: int = 0) -> None:
         lm.attach_comm(comm, world)
     losses, norms = [], []
     for step in range(1, steps + 1):
-        ids = rank_share(0x5EED1009 + step, GLOBAL_SEQS, ACCUM, cfg.seq, cfg.vocab, rank, world)
+        ids = rank_share(0x5EED1009 + step, GLOBAL_SEQS, accum(world), cfg.seq, cfg.vocab, rank,
+                         world)
         loss, norm, flags = lm.train_step(ids, 3e-4, step=step)
         if flags != (0, 0):
             raise RuntimeError(f"rank {rank} step {step}: flags {flags}")

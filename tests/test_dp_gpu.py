@@ -3,16 +3,16 @@
 tests/dp_parity_run.py runs two optimiser steps of the runtime under torchrun on 2 GPUs (NCCL
 bucket reduction inside the last micro-step's backward; with the sharded optimiser, the default,
 reduce-scatter + per-piece norm and AdamW + parameter all-gather; SPAR_B200_SHARD_OPT=0 the
-replicated all-reduce path) and in one process on one GPU (16-sequence micro-steps). The mean loss
-of the global batch, the gradient norm of each step, every parameter after step 2 (relative L2
-<= 1e-5 in 3xTF32, <= 2e-3 in TF32), and every gradient and first moment must agree. The two runs
-use different micro-batch sizes, hence different tile plans and rounding; each is within the step
-parity bars of the float64 oracle, so by the triangle inequality they agree within twice those
-bars per tensor: 2e-5 in 3xTF32 (per-run 1e-5), 1e-2 for the LayerNorm / GELU block in TF32, 2e-2
-for Spar's own block in TF32 (its per-run bar against the oracle is 1e-2: grouped key / value heads
-sum several heads' TF32 products); all tensors together within the per-run bars (1e-5, 2e-3).
-Parameter updates are compared where the first moment is well conditioned (|m| >= 5 % of the
-tensor's RMS; AdamW's update lr * m / sqrt(v) only tests a sign where m cancels to near zero).
+replicated all-reduce path) and in one process on one GPU. Both use 8-sequence micro-steps, so each
+micro-step's gradients are the same computation on both sides (same tile plans, deterministic
+kernels) and what the comparison tests is the data-parallel path itself: the summation of the
+micro-steps' gradients across ranks, the sharded or replicated norm and AdamW, the parameter
+all-gather. The runs differ only in the order of fp32 gradient sums, so the bar is 1e-5 relative
+L2 in either precision: the mean loss and the gradient norm of each step, all parameters after
+step 2, and every tensor's gradient and first moment. Parameter updates are compared where the
+first moment is well conditioned (|m| >= 5 % of the tensor's RMS; AdamW's update lr * m / sqrt(v)
+only tests a sign where m cancels to near zero, e.g. the key-projection bias, whose exact
+gradient is zero because softmax ignores a per-row shift of the scores).
 
 Needs two GPUs (skipped otherwise); run with `gpurun --gpus 2`.
 """
@@ -60,21 +60,21 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, family, shard):
     one = _launch(str(tmp_path / "one.npz"), precision, 1, env, family)
     two = _launch(str(tmp_path / "two.npz"), precision, 2, env, family)
     assert int(two["world"]) == 2
-    if precision == 1:
-        tol_all, tol_each = 1e-5, 2e-5
-    else:
-        tol_all, tol_each = 2e-3, (2e-2 if family else 1e-2)
+    tol_all = tol_each = 1e-5
     np.testing.assert_allclose(two["losses"], one["losses"], rtol=tol_all)
     np.testing.assert_allclose(two["norms"], one["norms"], rtol=tol_all)
     names = sorted(k.split(":", 1)[1] for k in one if k.startswith("param:"))
-    for n in names:
-        assert rel_l2(two[f"param:{n}"], one[f"param:{n}"]) <= tol_all, ("param", n)
+    p1 = np.concatenate([one[f"param:{n}"].ravel() for n in names])
+    p2 = np.concatenate([two[f"param:{n}"].ravel() for n in names])
+    assert rel_l2(p2, p1) <= tol_all, "parameters"
     for kind in ("grad", "m"):
         flat1 = np.concatenate([one[f"{kind}:{n}"].ravel() for n in names])
         flat2 = np.concatenate([two[f"{kind}:{n}"].ravel() for n in names])
-        assert rel_l2(flat2, flat1) <= tol_all, kind
-        for n in names:
-            assert rel_l2(two[f"{kind}:{n}"], one[f"{kind}:{n}"]) <= tol_each, (kind, n)
+        worst = sorted(((rel_l2(two[f"{kind}:{n}"], one[f"{kind}:{n}"]), n) for n in names),
+                       reverse=True)[:6]
+        report = f"{kind}: " + ", ".join(f"{n} {e:.2e}" for e, n in worst)
+        assert rel_l2(flat2, flat1) <= tol_all, report
+        assert worst[0][0] <= tol_each, report
     from spar_b200.lm import DecoderLM
 
     sys.path.insert(0, HERE)
@@ -92,7 +92,8 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, family, shard):
         assert rel_l2(d2[mask], d1[mask]) <= tol_each, n
 
 
-def test_peer_missing_a_step_gets_code_3(cuda, tmp_path):
+@pytest.mark.parametrize("graphs", ["1", "0"])
+def test_peer_missing_a_step_gets_code_3(cuda, tmp_path, graphs):
     """A peer that stays alive but skips a step (after two steps together): the other rank's
     collectives can never complete; the runtime's bounded wait (5 s here) aborts the communicator
     and the step returns code 3, the device context stays usable. Two GPUs, NVLS off."""
@@ -101,12 +102,15 @@ def test_peer_missing_a_step_gets_code_3(cuda, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     out = str(tmp_path / "seen.txt")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SPAR_B200_COMM_TRACE="1",
+               SPAR_B200_GRAPHS=graphs)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port",
            str(_free_port()), os.path.join(HERE, "dp_failure_run.py"), "--out", out]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
-    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    marks = open(out + ".progress").read() if os.path.exists(out + ".progress") else ""
+    trace = "\n".join(l for l in r.stderr.splitlines() if "spar_b200 comm_wait" in l)
+    assert r.returncode == 0, marks + trace + r.stdout[-2000:] + r.stderr[-2000:]
     seen = open(out).read()
     assert seen.startswith("code 3 after"), seen
     waited = float(seen.split("after ")[1].split("s")[0])
