@@ -541,6 +541,11 @@ struct SparCudaStatus spar_b200_comm_destroy(void* comm, int abort);
 /* (spar_b200.dp.Heartbeat). After code 3 the communicator is aborted (destroy it with abort =  */
 /* 1, which then only frees the handle), the trainer's captured steps are dropped without being */
 /* destroyed, and its sharded state holds only this rank's pieces: resume from a checkpoint.    */
+/* ncclCommAbort does not return while CUDA graphs holding the communicator's collectives are   */
+/* in flight or alive (seen on this build's NCCL 2.28): the bounded wait therefore runs it on a */
+/* detached thread and waits at most 20 s (then cuda_error = ncclInProgress: the step's streams */
+/* may still hold the aborted work; end the process), and a rank tearing down normally destroys */
+/* the trainer (spar_b200_lm_destroy, which releases its graphs) before the communicator.       */
 struct SparCudaStatus spar_b200_comm_set_timeout(void* comm, double seconds);
 struct SparCudaStatus spar_b200_comm_wait(void* comm, void* stream);
 

@@ -66,9 +66,11 @@ def main(out: str) -> None:
     dist.barrier()  # steps 1 and 2 done everywhere
     progress(out, f"rank {rank}: steps 1 and 2 done")
     if rank == world - 1:
-        store.wait(["rank0_done"], datetime.timedelta(seconds=120))  # alive, but skips step 2
-        lib.spar_b200_comm_destroy(comm, 1)
+        store.wait(["rank0_done"], datetime.timedelta(seconds=120))  # alive, but skips step 3
+        # The trainer (its captured steps hold the communicator's collectives) goes first: an
+        # NCCL abort with such graphs still alive did not return.
         lm.close()
+        lib.spar_b200_comm_destroy(comm, 1)
         return
     start = time.monotonic()
     progress(out, "rank 0: step 3 starts")

@@ -75,6 +75,7 @@ def run(out: str, precision: int, steps: int = 2, family: int = 0) -> None:
                                                                   ctypes.byref(comm)))
         lm.attach_comm(comm, world)
     losses, norms = [], []
+    state = {}
     for step in range(1, steps + 1):
         ids = rank_share(0x5EED1009 + step, GLOBAL_SEQS, accum(world), cfg.seq, cfg.vocab, rank,
                          world)
@@ -83,10 +84,16 @@ def run(out: str, precision: int, steps: int = 2, family: int = 0) -> None:
             raise RuntimeError(f"rank {rank} step {step}: flags {flags}")
         losses.append(loss)
         norms.append(norm)
+        if step == 1:  # step 1's gradients and update, before they shape step 2's inputs
+            if comm is not None:
+                for which in ("param", "grad"):
+                    lm.gather(which)
+            state["param1"] = lm.state_dict("param")
+            state["grad1"] = lm.state_dict("grad")
     if comm is not None:
         for which in ("param", "grad", "m"):
             lm.gather(which)
-    state = {w: lm.state_dict(w) for w in ("param", "grad", "m")}
+    state.update({w: lm.state_dict(w) for w in ("param", "grad", "m")})
     if world > 1:  # each rank reports the mean loss over its own (equal) share
         all_losses = [None] * world
         dist.all_gather_object(all_losses, losses)

@@ -7,12 +7,16 @@ replicated all-reduce path) and in one process on one GPU. Both use 8-sequence m
 micro-step's gradients are the same computation on both sides (same tile plans, deterministic
 kernels) and what the comparison tests is the data-parallel path itself: the summation of the
 micro-steps' gradients across ranks, the sharded or replicated norm and AdamW, the parameter
-all-gather. The runs differ only in the order of fp32 gradient sums, so the bar is 1e-5 relative
-L2 in either precision: the mean loss and the gradient norm of each step, all parameters after
-step 2, and every tensor's gradient and first moment. Parameter updates are compared where the
-first moment is well conditioned (|m| >= 5 % of the tensor's RMS; AdamW's update lr * m / sqrt(v)
-only tests a sign where m cancels to near zero, e.g. the key-projection bias, whose exact
-gradient is zero because softmax ignores a per-row shift of the scores).
+all-gather. Step 1 differs only in the order of fp32 gradient sums, so its gradients (every
+tensor) and its parameter update (where the gradient is well conditioned, |g| >= 5 % of the
+tensor's RMS: AdamW's first update is lr * g / (|g| + eps), only a sign where g is rounding noise)
+must agree within 1e-5 relative L2, as must both steps' mean loss and gradient norm and all
+parameters after step 2. Step 2's inputs differ by more than rounding: the key-projection bias
+has an exactly zero gradient (softmax ignores a per-row shift of the scores), so its first update
+follows the sign of rounding noise, which the two summation orders draw differently, and TF32
+products resolve the resulting differences in the keys. Step 2's gradients and first moments are
+therefore held to the step-parity bars of each precision: 1e-5 per tensor in 3xTF32, 2e-3 in TF32
+(2e-2 per tensor for Spar's own block, as against the oracle).
 
 Needs two GPUs (skipped otherwise); run with `gpurun --gpus 2`.
 """
@@ -60,21 +64,13 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, family, shard):
     one = _launch(str(tmp_path / "one.npz"), precision, 1, env, family)
     two = _launch(str(tmp_path / "two.npz"), precision, 2, env, family)
     assert int(two["world"]) == 2
-    tol_all = tol_each = 1e-5
+    tol_all = 1e-5
     np.testing.assert_allclose(two["losses"], one["losses"], rtol=tol_all)
     np.testing.assert_allclose(two["norms"], one["norms"], rtol=tol_all)
     names = sorted(k.split(":", 1)[1] for k in one if k.startswith("param:"))
     p1 = np.concatenate([one[f"param:{n}"].ravel() for n in names])
     p2 = np.concatenate([two[f"param:{n}"].ravel() for n in names])
     assert rel_l2(p2, p1) <= tol_all, "parameters"
-    for kind in ("grad", "m"):
-        flat1 = np.concatenate([one[f"{kind}:{n}"].ravel() for n in names])
-        flat2 = np.concatenate([two[f"{kind}:{n}"].ravel() for n in names])
-        worst = sorted(((rel_l2(two[f"{kind}:{n}"], one[f"{kind}:{n}"]), n) for n in names),
-                       reverse=True)[:6]
-        report = f"{kind}: " + ", ".join(f"{n} {e:.2e}" for e, n in worst)
-        assert rel_l2(flat2, flat1) <= tol_all, report
-        assert worst[0][0] <= tol_each, report
     from spar_b200.lm import DecoderLM
 
     sys.path.insert(0, HERE)
@@ -84,6 +80,29 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, family, shard):
     lm.init_normal(0x5EED0009, 0.02)
     init = lm.state_dict()
     lm.close()
+    # Step 1: gradients of every tensor, and the update where the gradient is well conditioned.
+    worst = sorted(((rel_l2(two[f"grad1:{n}"], one[f"grad1:{n}"]), n) for n in names),
+                   reverse=True)[:6]
+    assert worst[0][0] <= tol_all, "step 1 grad: " + ", ".join(f"{n} {e:.2e}" for e, n in worst)
+    for n in names:
+        g = one[f"grad1:{n}"].astype(np.float64)
+        mask = np.abs(g) >= 0.05 * np.sqrt(np.mean(g * g))
+        d1 = one[f"param1:{n}"].astype(np.float64) - init[n]
+        d2 = two[f"param1:{n}"].astype(np.float64) - init[n]
+        assert rel_l2(d2[mask], d1[mask]) <= tol_all, ("step 1 update", n)
+    # Step 2: the precision's step-parity bars.
+    if precision == 1:
+        tol_all2, tol_each = 1e-5, 1e-5
+    else:
+        tol_all2, tol_each = 2e-3, (2e-2 if family else 2e-3)
+    for kind in ("grad", "m"):
+        flat1 = np.concatenate([one[f"{kind}:{n}"].ravel() for n in names])
+        flat2 = np.concatenate([two[f"{kind}:{n}"].ravel() for n in names])
+        worst = sorted(((rel_l2(two[f"{kind}:{n}"], one[f"{kind}:{n}"]), n) for n in names),
+                       reverse=True)[:6]
+        report = f"{kind}: " + ", ".join(f"{n} {e:.2e}" for e, n in worst)
+        assert rel_l2(flat2, flat1) <= tol_all2, report
+        assert worst[0][0] <= tol_each, report
     for n in names:
         m = one[f"m:{n}"].astype(np.float64)
         mask = np.abs(m) >= 0.05 * np.sqrt(np.mean(m * m))
