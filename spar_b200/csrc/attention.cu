@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   // many jobs (several uses of a buffer by the other tile) past their previous job, so a
   // barrier shared by both tiles could complete two phases between their waits.
   uint64_t* s_full = bars + 10;
-  uint64_t* s_used = bars + 16;    // [3] the P V product has read the buffer
+  // bars + 16 .. 18: unused (buffer reuse needs no barrier, see the MMA issuer)
   uint64_t* p_full = bars + 19;    // [3] probabilities in buffer
   uint64_t* drain = bars + 22;
   uint64_t* k_full = bars + 23;                      // [kKStages]
@@ -395,7 +395,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     for (uint32_t b = 0; b < kSBufs; ++b) {
       tc::mbar_init(s_full + b, 1);
       tc::mbar_init(s_full + kSBufs + b, 1);
-      tc::mbar_init(s_used + b, 1);
       tc::mbar_init(p_full + b, 4);
     }
     tc::mbar_init(drain, 1);
@@ -505,14 +504,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         int k_ready = -1, v_ready = -1;  // key tiles whose K / V stage has been waited for
         uint32_t is = 0;                 // S jobs issued (P V jobs: ip)
         for (uint32_t ip = 0; ip < njobs && ok; ++ip) {
-          // S jobs up to three ahead: job g reuses the buffer of job g - 3, so that job's P V
-          // product must have read it.
+          // S jobs up to three ahead: job g reuses the buffer of job g - 3, whose P V product
+          // this thread issued before (S(g) is issued once ip > g - 3). The tensor core runs
+          // one thread's tcgen05.mma operations in issue order, so that product reads P before
+          // S(g) overwrites it: no wait for its completion (the softmax warps finished with the
+          // buffer before p_full, which the P V product waited for).
           while (is < njobs && is < ip + kSBufs && ok) {
             uint32_t x, j;
             job_of(it, is, x, j);
             const uint32_t g = gbase + is, buf = g % kSBufs;
-            if (g >= kSBufs && !(ok = wait_or_abort(s_used + buf, (g / kSBufs - 1) & 1, abort_flag)))
-              break;
             const uint32_t kst = (kn + j) % L::kKStages;
             if (static_cast<int>(j) > k_ready) {
               if (!(ok = wait_or_abort(k_full + kst, ((kn + j) / L::kKStages) & 1, abort_flag))) break;
@@ -545,7 +545,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           for (int ks = 0; ks < 16; ++ks)
             tc::mma_tf32_ts(tmem + 384 + x * 64, tmem + buf * 128 + ks * 8,
                             mnmajor_desc<DH>(v_addr + vst * L::kTile, ks), idesc_o, (j | ks) != 0);
-          tc::mma_commit(s_used + buf);
           tc::mma_commit(o_pv + x);
           if (j + 1 == n[x]) {
             tc::mma_commit(o_full + x);
@@ -704,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
   uint64_t* kv_full = bars + 2;   // [kStages]
   uint64_t* kv_empty = bars + 5;  // [kStages]
   uint64_t* s_full = bars + 8;    // [2]
-  uint64_t* s_empty = bars + 10;  // [2]
+  // bars + 10, 11: unused (S / dP buffer reuse needs no barrier, see issue_s)
   uint64_t* ds_full = bars + 12;  // [2] dS ready, alternating by step (see p_full above)
   uint64_t* acc_full = bars + 14;
   uint64_t* acc_empty = bars + 15;
@@ -722,7 +721,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(s_full + i, 1);
-      tc::mbar_init(s_empty + i, 1);  // freed by the MMA once dQ has read dS (aliasing S)
     }
     tc::mbar_init(ds_full, kSoftWarps);
     tc::mbar_init(ds_full + 1, kSoftWarps);
@@ -803,10 +801,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
       uint32_t n = 0, sn = 0, dn = 0, item = 0;
       bool ok = true;
       // kv load number kn sits in stage kn % kStages, phase (kn / kStages) & 1.
+      // Buffer sb was last read by the dQ product of two steps back (dS over S), which this
+      // thread issued before; one thread's tcgen05.mma operations run in issue order, so S and
+      // dP can be issued into it without waiting for that product (the softmax warps were done
+      // with it before ds_full, which the dQ product waited for).
       auto issue_s = [&](uint32_t kn) -> bool {  // S and dP for kv load number kn
         const uint32_t st = kn % L::kStages, sb = sn & 1;
         if (!wait_or_abort(kv_full + st, (kn / L::kStages) & 1, abort_flag)) return false;
-        if (!wait_or_abort(s_empty + sb, ((sn >> 1) & 1) ^ 1, abort_flag)) return false;
         tc::tc_fence_after();
         const uint32_t s = kv_addr + st * L::kStage;
 #pragma unroll
@@ -844,7 +845,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_q_kernel(const __grid_co
           for (int ks = 0; ks < 8; ++ks)
             tc::mma_tf32_ts(tmem + 256, tmem + sb * 64 + ks * 8, mnmajor_desc<DH>(kmn, ks),
                             idesc_q, (j | ks) != 0);
-          tc::mma_commit(s_empty + sb);
           tc::mma_commit(kv_empty + st);
         }
         n = n0 + nkv;
@@ -978,7 +978,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
   uint64_t* kq_full = bars + 2;   // [2]
   uint64_t* kq_empty = bars + 4;  // [2]
   uint64_t* s_full = bars + 6;    // [2]
-  uint64_t* s_empty = bars + 8;   // [2]
+  // bars + 8, 9: unused (S^T / dP^T buffer reuse needs no barrier, see issue_s)
   uint64_t* mn_full = bars + 10;  // [2]
   uint64_t* mn_empty = bars + 12;  // [2]
   uint64_t* pd_full = bars + 14;  // [2] P^T / dS^T ready, alternating by step (see p_full above)
@@ -997,7 +997,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       tc::mbar_init(kq_full + i, 1);
       tc::mbar_init(kq_empty + i, 1);
       tc::mbar_init(s_full + i, 1);
-      tc::mbar_init(s_empty + i, 1);  // freed by the MMA once dV / dK have read P^T / dS^T
       tc::mbar_init(mn_full + i, 1);
       tc::mbar_init(mn_empty + i, 1);
     }
@@ -1088,10 +1087,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
       const uint32_t mn_addr = tc::smem_u32(smem + L::kMN);
       uint32_t n = 0, sn = 0, item = 0;
       bool ok = true;
+      // Buffer sb was last read by the dV / dK products of two steps back (P^T, dS^T over S^T,
+      // dP^T), issued before by this thread; in-order tcgen05.mma execution makes the wait for
+      // their completion unnecessary (the softmax warps were done before pd_full).
       auto issue_s = [&](uint32_t qn) -> bool {  // S^T and dP^T for query load number qn
         const uint32_t st = qn & 1, sb = sn & 1;
         if (!wait_or_abort(kq_full + st, (qn >> 1) & 1, abort_flag)) return false;
-        if (!wait_or_abort(s_empty + sb, ((sn >> 1) & 1) ^ 1, abort_flag)) return false;
         tc::tc_fence_after();
         const uint32_t s = kq_addr + st * 2 * L::kTile64;
 #pragma unroll
@@ -1133,7 +1134,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_kv_kernel(const __grid_c
             tc::mma_tf32_ts(tmem + 256 + DH, tmem + 128 + sb * 64 + ks * 8,
                             mnmajor_desc<DH>(m, ks), idesc_g, (i | ks) != 0);
           }
-          tc::mma_commit(s_empty + sb);
           tc::mma_commit(mn_empty + st);
         }
         n = n0 + steps;
