@@ -4,8 +4,9 @@ Two optimiser steps of the training runtime over a 64-sequence global batch, spl
 ranks (spar_b200.data.rank_share: rank r takes sequences [r*per, (r+1)*per) as micro-steps of 8
 sequences), gradients reduced over NCCL by the runtime itself (bucket all-reduce, or
 reduce-scatter + per-piece AdamW + parameter all-gather with the sharded optimiser). Afterwards
-every arena is gathered (a collective) and rank 0 writes parameters, gradients and first
-moments, plus each step's mean loss over the global batch and norm, to --out. Run with world
+every arena is gathered (a collective) and rank 0 writes parameters, gradients and both moments
+(and step 1's gradients and parameters), plus each step's mean loss over the global batch and
+norm, to --out. Run with world
 size 1 (no torchrun) it is the single-GPU run of the same global batch: the same 8-sequence
 micro-steps (eight of them), so every micro-step computes exactly what the matching micro-step of
 a rank computes, and the runs differ only in how the micro-steps' gradients are summed (in one
@@ -91,9 +92,9 @@ def run(out: str, precision: int, steps: int = 2, family: int = 0) -> None:
             state["param1"] = lm.state_dict("param")
             state["grad1"] = lm.state_dict("grad")
     if comm is not None:
-        for which in ("param", "grad", "m"):
+        for which in ("param", "grad", "m", "v"):
             lm.gather(which)
-    state.update({w: lm.state_dict(w) for w in ("param", "grad", "m")})
+    state.update({w: lm.state_dict(w) for w in ("param", "grad", "m", "v")})
     if world > 1:  # each rank reports the mean loss over its own (equal) share
         all_losses = [None] * world
         dist.all_gather_object(all_losses, losses)

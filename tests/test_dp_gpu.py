@@ -14,9 +14,11 @@ must agree within 1e-5 relative L2, as must both steps' mean loss and gradient n
 parameters after step 2. Step 2's inputs differ by more than rounding: the key-projection bias
 has an exactly zero gradient (softmax ignores a per-row shift of the scores), so its first update
 follows the sign of rounding noise, which the two summation orders draw differently, and TF32
-products resolve the resulting differences in the keys. Step 2's gradients and first moments are
+products resolve the resulting differences in the keys. Step 2's gradients and both moments are
 therefore held to the step-parity bars of each precision: 1e-5 per tensor in 3xTF32, 2e-3 in TF32
-(2e-2 per tensor for Spar's own block, as against the oracle).
+(2e-2 per tensor for Spar's own block, as against the oracle). With step 1's parameters, both
+moments and the final parameters checked, step 2's update is determined; its quotient
+m / sqrt(v) is not compared element by element (it amplifies small first moments).
 
 Needs two GPUs (skipped otherwise); run with `gpurun --gpus 2`.
 """
@@ -95,7 +97,7 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, family, shard):
         tol_all2, tol_each = 1e-5, 1e-5
     else:
         tol_all2, tol_each = 2e-3, (2e-2 if family else 2e-3)
-    for kind in ("grad", "m"):
+    for kind in ("grad", "m", "v"):
         flat1 = np.concatenate([one[f"{kind}:{n}"].ravel() for n in names])
         flat2 = np.concatenate([two[f"{kind}:{n}"].ravel() for n in names])
         worst = sorted(((rel_l2(two[f"{kind}:{n}"], one[f"{kind}:{n}"]), n) for n in names),
@@ -103,12 +105,6 @@ def test_two_gpus_match_one_gpu(cuda, tmp_path, precision, family, shard):
         report = f"{kind}: " + ", ".join(f"{n} {e:.2e}" for e, n in worst)
         assert rel_l2(flat2, flat1) <= tol_all2, report
         assert worst[0][0] <= tol_each, report
-    for n in names:
-        m = one[f"m:{n}"].astype(np.float64)
-        mask = np.abs(m) >= 0.05 * np.sqrt(np.mean(m * m))
-        d1 = one[f"param:{n}"].astype(np.float64) - init[n]
-        d2 = two[f"param:{n}"].astype(np.float64) - init[n]
-        assert rel_l2(d2[mask], d1[mask]) <= tol_each, n
 
 
 @pytest.mark.parametrize("graphs", ["1", "0"])
