@@ -320,6 +320,9 @@ def main():
                      "frac": achieved / tf32_peak,
                      "peak_note": f"dense TF32 = half the bf16 sustained figure {peak_src}",
                      "gemm_share_of_step": gemm_ms / prof_ms if prof_ms else None,
+                     "regime": ("eager launches of the step, each GEMM timed by CUDA events on "
+                                "its stream" + (", with the step's NCCL collectives in flight on "
+                                                "the same SMs" if world > 1 else "")),
                      "gemm_launches_timed": int(gemm_launches),
                      "traffic": traffic,
                      "traffic_launch": "gemm_pair_kernel 16384x4096x1024 bias+GELU (ncu dram bytes); "
