@@ -13,7 +13,8 @@ tensor's RMS: AdamW's first update is lr * g / (|g| + eps), only a sign where g 
 must agree within 1e-5 relative L2, as must both steps' mean loss and gradient norm and all
 parameters after step 2. Step 2 starts from parameters that already differ by the step-1 update's
 rounding, which TF32 rounding of its inputs then resolves (measured: 3.4e-4 in TF32, within 1e-5
-in 3xTF32), so step 2's gradients and both moments are held to the step-parity bars of each
+in 3xTF32; one GPU summing step 1's gradients in the two-rank order reproduces the same 3.4e-4),
+so step 2's gradients and both moments are held to the step-parity bars of each
 precision: 1e-5 per tensor in 3xTF32, 2e-3 in TF32 (2e-2 per tensor for Spar's own block, as
 against the oracle). With step 1's parameters, both
 moments and the final parameters checked, step 2's update is determined; its quotient
