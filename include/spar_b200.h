@@ -234,7 +234,9 @@ struct SparCudaStatus spar_b200_rope_apply(float* x, const float* table, uint64_
 /* base pointers 16-byte aligned.                                                               */
 enum SparB200Precision {
   SPAR_B200_TF32 = 0,   /* operands rounded to TF32 (10-bit mantissa), fp32 accumulate */
-  SPAR_B200_TF32X3 = 1, /* split a = hi + lo, three TF32 products: fp32-faithful */
+  SPAR_B200_TF32X3 = 1, /* split a = hi + lo, three TF32 products: fp32-faithful; no      */
+                        /* tensor-core accumulator sums more than 512 K elements (the      */
+                        /* sums move to fp32 registers or split-K partials beyond that)    */
 };
 enum SparB200Epilogue {
   SPAR_B200_EPI_NONE = 0,      /* C = alpha*acc                                            */
