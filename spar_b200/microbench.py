@@ -64,10 +64,17 @@ def timed(fn, iters=10, warmup=3):
     return a.elapsed_time(b) / iters
 
 
+PEAK_NOTES = {
+    "GB/s": "measured HBM copy (MEASURED_PEAKS.json hbm_gbs)",
+    "TFLOP/s": "dense TF32 = half the measured bf16 burst GEMM rate (MEASURED_PEAKS.json "
+               "bf16_tflops / 2); no TF32 rate is measured directly",
+}
+
+
 def report(name, ms, work, unit, peak):
     rate = work / (ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
     line = {"kernel": name, "ms": round(ms, 4), "achieved": round(rate, 1), "unit": unit,
-            "peak": round(peak, 1), "frac": round(rate / peak, 3)}
+            "peak": round(peak, 1), "frac": round(rate / peak, 3), "peak_note": PEAK_NOTES[unit]}
     print(json.dumps(line), flush=True)
     return line
 
