@@ -294,8 +294,11 @@ __device__ __forceinline__ void probs64(uint32_t (&v0)[32], uint32_t (&v1)[32], 
 template <int DH>
 struct Fwd {
   static constexpr uint32_t kTile = DH * 512;  // 128 rows x DH fp32
-  static constexpr uint32_t kKStages = DH == 64 ? 3 : 4;
-  static constexpr uint32_t kVStages = 2;
+  // head_dim 64: two K and three V stages (V_j is read last, by the P V products, so its stage
+  // frees latest); measured against three K and two V stages: 122.9 vs 124.7 us at 16 sequences,
+  // 21.2 vs 22.5 us at 2 (C5 widths).
+  static constexpr uint32_t kKStages = DH == 64 ? 2 : 4;
+  static constexpr uint32_t kVStages = DH == 64 ? 3 : 2;
   static constexpr uint32_t kQ = 0;  // [2] query tiles A, B
   static constexpr uint32_t kK = kQ + 2 * kTile;
   static constexpr uint32_t kV = kK + kKStages * kTile;
