@@ -20,7 +20,7 @@ against the oracle). With step 1's parameters, both
 moments and the final parameters checked, step 2's update is determined; its quotient
 m / sqrt(v) is not compared element by element (it amplifies small first moments).
 
-Needs two GPUs (skipped otherwise); run with `gpurun --gpus 2`.
+Needs two GPUs (skipped otherwise).
 """
 import os
 import socket
