@@ -155,13 +155,48 @@ __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* m
 }
 
 // 4-D tiled tensor store from this CTA's shared memory (bulk-group completion); elements outside
-// the tensor bounds are not written.
+// the tensor bounds are not written, in whole 16-byte units along the innermost dimension (a row
+// that ends inside a 16-byte chunk has that chunk's last elements written too, measured).
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0,
                                              int c1, int c2, int c3) {
   asm volatile(
       "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
       "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// L2 eviction priorities for the bulk copies (hints only; results do not depend on them).
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// tma_load_4d_pair with an L2 cache policy.
+__device__ __forceinline__ void tma_load_4d_pair_hint(void* dst, const CUtensorMap* map,
+                                                      uint32_t bar_cluster, int c0, int c1, int c2,
+                                                      int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar_cluster),
+      "l"(policy)
+      : "memory");
+}
+
+// tma_store_4d with an L2 cache policy.
+__device__ __forceinline__ void tma_store_4d_hint(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3, %4, %5}], [%1], %6;" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
       : "memory");
 }
 
